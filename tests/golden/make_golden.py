@@ -1,0 +1,366 @@
+"""Generate the golden fixtures by running the reference implementation itself.
+
+Usage::
+
+    python tests/golden/make_golden.py --reference <path to the shadow-infer source tree>
+
+The reference (``shadowinfer`` package, pure Python + torch CPU) is imported
+from its source tree with a no-op ``structlog`` stand-in (``_stub/``).  It is
+run on seeded inputs and its outputs are written to
+
+* ``small_cases.npz`` -- inputs and full outputs of small edge cases;
+* ``pins.json``       -- scalar outputs of those cases, plus SHA-256 digests of
+  full-size outputs of the cfg1 / cfg2 pipelines (inputs regenerated from
+  ``shadow_infer_b200.workloads`` at test time).
+
+Nothing at test time imports the reference; only these files are read.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import sys
+import types
+
+import numpy as np
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+REPO = os.path.dirname(os.path.dirname(HERE))
+sys.path.insert(0, REPO)
+sys.path.insert(0, HERE)
+
+from golden_lib import PINS_JSON, SMALL_NPZ, array_digest, packed_summary, to_numpy  # noqa: E402
+
+from shadow_infer_b200 import workloads as W  # noqa: E402
+
+PRECISIONS = ("fp32", "fp16", "int8", "int4")
+
+
+def _import_reference(path: str):
+    sys.path.insert(0, os.path.join(HERE, "_stub"))
+    sys.path.insert(0, path)
+    from shadowinfer.shadowkv import rd_allocator, precision_plan, packed_kv_cache  # noqa
+    from shadowinfer.shadowkv.shadowkv_agent import ShadowKVAgent  # noqa
+    return types.SimpleNamespace(
+        rd=rd_allocator, plan=precision_plan, pkc=packed_kv_cache, Agent=ShadowKVAgent
+    )
+
+
+ARR: dict = {}
+PINS: dict = {"cases": {}, "full": {}}
+
+
+def put(case: str, name: str, x) -> None:
+    ARR[f"{case}/{name}"] = to_numpy(x)
+
+
+def packed_arrays(case: str, prefix: str, packed) -> None:
+    """Store every tensor and list of a reference packed cache."""
+    for pname, d in packed.packed_data.items():
+        for key in ("k", "v", "scale_k", "scale_v"):
+            if d.get(key) is not None:
+                put(case, f"{prefix}{pname}.{key}", d[key])
+        put(case, f"{prefix}{pname}.indices", np.array(d["indices"], dtype=np.int64).reshape(-1, 2))
+        if "byte_offsets" in d:
+            put(case, f"{prefix}{pname}.byte_offsets", np.array(d["byte_offsets"], dtype=np.int64).reshape(-1, 4))
+
+
+def codes_of(gen, S, H, probs):
+    p = torch.tensor(probs, dtype=torch.float64)
+    return torch.multinomial(p, S * H, replacement=True, generator=gen).reshape(S, H).to(torch.int8)
+
+
+def kv(gen, B, H, S, D, zero_rows=0, big=False):
+    k = torch.randn(B, H, S, D, generator=gen)
+    v = torch.randn(B, H, S, D, generator=gen)
+    m = torch.rand(B, H, S, D, generator=gen) < 0.01
+    k = torch.where(m, k * 8, k)
+    if zero_rows:
+        for i in range(zero_rows):
+            k[0, i % H, (3 * i) % S, :] = 0.0
+            v[-1, (i + 1) % H, (5 * i + 1) % S, :] = 0.0
+    if big:
+        k[0, 0, 0, :4] = torch.tensor([7.0e4, -1.0e5, 65519.0, 65520.0])
+    return k.contiguous(), v.contiguous()
+
+
+def pack_case(R, case, gen, B, H, S, D, probs, group=16, reuse_p=0.3, zero_rows=0, big=False):
+    k, v = kv(gen, B, H, S, D, zero_rows, big)
+    codes = codes_of(gen, S, H, probs)
+    reuse = torch.rand(S, H, generator=gen) < reuse_p
+    reuse_dict = {(t, h): bool(reuse[t, h]) for t in range(S) for h in range(H)}
+    plan = R.plan.PrecisionPlan.from_codes(codes, reuse_mask=reuse_dict)
+    packed = R.pkc.PackedKVCache.pack(k, v, None, group_size=group, plan=plan)["packed_kv"]
+    # the map path must agree with the plan path
+    pmap = R.plan.codes_to_map(codes)
+    packed_map = R.pkc.PackedKVCache.pack(k, v, pmap, group_size=group)["packed_kv"]
+    assert packed_summary(packed.packed_data, packed.memory_bytes()) == packed_summary(
+        packed_map.packed_data, packed_map.memory_bytes())
+    ku, vu = packed.unpack()
+    kr, vr = packed.unpack_reference()
+    put(case, "k", k); put(case, "v", v); put(case, "codes", codes); put(case, "reuse", reuse)
+    for p in PRECISIONS:
+        put(case, f"plan.flat.{p}", plan.flat_indices[p])
+    put(case, "plan.evicted", np.array(plan.evicted_entries, dtype=np.int64).reshape(-1, 2))
+    put(case, "plan.reuse_flat", plan.reuse_flat)
+    packed_arrays(case, "packed.", packed)
+    put(case, "unpack.k", ku); put(case, "unpack.v", vu)
+    assert torch.allclose(kr, ku, atol=1e-6, rtol=1e-6) and torch.allclose(vr, vu, atol=1e-6, rtol=1e-6)
+    # dense working copy of compress_kv (no previous step, then with one)
+    fake = types.SimpleNamespace(int4_group_size=group)
+    core = R.Agent._compress_kv_with_plan(fake, k, v, None, None, plan, build_scale_map=False)
+    put(case, "dense.k", core["k"]); put(case, "dense.v", core["v"])
+    kp = k + 0.01 * torch.randn(k.shape, generator=gen)
+    vp = v + 0.01 * torch.randn(v.shape, generator=gen)
+    core2 = R.Agent._compress_kv_with_plan(fake, k, v, kp, vp, plan, build_scale_map=False)
+    put(case, "k_prev", kp); put(case, "v_prev", vp)
+    put(case, "dense_reuse.k", core2["k"]); put(case, "dense_reuse.v", core2["v"])
+    PINS["cases"][case] = {
+        "kind": "pack", "B": B, "H": H, "S": S, "D": D, "group": group,
+        "fingerprint": plan.fingerprint,
+        "summary": packed_summary(packed.packed_data, packed.memory_bytes()),
+        "memory_bytes": packed.memory_bytes(),
+        "data_plane_bytes": packed.data_plane_bytes(),
+        "resident_bytes": packed.resident_bytes(),
+    }
+    return k, v, codes, packed
+
+
+def reuse_case(R, case, gen, B, H, S, D, group=16):
+    k, v = kv(gen, B, H, S, D)
+    probs = (0.15, 0.3, 0.25, 0.2, 0.1)
+    codes = codes_of(gen, S, H, probs)
+    prev_codes = torch.where(torch.rand(S, H, generator=gen) < 0.6, codes, codes_of(gen, S, H, probs))
+    kp = k + 0.01 * torch.randn(k.shape, generator=gen)
+    vp = v + 0.01 * torch.randn(v.shape, generator=gen)
+    mask = torch.rand(S, H, generator=gen) < 0.5
+    mask_dict = {(t, h): bool(mask[t, h]) for t in range(S) for h in range(H)}
+    P = R.pkc.PackedKVCache
+    cur = P.pack(k, v, R.plan.codes_to_map(codes), group_size=group)["packed_kv"]
+    prev = P.pack(kp, vp, R.plan.codes_to_map(prev_codes), group_size=group)["packed_kv"]
+    stats = cur.apply_reuse_mask(prev, mask_dict, return_stats=True)
+    put(case, "k", k); put(case, "v", v); put(case, "k_prev", kp); put(case, "v_prev", vp)
+    put(case, "codes", codes); put(case, "prev_codes", prev_codes); put(case, "mask", mask)
+    packed_arrays(case, "after.", cur)
+    ku, vu = cur.unpack()
+    put(case, "unpack.k", ku); put(case, "unpack.v", vu)
+    PINS["cases"][case] = {
+        "kind": "reuse", "B": B, "H": H, "S": S, "D": D, "group": group, "stats": stats,
+        "summary": packed_summary(cur.packed_data, cur.memory_bytes()),
+    }
+
+
+def evict_case(R, case, gen, B, H, S, D, group=16, frac=0.25):
+    k, v = kv(gen, B, H, S, D)
+    codes = codes_of(gen, S, H, (0.2, 0.3, 0.3, 0.15, 0.05))
+    cache = R.pkc.PackedKVCache.pack(k, v, R.plan.codes_to_map(codes), group_size=group)["packed_kv"]
+    mask = torch.rand(S, H, generator=gen) < frac
+    ts, hs = torch.nonzero(mask, as_tuple=True)
+    entries = set(zip(ts.tolist(), hs.tolist()))
+    removed = cache.evict(entries)
+    again = cache.evict(entries)
+    put(case, "k", k); put(case, "v", v); put(case, "codes", codes); put(case, "mask", mask)
+    packed_arrays(case, "after.", cache)
+    ku, vu = cache.unpack()
+    put(case, "unpack.k", ku); put(case, "unpack.v", vu)
+    # evicting a whole bucket deletes its key
+    whole = torch.zeros(S, H, dtype=torch.bool)
+    idx = cache.packed_data.get("int8", {}).get("indices", [])
+    for t, h in idx:
+        whole[t, h] = True
+    removed_whole = cache.evict(set(idx))
+    put(case, "whole_mask", whole)
+    PINS["cases"][case] = {
+        "kind": "evict", "B": B, "H": H, "S": S, "D": D, "group": group,
+        "removed": removed, "removed_again": again, "removed_whole": removed_whole,
+        "summary_after_whole": packed_summary(cache.packed_data, cache.memory_bytes()),
+        "resident_after_whole": cache.resident_bytes(),
+    }
+
+
+def admit_case(R, case, gen, S, H, B, D, budget_frac, *, sink=0, rd=True, evict=False,
+               protected_p=0.0, ties=False, group=16, signed_zero=False, nan=False,
+               sens_mismatch=False, budget_abs=None):
+    probs = (0.1, 0.4, 0.25, 0.2, 0.05)
+    codes = codes_of(gen, S, H, probs)
+    if ties:
+        imp = (torch.randint(0, 3, (S, H), generator=gen).float() * 0.5)
+        sens = torch.ones(S, H)
+    else:
+        imp = torch.rand(S, H, generator=gen)
+        k, v = kv(gen, B, H, S, D)
+        sens = R.rd.kv_sensitivity(k, v)
+    if signed_zero:
+        z = torch.rand(S, H, generator=gen) < 0.2
+        imp = torch.where(z, torch.where(torch.rand(S, H, generator=gen) < 0.5, -0.0, 0.0), imp)
+    if nan:
+        imp[1, 0] = float("nan")
+        imp[S // 2, H - 1] = float("nan")
+    if sens_mismatch:
+        sens = torch.ones(S + 1, H)
+    protected = None
+    if protected_p > 0:
+        protected = torch.rand(S, H, generator=gen) < protected_p
+    predicted0 = R.rd.predict_codes_bytes(codes, B, D, group_size=group)
+    budget = budget_abs if budget_abs is not None else int(predicted0 * budget_frac)
+    out, pred, ev = R.rd.admit_codes(
+        codes, imp, sens, budget, batch=B, head_dim=D, sink_tokens=sink, rd_allocation=rd,
+        allow_eviction=evict, protected_mask=protected, group_size=group)
+    put(case, "codes", codes); put(case, "importance", imp); put(case, "sensitivity", sens)
+    if protected is not None:
+        put(case, "protected", protected)
+    put(case, "out", out)
+    PINS["cases"][case] = {
+        "kind": "admit", "S": S, "H": H, "B": B, "D": D, "group": group, "budget": budget,
+        "sink": sink, "rd": rd, "evict": evict, "predicted": pred, "evicted": ev,
+        "predicted0": predicted0,
+    }
+
+
+def allocate_case(R, case):
+    vals = []
+    for base in (0.0, 0.1, 0.2, 0.3, 0.4, 0.5, 0.6, 0.7, 0.8, 0.9, 1.0):
+        for d in (-1e-6, 0.0, 1e-6):
+            vals.append(base + d)
+    vals += [0.7000000000000001, 0.19999999, 0.20000001, -0.5, 2.0]
+    imp = torch.tensor(vals, dtype=torch.float32).reshape(-1, 1).repeat(1, 3)
+    put(case, "importance", imp)
+    for mode in ("aggressive", "balanced", "conservative", "unknown"):
+        put(case, f"codes.{mode}", R.Agent.allocate_precision_codes(None, imp, mode))
+    PINS["cases"][case] = {"kind": "allocate"}
+
+
+def sensitivity_case(R, case, gen):
+    k, v = kv(gen, 2, 3, 17, 64)
+    put(case, "k", k); put(case, "v", v); put(case, "sens", R.rd.kv_sensitivity(k, v))
+    PINS["cases"][case] = {"kind": "sensitivity"}
+
+
+def attention_case(R, case, gen, B, H, S, D):
+    k, v = kv(gen, B, H, S, D)
+    codes = codes_of(gen, S, H, (0.1, 0.3, 0.3, 0.25, 0.05))
+    packed = R.pkc.PackedKVCache.pack(k, v, R.plan.codes_to_map(codes), group_size=16)["packed_kv"]
+    q = torch.randn(B, H, S, D, generator=gen).to(torch.float16)
+    ku, vu = packed.unpack()
+    qf = q.float()
+    scores = torch.matmul(qf, ku.transpose(-2, -1)) / (D ** 0.5)
+    out = torch.matmul(torch.softmax(scores, dim=-1), vu)
+    put(case, "k", k); put(case, "v", v); put(case, "codes", codes); put(case, "q", q)
+    put(case, "out", out)
+    PINS["cases"][case] = {"kind": "attention", "B": B, "H": H, "S": S, "D": D}
+
+
+def full_pins(R):
+    """cfg1 / cfg2 pipelines at full size: digests only."""
+    c1 = W.CONFIGS["cfg1"]
+    k, v = W.kv_tensors(c1["B"], c1["H"], c1["S"], c1["D"], c1["seed"])
+    imp = W.importance_map(c1["S"], c1["H"], c1["seed"], c1["fractions"])
+    codes = R.Agent.allocate_precision_codes(None, imp, "balanced")
+    plan = R.plan.PrecisionPlan.from_codes(codes)
+    packed = R.pkc.PackedKVCache.pack(k, v, None, group_size=16, plan=plan)["packed_kv"]
+    ku, vu = packed.unpack()
+    fake = types.SimpleNamespace(int4_group_size=16)
+    core = R.Agent._compress_kv_with_plan(fake, k, v, None, None, plan, build_scale_map=False)
+    counts = {p: len(plan.groups[p]) for p in PRECISIONS}
+    PINS["full"]["cfg1"] = {
+        "k": array_digest(k), "importance": array_digest(imp),
+        "codes": array_digest(codes), "counts": counts, "fingerprint": plan.fingerprint,
+        "packed": packed_summary(packed.packed_data, packed.memory_bytes()),
+        "unpack_k": array_digest(ku), "unpack_v": array_digest(vu),
+        "dense_k": array_digest(core["k"]), "dense_v": array_digest(core["v"]),
+    }
+    print("cfg1 done", counts, packed.memory_bytes())
+
+    I = W.cfg2_inputs()
+    k, v = I["k"], I["v"]
+    sens = R.rd.kv_sensitivity(k, v)
+    codes0 = R.Agent.allocate_precision_codes(None, I["importance"], "balanced")
+    admitted, pred, ev = R.rd.admit_codes(
+        codes0, I["importance"], sens, I["budget"], batch=1, head_dim=128,
+        sink_tokens=I["sink_tokens"], rd_allocation=True, allow_eviction=True, group_size=16)
+    reuse = I["reuse"]
+    ts, hs = torch.nonzero(reuse, as_tuple=True)
+    reuse_dict = {(t, h): True for t, h in zip(ts.tolist(), hs.tolist())}
+    plan = R.plan.PrecisionPlan.from_codes(admitted, reuse_mask=reuse_dict)
+    packed = R.pkc.PackedKVCache.pack(k, v, None, group_size=16, plan=plan)["packed_kv"]
+    summary_pack = packed_summary(packed.packed_data, packed.memory_bytes())
+    plan_prev = R.plan.PrecisionPlan.from_codes(admitted)
+    prev = R.pkc.PackedKVCache.pack(I["k_prev"], I["v_prev"], None, group_size=16, plan=plan_prev)["packed_kv"]
+    stats = packed.apply_reuse_mask(prev, reuse_dict, return_stats=True)
+    summary_reuse = packed_summary(packed.packed_data, packed.memory_bytes())
+    ku, vu = packed.unpack()
+    g = torch.Generator().manual_seed(424242)
+    emask = torch.rand(admitted.shape, generator=g) < 0.25
+    ts, hs = torch.nonzero(emask, as_tuple=True)
+    removed = packed.evict(set(zip(ts.tolist(), hs.tolist())))
+    ke, ve = packed.unpack()
+    PINS["full"]["cfg2"] = {
+        "k": array_digest(k), "importance": array_digest(I["importance"]),
+        "reuse": array_digest(reuse), "k_prev": array_digest(I["k_prev"]),
+        "budget": I["budget"], "sensitivity": array_digest(sens),
+        "codes0": array_digest(codes0), "admitted": array_digest(admitted),
+        "predicted": pred, "evicted": ev, "fingerprint": plan.fingerprint,
+        "counts": {p: len(plan.groups[p]) for p in PRECISIONS},
+        "packed": summary_pack, "reuse_stats": stats, "after_reuse": summary_reuse,
+        "unpack_k": array_digest(ku), "unpack_v": array_digest(vu),
+        "evict_seed": 424242, "evict_frac": 0.25, "removed": removed,
+        "after_evict": packed_summary(packed.packed_data, packed.memory_bytes()),
+        "resident_after_evict": packed.resident_bytes(),
+        "unpack_evict_k": array_digest(ke), "unpack_evict_v": array_digest(ve),
+    }
+    print("cfg2 done", pred, ev, stats, removed)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", required=True, help="path of the shadow-infer source tree")
+    args = ap.parse_args()
+    torch.set_num_threads(os.cpu_count() or 1)
+    R = _import_reference(args.reference)
+    gen = torch.Generator().manual_seed(20261201)
+    mixed = (0.15, 0.3, 0.25, 0.2, 0.1)
+    pack_case(R, "pack_b1_d64", gen, 1, 4, 16, 64, mixed)
+    pack_case(R, "pack_b2_d64", gen, 2, 3, 10, 64, mixed)
+    pack_case(R, "pack_b1_d63_odd", gen, 1, 2, 7, 63, mixed)
+    pack_case(R, "pack_b3_d40", gen, 3, 2, 9, 40, mixed)
+    pack_case(R, "pack_b1_d128_g32_int4", gen, 1, 2, 8, 128, (0, 0, 0, 1.0, 0), group=32)
+    pack_case(R, "pack_b2_d128_zero_rows", gen, 2, 3, 11, 128, mixed, zero_rows=6)
+    pack_case(R, "pack_b1_d128_fp16_overflow", gen, 1, 2, 5, 128, (0.0, 1.0, 0, 0, 0), big=True)
+    pack_case(R, "pack_b1_d256", gen, 1, 2, 12, 256, mixed)
+    pack_case(R, "pack_b1_d32", gen, 1, 3, 11, 32, mixed)
+    pack_case(R, "pack_b1_all_evicted_but_one", gen, 1, 2, 6, 64, (0, 0, 0, 0, 1.0))
+    pack_case(R, "pack_b4_d128", gen, 4, 2, 9, 128, mixed)
+    reuse_case(R, "reuse_b1_d64", gen, 1, 4, 24, 64)
+    reuse_case(R, "reuse_b2_d128", gen, 2, 3, 12, 128)
+    reuse_case(R, "reuse_b1_d63", gen, 1, 2, 9, 63)
+    evict_case(R, "evict_b1_d64", gen, 1, 4, 24, 64)
+    evict_case(R, "evict_b2_d128", gen, 2, 3, 16, 128)
+    admit_case(R, "admit_basic", gen, 64, 8, 1, 128, 0.6)
+    admit_case(R, "admit_evict_tiny", gen, 64, 8, 1, 128, 0.05, evict=True)
+    admit_case(R, "admit_ties", gen, 48, 6, 1, 64, 0.5, ties=True, evict=True)
+    admit_case(R, "admit_sink_protected", gen, 40, 4, 2, 64, 0.3, sink=3, protected_p=0.2, evict=True)
+    admit_case(R, "admit_budget_none", gen, 16, 4, 1, 64, 0.5, budget_abs=-1)
+    admit_case(R, "admit_budget_loose", gen, 16, 4, 1, 64, 2.0)
+    admit_case(R, "admit_no_rd", gen, 64, 8, 1, 128, 0.55, rd=False)
+    admit_case(R, "admit_signed_zero", gen, 64, 8, 1, 128, 0.5, signed_zero=True, evict=True)
+    admit_case(R, "admit_nan", gen, 32, 4, 1, 64, 0.4, nan=True, evict=True)
+    admit_case(R, "admit_sens_mismatch", gen, 32, 4, 1, 64, 0.45)
+    admit_case(R, "admit_b2_g16", gen, 96, 8, 2, 64, 0.35, sink=4, evict=True)
+    admit_case(R, "admit_boundary_mid", gen, 256, 8, 1, 128, 0.93)
+    admit_case(R, "admit_all_sinks", gen, 8, 4, 1, 64, 0.1, sink=16, evict=True)
+    allocate_case(R, "allocate")
+    sensitivity_case(R, "sensitivity", gen)
+    attention_case(R, "attention_b1", gen, 1, 2, 64, 64)
+    attention_case(R, "attention_b2_d128", gen, 2, 1, 80, 128)
+    full_pins(R)
+    np.savez_compressed(SMALL_NPZ, **ARR)
+    with open(PINS_JSON, "w") as f:
+        json.dump(PINS, f, indent=1, sort_keys=True)
+    print("wrote", SMALL_NPZ, os.path.getsize(SMALL_NPZ), PINS_JSON)
+
+
+if __name__ == "__main__":
+    main()

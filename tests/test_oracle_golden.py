@@ -1,0 +1,163 @@
+"""Pin the CPU oracle to the reference: every golden fixture must be reproduced.
+
+The fixtures were produced by the reference implementation itself
+(``tests/golden/make_golden.py``); these tests run on the CPU only.
+"""
+
+import numpy as np
+import pytest
+
+from golden_lib import array_digest, case_arrays, packed_summary
+from oracle import shadowkv_oracle as O
+
+PRECISIONS = ("fp32", "fp16", "int8", "int4")
+
+
+def _cases(pins, kind):
+    return sorted(c for c, v in pins["cases"].items() if v["kind"] == kind)
+
+
+def _pins():
+    from golden_lib import load_pins
+    return load_pins()
+
+
+@pytest.mark.parametrize("case", _cases(_pins(), "pack"))
+def test_pack_plan_unpack_dense(case, golden_small, golden_pins):
+    a = case_arrays(golden_small, case)
+    p = golden_pins["cases"][case]
+    plan = O.plan_from_codes(a["codes"], a["reuse"])
+    for prec in PRECISIONS:
+        assert np.array_equal(plan["flat_indices"][prec], a[f"plan.flat.{prec}"]), prec
+    assert np.array_equal(np.array(plan["evicted_entries"], dtype=np.int64).reshape(-1, 2), a["plan.evicted"])
+    assert np.array_equal(plan["reuse_flat"], a["plan.reuse_flat"])
+    assert plan["fingerprint"] == p["fingerprint"]
+    cache = O.pack(a["k"], a["v"], plan, p["group"])
+    assert packed_summary(cache.packed_data, cache.memory_bytes()) == p["summary"]
+    assert cache.memory_bytes() == p["memory_bytes"]
+    assert cache.data_plane_bytes() == p["data_plane_bytes"]
+    assert cache.resident_bytes() == p["resident_bytes"]
+    ku, vu = O.unpack(cache)
+    assert np.array_equal(ku, a["unpack.k"]) and np.array_equal(vu, a["unpack.v"])
+    kd, vd = O.compress_dense(a["k"], a["v"], plan, p["group"])
+    assert np.array_equal(kd, a["dense.k"]) and np.array_equal(vd, a["dense.v"])
+    kd, vd = O.compress_dense(a["k"], a["v"], plan, p["group"], a["k_prev"], a["v_prev"])
+    assert np.array_equal(kd, a["dense_reuse.k"]) and np.array_equal(vd, a["dense_reuse.v"])
+
+
+@pytest.mark.parametrize("case", _cases(_pins(), "reuse"))
+def test_reuse(case, golden_small, golden_pins):
+    a = case_arrays(golden_small, case)
+    p = golden_pins["cases"][case]
+    cur = O.pack(a["k"], a["v"], O.plan_from_codes(a["codes"]), p["group"])
+    prev = O.pack(a["k_prev"], a["v_prev"], O.plan_from_codes(a["prev_codes"]), p["group"])
+    stats = O.apply_reuse_mask(cur, prev, a["mask"])
+    assert stats == p["stats"]
+    assert packed_summary(cur.packed_data, cur.memory_bytes()) == p["summary"]
+    ku, vu = O.unpack(cur)
+    assert np.array_equal(ku, a["unpack.k"]) and np.array_equal(vu, a["unpack.v"])
+
+
+@pytest.mark.parametrize("case", _cases(_pins(), "evict"))
+def test_evict(case, golden_small, golden_pins):
+    a = case_arrays(golden_small, case)
+    p = golden_pins["cases"][case]
+    cache = O.pack(a["k"], a["v"], O.plan_from_codes(a["codes"]), p["group"])
+    assert O.evict(cache, a["mask"]) == p["removed"]
+    assert O.evict(cache, a["mask"]) == p["removed_again"] == 0
+    ku, vu = O.unpack(cache)
+    assert np.array_equal(ku, a["unpack.k"]) and np.array_equal(vu, a["unpack.v"])
+    assert O.evict(cache, a["whole_mask"]) == p["removed_whole"]
+    assert "int8" not in cache.packed_data
+    assert packed_summary(cache.packed_data, cache.memory_bytes()) == p["summary_after_whole"]
+    assert cache.resident_bytes() == p["resident_after_whole"]
+
+
+@pytest.mark.parametrize("case", _cases(_pins(), "admit"))
+def test_admit(case, golden_small, golden_pins):
+    a = case_arrays(golden_small, case)
+    p = golden_pins["cases"][case]
+    out, pred, ev = O.admit_codes(
+        a["codes"], a["importance"], a["sensitivity"], p["budget"], p["B"], p["D"],
+        sink_tokens=p["sink"], rd_allocation=p["rd"], allow_eviction=p["evict"],
+        protected_mask=a.get("protected"), group_size=p["group"])
+    assert np.array_equal(out, a["out"])
+    assert (pred, ev) == (p["predicted"], p["evicted"])
+    assert O.predict_codes_bytes(a["codes"], p["B"], p["D"], p["group"]) == p["predicted0"]
+
+
+def test_allocate(golden_small):
+    a = case_arrays(golden_small, "allocate")
+    for mode in ("aggressive", "balanced", "conservative", "unknown"):
+        assert np.array_equal(O.allocate_precision_codes(a["importance"], mode), a[f"codes.{mode}"]), mode
+
+
+def test_sensitivity(golden_small):
+    a = case_arrays(golden_small, "sensitivity")
+    assert np.array_equal(O.kv_sensitivity(a["k"], a["v"]), a["sens"])
+
+
+@pytest.mark.parametrize("case", _cases(_pins(), "attention"))
+def test_attention(case, golden_small):
+    a = case_arrays(golden_small, case)
+    cache = O.pack(a["k"], a["v"], O.plan_from_codes(a["codes"]), 16)
+    out = O.packed_attention(a["q"].astype(np.float32), cache)
+    ref = a["out"].astype(np.float64)
+    rel = np.linalg.norm(out - ref) / np.linalg.norm(ref)
+    assert rel < 1e-5, rel
+
+
+def test_entry_bytes_table():
+    # rd_allocator.py:26-44 values at B=1 and B=8, D=128 (fp32/fp16/int8/int4)
+    assert list(O.code_costs(1, 128, 16)) == [1024, 512, 264, 192, 0]
+    assert list(O.code_costs(8, 128, 16)) == [8192, 4096, 2112, 1536, 0]
+
+
+def test_full_cfg1_pins(golden_pins):
+    from shadow_infer_b200 import workloads as W
+    pin = golden_pins["full"]["cfg1"]
+    c = W.CONFIGS["cfg1"]
+    k, v = W.kv_tensors(c["B"], c["H"], c["S"], c["D"], c["seed"])
+    imp = W.importance_map(c["S"], c["H"], c["seed"], c["fractions"])
+    assert array_digest(k) == pin["k"] and array_digest(imp) == pin["importance"]
+    codes = O.allocate_precision_codes(imp.numpy(), "balanced")
+    assert array_digest(codes) == pin["codes"]
+    plan = O.plan_from_codes(codes)
+    assert plan["fingerprint"] == pin["fingerprint"]
+    cache = O.pack(k.numpy(), v.numpy(), plan, 16)
+    assert packed_summary(cache.packed_data, cache.memory_bytes()) == pin["packed"]
+    ku, vu = O.unpack(cache)
+    assert array_digest(ku) == pin["unpack_k"] and array_digest(vu) == pin["unpack_v"]
+    kd, vd = O.compress_dense(k.numpy(), v.numpy(), plan, 16)
+    assert array_digest(kd) == pin["dense_k"] and array_digest(vd) == pin["dense_v"]
+
+
+def test_full_cfg2_pins(golden_pins):
+    import torch
+    from shadow_infer_b200 import workloads as W
+    pin = golden_pins["full"]["cfg2"]
+    I = W.cfg2_inputs()
+    k, v = I["k"].numpy(), I["v"].numpy()
+    assert array_digest(I["k"]) == pin["k"] and array_digest(I["reuse"]) == pin["reuse"]
+    sens = O.kv_sensitivity(k, v)
+    assert array_digest(sens) == pin["sensitivity"]
+    codes0 = O.allocate_precision_codes(I["importance"].numpy(), "balanced")
+    assert array_digest(codes0) == pin["codes0"]
+    adm, pred, ev = O.admit_codes(codes0, I["importance"].numpy(), sens, I["budget"], 1, 128,
+                                  sink_tokens=I["sink_tokens"], rd_allocation=True, allow_eviction=True)
+    assert array_digest(adm) == pin["admitted"] and (pred, ev) == (pin["predicted"], pin["evicted"])
+    reuse = I["reuse"].numpy()
+    plan = O.plan_from_codes(adm, reuse)
+    assert plan["fingerprint"] == pin["fingerprint"]
+    cache = O.pack(k, v, plan, 16)
+    assert packed_summary(cache.packed_data, cache.memory_bytes()) == pin["packed"]
+    prev = O.pack(I["k_prev"].numpy(), I["v_prev"].numpy(), O.plan_from_codes(adm), 16)
+    assert O.apply_reuse_mask(cache, prev, reuse) == pin["reuse_stats"]
+    assert packed_summary(cache.packed_data, cache.memory_bytes()) == pin["after_reuse"]
+    ku, vu = O.unpack(cache)
+    assert array_digest(ku) == pin["unpack_k"] and array_digest(vu) == pin["unpack_v"]
+    g = torch.Generator().manual_seed(pin["evict_seed"])
+    emask = (torch.rand(adm.shape, generator=g) < pin["evict_frac"]).numpy()
+    assert O.evict(cache, emask) == pin["removed"]
+    assert packed_summary(cache.packed_data, cache.memory_bytes()) == pin["after_evict"]
+    assert cache.resident_bytes() == pin["resident_after_evict"]
