@@ -1,0 +1,131 @@
+/*
+ * shadowkv_b200.h -- C ABI of the B200 (sm_100a) ShadowKV packed-KV data plane.
+ *
+ * Every entry point takes DEVICE pointers, plain sizes and a cudaStream_t
+ * (passed as void*), enqueues its kernels on that stream and returns an int
+ * status (SKV_OK == 0).  Nothing here allocates memory: outputs, and the
+ * scratch buffers whose sizes the *_scratch_bytes queries return, belong to the
+ * caller.  Functions are reentrant; the only process-wide state is the
+ * thread-local last-error message returned by skv_last_error().
+ *
+ * Layouts (reference schema of shadowinfer/shadowkv/packed_kv_cache.py):
+ *   K, V        float32 [B, H, S, D], contiguous
+ *   codes       int8    [S, H]   0=fp32 1=fp16 2=int8 3=int4 4=evicted
+ *   masks       uint8   [S, H]   0/1 (reuse / protected / evict sets)
+ *   slot        int32   [S, H]   (pos << 2) | code for a stored entry, -1 if absent
+ *   bucket fp32 k/v float[N,B,D]; fp16 half[N,B,D];
+ *          int8 k/v int8[N,B,D] + scale float[N,B];
+ *          int4 k/v uint8[N*rb], rb = ceil(B*D/2), scale float[N*B*G]
+ *   flat        int64   h*S + t of each bucket entry, in bucket order
+ *
+ * The entry each declaration replaces is cited as reference-file:line.
+ */
+#ifndef SHADOWKV_B200_H
+#define SHADOWKV_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+    SKV_OK = 0,
+    SKV_ERR_INVALID_ARGUMENT = 1, /* null pointer, non-positive size */
+    SKV_ERR_SHAPE = 2,            /* shape mismatch between operands */
+    SKV_ERR_GROUP_SIZE = 3,       /* int4 group size mismatch / invalid */
+    SKV_ERR_SCRATCH = 4,          /* scratch buffer smaller than required */
+    SKV_ERR_TOO_LARGE = 5,        /* size beyond a documented limit */
+    SKV_ERR_CUDA = 6,             /* a CUDA launch or runtime call failed */
+    SKV_ERR_UNSUPPORTED = 7       /* configuration the kernels do not cover */
+};
+
+/* One precision bucket (fp32, fp16, int8 or int4) of a packed cache. */
+typedef struct skv_bucket {
+    void* k;          /* payload of K (layout per precision, see above) */
+    void* v;          /* payload of V */
+    float* scale_k;   /* int8/int4 scales of K, NULL for fp32/fp16 */
+    float* scale_v;   /* int8/int4 scales of V */
+    int64_t* flat;    /* [count] h*S+t of every entry, bucket order */
+    int64_t count;    /* number of entries */
+} skv_bucket;
+
+/* Library identification and error reporting. */
+const char* skv_version(void);
+const char* skv_status_string(int status);
+const char* skv_last_error(void);
+
+/* ShadowKVAgent.allocate_precision_codes  (shadowinfer/shadowkv/shadowkv_agent.py:1028-1059)
+ * mode: 0 aggressive, 1 balanced, 2 conservative, other -> no adjustment. */
+int skv_allocate_codes(const float* importance, int64_t n, int mode, int8_t* codes, void* stream);
+
+/* kv_sensitivity  (shadowinfer/shadowkv/rd_allocator.py:47-61) -> float32 [S,H] */
+int skv_kv_sensitivity(const float* k, const float* v, int B, int H, int S, int D,
+                       float* sensitivity, void* stream);
+
+/* predict_codes_bytes  (shadowinfer/shadowkv/rd_allocator.py:170-187) -> *out (device int64) */
+int skv_predict_codes_bytes(const int8_t* codes, int64_t n, int batch, int head_dim,
+                            int group_size, int64_t* out, void* stream);
+
+/* admit_codes  (shadowinfer/shadowkv/rd_allocator.py:190-318)
+ * sensitivity may be NULL (treated as ones), protected_mask may be NULL.
+ * budget_bytes < 0 means "no budget".  result[0] = predicted bytes,
+ * result[1] = evicted count (device int64[2]).  codes_in is not modified. */
+size_t skv_admit_scratch_bytes(int S, int H);
+int skv_admit_codes(const int8_t* codes_in, int8_t* codes_out, const float* importance,
+                    const float* sensitivity, const uint8_t* protected_mask, int S, int H,
+                    int64_t budget_bytes, int batch, int head_dim, int group_size,
+                    int sink_tokens, int rd_allocation, int allow_eviction,
+                    void* scratch, size_t scratch_bytes, int64_t* result, void* stream);
+
+/* PrecisionPlan.from_codes  (shadowinfer/shadowkv/precision_plan.py:113-177)
+ * flat_out  int64[S*H]: entries of codes 0,1,2,3,4 concatenated, each token-major
+ * slot_out  int32[S*H]; reuse_flat_out int64[S*H] (may be NULL with reuse_mask NULL)
+ * counts    int64[6] (device): entries per code 0..4, then reuse entries. */
+size_t skv_plan_scratch_bytes(int S, int H);
+int skv_plan_bucket(const int8_t* codes, const uint8_t* reuse_mask, int S, int H,
+                    int64_t* flat_out, int32_t* slot_out, int64_t* reuse_flat_out,
+                    int64_t* counts, void* scratch, size_t scratch_bytes, void* stream);
+
+/* PackedKVCache._do_pack_with_plan / _pack_int4_rows
+ * (shadowinfer/shadowkv/packed_kv_cache.py:222-388) fused with the dense working
+ * copy of ShadowKVAgent._compress_kv_with_plan (shadowkv_agent.py:1698-1809):
+ * dense_k/dense_v (nullable) receive the compress_kv "k"/"v" tensors; rows with
+ * reuse_mask set are taken from k_prev/v_prev when those are given. */
+int skv_pack(const float* k, const float* v, int B, int H, int S, int D, int group_size,
+             const int32_t* slot, const skv_bucket* buckets /* [4] */,
+             float* dense_k, float* dense_v, const float* k_prev, const float* v_prev,
+             const uint8_t* reuse_mask, void* stream);
+
+/* PackedKVCache.unpack / _dequantize_int4_bucket
+ * (shadowinfer/shadowkv/packed_kv_cache.py:535-577, :636-656) -> zero-filled
+ * float32 [B,H,S,D] K and V.  int4_group is the int4 bucket's group_size. */
+int skv_unpack(const skv_bucket* buckets /* [4] */, const int32_t* slot, int B, int H, int S,
+               int D, int int4_group, float* k_out, float* v_out, void* stream);
+
+/* PackedKVCache.apply_reuse_mask  (shadowinfer/shadowkv/packed_kv_cache.py:753-854)
+ * stats[0] = applied, stats[1] = skipped_precision (device int64[2], overwritten). */
+int skv_apply_reuse(const skv_bucket* cur /* [4] */, const int32_t* cur_slot, int S,
+                    const skv_bucket* prev /* [4] */, const int32_t* prev_slot, int S_prev,
+                    const uint8_t* reuse_mask, int B, int H, int D, int int4_group,
+                    int64_t* stats, void* stream);
+
+/* PackedKVCache.evict  (shadowinfer/shadowkv/packed_kv_cache.py:666-740), two steps:
+ * skv_evict_count: kept[p] (device int64[4]) = entries of bucket p not in evict_mask,
+ *   kept[4] = removed total.
+ * skv_evict_compact: stable compaction of every bucket into dst (sized kept[p]),
+ *   slot rewritten in place (removed -> -1, kept -> new position).  Pass the same src
+ *   array to both calls; a bucket with dst[p].count == src[p].count is left untouched. */
+size_t skv_evict_scratch_bytes(int64_t max_bucket_entries);
+int skv_evict_count(const skv_bucket* src /* [4] */, const uint8_t* evict_mask, int S, int H,
+                    int64_t* kept, void* scratch, size_t scratch_bytes, void* stream);
+int skv_evict_compact(const skv_bucket* src /* [4] */, const skv_bucket* dst /* [4] */,
+                      const uint8_t* evict_mask, int32_t* slot, int B, int S, int H, int D,
+                      int int4_group, void* scratch, size_t scratch_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SHADOWKV_B200_H */

@@ -1,0 +1,51 @@
+"""Device placement for the data plane: all compute runs on a CUDA device.
+
+Tensors keep the device the caller gave them (the reference's semantics):
+host tensors are copied to the current CUDA device for the kernels and the
+results are copied back.  There is no CPU compute path -- without a CUDA device
+every data-plane call raises ``RuntimeError``.
+"""
+
+from __future__ import annotations
+
+from typing import Any, Optional
+
+import torch
+
+
+def compute_device(*tensors: Optional[torch.Tensor]) -> torch.device:
+    """The CUDA device to compute on: that of the first CUDA tensor, else the current one."""
+    for t in tensors:
+        if t is not None and t.is_cuda:
+            return t.device
+    if not torch.cuda.is_available():
+        raise RuntimeError(
+            "shadow_infer_b200 runs the ShadowKV data plane on a CUDA (sm_100a) device only; "
+            "no CUDA device is available"
+        )
+    return torch.device("cuda", torch.cuda.current_device())
+
+
+def as_device(device: Any) -> torch.device:
+    return device if isinstance(device, torch.device) else torch.device(device)
+
+
+def on(t: Optional[torch.Tensor], dev: torch.device, dtype: Optional[torch.dtype] = None) -> Optional[torch.Tensor]:
+    """``t`` contiguous on ``dev`` (and ``dtype``), copying only when needed."""
+    if t is None:
+        return None
+    if dtype is not None and t.dtype != dtype:
+        t = t.to(dtype)
+    if t.device != dev:
+        t = t.to(dev, non_blocking=True)
+    return t.contiguous()
+
+
+def back(t: torch.Tensor, device: torch.device) -> torch.Tensor:
+    """Move a result to the caller's device."""
+    return t if t.device == device else t.to(device)
+
+
+def scratch(nbytes: int, dev: torch.device) -> torch.Tensor:
+    """Scratch buffer from the caching allocator (at least 256 bytes, 256-byte aligned)."""
+    return torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=dev)

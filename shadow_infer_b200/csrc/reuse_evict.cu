@@ -1,0 +1,285 @@
+// Reuse scatter and in-bucket eviction.
+//
+//  * skv_apply_reuse   -- PackedKVCache.apply_reuse_mask (shadowinfer/shadowkv/
+//                         packed_kv_cache.py:753-854): per current entry with the reuse
+//                         flag, copy the previous step's row (payload + scales) when the
+//                         previous cache holds the entry in the same precision; count the
+//                         cross-precision ones.  One warp per 32 entries, ballot over the
+//                         flags, then the warp copies each selected row with 16-byte vectors.
+//  * skv_evict_count / skv_evict_compact -- PackedKVCache.evict (packed_kv_cache.py:666-740):
+//                         stable compaction of every bucket without the evicted (t,h): a
+//                         tile-count pass, then a scan + row-move pass into new buckets.
+#include "skv_common.cuh"
+
+namespace skv {
+
+__global__ void __launch_bounds__(256) reuse_kernel(Buckets cur, const int32_t* __restrict__ cur_slot,
+                                                    int S, Buckets prev, const int32_t* __restrict__ prev_slot,
+                                                    int S_prev, const uint8_t* __restrict__ mask, int B,
+                                                    int H, int D, int NG, long long* __restrict__ stats) {
+    const int lane = threadIdx.x & 31;
+    const int64_t n = (int64_t)S * H;
+    const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+    long long applied = 0, skipped = 0;
+    for (int64_t base = (((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5) * 32; base < n;
+         base += nwarps * 32) {
+        const int64_t e = base + lane;
+        int32_t cs = -1, ps = -1;
+        bool copy = false;
+        if (e < n && mask[e]) {
+            cs = cur_slot[e];
+            if (cs >= 0) {
+                const int64_t t = e / H, h = e - t * H;
+                ps = t < S_prev ? prev_slot[t * H + h] : -1;
+                if (ps >= 0) {
+                    if (slot_code(ps) == slot_code(cs)) copy = true;
+                    else skipped += 1;
+                }
+            }
+        }
+        unsigned todo = __ballot_sync(0xffffffffu, copy);
+        applied += copy ? 1 : 0;
+        while (todo) {
+            const int src = __ffs(todo) - 1;
+            todo &= todo - 1;
+            const int32_t c = __shfl_sync(0xffffffffu, cs, src);
+            const int32_t p = __shfl_sync(0xffffffffu, ps, src);
+            const int code = slot_code(c);
+            const int64_t cpos = slot_pos(c), ppos = slot_pos(p);
+            const int64_t rb = payload_row_bytes(code, B, D);
+            const skv_bucket& cb = cur.b[code];
+            const skv_bucket& pb = prev.b[code];
+            warp_copy(reinterpret_cast<uint8_t*>(cb.k) + cpos * rb,
+                      reinterpret_cast<const uint8_t*>(pb.k) + ppos * rb, rb, lane);
+            warp_copy(reinterpret_cast<uint8_t*>(cb.v) + cpos * rb,
+                      reinterpret_cast<const uint8_t*>(pb.v) + ppos * rb, rb, lane);
+            const int64_t sf = scale_row_floats(code, B, D, NG);
+            if (sf) {
+                for (int64_t i = lane; i < sf; i += 32) {
+                    cb.scale_k[cpos * sf + i] = pb.scale_k[ppos * sf + i];
+                    cb.scale_v[cpos * sf + i] = pb.scale_v[ppos * sf + i];
+                }
+            }
+        }
+    }
+    applied = warp_sum_ll(applied);
+    skipped = warp_sum_ll(skipped);
+    if (lane == 0) {
+        if (applied) atomicAdd((unsigned long long*)&stats[0], (unsigned long long)applied);
+        if (skipped) atomicAdd((unsigned long long*)&stats[1], (unsigned long long)skipped);
+    }
+}
+
+// ---------------------------------------------------------------------------------------
+// evict
+// ---------------------------------------------------------------------------------------
+constexpr int kEvThreads = 256;
+constexpr int kEvItems = 4;
+constexpr int kEvTile = kEvThreads * kEvItems;
+
+__device__ __forceinline__ bool evicted_flag(const uint8_t* __restrict__ mask, int64_t f, int S, int H) {
+    const int64_t h = f / S, t = f - h * S;
+    return mask[t * H + h] != 0;
+}
+
+// Block-wide exclusive scan of one int per thread; returns the block total.
+__device__ __forceinline__ int block_exclusive_scan(int x, int& total) {
+    __shared__ int s_w[kEvThreads / 32];
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    int inc = x;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, inc, o);
+        if (lane >= o) inc += y;
+    }
+    if (lane == 31) s_w[w] = inc;
+    __syncthreads();
+    int before = 0;
+    total = 0;
+#pragma unroll
+    for (int k = 0; k < kEvThreads / 32; ++k) {
+        if (k < w) before += s_w[k];
+        total += s_w[k];
+    }
+    __syncthreads();
+    return before + inc - x;
+}
+
+__global__ void __launch_bounds__(kEvThreads) evict_count_kernel(Buckets src, const uint8_t* __restrict__ mask,
+                                                                 int S, int H, int max_tiles,
+                                                                 int* __restrict__ tile_kept,
+                                                                 long long* __restrict__ kept) {
+    const int p = blockIdx.y;
+    const int64_t count = src.b[p].count;
+    const int64_t first = (int64_t)blockIdx.x * kEvTile;
+    if (first >= count) return;
+    int keep = 0;
+    for (int j = 0; j < kEvItems; ++j) {
+        const int64_t i = first + (int64_t)threadIdx.x * kEvItems + j;
+        if (i < count && !evicted_flag(mask, src.b[p].flat[i], S, H)) ++keep;
+    }
+    int total;
+    block_exclusive_scan(keep, total);
+    if (threadIdx.x == 0) {
+        tile_kept[(int64_t)p * max_tiles + blockIdx.x] = total;
+        const int64_t in_tile = count - first < kEvTile ? count - first : kEvTile;
+        atomicAdd((unsigned long long*)&kept[p], (unsigned long long)total);
+        atomicAdd((unsigned long long*)&kept[4], (unsigned long long)(in_tile - total));
+    }
+}
+
+__global__ void __launch_bounds__(kEvThreads) evict_compact_kernel(
+    Buckets src, Buckets dst, const uint8_t* __restrict__ mask, int32_t* __restrict__ slot, int B, int S,
+    int H, int D, int NG, int max_tiles, const int* __restrict__ tile_kept) {
+    const int p = blockIdx.y;
+    const int64_t count = src.b[p].count;
+    const int64_t first = (int64_t)blockIdx.x * kEvTile;
+    // a bucket that loses nothing is passed with dst.count == src.count and left untouched
+    if (first >= count || dst.b[p].count == count) return;
+    __shared__ int s_red[kEvThreads / 32];
+    __shared__ int32_t s_new[kEvTile];
+    // prefix of kept entries in earlier tiles of this bucket
+    int pre = 0;
+    for (int t = threadIdx.x; t < (int)blockIdx.x; t += kEvThreads) pre += tile_kept[(int64_t)p * max_tiles + t];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) pre += __shfl_xor_sync(0xffffffffu, pre, o);
+    if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = pre;
+    __syncthreads();
+    int prefix = 0;
+    for (int k = 0; k < kEvThreads / 32; ++k) prefix += s_red[k];
+    __syncthreads();
+
+    int64_t f[kEvItems];
+    bool keep[kEvItems];
+    int nkeep = 0;
+    for (int j = 0; j < kEvItems; ++j) {
+        const int64_t i = first + (int64_t)threadIdx.x * kEvItems + j;
+        keep[j] = false;
+        f[j] = -1;
+        if (i < count) {
+            f[j] = src.b[p].flat[i];
+            keep[j] = !evicted_flag(mask, f[j], S, H);
+            nkeep += keep[j];
+        }
+    }
+    int total;
+    int run = block_exclusive_scan(nkeep, total) + prefix;
+    for (int j = 0; j < kEvItems; ++j) {
+        const int li = threadIdx.x * kEvItems + j;
+        s_new[li] = -1;
+        if (f[j] < 0) continue;
+        const int64_t h = f[j] / S, t = f[j] - h * S;
+        if (keep[j]) {
+            dst.b[p].flat[run] = f[j];
+            slot[t * H + h] = make_slot(run, p);
+            s_new[li] = run;
+            ++run;
+        } else {
+            slot[t * H + h] = -1;
+        }
+    }
+    __syncthreads();
+    // move the kept rows, one warp per entry
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const int64_t rb = payload_row_bytes(p, B, D);
+    const int64_t sf = scale_row_floats(p, B, D, NG);
+    const int64_t in_tile = count - first < kEvTile ? count - first : kEvTile;
+    for (int li = w; li < in_tile; li += kEvThreads / 32) {
+        const int32_t np = s_new[li];
+        if (np < 0) continue;
+        const int64_t op = first + li;
+        warp_copy(reinterpret_cast<uint8_t*>(dst.b[p].k) + np * rb,
+                  reinterpret_cast<const uint8_t*>(src.b[p].k) + op * rb, rb, lane);
+        warp_copy(reinterpret_cast<uint8_t*>(dst.b[p].v) + np * rb,
+                  reinterpret_cast<const uint8_t*>(src.b[p].v) + op * rb, rb, lane);
+        for (int64_t i = lane; i < sf; i += 32) {
+            dst.b[p].scale_k[np * sf + i] = src.b[p].scale_k[op * sf + i];
+            dst.b[p].scale_v[np * sf + i] = src.b[p].scale_v[op * sf + i];
+        }
+    }
+}
+
+static int64_t max_count(const skv_bucket* b) {
+    int64_t m = 0;
+    for (int p = 0; p < kNumBuckets; ++p) m = b[p].count > m ? b[p].count : m;
+    return m;
+}
+
+}  // namespace skv
+
+using namespace skv;
+
+extern "C" {
+
+int skv_apply_reuse(const skv_bucket* cur, const int32_t* cur_slot, int S, const skv_bucket* prev,
+                    const int32_t* prev_slot, int S_prev, const uint8_t* reuse_mask, int B, int H, int D,
+                    int int4_group, int64_t* stats, void* stream) {
+    if (!cur || !prev || !cur_slot || !prev_slot || !reuse_mask || !stats)
+        return fail(SKV_ERR_INVALID_ARGUMENT, "apply_reuse: null pointer");
+    if (B <= 0 || H <= 0 || S <= 0 || S_prev <= 0 || D <= 0)
+        return fail(SKV_ERR_INVALID_ARGUMENT, "apply_reuse: bad shape");
+    cudaStream_t s = as_stream(stream);
+    if (cudaMemsetAsync(stats, 0, 2 * sizeof(int64_t), s) != cudaSuccess)
+        return fail(SKV_ERR_CUDA, "apply_reuse: memset failed");
+    const int G = int4_group > 0 && D % int4_group == 0 ? int4_group : D;
+    Buckets c, p;
+    for (int i = 0; i < kNumBuckets; ++i) {
+        c.b[i] = cur[i];
+        p.b[i] = prev[i];
+    }
+    const int64_t n = (int64_t)S * H;
+    const int64_t want = (n + 255) / 256;
+    const int blocks = (int)(want < (int64_t)sm_count() * 8 ? want : (int64_t)sm_count() * 8);
+    reuse_kernel<<<blocks > 0 ? blocks : 1, 256, 0, s>>>(c, cur_slot, S, p, prev_slot, S_prev, reuse_mask, B, H, D,
+                                                         D / G, (long long*)stats);
+    return check_launch("apply_reuse");
+}
+
+size_t skv_evict_scratch_bytes(int64_t max_bucket_entries) {
+    const int64_t tiles = (max_bucket_entries + kEvTile - 1) / kEvTile;
+    return (size_t)(tiles > 0 ? tiles : 1) * kNumBuckets * sizeof(int);
+}
+
+int skv_evict_count(const skv_bucket* src, const uint8_t* evict_mask, int S, int H, int64_t* kept,
+                    void* scratch, size_t scratch_bytes, void* stream) {
+    if (!src || !evict_mask || !kept || !scratch) return fail(SKV_ERR_INVALID_ARGUMENT, "evict_count: null pointer");
+    if (S <= 0 || H <= 0) return fail(SKV_ERR_INVALID_ARGUMENT, "evict_count: bad shape");
+    const int64_t m = max_count(src);
+    if (scratch_bytes < skv_evict_scratch_bytes(m))
+        return fail(SKV_ERR_SCRATCH, "evict_count: scratch %zu < %zu", scratch_bytes, skv_evict_scratch_bytes(m));
+    cudaStream_t s = as_stream(stream);
+    if (cudaMemsetAsync(kept, 0, 5 * sizeof(int64_t), s) != cudaSuccess)
+        return fail(SKV_ERR_CUDA, "evict_count: memset failed");
+    if (m == 0) return SKV_OK;
+    Buckets b;
+    for (int i = 0; i < kNumBuckets; ++i) b.b[i] = src[i];
+    const int tiles = (int)((m + kEvTile - 1) / kEvTile);
+    evict_count_kernel<<<dim3(tiles, kNumBuckets), kEvThreads, 0, s>>>(b, evict_mask, S, H, tiles,
+                                                                       reinterpret_cast<int*>(scratch),
+                                                                       (long long*)kept);
+    return check_launch("evict_count");
+}
+
+int skv_evict_compact(const skv_bucket* src, const skv_bucket* dst, const uint8_t* evict_mask, int32_t* slot,
+                      int B, int S, int H, int D, int int4_group, void* scratch, size_t scratch_bytes,
+                      void* stream) {
+    if (!src || !dst || !evict_mask || !slot || !scratch)
+        return fail(SKV_ERR_INVALID_ARGUMENT, "evict_compact: null pointer");
+    if (B <= 0 || S <= 0 || H <= 0 || D <= 0) return fail(SKV_ERR_INVALID_ARGUMENT, "evict_compact: bad shape");
+    const int64_t m = max_count(src);
+    if (scratch_bytes < skv_evict_scratch_bytes(m))
+        return fail(SKV_ERR_SCRATCH, "evict_compact: scratch too small");
+    if (m == 0) return SKV_OK;
+    const int G = int4_group > 0 && D % int4_group == 0 ? int4_group : D;
+    Buckets a, b;
+    for (int i = 0; i < kNumBuckets; ++i) {
+        a.b[i] = src[i];
+        b.b[i] = dst[i];
+    }
+    const int tiles = (int)((m + kEvTile - 1) / kEvTile);
+    evict_compact_kernel<<<dim3(tiles, kNumBuckets), kEvThreads, 0, as_stream(stream)>>>(
+        a, b, evict_mask, slot, B, S, H, D, D / G, tiles, reinterpret_cast<const int*>(scratch));
+    return check_launch("evict_compact");
+}
+
+}  // extern "C"

@@ -1,0 +1,19 @@
+"""ShadowKV packed-KV data plane on B200 (drop-in for ``shadowinfer.shadowkv``'s data plane)."""
+
+from .packed_kv_cache import PackedKVCache
+from .precision_plan import (
+    CODE_PRECISIONS,
+    EVICTED,
+    PRECISION_CODES,
+    PRECISION_ORDER,
+    PrecisionPlan,
+    codes_to_map,
+    map_to_codes,
+)
+from .rd_allocator import admit_budget, admit_codes, entry_bytes, kv_sensitivity, predict_codes_bytes
+
+__all__ = [
+    "PackedKVCache", "PrecisionPlan", "map_to_codes", "codes_to_map", "PRECISION_ORDER", "PRECISION_CODES",
+    "CODE_PRECISIONS", "EVICTED", "admit_codes", "admit_budget", "entry_bytes", "kv_sensitivity",
+    "predict_codes_bytes",
+]

@@ -1,0 +1,558 @@
+"""Byte-level packed KV cache (drop-in for ``shadowinfer/shadowkv/packed_kv_cache.py``).
+
+Same class, methods, ``packed_data`` schema and byte accounting as the
+reference ``PackedKVCache``; every data-plane operation is one or two sm_100a
+kernels behind the C ABI:
+
+============================  ===============================  ======================
+reference method              kernel(s)                        reference lines
+============================  ===============================  ======================
+``pack`` (plan or map)        skv_plan_bucket + skv_pack       packed_kv_cache.py:44-388
+``unpack``                    skv_unpack                       :535-577, :636-656
+``apply_reuse_mask``          skv_apply_reuse                  :753-854
+``evict``                     skv_evict_count + _compact       :666-740
+============================  ===============================  ======================
+
+Per bucket the cache also keeps the device ``flat`` index list (``h*S+t`` in
+bucket order) and one ``slot`` map (``int32 [S*H]``: ``(pos << 2) | code``, -1
+when absent), so no operation rebuilds Python lists.  ``indices`` and
+``byte_offsets`` in ``packed_data`` are materialised on first access.
+Tensors stay on the device the caller packed from; host tensors are computed
+on the current CUDA device and copied back.
+"""
+
+from __future__ import annotations
+
+from typing import Any, Callable, Dict, List, Optional, Set, Tuple
+
+import torch
+
+from .. import _lib
+from .._device import back, compute_device, on, scratch
+from .precision_plan import EVICTED, PRECISION_ORDER, PrecisionPlan, _entries, map_to_codes
+
+_LAZY = object()
+_CODE = {p: i for i, p in enumerate(PRECISION_ORDER)}
+
+
+class _Bucket(dict):
+    """One ``packed_data`` entry; ``indices`` / ``byte_offsets`` materialise on first read."""
+
+    __slots__ = ("_resolvers",)
+
+    def __init__(self, data: Dict[str, Any], resolvers: Dict[str, Callable[[], Any]]):
+        dict.__init__(self, data)
+        self._resolvers = dict(resolvers)
+        for key in resolvers:
+            dict.__setitem__(self, key, _LAZY)
+
+    def set_lazy(self, key: str, fn: Callable[[], Any]) -> None:
+        self._resolvers[key] = fn
+        dict.__setitem__(self, key, _LAZY)
+
+    def __getitem__(self, key):
+        value = dict.__getitem__(self, key)
+        if value is _LAZY:
+            value = self._resolvers.pop(key)()
+            dict.__setitem__(self, key, value)
+        return value
+
+    def get(self, key, default=None):
+        return self[key] if dict.__contains__(self, key) else default
+
+    def items(self):
+        return [(k, self[k]) for k in dict.keys(self)]
+
+    def values(self):
+        return [self[k] for k in dict.keys(self)]
+
+    def copy(self):
+        return {k: self[k] for k in dict.keys(self)}
+
+    def pop(self, key, *default):
+        if dict.__contains__(self, key):
+            value = self[key]
+            dict.__delitem__(self, key)
+            return value
+        if default:
+            return default[0]
+        raise KeyError(key)
+
+    def __eq__(self, other):
+        return dict(self.items()) == (dict(other.items()) if isinstance(other, dict) else other)
+
+    def __ne__(self, other):
+        return not self.__eq__(other)
+
+    __hash__ = None
+
+    def __repr__(self):
+        return repr(dict(self.items()))
+
+
+def _int4_group(head_dim: int, group_size: int) -> int:
+    if group_size < 1:
+        raise ValueError(f"int4 group_size must be >= 1, got {group_size}")
+    return group_size if head_dim % group_size == 0 else head_dim
+
+
+def _alloc_bucket(code: int, n: int, B: int, D: int, G: int, dev: torch.device) -> Dict[str, torch.Tensor]:
+    """Bucket tensors in the reference layout (packed_kv_cache.py:265-363)."""
+    if code == 0:
+        return {"k": torch.empty(n, B, D, dtype=torch.float32, device=dev),
+                "v": torch.empty(n, B, D, dtype=torch.float32, device=dev), "scale_k": None, "scale_v": None}
+    if code == 1:
+        return {"k": torch.empty(n, B, D, dtype=torch.float16, device=dev),
+                "v": torch.empty(n, B, D, dtype=torch.float16, device=dev), "scale_k": None, "scale_v": None}
+    if code == 2:
+        return {"k": torch.empty(n, B, D, dtype=torch.int8, device=dev),
+                "v": torch.empty(n, B, D, dtype=torch.int8, device=dev),
+                "scale_k": torch.empty(n, B, 1, dtype=torch.float32, device=dev),
+                "scale_v": torch.empty(n, B, 1, dtype=torch.float32, device=dev)}
+    rb = (B * D + 1) // 2
+    ng = D // G
+    return {"k": torch.empty(n * rb, dtype=torch.uint8, device=dev),
+            "v": torch.empty(n * rb, dtype=torch.uint8, device=dev),
+            "scale_k": torch.empty(n * B, ng, 1, dtype=torch.float32, device=dev),
+            "scale_v": torch.empty(n * B, ng, 1, dtype=torch.float32, device=dev)}
+
+
+def _nbytes(t: Optional[torch.Tensor]) -> int:
+    return 0 if t is None else t.numel() * t.element_size()
+
+
+def run_pack(k: torch.Tensor, v: torch.Tensor, plan: PrecisionPlan, group_size: int, dense: bool = False,
+             k_prev: Optional[torch.Tensor] = None, v_prev: Optional[torch.Tensor] = None
+             ) -> Tuple[List[Optional[Dict[str, torch.Tensor]]], Optional[torch.Tensor], Optional[torch.Tensor]]:
+    """Launch ``skv_pack`` for ``plan``; returns device buckets (+ dense working copy)."""
+    B, H, S, D = k.shape
+    dev = plan.compute_device
+    G = _int4_group(D, group_size)
+    kd = on(k.detach(), dev, torch.float32)
+    vd = on(v.detach(), dev, torch.float32)
+    buckets: List[Optional[Dict[str, torch.Tensor]]] = []
+    for code in range(4):
+        n = plan.counts[code]
+        if n == 0:
+            buckets.append(None)
+            continue
+        b = _alloc_bucket(code, n, B, D, G, dev)
+        b["flat"] = plan.bucket_flat(code)
+        b["count"] = n
+        buckets.append(b)
+    dk = dv = None
+    kp = vp = None
+    if dense:
+        dk = torch.empty(B, H, S, D, dtype=torch.float32, device=dev)
+        dv = torch.empty(B, H, S, D, dtype=torch.float32, device=dev)
+        if k_prev is not None and plan.reuse_mask_device is not None:
+            kp = on(k_prev.detach(), dev, torch.float32)
+            vp = on(v_prev.detach(), dev, torch.float32)
+    lib = _lib.load()
+    arr = _lib.buckets(buckets)
+    with torch.cuda.device(dev):
+        st = lib.skv_pack(_lib.ptr(kd), _lib.ptr(vd), B, H, S, D, group_size, _lib.ptr(plan.slot), arr,
+                          _lib.ptr(dk), _lib.ptr(dv), _lib.ptr(kp), _lib.ptr(vp),
+                          _lib.ptr(plan.reuse_mask_device) if kp is not None else None, _lib.stream_of(dev))
+    _lib.check(st, "PackedKVCache.pack")
+    return buckets, dk, dv
+
+
+class PackedKVCache:
+    """Byte-level packed KV cache storage with per-token-head precision."""
+
+    PRECISION_BITS = {"fp32": 32, "fp16": 16, "int8": 8, "int4": 4}
+
+    def __init__(self, batch_size: int, num_heads: int, seq_len: int, head_dim: int, device: Any = "cpu"):
+        self.batch_size = batch_size
+        self.num_heads = num_heads
+        self.seq_len = seq_len
+        self.head_dim = head_dim
+        self.device = device
+        self.packed_data: Dict[str, Dict[str, Any]] = {}
+        self._memory_bytes = 0
+        self._slot: Optional[torch.Tensor] = None       # device int32 [S*H]
+        self._slot_owned = False
+        self._flat: Dict[str, torch.Tensor] = {}         # device int64 per bucket
+        self._count: Dict[str, int] = {}
+        self._dev: Optional[torch.device] = None
+
+    # ------------------------------------------------------------------------------ pack
+    @classmethod
+    def pack(
+        cls,
+        k_tensor: torch.Tensor,
+        v_tensor: torch.Tensor,
+        precision_map: Optional[Dict[int, Dict[int, str]]],
+        group_size: int = 16,
+        plan: Any = None,
+        precomputed: Optional[Dict[str, Any]] = None,
+    ) -> Dict[str, Any]:
+        """Pack K/V ``[B, H, S, D]`` into byte-level buckets (packed_kv_cache.py:44-82).
+
+        Returns ``{"packed_kv", "memory_bytes", "memory_mb"}``.  ``precomputed``
+        is accepted for API compatibility; the fused kernel always quantises
+        (the reference's precomputed payloads are bit-identical to it).
+        """
+        batch_size, num_heads, seq_len, head_dim = k_tensor.shape
+        cache = cls(batch_size, num_heads, seq_len, head_dim, device=k_tensor.device)
+        cache._do_pack(k_tensor, v_tensor, precision_map, group_size=group_size, plan=plan, precomputed=precomputed)
+        return {"packed_kv": cache, "memory_bytes": cache.memory_bytes(), "memory_mb": cache.memory_mb()}
+
+    def _do_pack(self, k_tensor, v_tensor, precision_map, group_size: int = 16, plan: Any = None,
+                 precomputed: Optional[Dict[str, Any]] = None) -> None:
+        """Map path: unknown precisions -> fp16, ``evicted`` skipped (packed_kv_cache.py:84-220)."""
+        if plan is None:
+            codes = map_to_codes(precision_map or {}, self.seq_len, self.num_heads, strict=False)
+            plan = PrecisionPlan.from_codes(codes, device=k_tensor.device)
+        self._do_pack_with_plan(k_tensor, v_tensor, plan, group_size, precomputed=precomputed)
+
+    def _do_pack_with_plan(self, k_tensor, v_tensor, plan: Any, group_size: int,
+                           precomputed: Optional[Dict[str, Any]] = None) -> None:
+        """Plan-driven packing with the reference's validation (packed_kv_cache.py:222-365)."""
+        batch_size, num_heads, seq_len, head_dim = k_tensor.shape
+        if plan.seq_len != seq_len or plan.num_heads != num_heads:
+            raise ValueError(
+                "PrecisionPlan shape mismatch: plan "
+                f"(seq_len={plan.seq_len}, num_heads={plan.num_heads}) vs "
+                f"tensor (seq_len={seq_len}, num_heads={num_heads})"
+            )
+        if v_tensor.shape != k_tensor.shape:
+            raise ValueError("k_tensor and v_tensor must have identical shapes")
+        if plan.codes.device.type != k_tensor.device.type:
+            raise ValueError(
+                f"PrecisionPlan device ({plan.codes.device}) does not match KV device ({k_tensor.device})"
+            )
+        if not isinstance(plan, PrecisionPlan):
+            plan = PrecisionPlan.from_codes(plan.codes, device=plan.codes.device)
+        buckets, _, _ = run_pack(k_tensor, v_tensor, plan, group_size)
+        self._adopt(buckets, plan.slot, shared_slot=True, group_size=group_size)
+
+    def _adopt(self, buckets, slot: torch.Tensor, shared_slot: bool, group_size: int) -> None:
+        """Install device buckets as ``packed_data`` (on the cache's device)."""
+        self._dev = slot.device
+        self._slot = slot
+        self._slot_owned = not shared_slot
+        self.packed_data = {}
+        self._flat = {}
+        self._count = {}
+        total = 0
+        G = _int4_group(self.head_dim, group_size)
+        for code, p in enumerate(PRECISION_ORDER):
+            b = buckets[code]
+            if b is None:
+                continue
+            self._flat[p] = b["flat"]
+            self._count[p] = int(b["count"])
+            data = {key: (None if b[key] is None else back(b[key], self.device))
+                    for key in ("k", "v", "scale_k", "scale_v")}
+            if code == 3:
+                data["group_size"] = G
+                data["num_groups"] = self.head_dim // G
+            bucket = _Bucket(data, {"indices": self._indices_fn(p)})
+            if code == 3:
+                bucket.set_lazy("byte_offsets", self._offsets_fn(p))
+            self.packed_data[p] = bucket
+            for key in ("k", "v", "scale_k", "scale_v"):
+                total += _nbytes(data[key])
+        self._memory_bytes = total
+
+    def _indices_fn(self, p: str) -> Callable[[], List[Tuple[int, int]]]:
+        flat, S = self._flat[p], self.seq_len
+        return lambda: _entries(flat, S)
+
+    def _offsets_fn(self, p: str) -> Callable[[], List[Tuple[int, int, int, int]]]:
+        n = self._count[p]
+        rb = (self.batch_size * self.head_dim + 1) // 2
+        return lambda: [(i * rb, (i + 1) * rb, i * rb, (i + 1) * rb) for i in range(n)]
+
+    @staticmethod
+    def _pack_int4_rows(quantized: torch.Tensor) -> Tuple[torch.Tensor, int]:
+        """Row-wise int4 nibble packing of ``[n, ...]`` int8 codes (packed_kv_cache.py:367-388)."""
+        if quantized.shape[0] == 0:
+            return torch.empty(0, 0, dtype=torch.uint8, device=quantized.device), 0
+        rows = quantized.reshape(quantized.shape[0], -1)
+        off = (rows + 8).to(torch.uint8)
+        if off.shape[1] % 2:
+            off = torch.cat([off, torch.zeros(off.shape[0], 1, dtype=torch.uint8, device=off.device)], dim=1)
+        packed = (off[:, 0::2] << 4) | (off[:, 1::2] & 0x0F)
+        return packed, packed.shape[1]
+
+    # ----------------------------------------------------------------------- device state
+    def _ensure_state(self) -> torch.device:
+        """Device slot/flat state, rebuilt from ``indices`` if the cache was filled by hand."""
+        if self._slot is not None:
+            return self._dev
+        dev = compute_device(*[d.get("k") for d in self.packed_data.values()])
+        slot = torch.full((self.seq_len * self.num_heads,), -1, dtype=torch.int32)
+        for p, data in self.packed_data.items():
+            idx = torch.tensor(list(data["indices"]), dtype=torch.int64).reshape(-1, 2)
+            n = idx.shape[0]
+            if n:
+                slot[idx[:, 0] * self.num_heads + idx[:, 1]] = (torch.arange(n, dtype=torch.int32) << 2) | _CODE[p]
+            self._flat[p] = (idx[:, 1] * self.seq_len + idx[:, 0]).to(dev)
+            self._count[p] = n
+        self._slot = slot.to(dev)
+        self._slot_owned = True
+        self._dev = dev
+        return dev
+
+    def _device_buckets(self, dev: torch.device) -> List[Optional[Dict[str, Any]]]:
+        out: List[Optional[Dict[str, Any]]] = []
+        for p in PRECISION_ORDER:
+            data = self.packed_data.get(p)
+            if data is None or self._count.get(p, 0) == 0:
+                out.append(None)
+                continue
+            out.append({"k": on(data["k"], dev), "v": on(data["v"], dev),
+                        "scale_k": on(data["scale_k"], dev), "scale_v": on(data["scale_v"], dev),
+                        "flat": self._flat[p].to(dev), "count": self._count[p]})
+        return out
+
+    def _int4_group_of(self) -> int:
+        d = self.packed_data.get("int4")
+        return int(d["group_size"]) if d is not None else self.head_dim
+
+    # ---------------------------------------------------------------------------- unpack
+    def unpack(self) -> Tuple[torch.Tensor, torch.Tensor]:
+        """Zero-filled float32 ``[B,H,S,D]`` K and V from all buckets (packed_kv_cache.py:535-577)."""
+        shape = (self.batch_size, self.num_heads, self.seq_len, self.head_dim)
+        if not self.packed_data:
+            k_out = torch.zeros(shape, dtype=torch.float32, device=self.device)
+            return k_out, torch.zeros_like(k_out)
+        dev = self._ensure_state()
+        k_out = torch.empty(shape, dtype=torch.float32, device=dev)
+        v_out = torch.empty(shape, dtype=torch.float32, device=dev)
+        arr = _lib.buckets(self._device_buckets(dev))
+        lib = _lib.load()
+        with torch.cuda.device(dev):
+            st = lib.skv_unpack(arr, _lib.ptr(self._slot.to(dev)), self.batch_size, self.num_heads, self.seq_len,
+                                self.head_dim, self._int4_group_of(), _lib.ptr(k_out), _lib.ptr(v_out),
+                                _lib.stream_of(dev))
+        _lib.check(st, "PackedKVCache.unpack")
+        return back(k_out, torch.device(self.device)), back(v_out, torch.device(self.device))
+
+    def unpack_reference(self) -> Tuple[torch.Tensor, torch.Tensor]:
+        """Independent torch restatement of the per-entry golden unpack (packed_kv_cache.py:579-634).
+
+        Kept for cross-checking ``unpack``; it uses plain torch indexing, not the kernels.
+        """
+        B, H, S, D = self.batch_size, self.num_heads, self.seq_len, self.head_dim
+        k_out = torch.zeros(B, H, S, D, dtype=torch.float32, device=self.device)
+        v_out = torch.zeros_like(k_out)
+        for p, data in self.packed_data.items():
+            idx = torch.tensor(list(data["indices"]), dtype=torch.int64, device=self.device).reshape(-1, 2)
+            n = idx.shape[0]
+            if n == 0:
+                continue
+            vals = []
+            for key in ("k", "v"):
+                x = data[key]
+                if p in ("fp32", "fp16"):
+                    y = x.float()
+                elif p == "int8":
+                    y = x.float() * data["scale_" + key]
+                else:
+                    rows = x.reshape(n, -1)
+                    nib = torch.stack([(rows >> 4) & 0x0F, rows & 0x0F], dim=-1).reshape(n, -1)[:, : B * D]
+                    g, ng = data["group_size"], data["num_groups"]
+                    y = ((nib.to(torch.int16) - 8).float().reshape(n, B, ng, g)
+                         * data["scale_" + key].reshape(n, B, ng, 1)).reshape(n, B, D)
+                vals.append(y.permute(1, 0, 2))
+            k_out[:, idx[:, 1], idx[:, 0], :] = vals[0]
+            v_out[:, idx[:, 1], idx[:, 0], :] = vals[1]
+        return k_out, v_out
+
+    # ------------------------------------------------------------------------ accounting
+    def memory_bytes(self) -> int:
+        """Actual byte-level memory usage."""
+        return self._memory_bytes
+
+    def memory_mb(self) -> float:
+        return self._memory_bytes / (1024.0 * 1024.0)
+
+    def _compute_data_bytes(self) -> int:
+        total = 0
+        for data in self.packed_data.values():
+            for key in ("k", "v", "scale_k", "scale_v"):
+                total += _nbytes(data.get(key))
+        return total
+
+    def data_plane_bytes(self) -> int:
+        """Tensor storage bytes only (packed_kv_cache.py:865-867)."""
+        return self._compute_data_bytes()
+
+    def resident_bytes(self) -> int:
+        """Data bytes + 48 bytes of metadata per token-head (packed_kv_cache.py:869-878)."""
+        if not self.packed_data:
+            return 0
+        n = 0
+        for p, data in self.packed_data.items():
+            n += self._count[p] if p in self._count else len(data["indices"])
+        return self._compute_data_bytes() + 48 * n
+
+    # ----------------------------------------------------------------------------- evict
+    def evict(self, token_head_set: Any) -> int:
+        """Remove token-heads from their buckets, keeping order (packed_kv_cache.py:666-740).
+
+        ``token_head_set``: set of ``(t, h)`` or a bool ``[S, H]`` mask.  Returns
+        the number of entries removed; buckets that become empty are deleted.
+        """
+        if token_head_set is None or not self.packed_data:
+            return 0
+        if not torch.is_tensor(token_head_set) and not token_head_set:
+            return 0
+        dev = self._ensure_state()
+        mask = self._entry_mask(token_head_set, dev)
+        src = self._device_buckets(dev)
+        lib = _lib.load()
+        max_n = max([b["count"] for b in src if b is not None] + [0])
+        scr = scratch(lib.skv_evict_scratch_bytes(max_n), dev)
+        kept_d = torch.empty(5, dtype=torch.int64, device=dev)
+        src_arr = _lib.buckets(src)
+        stream = _lib.stream_of(dev)
+        with torch.cuda.device(dev):
+            st = lib.skv_evict_count(src_arr, _lib.ptr(mask), self.seq_len, self.num_heads, _lib.ptr(kept_d),
+                                     _lib.ptr(scr), scr.numel(), stream)
+        _lib.check(st, "PackedKVCache.evict")
+        kept = [int(x) for x in kept_d.tolist()]
+        removed = kept[4]
+        if removed == 0:
+            return 0
+        if not self._slot_owned:
+            self._slot = self._slot.clone()
+            self._slot_owned = True
+        G = self._int4_group_of()
+        dst: List[Optional[Dict[str, Any]]] = []
+        work: List[Optional[Dict[str, Any]]] = []
+        for code, p in enumerate(PRECISION_ORDER):
+            b = src[code]
+            if b is None or kept[code] == b["count"]:
+                dst.append(b)           # untouched bucket: dst.count == src.count
+                work.append(None)
+                continue
+            work.append(b)
+            if kept[code] == 0:
+                dst.append(None)
+                continue
+            nb = _alloc_bucket(code, kept[code], self.batch_size, self.head_dim, G, dev)
+            nb["flat"] = torch.empty(kept[code], dtype=torch.int64, device=dev)
+            nb["count"] = kept[code]
+            dst.append(nb)
+        with torch.cuda.device(dev):
+            st = lib.skv_evict_compact(src_arr, _lib.buckets(dst), _lib.ptr(mask), _lib.ptr(self._slot),
+                                       self.batch_size, self.seq_len, self.num_heads, self.head_dim, G,
+                                       _lib.ptr(scr), scr.numel(), stream)
+        _lib.check(st, "PackedKVCache.evict")
+        for code, p in enumerate(PRECISION_ORDER):
+            if work[code] is None:
+                continue
+            if dst[code] is None:
+                del self.packed_data[p]
+                del self._flat[p]
+                del self._count[p]
+                continue
+            nb = dst[code]
+            data = self.packed_data[p]
+            for key in ("k", "v", "scale_k", "scale_v"):
+                dict.__setitem__(data, key, None if nb[key] is None else back(nb[key], torch.device(self.device)))
+            self._flat[p] = nb["flat"]
+            self._count[p] = nb["count"]
+            data.set_lazy("indices", self._indices_fn(p)) if isinstance(data, _Bucket) else None
+            if isinstance(data, _Bucket) and p == "int4":
+                data.set_lazy("byte_offsets", self._offsets_fn(p))
+        self._memory_bytes = self._compute_data_bytes()
+        return removed
+
+    def _entry_mask(self, entries: Any, dev: torch.device) -> torch.Tensor:
+        S, H = self.seq_len, self.num_heads
+        if torch.is_tensor(entries):
+            m = torch.zeros(S, H, dtype=torch.uint8, device=dev)
+            s, h = min(S, entries.shape[0]), min(H, entries.shape[1])
+            m[:s, :h] = on(entries[:s, :h], dev).to(torch.uint8)
+            return m
+        keys = [(int(t), int(h)) for (t, h) in entries if 0 <= t < S and 0 <= h < H]
+        m = torch.zeros(S * H, dtype=torch.uint8)
+        if keys:
+            idx = torch.tensor(keys, dtype=torch.int64)
+            m[idx[:, 0] * H + idx[:, 1]] = 1
+        return m.view(S, H).to(dev, non_blocking=True)
+
+    def _precision_for(self, token_idx: int, head_idx: int) -> str:
+        """Bucket holding ``(t, h)``; missing entries are evicted (packed_kv_cache.py:742-751)."""
+        if not self.packed_data or not (0 <= token_idx < self.seq_len and 0 <= head_idx < self.num_heads):
+            return EVICTED
+        self._ensure_state()
+        s = int(self._slot[token_idx * self.num_heads + head_idx].item())
+        return EVICTED if s < 0 else PRECISION_ORDER[s & 3]
+
+    # ----------------------------------------------------------------------------- reuse
+    def apply_reuse_mask(
+        self,
+        kv_previous_packed: "PackedKVCache",
+        reuse_mask: Any,
+        return_stats: bool = False,
+    ) -> Optional[Dict[str, int]]:
+        """Copy same-precision reused rows from the previous cache (packed_kv_cache.py:753-854).
+
+        ``reuse_mask``: ``{(t, h): bool}`` or a bool ``[S, H]`` tensor.
+        Cross-precision entries keep their values and count as ``skipped_precision``.
+        """
+        prev = kv_previous_packed
+        if (self.batch_size != prev.batch_size or self.num_heads != prev.num_heads
+                or self.head_dim != prev.head_dim):
+            raise ValueError(
+                "packed cache shape mismatch for reuse: "
+                f"current=({self.batch_size},{self.num_heads},{self.head_dim}) "
+                f"previous=({prev.batch_size},{prev.num_heads},{prev.head_dim})"
+            )
+        cur4 = self.packed_data.get("int4")
+        prev4 = prev.packed_data.get("int4")
+        if cur4 is not None and prev4 is not None and cur4["group_size"] != prev4["group_size"]:
+            raise ValueError(
+                "INT4 group_size mismatch for reuse: "
+                f"current={cur4['group_size']} previous={prev4['group_size']}"
+            )
+        stats = {"applied": 0, "skipped_precision": 0}
+        empty_mask = reuse_mask is None or (not torch.is_tensor(reuse_mask) and not reuse_mask)
+        if empty_mask or not prev.packed_data or not self.packed_data:
+            return stats if return_stats else None
+        dev = self._ensure_state()
+        prev._ensure_state()
+        mask = self._entry_mask_from_reuse(reuse_mask, dev)
+        cur_b = self._device_buckets(dev)
+        prev_b = prev._device_buckets(dev)
+        stats_d = torch.empty(2, dtype=torch.int64, device=dev)
+        lib = _lib.load()
+        with torch.cuda.device(dev):
+            st = lib.skv_apply_reuse(_lib.buckets(cur_b), _lib.ptr(self._slot), self.seq_len, _lib.buckets(prev_b),
+                                     _lib.ptr(prev._slot.to(dev)), prev.seq_len, _lib.ptr(mask), self.batch_size,
+                                     self.num_heads, self.head_dim, self._int4_group_of(), _lib.ptr(stats_d),
+                                     _lib.stream_of(dev))
+        _lib.check(st, "PackedKVCache.apply_reuse_mask")
+        # write back when the payload lives elsewhere (host caches, non-contiguous views)
+        for code, p in enumerate(PRECISION_ORDER):
+            b = cur_b[code]
+            if b is None:
+                continue
+            data = self.packed_data[p]
+            for key in ("k", "v", "scale_k", "scale_v"):
+                orig = data[key]
+                if orig is not None and b[key] is not orig:
+                    orig.copy_(b[key].view(orig.shape))
+        if not return_stats:
+            return None
+        a, s = stats_d.tolist()
+        return {"applied": int(a), "skipped_precision": int(s)}
+
+    def _entry_mask_from_reuse(self, reuse_mask: Any, dev: torch.device) -> torch.Tensor:
+        if torch.is_tensor(reuse_mask):
+            return self._entry_mask(reuse_mask, dev)
+        return self._entry_mask([key for key, flag in reuse_mask.items() if flag], dev)
+
+    def __repr__(self) -> str:
+        return (
+            f"PackedKVCache(batch={self.batch_size}, heads={self.num_heads}, "
+            f"seq_len={self.seq_len}, head_dim={self.head_dim}, "
+            f"memory_mb={self.memory_mb():.2f})"
+        )
