@@ -1,0 +1,405 @@
+#!/usr/bin/env python
+"""Benchmark of the ShadowKV packed-KV data plane on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+One STEP is one pass of the data plane over one layer of the cfg2 workload
+(B=1, H=32, S=8192, D=128 fp32 K/V, inputs resident in HBM):
+
+    allocate_precision_codes -> kv_sensitivity -> admit_codes (30 % fp16 budget,
+    hard eviction, 4 sink tokens) -> PrecisionPlan.from_codes (50 % reuse mask)
+    -> PackedKVCache.pack -> apply_reuse_mask (previous step's cache) -> unpack
+
+``value`` is algorithmic bytes per step / device time (GB/s).  With N GPUs
+(torchrun) every rank packs its own layer (layers are independent objects, so
+there is no collective on the data path): weak scaling, value = N layers'
+bytes / max-over-ranks time.  ``e2e`` is the same step through the public API
+from pinned host buffers (K, V, importance, reuse mask copied in; the packed
+payload copied out).  ``roofline`` covers the pack kernel (the dominant
+kernel), timed with CUDA events around each launch in the timed region.
+``--impl reference`` times the CPU restatement of the reference algorithm
+(``oracle/``) on a head slice of the same workload, on rank 0 only.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+METRIC = "packed-KV GB/s (compress+pack, unpack) & packed-attn tokens/s at 1/2/4/8 B200, % roofline"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
+    ap.add_argument("--ref-heads", type=int, default=8, help="head slice timed by the CPU reference arm")
+    return ap.parse_args()
+
+
+# ----------------------------------------------------------------------------------- peaks
+def hbm_peak():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def committed_traffic(name: str):
+    """Per-launch DRAM bytes of a kernel from its committed ncu summary (profiles/)."""
+    path = os.path.join(REPO, "profiles", name)
+    try:
+        for line in open(path):
+            if line.startswith("traffic_bytes_per_launch:"):
+                return int(line.split(":", 1)[1].strip())
+    except OSError:
+        pass
+    return None
+
+
+# ---------------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """Samples nvidia-smi SM clocks and throttle reasons while the benchmark runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.rows = []
+        self._proc = None
+        self._thread = None
+
+    def start(self):
+        try:
+            self._proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self._proc = None
+            return
+        self._thread = threading.Thread(target=self._read, daemon=True)
+        self._thread.start()
+
+    def _read(self):
+        for line in self._proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                self.rows.append(parts)
+
+    def stop(self):
+        if self._proc is not None:
+            self._proc.terminate()
+            try:
+                self._proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self._proc.kill()
+        if self._thread is not None:
+            self._thread.join(timeout=5)
+
+    def summary(self):
+        def num(x):
+            try:
+                return float(x)
+            except ValueError:
+                return None
+        sm = [num(r[1]) for r in self.rows if num(r[1])]
+        mx = [num(r[2]) for r in self.rows if num(r[2])]
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        reasons = sorted({names[i] for r in self.rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.rows)}
+
+
+# ------------------------------------------------------------------------- algorithmic bytes
+def step_bytes(B, H, S, D, packed_bytes, n_kept, n_reuse_rows_bytes, n_reuse):
+    """Algorithmic HBM bytes of one data-plane step, per kernel."""
+    N = S * H
+    fp32 = 2 * B * H * S * D * 4
+    parts = {
+        "allocate": 4 * N + N,
+        "sensitivity": fp32 + 4 * N,
+        "admission": 9 * N + 4 * N,
+        "plan": N + N + 8 * N + 4 * N + 8 * n_reuse,
+        "pack": fp32 + N + packed_bytes + 8 * n_kept,
+        "reuse": N + 2 * n_reuse_rows_bytes,
+        "unpack": packed_bytes + 8 * n_kept + fp32,
+    }
+    return parts
+
+
+# ------------------------------------------------------------------------------- reference
+def reference_sample(I, heads: int):
+    """The CPU oracle pipeline on the first ``heads`` heads of the workload; returns (seconds, bytes)."""
+    import numpy as np
+    from oracle import shadowkv_oracle as O
+
+    k = np.ascontiguousarray(I["k"][:, :heads].numpy())
+    v = np.ascontiguousarray(I["v"][:, :heads].numpy())
+    imp = np.ascontiguousarray(I["importance"][:, :heads].numpy())
+    reuse = np.ascontiguousarray(I["reuse"][:, :heads].numpy())
+    B, H, S, D = k.shape
+    budget = I["budget"] * heads // I["k"].shape[1]
+    codes0 = O.allocate_precision_codes(imp, "balanced")
+    adm, _, _ = O.admit_codes(codes0, imp, O.kv_sensitivity(k, v), budget, B, D, sink_tokens=4,
+                              allow_eviction=True)
+    prev = O.pack(np.ascontiguousarray(I["k_prev"][:, :heads].numpy()),
+                  np.ascontiguousarray(I["v_prev"][:, :heads].numpy()), O.plan_from_codes(adm), 16)
+
+    def run():
+        t0 = time.perf_counter()
+        codes = O.allocate_precision_codes(imp, "balanced")
+        sens = O.kv_sensitivity(k, v)
+        a, _, _ = O.admit_codes(codes, imp, sens, budget, B, D, sink_tokens=4, allow_eviction=True)
+        plan = O.plan_from_codes(a, reuse)
+        cache = O.pack(k, v, plan, 16)
+        st = O.apply_reuse_mask(cache, prev, reuse)
+        O.unpack(cache)
+        dt = time.perf_counter() - t0
+        kept = sum(len(d["indices"]) for d in cache.packed_data.values())
+        flagged = reuse & (a < 4)   # previous cache holds the same codes: every flagged entry is copied
+        assert st["applied"] == int(flagged.sum())
+        reuse_bytes = int(O.code_costs(B, D, 16)[a[flagged].astype(np.int64)].sum())
+        parts = step_bytes(B, H, S, D, cache.memory_bytes(), kept, reuse_bytes, int(reuse.sum()))
+        return dt, sum(parts.values())
+
+    return run
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    from shadow_infer_b200 import workloads as W
+
+    I = W.cfg2_inputs()
+    run = reference_sample(I, args.ref_heads)
+    for _ in range(args.warmup):
+        run()
+    times, nbytes = [], 0
+    for _ in range(args.steps):
+        dt, nbytes = run()
+        times.append(dt)
+    total = sum(times)
+    value = nbytes * args.steps / total / 1e9
+    sample = (f"CPU oracle (numpy restatement of the reference path) on heads 0..{args.ref_heads - 1} of cfg2 "
+              f"(B1 S8192 D128), per step")
+    line = {
+        "metric": METRIC, "value": value, "unit": "GB/s", "impl": "reference", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * total / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "cfg2 data-plane step (head slice)", "B": 1, "H": args.ref_heads, "S": 8192,
+                   "D": 128},
+        "cpu_baseline": {"value": value, "unit": "GB/s", "cores": 1, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ------------------------------------------------------------------------------------ b200
+def run_b200(args):
+    import torch
+    import torch.distributed as dist
+
+    from shadow_infer_b200 import _lib
+    from shadow_infer_b200 import workloads as W
+    from shadow_infer_b200.shadowkv import PackedKVCache, PrecisionPlan, kv_sensitivity
+    from shadow_infer_b200.shadowkv.rd_allocator import admit_codes_device
+    from shadow_infer_b200.shadowkv.shadowkv_agent import allocate_precision_codes
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    lib = _lib.load()
+
+    # every rank packs its own layer: seed = rank
+    I = W.cfg2_inputs(seed=rank)
+    B, H, S, D = I["k"].shape
+    k, v = I["k"].to(dev), I["v"].to(dev)
+    imp, reuse = I["importance"].to(dev), I["reuse"].to(dev)
+    budget, sink = I["budget"], I["sink_tokens"]
+
+    codes0 = allocate_precision_codes(imp, "balanced")
+    adm, _ = admit_codes_device(codes0, imp, kv_sensitivity(k, v), budget, B, D, sink, True, True)
+    prev = PackedKVCache.pack(I["k_prev"].to(dev), I["v_prev"].to(dev), None, 16,
+                              plan=PrecisionPlan.from_codes(adm))["packed_kv"]
+
+    def step(kk, vv, ii, rr):
+        codes = allocate_precision_codes(ii, "balanced")
+        sens = kv_sensitivity(kk, vv)
+        a, res = admit_codes_device(codes, ii, sens, budget, B, D, sink, True, True)
+        plan = PrecisionPlan.from_codes(a, reuse_mask=rr)
+        cache = PackedKVCache.pack(kk, vv, None, 16, plan=plan)["packed_kv"]
+        cache.apply_reuse_mask(prev, rr)
+        ku, vu = cache.unpack()
+        return cache, res, ku, vu
+
+    # algorithmic bytes of the step (fixed across steps: same inputs)
+    cache, res, _, _ = step(k, v, imp, reuse)
+    stats = cache.apply_reuse_mask(prev, reuse, return_stats=True)
+    kept = sum(cache._count.values())
+    from shadow_infer_b200.shadowkv.rd_allocator import entry_bytes
+    per_code = {p: int(entry_bytes(p, B, D, 16)) for p in ("fp32", "fp16", "int8", "int4")}
+    # reused rows: entries present in both caches with the same precision; same codes here, so
+    # every flagged stored entry is copied
+    reused_bytes = 0
+    slot = cache._slot
+    flagged = reuse.reshape(-1).bool() & (slot >= 0)
+    for code, p in enumerate(("fp32", "fp16", "int8", "int4")):
+        reused_bytes += int(((slot & 3) == code)[flagged].sum().item()) * per_code[p]
+    assert stats["applied"] == int(flagged.sum().item())
+    parts = step_bytes(B, H, S, D, cache.memory_bytes(), kept, reused_bytes, int(reuse.sum().item()))
+    nbytes = sum(parts.values())
+
+    sampler = ClockSampler(local) if rank == 0 else None
+    if sampler:
+        sampler.start()
+    for _ in range(args.warmup):
+        step(k, v, imp, reuse)
+    # pack-kernel events inside the timed region
+    n_ev = args.steps
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n_ev)]
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    launches0 = lib.skv_launch_count()
+    t0.record()
+    for i in range(args.steps):
+        PackedKVCache._pack_events = evs[i]
+        step(k, v, imp, reuse)
+    PackedKVCache._pack_events = None
+    t1.record()
+    torch.cuda.synchronize()
+    launches = lib.skv_launch_count() - launches0
+    if world > 1:
+        dist.barrier()
+    elapsed_ms = t0.elapsed_time(t1)
+    pack_ms = [a.elapsed_time(b) for a, b in evs]
+    tmax = torch.tensor([elapsed_ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(tmax, op=dist.ReduceOp.MAX)
+    elapsed_ms = float(tmax.item())
+    ms_per_step = elapsed_ms / args.steps
+    value = world * nbytes * args.steps / (elapsed_ms / 1e3) / 1e9
+
+    # ---- e2e: pinned host buffers through the public API
+    hk = I["k"].pin_memory()
+    hv = I["v"].pin_memory()
+    himp = I["importance"].pin_memory()
+    hreuse = I["reuse"].pin_memory()
+    out_host = torch.empty(cache.memory_bytes() + 64, dtype=torch.uint8).pin_memory()
+    res_host = torch.empty(2, dtype=torch.int64).pin_memory()
+
+    def e2e_step():
+        kk = hk.to(dev, non_blocking=True)
+        vv = hv.to(dev, non_blocking=True)
+        ii = himp.to(dev, non_blocking=True)
+        rr = hreuse.to(dev, non_blocking=True)
+        c, r, _, _ = step(kk, vv, ii, rr)
+        off = 0
+        for d in c.packed_data.values():
+            for key in ("k", "v", "scale_k", "scale_v"):
+                t = d[key]
+                if t is None:
+                    continue
+                nb = t.numel() * t.element_size()
+                out_host[off:off + nb].copy_(t.reshape(-1).view(torch.uint8), non_blocking=True)
+                off += nb
+        res_host.copy_(r, non_blocking=True)
+        return off
+
+    e2e_steps = max(3, min(args.steps, 30))
+    for _ in range(3):
+        e2e_step()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    d2h = 0
+    for _ in range(e2e_steps):
+        d2h = e2e_step()
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
+    e2e_ms = float(e2e_ms.item())
+    h2d = (hk.numel() + hv.numel() + himp.numel()) * 4 + hreuse.numel()
+    if sampler:
+        sampler.stop()
+
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+
+    peak, peak_kind = hbm_peak()
+    pack_avg_ms = statistics.mean(pack_ms)
+    achieved = parts["pack"] / (pack_avg_ms / 1e3) / 1e9
+    traffic = committed_traffic("pack_fast_kernel_cfg2.md")
+    line = {
+        "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "cfg2 data-plane step: codes, sensitivity, budget admission + hard eviction, "
+                               "plan, compress+pack, reuse (50%), unpack",
+                   "B": B, "H": H, "S": S, "D": D, "layers_per_gpu": 1, "budget_bytes": budget,
+                   "l2": "inputs larger than L2 (K+V 268 MB per layer)",
+                   "bytes_per_step": parts},
+        "roofline": {"kernel": "pack_fast_kernel", "bound": "hbm", "achieved": achieved, "peak": peak,
+                     "unit": "GB/s", "frac": achieved / peak, "peak_source": f"{peak_kind} hbm_gbs",
+                     "traffic": traffic, "algorithmic_bytes": parts["pack"], "avg_launch_ms": pack_avg_ms},
+        "e2e": {"value": world * nbytes * e2e_steps / (e2e_ms / 1e3) / 1e9, "unit": "GB/s",
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h + 16, "steps": e2e_steps,
+                "ms_per_step": e2e_ms / e2e_steps},
+        "gpu_launches": launches,
+        "clocks": sampler.summary() if sampler else None,
+    }
+    if world == 1:
+        run = reference_sample(I, args.ref_heads)
+        run()
+        samples = [run() for _ in range(3)]
+        ref_val = sum(b for _, b in samples) / sum(t for t, _ in samples) / 1e9
+        line["cpu_baseline"] = {
+            "value": ref_val, "unit": "GB/s", "cores": 1, "kind": "port",
+            "sample": f"numpy oracle pipeline on heads 0..{args.ref_heads - 1} of the cfg2 layer, 3 runs",
+        }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_b200(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -55,6 +55,8 @@ typedef struct skv_bucket {
 const char* skv_version(void);
 const char* skv_status_string(int status);
 const char* skv_last_error(void);
+/* Number of kernels this library has launched in the process (all threads). */
+int64_t skv_launch_count(void);
 
 /* ShadowKVAgent.allocate_precision_codes  (shadowinfer/shadowkv/shadowkv_agent.py:1028-1059)
  * mode: 0 aggressive, 1 balanced, 2 conservative, other -> no adjustment. */

@@ -53,6 +53,7 @@ _SIGNATURES = {
     "skv_version": (ctypes.c_char_p, []),
     "skv_status_string": (ctypes.c_char_p, [c_int]),
     "skv_last_error": (ctypes.c_char_p, []),
+    "skv_launch_count": (c_int64, []),
     "skv_allocate_codes": (c_int, [c_void_p, c_int64, c_int, c_void_p, c_void_p]),
     "skv_kv_sensitivity": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p]),
     "skv_predict_codes_bytes": (c_int, [c_void_p, c_int64, c_int, c_int, c_int, c_void_p, c_void_p]),

@@ -2,11 +2,14 @@
 #include <stdarg.h>
 #include <stdio.h>
 
+#include <atomic>
+
 #include "skv_common.cuh"
 
 namespace skv {
 
 static thread_local char g_last_error[512] = "";
+static std::atomic<long long> g_launches{0};
 
 int fail(int status, const char* fmt, ...) {
     va_list ap;
@@ -19,6 +22,7 @@ int fail(int status, const char* fmt, ...) {
 int check_launch(const char* what) {
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return fail(SKV_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+    g_launches.fetch_add(1, std::memory_order_relaxed);
     return SKV_OK;
 }
 
@@ -54,5 +58,7 @@ const char* skv_status_string(int status) {
 }
 
 const char* skv_last_error(void) { return skv::g_last_error; }
+
+int64_t skv_launch_count(void) { return skv::g_launches.load(std::memory_order_relaxed); }
 
 }  // extern "C"

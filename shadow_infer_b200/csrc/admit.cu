@@ -21,37 +21,66 @@ namespace skv {
 // ---------------------------------------------------------------------------------------
 // sensitivity
 // ---------------------------------------------------------------------------------------
+// Generic shapes: one warp per (h, t), lanes strided over D.
 __global__ void __launch_bounds__(256) sensitivity_kernel(const float* __restrict__ k,
                                                           const float* __restrict__ v, int B, int H,
                                                           int S, int D, float* __restrict__ sens) {
     const int lane = threadIdx.x & 31;
     const int64_t n = (int64_t)H * S;
     const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
-    const bool vec = (D % 4) == 0;
     for (int64_t r = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; r < n; r += nwarps) {
         const int64_t h = r / S, t = r - h * S;
         float mk = 0.0f, mv = 0.0f;
         for (int b = 0; b < B; ++b) {
             const int64_t off = (((int64_t)b * H + h) * S + t) * D;
-            if (vec) {
-                const float4* pk = reinterpret_cast<const float4*>(k + off);
-                const float4* pv = reinterpret_cast<const float4*>(v + off);
-                for (int i = lane; i < D / 4; i += 32) {
-                    const float4 a = __ldcs(pk + i);
-                    const float4 c = __ldcs(pv + i);
-                    mk = fmaxf(mk, fmaxf(fmaxf(fabsf(a.x), fabsf(a.y)), fmaxf(fabsf(a.z), fabsf(a.w))));
-                    mv = fmaxf(mv, fmaxf(fmaxf(fabsf(c.x), fabsf(c.y)), fmaxf(fabsf(c.z), fabsf(c.w))));
-                }
-            } else {
-                for (int i = lane; i < D; i += 32) {
-                    mk = fmaxf(mk, fabsf(k[off + i]));
-                    mv = fmaxf(mv, fabsf(v[off + i]));
-                }
+            for (int i = lane; i < D; i += 32) {
+                mk = fmaxf(mk, fabsf(k[off + i]));
+                mv = fmaxf(mv, fabsf(v[off + i]));
             }
         }
         mk = warp_max(mk);
         mv = warp_max(mv);
         if (lane == 0) sens[t * H + h] = __fdiv_rn(__fadd_rn(__fmul_rn(mk, mk), __fmul_rn(mv, mv)), 2.0f);
+    }
+}
+
+// D == 128: grid x over token chunks (8 warps * RPW rows), y over heads; each warp keeps
+// 2*RPW 128-bit loads in flight per batch.
+template <int RPW>
+__global__ void __launch_bounds__(256) sensitivity_d128_kernel(const float* __restrict__ k,
+                                                               const float* __restrict__ v, int B, int H,
+                                                               int S, float* __restrict__ sens) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int h = blockIdx.y;
+    const int t0 = (blockIdx.x * 8 + warp) * RPW;
+    if (t0 >= S) return;
+    float mk[RPW], mv[RPW];
+#pragma unroll
+    for (int i = 0; i < RPW; ++i) mk[i] = mv[i] = 0.0f;
+    for (int b = 0; b < B; ++b) {
+        const int64_t base = (((int64_t)b * H + h) * S) * 128 + lane * 4;
+        float4 a[RPW], c[RPW];
+#pragma unroll
+        for (int i = 0; i < RPW; ++i) {
+            if (t0 + i < S) {
+                a[i] = __ldcs(reinterpret_cast<const float4*>(k + base + (int64_t)(t0 + i) * 128));
+                c[i] = __ldcs(reinterpret_cast<const float4*>(v + base + (int64_t)(t0 + i) * 128));
+            } else {
+                a[i] = c[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < RPW; ++i) {
+            mk[i] = fmaxf(mk[i], fmaxf(fmaxf(fabsf(a[i].x), fabsf(a[i].y)), fmaxf(fabsf(a[i].z), fabsf(a[i].w))));
+            mv[i] = fmaxf(mv[i], fmaxf(fmaxf(fabsf(c[i].x), fabsf(c[i].y)), fmaxf(fabsf(c[i].z), fabsf(c[i].w))));
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < RPW; ++i) {
+        const float a = warp_max(mk[i]);
+        const float c = warp_max(mv[i]);
+        if (lane == i && t0 + i < S)
+            sens[(int64_t)(t0 + i) * H + h] = __fdiv_rn(__fadd_rn(__fmul_rn(a, a), __fmul_rn(c, c)), 2.0f);
     }
 }
 
@@ -331,6 +360,12 @@ int skv_kv_sensitivity(const float* k, const float* v, int B, int H, int S, int 
                        void* stream) {
     if (!k || !v || !sensitivity) return fail(SKV_ERR_INVALID_ARGUMENT, "kv_sensitivity: null pointer");
     if (B <= 0 || H <= 0 || S <= 0 || D <= 0) return fail(SKV_ERR_INVALID_ARGUMENT, "kv_sensitivity: bad shape");
+    if (D == 128 && ((reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v)) & 15) == 0) {
+        constexpr int kRPW = 4;
+        const dim3 grid((unsigned)((S + 8 * kRPW - 1) / (8 * kRPW)), (unsigned)H);
+        sensitivity_d128_kernel<kRPW><<<grid, 256, 0, as_stream(stream)>>>(k, v, B, H, S, sensitivity);
+        return check_launch("kv_sensitivity");
+    }
     const int64_t n = (int64_t)H * S;
     const int64_t want = (n + 7) / 8;
     const int blocks = (int)(want < (int64_t)sm_count() * 8 ? want : (int64_t)sm_count() * 8);

@@ -123,42 +123,32 @@ __device__ __forceinline__ void pack_row(const float (&x)[VEC], int code, int64_
         for (int j = 0; j < VEC; ++j) m = fmaxf(m, fabsf(x[j]));
         m = warp_max(m);
         const float s = quant_scale(m, 127.0f);
+        const float r = __frcp_rn(s);
         uint8_t q[VEC];
 #pragma unroll
         for (int j = 0; j < VEC; ++j) {
-            const int v = quant_value(x[j], s, -128, 127);
+            const int v = quant_value_fast(x[j], s, r, -128, 127);
             q[j] = (uint8_t)(int8_t)v;
             dense[j] = (float)v;
         }
         store_bytes<VEC>(reinterpret_cast<uint8_t*>(payload) + row * D + lane * VEC, q);
         if (lane == 0) scale[row] = s;
     } else if (code == 3) {
+        // the fast path requires the group to span a power-of-two number of whole lanes
         const int NG = D / G;
-        float sc[VEC];
-        if (G >= VEC) {
-            float m = 0.0f;
+        float m = 0.0f;
 #pragma unroll
-            for (int j = 0; j < VEC; ++j) m = fmaxf(m, fabsf(x[j]));
-            const int L = G / VEC;
-            m = group_max(m, L);
-            const float s = quant_scale(m, 7.0f);
-#pragma unroll
-            for (int j = 0; j < VEC; ++j) sc[j] = s;
-            if ((lane & (L - 1)) == 0) scale[row * NG + (lane * VEC) / G] = s;
-        } else {
-            for (int sub = 0; sub < VEC / G; ++sub) {
-                float m = 0.0f;
-                for (int j = 0; j < G; ++j) m = fmaxf(m, fabsf(x[sub * G + j]));
-                const float s = quant_scale(m, 7.0f);
-                for (int j = 0; j < G; ++j) sc[sub * G + j] = s;
-                scale[row * NG + (lane * VEC) / G + sub] = s;
-            }
-        }
+        for (int j = 0; j < VEC; ++j) m = fmaxf(m, fabsf(x[j]));
+        const int L = G / VEC;
+        m = group_max(m, L);
+        const float s = quant_scale(m, 7.0f);
+        const float r = __frcp_rn(s);
+        if ((lane & (L - 1)) == 0) scale[row * NG + (lane * VEC) / G] = s;
         uint8_t bytes[VEC / 2];
 #pragma unroll
         for (int j = 0; j < VEC; j += 2) {
-            const int q0 = quant_value(x[j], sc[j], -8, 7);
-            const int q1 = quant_value(x[j + 1], sc[j + 1], -8, 7);
+            const int q0 = quant_value_fast(x[j], s, r, -8, 7);
+            const int q1 = quant_value_fast(x[j + 1], s, r, -8, 7);
             dense[j] = (float)q0;
             dense[j + 1] = (float)q1;
             bytes[j / 2] = (uint8_t)(((q0 + 8) << 4) | ((q1 + 8) & 0x0F));
@@ -173,43 +163,55 @@ __device__ __forceinline__ void pack_row(const float (&x)[VEC], int code, int64_
     }
 }
 
-template <int VEC>
+// Grid: x over token chunks of 8 warps * RPW rows, y over (b, h).  Each warp loads all
+// of its RPW K and V rows (128-bit streaming loads) before quantising any of them.
+template <int VEC, int RPW>
 __global__ void __launch_bounds__(256) pack_fast_kernel(
     const float* __restrict__ k, const float* __restrict__ v, int B, int H, int S, int G,
     const int32_t* __restrict__ slot, Buckets bk, float* __restrict__ dense_k,
     float* __restrict__ dense_v, const float* __restrict__ k_prev, const float* __restrict__ v_prev,
     const uint8_t* __restrict__ reuse) {
     constexpr int D = 32 * VEC;
-    const int lane = threadIdx.x & 31;
-    const int64_t rows = (int64_t)B * H * S;
-    const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
-    for (int64_t r = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; r < rows; r += nwarps) {
-        const int64_t t = r % S;
-        const int64_t bh = r / S;
-        const int64_t h = bh % H;
-        const int b = (int)(bh / H);
-        const int64_t e = t * H + h;
-        const int32_t sl = slot[e];
-        const int code = sl < 0 ? kCodeEvicted : slot_code(sl);
-        const int64_t pos = sl < 0 ? 0 : slot_pos(sl);
-        float xk[VEC], xv[VEC], dk[VEC], dv[VEC];
-        Vec<VEC>::load(k + r * D + lane * VEC, xk);
-        Vec<VEC>::load(v + r * D + lane * VEC, xv);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int bh = blockIdx.y;
+    const int h = bh % H, b = bh / H;
+    const int t0 = (blockIdx.x * 8 + warp) * RPW;
+    if (t0 >= S) return;
+    const int64_t base = (int64_t)bh * S * D + lane * VEC;
+    float xk[RPW][VEC], xv[RPW][VEC];
+    int32_t sl[RPW];
+#pragma unroll
+    for (int i = 0; i < RPW; ++i) {
+        const int t = t0 + i;
+        if (t < S) {
+            Vec<VEC>::load(k + base + (int64_t)t * D, xk[i]);
+            Vec<VEC>::load(v + base + (int64_t)t * D, xv[i]);
+            sl[i] = slot[t * H + h];
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < RPW; ++i) {
+        const int t = t0 + i;
+        if (t >= S) break;
+        const int code = sl[i] < 0 ? kCodeEvicted : slot_code(sl[i]);
+        const int64_t pos = sl[i] < 0 ? 0 : slot_pos(sl[i]);
+        float dk[VEC], dv[VEC];
         if (code < kCodeEvicted) {
             const skv_bucket& bb = bk.b[code];
-            pack_row<VEC>(xk, code, pos, b, B, G, bb.k, bb.scale_k, dk, lane);
-            pack_row<VEC>(xv, code, pos, b, B, G, bb.v, bb.scale_v, dv, lane);
+            pack_row<VEC>(xk[i], code, pos, b, B, G, bb.k, bb.scale_k, dk, lane);
+            pack_row<VEC>(xv[i], code, pos, b, B, G, bb.v, bb.scale_v, dv, lane);
         } else {
 #pragma unroll
             for (int j = 0; j < VEC; ++j) dk[j] = dv[j] = 0.0f;
         }
         if (dense_k) {
-            if (reuse && k_prev && reuse[e]) {
-                Vec<VEC>::load(k_prev + r * D + lane * VEC, dk);
-                Vec<VEC>::load(v_prev + r * D + lane * VEC, dv);
+            const int64_t off = base + (int64_t)t * D;
+            if (reuse && k_prev && reuse[(int64_t)t * H + h]) {
+                Vec<VEC>::load(k_prev + off, dk);
+                Vec<VEC>::load(v_prev + off, dv);
             }
-            Vec<VEC>::store(dense_k + r * D + lane * VEC, dk);
-            Vec<VEC>::store(dense_v + r * D + lane * VEC, dv);
+            Vec<VEC>::store(dense_k + off, dk);
+            Vec<VEC>::store(dense_v + off, dv);
         }
     }
 }
@@ -334,12 +336,21 @@ __device__ __forceinline__ void unpack_row(int code, int64_t pos, int b, int B, 
         load_bytes<VEC / 2>(reinterpret_cast<const uint8_t*>(payload) + pos * rb + (int64_t)b * (D / 2) +
                                 lane * (VEC / 2),
                             bytes);
+        if (G >= VEC) {
+            const float s0 = scale[row * NG + (lane * VEC) / G];
 #pragma unroll
-        for (int j = 0; j < VEC; j += 2) {
-            const float s0 = scale[row * NG + (lane * VEC + j) / G];
-            const float s1 = scale[row * NG + (lane * VEC + j + 1) / G];
-            y[j] = __fmul_rn((float)((int)(bytes[j / 2] >> 4) - 8), s0);
-            y[j + 1] = __fmul_rn((float)((int)(bytes[j / 2] & 0x0F) - 8), s1);
+            for (int j = 0; j < VEC; j += 2) {
+                y[j] = __fmul_rn((float)((int)(bytes[j / 2] >> 4) - 8), s0);
+                y[j + 1] = __fmul_rn((float)((int)(bytes[j / 2] & 0x0F) - 8), s0);
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < VEC; j += 2) {
+                const float s0 = scale[row * NG + (lane * VEC + j) / G];
+                const float s1 = scale[row * NG + (lane * VEC + j + 1) / G];
+                y[j] = __fmul_rn((float)((int)(bytes[j / 2] >> 4) - 8), s0);
+                y[j + 1] = __fmul_rn((float)((int)(bytes[j / 2] & 0x0F) - 8), s1);
+            }
         }
     } else {
 #pragma unroll
@@ -347,36 +358,126 @@ __device__ __forceinline__ void unpack_row(int code, int64_t pos, int b, int B, 
     }
 }
 
+// Raw bytes of one lane's slice of a packed row (VEC values), fetched before decoding so a
+// warp keeps all of its rows' loads in flight at once.
 template <int VEC>
+struct RawSlice {
+    uint32_t w[VEC];   // fp32: VEC words; fp16: VEC/2; int8: VEC/4 (or 1 sub-word); int4: VEC/8 (or 1 sub-word)
+    float s;           // int8 row scale / int4 group scale
+};
+
+template <int VEC>
+__device__ __forceinline__ void load_raw(int code, int64_t pos, int b, int B, int G, const void* payload,
+                                         const float* scale, RawSlice<VEC>& r, int lane) {
+    constexpr int D = 32 * VEC;
+    const int64_t row = pos * B + b;
+    if (code == 0) {
+        const uint32_t* p = reinterpret_cast<const uint32_t*>(payload) + row * D + lane * VEC;
+        if constexpr (VEC == 2) {
+            const uint2 a = *reinterpret_cast<const uint2*>(p);
+            r.w[0] = a.x; r.w[1] = a.y;
+        } else {
+#pragma unroll
+            for (int j = 0; j < VEC; j += 4) {
+                const uint4 a = *reinterpret_cast<const uint4*>(p + j);
+                r.w[j] = a.x; r.w[j + 1] = a.y; r.w[j + 2] = a.z; r.w[j + 3] = a.w;
+            }
+        }
+    } else if (code == 1) {
+        const uint16_t* p = reinterpret_cast<const uint16_t*>(payload) + row * D + lane * VEC;
+        if constexpr (VEC == 2) {
+            r.w[0] = *reinterpret_cast<const uint32_t*>(p);
+        } else {
+#pragma unroll
+            for (int j = 0; j < VEC / 2; j += 2) {
+                const uint2 a = *reinterpret_cast<const uint2*>(p + 2 * j);
+                r.w[j] = a.x; r.w[j + 1] = a.y;
+            }
+        }
+    } else if (code == 2) {
+        const uint8_t* p = reinterpret_cast<const uint8_t*>(payload) + row * D + lane * VEC;
+        if constexpr (VEC == 2) r.w[0] = *reinterpret_cast<const uint16_t*>(p);
+        else if constexpr (VEC == 4) r.w[0] = *reinterpret_cast<const uint32_t*>(p);
+        else { const uint2 a = *reinterpret_cast<const uint2*>(p); r.w[0] = a.x; r.w[1] = a.y; }
+        r.s = scale[row];
+    } else {
+        const int64_t rb = (int64_t)B * D / 2;
+        const uint8_t* p = reinterpret_cast<const uint8_t*>(payload) + pos * rb + (int64_t)b * (D / 2) + lane * (VEC / 2);
+        if constexpr (VEC == 2) r.w[0] = *p;
+        else if constexpr (VEC == 4) r.w[0] = *reinterpret_cast<const uint16_t*>(p);
+        else r.w[0] = *reinterpret_cast<const uint32_t*>(p);
+        const int NG = D / G;
+        r.s = scale[row * NG + (lane * VEC) / G];
+    }
+}
+
+// Decodes a RawSlice; int4 requires G >= VEC (one group scale per lane).
+template <int VEC>
+__device__ __forceinline__ void decode_raw(int code, const RawSlice<VEC>& r, float (&y)[VEC]) {
+    if (code == 0) {
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) y[j] = __uint_as_float(r.w[j]);
+    } else if (code == 1) {
+#pragma unroll
+        for (int j = 0; j < VEC; j += 2) {
+            y[j] = __half2float(__ushort_as_half((unsigned short)(r.w[j / 2] & 0xffff)));
+            y[j + 1] = __half2float(__ushort_as_half((unsigned short)(r.w[j / 2] >> 16)));
+        }
+    } else if (code == 2) {
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) {
+            const int8_t q = (int8_t)((r.w[j / 4] >> (8 * (j % 4))) & 0xff);
+            y[j] = __fmul_rn((float)q, r.s);
+        }
+    } else if (code == 3) {
+#pragma unroll
+        for (int j = 0; j < VEC; j += 2) {
+            const uint32_t byte = (r.w[(j / 2) / 4] >> (8 * ((j / 2) % 4))) & 0xff;
+            y[j] = __fmul_rn((float)((int)(byte >> 4) - 8), r.s);
+            y[j + 1] = __fmul_rn((float)((int)(byte & 0x0F) - 8), r.s);
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) y[j] = 0.0f;
+    }
+}
+
+template <int VEC, int RPW>
 __global__ void __launch_bounds__(256) unpack_fast_kernel(Buckets bk, const int32_t* __restrict__ slot,
                                                           int B, int H, int S, int G,
                                                           float* __restrict__ k_out,
                                                           float* __restrict__ v_out) {
     constexpr int D = 32 * VEC;
-    const int lane = threadIdx.x & 31;
-    const int64_t rows = (int64_t)B * H * S;
-    const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
-    for (int64_t r = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; r < rows; r += nwarps) {
-        const int64_t t = r % S;
-        const int64_t bh = r / S;
-        const int64_t h = bh % H;
-        const int b = (int)(bh / H);
-        const int32_t sl = slot[t * H + h];
-        const int code = sl < 0 ? kCodeEvicted : slot_code(sl);
-        const int64_t pos = sl < 0 ? 0 : slot_pos(sl);
-        float yk[VEC], yv[VEC];
-        if (code < kCodeEvicted) {
-            const skv_bucket& bb = bk.b[code];
-            unpack_row<VEC>(code, pos, b, B, G, bb.k, bb.scale_k, yk, lane);
-            unpack_row<VEC>(code, pos, b, B, G, bb.v, bb.scale_v, yv, lane);
-        } else {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int bh = blockIdx.y;
+    const int h = bh % H, b = bh / H;
+    const int t0 = (blockIdx.x * 8 + warp) * RPW;
+    if (t0 >= S) return;
+    const int64_t base = (int64_t)bh * S * D + lane * VEC;
+    int32_t sl[RPW];
 #pragma unroll
-            for (int j = 0; j < VEC; ++j) yk[j] = yv[j] = 0.0f;
+    for (int i = 0; i < RPW; ++i) sl[i] = (t0 + i < S) ? slot[(t0 + i) * H + h] : -1;
+    RawSlice<VEC> rk[RPW], rv[RPW];
+#pragma unroll
+    for (int i = 0; i < RPW; ++i) {
+        const int code = sl[i] < 0 ? kCodeEvicted : slot_code(sl[i]);
+        if (code < kCodeEvicted) {
+            const int64_t pos = slot_pos(sl[i]);
+            const skv_bucket& bb = bk.b[code];
+            load_raw<VEC>(code, pos, b, B, G, bb.k, bb.scale_k, rk[i], lane);
+            load_raw<VEC>(code, pos, b, B, G, bb.v, bb.scale_v, rv[i], lane);
         }
-        float* ok = k_out + r * D + lane * VEC;
-        float* ov = v_out + r * D + lane * VEC;
-        Vec<VEC>::store(ok, yk);
-        Vec<VEC>::store(ov, yv);
+    }
+#pragma unroll
+    for (int i = 0; i < RPW; ++i) {
+        const int t = t0 + i;
+        if (t >= S) break;
+        const int code = sl[i] < 0 ? kCodeEvicted : slot_code(sl[i]);
+        float yk[VEC], yv[VEC];
+        decode_raw<VEC>(code, rk[i], yk);
+        decode_raw<VEC>(code, rv[i], yv);
+        Vec<VEC>::store(k_out + base + (int64_t)t * D, yk);
+        Vec<VEC>::store(v_out + base + (int64_t)t * D, yv);
     }
 }
 
@@ -423,28 +524,36 @@ __global__ void unpack_generic_kernel(Buckets bk, const int32_t* __restrict__ sl
     }
 }
 
-// True when the warp-per-row kernels cover (D, G): D = 32*VEC with VEC in {2,4,8}, and the
-// int4 group either spans a power-of-two number of lanes or divides a lane's VEC values.
-static int fast_vec(int D, int G) {
-    int vec = 0;
-    if (D == 64) vec = 2;
-    else if (D == 128) vec = 4;
-    else if (D == 256) vec = 8;
-    if (!vec) return 0;
-    if (G >= vec) {
-        if (G % vec) return 0;
-        const int L = G / vec;
-        if (L > 32 || (L & (L - 1))) return 0;
-    } else if (vec % G) {
-        return 0;
-    }
-    return vec;
+// The warp-per-row kernels cover D = 32*VEC with VEC in {2,4,8} and an int4 group that spans a
+// power-of-two number of whole lanes (group 16 at D = 64/128/256); other shapes take the
+// generic kernels.
+static int fast_vec_unpack(int D, int G) {
+    const int vec = D == 64 ? 2 : (D == 128 ? 4 : (D == 256 ? 8 : 0));
+    if (!vec || G < vec || G % vec) return 0;
+    const int L = G / vec;
+    return (L <= 32 && (L & (L - 1)) == 0) ? vec : 0;
 }
 
-static int grid_for_rows(int64_t rows) {
-    const int64_t want = (rows + 7) / 8;  // 8 warps per block
-    const int64_t cap = (int64_t)sm_count() * 8;
-    return (int)(want < cap ? want : cap);
+static int fast_vec(int D, int G) { return fast_vec_unpack(D, G); }
+
+static bool is_aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+// The vectorised kernels use 16-byte accesses on the fp32 side and row-aligned accesses on
+// the bucket side; any pointer off a 16-byte boundary sends the call to the generic kernel.
+static bool buckets_aligned(const skv_bucket* bk) {
+    for (int p = 0; p < kNumBuckets; ++p) {
+        if (bk[p].count == 0) continue;
+        if (!is_aligned16(bk[p].k) || !is_aligned16(bk[p].v)) return false;
+        if (bk[p].scale_k && (!is_aligned16(bk[p].scale_k) || !is_aligned16(bk[p].scale_v))) return false;
+    }
+    return true;
+}
+
+constexpr int kPackRPW = 2;
+constexpr int kUnpackRPW = 4;
+
+static dim3 grid_2d(int B, int H, int S, int rpw) {
+    return dim3((unsigned)((S + 8 * rpw - 1) / (8 * rpw)), (unsigned)(B * H));
 }
 
 static int check_buckets(const skv_bucket* bk, const char* what) {
@@ -483,18 +592,20 @@ int skv_pack(const float* k, const float* v, int B, int H, int S, int D, int gro
     for (int p = 0; p < kNumBuckets; ++p) bk.b[p] = buckets[p];
     cudaStream_t s = as_stream(stream);
     const int64_t rows = (int64_t)B * H * S;
-    switch (fast_vec(D, G)) {
+    const bool aligned = is_aligned16(k) && is_aligned16(v) && is_aligned16(dense_k) && is_aligned16(dense_v) &&
+                         is_aligned16(k_prev) && is_aligned16(v_prev) && buckets_aligned(buckets);
+    switch (aligned ? fast_vec(D, G) : 0) {
         case 2:
-            pack_fast_kernel<2><<<grid_for_rows(rows), 256, 0, s>>>(k, v, B, H, S, G, slot, bk, dense_k,
-                                                                  dense_v, k_prev, v_prev, reuse_mask);
+            pack_fast_kernel<2, kPackRPW><<<grid_2d(B, H, S, kPackRPW), 256, 0, s>>>(
+                k, v, B, H, S, G, slot, bk, dense_k, dense_v, k_prev, v_prev, reuse_mask);
             break;
         case 4:
-            pack_fast_kernel<4><<<grid_for_rows(rows), 256, 0, s>>>(k, v, B, H, S, G, slot, bk, dense_k,
-                                                                  dense_v, k_prev, v_prev, reuse_mask);
+            pack_fast_kernel<4, kPackRPW><<<grid_2d(B, H, S, kPackRPW), 256, 0, s>>>(
+                k, v, B, H, S, G, slot, bk, dense_k, dense_v, k_prev, v_prev, reuse_mask);
             break;
         case 8:
-            pack_fast_kernel<8><<<grid_for_rows(rows), 256, 0, s>>>(k, v, B, H, S, G, slot, bk, dense_k,
-                                                                  dense_v, k_prev, v_prev, reuse_mask);
+            pack_fast_kernel<8, kPackRPW><<<grid_2d(B, H, S, kPackRPW), 256, 0, s>>>(
+                k, v, B, H, S, G, slot, bk, dense_k, dense_v, k_prev, v_prev, reuse_mask);
             break;
         default: {
             const int64_t n = 2 * (int64_t)S * H;
@@ -518,10 +629,20 @@ int skv_unpack(const skv_bucket* buckets, const int32_t* slot, int B, int H, int
     for (int p = 0; p < kNumBuckets; ++p) bk.b[p] = buckets[p];
     cudaStream_t s = as_stream(stream);
     const int64_t rows = (int64_t)B * H * S;
-    switch (fast_vec(D, G)) {
-        case 2: unpack_fast_kernel<2><<<grid_for_rows(rows), 256, 0, s>>>(bk, slot, B, H, S, G, k_out, v_out); break;
-        case 4: unpack_fast_kernel<4><<<grid_for_rows(rows), 256, 0, s>>>(bk, slot, B, H, S, G, k_out, v_out); break;
-        case 8: unpack_fast_kernel<8><<<grid_for_rows(rows), 256, 0, s>>>(bk, slot, B, H, S, G, k_out, v_out); break;
+    const bool aligned = is_aligned16(k_out) && is_aligned16(v_out) && buckets_aligned(buckets);
+    switch (aligned ? fast_vec_unpack(D, G) : 0) {
+        case 2:
+            unpack_fast_kernel<2, kUnpackRPW><<<grid_2d(B, H, S, kUnpackRPW), 256, 0, s>>>(bk, slot, B, H, S, G,
+                                                                                            k_out, v_out);
+            break;
+        case 4:
+            unpack_fast_kernel<4, kUnpackRPW><<<grid_2d(B, H, S, kUnpackRPW), 256, 0, s>>>(bk, slot, B, H, S, G,
+                                                                                            k_out, v_out);
+            break;
+        case 8:
+            unpack_fast_kernel<8, kUnpackRPW><<<grid_2d(B, H, S, kUnpackRPW), 256, 0, s>>>(bk, slot, B, H, S, G,
+                                                                                            k_out, v_out);
+            break;
         default: {
             const int64_t total = rows * D;
             const int64_t want = (total + 255) / 256;

@@ -13,6 +13,32 @@
 
 namespace skv {
 
+// Bit position of the n-th (0-based) set bit of m; requires popc(m) > n.
+__device__ __forceinline__ int nth_set_bit(unsigned m, int n) {
+    int pos = 0;
+#pragma unroll
+    for (int w = 16; w > 0; w >>= 1) {
+        const unsigned low = m & ((1u << w) - 1u);
+        const int c = __popc(low);
+        if (n >= c) {
+            n -= c;
+            m >>= w;
+            pos += w;
+        } else {
+            m = low;
+        }
+    }
+    return pos;
+}
+
+__device__ __forceinline__ bool aligned16(const void* a, const void* b, const void* c, const void* d) {
+    return ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b) | reinterpret_cast<uintptr_t>(c) |
+             reinterpret_cast<uintptr_t>(d)) & 15) == 0;
+}
+
+// One warp per 32 consecutive entries.  Rows to copy are grouped by precision; the 16-byte
+// chunks of all selected rows of a group are spread over the lanes, so a warp has up to 32
+// independent copies in flight instead of one row at a time.
 __global__ void __launch_bounds__(256) reuse_kernel(Buckets cur, const int32_t* __restrict__ cur_slot,
                                                     int S, Buckets prev, const int32_t* __restrict__ prev_slot,
                                                     int S_prev, const uint8_t* __restrict__ mask, int B,
@@ -37,27 +63,60 @@ __global__ void __launch_bounds__(256) reuse_kernel(Buckets cur, const int32_t* 
                 }
             }
         }
-        unsigned todo = __ballot_sync(0xffffffffu, copy);
         applied += copy ? 1 : 0;
-        while (todo) {
-            const int src = __ffs(todo) - 1;
-            todo &= todo - 1;
-            const int32_t c = __shfl_sync(0xffffffffu, cs, src);
-            const int32_t p = __shfl_sync(0xffffffffu, ps, src);
-            const int code = slot_code(c);
-            const int64_t cpos = slot_pos(c), ppos = slot_pos(p);
+        for (int code = 0; code < kNumBuckets; ++code) {
+            const unsigned m = __ballot_sync(0xffffffffu, copy && slot_code(cs) == code);
+            if (!m) continue;
+            const int nrows = __popc(m);
             const int64_t rb = payload_row_bytes(code, B, D);
+            const int64_t sf = scale_row_floats(code, B, D, NG);
             const skv_bucket& cb = cur.b[code];
             const skv_bucket& pb = prev.b[code];
-            warp_copy(reinterpret_cast<uint8_t*>(cb.k) + cpos * rb,
-                      reinterpret_cast<const uint8_t*>(pb.k) + ppos * rb, rb, lane);
-            warp_copy(reinterpret_cast<uint8_t*>(cb.v) + cpos * rb,
-                      reinterpret_cast<const uint8_t*>(pb.v) + ppos * rb, rb, lane);
-            const int64_t sf = scale_row_floats(code, B, D, NG);
+            if ((rb & 15) == 0 && aligned16(cb.k, cb.v, pb.k, pb.v)) {
+                const int cpr = (int)(rb / 16);
+                const int total = nrows * cpr;
+                for (int j0 = 0; j0 < total; j0 += 32) {
+                    const int j = j0 + lane;
+                    const int rr = j < total ? j / cpr : 0;
+                    const int src = nth_set_bit(m, rr);
+                    const int32_t c2 = __shfl_sync(0xffffffffu, cs, src);
+                    const int32_t p2 = __shfl_sync(0xffffffffu, ps, src);
+                    if (j < total) {
+                        const int64_t off = (int64_t)(j - rr * cpr) * 16;
+                        const int64_t d_off = (int64_t)slot_pos(c2) * rb + off;
+                        const int64_t s_off = (int64_t)slot_pos(p2) * rb + off;
+                        const uint4 a = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint8_t*>(pb.k) + s_off);
+                        const uint4 b = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint8_t*>(pb.v) + s_off);
+                        *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(cb.k) + d_off) = a;
+                        *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(cb.v) + d_off) = b;
+                    }
+                }
+            } else {
+                unsigned todo = m;
+                while (todo) {
+                    const int src = __ffs(todo) - 1;
+                    todo &= todo - 1;
+                    const int64_t cpos = slot_pos(__shfl_sync(0xffffffffu, cs, src));
+                    const int64_t ppos = slot_pos(__shfl_sync(0xffffffffu, ps, src));
+                    warp_copy(reinterpret_cast<uint8_t*>(cb.k) + cpos * rb,
+                              reinterpret_cast<const uint8_t*>(pb.k) + ppos * rb, rb, lane);
+                    warp_copy(reinterpret_cast<uint8_t*>(cb.v) + cpos * rb,
+                              reinterpret_cast<const uint8_t*>(pb.v) + ppos * rb, rb, lane);
+                }
+            }
             if (sf) {
-                for (int64_t i = lane; i < sf; i += 32) {
-                    cb.scale_k[cpos * sf + i] = pb.scale_k[ppos * sf + i];
-                    cb.scale_v[cpos * sf + i] = pb.scale_v[ppos * sf + i];
+                const int total = nrows * (int)sf;
+                for (int j0 = 0; j0 < total; j0 += 32) {
+                    const int j = j0 + lane;
+                    const int rr = j < total ? j / (int)sf : 0;
+                    const int src = nth_set_bit(m, rr);
+                    const int32_t c2 = __shfl_sync(0xffffffffu, cs, src);
+                    const int32_t p2 = __shfl_sync(0xffffffffu, ps, src);
+                    if (j < total) {
+                        const int64_t i = j - (int64_t)rr * sf;
+                        cb.scale_k[slot_pos(c2) * sf + i] = pb.scale_k[slot_pos(p2) * sf + i];
+                        cb.scale_v[slot_pos(c2) * sf + i] = pb.scale_v[slot_pos(p2) * sf + i];
+                    }
                 }
             }
         }

@@ -68,6 +68,20 @@ __device__ __forceinline__ int quant_value(float x, float scale, int lo, int hi)
     return (int)q;
 }
 
+// Same result as quant_value without a division per element.  `rcp` must be
+// __frcp_rn(scale).  y = x*rcp differs from the correctly rounded quotient
+// fl(x/scale) by at most ~2.3e-5 for |x/scale| <= 128 (two roundings of 2^-24
+// relative each, plus the half-ulp of fl itself), so rint(y) == rint(fl(x/scale))
+// unless y lies within 1e-4 of a half-integer (or is not finite); only those
+// rare elements take the exact IEEE division.
+__device__ __forceinline__ int quant_value_fast(float x, float scale, float rcp, int lo, int hi) {
+    const float y = __fmul_rn(x, rcp);
+    float q = rintf(y);
+    if (!(fabsf(y - q) < 0.4999f)) q = rintf(__fdiv_rn(x, scale));
+    q = fminf(fmaxf(q, (float)lo), (float)hi);
+    return (int)q;
+}
+
 // Copies `bytes` bytes with a warp, using 16-byte vectors when both ends allow.
 __device__ __forceinline__ void warp_copy(void* dst, const void* src, int64_t bytes, int lane) {
     const uintptr_t a = reinterpret_cast<uintptr_t>(dst) | reinterpret_cast<uintptr_t>(src);

@@ -122,9 +122,13 @@ def _nbytes(t: Optional[torch.Tensor]) -> int:
 
 
 def run_pack(k: torch.Tensor, v: torch.Tensor, plan: PrecisionPlan, group_size: int, dense: bool = False,
-             k_prev: Optional[torch.Tensor] = None, v_prev: Optional[torch.Tensor] = None
+             k_prev: Optional[torch.Tensor] = None, v_prev: Optional[torch.Tensor] = None,
+             events: Optional[Tuple[Any, Any]] = None,
              ) -> Tuple[List[Optional[Dict[str, torch.Tensor]]], Optional[torch.Tensor], Optional[torch.Tensor]]:
-    """Launch ``skv_pack`` for ``plan``; returns device buckets (+ dense working copy)."""
+    """Launch ``skv_pack`` for ``plan``; returns device buckets (+ dense working copy).
+
+    ``events``: optional pair of CUDA events recorded immediately around the kernel launch.
+    """
     B, H, S, D = k.shape
     dev = plan.compute_device
     G = _int4_group(D, group_size)
@@ -151,9 +155,13 @@ def run_pack(k: torch.Tensor, v: torch.Tensor, plan: PrecisionPlan, group_size: 
     lib = _lib.load()
     arr = _lib.buckets(buckets)
     with torch.cuda.device(dev):
+        if events is not None:
+            events[0].record()
         st = lib.skv_pack(_lib.ptr(kd), _lib.ptr(vd), B, H, S, D, group_size, _lib.ptr(plan.slot), arr,
                           _lib.ptr(dk), _lib.ptr(dv), _lib.ptr(kp), _lib.ptr(vp),
                           _lib.ptr(plan.reuse_mask_device) if kp is not None else None, _lib.stream_of(dev))
+        if events is not None:
+            events[1].record()
     _lib.check(st, "PackedKVCache.pack")
     return buckets, dk, dv
 
@@ -162,6 +170,8 @@ class PackedKVCache:
     """Byte-level packed KV cache storage with per-token-head precision."""
 
     PRECISION_BITS = {"fp32": 32, "fp16": 16, "int8": 8, "int4": 4}
+    # optional (start, end) CUDA events recorded around every pack kernel launch (profiling hook)
+    _pack_events: Optional[Tuple[Any, Any]] = None
 
     def __init__(self, batch_size: int, num_heads: int, seq_len: int, head_dim: int, device: Any = "cpu"):
         self.batch_size = batch_size
@@ -225,7 +235,7 @@ class PackedKVCache:
             )
         if not isinstance(plan, PrecisionPlan):
             plan = PrecisionPlan.from_codes(plan.codes, device=plan.codes.device)
-        buckets, _, _ = run_pack(k_tensor, v_tensor, plan, group_size)
+        buckets, _, _ = run_pack(k_tensor, v_tensor, plan, group_size, events=self._pack_events)
         self._adopt(buckets, plan.slot, shared_slot=True, group_size=group_size)
 
     def _adopt(self, buckets, slot: torch.Tensor, shared_slot: bool, group_size: int) -> None:

@@ -123,11 +123,13 @@ def queries(B: int, H: int, S: int, D: int, seed: int) -> torch.Tensor:
     return torch.randn(B, H, S, D, generator=g).to(torch.float16)
 
 
-def cfg2_inputs(S: Optional[int] = None) -> Dict[str, torch.Tensor]:
-    """K, V, importance, reuse mask, previous K/V and the budget of cfg2 (``S`` overrides)."""
+def cfg2_inputs(S: Optional[int] = None, seed: Optional[int] = None) -> Dict[str, torch.Tensor]:
+    """K, V, importance, reuse mask, previous K/V and the budget of cfg2 (``S``/``seed`` override)."""
     c = dict(CONFIGS["cfg2"])
     if S is not None:
         c["S"] = S
+    if seed is not None:
+        c["seed"] = seed
     B, H, S, D = c["B"], c["H"], c["S"], c["D"]
     k, v = kv_tensors(B, H, S, D, c["seed"])
     imp = importance_map(S, H, c["seed"], c["fractions"], c["sink_tokens"])
