@@ -90,6 +90,22 @@ int skv_plan_bucket(const int8_t* codes, const uint8_t* reuse_mask, int S, int H
                     int64_t* flat_out, int32_t* slot_out, int64_t* reuse_flat_out,
                     int64_t* counts, void* scratch, size_t scratch_bytes, void* stream);
 
+/* Allocation-free skv_plan_bucket (no counterpart in the reference).
+ * For callers that cannot allocate device memory -- e.g. a host runtime that has handed the
+ * whole device pool to its own allocator, or code that must not call into the CUDA
+ * allocator between launches -- and so cannot provide the scratch buffer skv_plan_bucket
+ * needs.  Outputs are identical to skv_plan_bucket; the tile counts live in a 64 KiB array in
+ * the library's device memory, held on every device that loads the library until exit.
+ * Limit: S*H <= skv_plan_static_max_entries() (4,194,304); larger sizes return
+ * SKV_ERR_TOO_LARGE without launching.  The first call on a device looks up the array's
+ * device address (cudaGetSymbolAddress); make that first call outside any stream capture.
+ * All calls share the array: calls that overlap on the GPU (other streams, other threads)
+ * race and must be serialised by the caller. */
+int64_t skv_plan_static_max_entries(void);
+int skv_plan_bucket_static(const int8_t* codes, const uint8_t* reuse_mask, int S, int H,
+                           int64_t* flat_out, int32_t* slot_out, int64_t* reuse_flat_out,
+                           int64_t* counts, void* stream);
+
 /* PackedKVCache._do_pack_with_plan / _pack_int4_rows
  * (shadowinfer/shadowkv/packed_kv_cache.py:222-388) fused with the dense working
  * copy of ShadowKVAgent._compress_kv_with_plan (shadowkv_agent.py:1698-1809):

@@ -64,6 +64,9 @@ _SIGNATURES = {
     "skv_plan_scratch_bytes": (c_size_t, [c_int, c_int]),
     "skv_plan_bucket": (c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p,
                                 c_void_p, c_size_t, c_void_p]),
+    "skv_plan_static_max_entries": (c_int64, []),
+    "skv_plan_bucket_static": (c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p,
+                                       c_void_p]),
     "skv_pack": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_void_p, ctypes.POINTER(SkvBucket),
                          c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
     "skv_unpack": (c_int, [ctypes.POINTER(SkvBucket), c_void_p, c_int, c_int, c_int, c_int, c_int, c_void_p,

@@ -10,6 +10,8 @@
 //                               a tile-count pass and a scan+scatter pass (no sort).
 #include <math.h>
 
+#include <mutex>
+
 #include "skv_common.cuh"
 
 namespace skv {
@@ -238,11 +240,70 @@ __global__ void __launch_bounds__(kPlanThreads) plan_scatter_kernel(
     }
 }
 
+// ---------------------------------------------------------------------------------------
+// Allocation-free variant of the plan bucketing: the tile counts live in a fixed array in
+// the library's device memory instead of a caller-provided scratch buffer.
+// ---------------------------------------------------------------------------------------
+constexpr int kStaticPlanTiles = 2048;                                  // tiles of kPlanTile entries
+constexpr int64_t kStaticPlanMaxEntries = (int64_t)kStaticPlanTiles * kPlanTile;   // 4,194,304
+static __device__ __align__(256) int g_plan_static_scratch[kStaticPlanTiles * kPlanStride];  // 64 KiB
+
+// Device address of g_plan_static_scratch for the current device.  The host-side symbol is
+// only a stand-in, so the address is looked up once per device (with that device current)
+// and cached.
+static int static_plan_scratch(int** out) {
+    static std::mutex mu;
+    static int* cached[64] = {nullptr};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
+        return fail(SKV_ERR_CUDA, "plan_bucket_static: no current CUDA device");
+    std::lock_guard<std::mutex> lock(mu);
+    if (cached[dev] == nullptr) {
+        void* p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_plan_static_scratch);
+        if (e != cudaSuccess || p == nullptr)
+            return fail(SKV_ERR_CUDA, "plan_bucket_static: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
+        cached[dev] = reinterpret_cast<int*>(p);
+    }
+    *out = cached[dev];
+    return SKV_OK;
+}
+
 }  // namespace skv
 
 using namespace skv;
 
 extern "C" {
+
+int64_t skv_plan_static_max_entries(void) { return kStaticPlanMaxEntries; }
+
+int skv_plan_bucket_static(const int8_t* codes, const uint8_t* reuse_mask, int S, int H, int64_t* flat_out,
+                           int32_t* slot_out, int64_t* reuse_flat_out, int64_t* counts, void* stream) {
+    if (S <= 0 || H <= 0)
+        return fail(SKV_ERR_INVALID_ARGUMENT, "seq_len and num_heads must be positive, got %d, %d", S, H);
+    if (!codes || !flat_out || !counts || (reuse_mask && !reuse_flat_out))
+        return fail(SKV_ERR_INVALID_ARGUMENT, "plan_bucket_static: null pointer");
+    const int64_t n = (int64_t)S * H;
+    if (n > kStaticPlanMaxEntries)
+        return fail(SKV_ERR_TOO_LARGE,
+                    "plan_bucket_static: seq_len*num_heads = %lld exceeds the %lld entries its fixed "
+                    "device scratch covers; use skv_plan_bucket with a caller-provided scratch",
+                    (long long)n, (long long)kStaticPlanMaxEntries);
+    int* tc = nullptr;
+    int st = static_plan_scratch(&tc);
+    if (st) return st;
+    // every tile count read by plan_scatter_kernel is written by plan_count_kernel of the
+    // same call, so nothing left over from an earlier call needs clearing
+    const int tiles = (int)((n + kPlanTile - 1) / kPlanTile);
+    cudaStream_t s = as_stream(stream);
+    plan_count_kernel<<<tiles, kPlanThreads, 0, s>>>(codes, reuse_mask, n, tc);
+    st = check_launch("plan_count");
+    if (st) return st;
+    plan_scatter_kernel<<<tiles, kPlanThreads, 0, s>>>(codes, reuse_mask, n, S, H, tc, tiles, flat_out, slot_out,
+                                                       reuse_flat_out, counts);
+    return check_launch("plan_scatter");
+}
+
 
 int skv_allocate_codes(const float* importance, int64_t n, int mode, int8_t* codes, void* stream) {
     if (n < 0) return fail(SKV_ERR_INVALID_ARGUMENT, "allocate_codes: negative size");

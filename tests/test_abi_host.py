@@ -30,7 +30,7 @@ def test_library_exports_every_declared_symbol():
     assert declared, "no declarations found"
     for name in declared:
         assert hasattr(lib, name), name
-    assert set(declared) <= set(_lib.EXPORTED_SYMBOLS) | {"skv_admit_codes_static"}
+    assert set(declared) <= set(_lib.EXPORTED_SYMBOLS)
 
 
 def test_status_strings_and_scratch_queries():
