@@ -142,6 +142,22 @@ int skv_evict_compact(const skv_bucket* src /* [4] */, const skv_bucket* dst /* 
                       const uint8_t* evict_mask, int32_t* slot, int B, int S, int H, int D,
                       int int4_group, void* scratch, size_t scratch_bytes, void* stream);
 
+/* Per-head KV row lists for skv_packed_attention: rows int32[H*S] (slot encoding, stored
+ * entries of head h grouped by precision fp32, fp16, int8, int4, token order inside a group),
+ * counts int32[H*5] (stored entries per precision, evicted entries).  Derived from the cache's
+ * slot map; no reference counterpart (the reference never attends over the packed form). */
+int skv_head_index(const int32_t* slot, int S, int H, int32_t* rows, int32_t* counts, void* stream);
+
+/* Attention read directly from the packed cache: O = softmax(Q K^T * scale) V, non-causal, with
+ * evicted entries as zero K/V rows -- the result of PackedKVCache.unpack()
+ * (shadowinfer/shadowkv/packed_kv_cache.py:535-577) fed to SimpleDiffusionLLM._compute_block's
+ * attention (shadowinfer/models/simple_diffusion_llm.py:165-169), without materialising K/V.
+ * q fp16 [B,H,S_q,D], out fp32 [B,H,S_q,D]; D = 64 or 128; error_flag (device int32) is cleared
+ * and set non-zero if a pipeline wait timed out (results then invalid). */
+int skv_packed_attention(const void* q, int B, int H, int S_q, int D, const skv_bucket* buckets /* [4] */,
+                         int S_kv, int int4_group, const int32_t* rows, const int32_t* counts, float scale,
+                         float* out, int32_t* error_flag, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

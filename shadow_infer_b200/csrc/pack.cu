@@ -591,7 +591,6 @@ int skv_pack(const float* k, const float* v, int B, int H, int S, int D, int gro
     Buckets bk;
     for (int p = 0; p < kNumBuckets; ++p) bk.b[p] = buckets[p];
     cudaStream_t s = as_stream(stream);
-    const int64_t rows = (int64_t)B * H * S;
     const bool aligned = is_aligned16(k) && is_aligned16(v) && is_aligned16(dense_k) && is_aligned16(dense_v) &&
                          is_aligned16(k_prev) && is_aligned16(v_prev) && buckets_aligned(buckets);
     switch (aligned ? fast_vec(D, G) : 0) {
@@ -628,7 +627,6 @@ int skv_unpack(const skv_bucket* buckets, const int32_t* slot, int B, int H, int
     Buckets bk;
     for (int p = 0; p < kNumBuckets; ++p) bk.b[p] = buckets[p];
     cudaStream_t s = as_stream(stream);
-    const int64_t rows = (int64_t)B * H * S;
     const bool aligned = is_aligned16(k_out) && is_aligned16(v_out) && buckets_aligned(buckets);
     switch (aligned ? fast_vec_unpack(D, G) : 0) {
         case 2:
@@ -644,7 +642,7 @@ int skv_unpack(const skv_bucket* buckets, const int32_t* slot, int B, int H, int
                                                                                             k_out, v_out);
             break;
         default: {
-            const int64_t total = rows * D;
+            const int64_t total = (int64_t)B * H * S * D;
             const int64_t want = (total + 255) / 256;
             const int blocks = (int)(want < (int64_t)sm_count() * 16 ? want : (int64_t)sm_count() * 16);
             unpack_generic_kernel<<<blocks, 256, 0, s>>>(bk, slot, B, H, S, D, G, k_out, v_out);

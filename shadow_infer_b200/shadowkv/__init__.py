@@ -1,5 +1,6 @@
 """ShadowKV packed-KV data plane on B200 (drop-in for ``shadowinfer.shadowkv``'s data plane)."""
 
+from .packed_attention import packed_attention
 from .packed_kv_cache import PackedKVCache
 from .precision_plan import (
     CODE_PRECISIONS,
@@ -15,5 +16,5 @@ from .rd_allocator import admit_budget, admit_codes, entry_bytes, kv_sensitivity
 __all__ = [
     "PackedKVCache", "PrecisionPlan", "map_to_codes", "codes_to_map", "PRECISION_ORDER", "PRECISION_CODES",
     "CODE_PRECISIONS", "EVICTED", "admit_codes", "admit_budget", "entry_bytes", "kv_sensitivity",
-    "predict_codes_bytes",
+    "predict_codes_bytes", "packed_attention",
 ]

@@ -1,0 +1,66 @@
+"""Attention over the packed cache, without unpacking it.
+
+In the reference the ``kv_execution="packed"`` path unpacks every layer to
+dense fp32 K/V (``PackedKVCache.unpack``, shadowinfer/shadowkv/packed_kv_cache.py:535-577,
+called from ``PyTorchModelBackend.forward_step``, core/backends/pytorch_backend.py:302-304)
+and then runs ``softmax(q @ k^T / sqrt(D)) @ v`` (shadowinfer/models/simple_diffusion_llm.py:165-169).
+``packed_attention`` computes the same result in one sm_100a kernel that reads the
+packed buckets directly: evicted token-heads behave exactly as the zero rows that
+``unpack`` would have produced (logit 0, value 0).
+"""
+
+from __future__ import annotations
+
+import math
+from typing import Optional
+
+import torch
+
+from .. import _lib
+from .._device import back, on
+from .packed_kv_cache import PackedKVCache
+
+
+def packed_attention(
+    q: torch.Tensor,
+    kv_cache: PackedKVCache,
+    scale: Optional[float] = None,
+    check: bool = True,
+) -> torch.Tensor:
+    """Non-causal attention of ``q`` [B, H, S_q, D] over a packed cache; returns fp32 [B, H, S_q, D].
+
+    ``scale`` defaults to ``1/sqrt(D)``.  ``q`` is used in fp16 (the tensor-core operand type).
+    With ``check`` the call synchronises and raises ``RuntimeError`` if the kernel
+    reported a pipeline timeout.
+    """
+    if q.dim() != 4:
+        raise ValueError(f"q must be 4-D [batch, heads, seq, head_dim], got shape {tuple(q.shape)}")
+    B, H, S_q, D = (int(x) for x in q.shape)
+    c = kv_cache
+    if (B, H, D) != (c.batch_size, c.num_heads, c.head_dim):
+        raise ValueError(
+            "q shape mismatch for packed attention: "
+            f"q=(batch={B}, heads={H}, head_dim={D}) cache=({c.batch_size},{c.num_heads},{c.head_dim})"
+        )
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    if not c.packed_data:
+        # every token-head evicted: unpack() would give zero K/V, so the output is zero
+        return torch.zeros(B, H, S_q, D, dtype=torch.float32, device=q.device)
+    dev = c._ensure_state()
+    qd = on(q.detach(), dev, torch.float16)
+    rows, counts = c._head_index(dev)
+    out = torch.empty(B, H, S_q, D, dtype=torch.float32, device=dev)
+    err = torch.empty(1, dtype=torch.int32, device=dev)
+    arr = _lib.buckets(c._device_buckets(dev))
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        st = lib.skv_packed_attention(_lib.ptr(qd), B, H, S_q, D, arr, c.seq_len, c._int4_group_of(), _lib.ptr(rows),
+                                      _lib.ptr(counts), float(scale), _lib.ptr(out), _lib.ptr(err),
+                                      _lib.stream_of(dev))
+    _lib.check(st, "packed_attention")
+    if check:
+        code = int(err.item())
+        if code:
+            raise RuntimeError(f"packed_attention: a pipeline wait timed out inside the kernel (code {code})")
+    return back(out, q.device)

@@ -186,6 +186,7 @@ class PackedKVCache:
         self._flat: Dict[str, torch.Tensor] = {}         # device int64 per bucket
         self._count: Dict[str, int] = {}
         self._dev: Optional[torch.device] = None
+        self._hidx: Optional[Tuple[torch.Tensor, torch.Tensor]] = None   # per-head row lists (attention)
 
     # ------------------------------------------------------------------------------ pack
     @classmethod
@@ -243,6 +244,7 @@ class PackedKVCache:
         self._dev = slot.device
         self._slot = slot
         self._slot_owned = not shared_slot
+        self._hidx = None
         self.packed_data = {}
         self._flat = {}
         self._count = {}
@@ -318,6 +320,20 @@ class PackedKVCache:
                         "scale_k": on(data["scale_k"], dev), "scale_v": on(data["scale_v"], dev),
                         "flat": self._flat[p].to(dev), "count": self._count[p]})
         return out
+
+    def _head_index(self, dev: torch.device) -> Tuple[torch.Tensor, torch.Tensor]:
+        """Per-head stored-entry lists grouped by precision (built once per layout, ``skv_head_index``)."""
+        if self._hidx is None:
+            S, H = self.seq_len, self.num_heads
+            rows = torch.empty(H * S, dtype=torch.int32, device=dev)
+            counts = torch.empty(H * 5, dtype=torch.int32, device=dev)
+            lib = _lib.load()
+            with torch.cuda.device(dev):
+                st = lib.skv_head_index(_lib.ptr(self._slot.to(dev)), S, H, _lib.ptr(rows), _lib.ptr(counts),
+                                        _lib.stream_of(dev))
+            _lib.check(st, "PackedKVCache head index")
+            self._hidx = (rows, counts)
+        return self._hidx
 
     def _int4_group_of(self) -> int:
         d = self.packed_data.get("int4")
@@ -432,6 +448,7 @@ class PackedKVCache:
         if not self._slot_owned:
             self._slot = self._slot.clone()
             self._slot_owned = True
+        self._hidx = None
         G = self._int4_group_of()
         dst: List[Optional[Dict[str, Any]]] = []
         work: List[Optional[Dict[str, Any]]] = []

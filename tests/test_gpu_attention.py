@@ -1,0 +1,100 @@
+"""Attention read from the packed cache vs the oracle (unpack + dense float64 attention).
+
+Tolerance: relative L2 error <= 1e-3 over the whole output, the bound the data plane is
+held to for attention (fp16 tensor-core operands, fp32 accumulation and softmax).
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from golden_lib import case_arrays, load_pins
+from oracle import shadowkv_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+REL_L2_TOL = 1e-3
+
+
+def rel_l2(a, b):
+    a = np.asarray(a, dtype=np.float64)
+    b = np.asarray(b, dtype=np.float64)
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+@pytest.fixture(scope="module")
+def skv():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    import shadow_infer_b200.shadowkv as m
+    return m
+
+
+def _pack(skv, k, v, codes, group=16):
+    plan = skv.PrecisionPlan.from_codes(torch.from_numpy(codes).cuda())
+    return skv.PackedKVCache.pack(torch.from_numpy(k).cuda(), torch.from_numpy(v).cuda(), None, group, plan=plan)["packed_kv"]
+
+
+@pytest.mark.parametrize("case", sorted(c for c, v in load_pins()["cases"].items() if v["kind"] == "attention"))
+def test_attention_matches_reference_fixture(case, skv, golden_small):
+    """The reference's own unpack + fp32 attention output, recorded by make_golden.py."""
+    a = case_arrays(golden_small, case)
+    cache = _pack(skv, a["k"], a["v"], a["codes"])
+    out = skv.packed_attention(torch.from_numpy(a["q"]).cuda(), cache)
+    assert rel_l2(out.cpu().numpy(), a["out"]) < REL_L2_TOL
+
+
+CASES = [
+    # B, H, S_kv, S_q, D, code probabilities (fp32, fp16, int8, int4, evicted), q scale
+    (1, 4, 300, 200, 128, (0.1, 0.2, 0.3, 0.3, 0.1), 1.0),
+    (2, 2, 129, 64, 64, (0.0, 0.3, 0.4, 0.2, 0.1), 1.0),
+    (1, 2, 1000, 257, 128, (0.05, 0.2, 0.5, 0.2, 0.05), 4.0),     # wide logits: running-max rescales
+    (1, 3, 512, 128, 128, (0.0, 0.0, 1.0, 0.0, 0.0), 1.0),       # int8 only (scales folded into softmax)
+    (1, 3, 512, 128, 128, (0.0, 0.0, 0.0, 1.0, 0.0), 1.0),       # int4 only
+    (1, 2, 384, 130, 128, (1.0, 0.0, 0.0, 0.0, 0.0), 1.0),       # fp32 only, ragged query tile
+    (3, 1, 77, 33, 64, (0.2, 0.2, 0.2, 0.2, 0.2), 2.0),
+]
+
+
+@pytest.mark.parametrize("B,H,S,SQ,D,probs,qs", CASES)
+def test_attention_matches_oracle(skv, B, H, S, SQ, D, probs, qs):
+    rng = np.random.default_rng(S * 31 + D)
+    k = rng.standard_normal((B, H, S, D)).astype(np.float32)
+    v = rng.standard_normal((B, H, S, D)).astype(np.float32)
+    k[rng.random(k.shape) < 0.01] *= 8
+    codes = rng.choice(5, size=(S, H), p=probs).astype(np.int8)
+    q = (rng.standard_normal((B, H, SQ, D)) * qs).astype(np.float16)
+    cache = _pack(skv, k, v, codes)
+    out = skv.packed_attention(torch.from_numpy(q).cuda(), cache)
+    ref = O.packed_attention(q.astype(np.float32), O.pack(k, v, O.plan_from_codes(codes), 16))
+    assert rel_l2(out.cpu().numpy(), ref) < REL_L2_TOL
+
+
+def test_attention_all_evicted_head_and_after_evict(skv):
+    rng = np.random.default_rng(5)
+    B, H, S, D = 1, 3, 200, 128
+    k = rng.standard_normal((B, H, S, D)).astype(np.float32)
+    v = rng.standard_normal((B, H, S, D)).astype(np.float32)
+    codes = rng.integers(1, 4, size=(S, H)).astype(np.int8)
+    codes[:, 1] = 4                       # head 1 fully evicted -> uniform weights over zero V
+    q = rng.standard_normal((B, H, 150, D)).astype(np.float16)
+    cache = _pack(skv, k, v, codes)
+    ref_cache = O.pack(k, v, O.plan_from_codes(codes), 16)
+    out = skv.packed_attention(torch.from_numpy(q).cuda(), cache).cpu().numpy()
+    assert rel_l2(out, O.packed_attention(q.astype(np.float32), ref_cache)) < REL_L2_TOL
+    assert np.abs(out[:, 1]).max() == 0.0
+    # evict a quarter of the entries: attention follows the compacted buckets
+    emask = rng.random((S, H)) < 0.25
+    assert cache.evict(torch.from_numpy(emask).cuda()) == O.evict(ref_cache, emask)
+    out = skv.packed_attention(torch.from_numpy(q).cuda(), cache).cpu().numpy()
+    assert rel_l2(out, O.packed_attention(q.astype(np.float32), ref_cache)) < REL_L2_TOL
+
+
+def test_attention_shape_errors(skv):
+    rng = np.random.default_rng(1)
+    k = rng.standard_normal((1, 2, 16, 128)).astype(np.float32)
+    cache = _pack(skv, k, k, np.full((16, 2), 2, dtype=np.int8))
+    with pytest.raises(ValueError, match="shape mismatch"):
+        skv.packed_attention(torch.zeros(1, 3, 8, 128, dtype=torch.float16, device="cuda"), cache)
+    with pytest.raises(ValueError, match="4-D"):
+        skv.packed_attention(torch.zeros(2, 8, 128, dtype=torch.float16, device="cuda"), cache)
