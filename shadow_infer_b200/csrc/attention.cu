@@ -34,7 +34,7 @@ constexpr int kBM = 128;          // queries per CTA
 constexpr int kBN = 128;          // KV rows per tile
 constexpr int kStages = 2;        // K/V tile stages in shared memory
 constexpr int kSoftmaxWarps = 4;
-constexpr int kConvWarps = 4;
+constexpr int kConvWarps = 8;
 constexpr int kAttnThreads = (kSoftmaxWarps + kConvWarps + 1) * 32;
 constexpr uint32_t kTmemCols = 512;
 constexpr float kRescaleThreshold = 8.0f;   // log2 units
@@ -50,8 +50,8 @@ struct AttnLayout {
     static constexpr int kK = kQ + NA * kAtomQ;
     static constexpr int kV = kK + kStages * NA * kBN * 128;
     static constexpr int kP = kV + kStages * NA * kBN * 128;
-    static constexpr int kCol = kP + 2 * kBM * 128;     // P: K-dim = kBN = 128 -> 2 atoms
-    static constexpr int kBar = kCol + kStages * 3 * kBN * 4;
+    static constexpr int kEnt = kP + 2 * kBM * 128;     // P: K-dim = kBN = 128 -> 2 atoms
+    static constexpr int kBar = kEnt + kStages * kBN * 4;   // per-stage entry (slot) lists
     static constexpr int kNumBars = 2 * kStages + 2 + 1 + 1 + 1;
     static constexpr int kTmemSlot = kBar + kNumBars * 8;
     static constexpr int kBytes = kTmemSlot + 16;
@@ -138,66 +138,110 @@ __device__ __forceinline__ uint4 f32x8_to_half(const float* p) {
     return r;
 }
 
-// One converter lane: 8 consecutive values (chunk `l8` of atom `a`) of row `r` of the K and
-// V tiles for entry `e` (slot encoding, -1 = padding row).
+// Raw packed bytes of one lane's share of one K row and one V row: chunk `l8` (8 values)
+// of each 64-value atom, plus the row/group scales.  Loaded for several rows before any is
+// converted, so a converter lane keeps several L2 requests in flight.
+template <int NA>
+struct RawRow {
+    uint4 k[NA][2], v[NA][2];   // fp32 uses both halves, fp16 one, int8 8 bytes, int4 4 bytes
+    float sk[NA], sv[NA];
+    int code;                   // 0..3, or -1 for a padding row
+};
+
 template <int D>
-__device__ __forceinline__ void convert_row(const AttnParams& p, int b, int32_t e, int r, int l8, uint8_t* ktile,
-                                            uint8_t* vtile, float* col_a, float* col_b, float* col_c) {
+__device__ __forceinline__ void load_raw_row(const AttnParams& p, int b, int32_t e, int l8, RawRow<D / 64>& r) {
     constexpr int NA = D / 64;
-    if (e < 0) {
-#pragma unroll
-        for (int a = 0; a < NA; ++a) {
-            *reinterpret_cast<uint4*>(ktile + a * kBN * 128 + sw128_offset(r, l8)) = make_uint4(0, 0, 0, 0);
-            *reinterpret_cast<uint4*>(vtile + a * kBN * 128 + sw128_offset(r, l8)) = make_uint4(0, 0, 0, 0);
-        }
-        if (l8 == 0) {
-            col_a[r] = 0.0f;
-            col_b[r] = 0.0f;
-            col_c[r] = -INFINITY;
-        }
-        return;
-    }
-    const int code = slot_code(e);
+    r.code = e < 0 ? -1 : slot_code(e);
+    if (e < 0) return;
     const int64_t row = (int64_t)slot_pos(e) * p.B + b;
-    const skv_bucket& bb = p.bk.b[code];
-    float fa = p.scale_log2, fb = 1.0f;
+    const skv_bucket& bb = p.bk.b[r.code];
 #pragma unroll
     for (int a = 0; a < NA; ++a) {
         const int d0 = a * 64 + l8 * 8;
-        uint4 hk, hv;
-        if (code == 0) {
-            hk = f32x8_to_half(reinterpret_cast<const float*>(bb.k) + row * D + d0);
-            hv = f32x8_to_half(reinterpret_cast<const float*>(bb.v) + row * D + d0);
-        } else if (code == 1) {
-            hk = *reinterpret_cast<const uint4*>(reinterpret_cast<const __half*>(bb.k) + row * D + d0);
-            hv = *reinterpret_cast<const uint4*>(reinterpret_cast<const __half*>(bb.v) + row * D + d0);
-        } else if (code == 2) {
+        if (r.code == 0) {
+            const uint4* pk = reinterpret_cast<const uint4*>(reinterpret_cast<const float*>(bb.k) + row * D + d0);
+            const uint4* pv = reinterpret_cast<const uint4*>(reinterpret_cast<const float*>(bb.v) + row * D + d0);
+            r.k[a][0] = pk[0];
+            r.k[a][1] = pk[1];
+            r.v[a][0] = pv[0];
+            r.v[a][1] = pv[1];
+        } else if (r.code == 1) {
+            r.k[a][0] = *reinterpret_cast<const uint4*>(reinterpret_cast<const __half*>(bb.k) + row * D + d0);
+            r.v[a][0] = *reinterpret_cast<const uint4*>(reinterpret_cast<const __half*>(bb.v) + row * D + d0);
+        } else if (r.code == 2) {
             const uint2 wk = *reinterpret_cast<const uint2*>(reinterpret_cast<const int8_t*>(bb.k) + row * D + d0);
             const uint2 wv = *reinterpret_cast<const uint2*>(reinterpret_cast<const int8_t*>(bb.v) + row * D + d0);
-            hk = int8x8_to_half(wk.x, wk.y);
-            hv = int8x8_to_half(wv.x, wv.y);
+            r.k[a][0] = make_uint4(wk.x, wk.y, 0, 0);
+            r.v[a][0] = make_uint4(wv.x, wv.y, 0, 0);
+            if (a == 0) {
+                r.sk[0] = bb.scale_k[row];
+                r.sv[0] = bb.scale_v[row];
+            }
         } else {
             const int64_t off = (int64_t)slot_pos(e) * ((int64_t)p.B * D / 2) + (int64_t)b * (D / 2) + d0 / 2;
-            const uint32_t wk = *reinterpret_cast<const uint32_t*>(reinterpret_cast<const uint8_t*>(bb.k) + off);
-            const uint32_t wv = *reinterpret_cast<const uint32_t*>(reinterpret_cast<const uint8_t*>(bb.v) + off);
+            r.k[a][0].x = *reinterpret_cast<const uint32_t*>(reinterpret_cast<const uint8_t*>(bb.k) + off);
+            r.v[a][0].x = *reinterpret_cast<const uint32_t*>(reinterpret_cast<const uint8_t*>(bb.v) + off);
             const int NG = D / p.G;
             const int g = d0 / p.G;
-            hk = int4x8_to_half(wk, bb.scale_k[row * NG + g]);
-            hv = int4x8_to_half(wv, bb.scale_v[row * NG + g]);
+            r.sk[a] = bb.scale_k[row * NG + g];
+            r.sv[a] = bb.scale_v[row * NG + g];
+        }
+    }
+}
+
+// Eight int8 codes times the row scale, in fp32 exactly as the reference dequantises
+// (q * scale), then rounded to fp16.  (q ^ 0x80) | 0x4B000000 is 2^23 + q + 128.
+__device__ __forceinline__ uint4 int8x8_scaled_to_half(uint32_t w0, uint32_t w1, float s) {
+    float v[8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        v[i] = __fmul_rn(__int_as_float(0x4B000000 | (((w0 >> (8 * i)) & 0xFFu) ^ 0x80u)) - 8388736.0f, s);
+        v[4 + i] = __fmul_rn(__int_as_float(0x4B000000 | (((w1 >> (8 * i)) & 0xFFu) ^ 0x80u)) - 8388736.0f, s);
+    }
+    uint4 r;
+    r.x = half2_bits(__floats2half2_rn(v[0], v[1]));
+    r.y = half2_bits(__floats2half2_rn(v[2], v[3]));
+    r.z = half2_bits(__floats2half2_rn(v[4], v[5]));
+    r.w = half2_bits(__floats2half2_rn(v[6], v[7]));
+    return r;
+}
+
+__device__ __forceinline__ uint4 f32x8_bits_to_half(const uint4& a, const uint4& b) {
+    uint4 r;
+    r.x = half2_bits(__floats2half2_rn(__uint_as_float(a.x), __uint_as_float(a.y)));
+    r.y = half2_bits(__floats2half2_rn(__uint_as_float(a.z), __uint_as_float(a.w)));
+    r.z = half2_bits(__floats2half2_rn(__uint_as_float(b.x), __uint_as_float(b.y)));
+    r.w = half2_bits(__floats2half2_rn(__uint_as_float(b.z), __uint_as_float(b.w)));
+    return r;
+}
+
+// Converts one lane's share of a K and a V row to fp16 and stores it, 128B-swizzled, at row
+// `r` of the tiles (zeros for a padding row).
+template <int D>
+__device__ __forceinline__ void store_row(const RawRow<D / 64>& raw, int r, int l8, uint8_t* ktile, uint8_t* vtile) {
+    constexpr int NA = D / 64;
+#pragma unroll
+    for (int a = 0; a < NA; ++a) {
+        uint4 hk = make_uint4(0, 0, 0, 0), hv = make_uint4(0, 0, 0, 0);
+        if (raw.code == 0) {
+            hk = f32x8_bits_to_half(raw.k[a][0], raw.k[a][1]);
+            hv = f32x8_bits_to_half(raw.v[a][0], raw.v[a][1]);
+        } else if (raw.code == 1) {
+            hk = raw.k[a][0];
+            hv = raw.v[a][0];
+        } else if (raw.code == 2) {
+            hk = int8x8_scaled_to_half(raw.k[a][0].x, raw.k[a][0].y, raw.sk[0]);
+            hv = int8x8_scaled_to_half(raw.v[a][0].x, raw.v[a][0].y, raw.sv[0]);
+        } else if (raw.code == 3) {
+            hk = int4x8_to_half(raw.k[a][0].x, raw.sk[a]);
+            hv = int4x8_to_half(raw.v[a][0].x, raw.sv[a]);
         }
         *reinterpret_cast<uint4*>(ktile + a * kBN * 128 + sw128_offset(r, l8)) = hk;
         *reinterpret_cast<uint4*>(vtile + a * kBN * 128 + sw128_offset(r, l8)) = hv;
     }
-    if (code == 2) {
-        fa = __fmul_rn(p.scale_log2, bb.scale_k[row]);
-        fb = bb.scale_v[row];
-    }
-    if (l8 == 0) {
-        col_a[r] = fa;
-        col_b[r] = fb;
-        col_c[r] = 0.0f;
-    }
 }
+
+__device__ __forceinline__ void converters_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kConvWarps * 32) : "memory"); }
 
 template <int D>
 __global__ void __launch_bounds__(kAttnThreads, 1) packed_attention_kernel(AttnParams p) {
@@ -221,7 +265,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) packed_attention_kernel(AttnP
     uint64_t* pv_done = p_full + 1;             // count 1 (commit)
     uint64_t* mma_done = pv_done + 1;           // count 1 (commit), drain before TMEM release
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kTmemSlot);
-    float* col = reinterpret_cast<float*>(smem + L::kCol);
+    int32_t* ent = reinterpret_cast<int32_t*>(smem + L::kEnt);
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
@@ -235,7 +279,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1) packed_attention_kernel(AttnP
         mbar_init(mma_done, 1);
         fence_mbarrier_init();
     }
-    if (warp == 8) {
+    constexpr int kMmaWarp = kSoftmaxWarps + kConvWarps;
+    if (warp == kMmaWarp) {
         tmem_alloc(tmem_slot, kTmemCols);
         tmem_relinquish();
     }
@@ -249,28 +294,35 @@ __global__ void __launch_bounds__(kAttnThreads, 1) packed_attention_kernel(AttnP
         // ------------------------------------------------------------------ softmax
         const int t = threadIdx.x;                       // query row in the tile == TMEM lane
         const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
-        float m_ref = n_ev > 0 ? 0.0f : -INFINITY;
+        const float sl2 = p.scale_log2;
+        float m_ref = n_ev > 0 ? 0.0f : -INFINITY;       // evicted rows: logit 0
         float l = (float)n_ev;
         bool ok = true;
         for (int j = 0; j < nt && ok; ++j) {
-            const int sb = j & 1, s = j % kStages;
+            const int sb = j & 1;
             const uint32_t tS = sb ? tS1 : tS0;
+            const int n_valid = min(kBN, n_stored - j * kBN);
             if (!warp_wait(&s_full[sb], (j >> 1) & 1, p.err, kErrSFull)) { ok = false; break; }
-            // the per-row factors of this tile come from the converters
-            if (!warp_wait(&kv_full[s], (j / kStages) & 1, p.err, kErrKvFull)) { ok = false; break; }
             tc_fence_after();
-            const float* ca = col + (s * 3 + 0) * kBN;
-            const float* cb = col + (s * 3 + 1) * kBN;
-            const float* cc = col + (s * 3 + 2) * kBN;
             uint32_t r[32];
-            float mt = -INFINITY;
+            // pass 1: row max of the raw scores (scale > 0; padding columns score exactly 0,
+            // which can only raise the reference max -- harmless)
+            float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
 #pragma unroll
-            for (int c = 0; c < kBN / 32; ++c) {
+            for (int c = 0; c < kBN / 32; c += 2) {
+                uint32_t r2[32];
                 tmem_ld32(tS + lane_off + c * 32, r);
+                tmem_ld32(tS + lane_off + (c + 1) * 32, r2);
                 tmem_wait_ld();
 #pragma unroll
-                for (int i = 0; i < 32; ++i) mt = fmaxf(mt, fmaf(__uint_as_float(r[i]), ca[c * 32 + i], cc[c * 32 + i]));
+                for (int i = 0; i < 32; i += 2) {
+                    mx0 = fmaxf(mx0, __uint_as_float(r[i]));
+                    mx1 = fmaxf(mx1, __uint_as_float(r[i + 1]));
+                    mx2 = fmaxf(mx2, __uint_as_float(r2[i]));
+                    mx3 = fmaxf(mx3, __uint_as_float(r2[i + 1]));
+                }
             }
+            const float mt = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * sl2;
             bool pv_seen = false;
             const bool need = mt > m_ref + kRescaleThreshold;
             if (__any_sync(0xffffffffu, need)) {
@@ -297,19 +349,30 @@ __global__ void __launch_bounds__(kAttnThreads, 1) packed_attention_kernel(AttnP
                 // the single P buffer is still read by the previous tile's P*V
                 if (!warp_wait(pv_done, (j - 1) & 1, p.err, kErrPvDone)) { ok = false; break; }
             }
+            // pass 2: P = 2^(s*scale - m_ref) in fp16 into shared memory
             uint8_t* ptile = smem + L::kP;
+            const float neg_m = -m_ref;
+            float l0 = 0.f, l1 = 0.f, l2 = 0.f, l3 = 0.f;
 #pragma unroll
             for (int c = 0; c < kBN / 32; ++c) {
                 tmem_ld32(tS + lane_off + c * 32, r);
                 tmem_wait_ld();
+                float pv[32];
+#pragma unroll
+                for (int i = 0; i < 32; ++i) pv[i] = ex2(fmaf(__uint_as_float(r[i]), sl2, neg_m));
+                if (n_valid < kBN) {
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) pv[i] = (c * 32 + i < n_valid) ? pv[i] : 0.0f;
+                }
                 uint32_t hp[16];
 #pragma unroll
-                for (int i = 0; i < 32; i += 2) {
-                    const int col0 = c * 32 + i;
-                    const float p0 = ex2(fmaf(__uint_as_float(r[i]), ca[col0], cc[col0]) - m_ref);
-                    const float p1 = ex2(fmaf(__uint_as_float(r[i + 1]), ca[col0 + 1], cc[col0 + 1]) - m_ref);
-                    l += p0 + p1;
-                    hp[i / 2] = half2_bits(__floats2half2_rn(p0 * cb[col0], p1 * cb[col0 + 1]));
+                for (int i = 0; i < 32; i += 4) {
+                    l0 += pv[i];
+                    l1 += pv[i + 1];
+                    l2 += pv[i + 2];
+                    l3 += pv[i + 3];
+                    hp[i / 2] = half2_bits(__floats2half2_rn(pv[i], pv[i + 1]));
+                    hp[i / 2 + 1] = half2_bits(__floats2half2_rn(pv[i + 2], pv[i + 3]));
                 }
                 // columns c*32 .. c*32+31 = 4 chunks of 8 in atom c/2
                 uint8_t* atom = ptile + (c >> 1) * kBM * 128;
@@ -320,6 +383,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) packed_attention_kernel(AttnP
                         make_uint4(hp[4 * k], hp[4 * k + 1], hp[4 * k + 2], hp[4 * k + 3]);
                 }
             }
+            l += (l0 + l1) + (l2 + l3);
             tc_fence_before();
             fence_proxy_async_smem();
             __syncwarp();
@@ -353,10 +417,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1) packed_attention_kernel(AttnP
     } else if (warp < kSoftmaxWarps + kConvWarps) {
         // --------------------------------------------------------------- converters
         const int wc = warp - kSoftmaxWarps;
+        const int ctid = threadIdx.x - kSoftmaxWarps * 32;      // 0 .. 32*kConvWarps-1
         const int lrow = lane >> 3, l8 = lane & 7;
         uint8_t* qtile = smem + L::kQ;
-        for (int step = 0; step < kBM / 16; ++step) {
-            const int r = step * 16 + wc * 4 + lrow;
+        const int32_t* hrows = p.rows + (int64_t)h * p.S_kv;
+        int32_t next_e = (ctid < kBN && ctid < n_stored) ? hrows[ctid] : -1;   // entry list of tile 0
+        constexpr int kRowsPerStep = kConvWarps * 4;
+        for (int step = 0; step < kBM / kRowsPerStep; ++step) {
+            const int r = step * kRowsPerStep + wc * 4 + lrow;
             const int qi = q0 + r;
 #pragma unroll
             for (int a = 0; a < NA; ++a) {
@@ -366,20 +434,36 @@ __global__ void __launch_bounds__(kAttnThreads, 1) packed_attention_kernel(AttnP
                 *reinterpret_cast<uint4*>(qtile + a * kBM * 128 + sw128_offset(r, l8)) = v;
             }
         }
-        const int32_t* hrows = p.rows + (int64_t)h * p.S_kv;
+        constexpr int kRowsPerBatch = 2;       // rows whose loads are in flight together
+        volatile int* conv_fail = reinterpret_cast<volatile int*>(smem + L::kTmemSlot + 8);
+        if (ctid == 0) *conv_fail = 0;
+        converters_sync();
         for (int j = 0; j < nt; ++j) {
             const int s = j % kStages;
-            if (j >= kStages && !warp_wait(&kv_empty[s], ((j / kStages) - 1) & 1, p.err, kErrKvEmpty)) break;
+            const bool ok = j < kStages || warp_wait(&kv_empty[s], ((j / kStages) - 1) & 1, p.err, kErrKvEmpty);
+            if (!ok && lane == 0) *conv_fail = 1;
+            int32_t* e_tile = ent + s * kBN;
+            if (ok && ctid < kBN) e_tile[ctid] = next_e;
+            const int nxt = (j + 1) * kBN + ctid;
+            next_e = (ctid < kBN && j + 1 < nt && nxt < n_stored) ? hrows[nxt] : -1;
+            // every converter warp reaches this barrier on every tile, so one warp's timeout
+            // stops all four together instead of leaving the others waiting here
+            converters_sync();
+            if (*conv_fail) break;
             uint8_t* ktile = smem + L::kK + s * NA * kBN * 128;
             uint8_t* vtile = smem + L::kV + s * NA * kBN * 128;
-            float* ca = col + (s * 3 + 0) * kBN;
-            float* cb = col + (s * 3 + 1) * kBN;
-            float* cc = col + (s * 3 + 2) * kBN;
-            for (int step = 0; step < kBN / 16; ++step) {
-                const int r = step * 16 + wc * 4 + lrow;
-                const int idx = j * kBN + r;
-                const int32_t e = idx < n_stored ? hrows[idx] : -1;
-                convert_row<D>(p, b, e, r, l8, ktile, vtile, ca, cb, cc);
+            for (int step = 0; step < kBN / kRowsPerStep; step += kRowsPerBatch) {
+                RawRow<NA> raw[kRowsPerBatch];
+#pragma unroll
+                for (int i = 0; i < kRowsPerBatch; ++i) {
+                    const int r = (step + i) * kRowsPerStep + wc * 4 + lrow;
+                    load_raw_row<D>(p, b, e_tile[r], l8, raw[i]);
+                }
+#pragma unroll
+                for (int i = 0; i < kRowsPerBatch; ++i) {
+                    const int r = (step + i) * kRowsPerStep + wc * 4 + lrow;
+                    store_row<D>(raw[i], r, l8, ktile, vtile);
+                }
             }
             fence_proxy_async_smem();
             __syncwarp();
@@ -433,7 +517,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) packed_attention_kernel(AttnP
 
     tc_fence_before();
     __syncthreads();
-    if (warp == 8) {
+    if (warp == kMmaWarp) {
         tc_fence_after();
         tmem_dealloc(tmem, kTmemCols);
     }
