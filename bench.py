@@ -19,6 +19,11 @@ payload copied out).  ``roofline`` covers the pack kernel (the dominant
 kernel), timed with CUDA events around each launch in the timed region.
 ``--impl reference`` times the CPU restatement of the reference algorithm
 (``oracle/``) on a head slice of the same workload, on rank 0 only.
+
+The line also carries ``attention``: packed attention over one cfg3 layer
+(B=1, H=32, S=4096, D=128, codes 20/50/30 % fp16/int8/int4), heads sharded over
+the ranks with an NCCL all-gather of the outputs, as tokens/s of the 32-layer
+stack and as tensor-core roofline of the kernel.
 """
 
 from __future__ import annotations
@@ -46,6 +51,7 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
     ap.add_argument("--ref-heads", type=int, default=8, help="head slice timed by the CPU reference arm")
+    ap.add_argument("--no-attention", action="store_true", help="skip the packed-attention measurement")
     return ap.parse_args()
 
 
@@ -212,6 +218,119 @@ def run_reference(args):
     return 0
 
 
+# ------------------------------------------------------------------------------- attention
+def attention_phase(args, world, rank, dev, dist, lib, tensor_peak):
+    """Packed attention on one cfg3 layer, heads sharded over ranks, outputs all-gathered.
+
+    One step = the layer's attention (this rank's heads) + an NCCL all-gather of the fp32
+    outputs on a side stream, so the gather of one step overlaps the next step's kernel.
+    """
+    import torch
+
+    from shadow_infer_b200 import workloads as W
+    from shadow_infer_b200.shadowkv import PackedKVCache, PrecisionPlan, packed_attention
+    from shadow_infer_b200.shadowkv.shadowkv_agent import allocate_precision_codes
+
+    c = W.CONFIGS["cfg3"]
+    B, H, S, D, L = c["B"], c["H"], c["S"], c["D"], c["layers"]
+    if H % world:
+        raise ValueError(f"{H} heads do not shard over {world} GPUs")
+    hs, h0 = H // world, rank * (H // world)
+    k, v = W.kv_tensors(B, H, S, D, 0)
+    imp = W.importance_map(S, H, 0, c["fractions"])
+    q = W.queries(B, H, S, D, 0)
+    k, v = k[:, h0:h0 + hs].contiguous(), v[:, h0:h0 + hs].contiguous()
+    codes = allocate_precision_codes(imp[:, h0:h0 + hs].contiguous().to(dev), "balanced")
+    cache = PackedKVCache.pack(k.to(dev), v.to(dev), None, c["group"], plan=PrecisionPlan.from_codes(codes))["packed_kv"]
+    qd = q[:, h0:h0 + hs].contiguous().to(dev)
+    packed_attention(qd, cache)                        # builds the head index, checks the error word
+    from shadow_infer_b200.shadowkv.sharding import all_gather_heads
+    gathered = torch.empty(B, H, S, D, dtype=torch.float32, device=dev)
+    comm = torch.cuda.Stream(device=dev)
+    steps = max(3, min(args.steps, 32))
+    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+
+    def step(i=None):
+        if i is not None:
+            kev[i][0].record()
+        out = packed_attention(qd, cache, check=False)
+        if i is not None:
+            kev[i][1].record()
+        if world > 1:
+            done = torch.cuda.Event()
+            done.record()
+            with torch.cuda.stream(comm):
+                comm.wait_event(done)
+                all_gather_heads(out, out=gathered)
+            out.record_stream(comm)
+        return out
+
+    for _ in range(3):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    n0 = lib.skv_launch_count()
+    t0.record()
+    for i in range(steps):
+        step(i)
+    if world > 1:
+        tail = torch.cuda.Event()
+        tail.record(comm)
+        torch.cuda.current_stream().wait_event(tail)
+    t1.record()
+    torch.cuda.synchronize()
+    launches = lib.skv_launch_count() - n0
+    packed_attention(qd, cache)                        # error word of the last launch
+    ms = torch.tensor([t0.elapsed_time(t1) / steps], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    ms = float(ms.item())
+    kms = statistics.mean(a.elapsed_time(b) for a, b in kev)
+    flops_rank = 4.0 * B * hs * S * S * D
+    res = {
+        "metric": "packed-attn tokens/s (32-layer stack, cfg3)",
+        "value": B * S / (L * ms / 1e3), "unit": "tokens/s", "ms_per_layer": ms, "steps": steps,
+        "scaling": "strong (heads sharded over GPUs, NCCL all-gather of outputs)",
+        "config": {"workload": "cfg3: packed K/V codes 20/50/30 fp16/int8/int4, fp16 queries, non-causal",
+                   "B": B, "H": H, "S_q": S, "S_kv": S, "D": D, "layers": L, "heads_per_gpu": hs},
+        "roofline": {"kernel": "packed_attention_kernel", "bound": "tensor",
+                     "achieved": flops_rank / (kms / 1e3) / 1e12, "peak": tensor_peak[0], "unit": "TFLOP/s",
+                     "frac": flops_rank / (kms / 1e3) / 1e12 / tensor_peak[0],
+                     "peak_source": tensor_peak[1], "avg_launch_ms": kms, "flops_per_launch": flops_rank,
+                     "traffic": None},
+        "gpu_launches": launches,
+        "output_dtype": "f32",
+    }
+    if world == 1 and rank == 0:
+        import numpy as np
+        from oracle import shadowkv_oracle as O
+
+        ko, vo = k[:, :1].numpy().copy(), v[:, :1].numpy().copy()
+        co = codes[:, :1].cpu().numpy()
+        cache_o = O.pack(ko, vo, O.plan_from_codes(co), c["group"])
+        qo = q[:, :1].float().numpy()
+        t = time.perf_counter()
+        O.packed_attention(qo, cache_o)
+        dt = time.perf_counter() - t
+        res["cpu_baseline"] = {"value": B * S / (dt * H * L), "unit": "tokens/s", "cores": os.cpu_count(),
+                               "kind": "port",
+                               "sample": "oracle unpack + float64 numpy attention of head 0 of the layer, "
+                                         "extrapolated x32 heads x32 layers"}
+    return res
+
+
+def tensor_peak():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured bf16_tflops (burst; fp16 runs at the same rate)"
+    except Exception:
+        return 1590.0, "fallback"
+
+
 # ------------------------------------------------------------------------------------ b200
 def run_b200(args):
     import torch
@@ -350,6 +469,7 @@ def run_b200(args):
         dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
     e2e_ms = float(e2e_ms.item())
     h2d = (hk.numel() + hv.numel() + himp.numel()) * 4 + hreuse.numel()
+    attn = attention_phase(args, world, rank, dev, dist, lib, tensor_peak()) if not args.no_attention else None
     if sampler:
         sampler.stop()
 
@@ -380,6 +500,7 @@ def run_b200(args):
                 "ms_per_step": e2e_ms / e2e_steps},
         "gpu_launches": launches,
         "clocks": sampler.summary() if sampler else None,
+        "attention": attn,
     }
     if world == 1:
         run = reference_sample(I, args.ref_heads)

@@ -1,0 +1,96 @@
+"""Head sharding of the data plane over the GPUs of one node (torch.distributed, NCCL).
+
+Every operation on the path is independent per attention head except budget
+admission, which ranks all (token, head) entries of a layer together.  A layer can
+therefore be split by heads: rank ``r`` of ``n`` owns heads ``[r*H/n, (r+1)*H/n)``
+and packs, unpacks, reuses, evicts and attends over them locally.  Two exchange
+steps remain:
+
+* ``admit_codes_sharded`` -- all-gather of the ``[S, H/n]`` codes, importance and
+  sensitivity slices; every rank then runs the same deterministic admission on the
+  full ``[S, H]`` problem and keeps its own columns, so the result equals the
+  single-GPU admission exactly.
+* ``all_gather_heads`` -- the attention outputs ``[B, H/n, S, D]`` of all ranks
+  assembled into ``[B, H, S, D]`` (one NCCL all-gather).
+
+The collectives go through ``torch.distributed``, so the same code runs on a gloo
+(CPU) group in tests.
+"""
+
+from __future__ import annotations
+
+from typing import Optional, Tuple
+
+import torch
+import torch.distributed as dist
+
+
+def head_range(num_heads: int, world_size: int, rank: int) -> Tuple[int, int]:
+    """Heads ``[h0, h1)`` owned by ``rank``; heads must divide evenly."""
+    if world_size <= 0 or not 0 <= rank < world_size:
+        raise ValueError(f"bad rank {rank} for world size {world_size}")
+    if num_heads % world_size:
+        raise ValueError(f"{num_heads} heads do not shard evenly over {world_size} ranks")
+    per = num_heads // world_size
+    return rank * per, (rank + 1) * per
+
+
+def _world(group) -> Tuple[int, int]:
+    return dist.get_world_size(group), dist.get_rank(group)
+
+
+def all_gather_heads(local: torch.Tensor, group=None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``[B, h, ...]`` per rank -> ``[B, world*h, ...]`` in rank order (heads are dim 1)."""
+    n, _ = _world(group)
+    local = local.contiguous()
+    buf = torch.empty((n * local.shape[0],) + tuple(local.shape[1:]), dtype=local.dtype, device=local.device)
+    dist.all_gather_into_tensor(buf, local, group=group)
+    buf = buf.view((n,) + tuple(local.shape))
+    full = buf.movedim(0, 1).reshape((local.shape[0], n * local.shape[1]) + tuple(local.shape[2:]))
+    if out is not None:
+        out.copy_(full)
+        return out
+    return full
+
+
+def all_gather_columns(local: torch.Tensor, group=None) -> torch.Tensor:
+    """``[S, h]`` per rank -> ``[S, world*h]`` (token-major maps of one layer)."""
+    n, _ = _world(group)
+    local = local.contiguous()
+    buf = torch.empty((n * local.shape[0],) + tuple(local.shape[1:]), dtype=local.dtype, device=local.device)
+    dist.all_gather_into_tensor(buf, local, group=group)
+    return buf.view((n,) + tuple(local.shape)).permute(1, 0, 2).reshape(local.shape[0], n * local.shape[1])
+
+
+def admit_codes_sharded(
+    codes_local: torch.Tensor,
+    importance_local: torch.Tensor,
+    sensitivity_local: Optional[torch.Tensor],
+    budget_bytes: Optional[int],
+    batch: int,
+    head_dim: int,
+    sink_tokens: int = 0,
+    rd_allocation: bool = True,
+    allow_eviction: bool = False,
+    protected_local: Optional[torch.Tensor] = None,
+    group=None,
+    group_size: int = 16,
+    admit=None,
+) -> Tuple[torch.Tensor, int, int]:
+    """Budget admission of a head-sharded layer; identical to the unsharded ``admit_codes``.
+
+    ``budget_bytes`` is the budget of the WHOLE layer.  Returns this rank's columns of
+    the admitted codes and the layer-wide predicted bytes and eviction count.
+    ``admit`` defaults to ``rd_allocator.admit_codes`` (the GPU kernel).
+    """
+    if admit is None:
+        from .rd_allocator import admit_codes as admit
+    n, r = _world(group)
+    h = codes_local.shape[1]
+    codes = all_gather_columns(codes_local.to(torch.int8), group)
+    imp = all_gather_columns(importance_local.float(), group)
+    sens = all_gather_columns(sensitivity_local.float(), group) if sensitivity_local is not None else None
+    prot = all_gather_columns(protected_local.to(torch.uint8), group).bool() if protected_local is not None else None
+    out, predicted, evicted = admit(codes, imp, sens, budget_bytes, batch, head_dim, sink_tokens, rd_allocation,
+                                    allow_eviction, prot, group_size)
+    return out[:, r * h:(r + 1) * h].contiguous(), predicted, evicted
