@@ -7,211 +7,283 @@
 //  * skv_unpack -- PackedKVCache.unpack / _dequantize_int4_bucket (packed_kv_cache.py:535-577,
 //                  :636-656).
 //
-// Both walk K/V in memory order ([B,H,S,D] rows, one warp per row of D floats), so the
-// fp32 side is streamed with 128-bit loads/stores; the per-entry slot (bucket position
-// from the plan) gives the packed side.  HBM-bound: a row costs 2*D*4 bytes of fp32 plus
-// the packed row.  Quantisation is bit-exact with the reference's torch CPU arithmetic:
-// IEEE division (no fast-math), round-half-even, clamp, nibble = q + 8, high nibble first.
+// Both walk K/V in memory order ([B,H,S,D] rows), so the fp32 side is streamed with 128-bit
+// loads/stores; the per-entry slot (bucket position from the plan) locates the packed row.
+// Lane layout of the vectorised kernels: every lane owns 16 consecutive values of a row
+// (one int4 group at group size 16), D/16 lanes per row, 32/(D/16) rows per warp.  The
+// int8 and int4 quantisers share one instruction stream (only the reduction width, the
+// divisor and the final packing differ), so rows of both kinds in one warp do not diverge.
+//
+// Bit-exactness with the reference's torch CPU arithmetic: scale = IEEE amax/qmax (0 -> 1);
+// q = clamp(rint(fl(x/scale))).  Each value is rounded from y = x * rcp(scale) with the
+// 1.5*2^23 magic-number trick (round-half-even in the FP32 adder); a value whose y lies
+// within 1e-4 of a .5 tie is recomputed with the exact IEEE division (|y - fl(x/scale)| is
+// at most ~2.3e-5 for |y| <= 128, so elsewhere both round identically).  Packing uses
+// cvt.pack.sat (int8: saturating s8; int4: saturating u4 of q + 8, high nibble first).
+// Built without fast-math.
 #include "skv_common.cuh"
 
 namespace skv {
 
-template <int VEC>
-struct Vec;
-template <>
-struct Vec<2> {
-    static __device__ __forceinline__ void load(const float* p, float (&x)[2]) {
-        const float2 a = __ldcs(reinterpret_cast<const float2*>(p));
-        x[0] = a.x; x[1] = a.y;
-    }
-    static __device__ __forceinline__ void store(float* p, const float (&x)[2]) {
-        *reinterpret_cast<float2*>(p) = make_float2(x[0], x[1]);
-    }
-};
-template <>
-struct Vec<4> {
-    static __device__ __forceinline__ void load(const float* p, float (&x)[4]) {
-        const float4 a = __ldcs(reinterpret_cast<const float4*>(p));
-        x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
-    }
-    static __device__ __forceinline__ void store(float* p, const float (&x)[4]) {
-        *reinterpret_cast<float4*>(p) = make_float4(x[0], x[1], x[2], x[3]);
-    }
-};
-template <>
-struct Vec<8> {
-    static __device__ __forceinline__ void load(const float* p, float (&x)[8]) {
-        const float4 a = __ldcs(reinterpret_cast<const float4*>(p));
-        const float4 b = __ldcs(reinterpret_cast<const float4*>(p) + 1);
-        x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
-        x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
-    }
-    static __device__ __forceinline__ void store(float* p, const float (&x)[8]) {
-        reinterpret_cast<float4*>(p)[0] = make_float4(x[0], x[1], x[2], x[3]);
-        reinterpret_cast<float4*>(p)[1] = make_float4(x[4], x[5], x[6], x[7]);
-    }
-};
-
-template <int N>
-__device__ __forceinline__ void store_bytes(uint8_t* p, const uint8_t (&b)[N]) {
-    if constexpr (N == 1) {
-        p[0] = b[0];
-    } else if constexpr (N == 2) {
-        *reinterpret_cast<uint16_t*>(p) = (uint16_t)(b[0] | (b[1] << 8));
-    } else if constexpr (N == 4) {
-        *reinterpret_cast<uint32_t*>(p) =
-            (uint32_t)b[0] | ((uint32_t)b[1] << 8) | ((uint32_t)b[2] << 16) | ((uint32_t)b[3] << 24);
-    } else {
+// ---------------------------------------------------------------------------------------
+// 16-value lane helpers
+// ---------------------------------------------------------------------------------------
+__device__ __forceinline__ void ld16_stream(const float* p, float (&x)[16]) {
+    const float4* q = reinterpret_cast<const float4*>(p);
 #pragma unroll
-        for (int i = 0; i < N; i += 4) {
-            *reinterpret_cast<uint32_t*>(p + i) = (uint32_t)b[i] | ((uint32_t)b[i + 1] << 8) |
-                                                  ((uint32_t)b[i + 2] << 16) | ((uint32_t)b[i + 3] << 24);
+    for (int i = 0; i < 4; ++i) {
+        const float4 a = __ldcs(q + i);
+        x[4 * i] = a.x;
+        x[4 * i + 1] = a.y;
+        x[4 * i + 2] = a.z;
+        x[4 * i + 3] = a.w;
+    }
+}
+
+__device__ __forceinline__ void st16(float* p, const float (&x)[16]) {
+    float4* q = reinterpret_cast<float4*>(p);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) q[i] = make_float4(x[4 * i], x[4 * i + 1], x[4 * i + 2], x[4 * i + 3]);
+}
+
+// Per-warp staging of RPW fp32 rows of D values (RPW*D*4 = 2 KB at D=128) in shared memory.
+// 16-byte chunk c of a row lives at chunk c ^ ((c >> 2) & 7): the coalesced side (lane i ->
+// chunk i + 32k) and the per-lane side (lane l of a row -> chunks 4l .. 4l+3) both touch 8
+// distinct bank groups per 8 lanes, i.e. the 4-wavefront minimum per 512-byte access.
+__device__ __forceinline__ int stage_chunk(int c) { return c ^ ((c >> 2) & 7); }
+
+// Coalesced global -> staging copy of `rows` (<= RPW) contiguous rows starting at `src`.
+template <int D, int RPW>
+__device__ __forceinline__ void stage_in(float4* stage, const float* src, int rows, int lane) {
+    constexpr int CPR = D / 4;                 // 16-byte chunks per row
+    const float4* g = reinterpret_cast<const float4*>(src);
+#pragma unroll
+    for (int k = 0; k < RPW * CPR / 32; ++k) {
+        const int q = lane + 32 * k;
+        const int r = q / CPR, c = q % CPR;
+        if (r < rows) stage[r * CPR + stage_chunk(c)] = __ldcs(g + q);
+    }
+}
+
+template <int D, int RPW>
+__device__ __forceinline__ void stage_out(const float4* stage, float* dst, int rows, int lane) {
+    constexpr int CPR = D / 4;
+    float4* g = reinterpret_cast<float4*>(dst);
+#pragma unroll
+    for (int k = 0; k < RPW * CPR / 32; ++k) {
+        const int q = lane + 32 * k;
+        const int r = q / CPR, c = q % CPR;
+        if (r < rows) g[q] = stage[r * CPR + stage_chunk(c)];
+    }
+}
+
+// The 16 values owned by lane l (chunks 4l .. 4l+3) of staged row r.
+template <int D>
+__device__ __forceinline__ void stage_get(const float4* stage, int r, int l, float (&x)[16]) {
+    constexpr int CPR = D / 4;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const float4 a = stage[r * CPR + stage_chunk(4 * l + j)];
+        x[4 * j] = a.x;
+        x[4 * j + 1] = a.y;
+        x[4 * j + 2] = a.z;
+        x[4 * j + 3] = a.w;
+    }
+}
+
+template <int D>
+__device__ __forceinline__ void stage_put(float4* stage, int r, int l, const float (&x)[16]) {
+    constexpr int CPR = D / 4;
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+        stage[r * CPR + stage_chunk(4 * l + j)] = make_float4(x[4 * j], x[4 * j + 1], x[4 * j + 2], x[4 * j + 3]);
+}
+
+// d = (c << 16) | (sat_s8(a) << 8) | sat_s8(b)
+__device__ __forceinline__ uint32_t pack_s8(int a, int b, uint32_t c) {
+    uint32_t d;
+    asm("cvt.pack.sat.s8.s32.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+// d = (c << 8) | (sat_u4(a) << 4) | sat_u4(b)
+__device__ __forceinline__ uint32_t pack_u4(int a, int b, uint32_t c) {
+    uint32_t d;
+    asm("cvt.pack.sat.u4.s32.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+constexpr float kRoundMagic = 12582912.0f;   // 1.5 * 2^23: adding it rounds |y| < 2^22 to an integer
+
+// q[i] = clamp(rint(fl(x[i] / s)), lo, hi) for 16 values; qf[i] = (float)q[i].
+__device__ __forceinline__ void quant16(const float (&x)[16], float s, float r, int lo, int hi, int (&q)[16],
+                                        float (&qf)[16]) {
+    bool slow = false;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+        const float y = __fmul_rn(x[i], r);
+        const float t = __fadd_rn(y, kRoundMagic);
+        const float rf = __fsub_rn(t, kRoundMagic);
+        slow |= !(fabsf(__fsub_rn(y, rf)) < 0.4999f);
+        q[i] = __float_as_int(t) - 0x4B400000;
+        qf[i] = rf;
+    }
+    if (slow) {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            q[i] = quant_value(x[i], s, lo, hi);
+            qf[i] = (float)q[i];
         }
     }
 }
 
-template <int N>
-__device__ __forceinline__ void load_bytes(const uint8_t* p, uint8_t (&b)[N]) {
-    if constexpr (N == 1) {
-        b[0] = p[0];
-    } else if constexpr (N == 2) {
-        const uint16_t w = *reinterpret_cast<const uint16_t*>(p);
-        b[0] = w & 0xff; b[1] = w >> 8;
-    } else {
-#pragma unroll
-        for (int i = 0; i < N; i += 4) {
-            const uint32_t w = *reinterpret_cast<const uint32_t*>(p + i);
-            b[i] = w & 0xff; b[i + 1] = (w >> 8) & 0xff; b[i + 2] = (w >> 16) & 0xff; b[i + 3] = w >> 24;
-        }
-    }
-}
-
-// Quantises one row slice (VEC values per lane, D = 32*VEC) into bucket `p` at entry `pos`,
-// batch `b`; `dense` receives the compress_kv working-copy values.
-template <int VEC>
-__device__ __forceinline__ void pack_row(const float (&x)[VEC], int code, int64_t pos, int b, int B,
-                                         int G, void* payload, float* scale, float (&dense)[VEC],
-                                         int lane) {
-    constexpr int D = 32 * VEC;
+// ---------------------------------------------------------------------------------------
+// pack
+// ---------------------------------------------------------------------------------------
+// One lane's 16 values of row (pos, b) into bucket `code`.  m_row / m_grp: absmax over the
+// whole row and over this lane's int4 group (already reduced across lanes by the caller).
+template <int LPR>
+__device__ __forceinline__ void pack_lane(const float (&x)[16], int code, int64_t pos, int b, int B, int G,
+                                          const skv_bucket& bb, bool is_v, float m_row, float m_grp,
+                                          float (&dense)[16], int l) {
+    constexpr int D = LPR * 16;
     const int64_t row = pos * B + b;
+    void* payload = is_v ? bb.v : bb.k;
+    float* scale = is_v ? bb.scale_v : bb.scale_k;
     if (code == 0) {
-        Vec<VEC>::store(reinterpret_cast<float*>(payload) + row * D + lane * VEC, x);
+        st16(reinterpret_cast<float*>(payload) + row * D + l * 16, x);
 #pragma unroll
-        for (int j = 0; j < VEC; ++j) dense[j] = x[j];
+        for (int i = 0; i < 16; ++i) dense[i] = x[i];
     } else if (code == 1) {
-        __half h[VEC];
+        uint32_t h[8];
 #pragma unroll
-        for (int j = 0; j < VEC; ++j) {
-            h[j] = __float2half_rn(x[j]);
-            dense[j] = __half2float(h[j]);
+        for (int i = 0; i < 8; ++i) {
+            const __half2 v = __floats2half2_rn(x[2 * i], x[2 * i + 1]);
+            h[i] = *reinterpret_cast<const uint32_t*>(&v);
+            const float2 f = __half22float2(v);
+            dense[2 * i] = f.x;
+            dense[2 * i + 1] = f.y;
         }
-        __half* dst = reinterpret_cast<__half*>(payload) + row * D + lane * VEC;
-        if constexpr (VEC == 2) {
-            *reinterpret_cast<__half2*>(dst) = __halves2half2(h[0], h[1]);
-        } else {
-#pragma unroll
-            for (int j = 0; j < VEC; j += 4) {
-                uint2 u;
-                u.x = (uint32_t)__half_as_ushort(h[j]) | ((uint32_t)__half_as_ushort(h[j + 1]) << 16);
-                u.y = (uint32_t)__half_as_ushort(h[j + 2]) | ((uint32_t)__half_as_ushort(h[j + 3]) << 16);
-                *reinterpret_cast<uint2*>(dst + j) = u;
-            }
-        }
-    } else if (code == 2) {
-        float m = 0.0f;
-#pragma unroll
-        for (int j = 0; j < VEC; ++j) m = fmaxf(m, fabsf(x[j]));
-        m = warp_max(m);
-        const float s = quant_scale(m, 127.0f);
-        const float r = __frcp_rn(s);
-        uint8_t q[VEC];
-#pragma unroll
-        for (int j = 0; j < VEC; ++j) {
-            const int v = quant_value_fast(x[j], s, r, -128, 127);
-            q[j] = (uint8_t)(int8_t)v;
-            dense[j] = (float)v;
-        }
-        store_bytes<VEC>(reinterpret_cast<uint8_t*>(payload) + row * D + lane * VEC, q);
-        if (lane == 0) scale[row] = s;
-    } else if (code == 3) {
-        // the fast path requires the group to span a power-of-two number of whole lanes
-        const int NG = D / G;
-        float m = 0.0f;
-#pragma unroll
-        for (int j = 0; j < VEC; ++j) m = fmaxf(m, fabsf(x[j]));
-        const int L = G / VEC;
-        m = group_max(m, L);
-        const float s = quant_scale(m, 7.0f);
-        const float r = __frcp_rn(s);
-        if ((lane & (L - 1)) == 0) scale[row * NG + (lane * VEC) / G] = s;
-        uint8_t bytes[VEC / 2];
-#pragma unroll
-        for (int j = 0; j < VEC; j += 2) {
-            const int q0 = quant_value_fast(x[j], s, r, -8, 7);
-            const int q1 = quant_value_fast(x[j + 1], s, r, -8, 7);
-            dense[j] = (float)q0;
-            dense[j + 1] = (float)q1;
-            bytes[j / 2] = (uint8_t)(((q0 + 8) << 4) | ((q1 + 8) & 0x0F));
-        }
-        const int64_t rb = (int64_t)B * D / 2;
-        store_bytes<VEC / 2>(reinterpret_cast<uint8_t*>(payload) + pos * rb + (int64_t)b * (D / 2) +
-                                 lane * (VEC / 2),
-                             bytes);
+        uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__half*>(payload) + row * D + l * 16);
+        dst[0] = make_uint4(h[0], h[1], h[2], h[3]);
+        dst[1] = make_uint4(h[4], h[5], h[6], h[7]);
     } else {
+        // int8 (code 2) and int4 (code 3)
+        const bool i4 = code == 3;
+        const float s = quant_scale(i4 ? m_grp : m_row, i4 ? 7.0f : 127.0f);
+        const float r = __frcp_rn(s);
+        int q[16];
+        quant16(x, s, r, i4 ? -8 : -128, i4 ? 7 : 127, q, dense);
+        if (i4) {
+            uint32_t w[2];
 #pragma unroll
-        for (int j = 0; j < VEC; ++j) dense[j] = 0.0f;
+            for (int k = 0; k < 2; ++k) {
+                uint32_t a = pack_u4(q[8 * k + 6] + 8, q[8 * k + 7] + 8, 0u);
+                a = pack_u4(q[8 * k + 4] + 8, q[8 * k + 5] + 8, a);
+                a = pack_u4(q[8 * k + 2] + 8, q[8 * k + 3] + 8, a);
+                w[k] = pack_u4(q[8 * k] + 8, q[8 * k + 1] + 8, a);
+            }
+            const int64_t rb = (int64_t)B * D / 2;
+            *reinterpret_cast<uint2*>(reinterpret_cast<uint8_t*>(payload) + pos * rb + (int64_t)b * (D / 2) + l * 8) =
+                make_uint2(w[0], w[1]);
+            const int lpg = G >> 4;   // lanes per int4 group
+            if ((l & (lpg - 1)) == 0) scale[row * (D / G) + (l * 16) / G] = s;
+        } else {
+            uint32_t w[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) w[k] = pack_s8(q[4 * k + 1], q[4 * k], pack_s8(q[4 * k + 3], q[4 * k + 2], 0u));
+            *reinterpret_cast<uint4*>(reinterpret_cast<int8_t*>(payload) + row * D + l * 16) =
+                make_uint4(w[0], w[1], w[2], w[3]);
+            if (l == 0) scale[row] = s;
+        }
     }
 }
 
-// Grid: x over token chunks of 8 warps * RPW rows, y over (b, h).  Each warp loads all
-// of its RPW K and V rows (128-bit streaming loads) before quantising any of them.
-template <int VEC, int RPW>
-__global__ void __launch_bounds__(256) pack_fast_kernel(
-    const float* __restrict__ k, const float* __restrict__ v, int B, int H, int S, int G,
-    const int32_t* __restrict__ slot, Buckets bk, float* __restrict__ dense_k,
-    float* __restrict__ dense_v, const float* __restrict__ k_prev, const float* __restrict__ v_prev,
-    const uint8_t* __restrict__ reuse) {
-    constexpr int D = 32 * VEC;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int bh = blockIdx.y;
-    const int h = bh % H, b = bh / H;
-    const int t0 = (blockIdx.x * 8 + warp) * RPW;
-    if (t0 >= S) return;
-    const int64_t base = (int64_t)bh * S * D + lane * VEC;
-    float xk[RPW][VEC], xv[RPW][VEC];
-    int32_t sl[RPW];
+// absmax of a lane's 16 values, reduced over its int4 group (m_grp) and its row (m_row).
+// Every lane of the warp executes the shuffles, whatever its row's precision.
+template <int LPR>
+__device__ __forceinline__ void row_group_max(const float (&x)[16], int G, float& m_row, float& m_grp) {
+    float m = 0.0f;
 #pragma unroll
-    for (int i = 0; i < RPW; ++i) {
-        const int t = t0 + i;
-        if (t < S) {
-            Vec<VEC>::load(k + base + (int64_t)t * D, xk[i]);
-            Vec<VEC>::load(v + base + (int64_t)t * D, xv[i]);
-            sl[i] = slot[t * H + h];
-        }
+    for (int i = 0; i < 16; ++i) m = fmaxf(m, fabsf(x[i]));
+    const int lpg = G >> 4;
+    m_grp = m;
+#pragma unroll
+    for (int o = 1; o < LPR; o <<= 1) {
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        if ((o << 1) == lpg) m_grp = m;
     }
-#pragma unroll
-    for (int i = 0; i < RPW; ++i) {
-        const int t = t0 + i;
-        if (t >= S) break;
-        const int code = sl[i] < 0 ? kCodeEvicted : slot_code(sl[i]);
-        const int64_t pos = sl[i] < 0 ? 0 : slot_pos(sl[i]);
-        float dk[VEC], dv[VEC];
-        if (code < kCodeEvicted) {
-            const skv_bucket& bb = bk.b[code];
-            pack_row<VEC>(xk[i], code, pos, b, B, G, bb.k, bb.scale_k, dk, lane);
-            pack_row<VEC>(xv[i], code, pos, b, B, G, bb.v, bb.scale_v, dv, lane);
+    m_row = m;
+}
+
+// Grid: x over (b, h), y over chunks of 8 warps * (32/LPR) rows.  A warp's RPW consecutive
+// token rows of K and of V are contiguous in memory: they are fetched with coalesced 128-bit
+// loads into the warp's staging buffer, then each lane quantises its 16 values, K first,
+// then V (one tensor live at a time keeps the register count low).  DENSE adds the
+// compress_kv working copy, staged back and stored coalesced.
+template <int LPR, bool DENSE>
+__global__ void __launch_bounds__(256, 4) pack16_kernel(
+    const float* __restrict__ k, const float* __restrict__ v, int B, int H, int S, int G,
+    const int32_t* __restrict__ slot, Buckets bk, float* __restrict__ dense_k, float* __restrict__ dense_v,
+    const float* __restrict__ k_prev, const float* __restrict__ v_prev, const uint8_t* __restrict__ reuse) {
+    constexpr int D = LPR * 16;
+    constexpr int RPW = 32 / LPR;
+    constexpr int CPR = D / 4;
+    constexpr int kStageF4 = RPW * CPR;                   // float4s per staged tensor
+    __shared__ float4 s_stage[8][2][kStageF4];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int l = lane % LPR, rsub = lane / LPR;
+    const int bh = blockIdx.x;
+    const int h = bh % H, b = bh / H;
+    const int t0 = (blockIdx.y * 8 + warp) * RPW;
+    if (t0 >= S) return;                                  // whole warp past the end
+    const int rows = min(RPW, S - t0);
+    const int t = t0 + rsub;
+    const bool active = rsub < rows;
+    const int64_t base = ((int64_t)bh * S + t0) * D;
+    stage_in<D, RPW>(s_stage[warp][0], k + base, rows, lane);
+    stage_in<D, RPW>(s_stage[warp][1], v + base, rows, lane);
+    const int32_t sl = active ? slot[(int64_t)t * H + h] : -1;
+    const bool from_prev = DENSE && active && reuse && k_prev && reuse[(int64_t)t * H + h];
+    __syncwarp();
+#pragma unroll 1
+    for (int tensor = 0; tensor < 2; ++tensor) {
+        float4* st = s_stage[warp][tensor];
+        float x[16];
+        if (active) {
+            stage_get<D>(st, rsub, l, x);
         } else {
 #pragma unroll
-            for (int j = 0; j < VEC; ++j) dk[j] = dv[j] = 0.0f;
+            for (int i = 0; i < 16; ++i) x[i] = 0.0f;
         }
-        if (dense_k) {
-            const int64_t off = base + (int64_t)t * D;
-            if (reuse && k_prev && reuse[(int64_t)t * H + h]) {
-                Vec<VEC>::load(k_prev + off, dk);
-                Vec<VEC>::load(v_prev + off, dv);
+        float mr, mg;
+        row_group_max<LPR>(x, G, mr, mg);
+        float dn[16];
+        if (active && sl >= 0) {
+            const int code = slot_code(sl);
+            pack_lane<LPR>(x, code, slot_pos(sl), b, B, G, bk.b[code], tensor == 1, mr, mg, dn, l);
+        } else {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) dn[i] = 0.0f;
+        }
+        if (DENSE) {
+            float* dout = tensor ? dense_v : dense_k;
+            __syncwarp();
+            if (active && !from_prev) stage_put<D>(st, rsub, l, dn);
+            __syncwarp();
+            if (from_prev) {
+                // reused rows come straight from the previous step's tensors
+                const float* pin = tensor ? v_prev : k_prev;
+                ld16_stream(pin + base + (int64_t)rsub * D + l * 16, dn);
+                st16(dout + base + (int64_t)rsub * D + l * 16, dn);
             }
-            Vec<VEC>::store(dense_k + off, dk);
-            Vec<VEC>::store(dense_v + off, dv);
+            const unsigned prev_rows = __ballot_sync(0xffffffffu, from_prev && l == 0);
+            float4* g = reinterpret_cast<float4*>(dout + base);
+#pragma unroll
+            for (int kk = 0; kk < kStageF4 / 32; ++kk) {
+                const int q = lane + 32 * kk;
+                const int r = q / CPR, c = q % CPR;
+                if (r < rows && !((prev_rows >> (r * LPR)) & 1u)) g[q] = st[r * CPR + stage_chunk(c)];
+            }
         }
     }
 }
@@ -299,185 +371,100 @@ __global__ void pack_generic_kernel(const float* __restrict__ k, const float* __
 // ---------------------------------------------------------------------------------------
 // unpack
 // ---------------------------------------------------------------------------------------
-template <int VEC>
-__device__ __forceinline__ void unpack_row(int code, int64_t pos, int b, int B, int G,
-                                           const void* payload, const float* scale, float (&y)[VEC],
-                                           int lane) {
-    constexpr int D = 32 * VEC;
+// One lane's 16 values of row (pos, b) of bucket `code`, dequantised exactly as the
+// reference does (q.float() * scale).  Integer codes become floats through the exponent
+// bits: 0x4B000000 | u is 2^23 + u.
+template <int LPR>
+__device__ __forceinline__ void unpack_lane(int code, int64_t pos, int b, int B, int G, const skv_bucket& bb,
+                                            bool is_v, float (&y)[16], int l) {
+    constexpr int D = LPR * 16;
     const int64_t row = pos * B + b;
+    const void* payload = is_v ? bb.v : bb.k;
+    const float* scale = is_v ? bb.scale_v : bb.scale_k;
     if (code == 0) {
-        Vec<VEC>::load(reinterpret_cast<const float*>(payload) + row * D + lane * VEC, y);
-    } else if (code == 1) {
-        const __half* src = reinterpret_cast<const __half*>(payload) + row * D + lane * VEC;
-        if constexpr (VEC == 2) {
-            const __half2 h2 = *reinterpret_cast<const __half2*>(src);
-            y[0] = __low2float(h2);
-            y[1] = __high2float(h2);
-        } else {
+        const float4* p = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(payload) + row * D + l * 16);
 #pragma unroll
-            for (int j = 0; j < VEC; j += 4) {
-                const uint2 u = *reinterpret_cast<const uint2*>(src + j);
-                y[j] = __half2float(__ushort_as_half((unsigned short)(u.x & 0xffff)));
-                y[j + 1] = __half2float(__ushort_as_half((unsigned short)(u.x >> 16)));
-                y[j + 2] = __half2float(__ushort_as_half((unsigned short)(u.y & 0xffff)));
-                y[j + 3] = __half2float(__ushort_as_half((unsigned short)(u.y >> 16)));
-            }
+        for (int i = 0; i < 4; ++i) {
+            const float4 a = p[i];
+            y[4 * i] = a.x;
+            y[4 * i + 1] = a.y;
+            y[4 * i + 2] = a.z;
+            y[4 * i + 3] = a.w;
+        }
+    } else if (code == 1) {
+        const uint4* p = reinterpret_cast<const uint4*>(reinterpret_cast<const __half*>(payload) + row * D + l * 16);
+        const uint4 a = p[0], c = p[1];
+        const uint32_t w[8] = {a.x, a.y, a.z, a.w, c.x, c.y, c.z, c.w};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+            y[2 * i] = f.x;
+            y[2 * i + 1] = f.y;
         }
     } else if (code == 2) {
-        uint8_t q[VEC];
-        load_bytes<VEC>(reinterpret_cast<const uint8_t*>(payload) + row * D + lane * VEC, q);
+        const uint4 a = *reinterpret_cast<const uint4*>(reinterpret_cast<const int8_t*>(payload) + row * D + l * 16);
         const float s = scale[row];
+        const uint32_t w[4] = {a.x ^ 0x80808080u, a.y ^ 0x80808080u, a.z ^ 0x80808080u, a.w ^ 0x80808080u};
 #pragma unroll
-        for (int j = 0; j < VEC; ++j) y[j] = __fmul_rn((float)(int8_t)q[j], s);
-    } else if (code == 3) {
-        const int NG = D / G;
-        const int64_t rb = (int64_t)B * D / 2;
-        uint8_t bytes[VEC / 2];
-        load_bytes<VEC / 2>(reinterpret_cast<const uint8_t*>(payload) + pos * rb + (int64_t)b * (D / 2) +
-                                lane * (VEC / 2),
-                            bytes);
-        if (G >= VEC) {
-            const float s0 = scale[row * NG + (lane * VEC) / G];
-#pragma unroll
-            for (int j = 0; j < VEC; j += 2) {
-                y[j] = __fmul_rn((float)((int)(bytes[j / 2] >> 4) - 8), s0);
-                y[j + 1] = __fmul_rn((float)((int)(bytes[j / 2] & 0x0F) - 8), s0);
-            }
-        } else {
-#pragma unroll
-            for (int j = 0; j < VEC; j += 2) {
-                const float s0 = scale[row * NG + (lane * VEC + j) / G];
-                const float s1 = scale[row * NG + (lane * VEC + j + 1) / G];
-                y[j] = __fmul_rn((float)((int)(bytes[j / 2] >> 4) - 8), s0);
-                y[j + 1] = __fmul_rn((float)((int)(bytes[j / 2] & 0x0F) - 8), s1);
-            }
-        }
-    } else {
-#pragma unroll
-        for (int j = 0; j < VEC; ++j) y[j] = 0.0f;
-    }
-}
-
-// Raw bytes of one lane's slice of a packed row (VEC values), fetched before decoding so a
-// warp keeps all of its rows' loads in flight at once.
-template <int VEC>
-struct RawSlice {
-    uint32_t w[VEC];   // fp32: VEC words; fp16: VEC/2; int8: VEC/4 (or 1 sub-word); int4: VEC/8 (or 1 sub-word)
-    float s;           // int8 row scale / int4 group scale
-};
-
-template <int VEC>
-__device__ __forceinline__ void load_raw(int code, int64_t pos, int b, int B, int G, const void* payload,
-                                         const float* scale, RawSlice<VEC>& r, int lane) {
-    constexpr int D = 32 * VEC;
-    const int64_t row = pos * B + b;
-    if (code == 0) {
-        const uint32_t* p = reinterpret_cast<const uint32_t*>(payload) + row * D + lane * VEC;
-        if constexpr (VEC == 2) {
-            const uint2 a = *reinterpret_cast<const uint2*>(p);
-            r.w[0] = a.x; r.w[1] = a.y;
-        } else {
-#pragma unroll
-            for (int j = 0; j < VEC; j += 4) {
-                const uint4 a = *reinterpret_cast<const uint4*>(p + j);
-                r.w[j] = a.x; r.w[j + 1] = a.y; r.w[j + 2] = a.z; r.w[j + 3] = a.w;
-            }
-        }
-    } else if (code == 1) {
-        const uint16_t* p = reinterpret_cast<const uint16_t*>(payload) + row * D + lane * VEC;
-        if constexpr (VEC == 2) {
-            r.w[0] = *reinterpret_cast<const uint32_t*>(p);
-        } else {
-#pragma unroll
-            for (int j = 0; j < VEC / 2; j += 2) {
-                const uint2 a = *reinterpret_cast<const uint2*>(p + 2 * j);
-                r.w[j] = a.x; r.w[j + 1] = a.y;
-            }
-        }
-    } else if (code == 2) {
-        const uint8_t* p = reinterpret_cast<const uint8_t*>(payload) + row * D + lane * VEC;
-        if constexpr (VEC == 2) r.w[0] = *reinterpret_cast<const uint16_t*>(p);
-        else if constexpr (VEC == 4) r.w[0] = *reinterpret_cast<const uint32_t*>(p);
-        else { const uint2 a = *reinterpret_cast<const uint2*>(p); r.w[0] = a.x; r.w[1] = a.y; }
-        r.s = scale[row];
-    } else {
-        const int64_t rb = (int64_t)B * D / 2;
-        const uint8_t* p = reinterpret_cast<const uint8_t*>(payload) + pos * rb + (int64_t)b * (D / 2) + lane * (VEC / 2);
-        if constexpr (VEC == 2) r.w[0] = *p;
-        else if constexpr (VEC == 4) r.w[0] = *reinterpret_cast<const uint16_t*>(p);
-        else r.w[0] = *reinterpret_cast<const uint32_t*>(p);
-        const int NG = D / G;
-        r.s = scale[row * NG + (lane * VEC) / G];
-    }
-}
-
-// Decodes a RawSlice; int4 requires G >= VEC (one group scale per lane).
-template <int VEC>
-__device__ __forceinline__ void decode_raw(int code, const RawSlice<VEC>& r, float (&y)[VEC]) {
-    if (code == 0) {
-#pragma unroll
-        for (int j = 0; j < VEC; ++j) y[j] = __uint_as_float(r.w[j]);
-    } else if (code == 1) {
-#pragma unroll
-        for (int j = 0; j < VEC; j += 2) {
-            y[j] = __half2float(__ushort_as_half((unsigned short)(r.w[j / 2] & 0xffff)));
-            y[j + 1] = __half2float(__ushort_as_half((unsigned short)(r.w[j / 2] >> 16)));
-        }
-    } else if (code == 2) {
-#pragma unroll
-        for (int j = 0; j < VEC; ++j) {
-            const int8_t q = (int8_t)((r.w[j / 4] >> (8 * (j % 4))) & 0xff);
-            y[j] = __fmul_rn((float)q, r.s);
+        for (int i = 0; i < 4; ++i) {
+            y[4 * i] = __fmul_rn(__fsub_rn(__int_as_float(__byte_perm(w[i], 0x4B000000u, 0x7540)), 8388736.0f), s);
+            y[4 * i + 1] = __fmul_rn(__fsub_rn(__int_as_float(__byte_perm(w[i], 0x4B000000u, 0x7541)), 8388736.0f), s);
+            y[4 * i + 2] = __fmul_rn(__fsub_rn(__int_as_float(__byte_perm(w[i], 0x4B000000u, 0x7542)), 8388736.0f), s);
+            y[4 * i + 3] = __fmul_rn(__fsub_rn(__int_as_float(__byte_perm(w[i], 0x4B000000u, 0x7543)), 8388736.0f), s);
         }
     } else if (code == 3) {
+        const int64_t rb = (int64_t)B * D / 2;
+        const uint2 a = *reinterpret_cast<const uint2*>(reinterpret_cast<const uint8_t*>(payload) + pos * rb +
+                                                        (int64_t)b * (D / 2) + l * 8);
+        const float s = scale[row * (D / G) + (l * 16) / G];
+        const uint32_t w[2] = {a.x, a.y};
 #pragma unroll
-        for (int j = 0; j < VEC; j += 2) {
-            const uint32_t byte = (r.w[(j / 2) / 4] >> (8 * ((j / 2) % 4))) & 0xff;
-            y[j] = __fmul_rn((float)((int)(byte >> 4) - 8), r.s);
-            y[j + 1] = __fmul_rn((float)((int)(byte & 0x0F) - 8), r.s);
+        for (int k = 0; k < 2; ++k) {
+            const uint32_t hi = (w[k] >> 4) & 0x0F0F0F0Fu, lo = w[k] & 0x0F0F0F0Fu;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const uint32_t sel = 0x7540u | (uint32_t)j;
+                y[8 * k + 2 * j] = __fmul_rn(__fsub_rn(__int_as_float(__byte_perm(hi, 0x4B000000u, sel)), 8388616.0f), s);
+                y[8 * k + 2 * j + 1] =
+                    __fmul_rn(__fsub_rn(__int_as_float(__byte_perm(lo, 0x4B000000u, sel)), 8388616.0f), s);
+            }
         }
     } else {
 #pragma unroll
-        for (int j = 0; j < VEC; ++j) y[j] = 0.0f;
+        for (int i = 0; i < 16; ++i) y[i] = 0.0f;
     }
 }
 
-template <int VEC, int RPW>
-__global__ void __launch_bounds__(256) unpack_fast_kernel(Buckets bk, const int32_t* __restrict__ slot,
-                                                          int B, int H, int S, int G,
-                                                          float* __restrict__ k_out,
+template <int LPR>
+__global__ void __launch_bounds__(256, 4) unpack16_kernel(Buckets bk, const int32_t* __restrict__ slot, int B, int H,
+                                                          int S, int G, float* __restrict__ k_out,
                                                           float* __restrict__ v_out) {
-    constexpr int D = 32 * VEC;
+    constexpr int D = LPR * 16;
+    constexpr int RPW = 32 / LPR;
+    constexpr int kStageF4 = RPW * D / 4;
+    __shared__ float4 s_stage[8][kStageF4];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int bh = blockIdx.y;
+    const int l = lane % LPR, rsub = lane / LPR;
+    const int bh = blockIdx.x;
     const int h = bh % H, b = bh / H;
-    const int t0 = (blockIdx.x * 8 + warp) * RPW;
+    const int t0 = (blockIdx.y * 8 + warp) * RPW;
     if (t0 >= S) return;
-    const int64_t base = (int64_t)bh * S * D + lane * VEC;
-    int32_t sl[RPW];
-#pragma unroll
-    for (int i = 0; i < RPW; ++i) sl[i] = (t0 + i < S) ? slot[(t0 + i) * H + h] : -1;
-    RawSlice<VEC> rk[RPW], rv[RPW];
-#pragma unroll
-    for (int i = 0; i < RPW; ++i) {
-        const int code = sl[i] < 0 ? kCodeEvicted : slot_code(sl[i]);
-        if (code < kCodeEvicted) {
-            const int64_t pos = slot_pos(sl[i]);
-            const skv_bucket& bb = bk.b[code];
-            load_raw<VEC>(code, pos, b, B, G, bb.k, bb.scale_k, rk[i], lane);
-            load_raw<VEC>(code, pos, b, B, G, bb.v, bb.scale_v, rv[i], lane);
-        }
-    }
-#pragma unroll
-    for (int i = 0; i < RPW; ++i) {
-        const int t = t0 + i;
-        if (t >= S) break;
-        const int code = sl[i] < 0 ? kCodeEvicted : slot_code(sl[i]);
-        float yk[VEC], yv[VEC];
-        decode_raw<VEC>(code, rk[i], yk);
-        decode_raw<VEC>(code, rv[i], yv);
-        Vec<VEC>::store(k_out + base + (int64_t)t * D, yk);
-        Vec<VEC>::store(v_out + base + (int64_t)t * D, yv);
+    const int rows = min(RPW, S - t0);
+    const int t = t0 + rsub;
+    const bool active = rsub < rows;
+    const int32_t sl = active ? slot[(int64_t)t * H + h] : -1;
+    const int code = sl < 0 ? kCodeEvicted : slot_code(sl);
+    const int64_t pos = sl < 0 ? 0 : slot_pos(sl);
+    const int64_t base = ((int64_t)bh * S + t0) * D;
+    float4* st = s_stage[warp];
+#pragma unroll 1
+    for (int tensor = 0; tensor < 2; ++tensor) {
+        float y[16];
+        unpack_lane<LPR>(code, pos, b, B, G, bk.b[code < kCodeEvicted ? code : 0], tensor == 1, y, l);
+        if (tensor) __syncwarp();        // the K rows have left the staging buffer
+        if (active) stage_put<D>(st, rsub, l, y);
+        __syncwarp();
+        stage_out<D, RPW>(st, (tensor ? v_out : k_out) + base, rows, lane);
     }
 }
 
@@ -524,17 +511,13 @@ __global__ void unpack_generic_kernel(Buckets bk, const int32_t* __restrict__ sl
     }
 }
 
-// The warp-per-row kernels cover D = 32*VEC with VEC in {2,4,8} and an int4 group that spans a
-// power-of-two number of whole lanes (group 16 at D = 64/128/256); other shapes take the
-// generic kernels.
-static int fast_vec_unpack(int D, int G) {
-    const int vec = D == 64 ? 2 : (D == 128 ? 4 : (D == 256 ? 8 : 0));
-    if (!vec || G < vec || G % vec) return 0;
-    const int L = G / vec;
-    return (L <= 32 && (L & (L - 1)) == 0) ? vec : 0;
+// Vectorised kernels: D in {64, 128, 256} (D/16 lanes per row) and an int4 group that is a
+// multiple of 16 values; other shapes take the generic kernels.
+static int fast_lpr(int D, int G) {
+    const int lpr = D == 64 ? 4 : (D == 128 ? 8 : (D == 256 ? 16 : 0));
+    if (!lpr || G % 16) return 0;
+    return lpr;
 }
-
-static int fast_vec(int D, int G) { return fast_vec_unpack(D, G); }
 
 static bool is_aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
@@ -549,11 +532,12 @@ static bool buckets_aligned(const skv_bucket* bk) {
     return true;
 }
 
-constexpr int kPackRPW = 2;
-constexpr int kUnpackRPW = 4;
-
-static dim3 grid_2d(int B, int H, int S, int rpw) {
-    return dim3((unsigned)((S + 8 * rpw - 1) / (8 * rpw)), (unsigned)(B * H));
+// Grid: x over (b, h), y over token chunks.  Blocks are issued x-fastest, so the blocks in
+// flight cover every head of the same token range, whose bucket rows (token-major order)
+// are contiguous: the packed side is then written / read sequentially.
+static dim3 grid_rows(int B, int H, int S, int lpr) {
+    const int rows_per_block = 8 * (32 / lpr);
+    return dim3((unsigned)(B * H), (unsigned)((S + rows_per_block - 1) / rows_per_block));
 }
 
 static int check_buckets(const skv_bucket* bk, const char* what) {
@@ -593,26 +577,28 @@ int skv_pack(const float* k, const float* v, int B, int H, int S, int D, int gro
     cudaStream_t s = as_stream(stream);
     const bool aligned = is_aligned16(k) && is_aligned16(v) && is_aligned16(dense_k) && is_aligned16(dense_v) &&
                          is_aligned16(k_prev) && is_aligned16(v_prev) && buckets_aligned(buckets);
-    switch (aligned ? fast_vec(D, G) : 0) {
-        case 2:
-            pack_fast_kernel<2, kPackRPW><<<grid_2d(B, H, S, kPackRPW), 256, 0, s>>>(
-                k, v, B, H, S, G, slot, bk, dense_k, dense_v, k_prev, v_prev, reuse_mask);
-            break;
-        case 4:
-            pack_fast_kernel<4, kPackRPW><<<grid_2d(B, H, S, kPackRPW), 256, 0, s>>>(
-                k, v, B, H, S, G, slot, bk, dense_k, dense_v, k_prev, v_prev, reuse_mask);
-            break;
-        case 8:
-            pack_fast_kernel<8, kPackRPW><<<grid_2d(B, H, S, kPackRPW), 256, 0, s>>>(
-                k, v, B, H, S, G, slot, bk, dense_k, dense_v, k_prev, v_prev, reuse_mask);
-            break;
-        default: {
-            const int64_t n = 2 * (int64_t)S * H;
-            const int64_t want = (n + 127) / 128;
-            const int blocks = (int)(want < (int64_t)sm_count() * 16 ? want : (int64_t)sm_count() * 16);
-            pack_generic_kernel<<<blocks, 128, 0, s>>>(k, v, B, H, S, D, G, slot, bk, dense_k, dense_v,
-                                                       k_prev, v_prev, reuse_mask);
+    const int lpr = aligned ? fast_lpr(D, G) : 0;
+    if (lpr) {
+        const dim3 grid = grid_rows(B, H, S, lpr);
+#define SKV_PACK16(L, DN)                                                                                 \
+    pack16_kernel<L, DN><<<grid, 256, 0, s>>>(k, v, B, H, S, G, slot, bk, dense_k, dense_v, k_prev, v_prev, \
+                                              reuse_mask)
+        if (dense_k) {
+            if (lpr == 4) SKV_PACK16(4, true);
+            else if (lpr == 8) SKV_PACK16(8, true);
+            else SKV_PACK16(16, true);
+        } else {
+            if (lpr == 4) SKV_PACK16(4, false);
+            else if (lpr == 8) SKV_PACK16(8, false);
+            else SKV_PACK16(16, false);
         }
+#undef SKV_PACK16
+    } else {
+        const int64_t n = 2 * (int64_t)S * H;
+        const int64_t want = (n + 127) / 128;
+        const int blocks = (int)(want < (int64_t)sm_count() * 16 ? want : (int64_t)sm_count() * 16);
+        pack_generic_kernel<<<blocks, 128, 0, s>>>(k, v, B, H, S, D, G, slot, bk, dense_k, dense_v, k_prev, v_prev,
+                                                   reuse_mask);
     }
     return check_launch("pack");
 }
@@ -628,18 +614,11 @@ int skv_unpack(const skv_bucket* buckets, const int32_t* slot, int B, int H, int
     for (int p = 0; p < kNumBuckets; ++p) bk.b[p] = buckets[p];
     cudaStream_t s = as_stream(stream);
     const bool aligned = is_aligned16(k_out) && is_aligned16(v_out) && buckets_aligned(buckets);
-    switch (aligned ? fast_vec_unpack(D, G) : 0) {
-        case 2:
-            unpack_fast_kernel<2, kUnpackRPW><<<grid_2d(B, H, S, kUnpackRPW), 256, 0, s>>>(bk, slot, B, H, S, G,
-                                                                                            k_out, v_out);
-            break;
-        case 4:
-            unpack_fast_kernel<4, kUnpackRPW><<<grid_2d(B, H, S, kUnpackRPW), 256, 0, s>>>(bk, slot, B, H, S, G,
-                                                                                            k_out, v_out);
-            break;
-        case 8:
-            unpack_fast_kernel<8, kUnpackRPW><<<grid_2d(B, H, S, kUnpackRPW), 256, 0, s>>>(bk, slot, B, H, S, G,
-                                                                                            k_out, v_out);
+    switch (aligned ? fast_lpr(D, G) : 0) {
+        case 4: unpack16_kernel<4><<<grid_rows(B, H, S, 4), 256, 0, s>>>(bk, slot, B, H, S, G, k_out, v_out); break;
+        case 8: unpack16_kernel<8><<<grid_rows(B, H, S, 8), 256, 0, s>>>(bk, slot, B, H, S, G, k_out, v_out); break;
+        case 16:
+            unpack16_kernel<16><<<grid_rows(B, H, S, 16), 256, 0, s>>>(bk, slot, B, H, S, G, k_out, v_out);
             break;
         default: {
             const int64_t total = (int64_t)B * H * S * D;
