@@ -9,9 +9,10 @@
 //    (order-preserving score bits << 32 | flat index, which reproduces the stable tie
 //    order), and 8-bit digit passes histogram the candidate weights (ladder savings for the
 //    downgrade phase, entry costs for the eviction phase) until the unique boundary entry
-//    is found.  Each pass is one launch; the last block of a pass (ticket counter, no
-//    spin-wait) scans the 256-bin histogram and narrows the key prefix.  A final pass
-//    writes the new codes, the predicted bytes and the eviction count.
+//    is found.  All passes run in one cooperative launch: blocks meet at a bounded grid
+//    barrier after each pass, every block scans the same 256-bin histogram and narrows the
+//    key prefix identically, and a final sweep writes the new codes, the predicted bytes
+//    and the eviction count.
 #include <math.h>
 
 #include "skv_common.cuh"
@@ -104,10 +105,6 @@ struct AdmitHeader {
     unsigned int pad1;
 };
 
-struct AdmitState : AdmitHeader {
-    unsigned long long hist[256];
-};
-
 struct AdmitArgs {
     const int8_t* codes;
     const float* imp;
@@ -156,156 +153,187 @@ __device__ __forceinline__ long long cost_of(const AdmitArgs& a, int code) {
     return (code >= 0 && code <= 4) ? a.cost[code] : 0;
 }
 
-// Decision after the downgrade phase: predicted bytes and whether eviction runs.
-__device__ void start_phase_b(const AdmitArgs& a, AdmitState* st, long long predicted_a) {
-    st->predicted_a = predicted_a;
-    st->b_active = (a.allow_evict && predicted_a > a.budget) ? 1 : 0;
-    st->rem = predicted_a - a.budget;
-    st->prefix = 0;
-    st->pmask = 0;
-}
+// ---------------------------------------------------------------------------------------
+// Persistent admission: every phase and digit pass of the radix select in ONE cooperative
+// launch.  Blocks meet at a bounded grid barrier after each histogram pass; each pass has its
+// own global histogram (no zeroing between passes), and every block derives the same
+// selection state from it, so no block has to broadcast decisions.
+// ---------------------------------------------------------------------------------------
+constexpr int kAdmitMaxPasses = 8;                     // 4 score digits + up to 4 index digits
 
-// Block-wide search of the first histogram bin whose inclusive prefix reaches `rem`.
-// Runs in the last block of a pass; all threads participate.
-template <int PHASE>
-__device__ void finish_pass(const AdmitArgs& a, AdmitState* st, int shift, int last_pass) {
-    __shared__ long long s_inc[256];
-    __shared__ int s_found;
-    const int tid = threadIdx.x;
-    long long hv = 0;
-    if (tid < 256) hv = (long long)__ldcg(&st->hist[tid]);
-    if (tid < 256) s_inc[tid] = hv;
-    if (tid == 0) s_found = 256;
-    __syncthreads();
-    for (int o = 1; o < 256; o <<= 1) {
-        long long add = (tid < 256 && tid >= o) ? s_inc[tid - o] : 0;
-        __syncthreads();
-        if (tid < 256) s_inc[tid] += add;
-        __syncthreads();
-    }
-    const long long rem = st->rem;
-    if (tid < 256 && s_inc[tid] >= rem) atomicMin(&s_found, tid);
-    __syncthreads();
-    if (tid == 0) {
-        const int d = s_found;
-        if (d == 256) {
-            // total weight below the requirement: the whole candidate list is consumed
-            const long long total = s_inc[255];
-            if (PHASE == 0) {
-                st->a_notenough = 1;
-                st->a_done = 1;
-                start_phase_b(a, st, st->predicted0 - total);
-            } else {
-                st->b_notenough = 1;
-                st->b_done = 1;
-            }
-        } else {
-            const long long before = d > 0 ? s_inc[d - 1] : 0;
-            st->rem = rem - before;
-            st->prefix |= (unsigned long long)d << shift;
-            st->pmask |= 0xFFull << shift;
-            if (last_pass) {
-                const unsigned long long key = st->prefix;
-                if (PHASE == 0) {
-                    const int64_t idx = (int64_t)(key & 0xFFFFFFFFull);
-                    const int base = a.codes[idx];
-                    const long long r = st->rem;  // remaining excess at the boundary entry
-                    const long long s1 = base < 3 ? a.delta[base] : 0;
-                    const int n1 = base < 3 ? base + 1 : base;
-                    const long long s2 = n1 < 3 ? a.delta[n1] : 0;
-                    const int n2 = n1 < 3 ? n1 + 1 : n1;
-                    int nc = base;
-                    if (base != 4) nc = r <= s1 ? n1 : (r <= s1 + s2 ? n2 : 3);
-                    st->a_key = key;
-                    st->a_newcode = nc;
-                    st->a_done = 1;
-                    const long long consumed = (st->predicted0 - a.budget) - r;
-                    start_phase_b(a, st, st->predicted0 - consumed - (a.cost[base] - a.cost[nc]));
-                } else {
-                    st->b_key = key;
-                    st->b_done = 1;
-                }
-            }
-        }
-    }
-    __syncthreads();
-    if (tid < 256) st->hist[tid] = 0;
-    if (tid == 0) st->counter = 0;
-}
+struct AdmitScratch {
+    unsigned long long hist[2 * kAdmitMaxPasses][256];
+    long long sums[4];                                 // predicted0, predicted_final, evicted, -
+    unsigned bar_count, bar_gen;
+    int err, pad;
+};
 
-template <int PHASE>
-__global__ void __launch_bounds__(256) admit_pass_kernel(AdmitArgs a, AdmitState* st, int shift, int last_pass) {
-    __shared__ unsigned long long s_hist[256];
-    __shared__ bool s_last;
-    const AdmitHeader snap = *static_cast<const AdmitHeader*>(st);
-    if (PHASE == 0 && (!snap.a_active || snap.a_done)) return;
-    if (PHASE == 1 && (!snap.b_active || snap.b_done)) return;
-    s_hist[threadIdx.x] = 0;
-    __syncthreads();
-    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < a.n; i += (int64_t)gridDim.x * blockDim.x) {
-        if (!eligible(a, i)) continue;
-        const unsigned long long key = entry_key(a, i);
-        if ((key & snap.pmask) != snap.prefix) continue;
-        const int base = a.codes[i];
-        long long w;
-        if (PHASE == 0) w = (base >= 0 && base <= 4) ? a.wA[base] : 0;
-        else w = cost_of(a, code_after_a(snap, base, key));
-        if (w == 0) continue;
-        atomicAdd(&s_hist[(key >> shift) & 0xFF], (unsigned long long)w);
-    }
-    __syncthreads();
-    const unsigned long long hv = s_hist[threadIdx.x];
-    if (hv) atomicAdd(&st->hist[threadIdx.x], hv);
-    __threadfence();
-    __syncthreads();
-    if (threadIdx.x == 0) s_last = atomicAdd(&st->counter, 1u) == gridDim.x - 1;
-    __syncthreads();
-    if (!s_last) return;
-    __threadfence();
-    finish_pass<PHASE>(a, st, shift, last_pass);
-}
+struct AdmitPlanDigits {
+    int shift[kAdmitMaxPasses];
+    int n;
+};
 
-__global__ void __launch_bounds__(256) admit_init_kernel(AdmitArgs a, AdmitState* st) {
-    __shared__ long long s_red[8];
-    __shared__ bool s_last;
-    long long acc = 0;
-    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < a.n; i += (int64_t)gridDim.x * blockDim.x)
-        acc += cost_of(a, a.codes[i]);
-    acc = warp_sum_ll(acc);
-    if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = acc;
+// Bounded grid barrier (cooperative launch guarantees every block is resident).  Returns
+// false, and records the failure, if the other blocks do not arrive within the limit.
+__device__ bool grid_barrier(AdmitScratch* sc, unsigned nblocks) {
+    __shared__ int s_ok;
     __syncthreads();
     if (threadIdx.x == 0) {
-        long long t = 0;
-        for (int k = 0; k < 8; ++k) t += s_red[k];
-        if (t) atomicAdd((unsigned long long*)&st->predicted0, (unsigned long long)t);
+        volatile unsigned* gen = &sc->bar_gen;
+        const unsigned g = *gen;
         __threadfence();
-        s_last = atomicAdd(&st->counter, 1u) == gridDim.x - 1;
+        int ok = 1;
+        if (atomicAdd(&sc->bar_count, 1u) == nblocks - 1) {
+            sc->bar_count = 0;
+            __threadfence();
+            atomicAdd(&sc->bar_gen, 1u);
+        } else {
+            long long it = 0;
+            while (*gen == g) {
+                if (++it > (1ll << 24) || *reinterpret_cast<volatile int*>(&sc->err)) {
+                    atomicExch(&sc->err, 1);
+                    ok = 0;
+                    break;
+                }
+                __nanosleep(32);
+            }
+        }
+        __threadfence();
+        s_ok = ok;
     }
     __syncthreads();
-    if (!s_last || threadIdx.x != 0) return;
-    __threadfence();
-    const long long p0 = (long long)atomicAdd((unsigned long long*)&st->predicted0, 0ull);
-    st->a_active = (a.budget >= 0 && p0 > a.budget) ? 1 : 0;
-    st->rem = p0 - a.budget;
-    st->prefix = 0;
-    st->pmask = 0;
-    st->predicted_a = p0;
-    st->b_active = 0;
-    st->counter = 0;
+    return s_ok != 0;
 }
 
-__global__ void __launch_bounds__(256) admit_apply_kernel(AdmitArgs a, AdmitState* st) {
-    __shared__ long long s_p[8], s_e[8];
-    __shared__ bool s_last;
-    const AdmitHeader snap = *static_cast<const AdmitHeader*>(st);
+__global__ void __launch_bounds__(256) admit_persistent_kernel(AdmitArgs a, AdmitScratch* sc, AdmitPlanDigits dg) {
+    __shared__ unsigned long long s_hist[256];
+    __shared__ long long s_inc[256];
+    __shared__ long long s_red[8];
+    __shared__ AdmitHeader st;                         // identical in every block
+    __shared__ int s_found;
+    const unsigned nblocks = gridDim.x;
+    const int tid = threadIdx.x;
+    bool ok = true;
+
+    // predicted bytes of the input codes
+    long long acc = 0;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + tid; i < a.n; i += (int64_t)nblocks * blockDim.x)
+        acc += cost_of(a, a.codes[i]);
+    acc = warp_sum_ll(acc);
+    if ((tid & 31) == 0) s_red[tid >> 5] = acc;
+    __syncthreads();
+    if (tid == 0) {
+        long long t = 0;
+        for (int k = 0; k < 8; ++k) t += s_red[k];
+        if (t) atomicAdd((unsigned long long*)&sc->sums[0], (unsigned long long)t);
+    }
+    ok = grid_barrier(sc, nblocks);
+    if (tid == 0) {
+        const long long p0 = (long long)__ldcg((const unsigned long long*)&sc->sums[0]);
+        memset(&st, 0, sizeof(st));
+        st.predicted0 = p0;
+        st.predicted_a = p0;
+        st.a_active = (a.budget >= 0 && p0 > a.budget) ? 1 : 0;
+        st.rem = p0 - a.budget;
+    }
+    __syncthreads();
+
+    int hist_id = 0;
+    for (int phase = 0; phase < 2 && ok; ++phase) {
+        if (phase == 0 && !st.a_active) continue;
+        if (phase == 1 && !st.b_active) break;
+        for (int pass = 0; pass < dg.n && ok; ++pass, ++hist_id) {
+            if (phase == 0 ? st.a_done : st.b_done) break;
+            const int shift = dg.shift[pass];
+            s_hist[tid] = 0;
+            __syncthreads();
+            const unsigned long long prefix = st.prefix, pmask = st.pmask;
+            for (int64_t i = blockIdx.x * (int64_t)blockDim.x + tid; i < a.n; i += (int64_t)nblocks * blockDim.x) {
+                if (!eligible(a, i)) continue;
+                const unsigned long long key = entry_key(a, i);
+                if ((key & pmask) != prefix) continue;
+                const int base = a.codes[i];
+                const long long w = phase == 0 ? ((base >= 0 && base <= 4) ? a.wA[base] : 0)
+                                               : cost_of(a, code_after_a(st, base, key));
+                if (w) atomicAdd(&s_hist[(key >> shift) & 0xFF], (unsigned long long)w);
+            }
+            __syncthreads();
+            if (s_hist[tid]) atomicAdd(&sc->hist[hist_id][tid], s_hist[tid]);
+            ok = grid_barrier(sc, nblocks);
+            if (!ok) break;
+            // every block scans the same global histogram
+            s_inc[tid] = (long long)__ldcg(&sc->hist[hist_id][tid]);
+            if (tid == 0) s_found = 256;
+            __syncthreads();
+            for (int o = 1; o < 256; o <<= 1) {
+                const long long add = tid >= o ? s_inc[tid - o] : 0;
+                __syncthreads();
+                s_inc[tid] += add;
+                __syncthreads();
+            }
+            const long long rem = st.rem;
+            if (s_inc[tid] >= rem) atomicMin(&s_found, tid);
+            __syncthreads();
+            if (tid == 0) {
+                const int d = s_found;
+                if (d == 256) {
+                    // all candidate weight falls short: the whole candidate list is consumed
+                    if (phase == 0) {
+                        st.a_notenough = 1;
+                        st.a_done = 1;
+                        st.predicted_a = st.predicted0 - s_inc[255];
+                    } else {
+                        st.b_notenough = 1;
+                        st.b_done = 1;
+                    }
+                } else {
+                    const long long before = d > 0 ? s_inc[d - 1] : 0;
+                    st.rem = rem - before;
+                    st.prefix |= (unsigned long long)d << shift;
+                    st.pmask |= 0xFFull << shift;
+                    if (pass == dg.n - 1) {
+                        const unsigned long long key = st.prefix;
+                        if (phase == 0) {
+                            const int64_t idx = (int64_t)(key & 0xFFFFFFFFull);
+                            const int base = a.codes[idx];
+                            const long long r = st.rem;
+                            const long long s1 = base < 3 ? a.delta[base] : 0;
+                            const int n1 = base < 3 ? base + 1 : base;
+                            const long long s2 = n1 < 3 ? a.delta[n1] : 0;
+                            const int n2 = n1 < 3 ? n1 + 1 : n1;
+                            int nc = base;
+                            if (base != 4) nc = r <= s1 ? n1 : (r <= s1 + s2 ? n2 : 3);
+                            st.a_key = key;
+                            st.a_newcode = nc;
+                            st.a_done = 1;
+                            const long long consumed = (st.predicted0 - a.budget) - r;
+                            st.predicted_a = st.predicted0 - consumed - (a.cost[base] - a.cost[nc]);
+                        } else {
+                            st.b_key = key;
+                            st.b_done = 1;
+                        }
+                    }
+                }
+                if (phase == 0 && st.a_done) {
+                    st.b_active = (a.allow_evict && st.predicted_a > a.budget) ? 1 : 0;
+                    st.rem = st.predicted_a - a.budget;
+                    st.prefix = 0;
+                    st.pmask = 0;
+                }
+            }
+            __syncthreads();
+        }
+    }
+
+    // apply: final codes, predicted bytes, evictions
     long long pred = 0, ev = 0;
-    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < a.n; i += (int64_t)gridDim.x * blockDim.x) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + tid; i < a.n; i += (int64_t)nblocks * blockDim.x) {
         const int base = a.codes[i];
         int code = base;
-        if (eligible(a, i) && (snap.a_active || snap.b_active)) {
+        if (ok && eligible(a, i) && (st.a_active || st.b_active)) {
             const unsigned long long key = entry_key(a, i);
-            code = code_after_a(snap, base, key);
-            if (snap.b_active && (snap.b_notenough || key <= snap.b_key)) {
+            code = code_after_a(st, base, key);
+            if (st.b_active && (st.b_notenough || key <= st.b_key)) {
                 if (code != 4) ++ev;
                 code = 4;
             }
@@ -315,28 +343,45 @@ __global__ void __launch_bounds__(256) admit_apply_kernel(AdmitArgs a, AdmitStat
     }
     pred = warp_sum_ll(pred);
     ev = warp_sum_ll(ev);
-    if ((threadIdx.x & 31) == 0) {
-        s_p[threadIdx.x >> 5] = pred;
-        s_e[threadIdx.x >> 5] = ev;
+    __shared__ long long s_e[8];
+    if ((tid & 31) == 0) {
+        s_red[tid >> 5] = pred;
+        s_e[tid >> 5] = ev;
     }
     __syncthreads();
-    if (threadIdx.x == 0) {
+    if (tid == 0) {
         long long tp = 0, te = 0;
         for (int k = 0; k < 8; ++k) {
-            tp += s_p[k];
+            tp += s_red[k];
             te += s_e[k];
         }
-        if (tp) atomicAdd((unsigned long long*)&st->predicted_final, (unsigned long long)tp);
-        if (te) atomicAdd((unsigned long long*)&st->evicted, (unsigned long long)te);
-        __threadfence();
-        s_last = atomicAdd(&st->counter, 1u) == gridDim.x - 1;
+        if (tp) atomicAdd((unsigned long long*)&sc->sums[1], (unsigned long long)tp);
+        if (te) atomicAdd((unsigned long long*)&sc->sums[2], (unsigned long long)te);
     }
-    __syncthreads();
-    if (!s_last || threadIdx.x != 0) return;
-    __threadfence();
-    a.result[0] = (long long)atomicAdd((unsigned long long*)&st->predicted_final, 0ull);
-    a.result[1] = (long long)atomicAdd((unsigned long long*)&st->evicted, 0ull);
-    st->counter = 0;
+    const bool fin = grid_barrier(sc, nblocks);
+    if (blockIdx.x == 0 && tid == 0) {
+        const bool good = ok && fin && __ldcg(&sc->err) == 0;
+        a.result[0] = good ? (long long)__ldcg((const unsigned long long*)&sc->sums[1]) : -1;
+        a.result[1] = good ? (long long)__ldcg((const unsigned long long*)&sc->sums[2]) : -1;
+    }
+}
+
+static int admit_coop_blocks(int64_t n) {
+    static int cached[64] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    int per_sm = 0;
+    if (dev >= 0 && dev < 64 && cached[dev] > 0) {
+        per_sm = cached[dev];
+    } else {
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, admit_persistent_kernel, 256, 0) != cudaSuccess ||
+            per_sm <= 0)
+            per_sm = 1;
+        if (dev >= 0 && dev < 64) cached[dev] = per_sm;
+    }
+    const int64_t cap = (int64_t)sm_count() * (per_sm < 2 ? per_sm : 2);
+    const int64_t want = (n + 1023) / 1024;
+    return (int)(want < 1 ? 1 : (want < cap ? want : cap));
 }
 
 static long long entry_cost(int code, int B, int D, int group_size) {
@@ -376,7 +421,7 @@ int skv_kv_sensitivity(const float* k, const float* v, int B, int H, int S, int 
 size_t skv_admit_scratch_bytes(int S, int H) {
     (void)S;
     (void)H;
-    return sizeof(AdmitState);
+    return sizeof(AdmitScratch);
 }
 
 int skv_admit_codes(const int8_t* codes_in, int8_t* codes_out, const float* importance, const float* sensitivity,
@@ -386,8 +431,8 @@ int skv_admit_codes(const int8_t* codes_in, int8_t* codes_out, const float* impo
     if (S <= 0 || H <= 0) return fail(SKV_ERR_INVALID_ARGUMENT, "admit_codes: bad shape");
     if (!codes_in || !codes_out || !importance || !scratch || !result)
         return fail(SKV_ERR_INVALID_ARGUMENT, "admit_codes: null pointer");
-    if (scratch_bytes < sizeof(AdmitState))
-        return fail(SKV_ERR_SCRATCH, "admit_codes: scratch %zu < %zu", scratch_bytes, sizeof(AdmitState));
+    if (scratch_bytes < sizeof(AdmitScratch))
+        return fail(SKV_ERR_SCRATCH, "admit_codes: scratch %zu < %zu", scratch_bytes, sizeof(AdmitScratch));
     const int64_t n = (int64_t)S * H;
     if (n > (int64_t(1) << 31)) return fail(SKV_ERR_TOO_LARGE, "admit_codes: S*H above 2^31");
     AdmitArgs a;
@@ -411,34 +456,24 @@ int skv_admit_codes(const int8_t* codes_in, int8_t* codes_out, const float* impo
         a.wA[c] = c < 3 ? w : 0;
     }
     cudaStream_t s = as_stream(stream);
-    AdmitState* st = reinterpret_cast<AdmitState*>(scratch);
-    if (cudaMemsetAsync(st, 0, sizeof(AdmitState), s) != cudaSuccess)
+    AdmitScratch* sc = reinterpret_cast<AdmitScratch*>(scratch);
+    if (cudaMemsetAsync(sc, 0, sizeof(AdmitScratch), s) != cudaSuccess)
         return fail(SKV_ERR_CUDA, "admit_codes: memset failed");
-    const int64_t want = (n + 1023) / 1024;
-    const int blocks = (int)(want < (int64_t)sm_count() * 2 ? (want > 0 ? want : 1) : (int64_t)sm_count() * 2);
-    admit_init_kernel<<<blocks, 256, 0, s>>>(a, st);
-    int stc = check_launch("admit_init");
-    if (stc) return stc;
     // digit shifts: 4 score digits, then enough index digits to cover n-1
     int idx_bits = 0;
     while (idx_bits < 63 && ((int64_t)1 << idx_bits) < n) ++idx_bits;
     const int idx_digits = (idx_bits + 7) / 8;
-    int shifts[8];
-    int np = 0;
-    for (int d = 3; d >= 0; --d) shifts[np++] = 32 + 8 * d;
-    for (int d = idx_digits - 1; d >= 0; --d) shifts[np++] = 8 * d;
-    if (budget_bytes >= 0) {
-        for (int phase = 0; phase < (allow_eviction ? 2 : 1); ++phase) {
-            for (int i = 0; i < np; ++i) {
-                if (phase == 0) admit_pass_kernel<0><<<blocks, 256, 0, s>>>(a, st, shifts[i], i == np - 1);
-                else admit_pass_kernel<1><<<blocks, 256, 0, s>>>(a, st, shifts[i], i == np - 1);
-                stc = check_launch("admit_pass");
-                if (stc) return stc;
-            }
-        }
-    }
-    admit_apply_kernel<<<blocks, 256, 0, s>>>(a, st);
-    return check_launch("admit_apply");
+    AdmitPlanDigits dg;
+    dg.n = 0;
+    for (int d = 3; d >= 0; --d) dg.shift[dg.n++] = 32 + 8 * d;
+    for (int d = idx_digits - 1; d >= 0; --d) dg.shift[dg.n++] = 8 * d;
+    if (budget_bytes < 0) dg.n = 0;
+    const int blocks = admit_coop_blocks(n);
+    void* args[] = {&a, &sc, &dg};
+    const cudaError_t e = cudaLaunchCooperativeKernel(reinterpret_cast<void*>(admit_persistent_kernel), dim3(blocks),
+                                                      dim3(256), args, 0, s);
+    if (e != cudaSuccess) return fail(SKV_ERR_CUDA, "admit_codes: cooperative launch failed: %s", cudaGetErrorString(e));
+    return check_launch("admit_persistent");
 }
 
 }  // extern "C"

@@ -142,6 +142,8 @@ def admit_codes(
     out, res = admit_codes_device(codes, importance, sensitivity, budget_bytes, batch, head_dim, sink_tokens,
                                   rd_allocation, allow_eviction, protected_mask, group_size)
     predicted, evicted = (int(x) for x in res.tolist())
+    if predicted < 0:
+        raise RuntimeError("admit_codes: the admission kernel's grid barrier timed out")
     return back(out, codes.device), predicted, evicted
 
 
