@@ -8,9 +8,25 @@ every data-plane call raises ``RuntimeError``.
 
 from __future__ import annotations
 
+import contextlib
 from typing import Any, Optional
 
 import torch
+
+_NULL_CTX = contextlib.nullcontext()
+
+
+def device_ctx(dev: torch.device):
+    """``torch.cuda.device(dev)`` only when ``dev`` is not already the current device."""
+    return _NULL_CTX if torch.cuda.current_device() == dev.index else torch.cuda.device(dev)
+
+
+def mask_u8(mask: torch.Tensor, rows: int, cols: int, dev: torch.device) -> Optional[torch.Tensor]:
+    """A bool/uint8 ``[rows, cols]`` mask already on ``dev`` as a zero-copy uint8 view, else None."""
+    if (mask.dim() == 2 and tuple(mask.shape) == (rows, cols) and mask.device == dev
+            and mask.dtype in (torch.bool, torch.uint8) and mask.is_contiguous()):
+        return mask if mask.dtype == torch.uint8 else mask.view(torch.uint8)
+    return None
 
 
 def compute_device(*tensors: Optional[torch.Tensor]) -> torch.device:

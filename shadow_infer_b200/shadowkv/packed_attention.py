@@ -17,7 +17,7 @@ from typing import Optional
 import torch
 
 from .. import _lib
-from .._device import back, on
+from .._device import back, on, device_ctx
 from .packed_kv_cache import PackedKVCache
 
 
@@ -52,9 +52,9 @@ def packed_attention(
     rows, counts = c._head_index(dev)
     out = torch.empty(B, H, S_q, D, dtype=torch.float32, device=dev)
     err = torch.empty(1, dtype=torch.int32, device=dev)
-    arr = _lib.buckets(c._device_buckets(dev))
+    arr, _, _ = c._device_arr(dev)
     lib = _lib.load()
-    with torch.cuda.device(dev):
+    with device_ctx(dev):
         st = lib.skv_packed_attention(_lib.ptr(qd), B, H, S_q, D, arr, c.seq_len, c._int4_group_of(), _lib.ptr(rows),
                                       _lib.ptr(counts), float(scale), _lib.ptr(out), _lib.ptr(err),
                                       _lib.stream_of(dev))

@@ -28,7 +28,7 @@ from typing import Any, Callable, Dict, List, Optional, Set, Tuple
 import torch
 
 from .. import _lib
-from .._device import back, compute_device, on, scratch
+from .._device import back, compute_device, device_ctx, mask_u8, on, scratch
 from .precision_plan import EVICTED, PRECISION_ORDER, PrecisionPlan, _entries, map_to_codes
 
 _LAZY = object()
@@ -154,7 +154,7 @@ def run_pack(k: torch.Tensor, v: torch.Tensor, plan: PrecisionPlan, group_size: 
             vp = on(v_prev.detach(), dev, torch.float32)
     lib = _lib.load()
     arr = _lib.buckets(buckets)
-    with torch.cuda.device(dev):
+    with device_ctx(dev):
         if events is not None:
             events[0].record()
         st = lib.skv_pack(_lib.ptr(kd), _lib.ptr(vd), B, H, S, D, group_size, _lib.ptr(plan.slot), arr,
@@ -187,6 +187,7 @@ class PackedKVCache:
         self._count: Dict[str, int] = {}
         self._dev: Optional[torch.device] = None
         self._hidx: Optional[Tuple[torch.Tensor, torch.Tensor]] = None   # per-head row lists (attention)
+        self._arr_cache = None                                           # (key, dev, skv_bucket[4], list, direct)
 
     # ------------------------------------------------------------------------------ pack
     @classmethod
@@ -245,6 +246,7 @@ class PackedKVCache:
         self._slot = slot
         self._slot_owned = not shared_slot
         self._hidx = None
+        self._arr_cache = None
         self.packed_data = {}
         self._flat = {}
         self._count = {}
@@ -309,6 +311,27 @@ class PackedKVCache:
         self._dev = dev
         return dev
 
+    def _device_arr(self, dev: torch.device):
+        """``skv_bucket[4]`` of this cache for ``dev`` plus a flag: True when the kernels work on
+        the ``packed_data`` tensors themselves (no copy-back needed).  Cached while those
+        tensor objects stay the same."""
+        key = tuple(None if d is None else tuple(None if t is None else (id(t), t.data_ptr())
+                                                 for t in (d.get("k"), d.get("v"), d.get("scale_k"), d.get("scale_v")))
+                    for d in (self.packed_data.get(p) for p in PRECISION_ORDER))
+        cached = self._arr_cache
+        if cached is not None and cached[0] == key and cached[1] == dev:
+            return cached[2], cached[3], cached[4]
+        bk = self._device_buckets(dev)
+        direct = True
+        for p, b in zip(PRECISION_ORDER, bk):
+            if b is None:
+                continue
+            data = self.packed_data[p]
+            direct &= all(b[x] is data[x] for x in ("k", "v", "scale_k", "scale_v"))
+        arr = _lib.buckets(bk)
+        self._arr_cache = (key, dev, arr, bk, direct)
+        return arr, bk, direct
+
     def _device_buckets(self, dev: torch.device) -> List[Optional[Dict[str, Any]]]:
         out: List[Optional[Dict[str, Any]]] = []
         for p in PRECISION_ORDER:
@@ -328,7 +351,7 @@ class PackedKVCache:
             rows = torch.empty(H * S, dtype=torch.int32, device=dev)
             counts = torch.empty(H * 5, dtype=torch.int32, device=dev)
             lib = _lib.load()
-            with torch.cuda.device(dev):
+            with device_ctx(dev):
                 st = lib.skv_head_index(_lib.ptr(self._slot.to(dev)), S, H, _lib.ptr(rows), _lib.ptr(counts),
                                         _lib.stream_of(dev))
             _lib.check(st, "PackedKVCache head index")
@@ -349,9 +372,9 @@ class PackedKVCache:
         dev = self._ensure_state()
         k_out = torch.empty(shape, dtype=torch.float32, device=dev)
         v_out = torch.empty(shape, dtype=torch.float32, device=dev)
-        arr = _lib.buckets(self._device_buckets(dev))
+        arr, _, _ = self._device_arr(dev)
         lib = _lib.load()
-        with torch.cuda.device(dev):
+        with device_ctx(dev):
             st = lib.skv_unpack(arr, _lib.ptr(self._slot.to(dev)), self.batch_size, self.num_heads, self.seq_len,
                                 self.head_dim, self._int4_group_of(), _lib.ptr(k_out), _lib.ptr(v_out),
                                 _lib.stream_of(dev))
@@ -437,7 +460,7 @@ class PackedKVCache:
         kept_d = torch.empty(5, dtype=torch.int64, device=dev)
         src_arr = _lib.buckets(src)
         stream = _lib.stream_of(dev)
-        with torch.cuda.device(dev):
+        with device_ctx(dev):
             st = lib.skv_evict_count(src_arr, _lib.ptr(mask), self.seq_len, self.num_heads, _lib.ptr(kept_d),
                                      _lib.ptr(scr), scr.numel(), stream)
         _lib.check(st, "PackedKVCache.evict")
@@ -449,6 +472,7 @@ class PackedKVCache:
             self._slot = self._slot.clone()
             self._slot_owned = True
         self._hidx = None
+        self._arr_cache = None
         G = self._int4_group_of()
         dst: List[Optional[Dict[str, Any]]] = []
         work: List[Optional[Dict[str, Any]]] = []
@@ -466,7 +490,7 @@ class PackedKVCache:
             nb["flat"] = torch.empty(kept[code], dtype=torch.int64, device=dev)
             nb["count"] = kept[code]
             dst.append(nb)
-        with torch.cuda.device(dev):
+        with device_ctx(dev):
             st = lib.skv_evict_compact(src_arr, _lib.buckets(dst), _lib.ptr(mask), _lib.ptr(self._slot),
                                        self.batch_size, self.seq_len, self.num_heads, self.head_dim, G,
                                        _lib.ptr(scr), scr.numel(), stream)
@@ -494,6 +518,9 @@ class PackedKVCache:
     def _entry_mask(self, entries: Any, dev: torch.device) -> torch.Tensor:
         S, H = self.seq_len, self.num_heads
         if torch.is_tensor(entries):
+            fast = mask_u8(entries.detach(), S, H, dev)
+            if fast is not None:
+                return fast
             m = torch.zeros(S, H, dtype=torch.uint8, device=dev)
             s, h = min(S, entries.shape[0]), min(H, entries.shape[1])
             m[:s, :h] = on(entries[:s, :h], dev).to(torch.uint8)
@@ -547,18 +574,18 @@ class PackedKVCache:
         dev = self._ensure_state()
         prev._ensure_state()
         mask = self._entry_mask_from_reuse(reuse_mask, dev)
-        cur_b = self._device_buckets(dev)
-        prev_b = prev._device_buckets(dev)
+        cur_arr, cur_b, direct = self._device_arr(dev)
+        prev_arr, _, _ = prev._device_arr(dev)
         stats_d = torch.empty(2, dtype=torch.int64, device=dev)
         lib = _lib.load()
-        with torch.cuda.device(dev):
-            st = lib.skv_apply_reuse(_lib.buckets(cur_b), _lib.ptr(self._slot), self.seq_len, _lib.buckets(prev_b),
+        with device_ctx(dev):
+            st = lib.skv_apply_reuse(cur_arr, _lib.ptr(self._slot), self.seq_len, prev_arr,
                                      _lib.ptr(prev._slot.to(dev)), prev.seq_len, _lib.ptr(mask), self.batch_size,
                                      self.num_heads, self.head_dim, self._int4_group_of(), _lib.ptr(stats_d),
                                      _lib.stream_of(dev))
         _lib.check(st, "PackedKVCache.apply_reuse_mask")
         # write back when the payload lives elsewhere (host caches, non-contiguous views)
-        for code, p in enumerate(PRECISION_ORDER):
+        for code, p in enumerate(PRECISION_ORDER if not direct else ()):
             b = cur_b[code]
             if b is None:
                 continue
@@ -576,6 +603,9 @@ class PackedKVCache:
         if torch.is_tensor(reuse_mask):
             return self._entry_mask(reuse_mask, dev)
         return self._entry_mask([key for key, flag in reuse_mask.items() if flag], dev)
+
+    def _invalidate_device_views(self) -> None:
+        self._arr_cache = None
 
     def __repr__(self) -> str:
         return (

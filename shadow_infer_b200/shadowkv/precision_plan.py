@@ -20,7 +20,7 @@ from typing import Any, Dict, List, Optional, Tuple
 import torch
 
 from .. import _lib
-from .._device import as_device, compute_device, on, scratch
+from .._device import as_device, compute_device, device_ctx, mask_u8, on, scratch
 
 PRECISION_ORDER: Tuple[str, ...] = ("fp32", "fp16", "int8", "int4")
 EVICTED = "evicted"
@@ -85,6 +85,9 @@ def reuse_mask_tensor(reuse_mask: Any, seq_len: int, num_heads: int, dev: torch.
         return None
     if torch.is_tensor(reuse_mask):
         m = reuse_mask.detach()
+        fast = mask_u8(m, seq_len, num_heads, dev)
+        if fast is not None:
+            return fast
         if m.dim() != 2:
             raise ValueError(f"reuse mask tensor must be 2-D [seq, heads], got {tuple(m.shape)}")
         full = torch.zeros(seq_len, num_heads, dtype=torch.uint8, device=dev)
@@ -168,7 +171,7 @@ class PrecisionPlan:
         lib = _lib.load()
         nbytes = lib.skv_plan_scratch_bytes(seq_len, num_heads)
         scr = scratch(nbytes, dev)
-        with torch.cuda.device(dev):
+        with device_ctx(dev):
             st = lib.skv_plan_bucket(_lib.ptr(codes_d), _lib.ptr(mask_d), seq_len, num_heads, _lib.ptr(flat_all),
                                      _lib.ptr(slot), _lib.ptr(reuse_all) if mask_d is not None else None,
                                      _lib.ptr(counts_d), _lib.ptr(scr), scr.numel(), _lib.stream_of(dev))

@@ -16,7 +16,7 @@ from typing import Dict, Optional, Set, Tuple
 import torch
 
 from .. import _lib
-from .._device import back, compute_device, on, scratch
+from .._device import back, compute_device, on, scratch, device_ctx
 from .precision_plan import codes_to_map, map_to_codes
 
 EVICTED = "evicted"
@@ -53,7 +53,7 @@ def kv_sensitivity(k: torch.Tensor, v: torch.Tensor) -> torch.Tensor:
     vd = on(v.detach(), dev, torch.float32)
     out = torch.empty(S, H, dtype=torch.float32, device=dev)
     lib = _lib.load()
-    with torch.cuda.device(dev):
+    with device_ctx(dev):
         st = lib.skv_kv_sensitivity(_lib.ptr(kd), _lib.ptr(vd), B, H, S, D, _lib.ptr(out), _lib.stream_of(dev))
     _lib.check(st, "kv_sensitivity")
     return back(out, k.device)
@@ -65,7 +65,7 @@ def predict_codes_bytes(codes: torch.Tensor, batch: int, head_dim: int, group_si
     cd = on(codes.detach(), dev, torch.int8)
     out = torch.empty(1, dtype=torch.int64, device=dev)
     lib = _lib.load()
-    with torch.cuda.device(dev):
+    with device_ctx(dev):
         st = lib.skv_predict_codes_bytes(_lib.ptr(cd), cd.numel(), batch, head_dim, group_size, _lib.ptr(out),
                                          _lib.stream_of(dev))
     _lib.check(st, "predict_codes_bytes")
@@ -110,7 +110,7 @@ def admit_codes_device(
     lib = _lib.load()
     scr = scratch(lib.skv_admit_scratch_bytes(S, H), dev)
     budget = -1 if budget_bytes is None or budget_bytes < 0 else int(budget_bytes)
-    with torch.cuda.device(dev):
+    with device_ctx(dev):
         st = lib.skv_admit_codes(_lib.ptr(cd), _lib.ptr(out), _lib.ptr(imp), _lib.ptr(sens), _lib.ptr(prot), S, H,
                                  budget, batch, head_dim, group_size, int(sink_tokens), int(bool(rd_allocation)),
                                  int(bool(allow_eviction)), _lib.ptr(scr), scr.numel(), _lib.ptr(res),

@@ -20,7 +20,7 @@ from typing import Any, Dict, Optional, Set, Tuple
 import torch
 
 from .. import _lib
-from .._device import back, compute_device, on
+from .._device import back, compute_device, on, device_ctx
 from .packed_kv_cache import PackedKVCache, run_pack
 from .precision_plan import PRECISION_ORDER, PrecisionPlan
 from .rd_allocator import admit_codes, kv_sensitivity, predict_codes_bytes
@@ -34,7 +34,7 @@ def allocate_precision_codes(importance_map: torch.Tensor, mode: str) -> torch.T
     imp = on(importance_map.detach(), dev, torch.float32)
     out = torch.empty(imp.shape, dtype=torch.int8, device=dev)
     lib = _lib.load()
-    with torch.cuda.device(dev):
+    with device_ctx(dev):
         st = lib.skv_allocate_codes(_lib.ptr(imp), imp.numel(), _MODES.get(mode, -1), _lib.ptr(out),
                                     _lib.stream_of(dev))
     _lib.check(st, "allocate_precision_codes")
