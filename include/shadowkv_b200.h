@@ -148,15 +148,29 @@ int skv_evict_compact(const skv_bucket* src /* [4] */, const skv_bucket* dst /* 
  * slot map; no reference counterpart (the reference never attends over the packed form). */
 int skv_head_index(const int32_t* slot, int S, int H, int32_t* rows, int32_t* counts, void* stream);
 
-/* Attention read directly from the packed cache: O = softmax(Q K^T * scale) V, non-causal, with
- * evicted entries as zero K/V rows -- the result of PackedKVCache.unpack()
+/* Attention over the packed cache: O = softmax(Q K^T * scale) V, non-causal, with evicted
+ * entries as zero K/V rows -- the result of PackedKVCache.unpack()
  * (shadowinfer/shadowkv/packed_kv_cache.py:535-577) fed to SimpleDiffusionLLM._compute_block's
- * attention (shadowinfer/models/simple_diffusion_llm.py:165-169), without materialising K/V.
+ * attention (shadowinfer/models/simple_diffusion_llm.py:165-169), without materialising the
+ * dense fp32 K/V.  The packed rows of each head are dequantised once into fp16 tensor-core tiles
+ * in `scratch` (at least skv_packed_attention_scratch_bytes bytes, 16-byte aligned), which
+ * every query tile of the head then reads.
  * q fp16 [B,H,S_q,D], out fp32 [B,H,S_q,D]; D = 64 or 128; error_flag (device int32) is cleared
  * and set non-zero if a pipeline wait timed out (results then invalid). */
+size_t skv_packed_attention_scratch_bytes(int B, int H, int S_kv, int D);
 int skv_packed_attention(const void* q, int B, int H, int S_q, int D, const skv_bucket* buckets /* [4] */,
                          int S_kv, int int4_group, const int32_t* rows, const int32_t* counts, float scale,
-                         float* out, int32_t* error_flag, void* stream);
+                         void* scratch, size_t scratch_bytes, float* out, int32_t* error_flag, void* stream);
+
+/* The two halves of skv_packed_attention, for callers that attend several query blocks over
+ * one unchanged cache (stage once, attend many times) or time the halves separately.
+ * skv_stage_kv_tiles: dequantises every stored row into the fp16 tiles in `scratch`.
+ * skv_attend_kv_tiles: the tensor-core attention over tiles staged for the same rows/counts. */
+int skv_stage_kv_tiles(const skv_bucket* buckets /* [4] */, int B, int H, int S_kv, int D, int int4_group,
+                       const int32_t* rows, const int32_t* counts, void* scratch, size_t scratch_bytes, void* stream);
+int skv_attend_kv_tiles(const void* q, int B, int H, int S_q, int D, int S_kv, const int32_t* rows,
+                        const int32_t* counts, float scale, const void* scratch, size_t scratch_bytes, float* out,
+                        int32_t* error_flag, void* stream);
 
 #ifdef __cplusplus
 }

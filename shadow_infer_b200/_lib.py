@@ -74,8 +74,14 @@ _SIGNATURES = {
     "skv_apply_reuse": (c_int, [ctypes.POINTER(SkvBucket), c_void_p, c_int, ctypes.POINTER(SkvBucket), c_void_p,
                                 c_int, c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p]),
     "skv_head_index": (c_int, [c_void_p, c_int, c_int, c_void_p, c_void_p, c_void_p]),
+    "skv_packed_attention_scratch_bytes": (c_size_t, [c_int, c_int, c_int, c_int]),
     "skv_packed_attention": (c_int, [c_void_p, c_int, c_int, c_int, c_int, ctypes.POINTER(SkvBucket), c_int, c_int,
-                                     c_void_p, c_void_p, ctypes.c_float, c_void_p, c_void_p, c_void_p]),
+                                     c_void_p, c_void_p, ctypes.c_float, c_void_p, c_size_t, c_void_p, c_void_p,
+                                     c_void_p]),
+    "skv_stage_kv_tiles": (c_int, [ctypes.POINTER(SkvBucket), c_int, c_int, c_int, c_int, c_int, c_void_p, c_void_p,
+                                   c_void_p, c_size_t, c_void_p]),
+    "skv_attend_kv_tiles": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_int, c_void_p, c_void_p, ctypes.c_float,
+                                    c_void_p, c_size_t, c_void_p, c_void_p, c_void_p]),
     "skv_evict_scratch_bytes": (c_size_t, [c_int64]),
     "skv_evict_count": (c_int, [ctypes.POINTER(SkvBucket), c_void_p, c_int, c_int, c_void_p, c_void_p, c_size_t,
                                 c_void_p]),

@@ -1,23 +1,33 @@
-// Attention read directly from the packed cache, on the sm_100a tensor cores.
+// Attention read from the packed cache, on the sm_100a tensor cores.
 //
 // Oracle: PackedKVCache.unpack() (shadowinfer/shadowkv/packed_kv_cache.py:535-577) followed by
 // the dense, non-causal attention of SimpleDiffusionLLM._compute_block
 // (shadowinfer/models/simple_diffusion_llm.py:165-169): O = softmax(Q K^T / sqrt(D)) V with
 // evicted (t,h) entries present as ZERO rows of K and V (logit 0, no value).
 //
-// skv_head_index   -- per head, the stored entries of the cache grouped by precision (token
-//                     order inside a group): the KV row list the attention kernel walks.
-// skv_packed_attention -- one CTA per (128-query tile, head, batch), warp-specialised:
-//   warps 0-3  softmax: thread i owns query row i = TMEM lane i; reads S from TMEM, keeps the
-//              running max / sum (lazy rescale of O when the max grows by more than 2^8),
-//              writes P (fp16) into shared memory, finally normalises O and stores it.
-//   warps 4-7  converters: fetch packed K/V rows straight from the buckets and write fp16 tiles
-//              in the 128B-swizzled UMMA layout (fp32 -> fp16 RNE; fp16 copied; int8 codes
-//              converted EXACTLY and their per-row scales folded into the softmax: K scale
-//              into the logit factor, V scale into P; int4 dequantised in fp32 then rounded).
-//   warp 8     MMA issuer: S_j = Q K_j^T into one of two TMEM S buffers, O += P_j V_j into the
-//              TMEM O accumulator (tcgen05.mma kind::f16, M=128, fp32 accumulate), completion
-//              signalled with tcgen05.commit on mbarriers.
+// skv_head_index       -- per head, the stored entries of the cache grouped by precision (token
+//                         order inside a group): the KV row list the attention walks.
+// skv_packed_attention -- two launches on the caller's stream:
+//   1. stage_tiles_kernel (skv_stage_kv_tiles), one CTA per (128-row KV tile, head, batch):
+//      gathers the tile's rows from the fp32/fp16/int8/int4 buckets and dequantises them ONCE
+//      into fp16 K and V tiles in exactly the byte layout the tensor cores read (128B-swizzled
+//      atoms of 128 rows x 64 values).  fp32 -> fp16 RNE; fp16 copied; int8 and int4 computed
+//      in fp32 as the reference dequantises (q * scale), then rounded.  Evicted entries are
+//      not staged.  Every query tile of the head reuses the staged tiles (from L2), so the
+//      packed bytes are read and converted once per head instead of once per query tile.
+//   2. packed_attention_kernel (skv_attend_kv_tiles), one CTA per (256 queries = two 128-row
+//      tiles, head, batch):
+//      warps 0-7  softmax, two groups of four: group t owns query tile t, thread i of the group
+//                 owns query row i = TMEM lane i.  Reads S_t from TMEM, keeps the running max
+//                 and sum (lazy rescale of O_t when the max grows by more than 2^8), and writes
+//                 P_t (fp16) back into TMEM over the first half of S_t's columns.
+//      warp 8     loader: streams the staged K and V tiles into a two-stage shared-memory ring
+//                 with bulk asynchronous copies (one copy per tile, byte-counted mbarriers).
+//      warp 9     MMA issuer (tcgen05.mma kind::f16, M=128, fp32 accumulate):
+//                 S_t = Q_t K_j^T (both operands in shared memory) and O_t += P_t V_j (P read
+//                 from TMEM), interleaved PV_0(j), S_0(j+1), PV_1(j), S_1(j+1) so that the
+//                 tensor cores work on one query tile while the other tile's softmax runs.
+//      TMEM: S_0 | S_1 | O_0 | O_1 (128 + 128 + D + D columns).
 // Evicted entries never enter a tile: their contribution (count * 2^(0 - m)) is added to the
 // softmax denominator analytically.  Every mbarrier wait is bounded; a timeout sets the error
 // word and all roles drain to the final barrier before TMEM is released.
@@ -30,29 +40,31 @@
 namespace skv {
 using namespace sm100;
 
-constexpr int kBM = 128;          // queries per CTA
+constexpr int kBM = 128;          // queries per tile (two tiles per CTA)
 constexpr int kBN = 128;          // KV rows per tile
-constexpr int kStages = 2;        // K/V tile stages in shared memory
-constexpr int kSoftmaxWarps = 4;
-constexpr int kConvWarps = 8;
-constexpr int kAttnThreads = (kSoftmaxWarps + kConvWarps + 1) * 32;
+constexpr int kSoftmaxWarps = 8;
+constexpr int kLoadWarp = 8;
+constexpr int kMmaWarp = 9;
+constexpr int kAttnThreads = 10 * 32;
+constexpr int kStageThreads = 256;
 constexpr uint32_t kTmemCols = 512;
 constexpr float kRescaleThreshold = 8.0f;   // log2 units
 
-enum AttnError { kErrNone = 0, kErrKvFull = 1, kErrKvEmpty = 2, kErrSFull = 3, kErrPFull = 4, kErrPvDone = 5,
-                 kErrDrain = 6 };
+enum AttnError { kErrNone = 0, kErrKFull = 1, kErrKEmpty = 2, kErrSFull = 3, kErrPFull = 4, kErrOFull = 5,
+                 kErrDrain = 6, kErrQFull = 7, kErrVFull = 8, kErrVEmpty = 9, kErrCopy = 10 };
+
+// Bytes of one staged K (or V) tile: D/64 swizzle atoms of 128 rows x 128 bytes.
+__host__ __device__ constexpr int staged_tile_bytes(int D) { return (D / 64) * kBN * 128; }
 
 template <int D>
 struct AttnLayout {
     static constexpr int NA = D / 64;                   // 128-byte swizzle atoms per row
-    static constexpr int kAtomQ = kBM * 128;            // bytes of one atom column of a 128-row tile
-    static constexpr int kQ = 0;
-    static constexpr int kK = kQ + NA * kAtomQ;
-    static constexpr int kV = kK + kStages * NA * kBN * 128;
-    static constexpr int kP = kV + kStages * NA * kBN * 128;
-    static constexpr int kEnt = kP + 2 * kBM * 128;     // P: K-dim = kBN = 128 -> 2 atoms
-    static constexpr int kBar = kEnt + kStages * kBN * 4;   // per-stage entry (slot) lists
-    static constexpr int kNumBars = 2 * kStages + 2 + 1 + 1 + 1;
+    static constexpr int kTile = staged_tile_bytes(D);  // one 128-row tile (Q, K or V)
+    static constexpr int kQ = 0;                        // two query tiles
+    static constexpr int kK = kQ + 2 * kTile;           // two K stages
+    static constexpr int kV = kK + 2 * kTile;           // two V stages
+    static constexpr int kBar = kV + 2 * kTile;
+    static constexpr int kNumBars = 16;
     static constexpr int kTmemSlot = kBar + kNumBars * 8;
     static constexpr int kBytes = kTmemSlot + 16;
     // + slack to align the base to 1024 B; at least 120 KB so that one CTA occupies an SM and
@@ -66,7 +78,8 @@ struct AttnParams {
     Buckets bk;
     const int32_t* rows;       // [H, S_kv] slot values of the stored entries, grouped by precision
     const int32_t* counts;     // [H, 5]: stored entries per precision, evicted entries
-    int B, H, S_q, S_kv, G;
+    uint8_t* stage;            // [B, H, ntmax, 2 (K, V), staged_tile_bytes(D)]
+    int B, H, S_q, S_kv, G, ntmax;
     float scale_log2;          // softmax scale * log2(e)
     int* err;
 };
@@ -90,25 +103,11 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* e
     return __all_sync(0xffffffffu, ok);
 }
 
-__device__ __forceinline__ __half2 bits_half2(uint32_t u) {
-    __half2 h;
-    memcpy(&h, &u, 4);
-    return h;
+__device__ __forceinline__ int64_t staged_offset(const AttnParams& p, int b, int h, int j, int kv, int tile_bytes) {
+    return ((((int64_t)b * p.H + h) * p.ntmax + j) * 2 + kv) * tile_bytes;
 }
 
-// Eight int8 codes (two words) -> eight exact fp16 values: (0x64 << 8 | (q ^ 0x80)) is
-// 1024 + q + 128 in fp16, minus 1152.
-__device__ __forceinline__ uint4 int8x8_to_half(uint32_t w0, uint32_t w1) {
-    const __half2 bias = bits_half2(0x64806480u);
-    const uint32_t x0 = w0 ^ 0x80808080u, x1 = w1 ^ 0x80808080u;
-    uint4 r;
-    r.x = half2_bits(__hsub2(bits_half2(__byte_perm(x0, 0x64646464u, 0x4140)), bias));
-    r.y = half2_bits(__hsub2(bits_half2(__byte_perm(x0, 0x64646464u, 0x4342)), bias));
-    r.z = half2_bits(__hsub2(bits_half2(__byte_perm(x1, 0x64646464u, 0x4140)), bias));
-    r.w = half2_bits(__hsub2(bits_half2(__byte_perm(x1, 0x64646464u, 0x4342)), bias));
-    return r;
-}
-
+// ------------------------------------------------------------------------------ staging
 // Eight int4 codes (one word, high nibble first per byte) times a group scale, computed in
 // fp32 exactly as the reference dequantises ((nibble - 8) * scale), then rounded to fp16.
 __device__ __forceinline__ uint4 int4x8_to_half(uint32_t w, float s) {
@@ -125,68 +124,6 @@ __device__ __forceinline__ uint4 int4x8_to_half(uint32_t w, float s) {
     r.z = half2_bits(__floats2half2_rn(v[4], v[5]));
     r.w = half2_bits(__floats2half2_rn(v[6], v[7]));
     return r;
-}
-
-__device__ __forceinline__ uint4 f32x8_to_half(const float* p) {
-    const float4 a = *reinterpret_cast<const float4*>(p);
-    const float4 b = *reinterpret_cast<const float4*>(p + 4);
-    uint4 r;
-    r.x = half2_bits(__floats2half2_rn(a.x, a.y));
-    r.y = half2_bits(__floats2half2_rn(a.z, a.w));
-    r.z = half2_bits(__floats2half2_rn(b.x, b.y));
-    r.w = half2_bits(__floats2half2_rn(b.z, b.w));
-    return r;
-}
-
-// Raw packed bytes of one lane's share of one K row and one V row: chunk `l8` (8 values)
-// of each 64-value atom, plus the row/group scales.  Loaded for several rows before any is
-// converted, so a converter lane keeps several L2 requests in flight.
-template <int NA>
-struct RawRow {
-    uint4 k[NA][2], v[NA][2];   // fp32 uses both halves, fp16 one, int8 8 bytes, int4 4 bytes
-    float sk[NA], sv[NA];
-    int code;                   // 0..3, or -1 for a padding row
-};
-
-template <int D>
-__device__ __forceinline__ void load_raw_row(const AttnParams& p, int b, int32_t e, int l8, RawRow<D / 64>& r) {
-    constexpr int NA = D / 64;
-    r.code = e < 0 ? -1 : slot_code(e);
-    if (e < 0) return;
-    const int64_t row = (int64_t)slot_pos(e) * p.B + b;
-    const skv_bucket& bb = p.bk.b[r.code];
-#pragma unroll
-    for (int a = 0; a < NA; ++a) {
-        const int d0 = a * 64 + l8 * 8;
-        if (r.code == 0) {
-            const uint4* pk = reinterpret_cast<const uint4*>(reinterpret_cast<const float*>(bb.k) + row * D + d0);
-            const uint4* pv = reinterpret_cast<const uint4*>(reinterpret_cast<const float*>(bb.v) + row * D + d0);
-            r.k[a][0] = pk[0];
-            r.k[a][1] = pk[1];
-            r.v[a][0] = pv[0];
-            r.v[a][1] = pv[1];
-        } else if (r.code == 1) {
-            r.k[a][0] = *reinterpret_cast<const uint4*>(reinterpret_cast<const __half*>(bb.k) + row * D + d0);
-            r.v[a][0] = *reinterpret_cast<const uint4*>(reinterpret_cast<const __half*>(bb.v) + row * D + d0);
-        } else if (r.code == 2) {
-            const uint2 wk = *reinterpret_cast<const uint2*>(reinterpret_cast<const int8_t*>(bb.k) + row * D + d0);
-            const uint2 wv = *reinterpret_cast<const uint2*>(reinterpret_cast<const int8_t*>(bb.v) + row * D + d0);
-            r.k[a][0] = make_uint4(wk.x, wk.y, 0, 0);
-            r.v[a][0] = make_uint4(wv.x, wv.y, 0, 0);
-            if (a == 0) {
-                r.sk[0] = bb.scale_k[row];
-                r.sv[0] = bb.scale_v[row];
-            }
-        } else {
-            const int64_t off = (int64_t)slot_pos(e) * ((int64_t)p.B * D / 2) + (int64_t)b * (D / 2) + d0 / 2;
-            r.k[a][0].x = *reinterpret_cast<const uint32_t*>(reinterpret_cast<const uint8_t*>(bb.k) + off);
-            r.v[a][0].x = *reinterpret_cast<const uint32_t*>(reinterpret_cast<const uint8_t*>(bb.v) + off);
-            const int NG = D / p.G;
-            const int g = d0 / p.G;
-            r.sk[a] = bb.scale_k[row * NG + g];
-            r.sv[a] = bb.scale_v[row * NG + g];
-        }
-    }
 }
 
 // Eight int8 codes times the row scale, in fp32 exactly as the reference dequantises
@@ -215,8 +152,59 @@ __device__ __forceinline__ uint4 f32x8_bits_to_half(const uint4& a, const uint4&
     return r;
 }
 
+// Raw packed bytes of one lane's share of one K row and one V row: chunk `l8` (8 values)
+// of each 64-value atom, plus the row/group scales.  Loaded for several rows before any is
+// converted, so each lane keeps several memory requests in flight.
+template <int NA>
+struct RawRow {
+    uint4 k[NA][2], v[NA][2];   // fp32 uses both halves, fp16 one, int8 8 bytes, int4 4 bytes
+    float sk[NA], sv[NA];
+    int code;                   // 0..3, or -1 for a padding row
+};
+
+template <int D>
+__device__ __forceinline__ void load_raw_row(const AttnParams& p, int b, int32_t e, int l8, RawRow<D / 64>& r) {
+    constexpr int NA = D / 64;
+    r.code = e < 0 ? -1 : slot_code(e);
+    if (e < 0) return;
+    const int64_t row = (int64_t)slot_pos(e) * p.B + b;
+    const skv_bucket& bb = p.bk.b[r.code];
+#pragma unroll
+    for (int a = 0; a < NA; ++a) {
+        const int d0 = a * 64 + l8 * 8;
+        if (r.code == 0) {
+            const uint4* pk = reinterpret_cast<const uint4*>(reinterpret_cast<const float*>(bb.k) + row * D + d0);
+            const uint4* pv = reinterpret_cast<const uint4*>(reinterpret_cast<const float*>(bb.v) + row * D + d0);
+            r.k[a][0] = __ldg(pk);
+            r.k[a][1] = __ldg(pk + 1);
+            r.v[a][0] = __ldg(pv);
+            r.v[a][1] = __ldg(pv + 1);
+        } else if (r.code == 1) {
+            r.k[a][0] = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const __half*>(bb.k) + row * D + d0));
+            r.v[a][0] = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const __half*>(bb.v) + row * D + d0));
+        } else if (r.code == 2) {
+            const uint2 wk = __ldg(reinterpret_cast<const uint2*>(reinterpret_cast<const int8_t*>(bb.k) + row * D + d0));
+            const uint2 wv = __ldg(reinterpret_cast<const uint2*>(reinterpret_cast<const int8_t*>(bb.v) + row * D + d0));
+            r.k[a][0] = make_uint4(wk.x, wk.y, 0, 0);
+            r.v[a][0] = make_uint4(wv.x, wv.y, 0, 0);
+            if (a == 0) {
+                r.sk[0] = __ldg(bb.scale_k + row);
+                r.sv[0] = __ldg(bb.scale_v + row);
+            }
+        } else {
+            const int64_t off = (int64_t)slot_pos(e) * ((int64_t)p.B * D / 2) + (int64_t)b * (D / 2) + d0 / 2;
+            r.k[a][0].x = __ldg(reinterpret_cast<const uint32_t*>(reinterpret_cast<const uint8_t*>(bb.k) + off));
+            r.v[a][0].x = __ldg(reinterpret_cast<const uint32_t*>(reinterpret_cast<const uint8_t*>(bb.v) + off));
+            const int NG = D / p.G;
+            const int g = d0 / p.G;
+            r.sk[a] = __ldg(bb.scale_k + row * NG + g);
+            r.sv[a] = __ldg(bb.scale_v + row * NG + g);
+        }
+    }
+}
+
 // Converts one lane's share of a K and a V row to fp16 and stores it, 128B-swizzled, at row
-// `r` of the tiles (zeros for a padding row).
+// `r` of the staged tiles (zeros for a padding row).
 template <int D>
 __device__ __forceinline__ void store_row(const RawRow<D / 64>& raw, int r, int l8, uint8_t* ktile, uint8_t* vtile) {
     constexpr int NA = D / 64;
@@ -241,45 +229,73 @@ __device__ __forceinline__ void store_row(const RawRow<D / 64>& raw, int r, int 
     }
 }
 
-__device__ __forceinline__ void converters_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kConvWarps * 32) : "memory"); }
+// One CTA per (KV tile j, head h, batch b); tiles past the head's stored rows exit at once.
+// Eight lanes per row (one 16-byte chunk of each atom per lane), 32 rows per pass, 4 passes.
+template <int D>
+__global__ void __launch_bounds__(kStageThreads) stage_tiles_kernel(AttnParams p) {
+    constexpr int NA = D / 64;
+    constexpr int kRowsPerPass = kStageThreads / 8;
+    constexpr int kPasses = kBN / kRowsPerPass;
+    const int j = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+    const int* cnt = p.counts + (int64_t)h * 5;
+    const int n_stored = cnt[0] + cnt[1] + cnt[2] + cnt[3];
+    if (j * kBN >= n_stored) return;
+    const int rsub = threadIdx.x >> 3, l8 = threadIdx.x & 7;
+    const int32_t* hrows = p.rows + (int64_t)h * p.S_kv;
+    uint8_t* ktile = p.stage + staged_offset(p, b, h, j, 0, staged_tile_bytes(D));
+    uint8_t* vtile = ktile + staged_tile_bytes(D);
+    RawRow<NA> raw[kPasses];
+#pragma unroll
+    for (int i = 0; i < kPasses; ++i) {
+        const int idx = j * kBN + i * kRowsPerPass + rsub;
+        load_raw_row<D>(p, b, idx < n_stored ? __ldg(hrows + idx) : -1, l8, raw[i]);
+    }
+#pragma unroll
+    for (int i = 0; i < kPasses; ++i) store_row<D>(raw[i], i * kRowsPerPass + rsub, l8, ktile, vtile);
+}
 
+// ------------------------------------------------------------------------------ attention
 template <int D>
 __global__ void __launch_bounds__(kAttnThreads, 1) packed_attention_kernel(AttnParams p) {
     using L = AttnLayout<D>;
     constexpr int NA = L::NA;
+    constexpr uint32_t TB = L::kTile;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int h = blockIdx.y, b = blockIdx.z;
-    const int q0 = blockIdx.x * kBM;
+    const int q0 = blockIdx.x * 2 * kBM;
     const int* cnt = p.counts + (int64_t)h * 5;
     const int n_stored = cnt[0] + cnt[1] + cnt[2] + cnt[3];
     const int n_ev = cnt[4];
     const int nt = (n_stored + kBN - 1) / kBN;
 
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBar);
-    uint64_t* kv_full = bars;                   // [kStages], count kConvWarps
-    uint64_t* kv_empty = bars + kStages;        // [kStages], count 1 (commit)
-    uint64_t* s_full = bars + 2 * kStages;      // [2], count 1 (commit)
-    uint64_t* p_full = bars + 2 * kStages + 2;  // count kSoftmaxWarps
-    uint64_t* pv_done = p_full + 1;             // count 1 (commit)
-    uint64_t* mma_done = pv_done + 1;           // count 1 (commit), drain before TMEM release
+    uint64_t* q_full = bars;            // count kSoftmaxWarps
+    uint64_t* k_full = bars + 1;        // [2], expect_tx arrive + copy bytes
+    uint64_t* v_full = bars + 3;        // [2]
+    uint64_t* k_empty = bars + 5;       // [2], commit
+    uint64_t* v_empty = bars + 7;       // [2], commit
+    uint64_t* s_full = bars + 9;        // [2] per query tile, commit
+    uint64_t* p_full = bars + 11;       // [2] per query tile, count 4 (the tile's softmax warps)
+    uint64_t* o_full = bars + 13;       // commit after the last P*V
+    uint64_t* drain = bars + 14;        // commit, drain before TMEM release
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kTmemSlot);
-    int32_t* ent = reinterpret_cast<int32_t*>(smem + L::kEnt);
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kStages; ++s) {
-            mbar_init(&kv_full[s], kConvWarps);
-            mbar_init(&kv_empty[s], 1);
+        mbar_init(q_full, kSoftmaxWarps);
+        for (int s = 0; s < 2; ++s) {
+            mbar_init(&k_full[s], 1);
+            mbar_init(&v_full[s], 1);
+            mbar_init(&k_empty[s], 1);
+            mbar_init(&v_empty[s], 1);
+            mbar_init(&s_full[s], 1);
+            mbar_init(&p_full[s], 4);
         }
-        mbar_init(&s_full[0], 1);
-        mbar_init(&s_full[1], 1);
-        mbar_init(p_full, kSoftmaxWarps);
-        mbar_init(pv_done, 1);
-        mbar_init(mma_done, 1);
+        mbar_init(o_full, 1);
+        mbar_init(drain, 1);
         fence_mbarrier_init();
     }
-    constexpr int kMmaWarp = kSoftmaxWarps + kConvWarps;
     if (warp == kMmaWarp) {
         tmem_alloc(tmem_slot, kTmemCols);
         tmem_relinquish();
@@ -288,229 +304,241 @@ __global__ void __launch_bounds__(kAttnThreads, 1) packed_attention_kernel(AttnP
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    const uint32_t tS0 = tmem, tS1 = tmem + 128, tO = tmem + 256;
 
     if (warp < kSoftmaxWarps) {
         // ------------------------------------------------------------------ softmax
-        const int t = threadIdx.x;                       // query row in the tile == TMEM lane
-        const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+        const int t = warp >> 2;                         // query tile of this warp group
+        const int qw = warp & 3;                         // TMEM lane quarter
+        const int row = qw * 32 + lane;                  // query row in the tile == TMEM lane
+        {
+            // this group's query tile -> shared memory (128B-swizzled, K-major)
+            uint8_t* qtile = smem + L::kQ + t * L::kTile;
+            const int lrow = lane >> 3, l8 = lane & 7;
+            const __half* qbase = p.q + ((int64_t)b * p.H + h) * p.S_q * D;
+            uint4 v[kBM / 16][NA];
+#pragma unroll
+            for (int it = 0; it < kBM / 16; ++it) {
+                const int qi = q0 + t * kBM + it * 16 + qw * 4 + lrow;
+#pragma unroll
+                for (int a = 0; a < NA; ++a)
+                    v[it][a] = qi < p.S_q ? __ldg(reinterpret_cast<const uint4*>(qbase + (int64_t)qi * D + a * 64 + l8 * 8))
+                                          : make_uint4(0, 0, 0, 0);
+            }
+#pragma unroll
+            for (int it = 0; it < kBM / 16; ++it)
+#pragma unroll
+                for (int a = 0; a < NA; ++a)
+                    *reinterpret_cast<uint4*>(qtile + a * kBM * 128 + sw128_offset(it * 16 + qw * 4 + lrow, l8)) = v[it][a];
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(q_full);
+        }
+        const uint32_t lane_off = (uint32_t)(qw * 32) << 16;
+        const uint32_t tS = tmem + t * kBN + lane_off;
+        const uint32_t tO = tmem + 2 * kBN + t * D + lane_off;
         const float sl2 = p.scale_log2;
         float m_ref = n_ev > 0 ? 0.0f : -INFINITY;       // evicted rows: logit 0
         float l = (float)n_ev;
         bool ok = true;
-        for (int j = 0; j < nt && ok; ++j) {
-            const int sb = j & 1;
-            const uint32_t tS = sb ? tS1 : tS0;
-            const int n_valid = min(kBN, n_stored - j * kBN);
-            if (!warp_wait(&s_full[sb], (j >> 1) & 1, p.err, kErrSFull)) { ok = false; break; }
+        for (int j = 0; j < nt; ++j) {
+            if (!warp_wait(&s_full[t], j & 1, p.err, kErrSFull)) { ok = false; break; }
             tc_fence_after();
-            uint32_t r[32];
-            // pass 1: row max of the raw scores (scale > 0; padding columns score exactly 0,
-            // which can only raise the reference max -- harmless)
+            // columns at or past n_valid hold no entry (past the head's last stored row)
+            const int n_valid = min(kBN, n_stored - j * kBN);
+            const bool partial = n_valid < kBN;
+            // pass 1: row max, 64 columns per TMEM round trip
             float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
 #pragma unroll
-            for (int c = 0; c < kBN / 32; c += 2) {
-                uint32_t r2[32];
-                tmem_ld32(tS + lane_off + c * 32, r);
-                tmem_ld32(tS + lane_off + (c + 1) * 32, r2);
+            for (int c = 0; c < kBN; c += 64) {
+                uint32_t s0[32], s1[32];
+                tmem_ld32(tS + c, s0);
+                tmem_ld32(tS + c + 32, s1);
                 tmem_wait_ld();
+                if (partial) {
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) {
+                        if (c + i >= n_valid) s0[i] = __float_as_uint(-INFINITY);
+                        if (c + 32 + i >= n_valid) s1[i] = __float_as_uint(-INFINITY);
+                    }
+                }
 #pragma unroll
                 for (int i = 0; i < 32; i += 2) {
-                    mx0 = fmaxf(mx0, __uint_as_float(r[i]));
-                    mx1 = fmaxf(mx1, __uint_as_float(r[i + 1]));
-                    mx2 = fmaxf(mx2, __uint_as_float(r2[i]));
-                    mx3 = fmaxf(mx3, __uint_as_float(r2[i + 1]));
+                    mx0 = fmaxf(mx0, __uint_as_float(s0[i]));
+                    mx1 = fmaxf(mx1, __uint_as_float(s0[i + 1]));
+                    mx2 = fmaxf(mx2, __uint_as_float(s1[i]));
+                    mx3 = fmaxf(mx3, __uint_as_float(s1[i + 1]));
                 }
             }
             const float mt = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * sl2;
-            bool pv_seen = false;
             const bool need = mt > m_ref + kRescaleThreshold;
             if (__any_sync(0xffffffffu, need)) {
-                // rows that keep their reference max use factor 1 (TMEM access is warp-wide)
+                // rows that keep their reference max use factor 1 (TMEM access is warp-wide);
+                // O_t is stable here: s_full[t] was committed after P_t(j-1) V(j-1)
                 const float f = need ? ex2(m_ref - mt) : 1.0f;   // 0 when m_ref = -inf
                 l *= f;
                 if (j > 0) {
-                    if (!warp_wait(pv_done, (j - 1) & 1, p.err, kErrPvDone)) { ok = false; break; }
-                    pv_seen = true;
-                    tc_fence_after();
+                    uint32_t o[32];
 #pragma unroll
                     for (int c = 0; c < D / 32; ++c) {
-                        tmem_ld32(tO + lane_off + c * 32, r);
+                        tmem_ld32(tO + c * 32, o);
                         tmem_wait_ld();
 #pragma unroll
-                        for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * f);
-                        tmem_st32(tO + lane_off + c * 32, r);
+                        for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * f);
+                        tmem_st32(tO + c * 32, o);
                     }
-                    tmem_wait_st();
                 }
                 if (need) m_ref = mt;
             }
-            if (j > 0 && !pv_seen) {
-                // the single P buffer is still read by the previous tile's P*V
-                if (!warp_wait(pv_done, (j - 1) & 1, p.err, kErrPvDone)) { ok = false; break; }
-            }
-            // pass 2: P = 2^(s*scale - m_ref) in fp16 into shared memory
-            uint8_t* ptile = smem + L::kP;
+            // pass 2: P = 2^(s*scale - m_ref) in fp16, written over the first kBN/2 columns of
+            // S_t; the packed words of columns [32c, 32c+32) land on columns [16c, 16c+16),
+            // all of which have already been read
             const float neg_m = -m_ref;
             float l0 = 0.f, l1 = 0.f, l2 = 0.f, l3 = 0.f;
+            uint32_t sa[32], sb[32];
+            tmem_ld32(tS, sa);
+            tmem_wait_ld();
 #pragma unroll
             for (int c = 0; c < kBN / 32; ++c) {
-                tmem_ld32(tS + lane_off + c * 32, r);
-                tmem_wait_ld();
-                float pv[32];
-#pragma unroll
-                for (int i = 0; i < 32; ++i) pv[i] = ex2(fmaf(__uint_as_float(r[i]), sl2, neg_m));
-                if (n_valid < kBN) {
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) pv[i] = (c * 32 + i < n_valid) ? pv[i] : 0.0f;
-                }
-                uint32_t hp[16];
+                uint32_t (&cur)[32] = (c & 1) ? sb : sa;
+                uint32_t (&nxt)[32] = (c & 1) ? sa : sb;
+                if (c + 1 < kBN / 32) tmem_ld32(tS + (c + 1) * 32, nxt);
+                uint32_t pk[16];
 #pragma unroll
                 for (int i = 0; i < 32; i += 4) {
-                    l0 += pv[i];
-                    l1 += pv[i + 1];
-                    l2 += pv[i + 2];
-                    l3 += pv[i + 3];
-                    hp[i / 2] = half2_bits(__floats2half2_rn(pv[i], pv[i + 1]));
-                    hp[i / 2 + 1] = half2_bits(__floats2half2_rn(pv[i + 2], pv[i + 3]));
+                    float e0 = ex2(fmaf(__uint_as_float(cur[i]), sl2, neg_m));
+                    float e1 = ex2(fmaf(__uint_as_float(cur[i + 1]), sl2, neg_m));
+                    float e2 = ex2(fmaf(__uint_as_float(cur[i + 2]), sl2, neg_m));
+                    float e3 = ex2(fmaf(__uint_as_float(cur[i + 3]), sl2, neg_m));
+                    if (partial) {
+                        const int col = c * 32 + i;
+                        e0 = col < n_valid ? e0 : 0.0f;
+                        e1 = col + 1 < n_valid ? e1 : 0.0f;
+                        e2 = col + 2 < n_valid ? e2 : 0.0f;
+                        e3 = col + 3 < n_valid ? e3 : 0.0f;
+                    }
+                    l0 += e0;
+                    l1 += e1;
+                    l2 += e2;
+                    l3 += e3;
+                    pk[i / 2] = half2_bits(__floats2half2_rn(e0, e1));
+                    pk[i / 2 + 1] = half2_bits(__floats2half2_rn(e2, e3));
                 }
-                // columns c*32 .. c*32+31 = 4 chunks of 8 in atom c/2
-                uint8_t* atom = ptile + (c >> 1) * kBM * 128;
-#pragma unroll
-                for (int k = 0; k < 4; ++k) {
-                    const int chunk = (c & 1) * 4 + k;
-                    *reinterpret_cast<uint4*>(atom + sw128_offset(t, chunk)) =
-                        make_uint4(hp[4 * k], hp[4 * k + 1], hp[4 * k + 2], hp[4 * k + 3]);
-                }
+                tmem_st16(tS + c * 16, pk);
+                if (c + 1 < kBN / 32) tmem_wait_ld();
             }
             l += (l0 + l1) + (l2 + l3);
+            tmem_wait_st();
             tc_fence_before();
-            fence_proxy_async_smem();
             __syncwarp();
-            if (lane == 0) mbar_arrive(p_full);
+            if (lane == 0) mbar_arrive(&p_full[t]);
         }
         // epilogue: O / l
-        const bool row_ok = q0 + t < p.S_q;
-        float* orow = p.out + (((int64_t)b * p.H + h) * p.S_q + (q0 + t)) * D;
+        const int qi = q0 + t * kBM + row;
+        float* orow = p.out + (((int64_t)b * p.H + h) * p.S_q + qi) * D;
         ok = __all_sync(0xffffffffu, ok);
-        if (nt == 0 || !ok) {
-            if (row_ok)
-                for (int d = 0; d < D; d += 4) *reinterpret_cast<float4*>(orow + d) = make_float4(0.f, 0.f, 0.f, 0.f);
-        } else {
-            const bool done = warp_wait(pv_done, (nt - 1) & 1, p.err, kErrPvDone);
+        const bool have = ok && nt > 0 && warp_wait(o_full, 0, p.err, kErrOFull);
+        if (have) {
             tc_fence_after();
-            const float inv = (done && l > 0.0f) ? 1.0f / l : 0.0f;
-            uint32_t r[32];
+            const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+            uint32_t o[32];
 #pragma unroll
             for (int c = 0; c < D / 32; ++c) {
-                tmem_ld32(tO + lane_off + c * 32, r);
+                tmem_ld32(tO + c * 32, o);
                 tmem_wait_ld();
-                if (row_ok) {
+                if (qi < p.S_q) {
 #pragma unroll
                     for (int i = 0; i < 32; i += 4)
                         *reinterpret_cast<float4*>(orow + c * 32 + i) =
-                            make_float4(__uint_as_float(r[i]) * inv, __uint_as_float(r[i + 1]) * inv,
-                                        __uint_as_float(r[i + 2]) * inv, __uint_as_float(r[i + 3]) * inv);
+                            make_float4(__uint_as_float(o[i]) * inv, __uint_as_float(o[i + 1]) * inv,
+                                        __uint_as_float(o[i + 2]) * inv, __uint_as_float(o[i + 3]) * inv);
                 }
             }
+        } else if (qi < p.S_q) {
+            for (int d = 0; d < D; d += 4) *reinterpret_cast<float4*>(orow + d) = make_float4(0.f, 0.f, 0.f, 0.f);
         }
-    } else if (warp < kSoftmaxWarps + kConvWarps) {
-        // --------------------------------------------------------------- converters
-        const int wc = warp - kSoftmaxWarps;
-        const int ctid = threadIdx.x - kSoftmaxWarps * 32;      // 0 .. 32*kConvWarps-1
-        const int lrow = lane >> 3, l8 = lane & 7;
-        uint8_t* qtile = smem + L::kQ;
-        const int32_t* hrows = p.rows + (int64_t)h * p.S_kv;
-        int32_t next_e = (ctid < kBN && ctid < n_stored) ? hrows[ctid] : -1;   // entry list of tile 0
-        constexpr int kRowsPerStep = kConvWarps * 4;
-        for (int step = 0; step < kBM / kRowsPerStep; ++step) {
-            const int r = step * kRowsPerStep + wc * 4 + lrow;
-            const int qi = q0 + r;
-#pragma unroll
-            for (int a = 0; a < NA; ++a) {
-                uint4 v = make_uint4(0, 0, 0, 0);
-                if (qi < p.S_q)
-                    v = *reinterpret_cast<const uint4*>(p.q + (((int64_t)b * p.H + h) * p.S_q + qi) * D + a * 64 + l8 * 8);
-                *reinterpret_cast<uint4*>(qtile + a * kBM * 128 + sw128_offset(r, l8)) = v;
+    } else if (warp == kLoadWarp) {
+        // ------------------------------------------------------------------ loader
+        if (lane == 0 && nt > 0) {
+            const uint8_t* g = p.stage + staged_offset(p, b, h, 0, 0, TB);
+            int nk[2] = {0, 0}, nv[2] = {0, 0};       // copies issued per stage
+            for (int j = 0; j < nt; ++j) {
+                const int s = j & 1;
+                if (j >= 2 && !mbar_wait(&k_empty[s], ((j >> 1) - 1) & 1, p.err, kErrKEmpty)) break;
+                mbar_arrive_expect_tx(&k_full[s], TB);
+                bulk_g2s(smem + L::kK + s * TB, g + (int64_t)j * 2 * TB, TB, &k_full[s]);
+                ++nk[s];
+                if (j >= 2 && !mbar_wait(&v_empty[s], ((j >> 1) - 1) & 1, p.err, kErrVEmpty)) break;
+                mbar_arrive_expect_tx(&v_full[s], TB);
+                bulk_g2s(smem + L::kV + s * TB, g + ((int64_t)j * 2 + 1) * TB, TB, &v_full[s]);
+                ++nv[s];
+            }
+            // every copy issued lands before the CTA can exit (a no-op when the MMA consumed them)
+            for (int s = 0; s < 2; ++s) {
+                if (nk[s]) mbar_wait(&k_full[s], (nk[s] - 1) & 1, p.err, kErrCopy);
+                if (nv[s]) mbar_wait(&v_full[s], (nv[s] - 1) & 1, p.err, kErrCopy);
             }
         }
-        constexpr int kRowsPerBatch = 2;       // rows whose loads are in flight together
-        volatile int* conv_fail = reinterpret_cast<volatile int*>(smem + L::kTmemSlot + 8);
-        if (ctid == 0) *conv_fail = 0;
-        converters_sync();
-        for (int j = 0; j < nt; ++j) {
-            const int s = j % kStages;
-            const bool ok = j < kStages || warp_wait(&kv_empty[s], ((j / kStages) - 1) & 1, p.err, kErrKvEmpty);
-            if (!ok && lane == 0) *conv_fail = 1;
-            int32_t* e_tile = ent + s * kBN;
-            if (ok && ctid < kBN) e_tile[ctid] = next_e;
-            const int nxt = (j + 1) * kBN + ctid;
-            next_e = (ctid < kBN && j + 1 < nt && nxt < n_stored) ? hrows[nxt] : -1;
-            // every converter warp reaches this barrier on every tile, so one warp's timeout
-            // stops all four together instead of leaving the others waiting here
-            converters_sync();
-            if (*conv_fail) break;
-            uint8_t* ktile = smem + L::kK + s * NA * kBN * 128;
-            uint8_t* vtile = smem + L::kV + s * NA * kBN * 128;
-            for (int step = 0; step < kBN / kRowsPerStep; step += kRowsPerBatch) {
-                RawRow<NA> raw[kRowsPerBatch];
-#pragma unroll
-                for (int i = 0; i < kRowsPerBatch; ++i) {
-                    const int r = (step + i) * kRowsPerStep + wc * 4 + lrow;
-                    load_raw_row<D>(p, b, e_tile[r], l8, raw[i]);
-                }
-#pragma unroll
-                for (int i = 0; i < kRowsPerBatch; ++i) {
-                    const int r = (step + i) * kRowsPerStep + wc * 4 + lrow;
-                    store_row<D>(raw[i], r, l8, ktile, vtile);
-                }
-            }
-            fence_proxy_async_smem();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&kv_full[s]);
-        }
+        __syncwarp();
     } else {
         // ----------------------------------------------------------------- MMA issue
         if (lane == 0 && nt > 0) {
             const uint32_t idesc_s = idesc_f16_f32(kBM, kBN, false, false);
             const uint32_t idesc_o = idesc_f16_f32(kBM, D, false, true);
             const uint32_t q_base = smem_u32(smem + L::kQ);
-            const uint32_t p_base = smem_u32(smem + L::kP);
-            bool ok = true;
-            auto issue_pv = [&](int i) -> bool {
-                if (!mbar_wait(p_full, i & 1, p.err, kErrPFull)) return false;
-                tc_fence_after();
-                const uint32_t v_base = smem_u32(smem + L::kV + (i % kStages) * NA * kBN * 128);
-#pragma unroll
-                for (int k = 0; k < kBN / 16; ++k) {
-                    const uint64_t adesc = smem_desc_sw128(p_base + (k >> 2) * kBM * 128 + (k & 3) * 32, 16, 1024);
-                    const uint64_t bdesc = smem_desc_sw128(v_base + k * 16 * 128, kBN * 128, 1024);
-                    umma_f16(tO, adesc, bdesc, idesc_o, (i > 0 || k > 0) ? 1u : 0u);
-                }
-                umma_commit(pv_done);
-                umma_commit(&kv_empty[i % kStages]);
-                return true;
-            };
-            for (int j = 0; j < nt && ok; ++j) {
-                const int s = j % kStages, sb = j & 1;
-                if (!mbar_wait(&kv_full[s], (j / kStages) & 1, p.err, kErrKvFull)) { ok = false; break; }
-                tc_fence_after();
-                const uint32_t k_base = smem_u32(smem + L::kK + s * NA * kBN * 128);
+            auto issue_s = [&](int t, int j) {
+                const uint32_t k_base = smem_u32(smem + L::kK + (j & 1) * TB);
 #pragma unroll
                 for (int k = 0; k < D / 16; ++k) {
-                    const uint32_t off = (k >> 2) * kBM * 128 + (k & 3) * 32;
-                    const uint32_t koff = (k >> 2) * kBN * 128 + (k & 3) * 32;
-                    const uint64_t adesc = smem_desc_sw128(q_base + off, 16, 1024);
-                    const uint64_t bdesc = smem_desc_sw128(k_base + koff, 16, 1024);
-                    umma_f16(sb ? tS1 : tS0, adesc, bdesc, idesc_s, k > 0 ? 1u : 0u);
+                    const uint32_t off = (k >> 2) * (kBN * 128) + (k & 3) * 32;
+                    umma_f16(tmem + t * kBN, smem_desc_sw128(q_base + t * TB + off, 16, 1024),
+                             smem_desc_sw128(k_base + off, 16, 1024), idesc_s, k > 0 ? 1u : 0u);
                 }
-                umma_commit(&s_full[sb]);
-                if (j > 0 && !issue_pv(j - 1)) { ok = false; break; }
+            };
+            auto issue_pv = [&](int t, int j) {
+                const uint32_t v_base = smem_u32(smem + L::kV + (j & 1) * TB);
+#pragma unroll
+                for (int k = 0; k < kBN / 16; ++k)
+                    umma_f16_ts(tmem + 2 * kBN + t * D, tmem + t * kBN + k * 8,
+                                smem_desc_sw128(v_base + k * 16 * 128, kBN * 128, 1024), idesc_o,
+                                (j > 0 || k > 0) ? 1u : 0u);
+            };
+            bool ok = mbar_wait(q_full, 0, p.err, kErrQFull) && mbar_wait(&k_full[0], 0, p.err, kErrKFull);
+            if (ok) {
+                tc_fence_after();
+                issue_s(0, 0);
+                umma_commit(&s_full[0]);
+                issue_s(1, 0);
+                umma_commit(&s_full[1]);
+                umma_commit(&k_empty[0]);
             }
-            if (ok) issue_pv(nt - 1);
+            for (int j = 0; ok && j < nt; ++j) {
+                const int s = j & 1, s1 = (j + 1) & 1;
+                const bool more = j + 1 < nt;
+                if (!mbar_wait(&v_full[s], (j >> 1) & 1, p.err, kErrVFull) ||
+                    !mbar_wait(&p_full[0], j & 1, p.err, kErrPFull)) { ok = false; break; }
+                tc_fence_after();
+                issue_pv(0, j);
+                if (more) {
+                    if (!mbar_wait(&k_full[s1], ((j + 1) >> 1) & 1, p.err, kErrKFull)) { ok = false; break; }
+                    tc_fence_after();
+                    // issued after P_0(j) V(j): the tensor pipe has read P_0 before S_0 is rewritten
+                    issue_s(0, j + 1);
+                    umma_commit(&s_full[0]);
+                }
+                if (!mbar_wait(&p_full[1], j & 1, p.err, kErrPFull)) { ok = false; break; }
+                tc_fence_after();
+                issue_pv(1, j);
+                umma_commit(&v_empty[s]);
+                if (more) {
+                    issue_s(1, j + 1);
+                    umma_commit(&s_full[1]);
+                    umma_commit(&k_empty[s1]);
+                }
+            }
+            if (ok) umma_commit(o_full);
             // drain: every UMMA issued above completes before TMEM is released
-            umma_commit(mma_done);
-            mbar_wait(mma_done, 0, p.err, kErrDrain);
+            umma_commit(drain);
+            mbar_wait(drain, 0, p.err, kErrDrain);
         }
         __syncwarp();
     }
@@ -623,39 +651,86 @@ int skv_head_index(const int32_t* slot, int S, int H, int32_t* rows, int32_t* co
     return check_launch("head_index");
 }
 
-int skv_packed_attention(const void* q, int B, int H, int S_q, int D, const skv_bucket* buckets, int S_kv,
-                         int int4_group, const int32_t* rows, const int32_t* counts, float scale, float* out,
-                         int32_t* error_flag, void* stream) {
-    if (!q || !buckets || !rows || !counts || !out || !error_flag)
-        return fail(SKV_ERR_INVALID_ARGUMENT, "packed_attention: null pointer");
-    if (B <= 0 || H <= 0 || S_q <= 0 || S_kv <= 0) return fail(SKV_ERR_INVALID_ARGUMENT, "packed_attention: bad shape");
-    if (D != 64 && D != 128) return fail(SKV_ERR_UNSUPPORTED, "packed_attention: head_dim %d (64 or 128 supported)", D);
+size_t skv_packed_attention_scratch_bytes(int B, int H, int S_kv, int D) {
+    if (B <= 0 || H <= 0 || S_kv <= 0 || (D != 64 && D != 128)) return 0;
+    const size_t ntmax = (size_t)(S_kv + kBN - 1) / kBN;
+    return (size_t)B * H * ntmax * 2 * staged_tile_bytes(D);
+}
+
+}  // extern "C"
+
+namespace {
+
+int attn_params(const void* q, int B, int H, int S_q, int D, const skv_bucket* buckets, int S_kv, int int4_group,
+                const int32_t* rows, const int32_t* counts, float scale, void* scratch, size_t scratch_bytes,
+                float* out, int32_t* error_flag, AttnParams& prm, const char* what) {
+    if (!rows || !counts || !scratch) return fail(SKV_ERR_INVALID_ARGUMENT, "%s: null pointer", what);
+    if (B <= 0 || H <= 0 || S_q <= 0 || S_kv <= 0) return fail(SKV_ERR_INVALID_ARGUMENT, "%s: bad shape", what);
+    if (D != 64 && D != 128) return fail(SKV_ERR_UNSUPPORTED, "%s: head_dim %d (64 or 128 supported)", what, D);
     const int G = int4_group > 0 && D % int4_group == 0 ? int4_group : D;
-    if (G % 8) return fail(SKV_ERR_UNSUPPORTED, "packed_attention: int4 group %d must be a multiple of 8", G);
-    for (int p = 0; p < kNumBuckets; ++p) {
-        if (buckets[p].count == 0) continue;
-        const uintptr_t a = reinterpret_cast<uintptr_t>(buckets[p].k) | reinterpret_cast<uintptr_t>(buckets[p].v);
-        if (a & 15) return fail(SKV_ERR_UNSUPPORTED, "packed_attention: bucket %d not 16-byte aligned", p);
+    if (G % 8) return fail(SKV_ERR_UNSUPPORTED, "%s: int4 group %d must be a multiple of 8", what, G);
+    if (buckets) {
+        for (int p = 0; p < kNumBuckets; ++p) {
+            if (buckets[p].count == 0) continue;
+            const uintptr_t a = reinterpret_cast<uintptr_t>(buckets[p].k) | reinterpret_cast<uintptr_t>(buckets[p].v);
+            if (a & 15) return fail(SKV_ERR_UNSUPPORTED, "%s: bucket %d not 16-byte aligned", what, p);
+        }
     }
-    if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(out)) & 15)
-        return fail(SKV_ERR_UNSUPPORTED, "packed_attention: q/out not 16-byte aligned");
-    AttnParams prm;
+    if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(out) | reinterpret_cast<uintptr_t>(scratch)) & 15)
+        return fail(SKV_ERR_UNSUPPORTED, "%s: q/out/scratch not 16-byte aligned", what);
+    const size_t need = skv_packed_attention_scratch_bytes(B, H, S_kv, D);
+    if (scratch_bytes < need)
+        return fail(SKV_ERR_SCRATCH, "%s: scratch of %zu bytes, %zu needed", what, scratch_bytes, need);
+    memset(&prm, 0, sizeof(prm));
     prm.q = reinterpret_cast<const __half*>(q);
     prm.out = out;
-    for (int p = 0; p < kNumBuckets; ++p) prm.bk.b[p] = buckets[p];
+    if (buckets)
+        for (int p = 0; p < kNumBuckets; ++p) prm.bk.b[p] = buckets[p];
     prm.rows = rows;
     prm.counts = counts;
+    prm.stage = reinterpret_cast<uint8_t*>(scratch);
     prm.B = B;
     prm.H = H;
     prm.S_q = S_q;
     prm.S_kv = S_kv;
     prm.G = G;
+    prm.ntmax = (S_kv + kBN - 1) / kBN;
     prm.scale_log2 = scale * 1.4426950408889634f;
     prm.err = error_flag;
+    return SKV_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int skv_stage_kv_tiles(const skv_bucket* buckets, int B, int H, int S_kv, int D, int int4_group, const int32_t* rows,
+                       const int32_t* counts, void* scratch, size_t scratch_bytes, void* stream) {
+    if (!buckets) return fail(SKV_ERR_INVALID_ARGUMENT, "stage_kv_tiles: null pointer");
+    AttnParams prm;
+    const int st = attn_params(nullptr, B, H, 1, D, buckets, S_kv, int4_group, rows, counts, 1.0f, scratch,
+                               scratch_bytes, nullptr, nullptr, prm, "stage_kv_tiles");
+    if (st != SKV_OK) return st;
+    const dim3 grid((unsigned)prm.ntmax, (unsigned)H, (unsigned)B);
+    if (D == 128)
+        stage_tiles_kernel<128><<<grid, kStageThreads, 0, as_stream(stream)>>>(prm);
+    else
+        stage_tiles_kernel<64><<<grid, kStageThreads, 0, as_stream(stream)>>>(prm);
+    return check_launch("stage_kv_tiles");
+}
+
+int skv_attend_kv_tiles(const void* q, int B, int H, int S_q, int D, int S_kv, const int32_t* rows,
+                        const int32_t* counts, float scale, const void* scratch, size_t scratch_bytes, float* out,
+                        int32_t* error_flag, void* stream) {
+    if (!q || !out || !error_flag) return fail(SKV_ERR_INVALID_ARGUMENT, "attend_kv_tiles: null pointer");
+    AttnParams prm;
+    const int st = attn_params(q, B, H, S_q, D, nullptr, S_kv, 0, rows, counts, scale, const_cast<void*>(scratch),
+                               scratch_bytes, out, error_flag, prm, "attend_kv_tiles");
+    if (st != SKV_OK) return st;
     cudaStream_t s = as_stream(stream);
     if (cudaMemsetAsync(error_flag, 0, sizeof(int32_t), s) != cudaSuccess)
-        return fail(SKV_ERR_CUDA, "packed_attention: memset failed");
-    const dim3 grid((unsigned)((S_q + kBM - 1) / kBM), (unsigned)H, (unsigned)B);
+        return fail(SKV_ERR_CUDA, "attend_kv_tiles: memset failed");
+    const dim3 grid((unsigned)((S_q + 2 * kBM - 1) / (2 * kBM)), (unsigned)H, (unsigned)B);
     if (D == 128) {
         const int smem = AttnLayout<128>::kAlloc;
         cudaFuncSetAttribute(packed_attention_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
@@ -665,7 +740,17 @@ int skv_packed_attention(const void* q, int B, int H, int S_q, int D, const skv_
         cudaFuncSetAttribute(packed_attention_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         packed_attention_kernel<64><<<grid, kAttnThreads, smem, s>>>(prm);
     }
-    return check_launch("packed_attention");
+    return check_launch("attend_kv_tiles");
+}
+
+int skv_packed_attention(const void* q, int B, int H, int S_q, int D, const skv_bucket* buckets, int S_kv,
+                         int int4_group, const int32_t* rows, const int32_t* counts, float scale, void* scratch,
+                         size_t scratch_bytes, float* out, int32_t* error_flag, void* stream) {
+    if (!q || !buckets || !out || !error_flag) return fail(SKV_ERR_INVALID_ARGUMENT, "packed_attention: null pointer");
+    const int st = skv_stage_kv_tiles(buckets, B, H, S_kv, D, int4_group, rows, counts, scratch, scratch_bytes, stream);
+    if (st != SKV_OK) return st;
+    return skv_attend_kv_tiles(q, B, H, S_q, D, S_kv, rows, counts, scale, scratch, scratch_bytes, out, error_flag,
+                               stream);
 }
 
 }  // extern "C"

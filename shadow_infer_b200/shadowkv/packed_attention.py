@@ -4,9 +4,11 @@ In the reference the ``kv_execution="packed"`` path unpacks every layer to
 dense fp32 K/V (``PackedKVCache.unpack``, shadowinfer/shadowkv/packed_kv_cache.py:535-577,
 called from ``PyTorchModelBackend.forward_step``, core/backends/pytorch_backend.py:302-304)
 and then runs ``softmax(q @ k^T / sqrt(D)) @ v`` (shadowinfer/models/simple_diffusion_llm.py:165-169).
-``packed_attention`` computes the same result in one sm_100a kernel that reads the
-packed buckets directly: evicted token-heads behave exactly as the zero rows that
-``unpack`` would have produced (logit 0, value 0).
+``packed_attention`` computes the same result from the packed buckets without the dense
+fp32 unpack: one kernel dequantises each head's stored rows once into fp16 tensor-core
+tiles (evicted rows are skipped), and a tcgen05 kernel runs the attention over those tiles.
+Evicted token-heads behave exactly as the zero rows that ``unpack`` would have produced
+(logit 0, value 0).
 """
 
 from __future__ import annotations
@@ -17,7 +19,7 @@ from typing import Optional
 import torch
 
 from .. import _lib
-from .._device import back, on, device_ctx
+from .._device import back, device_ctx, on, scratch
 from .packed_kv_cache import PackedKVCache
 
 
@@ -26,12 +28,14 @@ def packed_attention(
     kv_cache: PackedKVCache,
     scale: Optional[float] = None,
     check: bool = True,
+    events: Optional[tuple] = None,
 ) -> torch.Tensor:
     """Non-causal attention of ``q`` [B, H, S_q, D] over a packed cache; returns fp32 [B, H, S_q, D].
 
     ``scale`` defaults to ``1/sqrt(D)``.  ``q`` is used in fp16 (the tensor-core operand type).
     With ``check`` the call synchronises and raises ``RuntimeError`` if the kernel
-    reported a pipeline timeout.
+    reported a pipeline timeout.  ``events``: three CUDA events recorded before the staging
+    kernel, between the two kernels and after the attention kernel (timing hook).
     """
     if q.dim() != 4:
         raise ValueError(f"q must be 4-D [batch, heads, seq, head_dim], got shape {tuple(q.shape)}")
@@ -54,10 +58,23 @@ def packed_attention(
     err = torch.empty(1, dtype=torch.int32, device=dev)
     arr, _, _ = c._device_arr(dev)
     lib = _lib.load()
+    tiles = scratch(lib.skv_packed_attention_scratch_bytes(B, H, c.seq_len, D), dev)
+    stream = _lib.stream_of(dev)
     with device_ctx(dev):
-        st = lib.skv_packed_attention(_lib.ptr(qd), B, H, S_q, D, arr, c.seq_len, c._int4_group_of(), _lib.ptr(rows),
-                                      _lib.ptr(counts), float(scale), _lib.ptr(out), _lib.ptr(err),
-                                      _lib.stream_of(dev))
+        if events is None:
+            st = lib.skv_packed_attention(_lib.ptr(qd), B, H, S_q, D, arr, c.seq_len, c._int4_group_of(),
+                                          _lib.ptr(rows), _lib.ptr(counts), float(scale), _lib.ptr(tiles),
+                                          tiles.numel(), _lib.ptr(out), _lib.ptr(err), stream)
+        else:
+            events[0].record()
+            st = lib.skv_stage_kv_tiles(arr, B, H, c.seq_len, D, c._int4_group_of(), _lib.ptr(rows),
+                                        _lib.ptr(counts), _lib.ptr(tiles), tiles.numel(), stream)
+            _lib.check(st, "packed_attention")
+            events[1].record()
+            st = lib.skv_attend_kv_tiles(_lib.ptr(qd), B, H, S_q, D, c.seq_len, _lib.ptr(rows), _lib.ptr(counts),
+                                         float(scale), _lib.ptr(tiles), tiles.numel(), _lib.ptr(out), _lib.ptr(err),
+                                         stream)
+            events[2].record()
     _lib.check(st, "packed_attention")
     if check:
         code = int(err.item())
