@@ -70,6 +70,7 @@ struct AttnLayout {
     // + slack to align the base to 1024 B; at least 120 KB so that one CTA occupies an SM and
     // its 512-column TMEM allocation never waits for another CTA's
     static constexpr int kAlloc = (kBytes + 1024) > 120 * 1024 ? (kBytes + 1024) : 120 * 1024;
+    static_assert(kSoftmaxWarps * 32 * 33 * 4 <= kBar, "epilogue transpose buffers overlap the barriers");
 };
 
 struct AttnParams {
@@ -90,6 +91,56 @@ __device__ __forceinline__ float ex2(float x) {
     return y;
 }
 
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+
+// 2^x on the FMA pipe, for part of the softmax elements so that the MUFU pipe (ex2) is not
+// the only one doing exponentials.  Range reduction x = n + f with n = rint(x) (the 1.5*2^23
+// rounding trick) and f in [-1/2, 1/2]; 2^f by a degree-3 polynomial whose coefficients are
+// the relative-error minimax fit on [-1/2, 1/2] (Remez exchange), max relative error 7.5e-5
+// -- below half an fp16 ulp (2^-12), the precision P is rounded to; 2^n is added to the
+// exponent field.  x is clamped at -125, so the result is never below 2^-125 (0 in fp16).
+constexpr float kExp2C0 = 0.99992805719375610f;
+constexpr float kExp2C1 = 0.69326096773147583f;
+constexpr float kExp2C2 = 0.24261112511157990f;
+constexpr float kExp2C3 = 0.05517166852951050f;
+constexpr float kRoundMagic = 12582912.0f;   // 1.5 * 2^23
+
+__host__ __device__ inline float exp2_poly(float x) {
+    x = fmaxf(x, -125.0f);
+    const float t = x + kRoundMagic;
+    const float f = x - (t - kRoundMagic);
+    const float q = fmaf(fmaf(fmaf(kExp2C3, f, kExp2C2), f, kExp2C1), f, kExp2C0);
+    uint32_t qb, tb;
+    memcpy(&qb, &q, 4);
+    memcpy(&tb, &t, 4);
+    qb += tb << 23;          // low mantissa bits of t hold n (two's complement)
+    float r;
+    memcpy(&r, &qb, 4);
+    return r;
+}
+
+// The same computation on two lanes of packed fp32 (fma.rn.f32x2 / add.rn.f32x2): identical
+// per-lane results, half the issue slots.
+__device__ __forceinline__ float2 exp2_poly2(float2 x) {
+    x.x = fmaxf(x.x, -125.0f);
+    x.y = fmaxf(x.y, -125.0f);
+    const float2 t = __fadd2_rn(x, make_float2(kRoundMagic, kRoundMagic));
+    const float2 n = __fadd2_rn(t, make_float2(-kRoundMagic, -kRoundMagic));
+    const float2 f = __ffma2_rn(n, make_float2(-1.0f, -1.0f), x);
+    float2 q = __ffma2_rn(make_float2(kExp2C3, kExp2C3), f, make_float2(kExp2C2, kExp2C2));
+    q = __ffma2_rn(q, f, make_float2(kExp2C1, kExp2C1));
+    q = __ffma2_rn(q, f, make_float2(kExp2C0, kExp2C0));
+    return make_float2(__uint_as_float(__float_as_uint(q.x) + (__float_as_uint(t.x) << 23)),
+                       __uint_as_float(__float_as_uint(q.y) + (__float_as_uint(t.y) << 23)));
+}
+
+// Of every 8 consecutive column pairs of a score row, this many take exp2_poly2, the rest ex2.
+constexpr int kPolyPairs = 3;
+
 __device__ __forceinline__ uint32_t half2_bits(__half2 h) {
     uint32_t u;
     memcpy(&u, &h, 4);
@@ -99,7 +150,7 @@ __device__ __forceinline__ uint32_t half2_bits(__half2 h) {
 // Warp-uniform bounded wait: every lane polls, and the warp fails together if any lane gave
 // up, so .sync.aligned tcgen05 instructions that follow stay convergent.
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
-    const bool ok = mbar_wait(bar, parity, err, code);
+    const bool ok = mbar_wait_spin(bar, parity, err, code);
     return __all_sync(0xffffffffu, ok);
 }
 
@@ -308,8 +359,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) packed_attention_kernel(AttnP
     if (warp < kSoftmaxWarps) {
         // ------------------------------------------------------------------ softmax
         const int t = warp >> 2;                         // query tile of this warp group
-        const int qw = warp & 3;                         // TMEM lane quarter
-        const int row = qw * 32 + lane;                  // query row in the tile == TMEM lane
+        const int qw = warp & 3;                         // TMEM lane quarter: rows qw*32 + lane
         {
             // this group's query tile -> shared memory (128B-swizzled, K-major)
             uint8_t* qtile = smem + L::kQ + t * L::kTile;
@@ -343,118 +393,100 @@ __global__ void __launch_bounds__(kAttnThreads, 1) packed_attention_kernel(AttnP
         for (int j = 0; j < nt; ++j) {
             if (!warp_wait(&s_full[t], j & 1, p.err, kErrSFull)) { ok = false; break; }
             tc_fence_after();
+            uint32_t sc[kBN];
+#pragma unroll
+            for (int c = 0; c < kBN / 32; ++c) tmem_ld32(tS + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&sc[c * 32]));
+            tmem_wait_ld();
             // columns at or past n_valid hold no entry (past the head's last stored row)
-            const int n_valid = min(kBN, n_stored - j * kBN);
-            const bool partial = n_valid < kBN;
-            // pass 1: row max, 64 columns per TMEM round trip
+            const int n_valid = n_stored - j * kBN;
+            if (n_valid < kBN) {
+#pragma unroll
+                for (int c = 0; c < kBN; ++c)
+                    if (c >= n_valid) sc[c] = __float_as_uint(-INFINITY);
+            }
             float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
 #pragma unroll
-            for (int c = 0; c < kBN; c += 64) {
-                uint32_t s0[32], s1[32];
-                tmem_ld32(tS + c, s0);
-                tmem_ld32(tS + c + 32, s1);
-                tmem_wait_ld();
-                if (partial) {
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) {
-                        if (c + i >= n_valid) s0[i] = __float_as_uint(-INFINITY);
-                        if (c + 32 + i >= n_valid) s1[i] = __float_as_uint(-INFINITY);
-                    }
-                }
-#pragma unroll
-                for (int i = 0; i < 32; i += 2) {
-                    mx0 = fmaxf(mx0, __uint_as_float(s0[i]));
-                    mx1 = fmaxf(mx1, __uint_as_float(s0[i + 1]));
-                    mx2 = fmaxf(mx2, __uint_as_float(s1[i]));
-                    mx3 = fmaxf(mx3, __uint_as_float(s1[i + 1]));
-                }
+            for (int i = 0; i < kBN; i += 8) {
+                mx0 = fmax3(mx0, __uint_as_float(sc[i]), __uint_as_float(sc[i + 1]));
+                mx1 = fmax3(mx1, __uint_as_float(sc[i + 2]), __uint_as_float(sc[i + 3]));
+                mx2 = fmax3(mx2, __uint_as_float(sc[i + 4]), __uint_as_float(sc[i + 5]));
+                mx3 = fmax3(mx3, __uint_as_float(sc[i + 6]), __uint_as_float(sc[i + 7]));
             }
             const float mt = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * sl2;
             const bool need = mt > m_ref + kRescaleThreshold;
-            if (__any_sync(0xffffffffu, need)) {
-                // rows that keep their reference max use factor 1 (TMEM access is warp-wide);
-                // O_t is stable here: s_full[t] was committed after P_t(j-1) V(j-1)
-                const float f = need ? ex2(m_ref - mt) : 1.0f;   // 0 when m_ref = -inf
-                l *= f;
-                if (j > 0) {
-                    uint32_t o[32];
-#pragma unroll
-                    for (int c = 0; c < D / 32; ++c) {
-                        tmem_ld32(tO + c * 32, o);
-                        tmem_wait_ld();
-#pragma unroll
-                        for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * f);
-                        tmem_st32(tO + c * 32, o);
-                    }
-                }
-                if (need) m_ref = mt;
-            }
-            // pass 2: P = 2^(s*scale - m_ref) in fp16, written over the first kBN/2 columns of
-            // S_t; the packed words of columns [32c, 32c+32) land on columns [16c, 16c+16),
-            // all of which have already been read
-            const float neg_m = -m_ref;
-            float l0 = 0.f, l1 = 0.f, l2 = 0.f, l3 = 0.f;
-            uint32_t sa[32], sb[32];
-            tmem_ld32(tS, sa);
-            tmem_wait_ld();
+            const bool rescale = __any_sync(0xffffffffu, need);
+            // rows that keep their reference max use factor 1 (TMEM access is warp-wide)
+            const float fac = need ? ex2(m_ref - mt) : 1.0f;   // 0 when m_ref = -inf
+            if (need) m_ref = mt;
+            l *= fac;
+            // P = 2^(s*scale - m_ref) in fp16, written over the first kBN/2 columns of S_t
+            // (all of S_t is in registers by now)
+            const float2 sl2x2 = make_float2(sl2, sl2), negm2 = make_float2(-m_ref, -m_ref);
+            float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
 #pragma unroll
             for (int c = 0; c < kBN / 32; ++c) {
-                uint32_t (&cur)[32] = (c & 1) ? sb : sa;
-                uint32_t (&nxt)[32] = (c & 1) ? sa : sb;
-                if (c + 1 < kBN / 32) tmem_ld32(tS + (c + 1) * 32, nxt);
                 uint32_t pk[16];
 #pragma unroll
-                for (int i = 0; i < 32; i += 4) {
-                    float e0 = ex2(fmaf(__uint_as_float(cur[i]), sl2, neg_m));
-                    float e1 = ex2(fmaf(__uint_as_float(cur[i + 1]), sl2, neg_m));
-                    float e2 = ex2(fmaf(__uint_as_float(cur[i + 2]), sl2, neg_m));
-                    float e3 = ex2(fmaf(__uint_as_float(cur[i + 3]), sl2, neg_m));
-                    if (partial) {
-                        const int col = c * 32 + i;
-                        e0 = col < n_valid ? e0 : 0.0f;
-                        e1 = col + 1 < n_valid ? e1 : 0.0f;
-                        e2 = col + 2 < n_valid ? e2 : 0.0f;
-                        e3 = col + 3 < n_valid ? e3 : 0.0f;
-                    }
-                    l0 += e0;
-                    l1 += e1;
-                    l2 += e2;
-                    l3 += e3;
-                    pk[i / 2] = half2_bits(__floats2half2_rn(e0, e1));
-                    pk[i / 2 + 1] = half2_bits(__floats2half2_rn(e2, e3));
+                for (int i = 0; i < 32; i += 2) {
+                    const int col = c * 32 + i;
+                    const float2 x = __ffma2_rn(make_float2(__uint_as_float(sc[col]), __uint_as_float(sc[col + 1])),
+                                                sl2x2, negm2);
+                    const float2 e = ((col >> 1) & 7) < kPolyPairs ? exp2_poly2(x) : make_float2(ex2(x.x), ex2(x.y));
+                    if ((col >> 1) & 1)
+                        acc1 = __fadd2_rn(acc1, e);
+                    else
+                        acc0 = __fadd2_rn(acc0, e);
+                    pk[i / 2] = half2_bits(__floats2half2_rn(e.x, e.y));
                 }
                 tmem_st16(tS + c * 16, pk);
-                if (c + 1 < kBN / 32) tmem_wait_ld();
             }
-            l += (l0 + l1) + (l2 + l3);
+            l += (acc0.x + acc0.y) + (acc1.x + acc1.y);
+            if (rescale && j > 0) {
+                // O_t holds tiles 0..j-1 (s_full[t] was committed after P_t(j-1) V(j-1)) and
+                // P_t(j) V(j) is not issued before p_full[t]: scale it to the new reference max
+                uint32_t o[32];
+#pragma unroll
+                for (int c = 0; c < D / 32; ++c) {
+                    tmem_ld32(tO + c * 32, o);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * fac);
+                    tmem_st32(tO + c * 32, o);
+                }
+            }
             tmem_wait_st();
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&p_full[t]);
         }
-        // epilogue: O / l
-        const int qi = q0 + t * kBM + row;
-        float* orow = p.out + (((int64_t)b * p.H + h) * p.S_q + qi) * D;
+        // epilogue: O / l.  Each warp turns its 32 rows x 32 columns per TMEM load around in
+        // shared memory (the Q/K area, idle once o_full has completed every MMA; rows padded to
+        // 33 words so both directions are bank-conflict free) and stores full 128-byte lines.
         ok = __all_sync(0xffffffffu, ok);
         const bool have = ok && nt > 0 && warp_wait(o_full, 0, p.err, kErrOFull);
+        const int row0 = q0 + t * kBM + qw * 32;             // first query row of this warp
+        const int nrows = min(32, p.S_q - row0);
+        float* obase = p.out + (((int64_t)b * p.H + h) * p.S_q + row0) * D;
         if (have) {
             tc_fence_after();
             const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+            float* buf = reinterpret_cast<float*>(smem) + warp * (32 * 33);
             uint32_t o[32];
 #pragma unroll
             for (int c = 0; c < D / 32; ++c) {
                 tmem_ld32(tO + c * 32, o);
                 tmem_wait_ld();
-                if (qi < p.S_q) {
 #pragma unroll
-                    for (int i = 0; i < 32; i += 4)
-                        *reinterpret_cast<float4*>(orow + c * 32 + i) =
-                            make_float4(__uint_as_float(o[i]) * inv, __uint_as_float(o[i + 1]) * inv,
-                                        __uint_as_float(o[i + 2]) * inv, __uint_as_float(o[i + 3]) * inv);
-                }
+                for (int i = 0; i < 32; ++i) buf[lane * 33 + i] = __uint_as_float(o[i]) * inv;
+                __syncwarp();
+#pragma unroll 8
+                for (int r = 0; r < 32; ++r)
+                    if (r < nrows) obase[(int64_t)r * D + c * 32 + lane] = buf[r * 33 + lane];
+                __syncwarp();
             }
-        } else if (qi < p.S_q) {
-            for (int d = 0; d < D; d += 4) *reinterpret_cast<float4*>(orow + d) = make_float4(0.f, 0.f, 0.f, 0.f);
+        } else {
+            for (int r = 0; r < nrows; ++r)
+                for (int d = lane; d < D; d += 32) obase[(int64_t)r * D + d] = 0.0f;
         }
     } else if (warp == kLoadWarp) {
         // ------------------------------------------------------------------ loader
@@ -463,19 +495,19 @@ __global__ void __launch_bounds__(kAttnThreads, 1) packed_attention_kernel(AttnP
             int nk[2] = {0, 0}, nv[2] = {0, 0};       // copies issued per stage
             for (int j = 0; j < nt; ++j) {
                 const int s = j & 1;
-                if (j >= 2 && !mbar_wait(&k_empty[s], ((j >> 1) - 1) & 1, p.err, kErrKEmpty)) break;
+                if (j >= 2 && !mbar_wait_spin(&k_empty[s], ((j >> 1) - 1) & 1, p.err, kErrKEmpty)) break;
                 mbar_arrive_expect_tx(&k_full[s], TB);
                 bulk_g2s(smem + L::kK + s * TB, g + (int64_t)j * 2 * TB, TB, &k_full[s]);
                 ++nk[s];
-                if (j >= 2 && !mbar_wait(&v_empty[s], ((j >> 1) - 1) & 1, p.err, kErrVEmpty)) break;
+                if (j >= 2 && !mbar_wait_spin(&v_empty[s], ((j >> 1) - 1) & 1, p.err, kErrVEmpty)) break;
                 mbar_arrive_expect_tx(&v_full[s], TB);
                 bulk_g2s(smem + L::kV + s * TB, g + ((int64_t)j * 2 + 1) * TB, TB, &v_full[s]);
                 ++nv[s];
             }
             // every copy issued lands before the CTA can exit (a no-op when the MMA consumed them)
             for (int s = 0; s < 2; ++s) {
-                if (nk[s]) mbar_wait(&k_full[s], (nk[s] - 1) & 1, p.err, kErrCopy);
-                if (nv[s]) mbar_wait(&v_full[s], (nv[s] - 1) & 1, p.err, kErrCopy);
+                if (nk[s]) mbar_wait_spin(&k_full[s], (nk[s] - 1) & 1, p.err, kErrCopy);
+                if (nv[s]) mbar_wait_spin(&v_full[s], (nv[s] - 1) & 1, p.err, kErrCopy);
             }
         }
         __syncwarp();
@@ -502,7 +534,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) packed_attention_kernel(AttnP
                                 smem_desc_sw128(v_base + k * 16 * 128, kBN * 128, 1024), idesc_o,
                                 (j > 0 || k > 0) ? 1u : 0u);
             };
-            bool ok = mbar_wait(q_full, 0, p.err, kErrQFull) && mbar_wait(&k_full[0], 0, p.err, kErrKFull);
+            bool ok = mbar_wait_spin(q_full, 0, p.err, kErrQFull) && mbar_wait_spin(&k_full[0], 0, p.err, kErrKFull);
             if (ok) {
                 tc_fence_after();
                 issue_s(0, 0);
@@ -514,18 +546,18 @@ __global__ void __launch_bounds__(kAttnThreads, 1) packed_attention_kernel(AttnP
             for (int j = 0; ok && j < nt; ++j) {
                 const int s = j & 1, s1 = (j + 1) & 1;
                 const bool more = j + 1 < nt;
-                if (!mbar_wait(&v_full[s], (j >> 1) & 1, p.err, kErrVFull) ||
-                    !mbar_wait(&p_full[0], j & 1, p.err, kErrPFull)) { ok = false; break; }
+                if (!mbar_wait_spin(&v_full[s], (j >> 1) & 1, p.err, kErrVFull) ||
+                    !mbar_wait_spin(&p_full[0], j & 1, p.err, kErrPFull)) { ok = false; break; }
                 tc_fence_after();
                 issue_pv(0, j);
                 if (more) {
-                    if (!mbar_wait(&k_full[s1], ((j + 1) >> 1) & 1, p.err, kErrKFull)) { ok = false; break; }
+                    if (!mbar_wait_spin(&k_full[s1], ((j + 1) >> 1) & 1, p.err, kErrKFull)) { ok = false; break; }
                     tc_fence_after();
                     // issued after P_0(j) V(j): the tensor pipe has read P_0 before S_0 is rewritten
                     issue_s(0, j + 1);
                     umma_commit(&s_full[0]);
                 }
-                if (!mbar_wait(&p_full[1], j & 1, p.err, kErrPFull)) { ok = false; break; }
+                if (!mbar_wait_spin(&p_full[1], j & 1, p.err, kErrPFull)) { ok = false; break; }
                 tc_fence_after();
                 issue_pv(1, j);
                 umma_commit(&v_empty[s]);
@@ -538,7 +570,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) packed_attention_kernel(AttnP
             if (ok) umma_commit(o_full);
             // drain: every UMMA issued above completes before TMEM is released
             umma_commit(drain);
-            mbar_wait(drain, 0, p.err, kErrDrain);
+            mbar_wait_spin(drain, 0, p.err, kErrDrain);
         }
         __syncwarp();
     }
@@ -650,6 +682,8 @@ int skv_head_index(const int32_t* slot, int S, int H, int32_t* rows, int32_t* co
     head_index_kernel<<<H, kHiThreads, 0, as_stream(stream)>>>(slot, S, H, rows, counts);
     return check_launch("head_index");
 }
+
+float skv_exp2_poly(float x) { return exp2_poly(x); }
 
 size_t skv_packed_attention_scratch_bytes(int B, int H, int S_kv, int D) {
     if (B <= 0 || H <= 0 || S_kv <= 0 || (D != 64 && D != 128)) return 0;

@@ -66,6 +66,32 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
     return false;
 }
 
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Bounded wait for a latency-critical pipeline: polls without sleeping (try_wait itself
+// suspends in hardware until the phase completes or a short hardware limit passes), stops
+// early when another role has already recorded an error, and gives up after `limit_ns` of
+// wall time (recording `code`).  Never spins forever.
+__device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity, int* err, int code,
+                                               uint64_t limit_ns = 1000000000ull) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t i = 1;; ++i) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((i & 255) == 0) {
+            if (*reinterpret_cast<volatile int*>(err) != 0) return false;
+            if (globaltimer_ns() - t0 > limit_ns) {
+                atomicCAS(err, 0, code);
+                return false;
+            }
+        }
+    }
+}
+
 // --------------------------------------------------------------------------------- fences
 __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
