@@ -15,14 +15,17 @@
 //      in fp32 as the reference dequantises (q * scale), then rounded.  Evicted entries are
 //      not staged.  Every query tile of the head reuses the staged tiles (from L2), so the
 //      packed bytes are read and converted once per head instead of once per query tile.
-//   2. packed_attention_kernel (skv_attend_kv_tiles), one CTA per (256 queries = two 128-row
-//      tiles, head, batch):
+//   2. packed_attention_kernel (skv_attend_kv_tiles): persistent, one CTA per SM, launched
+//      cooperatively.  A work unit is 256 queries (two 128-row tiles) of one head; the units'
+//      KV steps are split evenly over the CTAs (a unit cut between two CTAs is merged through
+//      a partial (O, max, sum) in scratch).  Per CTA:
 //      warps 0-7  softmax, two groups of four: group t owns query tile t, thread i of the group
 //                 owns query row i = TMEM lane i.  Reads S_t from TMEM, keeps the running max
 //                 and sum (lazy rescale of O_t when the max grows by more than 2^8), and writes
-//                 P_t (fp16) back into TMEM over the first half of S_t's columns.
-//      warp 8     loader: streams the staged K and V tiles into a two-stage shared-memory ring
-//                 with bulk asynchronous copies (one copy per tile, byte-counted mbarriers).
+//                 P_t (fp16) back into TMEM over the first half of S_t's columns; at the end of
+//                 a unit, normalises O_t and stores it.
+//      warp 8     loader: Q tiles by TMA (128B swizzle, no multicast) and the staged K and V
+//                 tiles by bulk asynchronous copies into a two-stage shared-memory ring.
 //      warp 9     MMA issuer (tcgen05.mma kind::f16, M=128, fp32 accumulate):
 //                 S_t = Q_t K_j^T (both operands in shared memory) and O_t += P_t V_j (P read
 //                 from TMEM), interleaved PV_0(j), S_0(j+1), PV_1(j), S_1(j+1) so that the
@@ -31,8 +34,12 @@
 // Evicted entries never enter a tile: their contribution (count * 2^(0 - m)) is added to the
 // softmax denominator analytically.  Every mbarrier wait is bounded; a timeout sets the error
 // word and all roles drain to the final barrier before TMEM is released.
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <math.h>
 #include <string.h>
+
+#include <mutex>
 
 #include "skv_common.cuh"
 #include "sm100_ptx.cuh"
@@ -51,10 +58,14 @@ constexpr uint32_t kTmemCols = 512;
 constexpr float kRescaleThreshold = 8.0f;   // log2 units
 
 enum AttnError { kErrNone = 0, kErrKFull = 1, kErrKEmpty = 2, kErrSFull = 3, kErrPFull = 4, kErrOFull = 5,
-                 kErrDrain = 6, kErrQFull = 7, kErrVFull = 8, kErrVEmpty = 9, kErrCopy = 10 };
+                 kErrDrain = 6, kErrQFull = 7, kErrVFull = 8, kErrVEmpty = 9, kErrCopy = 10, kErrQEmpty = 11,
+                 kErrOEmpty = 12, kErrPartial = 13, kErrSchedule = 14 };
 
 // Bytes of one staged K (or V) tile: D/64 swizzle atoms of 128 rows x 128 bytes.
 __host__ __device__ constexpr int staged_tile_bytes(int D) { return (D / 64) * kBN * 128; }
+
+constexpr int kMaxHeads = 256;     // heads per launch (the schedule keeps a per-head prefix in smem)
+constexpr int kUnitRows = 2 * kBM;  // queries per work unit
 
 template <int D>
 struct AttnLayout {
@@ -64,13 +75,14 @@ struct AttnLayout {
     static constexpr int kK = kQ + 2 * kTile;           // two K stages
     static constexpr int kV = kK + 2 * kTile;           // two V stages
     static constexpr int kBar = kV + 2 * kTile;
-    static constexpr int kNumBars = 16;
-    static constexpr int kTmemSlot = kBar + kNumBars * 8;
+    static constexpr int kNumBars = 24;
+    static constexpr int kHP = kBar + kNumBars * 8;     // int64 [kMaxHeads + 1]: prefix of KV tiles per head
+    static constexpr int kMisc = kHP + (kMaxHeads + 1) * 8;
+    static constexpr int kTmemSlot = kMisc + 16;
     static constexpr int kBytes = kTmemSlot + 16;
     // + slack to align the base to 1024 B; at least 120 KB so that one CTA occupies an SM and
     // its 512-column TMEM allocation never waits for another CTA's
     static constexpr int kAlloc = (kBytes + 1024) > 120 * 1024 ? (kBytes + 1024) : 120 * 1024;
-    static_assert(kSoftmaxWarps * 32 * 33 * 4 <= kBar, "epilogue transpose buffers overlap the barriers");
 };
 
 struct AttnParams {
@@ -80,7 +92,10 @@ struct AttnParams {
     const int32_t* rows;       // [H, S_kv] slot values of the stored entries, grouped by precision
     const int32_t* counts;     // [H, 5]: stored entries per precision, evicted entries
     uint8_t* stage;            // [B, H, ntmax, 2 (K, V), staged_tile_bytes(D)]
-    int B, H, S_q, S_kv, G, ntmax;
+    float* part_o;             // [slots, kUnitRows, D]: unnormalised O of a unit's second part
+    float2* part_ml;           // [slots, kUnitRows]: its (reference max, sum) per query row
+    int* part_flag;            // [slots]: softmax warps that have published their rows
+    int B, H, S_q, S_kv, G, ntmax, QP, slots;
     float scale_log2;          // softmax scale * log2(e)
     int* err;
 };
@@ -282,59 +297,130 @@ __device__ __forceinline__ void store_row(const RawRow<D / 64>& raw, int r, int 
 
 // One CTA per (KV tile j, head h, batch b); tiles past the head's stored rows exit at once.
 // Eight lanes per row (one 16-byte chunk of each atom per lane), 32 rows per pass, 4 passes.
+// The row-list entries are fetched together with the head's counts (entries past the stored
+// rows are discarded afterwards), so a CTA waits for two memory round trips, not three.
 template <int D>
-__global__ void __launch_bounds__(kStageThreads) stage_tiles_kernel(AttnParams p) {
+__global__ void __launch_bounds__(kStageThreads, 2) stage_tiles_kernel(AttnParams p) {
     constexpr int NA = D / 64;
     constexpr int kRowsPerPass = kStageThreads / 8;
     constexpr int kPasses = kBN / kRowsPerPass;
     const int j = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
-    const int* cnt = p.counts + (int64_t)h * 5;
-    const int n_stored = cnt[0] + cnt[1] + cnt[2] + cnt[3];
-    if (j * kBN >= n_stored) return;
     const int rsub = threadIdx.x >> 3, l8 = threadIdx.x & 7;
     const int32_t* hrows = p.rows + (int64_t)h * p.S_kv;
+    int32_t e[kPasses];
+#pragma unroll
+    for (int i = 0; i < kPasses; ++i) {
+        const int idx = j * kBN + i * kRowsPerPass + rsub;
+        e[i] = idx < p.S_kv ? __ldg(hrows + idx) : -1;
+    }
+    const int* cnt = p.counts + (int64_t)h * 5;
+    const int n_stored = __ldg(cnt) + __ldg(cnt + 1) + __ldg(cnt + 2) + __ldg(cnt + 3);
+    if (j * kBN >= n_stored) return;
     uint8_t* ktile = p.stage + staged_offset(p, b, h, j, 0, staged_tile_bytes(D));
     uint8_t* vtile = ktile + staged_tile_bytes(D);
     RawRow<NA> raw[kPasses];
 #pragma unroll
-    for (int i = 0; i < kPasses; ++i) {
-        const int idx = j * kBN + i * kRowsPerPass + rsub;
-        load_raw_row<D>(p, b, idx < n_stored ? __ldg(hrows + idx) : -1, l8, raw[i]);
-    }
+    for (int i = 0; i < kPasses; ++i)
+        load_raw_row<D>(p, b, j * kBN + i * kRowsPerPass + rsub < n_stored ? e[i] : -1, l8, raw[i]);
 #pragma unroll
     for (int i = 0; i < kPasses; ++i) store_row<D>(raw[i], i * kRowsPerPass + rsub, l8, ktile, vtile);
 }
 
 // ------------------------------------------------------------------------------ attention
+// Work schedule.  A unit is (batch b, head h, query pair qp): 256 queries against the head's
+// nt_h staged KV tiles, one step per tile.  Units are ordered (b, h, qp) with qp fastest and
+// their steps laid end to end; CTA c of the G working CTAs takes the contiguous step range
+// [c*T/G, (c+1)*T/G).  G <= T / max(nt_h), so every range holds at least one whole unit's
+// worth of steps and a unit is cut at most once: its first part (steps [0, k)) is the last
+// segment of CTA c, its second part (steps [k, nt)) the first segment of CTA c+1.
+struct Segment {
+    int b, h, qp, j0, j1, nt;
+};
+
+struct Schedule {
+    const long long* hp;       // [H + 1] prefix of KV tiles per head
+    int H, QP;
+    long long per_batch;       // QP * hp[H]
+    long long pos, end;
+
+    __device__ bool next(Segment& s) {
+        if (pos >= end) return false;
+        const long long bb = pos / per_batch;
+        const long long r = pos - bb * per_batch;
+        // largest h with QP * hp[h] <= r; heads without tiles are skipped by construction
+        int lo = 0, hi = H - 1;
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if ((long long)QP * hp[mid] <= r) lo = mid;
+            else hi = mid - 1;
+        }
+        const int nt = (int)(hp[lo + 1] - hp[lo]);
+        const long long r2 = r - (long long)QP * hp[lo];
+        s.b = (int)bb;
+        s.h = lo;
+        s.nt = nt;
+        s.qp = (int)(r2 / nt);
+        s.j0 = (int)(r2 - (long long)s.qp * nt);
+        const long long e = min(pos - s.j0 + nt, end);
+        s.j1 = s.j0 + (int)(e - pos);
+        pos = e;
+        return true;
+    }
+};
+
+// Bounded wait (wall time) until `*flag` reaches `target` (acquire).
+__device__ __forceinline__ bool wait_flag(const int* flag, int target, int* err, int code,
+                                          uint64_t limit_ns = 1000000000ull) {
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t i = 0;; ++i) {
+        int v;
+        asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
+        if (v >= target) return true;
+        __nanosleep(32);
+        if ((i & 63) == 63) {
+            if (*reinterpret_cast<volatile int*>(err) != 0) return false;
+            if (globaltimer_ns() - t0 > limit_ns) {
+                atomicCAS(err, 0, code);
+                return false;
+            }
+        }
+    }
+}
+
+// Persistent, cooperatively launched (one CTA per SM, all resident): warps 0-7 softmax,
+// warp 8 loader, warp 9 MMA issuer, as described at the top of this file, looping over the
+// CTA's segments.  Barrier phases run on across segments (per step for the KV ring, S and P;
+// per segment for Q and O), so the next unit's Q load and first S MMAs overlap the previous
+// unit's epilogue.
 template <int D>
-__global__ void __launch_bounds__(kAttnThreads, 1) packed_attention_kernel(AttnParams p) {
+__global__ void __launch_bounds__(kAttnThreads, 1)
+    packed_attention_kernel(const __grid_constant__ CUtensorMap qmap, AttnParams p) {
     using L = AttnLayout<D>;
     constexpr int NA = L::NA;
     constexpr uint32_t TB = L::kTile;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int h = blockIdx.y, b = blockIdx.z;
-    const int q0 = blockIdx.x * 2 * kBM;
-    const int* cnt = p.counts + (int64_t)h * 5;
-    const int n_stored = cnt[0] + cnt[1] + cnt[2] + cnt[3];
-    const int n_ev = cnt[4];
-    const int nt = (n_stored + kBN - 1) / kBN;
 
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBar);
-    uint64_t* q_full = bars;            // count kSoftmaxWarps
-    uint64_t* k_full = bars + 1;        // [2], expect_tx arrive + copy bytes
-    uint64_t* v_full = bars + 3;        // [2]
-    uint64_t* k_empty = bars + 5;       // [2], commit
-    uint64_t* v_empty = bars + 7;       // [2], commit
-    uint64_t* s_full = bars + 9;        // [2] per query tile, commit
-    uint64_t* p_full = bars + 11;       // [2] per query tile, count 4 (the tile's softmax warps)
-    uint64_t* o_full = bars + 13;       // commit after the last P*V
-    uint64_t* drain = bars + 14;        // commit, drain before TMEM release
+    uint64_t* q_full = bars;            // expect_tx arrive + TMA bytes, per segment
+    uint64_t* q_empty = bars + 1;       // commit after the segment's last S MMAs
+    uint64_t* k_full = bars + 2;        // [2] ring stages
+    uint64_t* v_full = bars + 4;        // [2]
+    uint64_t* k_empty = bars + 6;       // [2] commit
+    uint64_t* v_empty = bars + 8;       // [2] commit
+    uint64_t* s_full = bars + 10;       // [2] per query tile, commit
+    uint64_t* p_full = bars + 12;       // [2] per query tile, 4 softmax warps
+    uint64_t* o_full = bars + 14;       // [2] per query tile, commit after the segment's last P*V
+    uint64_t* o_empty = bars + 16;      // [2] per query tile, 4 softmax warps (O read out)
+    uint64_t* drain = bars + 18;        // commit, drain before TMEM release
+    long long* hp = reinterpret_cast<long long*>(smem + L::kHP);
+    int* misc = reinterpret_cast<int*>(smem + L::kMisc);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kTmemSlot);
 
     if (threadIdx.x == 0) {
-        mbar_init(q_full, kSoftmaxWarps);
+        mbar_init(q_full, 1);
+        mbar_init(q_empty, 1);
         for (int s = 0; s < 2; ++s) {
             mbar_init(&k_full[s], 1);
             mbar_init(&v_full[s], 1);
@@ -342,10 +428,22 @@ __global__ void __launch_bounds__(kAttnThreads, 1) packed_attention_kernel(AttnP
             mbar_init(&v_empty[s], 1);
             mbar_init(&s_full[s], 1);
             mbar_init(&p_full[s], 4);
+            mbar_init(&o_full[s], 1);
+            mbar_init(&o_empty[s], 4);
         }
-        mbar_init(o_full, 1);
         mbar_init(drain, 1);
         fence_mbarrier_init();
+        long long acc = 0;
+        int ntm = 0;
+        for (int hh = 0; hh < p.H; ++hh) {
+            const int* c = p.counts + (int64_t)hh * 5;
+            const int n = (c[0] + c[1] + c[2] + c[3] + kBN - 1) / kBN;
+            hp[hh] = acc;
+            acc += n;
+            ntm = max(ntm, n);
+        }
+        hp[p.H] = acc;
+        misc[0] = ntm;
     }
     if (warp == kMmaWarp) {
         tmem_alloc(tmem_slot, kTmemCols);
@@ -356,169 +454,265 @@ __global__ void __launch_bounds__(kAttnThreads, 1) packed_attention_kernel(AttnP
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
+    Schedule sched;
+    sched.hp = hp;
+    sched.H = p.H;
+    sched.QP = p.QP;
+    sched.per_batch = (long long)p.QP * hp[p.H];
+    sched.pos = sched.end = 0;
+    {
+        const long long T = sched.per_batch * p.B;
+        const int ntm = misc[0];
+        if (T > 0) {
+            const long long cap = T / ntm;
+            const int G = (int)min((long long)gridDim.x, cap);
+            if ((int)blockIdx.x < G) {
+                sched.pos = (long long)blockIdx.x * T / G;
+                sched.end = ((long long)blockIdx.x + 1) * T / G;
+            }
+        }
+    }
+
     if (warp < kSoftmaxWarps) {
         // ------------------------------------------------------------------ softmax
         const int t = warp >> 2;                         // query tile of this warp group
         const int qw = warp & 3;                         // TMEM lane quarter: rows qw*32 + lane
-        {
-            // this group's query tile -> shared memory (128B-swizzled, K-major)
-            uint8_t* qtile = smem + L::kQ + t * L::kTile;
-            const int lrow = lane >> 3, l8 = lane & 7;
-            const __half* qbase = p.q + ((int64_t)b * p.H + h) * p.S_q * D;
-            uint4 v[kBM / 16][NA];
-#pragma unroll
-            for (int it = 0; it < kBM / 16; ++it) {
-                const int qi = q0 + t * kBM + it * 16 + qw * 4 + lrow;
-#pragma unroll
-                for (int a = 0; a < NA; ++a)
-                    v[it][a] = qi < p.S_q ? __ldg(reinterpret_cast<const uint4*>(qbase + (int64_t)qi * D + a * 64 + l8 * 8))
-                                          : make_uint4(0, 0, 0, 0);
-            }
-#pragma unroll
-            for (int it = 0; it < kBM / 16; ++it)
-#pragma unroll
-                for (int a = 0; a < NA; ++a)
-                    *reinterpret_cast<uint4*>(qtile + a * kBM * 128 + sw128_offset(it * 16 + qw * 4 + lrow, l8)) = v[it][a];
-            fence_proxy_async_smem();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(q_full);
-        }
         const uint32_t lane_off = (uint32_t)(qw * 32) << 16;
         const uint32_t tS = tmem + t * kBN + lane_off;
         const uint32_t tO = tmem + 2 * kBN + t * D + lane_off;
         const float sl2 = p.scale_log2;
-        float m_ref = n_ev > 0 ? 0.0f : -INFINITY;       // evicted rows: logit 0
-        float l = (float)n_ev;
+        const int rt = t * kBM + qw * 32;                // first row of this warp in a unit
+        Segment sg;
+        long long g = 0;                                 // steps so far (KV tiles consumed)
+        int si = 0;                                      // segments so far
         bool ok = true;
-        for (int j = 0; j < nt; ++j) {
-            if (!warp_wait(&s_full[t], j & 1, p.err, kErrSFull)) { ok = false; break; }
-            tc_fence_after();
-            uint32_t sc[kBN];
-#pragma unroll
-            for (int c = 0; c < kBN / 32; ++c) tmem_ld32(tS + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&sc[c * 32]));
-            tmem_wait_ld();
-            // columns at or past n_valid hold no entry (past the head's last stored row)
-            const int n_valid = n_stored - j * kBN;
-            if (n_valid < kBN) {
-#pragma unroll
-                for (int c = 0; c < kBN; ++c)
-                    if (c >= n_valid) sc[c] = __float_as_uint(-INFINITY);
+        while (ok && sched.next(sg)) {
+            const int* cnt = p.counts + (int64_t)sg.h * 5;
+            const int n_stored = cnt[0] + cnt[1] + cnt[2] + cnt[3];
+            const int n_ev = cnt[4];
+            const bool first_part = sg.j0 == 0;
+            if (sg.j0 > 0 && sg.j1 < sg.nt) {            // cannot happen with the schedule above
+                atomicCAS(p.err, 0, (int)kErrSchedule);
+                ok = false;
+                break;
             }
-            float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
+            // evicted rows (logit 0, no value) are counted once, by the unit's first part
+            float m_ref = first_part && n_ev > 0 ? 0.0f : -INFINITY;
+            float l = first_part ? (float)n_ev : 0.0f;
+            for (int j = sg.j0; j < sg.j1; ++j, ++g) {
+                if (!warp_wait(&s_full[t], (uint32_t)(g & 1), p.err, kErrSFull)) { ok = false; break; }
+                tc_fence_after();
+                uint32_t sc[kBN];
 #pragma unroll
-            for (int i = 0; i < kBN; i += 8) {
-                mx0 = fmax3(mx0, __uint_as_float(sc[i]), __uint_as_float(sc[i + 1]));
-                mx1 = fmax3(mx1, __uint_as_float(sc[i + 2]), __uint_as_float(sc[i + 3]));
-                mx2 = fmax3(mx2, __uint_as_float(sc[i + 4]), __uint_as_float(sc[i + 5]));
-                mx3 = fmax3(mx3, __uint_as_float(sc[i + 6]), __uint_as_float(sc[i + 7]));
-            }
-            const float mt = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * sl2;
-            const bool need = mt > m_ref + kRescaleThreshold;
-            const bool rescale = __any_sync(0xffffffffu, need);
-            // rows that keep their reference max use factor 1 (TMEM access is warp-wide)
-            const float fac = need ? ex2(m_ref - mt) : 1.0f;   // 0 when m_ref = -inf
-            if (need) m_ref = mt;
-            l *= fac;
-            // P = 2^(s*scale - m_ref) in fp16, written over the first kBN/2 columns of S_t
-            // (all of S_t is in registers by now)
-            const float2 sl2x2 = make_float2(sl2, sl2), negm2 = make_float2(-m_ref, -m_ref);
-            float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
+                for (int c = 0; c < kBN / 32; ++c)
+                    tmem_ld32(tS + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&sc[c * 32]));
+                tmem_wait_ld();
+                // columns at or past n_valid hold no entry (past the head's last stored row)
+                const int n_valid = n_stored - j * kBN;
+                if (n_valid < kBN) {
 #pragma unroll
-            for (int c = 0; c < kBN / 32; ++c) {
-                uint32_t pk[16];
-#pragma unroll
-                for (int i = 0; i < 32; i += 2) {
-                    const int col = c * 32 + i;
-                    const float2 x = __ffma2_rn(make_float2(__uint_as_float(sc[col]), __uint_as_float(sc[col + 1])),
-                                                sl2x2, negm2);
-                    const float2 e = ((col >> 1) & 7) < kPolyPairs ? exp2_poly2(x) : make_float2(ex2(x.x), ex2(x.y));
-                    if ((col >> 1) & 1)
-                        acc1 = __fadd2_rn(acc1, e);
-                    else
-                        acc0 = __fadd2_rn(acc0, e);
-                    pk[i / 2] = half2_bits(__floats2half2_rn(e.x, e.y));
+                    for (int c = 0; c < kBN; ++c)
+                        if (c >= n_valid) sc[c] = __float_as_uint(-INFINITY);
                 }
-                tmem_st16(tS + c * 16, pk);
+                float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
+#pragma unroll
+                for (int i = 0; i < kBN; i += 8) {
+                    mx0 = fmax3(mx0, __uint_as_float(sc[i]), __uint_as_float(sc[i + 1]));
+                    mx1 = fmax3(mx1, __uint_as_float(sc[i + 2]), __uint_as_float(sc[i + 3]));
+                    mx2 = fmax3(mx2, __uint_as_float(sc[i + 4]), __uint_as_float(sc[i + 5]));
+                    mx3 = fmax3(mx3, __uint_as_float(sc[i + 6]), __uint_as_float(sc[i + 7]));
+                }
+                const float mt = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * sl2;
+                const bool need = mt > m_ref + kRescaleThreshold;
+                const bool rescale = __any_sync(0xffffffffu, need);
+                // rows that keep their reference max use factor 1 (TMEM access is warp-wide)
+                const float fac = need ? ex2(m_ref - mt) : 1.0f;   // 0 when m_ref = -inf
+                if (need) m_ref = mt;
+                l *= fac;
+                // P = 2^(s*scale - m_ref) in fp16, written over the first kBN/2 columns of S_t
+                // (all of S_t is in registers by now)
+                const float2 sl2x2 = make_float2(sl2, sl2), negm2 = make_float2(-m_ref, -m_ref);
+                float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
+#pragma unroll
+                for (int c = 0; c < kBN / 32; ++c) {
+                    uint32_t pk[16];
+#pragma unroll
+                    for (int i = 0; i < 32; i += 2) {
+                        const int col = c * 32 + i;
+                        const float2 x = __ffma2_rn(
+                            make_float2(__uint_as_float(sc[col]), __uint_as_float(sc[col + 1])), sl2x2, negm2);
+                        const float2 e =
+                            ((col >> 1) & 7) < kPolyPairs ? exp2_poly2(x) : make_float2(ex2(x.x), ex2(x.y));
+                        if ((col >> 1) & 1)
+                            acc1 = __fadd2_rn(acc1, e);
+                        else
+                            acc0 = __fadd2_rn(acc0, e);
+                        pk[i / 2] = half2_bits(__floats2half2_rn(e.x, e.y));
+                    }
+                    tmem_st16(tS + c * 16, pk);
+                }
+                l += (acc0.x + acc0.y) + (acc1.x + acc1.y);
+                if (rescale && j > sg.j0) {
+                    // O_t holds this segment's tiles so far (s_full[t] was committed after the
+                    // previous P_t V) and the next P_t V waits for p_full[t]: rescale it now
+                    uint32_t o[32];
+#pragma unroll
+                    for (int c = 0; c < D / 32; ++c) {
+                        tmem_ld32(tO + c * 32, o);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * fac);
+                        tmem_st32(tO + c * 32, o);
+                    }
+                }
+                tmem_wait_st();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&p_full[t]);
             }
-            l += (acc0.x + acc0.y) + (acc1.x + acc1.y);
-            if (rescale && j > 0) {
-                // O_t holds tiles 0..j-1 (s_full[t] was committed after P_t(j-1) V(j-1)) and
-                // P_t(j) V(j) is not issued before p_full[t]: scale it to the new reference max
-                uint32_t o[32];
+            if (!ok) break;
+            // ---------------------------------------------------------------- epilogue
+            if (!warp_wait(&o_full[t], (uint32_t)(si & 1), p.err, kErrOFull)) { ok = false; break; }
+            tc_fence_after();
+            const bool split_tail = sg.j0 > 0;                   // second part: publish, unnormalised
+            const bool split_head = first_part && sg.j1 < sg.nt; // first part: merge the second
+            const int slot = blockIdx.x + 1;
+            float mB = -INFINITY, lB = 0.0f;
+            if (split_head) {
+                int got = 1;
+                if (lane == 0) got = wait_flag(p.part_flag + slot, kSoftmaxWarps, p.err, kErrPartial) ? 1 : 0;
+                got = __shfl_sync(0xffffffffu, got, 0);
+                __syncwarp();
+                if (!got) { ok = false; break; }
+                const float2 ml = __ldcg(p.part_ml + (size_t)slot * kUnitRows + rt + lane);
+                mB = ml.x;
+                lB = ml.y;
+            }
+            // per-row factors (thread = row): O = O_this * fa + O_other * fb
+            float fa = 1.0f, fb = 0.0f;
+            if (!split_tail) {
+                const float m = fmaxf(m_ref, mB);
+                fa = m_ref == -INFINITY ? 0.0f : ex2(m_ref - m);
+                fb = split_head ? ex2(mB - m) : 0.0f;
+                const float lt = l * fa + lB * fb;
+                const float inv = lt > 0.0f ? 1.0f / lt : 0.0f;
+                fa *= inv;
+                fb *= inv;
+            }
+            const int row0 = sg.qp * kUnitRows + rt;             // query row within the head
+            float* dst = split_tail ? p.part_o + ((size_t)blockIdx.x * kUnitRows + rt) * D
+                                    : p.out + (((int64_t)sg.b * p.H + sg.h) * p.S_q + row0) * D;
+            const float* src = p.part_o + ((size_t)slot * kUnitRows + rt) * D;
+            const int nrows = split_tail ? 32 : min(32, p.S_q - row0);
+            // O is read in the 16x256b shape: four threads hold 32 contiguous bytes of a row, so
+            // each store instruction writes whole sectors without a shared-memory transpose
+            // (shared memory bandwidth stays with the tensor cores)
+#pragma unroll
+            for (int hf = 0; hf < 2; ++hf) {
+                const int rA = hf * 16 + (lane >> 2), rB = rA + 8;
+                const float faA = __shfl_sync(0xffffffffu, fa, rA), faB = __shfl_sync(0xffffffffu, fa, rB);
+                const float fbA = __shfl_sync(0xffffffffu, fb, rA), fbB = __shfl_sync(0xffffffffu, fb, rB);
 #pragma unroll
                 for (int c = 0; c < D / 32; ++c) {
-                    tmem_ld32(tO + c * 32, o);
+                    uint32_t o[16];
+                    tmem_ld16x256b_x4(tO + c * 32 + ((uint32_t)(hf * 16) << 16), o);
                     tmem_wait_ld();
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * fac);
-                    tmem_st32(tO + c * 32, o);
+                    for (int k = 0; k < 4; ++k) {
+                        const int col = c * 32 + 8 * k + 2 * (lane & 3);
+                        float2 a = make_float2(__uint_as_float(o[4 * k]) * faA, __uint_as_float(o[4 * k + 1]) * faA);
+                        float2 bq = make_float2(__uint_as_float(o[4 * k + 2]) * faB, __uint_as_float(o[4 * k + 3]) * faB);
+                        if (split_head) {
+                            const float2 wa = __ldcg(reinterpret_cast<const float2*>(src + (int64_t)rA * D + col));
+                            const float2 wb = __ldcg(reinterpret_cast<const float2*>(src + (int64_t)rB * D + col));
+                            a.x = fmaf(wa.x, fbA, a.x);
+                            a.y = fmaf(wa.y, fbA, a.y);
+                            bq.x = fmaf(wb.x, fbB, bq.x);
+                            bq.y = fmaf(wb.y, fbB, bq.y);
+                        }
+                        if (rA < nrows) *reinterpret_cast<float2*>(dst + (int64_t)rA * D + col) = a;
+                        if (rB < nrows) *reinterpret_cast<float2*>(dst + (int64_t)rB * D + col) = bq;
+                    }
                 }
             }
-            tmem_wait_st();
+            // O_t has been read out: the next segment's first P_t V may overwrite it
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&p_full[t]);
-        }
-        // epilogue: O / l.  Each warp turns its 32 rows x 32 columns per TMEM load around in
-        // shared memory (the Q/K area, idle once o_full has completed every MMA; rows padded to
-        // 33 words so both directions are bank-conflict free) and stores full 128-byte lines.
-        ok = __all_sync(0xffffffffu, ok);
-        const bool have = ok && nt > 0 && warp_wait(o_full, 0, p.err, kErrOFull);
-        const int row0 = q0 + t * kBM + qw * 32;             // first query row of this warp
-        const int nrows = min(32, p.S_q - row0);
-        float* obase = p.out + (((int64_t)b * p.H + h) * p.S_q + row0) * D;
-        if (have) {
-            tc_fence_after();
-            const float inv = l > 0.0f ? 1.0f / l : 0.0f;
-            float* buf = reinterpret_cast<float*>(smem) + warp * (32 * 33);
-            uint32_t o[32];
-#pragma unroll
-            for (int c = 0; c < D / 32; ++c) {
-                tmem_ld32(tO + c * 32, o);
-                tmem_wait_ld();
-#pragma unroll
-                for (int i = 0; i < 32; ++i) buf[lane * 33 + i] = __uint_as_float(o[i]) * inv;
+            if (lane == 0) mbar_arrive(&o_empty[t]);
+            if (split_tail) {
+                p.part_ml[(size_t)blockIdx.x * kUnitRows + rt + lane] = make_float2(m_ref, l);
+                __threadfence();
                 __syncwarp();
-#pragma unroll 8
-                for (int r = 0; r < 32; ++r)
-                    if (r < nrows) obase[(int64_t)r * D + c * 32 + lane] = buf[r * 33 + lane];
-                __syncwarp();
+                if (lane == 0) atomicAdd(p.part_flag + blockIdx.x, 1);
             }
-        } else {
-            for (int r = 0; r < nrows; ++r)
-                for (int d = lane; d < D; d += 32) obase[(int64_t)r * D + d] = 0.0f;
+            ++si;
+        }
+        // units of heads without a stored entry are never scheduled: their output is zero
+        const long long U = (long long)p.B * p.H * p.QP;
+        for (long long u = blockIdx.x; u < U; u += gridDim.x) {
+            const int qp = (int)(u % p.QP);
+            const int hh = (int)((u / p.QP) % p.H);
+            const int bb = (int)(u / ((long long)p.QP * p.H));
+            if (hp[hh + 1] != hp[hh]) continue;
+            const int row0 = qp * kUnitRows + rt;
+            float* dst = p.out + (((int64_t)bb * p.H + hh) * p.S_q + row0) * D;
+            for (int r = 0; r < min(32, p.S_q - row0); ++r)
+                for (int d = lane; d < D; d += 32) dst[(int64_t)r * D + d] = 0.0f;
         }
     } else if (warp == kLoadWarp) {
         // ------------------------------------------------------------------ loader
-        if (lane == 0 && nt > 0) {
-            const uint8_t* g = p.stage + staged_offset(p, b, h, 0, 0, TB);
-            int nk[2] = {0, 0}, nv[2] = {0, 0};       // copies issued per stage
-            for (int j = 0; j < nt; ++j) {
-                const int s = j & 1;
-                if (j >= 2 && !mbar_wait_spin(&k_empty[s], ((j >> 1) - 1) & 1, p.err, kErrKEmpty)) break;
-                mbar_arrive_expect_tx(&k_full[s], TB);
-                bulk_g2s(smem + L::kK + s * TB, g + (int64_t)j * 2 * TB, TB, &k_full[s]);
-                ++nk[s];
-                if (j >= 2 && !mbar_wait_spin(&v_empty[s], ((j >> 1) - 1) & 1, p.err, kErrVEmpty)) break;
-                mbar_arrive_expect_tx(&v_full[s], TB);
-                bulk_g2s(smem + L::kV + s * TB, g + ((int64_t)j * 2 + 1) * TB, TB, &v_full[s]);
-                ++nv[s];
+        if (lane == 0) {
+            Segment sg;
+            long long g = 0;
+            int si = 0, nq = 0;
+            int nk[2] = {0, 0}, nv[2] = {0, 0};          // copies issued per stage
+            bool ok = true;
+            while (ok && sched.next(sg)) {
+                if (si > 0 && !mbar_wait_spin(q_empty, (uint32_t)((si - 1) & 1), p.err, kErrQEmpty)) break;
+                mbar_arrive_expect_tx(q_full, 2 * TB);
+                const int qrow = (sg.b * p.H + sg.h) * p.S_q + sg.qp * kUnitRows;
+#pragma unroll
+                for (int t = 0; t < 2; ++t)
+#pragma unroll
+                    for (int a = 0; a < NA; ++a)
+                        tma_load_2d(smem + L::kQ + t * TB + a * kBM * 128, &qmap, a * 64, qrow + t * kBM, q_full);
+                ++nq;
+                const uint8_t* gkv = p.stage + staged_offset(p, sg.b, sg.h, 0, 0, TB);
+                for (int j = sg.j0; j < sg.j1; ++j, ++g) {
+                    const int s = (int)(g & 1);
+                    if (g >= 2 && !mbar_wait_spin(&k_empty[s], (uint32_t)(((g >> 1) - 1) & 1), p.err, kErrKEmpty)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&k_full[s], TB);
+                    bulk_g2s(smem + L::kK + s * TB, gkv + (int64_t)j * 2 * TB, TB, &k_full[s]);
+                    ++nk[s];
+                    if (g >= 2 && !mbar_wait_spin(&v_empty[s], (uint32_t)(((g >> 1) - 1) & 1), p.err, kErrVEmpty)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&v_full[s], TB);
+                    bulk_g2s(smem + L::kV + s * TB, gkv + ((int64_t)j * 2 + 1) * TB, TB, &v_full[s]);
+                    ++nv[s];
+                }
+                ++si;
             }
             // every copy issued lands before the CTA can exit (a no-op when the MMA consumed them)
+            if (nq) mbar_wait_spin(q_full, (uint32_t)((nq - 1) & 1), p.err, kErrCopy);
             for (int s = 0; s < 2; ++s) {
-                if (nk[s]) mbar_wait_spin(&k_full[s], (nk[s] - 1) & 1, p.err, kErrCopy);
-                if (nv[s]) mbar_wait_spin(&v_full[s], (nv[s] - 1) & 1, p.err, kErrCopy);
+                if (nk[s]) mbar_wait_spin(&k_full[s], (uint32_t)((nk[s] - 1) & 1), p.err, kErrCopy);
+                if (nv[s]) mbar_wait_spin(&v_full[s], (uint32_t)((nv[s] - 1) & 1), p.err, kErrCopy);
             }
         }
         __syncwarp();
     } else {
         // ----------------------------------------------------------------- MMA issue
-        if (lane == 0 && nt > 0) {
+        if (lane == 0) {
             const uint32_t idesc_s = idesc_f16_f32(kBM, kBN, false, false);
             const uint32_t idesc_o = idesc_f16_f32(kBM, D, false, true);
             const uint32_t q_base = smem_u32(smem + L::kQ);
-            auto issue_s = [&](int t, int j) {
-                const uint32_t k_base = smem_u32(smem + L::kK + (j & 1) * TB);
+            auto issue_s = [&](int t, long long g) {
+                const uint32_t k_base = smem_u32(smem + L::kK + (int)(g & 1) * TB);
 #pragma unroll
                 for (int k = 0; k < D / 16; ++k) {
                     const uint32_t off = (k >> 2) * (kBN * 128) + (k & 3) * 32;
@@ -526,51 +720,80 @@ __global__ void __launch_bounds__(kAttnThreads, 1) packed_attention_kernel(AttnP
                              smem_desc_sw128(k_base + off, 16, 1024), idesc_s, k > 0 ? 1u : 0u);
                 }
             };
-            auto issue_pv = [&](int t, int j) {
-                const uint32_t v_base = smem_u32(smem + L::kV + (j & 1) * TB);
+            auto issue_pv = [&](int t, long long g, bool acc) {
+                const uint32_t v_base = smem_u32(smem + L::kV + (int)(g & 1) * TB);
 #pragma unroll
                 for (int k = 0; k < kBN / 16; ++k)
                     umma_f16_ts(tmem + 2 * kBN + t * D, tmem + t * kBN + k * 8,
                                 smem_desc_sw128(v_base + k * 16 * 128, kBN * 128, 1024), idesc_o,
-                                (j > 0 || k > 0) ? 1u : 0u);
+                                (acc || k > 0) ? 1u : 0u);
             };
-            bool ok = mbar_wait_spin(q_full, 0, p.err, kErrQFull) && mbar_wait_spin(&k_full[0], 0, p.err, kErrKFull);
-            if (ok) {
+            Segment sg;
+            long long g = 0;
+            int si = 0;
+            bool ok = true, issued = false;
+            while (ok && sched.next(sg)) {
+                const int len = sg.j1 - sg.j0;
+                if (!mbar_wait_spin(q_full, (uint32_t)(si & 1), p.err, kErrQFull) ||
+                    !mbar_wait_spin(&k_full[g & 1], (uint32_t)((g >> 1) & 1), p.err, kErrKFull)) {
+                    ok = false;
+                    break;
+                }
                 tc_fence_after();
-                issue_s(0, 0);
+                // S of the segment's first step; P_t of the previous segment's last step has
+                // been read by its P_t V, issued before (the tensor pipe runs in issue order)
+                issue_s(0, g);
                 umma_commit(&s_full[0]);
-                issue_s(1, 0);
+                issue_s(1, g);
                 umma_commit(&s_full[1]);
-                umma_commit(&k_empty[0]);
-            }
-            for (int j = 0; ok && j < nt; ++j) {
-                const int s = j & 1, s1 = (j + 1) & 1;
-                const bool more = j + 1 < nt;
-                if (!mbar_wait_spin(&v_full[s], (j >> 1) & 1, p.err, kErrVFull) ||
-                    !mbar_wait_spin(&p_full[0], j & 1, p.err, kErrPFull)) { ok = false; break; }
-                tc_fence_after();
-                issue_pv(0, j);
-                if (more) {
-                    if (!mbar_wait_spin(&k_full[s1], ((j + 1) >> 1) & 1, p.err, kErrKFull)) { ok = false; break; }
+                umma_commit(&k_empty[g & 1]);
+                if (len == 1) umma_commit(q_empty);
+                issued = true;
+                for (int j = 0; j < len; ++j, ++g) {
+                    const int s = (int)(g & 1), s1 = (int)((g + 1) & 1);
+                    const bool more = j + 1 < len;
+                    if (!mbar_wait_spin(&v_full[s], (uint32_t)((g >> 1) & 1), p.err, kErrVFull) ||
+                        !mbar_wait_spin(&p_full[0], (uint32_t)(g & 1), p.err, kErrPFull) ||
+                        (j == 0 && si > 0 && !mbar_wait_spin(&o_empty[0], (uint32_t)((si - 1) & 1), p.err, kErrOEmpty))) {
+                        ok = false;
+                        break;
+                    }
                     tc_fence_after();
-                    // issued after P_0(j) V(j): the tensor pipe has read P_0 before S_0 is rewritten
-                    issue_s(0, j + 1);
-                    umma_commit(&s_full[0]);
+                    issue_pv(0, g, j > 0);
+                    if (!more) umma_commit(&o_full[0]);
+                    if (more) {
+                        if (!mbar_wait_spin(&k_full[s1], (uint32_t)(((g + 1) >> 1) & 1), p.err, kErrKFull)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        // issued after P_0 V: the tensor pipe has read P_0 before S_0 is rewritten
+                        issue_s(0, g + 1);
+                        umma_commit(&s_full[0]);
+                    }
+                    if (!mbar_wait_spin(&p_full[1], (uint32_t)(g & 1), p.err, kErrPFull) ||
+                        (j == 0 && si > 0 && !mbar_wait_spin(&o_empty[1], (uint32_t)((si - 1) & 1), p.err, kErrOEmpty))) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    issue_pv(1, g, j > 0);
+                    umma_commit(&v_empty[s]);
+                    if (!more) umma_commit(&o_full[1]);
+                    if (more) {
+                        issue_s(1, g + 1);
+                        umma_commit(&s_full[1]);
+                        umma_commit(&k_empty[s1]);
+                        if (j + 2 == len) umma_commit(q_empty);
+                    }
                 }
-                if (!mbar_wait_spin(&p_full[1], j & 1, p.err, kErrPFull)) { ok = false; break; }
-                tc_fence_after();
-                issue_pv(1, j);
-                umma_commit(&v_empty[s]);
-                if (more) {
-                    issue_s(1, j + 1);
-                    umma_commit(&s_full[1]);
-                    umma_commit(&k_empty[s1]);
-                }
+                ++si;
             }
-            if (ok) umma_commit(o_full);
-            // drain: every UMMA issued above completes before TMEM is released
-            umma_commit(drain);
-            mbar_wait_spin(drain, 0, p.err, kErrDrain);
+            if (issued) {
+                // drain: every UMMA issued above completes before TMEM is released
+                umma_commit(drain);
+                mbar_wait_spin(drain, 0, p.err, kErrDrain);
+            }
         }
         __syncwarp();
     }
@@ -688,7 +911,11 @@ float skv_exp2_poly(float x) { return exp2_poly(x); }
 size_t skv_packed_attention_scratch_bytes(int B, int H, int S_kv, int D) {
     if (B <= 0 || H <= 0 || S_kv <= 0 || (D != 64 && D != 128)) return 0;
     const size_t ntmax = (size_t)(S_kv + kBN - 1) / kBN;
-    return (size_t)B * H * ntmax * 2 * staged_tile_bytes(D);
+    const size_t slots = (size_t)sm_count();
+    return (size_t)B * H * ntmax * 2 * staged_tile_bytes(D)           // staged K/V tiles
+           + slots * kUnitRows * D * sizeof(float)                    // partial O
+           + slots * kUnitRows * sizeof(float2)                       // partial (max, sum)
+           + ((slots * sizeof(int) + 255) & ~size_t(255));            // partial flags
 }
 
 }  // extern "C"
@@ -715,6 +942,8 @@ int attn_params(const void* q, int B, int H, int S_q, int D, const skv_bucket* b
     const size_t need = skv_packed_attention_scratch_bytes(B, H, S_kv, D);
     if (scratch_bytes < need)
         return fail(SKV_ERR_SCRATCH, "%s: scratch of %zu bytes, %zu needed", what, scratch_bytes, need);
+    if ((long long)B * H * S_q >= (1ll << 31) || H > kMaxHeads)
+        return fail(SKV_ERR_TOO_LARGE, "%s: B*H*S_q must stay below 2^31 and H <= %d", what, kMaxHeads);
     memset(&prm, 0, sizeof(prm));
     prm.q = reinterpret_cast<const __half*>(q);
     prm.out = out;
@@ -723,12 +952,20 @@ int attn_params(const void* q, int B, int H, int S_q, int D, const skv_bucket* b
     prm.rows = rows;
     prm.counts = counts;
     prm.stage = reinterpret_cast<uint8_t*>(scratch);
+    prm.ntmax = (S_kv + kBN - 1) / kBN;
+    prm.slots = sm_count();
+    uint8_t* part = prm.stage + (size_t)B * H * prm.ntmax * 2 * staged_tile_bytes(D);
+    prm.part_o = reinterpret_cast<float*>(part);
+    part += (size_t)prm.slots * kUnitRows * D * sizeof(float);
+    prm.part_ml = reinterpret_cast<float2*>(part);
+    part += (size_t)prm.slots * kUnitRows * sizeof(float2);
+    prm.part_flag = reinterpret_cast<int*>(part);
     prm.B = B;
     prm.H = H;
     prm.S_q = S_q;
     prm.S_kv = S_kv;
     prm.G = G;
-    prm.ntmax = (S_kv + kBN - 1) / kBN;
+    prm.QP = (S_q + kUnitRows - 1) / kUnitRows;
     prm.scale_log2 = scale * 1.4426950408889634f;
     prm.err = error_flag;
     return SKV_OK;
@@ -753,6 +990,57 @@ int skv_stage_kv_tiles(const skv_bucket* buckets, int B, int H, int S_kv, int D,
     return check_launch("stage_kv_tiles");
 }
 
+}  // extern "C"
+
+namespace {
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link against libcuda).
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static std::once_flag once;
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    std::call_once(once, [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+    });
+    return fn;
+}
+
+template <int D>
+int launch_attention(const AttnParams& prm, cudaStream_t s) {
+    auto enc = tensor_map_encoder();
+    if (!enc) return fail(SKV_ERR_CUDA, "attend_kv_tiles: cuTensorMapEncodeTiled is not available");
+    // Q as a 2-D tensor [B*H*S_q rows, D columns] of fp16; boxes of 128 rows x 64 columns land
+    // in shared memory in the 128-byte-swizzled layout the UMMA descriptors describe
+    CUtensorMap qmap;
+    const cuuint64_t dims[2] = {(cuuint64_t)D, (cuuint64_t)prm.B * prm.H * prm.S_q};
+    const cuuint64_t strides[1] = {(cuuint64_t)D * sizeof(__half)};
+    const cuuint32_t box[2] = {64, (cuuint32_t)kBM};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = enc(&qmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(prm.q), dims, strides, box,
+                           estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(SKV_ERR_CUDA, "attend_kv_tiles: tensor map encoding failed (%d)", (int)r);
+    if (cudaMemsetAsync(prm.part_flag, 0, (size_t)prm.slots * sizeof(int), s) != cudaSuccess)
+        return fail(SKV_ERR_CUDA, "attend_kv_tiles: memset failed");
+    const int smem = AttnLayout<D>::kAlloc;
+    cudaFuncSetAttribute(packed_attention_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    AttnParams a = prm;
+    void* args[] = {&qmap, &a};
+    const cudaError_t e = cudaLaunchCooperativeKernel(reinterpret_cast<void*>(packed_attention_kernel<D>),
+                                                      dim3((unsigned)prm.slots), dim3(kAttnThreads), args,
+                                                      (size_t)smem, s);
+    if (e != cudaSuccess)
+        return fail(SKV_ERR_CUDA, "attend_kv_tiles: cooperative launch failed: %s", cudaGetErrorString(e));
+    return check_launch("attend_kv_tiles");
+}
+
+}  // namespace
+
+extern "C" {
+
 int skv_attend_kv_tiles(const void* q, int B, int H, int S_q, int D, int S_kv, const int32_t* rows,
                         const int32_t* counts, float scale, const void* scratch, size_t scratch_bytes, float* out,
                         int32_t* error_flag, void* stream) {
@@ -764,17 +1052,7 @@ int skv_attend_kv_tiles(const void* q, int B, int H, int S_q, int D, int S_kv, c
     cudaStream_t s = as_stream(stream);
     if (cudaMemsetAsync(error_flag, 0, sizeof(int32_t), s) != cudaSuccess)
         return fail(SKV_ERR_CUDA, "attend_kv_tiles: memset failed");
-    const dim3 grid((unsigned)((S_q + 2 * kBM - 1) / (2 * kBM)), (unsigned)H, (unsigned)B);
-    if (D == 128) {
-        const int smem = AttnLayout<128>::kAlloc;
-        cudaFuncSetAttribute(packed_attention_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-        packed_attention_kernel<128><<<grid, kAttnThreads, smem, s>>>(prm);
-    } else {
-        const int smem = AttnLayout<64>::kAlloc;
-        cudaFuncSetAttribute(packed_attention_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-        packed_attention_kernel<64><<<grid, kAttnThreads, smem, s>>>(prm);
-    }
-    return check_launch("attend_kv_tiles");
+    return D == 128 ? launch_attention<128>(prm, s) : launch_attention<64>(prm, s);
 }
 
 int skv_packed_attention(const void* q, int B, int H, int S_q, int D, const skv_bucket* buckets, int S_kv,

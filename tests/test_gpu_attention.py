@@ -49,7 +49,7 @@ CASES = [
     (1, 4, 300, 200, 128, (0.1, 0.2, 0.3, 0.3, 0.1), 1.0),
     (2, 2, 129, 64, 64, (0.0, 0.3, 0.4, 0.2, 0.1), 1.0),
     (1, 2, 1000, 257, 128, (0.05, 0.2, 0.5, 0.2, 0.05), 4.0),     # wide logits: running-max rescales
-    (1, 3, 512, 128, 128, (0.0, 0.0, 1.0, 0.0, 0.0), 1.0),       # int8 only (scales folded into softmax)
+    (1, 3, 512, 128, 128, (0.0, 0.0, 1.0, 0.0, 0.0), 1.0),       # int8 only
     (1, 3, 512, 128, 128, (0.0, 0.0, 0.0, 1.0, 0.0), 1.0),       # int4 only
     (1, 2, 384, 130, 128, (1.0, 0.0, 0.0, 0.0, 0.0), 1.0),       # fp32 only, ragged query tile
     (3, 1, 77, 33, 64, (0.2, 0.2, 0.2, 0.2, 0.2), 2.0),
@@ -68,6 +68,43 @@ def test_attention_matches_oracle(skv, B, H, S, SQ, D, probs, qs):
     out = skv.packed_attention(torch.from_numpy(q).cuda(), cache)
     ref = O.packed_attention(q.astype(np.float32), O.pack(k, v, O.plan_from_codes(codes), 16))
     assert rel_l2(out.cpu().numpy(), ref) < REL_L2_TOL
+
+
+def _check(skv, k, v, codes, q):
+    cache = _pack(skv, k, v, codes)
+    out = skv.packed_attention(torch.from_numpy(q).cuda(), cache).cpu().numpy()
+    ref = O.packed_attention(q.astype(np.float32), O.pack(k, v, O.plan_from_codes(codes), 16))
+    assert rel_l2(out, ref) < REL_L2_TOL
+    # row by row too: a unit merged from two CTAs' partial results must be right everywhere
+    err = np.linalg.norm(out - ref, axis=-1) / np.maximum(np.linalg.norm(ref, axis=-1), 1e-30)
+    assert float(err.max()) < 1e-2
+
+
+@pytest.mark.parametrize("B,D", [(1, 64), (2, 128)])
+def test_attention_units_cut_between_ctas(skv, B, D):
+    """Heads with 1, 2, 3 and 4 KV tiles: the even split of the steps over the working CTAs
+    cuts units in two, whose partial (O, max, sum) are merged; evicted entries in a cut unit
+    are counted once."""
+    rng = np.random.default_rng(11 + D)
+    H, S, SQ = 4, 512, 256
+    k = rng.standard_normal((B, H, S, D)).astype(np.float32)
+    v = rng.standard_normal((B, H, S, D)).astype(np.float32)
+    codes = rng.integers(1, 4, size=(S, H)).astype(np.int8)
+    for h in range(H):
+        codes[(h + 1) * 128 - 7:, h] = 4               # head h keeps (h+1)*128-7 rows
+    q = rng.standard_normal((B, H, SQ, D)).astype(np.float16)
+    _check(skv, k, v, codes, q)
+
+
+def test_attention_more_units_than_sms(skv):
+    """160 units of 256 queries (more than one per SM): every CTA's range is cut somewhere."""
+    rng = np.random.default_rng(23)
+    B, H, S, SQ, D = 1, 8, 384, 5000, 128
+    k = rng.standard_normal((B, H, S, D)).astype(np.float32)
+    v = rng.standard_normal((B, H, S, D)).astype(np.float32)
+    codes = rng.choice(5, size=(S, H), p=(0.0, 0.3, 0.4, 0.25, 0.05)).astype(np.int8)
+    q = rng.standard_normal((B, H, SQ, D)).astype(np.float16)
+    _check(skv, k, v, codes, q)
 
 
 def test_attention_all_evicted_head_and_after_evict(skv):
