@@ -248,14 +248,11 @@ def attention_phase(args, world, rank, dev, dist, lib, tensor_peak):
     gathered = torch.empty(B, H, S, D, dtype=torch.float32, device=dev)
     comm = torch.cuda.Stream(device=dev)
     steps = max(3, min(args.steps, 32))
-    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    kev = [tuple(torch.cuda.Event(enable_timing=True) for _ in range(3)) for _ in range(steps)]
 
     def step(i=None):
-        if i is not None:
-            kev[i][0].record()
-        out = packed_attention(qd, cache, check=False)
-        if i is not None:
-            kev[i][1].record()
+        # events: before the staging kernel, between the two kernels, after the attention kernel
+        out = packed_attention(qd, cache, check=False, events=kev[i] if i is not None else None)
         if world > 1:
             done = torch.cuda.Event()
             done.record()
@@ -288,8 +285,12 @@ def attention_phase(args, world, rank, dev, dist, lib, tensor_peak):
     if world > 1:
         dist.all_reduce(ms, op=dist.ReduceOp.MAX)
     ms = float(ms.item())
-    kms = statistics.mean(a.elapsed_time(b) for a, b in kev)
+    stage_ms = statistics.mean(a.elapsed_time(b) for a, b, _ in kev)
+    kms = statistics.mean(b.elapsed_time(c) for _, b, c in kev)
     flops_rank = 4.0 * B * hs * S * S * D
+    # staging kernel: reads the packed rows, writes fp16 K/V tiles (evicted entries skipped)
+    stored = int(sum(cache._count.values()))
+    stage_bytes = cache.memory_bytes() + stored * 4 + stored * 2 * B * D * 2
     res = {
         "metric": "packed-attn tokens/s (32-layer stack, cfg3)",
         "value": B * S / (L * ms / 1e3), "unit": "tokens/s", "ms_per_layer": ms, "steps": steps,
@@ -300,7 +301,10 @@ def attention_phase(args, world, rank, dev, dist, lib, tensor_peak):
                      "achieved": flops_rank / (kms / 1e3) / 1e12, "peak": tensor_peak[0], "unit": "TFLOP/s",
                      "frac": flops_rank / (kms / 1e3) / 1e12 / tensor_peak[0],
                      "peak_source": tensor_peak[1], "avg_launch_ms": kms, "flops_per_launch": flops_rank,
-                     "traffic": None},
+                     "traffic": committed_traffic("packed_attention_kernel_cfg3.md")},
+        "staging": {"kernel": "stage_tiles_kernel", "bound": "hbm", "avg_launch_ms": stage_ms,
+                    "algorithmic_bytes": stage_bytes, "achieved_gbs": stage_bytes / (stage_ms / 1e3) / 1e9,
+                    "traffic": committed_traffic("stage_tiles_kernel_cfg3.md")},
         "gpu_launches": launches,
         "output_dtype": "f32",
     }
@@ -482,7 +486,7 @@ def run_b200(args):
     peak, peak_kind = hbm_peak()
     pack_avg_ms = statistics.mean(pack_ms)
     achieved = parts["pack"] / (pack_avg_ms / 1e3) / 1e9
-    traffic = committed_traffic("pack_fast_kernel_cfg2.md")
+    traffic = committed_traffic("pack16_kernel_cfg2.md")
     line = {
         "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
@@ -492,7 +496,7 @@ def run_b200(args):
                    "B": B, "H": H, "S": S, "D": D, "layers_per_gpu": 1, "budget_bytes": budget,
                    "l2": "inputs larger than L2 (K+V 268 MB per layer)",
                    "bytes_per_step": parts},
-        "roofline": {"kernel": "pack_fast_kernel", "bound": "hbm", "achieved": achieved, "peak": peak,
+        "roofline": {"kernel": "pack16_kernel", "bound": "hbm", "achieved": achieved, "peak": peak,
                      "unit": "GB/s", "frac": achieved / peak, "peak_source": f"{peak_kind} hbm_gbs",
                      "traffic": traffic, "algorithmic_bytes": parts["pack"], "avg_launch_ms": pack_avg_ms},
         "e2e": {"value": world * nbytes * e2e_steps / (e2e_ms / 1e3) / 1e9, "unit": "GB/s",
