@@ -14,6 +14,7 @@
 //    key prefix identically, and a final sweep writes the new codes, the predicted bytes
 //    and the eviction count.
 #include <math.h>
+#include <stddef.h>
 
 #include "skv_common.cuh"
 
@@ -136,10 +137,12 @@ __device__ __forceinline__ bool eligible(const AdmitArgs& a, int64_t i) {
     return true;
 }
 
-__device__ __forceinline__ unsigned long long entry_key(const AdmitArgs& a, int64_t i) {
+// Unique, order-preserving key: score bits above the flat index (idx_bits >= log2(n)), so
+// ascending keys are the reference's stable ascending-score order.
+__device__ __forceinline__ unsigned long long entry_key(const AdmitArgs& a, int64_t i, int idx_bits) {
     const float imp = a.imp[i];
     const float s = (a.rd && a.sens) ? __fmul_rn(imp, a.sens[i]) : imp;
-    return ((unsigned long long)score_bits(s) << 32) | (unsigned long long)i;
+    return ((unsigned long long)score_bits(s) << idx_bits) | (unsigned long long)i;
 }
 
 __device__ __forceinline__ int code_after_a(const AdmitHeader& st, int base, unsigned long long key) {
@@ -155,48 +158,57 @@ __device__ __forceinline__ long long cost_of(const AdmitArgs& a, int code) {
 
 // ---------------------------------------------------------------------------------------
 // Persistent admission: every phase and digit pass of the radix select in ONE cooperative
-// launch.  Blocks meet at a bounded grid barrier after each histogram pass; each pass has its
-// own global histogram (no zeroing between passes), and every block derives the same
-// selection state from it, so no block has to broadcast decisions.
+// launch (one 1024-thread block per SM).  Keys are (score bits << idx_bits) | flat index, cut
+// into 10-bit digits from the top.  Each pass histograms the candidates' weights per digit,
+// together with their count and largest key, into its own global histogram (zeroed in-kernel
+// before the first barrier); after a bounded grid barrier every block scans the same
+// histogram and narrows the key prefix identically.  When the boundary bin holds a single
+// candidate its key is that bin's largest key, so a phase usually ends after 2-3 passes.
 // ---------------------------------------------------------------------------------------
-constexpr int kAdmitMaxPasses = 8;                     // 4 score digits + up to 4 index digits
+constexpr int kAdmitThreads = 1024;
+constexpr int kDigitBits = 10;
+constexpr int kBins = 1 << kDigitBits;
+constexpr int kAdmitMaxPasses = 7;                     // ceil(64 / 10)
+static_assert(kBins == kAdmitThreads, "one histogram bin per thread");
 
 struct AdmitScratch {
-    unsigned long long hist[2 * kAdmitMaxPasses][256];
     long long sums[4];                                 // predicted0, predicted_final, evicted, -
     unsigned bar_count, bar_gen;
     int err, pad;
+    unsigned long long hist_k[2 * kAdmitMaxPasses][kBins];
+    unsigned int hist_c[2 * kAdmitMaxPasses][5][kBins];   // candidates per (weight class, digit)
 };
+constexpr size_t kAdmitHeaderBytes = offsetof(AdmitScratch, hist_k);
 
 struct AdmitPlanDigits {
-    int shift[kAdmitMaxPasses];
+    int lo[kAdmitMaxPasses];                           // lowest key bit of each digit
+    int width[kAdmitMaxPasses];                        // bits in each digit (<= kDigitBits)
     int n;
+    int idx_bits;
 };
 
-// Bounded grid barrier (cooperative launch guarantees every block is resident).  Returns
-// false, and records the failure, if the other blocks do not arrive within the limit.
-__device__ bool grid_barrier(AdmitScratch* sc, unsigned nblocks) {
+// Bounded grid barrier (cooperative launch guarantees every block is resident).  The arrival
+// counter only grows within a launch (zeroed by the host with the header): barrier number k
+// completes when it reaches k * nblocks.  Returns false, and records the failure, if the
+// other blocks do not arrive within the limit.
+__device__ bool grid_barrier(AdmitScratch* sc, unsigned nblocks, unsigned& epoch) {
     __shared__ int s_ok;
     __syncthreads();
+    ++epoch;
     if (threadIdx.x == 0) {
-        volatile unsigned* gen = &sc->bar_gen;
-        const unsigned g = *gen;
+        const unsigned target = epoch * nblocks;
         __threadfence();
+        atomicAdd(&sc->bar_count, 1u);
+        volatile unsigned* cnt = &sc->bar_count;
         int ok = 1;
-        if (atomicAdd(&sc->bar_count, 1u) == nblocks - 1) {
-            sc->bar_count = 0;
-            __threadfence();
-            atomicAdd(&sc->bar_gen, 1u);
-        } else {
-            long long it = 0;
-            while (*gen == g) {
-                if (++it > (1ll << 24) || *reinterpret_cast<volatile int*>(&sc->err)) {
-                    atomicExch(&sc->err, 1);
-                    ok = 0;
-                    break;
-                }
-                __nanosleep(32);
+        long long it = 0;
+        while (*cnt < target) {
+            if (++it > (1ll << 24) || *reinterpret_cast<volatile int*>(&sc->err)) {
+                atomicExch(&sc->err, 1);
+                ok = 0;
+                break;
             }
+            if (it > 256) __nanosleep(32);
         }
         __threadfence();
         s_ok = ok;
@@ -205,29 +217,73 @@ __device__ bool grid_barrier(AdmitScratch* sc, unsigned nblocks) {
     return s_ok != 0;
 }
 
-__global__ void __launch_bounds__(256) admit_persistent_kernel(AdmitArgs a, AdmitScratch* sc, AdmitPlanDigits dg) {
-    __shared__ unsigned long long s_hist[256];
-    __shared__ long long s_inc[256];
-    __shared__ long long s_red[8];
+__device__ __forceinline__ long long block_sum_ll(long long v, long long* s_red) {
+    v = warp_sum_ll(v);
+    if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = v;
+    __syncthreads();
+    long long t = 0;
+    if (threadIdx.x == 0)
+        for (int k = 0; k < kAdmitThreads / 32; ++k) t += s_red[k];
+    __syncthreads();
+    return t;
+}
+
+// KC > 0: each thread keeps its (at most KC) entries' keys and codes in registers for all
+// passes; KC == 0: entries are re-read from memory in every pass (inputs beyond KC per thread).
+template <int KC>
+__global__ void __launch_bounds__(kAdmitThreads, 1)
+    admit_persistent_kernel(AdmitArgs a, AdmitScratch* sc, AdmitPlanDigits dg) {
+    __shared__ unsigned long long s_k[kBins];
+    __shared__ unsigned int s_c[5][kBins];             // candidates per (weight class, digit)
+    __shared__ unsigned long long s_before;
+    __shared__ long long s_red[kAdmitThreads / 32];
     __shared__ AdmitHeader st;                         // identical in every block
     __shared__ int s_found;
     const unsigned nblocks = gridDim.x;
     const int tid = threadIdx.x;
+    const int64_t stride = (int64_t)nblocks * kAdmitThreads;
+    const unsigned long long idx_mask = dg.idx_bits >= 64 ? ~0ull : ((1ull << dg.idx_bits) - 1ull);
     bool ok = true;
+    unsigned epoch = 0;                                // grid barriers passed
 
-    // predicted bytes of the input codes
-    long long acc = 0;
-    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + tid; i < a.n; i += (int64_t)nblocks * blockDim.x)
-        acc += cost_of(a, a.codes[i]);
-    acc = warp_sum_ll(acc);
-    if ((tid & 31) == 0) s_red[tid >> 5] = acc;
-    __syncthreads();
-    if (tid == 0) {
-        long long t = 0;
-        for (int k = 0; k < 8; ++k) t += s_red[k];
-        if (t) atomicAdd((unsigned long long*)&sc->sums[0], (unsigned long long)t);
+    // zero this launch's histograms (ordered before their first use by the barrier below)
+    {
+        unsigned long long* k = &sc->hist_k[0][0];
+        unsigned int* c = &sc->hist_c[0][0][0];
+        for (int64_t i = blockIdx.x * (int64_t)kAdmitThreads + tid; i < 2 * kAdmitMaxPasses * kBins; i += stride) {
+            k[i] = 0;
+#pragma unroll
+            for (int q = 0; q < 5; ++q) c[q * 2 * kAdmitMaxPasses * kBins + i] = 0;
+        }
     }
-    ok = grid_barrier(sc, nblocks);
+    // predicted bytes of the input codes (and the register cache of keys and codes)
+    constexpr int KR = KC > 0 ? KC : 1;
+    unsigned long long ck[KR];
+    int cb[KR];                                        // base code (low byte) | 0x100 if a candidate
+    const int64_t gtid = blockIdx.x * (int64_t)kAdmitThreads + tid;
+    long long acc = 0;
+    if (KC > 0) {
+#pragma unroll
+        for (int r = 0; r < KR; ++r) {
+            const int64_t i = gtid + r * stride;
+            ck[r] = 0;
+            cb[r] = 0;
+            if (i < a.n) {
+                const int base = a.codes[i];
+                acc += cost_of(a, base);
+                cb[r] = (base & 0xFF);
+                if (eligible(a, i)) {
+                    ck[r] = entry_key(a, i, dg.idx_bits);
+                    cb[r] |= 0x100;
+                }
+            }
+        }
+    } else {
+        for (int64_t i = gtid; i < a.n; i += stride) acc += cost_of(a, a.codes[i]);
+    }
+    acc = block_sum_ll(acc, s_red);
+    if (tid == 0 && acc) atomicAdd((unsigned long long*)&sc->sums[0], (unsigned long long)acc);
+    ok = grid_barrier(sc, nblocks, epoch);
     if (tid == 0) {
         const long long p0 = (long long)__ldcg((const unsigned long long*)&sc->sums[0]);
         memset(&st, 0, sizeof(st));
@@ -242,59 +298,122 @@ __global__ void __launch_bounds__(256) admit_persistent_kernel(AdmitArgs a, Admi
     for (int phase = 0; phase < 2 && ok; ++phase) {
         if (phase == 0 && !st.a_active) continue;
         if (phase == 1 && !st.b_active) break;
+        hist_id = phase * kAdmitMaxPasses;
         for (int pass = 0; pass < dg.n && ok; ++pass, ++hist_id) {
             if (phase == 0 ? st.a_done : st.b_done) break;
-            const int shift = dg.shift[pass];
-            s_hist[tid] = 0;
+            const int lo = dg.lo[pass];
+            const unsigned long long dmask = (1ull << dg.width[pass]) - 1ull;
+            s_k[tid] = 0;
+#pragma unroll
+            for (int q = 0; q < 5; ++q) s_c[q][tid] = 0;
             __syncthreads();
             const unsigned long long prefix = st.prefix, pmask = st.pmask;
-            for (int64_t i = blockIdx.x * (int64_t)blockDim.x + tid; i < a.n; i += (int64_t)nblocks * blockDim.x) {
-                if (!eligible(a, i)) continue;
-                const unsigned long long key = entry_key(a, i);
-                if ((key & pmask) != prefix) continue;
-                const int base = a.codes[i];
-                const long long w = phase == 0 ? ((base >= 0 && base <= 4) ? a.wA[base] : 0)
-                                               : cost_of(a, code_after_a(st, base, key));
-                if (w) atomicAdd(&s_hist[(key >> shift) & 0xFF], (unsigned long long)w);
+            // a candidate's weight depends only on its weight class: the base code in the
+            // downgrade phase (ladder saving wA), the code after it in the eviction phase
+            // (entry cost), so the pass counts candidates per (class, digit).  Lanes with the
+            // same (class, digit) are combined and one of them adds to the shared count.
+            auto add = [&](bool cand, unsigned long long key, int base) {
+                int cls = -1;
+                if (cand && (key & pmask) == prefix) {
+                    cls = phase == 0 ? base : code_after_a(st, base, key);
+                    if (cls < 0 || cls > 4 || (phase == 0 ? a.wA[cls] : a.cost[cls]) == 0) cls = -1;
+                }
+                const unsigned active = __ballot_sync(0xffffffffu, cls >= 0);
+                if (cls < 0) return;
+                const int d = (int)((key >> lo) & dmask);
+                const unsigned grp = __match_any_sync(active, d * 8 + cls);
+                if ((threadIdx.x & 31) == __ffs(grp) - 1) {
+                    atomicAdd(&s_c[cls][d], (unsigned)__popc(grp));
+                    // a bin's key is read only when it ends up with ONE candidate in the whole
+                    // grid, and then this is the only write to it
+                    s_k[d] = key;
+                }
+            };
+            if (KC > 0) {
+#pragma unroll
+                for (int r = 0; r < KR; ++r) add((cb[r] & 0x100) != 0, ck[r], (int)(int8_t)(cb[r] & 0xFF));
+            } else {
+                // warp-uniform trip count: rounds start at the warp's first entry
+                const int64_t w0 = gtid - (tid & 31);
+                for (int64_t i0 = w0; i0 < a.n; i0 += stride) {
+                    const int64_t i = i0 + (tid & 31);
+                    const bool cand = i < a.n && eligible(a, i);
+                    add(cand, cand ? entry_key(a, i, dg.idx_bits) : 0ull, cand ? (int)a.codes[i] : 0);
+                }
             }
             __syncthreads();
-            if (s_hist[tid]) atomicAdd(&sc->hist[hist_id][tid], s_hist[tid]);
-            ok = grid_barrier(sc, nblocks);
+            {
+                unsigned tot = 0;
+#pragma unroll
+                for (int q = 0; q < 5; ++q) {
+                    const unsigned c = s_c[q][tid];
+                    if (c) atomicAdd(&sc->hist_c[hist_id][q][tid], c);
+                    tot += c;
+                }
+                if (tot == 1) sc->hist_k[hist_id][tid] = s_k[tid];   // see above
+            }
+            ok = grid_barrier(sc, nblocks, epoch);
             if (!ok) break;
-            // every block scans the same global histogram
-            s_inc[tid] = (long long)__ldcg(&sc->hist[hist_id][tid]);
-            if (tid == 0) s_found = 256;
-            __syncthreads();
-            for (int o = 1; o < 256; o <<= 1) {
-                const long long add = tid >= o ? s_inc[tid - o] : 0;
-                __syncthreads();
-                s_inc[tid] += add;
-                __syncthreads();
+            // every block scans the same global histogram: inclusive prefix of the weights
+            long long v = 0;
+            unsigned cnt_t = 0;
+#pragma unroll
+            for (int q = 0; q < 5; ++q) {
+                const unsigned c = __ldcg(&sc->hist_c[hist_id][q][tid]);
+                cnt_t += c;
+                v += (long long)c * (phase == 0 ? a.wA[q] : a.cost[q]);
             }
+            s_c[0][tid] = cnt_t;
+            s_k[tid] = __ldcg(&sc->hist_k[hist_id][tid]);
+            const int lane = tid & 31, wid = tid >> 5;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const long long y = __shfl_up_sync(0xffffffffu, v, o);
+                if (lane >= o) v += y;
+            }
+            if (lane == 31) s_red[wid] = v;
+            if (tid == 0) s_found = kBins;
+            __syncthreads();
+            if (wid == 0) {
+                long long t = s_red[lane];
+#pragma unroll
+                for (int o = 1; o < 32; o <<= 1) {
+                    const long long y = __shfl_up_sync(0xffffffffu, t, o);
+                    if (lane >= o) t += y;
+                }
+                s_red[lane] = t;
+            }
+            __syncthreads();
+            const long long cum = v + (wid > 0 ? s_red[wid - 1] : 0);
+            const long long total = s_red[kAdmitThreads / 32 - 1];
             const long long rem = st.rem;
-            if (s_inc[tid] >= rem) atomicMin(&s_found, tid);
+            if (cum >= rem) atomicMin(&s_found, tid);
+            __syncthreads();
+            const int d = s_found;
+            // the bin just below the boundary bin holds the weight before it
+            if (d < kBins && tid == (d > 0 ? d - 1 : 0)) s_before = d > 0 ? (unsigned long long)cum : 0ull;
             __syncthreads();
             if (tid == 0) {
-                const int d = s_found;
-                if (d == 256) {
+                if (d == kBins) {
                     // all candidate weight falls short: the whole candidate list is consumed
                     if (phase == 0) {
                         st.a_notenough = 1;
                         st.a_done = 1;
-                        st.predicted_a = st.predicted0 - s_inc[255];
+                        st.predicted_a = st.predicted0 - total;
                     } else {
                         st.b_notenough = 1;
                         st.b_done = 1;
                     }
                 } else {
-                    const long long before = d > 0 ? s_inc[d - 1] : 0;
+                    const long long before = (long long)s_before;
                     st.rem = rem - before;
-                    st.prefix |= (unsigned long long)d << shift;
-                    st.pmask |= 0xFFull << shift;
-                    if (pass == dg.n - 1) {
-                        const unsigned long long key = st.prefix;
+                    st.prefix |= (unsigned long long)d << lo;
+                    st.pmask |= dmask << lo;
+                    const unsigned cnt = s_c[0][d];
+                    if (cnt == 1 || pass == dg.n - 1) {
+                        const unsigned long long key = cnt == 1 ? s_k[d] : st.prefix;
                         if (phase == 0) {
-                            const int64_t idx = (int64_t)(key & 0xFFFFFFFFull);
+                            const int64_t idx = (int64_t)(key & idx_mask);
                             const int base = a.codes[idx];
                             const long long r = st.rem;
                             const long long s1 = base < 3 ? a.delta[base] : 0;
@@ -327,11 +446,9 @@ __global__ void __launch_bounds__(256) admit_persistent_kernel(AdmitArgs a, Admi
 
     // apply: final codes, predicted bytes, evictions
     long long pred = 0, ev = 0;
-    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + tid; i < a.n; i += (int64_t)nblocks * blockDim.x) {
-        const int base = a.codes[i];
+    auto apply = [&](int64_t i, int base, bool cand, unsigned long long key) {
         int code = base;
-        if (ok && eligible(a, i) && (st.a_active || st.b_active)) {
-            const unsigned long long key = entry_key(a, i);
+        if (ok && cand && (st.a_active || st.b_active)) {
             code = code_after_a(st, base, key);
             if (st.b_active && (st.b_notenough || key <= st.b_key)) {
                 if (code != 4) ++ev;
@@ -340,25 +457,26 @@ __global__ void __launch_bounds__(256) admit_persistent_kernel(AdmitArgs a, Admi
         }
         a.out[i] = (int8_t)code;
         pred += cost_of(a, code);
-    }
-    pred = warp_sum_ll(pred);
-    ev = warp_sum_ll(ev);
-    __shared__ long long s_e[8];
-    if ((tid & 31) == 0) {
-        s_red[tid >> 5] = pred;
-        s_e[tid >> 5] = ev;
-    }
-    __syncthreads();
-    if (tid == 0) {
-        long long tp = 0, te = 0;
-        for (int k = 0; k < 8; ++k) {
-            tp += s_red[k];
-            te += s_e[k];
+    };
+    if (KC > 0) {
+#pragma unroll
+        for (int r = 0; r < KR; ++r) {
+            const int64_t i = gtid + r * stride;
+            if (i < a.n) apply(i, (int)(int8_t)(cb[r] & 0xFF), (cb[r] & 0x100) != 0, ck[r]);
         }
-        if (tp) atomicAdd((unsigned long long*)&sc->sums[1], (unsigned long long)tp);
-        if (te) atomicAdd((unsigned long long*)&sc->sums[2], (unsigned long long)te);
+    } else {
+        for (int64_t i = gtid; i < a.n; i += stride) {
+            const bool cand = eligible(a, i);
+            apply(i, a.codes[i], cand, cand ? entry_key(a, i, dg.idx_bits) : 0ull);
+        }
     }
-    const bool fin = grid_barrier(sc, nblocks);
+    pred = block_sum_ll(pred, s_red);
+    ev = block_sum_ll(ev, s_red);
+    if (tid == 0) {
+        if (pred) atomicAdd((unsigned long long*)&sc->sums[1], (unsigned long long)pred);
+        if (ev) atomicAdd((unsigned long long*)&sc->sums[2], (unsigned long long)ev);
+    }
+    const bool fin = grid_barrier(sc, nblocks, epoch);
     if (blockIdx.x == 0 && tid == 0) {
         const bool good = ok && fin && __ldcg(&sc->err) == 0;
         a.result[0] = good ? (long long)__ldcg((const unsigned long long*)&sc->sums[1]) : -1;
@@ -366,21 +484,10 @@ __global__ void __launch_bounds__(256) admit_persistent_kernel(AdmitArgs a, Admi
     }
 }
 
+// One block per SM (cooperative launch: all resident), fewer for small inputs.
 static int admit_coop_blocks(int64_t n) {
-    static int cached[64] = {0};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    int per_sm = 0;
-    if (dev >= 0 && dev < 64 && cached[dev] > 0) {
-        per_sm = cached[dev];
-    } else {
-        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, admit_persistent_kernel, 256, 0) != cudaSuccess ||
-            per_sm <= 0)
-            per_sm = 1;
-        if (dev >= 0 && dev < 64) cached[dev] = per_sm;
-    }
-    const int64_t cap = (int64_t)sm_count() * (per_sm < 2 ? per_sm : 2);
-    const int64_t want = (n + 1023) / 1024;
+    const int64_t want = (n + kAdmitThreads - 1) / kAdmitThreads;
+    const int64_t cap = sm_count();
     return (int)(want < 1 ? 1 : (want < cap ? want : cap));
 }
 
@@ -457,21 +564,29 @@ int skv_admit_codes(const int8_t* codes_in, int8_t* codes_out, const float* impo
     }
     cudaStream_t s = as_stream(stream);
     AdmitScratch* sc = reinterpret_cast<AdmitScratch*>(scratch);
-    if (cudaMemsetAsync(sc, 0, sizeof(AdmitScratch), s) != cudaSuccess)
+    // the header (sums, barrier, error word); the kernel zeroes its own histograms
+    if (cudaMemsetAsync(sc, 0, kAdmitHeaderBytes, s) != cudaSuccess)
         return fail(SKV_ERR_CUDA, "admit_codes: memset failed");
-    // digit shifts: 4 score digits, then enough index digits to cover n-1
+    // 10-bit digits of the (32 + idx_bits)-bit key, from the top
     int idx_bits = 0;
-    while (idx_bits < 63 && ((int64_t)1 << idx_bits) < n) ++idx_bits;
-    const int idx_digits = (idx_bits + 7) / 8;
+    while (idx_bits < 32 && ((int64_t)1 << idx_bits) < n) ++idx_bits;
     AdmitPlanDigits dg;
+    dg.idx_bits = idx_bits;
     dg.n = 0;
-    for (int d = 3; d >= 0; --d) dg.shift[dg.n++] = 32 + 8 * d;
-    for (int d = idx_digits - 1; d >= 0; --d) dg.shift[dg.n++] = 8 * d;
+    for (int hi = 32 + idx_bits; hi > 0 && dg.n < kAdmitMaxPasses; hi -= kDigitBits) {
+        const int lo = hi > kDigitBits ? hi - kDigitBits : 0;
+        dg.lo[dg.n] = lo;
+        dg.width[dg.n] = hi - lo;
+        ++dg.n;
+    }
     if (budget_bytes < 0) dg.n = 0;
     const int blocks = admit_coop_blocks(n);
     void* args[] = {&a, &sc, &dg};
-    const cudaError_t e = cudaLaunchCooperativeKernel(reinterpret_cast<void*>(admit_persistent_kernel), dim3(blocks),
-                                                      dim3(256), args, 0, s);
+    constexpr int kCache = 8;
+    void* fn = n <= (int64_t)blocks * kAdmitThreads * kCache ? reinterpret_cast<void*>(admit_persistent_kernel<kCache>)
+                                                             : reinterpret_cast<void*>(admit_persistent_kernel<0>);
+    const cudaError_t e = cudaLaunchCooperativeKernel(fn, dim3(blocks),
+                                                      dim3(kAdmitThreads), args, 0, s);
     if (e != cudaSuccess) return fail(SKV_ERR_CUDA, "admit_codes: cooperative launch failed: %s", cudaGetErrorString(e));
     return check_launch("admit_persistent");
 }
