@@ -162,12 +162,6 @@ int skv_packed_attention(const void* q, int B, int H, int S_q, int D, const skv_
                          int S_kv, int int4_group, const int32_t* rows, const int32_t* counts, float scale,
                          void* scratch, size_t scratch_bytes, float* out, int32_t* error_flag, void* stream);
 
-/* The polynomial 2^x the attention softmax evaluates on the FMA pipe for part of its
- * elements (the rest use the hardware ex2), evaluated on the host with the same float
- * operations: relative error <= 7.5e-5 for x in [-125, 8]; x below -125 gives 2^-125.
- * Exported so that the bound can be checked without a GPU. */
-float skv_exp2_poly(float x);
-
 /* The two halves of skv_packed_attention, for callers that attend several query blocks over
  * one unchanged cache (stage once, attend many times) or time the halves separately.
  * skv_stage_kv_tiles: dequantises every stored row into the fp16 tiles in `scratch`.

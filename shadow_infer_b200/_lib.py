@@ -75,7 +75,6 @@ _SIGNATURES = {
                                 c_int, c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p]),
     "skv_head_index": (c_int, [c_void_p, c_int, c_int, c_void_p, c_void_p, c_void_p]),
     "skv_packed_attention_scratch_bytes": (c_size_t, [c_int, c_int, c_int, c_int]),
-    "skv_exp2_poly": (ctypes.c_float, [ctypes.c_float]),
     "skv_packed_attention": (c_int, [c_void_p, c_int, c_int, c_int, c_int, ctypes.POINTER(SkvBucket), c_int, c_int,
                                      c_void_p, c_void_p, ctypes.c_float, c_void_p, c_size_t, c_void_p, c_void_p,
                                      c_void_p]),

@@ -112,50 +112,6 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
     return d;
 }
 
-// 2^x on the FMA pipe, for part of the softmax elements so that the MUFU pipe (ex2) is not
-// the only one doing exponentials.  Range reduction x = n + f with n = rint(x) (the 1.5*2^23
-// rounding trick) and f in [-1/2, 1/2]; 2^f by a degree-3 polynomial whose coefficients are
-// the relative-error minimax fit on [-1/2, 1/2] (Remez exchange), max relative error 7.5e-5
-// -- below half an fp16 ulp (2^-12), the precision P is rounded to; 2^n is added to the
-// exponent field.  x is clamped at -125, so the result is never below 2^-125 (0 in fp16).
-constexpr float kExp2C0 = 0.99992805719375610f;
-constexpr float kExp2C1 = 0.69326096773147583f;
-constexpr float kExp2C2 = 0.24261112511157990f;
-constexpr float kExp2C3 = 0.05517166852951050f;
-constexpr float kRoundMagic = 12582912.0f;   // 1.5 * 2^23
-
-__host__ __device__ inline float exp2_poly(float x) {
-    x = fmaxf(x, -125.0f);
-    const float t = x + kRoundMagic;
-    const float f = x - (t - kRoundMagic);
-    const float q = fmaf(fmaf(fmaf(kExp2C3, f, kExp2C2), f, kExp2C1), f, kExp2C0);
-    uint32_t qb, tb;
-    memcpy(&qb, &q, 4);
-    memcpy(&tb, &t, 4);
-    qb += tb << 23;          // low mantissa bits of t hold n (two's complement)
-    float r;
-    memcpy(&r, &qb, 4);
-    return r;
-}
-
-// The same computation on two lanes of packed fp32 (fma.rn.f32x2 / add.rn.f32x2): identical
-// per-lane results, half the issue slots.
-__device__ __forceinline__ float2 exp2_poly2(float2 x) {
-    x.x = fmaxf(x.x, -125.0f);
-    x.y = fmaxf(x.y, -125.0f);
-    const float2 t = __fadd2_rn(x, make_float2(kRoundMagic, kRoundMagic));
-    const float2 n = __fadd2_rn(t, make_float2(-kRoundMagic, -kRoundMagic));
-    const float2 f = __ffma2_rn(n, make_float2(-1.0f, -1.0f), x);
-    float2 q = __ffma2_rn(make_float2(kExp2C3, kExp2C3), f, make_float2(kExp2C2, kExp2C2));
-    q = __ffma2_rn(q, f, make_float2(kExp2C1, kExp2C1));
-    q = __ffma2_rn(q, f, make_float2(kExp2C0, kExp2C0));
-    return make_float2(__uint_as_float(__float_as_uint(q.x) + (__float_as_uint(t.x) << 23)),
-                       __uint_as_float(__float_as_uint(q.y) + (__float_as_uint(t.y) << 23)));
-}
-
-// Of every 8 consecutive column pairs of a score row, this many take exp2_poly2, the rest ex2.
-constexpr int kPolyPairs = 3;
-
 __device__ __forceinline__ uint32_t half2_bits(__half2 h) {
     uint32_t u;
     memcpy(&u, &h, 4);
@@ -223,9 +179,9 @@ __device__ __forceinline__ uint4 f32x8_bits_to_half(const uint4& a, const uint4&
 // converted, so each lane keeps several memory requests in flight.
 template <int NA>
 struct RawRow {
-    uint4 k[NA][2], v[NA][2];   // fp32 uses both halves, fp16 one, int8 8 bytes, int4 4 bytes
+    uint4 k[NA], v[NA];         // fp16 (fp32 rows are converted on load), int8 8 bytes, int4 4 bytes
     float sk[NA], sv[NA];
-    int code;                   // 0..3, or -1 for a padding row
+    int code;                   // 1..3 (fp32 rows arrive as 1), or -1 for a padding row
 };
 
 template <int D>
@@ -239,34 +195,34 @@ __device__ __forceinline__ void load_raw_row(const AttnParams& p, int b, int32_t
     for (int a = 0; a < NA; ++a) {
         const int d0 = a * 64 + l8 * 8;
         if (r.code == 0) {
+            // rare: converted at once (RNE), which keeps the raw buffer at 16 bytes per chunk
             const uint4* pk = reinterpret_cast<const uint4*>(reinterpret_cast<const float*>(bb.k) + row * D + d0);
             const uint4* pv = reinterpret_cast<const uint4*>(reinterpret_cast<const float*>(bb.v) + row * D + d0);
-            r.k[a][0] = __ldg(pk);
-            r.k[a][1] = __ldg(pk + 1);
-            r.v[a][0] = __ldg(pv);
-            r.v[a][1] = __ldg(pv + 1);
+            r.k[a] = f32x8_bits_to_half(__ldg(pk), __ldg(pk + 1));
+            r.v[a] = f32x8_bits_to_half(__ldg(pv), __ldg(pv + 1));
         } else if (r.code == 1) {
-            r.k[a][0] = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const __half*>(bb.k) + row * D + d0));
-            r.v[a][0] = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const __half*>(bb.v) + row * D + d0));
+            r.k[a] = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const __half*>(bb.k) + row * D + d0));
+            r.v[a] = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const __half*>(bb.v) + row * D + d0));
         } else if (r.code == 2) {
             const uint2 wk = __ldg(reinterpret_cast<const uint2*>(reinterpret_cast<const int8_t*>(bb.k) + row * D + d0));
             const uint2 wv = __ldg(reinterpret_cast<const uint2*>(reinterpret_cast<const int8_t*>(bb.v) + row * D + d0));
-            r.k[a][0] = make_uint4(wk.x, wk.y, 0, 0);
-            r.v[a][0] = make_uint4(wv.x, wv.y, 0, 0);
+            r.k[a] = make_uint4(wk.x, wk.y, 0, 0);
+            r.v[a] = make_uint4(wv.x, wv.y, 0, 0);
             if (a == 0) {
                 r.sk[0] = __ldg(bb.scale_k + row);
                 r.sv[0] = __ldg(bb.scale_v + row);
             }
         } else {
             const int64_t off = (int64_t)slot_pos(e) * ((int64_t)p.B * D / 2) + (int64_t)b * (D / 2) + d0 / 2;
-            r.k[a][0].x = __ldg(reinterpret_cast<const uint32_t*>(reinterpret_cast<const uint8_t*>(bb.k) + off));
-            r.v[a][0].x = __ldg(reinterpret_cast<const uint32_t*>(reinterpret_cast<const uint8_t*>(bb.v) + off));
+            r.k[a].x = __ldg(reinterpret_cast<const uint32_t*>(reinterpret_cast<const uint8_t*>(bb.k) + off));
+            r.v[a].x = __ldg(reinterpret_cast<const uint32_t*>(reinterpret_cast<const uint8_t*>(bb.v) + off));
             const int NG = D / p.G;
             const int g = d0 / p.G;
             r.sk[a] = __ldg(bb.scale_k + row * NG + g);
             r.sv[a] = __ldg(bb.scale_v + row * NG + g);
         }
     }
+    if (r.code == 0) r.code = 1;
 }
 
 // Converts one lane's share of a K and a V row to fp16 and stores it, 128B-swizzled, at row
@@ -277,18 +233,15 @@ __device__ __forceinline__ void store_row(const RawRow<D / 64>& raw, int r, int 
 #pragma unroll
     for (int a = 0; a < NA; ++a) {
         uint4 hk = make_uint4(0, 0, 0, 0), hv = make_uint4(0, 0, 0, 0);
-        if (raw.code == 0) {
-            hk = f32x8_bits_to_half(raw.k[a][0], raw.k[a][1]);
-            hv = f32x8_bits_to_half(raw.v[a][0], raw.v[a][1]);
-        } else if (raw.code == 1) {
-            hk = raw.k[a][0];
-            hv = raw.v[a][0];
+        if (raw.code == 1) {
+            hk = raw.k[a];
+            hv = raw.v[a];
         } else if (raw.code == 2) {
-            hk = int8x8_scaled_to_half(raw.k[a][0].x, raw.k[a][0].y, raw.sk[0]);
-            hv = int8x8_scaled_to_half(raw.v[a][0].x, raw.v[a][0].y, raw.sv[0]);
+            hk = int8x8_scaled_to_half(raw.k[a].x, raw.k[a].y, raw.sk[0]);
+            hv = int8x8_scaled_to_half(raw.v[a].x, raw.v[a].y, raw.sv[0]);
         } else if (raw.code == 3) {
-            hk = int4x8_to_half(raw.k[a][0].x, raw.sk[a]);
-            hv = int4x8_to_half(raw.v[a][0].x, raw.sv[a]);
+            hk = int4x8_to_half(raw.k[a].x, raw.sk[a]);
+            hv = int4x8_to_half(raw.v[a].x, raw.sv[a]);
         }
         *reinterpret_cast<uint4*>(ktile + a * kBN * 128 + sw128_offset(r, l8)) = hk;
         *reinterpret_cast<uint4*>(vtile + a * kBN * 128 + sw128_offset(r, l8)) = hv;
@@ -300,7 +253,7 @@ __device__ __forceinline__ void store_row(const RawRow<D / 64>& raw, int r, int 
 // The row-list entries are fetched together with the head's counts (entries past the stored
 // rows are discarded afterwards), so a CTA waits for two memory round trips, not three.
 template <int D>
-__global__ void __launch_bounds__(kStageThreads, 2) stage_tiles_kernel(AttnParams p) {
+__global__ void __launch_bounds__(kStageThreads, 3) stage_tiles_kernel(AttnParams p) {
     constexpr int NA = D / 64;
     constexpr int kRowsPerPass = kStageThreads / 8;
     constexpr int kPasses = kBN / kRowsPerPass;
@@ -367,6 +320,13 @@ struct Schedule {
         return true;
     }
 };
+
+// Output store that the compiler does not treat as a memory clobber: the epilogue writes `out`
+// (or this CTA's partial slot) and reads only another CTA's partial slot, which never overlap,
+// so the partial loads may be scheduled ahead of these stores.
+__device__ __forceinline__ void st_global_f2(float* ptr, float2 v) {
+    asm volatile("st.global.v2.f32 [%0], {%1, %2};" ::"l"(ptr), "f"(v.x), "f"(v.y));
+}
 
 // Bounded wait (wall time) until `*flag` reaches `target` (acquire).
 __device__ __forceinline__ bool wait_flag(const int* flag, int target, int* err, int code,
@@ -541,8 +501,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                         const int col = c * 32 + i;
                         const float2 x = __ffma2_rn(
                             make_float2(__uint_as_float(sc[col]), __uint_as_float(sc[col + 1])), sl2x2, negm2);
-                        const float2 e =
-                            ((col >> 1) & 7) < kPolyPairs ? exp2_poly2(x) : make_float2(ex2(x.x), ex2(x.y));
+                        const float2 e = make_float2(ex2(x.x), ex2(x.y));
                         if ((col >> 1) & 1)
                             acc1 = __fadd2_rn(acc1, e);
                         else
@@ -612,33 +571,44 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                 const int rA = hf * 16 + (lane >> 2), rB = rA + 8;
                 const float faA = __shfl_sync(0xffffffffu, fa, rA), faB = __shfl_sync(0xffffffffu, fa, rB);
                 const float fbA = __shfl_sync(0xffffffffu, fb, rA), fbB = __shfl_sync(0xffffffffu, fb, rB);
+                // all of this half's TMEM columns first (one wait), then the stores
+                uint32_t o[D / 32][16];
+#pragma unroll
+                for (int c = 0; c < D / 32; ++c)
+                    tmem_ld16x256b_x4(tO + c * 32 + ((uint32_t)(hf * 16) << 16), o[c]);
+                tmem_wait_ld();
+                if (hf == 1) {
+                    // O_t has been read out: the next segment's first P_t V may overwrite it
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&o_empty[t]);
+                }
 #pragma unroll
                 for (int c = 0; c < D / 32; ++c) {
-                    uint32_t o[16];
-                    tmem_ld16x256b_x4(tO + c * 32 + ((uint32_t)(hf * 16) << 16), o);
-                    tmem_wait_ld();
 #pragma unroll
                     for (int k = 0; k < 4; ++k) {
                         const int col = c * 32 + 8 * k + 2 * (lane & 3);
-                        float2 a = make_float2(__uint_as_float(o[4 * k]) * faA, __uint_as_float(o[4 * k + 1]) * faA);
-                        float2 bq = make_float2(__uint_as_float(o[4 * k + 2]) * faB, __uint_as_float(o[4 * k + 3]) * faB);
+                        float2 va = make_float2(__uint_as_float(o[c][4 * k]) * faA, __uint_as_float(o[c][4 * k + 1]) * faA);
+                        float2 vb = make_float2(__uint_as_float(o[c][4 * k + 2]) * faB, __uint_as_float(o[c][4 * k + 3]) * faB);
                         if (split_head) {
-                            const float2 wa = __ldcg(reinterpret_cast<const float2*>(src + (int64_t)rA * D + col));
-                            const float2 wb = __ldcg(reinterpret_cast<const float2*>(src + (int64_t)rB * D + col));
-                            a.x = fmaf(wa.x, fbA, a.x);
-                            a.y = fmaf(wa.y, fbA, a.y);
-                            bq.x = fmaf(wb.x, fbB, bq.x);
-                            bq.y = fmaf(wb.y, fbB, bq.y);
+                            const float2 pa = __ldcg(reinterpret_cast<const float2*>(src + (int64_t)rA * D + col));
+                            const float2 pb = __ldcg(reinterpret_cast<const float2*>(src + (int64_t)rB * D + col));
+                            va.x = fmaf(pa.x, fbA, va.x);
+                            va.y = fmaf(pa.y, fbA, va.y);
+                            vb.x = fmaf(pb.x, fbB, vb.x);
+                            vb.y = fmaf(pb.y, fbB, vb.y);
                         }
-                        if (rA < nrows) *reinterpret_cast<float2*>(dst + (int64_t)rA * D + col) = a;
-                        if (rB < nrows) *reinterpret_cast<float2*>(dst + (int64_t)rB * D + col) = bq;
+                        if (split_tail) {
+                            // published to another CTA behind a fence: ordinary stores
+                            *reinterpret_cast<float2*>(dst + (int64_t)rA * D + col) = va;
+                            *reinterpret_cast<float2*>(dst + (int64_t)rB * D + col) = vb;
+                        } else {
+                            if (rA < nrows) st_global_f2(dst + (int64_t)rA * D + col, va);
+                            if (rB < nrows) st_global_f2(dst + (int64_t)rB * D + col, vb);
+                        }
                     }
                 }
             }
-            // O_t has been read out: the next segment's first P_t V may overwrite it
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&o_empty[t]);
             if (split_tail) {
                 p.part_ml[(size_t)blockIdx.x * kUnitRows + rt + lane] = make_float2(m_ref, l);
                 __threadfence();
@@ -905,8 +875,6 @@ int skv_head_index(const int32_t* slot, int S, int H, int32_t* rows, int32_t* co
     head_index_kernel<<<H, kHiThreads, 0, as_stream(stream)>>>(slot, S, H, rows, counts);
     return check_launch("head_index");
 }
-
-float skv_exp2_poly(float x) { return exp2_poly(x); }
 
 size_t skv_packed_attention_scratch_bytes(int B, int H, int S_kv, int D) {
     if (B <= 0 || H <= 0 || S_kv <= 0 || (D != 64 && D != 128)) return 0;

@@ -53,6 +53,20 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
                  : "memory");
 }
 
+// try_wait with a suspend-time hint: the thread sleeps in hardware until the phase completes
+// or `hint_ns` passes, instead of spinning and taking issue slots from its SMSP neighbours.
+__device__ __forceinline__ bool mbar_try_wait_hint(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.b32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
+
 // Bounded wait: gives up after `limit` polls (each poll may suspend briefly in hardware),
 // records `code` in *err and returns false.  Never spins forever.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code,
@@ -89,14 +103,13 @@ __device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity, i
                                                uint64_t limit_ns = 1000000000ull) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
-    for (uint32_t i = 1;; ++i) {
-        if (mbar_try_wait(bar, parity)) return true;
-        if ((i & 255) == 0) {
-            if (*reinterpret_cast<volatile int*>(err) != 0) return false;
-            if (globaltimer_ns() - t0 > limit_ns) {
-                atomicCAS(err, 0, code);
-                return false;
-            }
+    for (;;) {
+        // each try suspends for at most 20 us; the wall-clock limit is checked after each
+        if (mbar_try_wait_hint(bar, parity, 20000u)) return true;
+        if (*reinterpret_cast<volatile int*>(err) != 0) return false;
+        if (globaltimer_ns() - t0 > limit_ns) {
+            atomicCAS(err, 0, code);
+            return false;
         }
     }
 }
