@@ -566,11 +566,46 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             // O is read in the 16x256b shape: four threads hold 32 contiguous bytes of a row, so
             // each store instruction writes whole sectors without a shared-memory transpose
             // (shared memory bandwidth stays with the tensor cores)
-#pragma unroll
+#pragma unroll 1
             for (int hf = 0; hf < 2; ++hf) {
                 const int rA = hf * 16 + (lane >> 2), rB = rA + 8;
                 const float faA = __shfl_sync(0xffffffffu, fa, rA), faB = __shfl_sync(0xffffffffu, fa, rB);
                 const float fbA = __shfl_sync(0xffffffffu, fb, rA), fbB = __shfl_sync(0xffffffffu, fb, rB);
+                if (split_head) {
+                    // a unit cut between two CTAs, merged here (once per CTA at most): all of this
+                    // half's partial values first, so their loads overlap, then O chunk by chunk
+                    float2 pa[D / 32][4], pb[D / 32][4];
+#pragma unroll
+                    for (int c = 0; c < D / 32; ++c)
+#pragma unroll
+                        for (int k = 0; k < 4; ++k) {
+                            const int col = c * 32 + 8 * k + 2 * (lane & 3);
+                            pa[c][k] = __ldcg(reinterpret_cast<const float2*>(src + (int64_t)rA * D + col));
+                            pb[c][k] = __ldcg(reinterpret_cast<const float2*>(src + (int64_t)rB * D + col));
+                        }
+#pragma unroll
+                    for (int c = 0; c < D / 32; ++c) {
+                        uint32_t o[16];
+                        tmem_ld16x256b_x4(tO + c * 32 + ((uint32_t)(hf * 16) << 16), o);
+                        tmem_wait_ld();
+                        if (hf == 1 && c == D / 32 - 1) {
+                            tc_fence_before();
+                            __syncwarp();
+                            if (lane == 0) mbar_arrive(&o_empty[t]);
+                        }
+#pragma unroll
+                        for (int k = 0; k < 4; ++k) {
+                            const int col = c * 32 + 8 * k + 2 * (lane & 3);
+                            const float2 va = make_float2(fmaf(pa[c][k].x, fbA, __uint_as_float(o[4 * k]) * faA),
+                                                          fmaf(pa[c][k].y, fbA, __uint_as_float(o[4 * k + 1]) * faA));
+                            const float2 vb = make_float2(fmaf(pb[c][k].x, fbB, __uint_as_float(o[4 * k + 2]) * faB),
+                                                          fmaf(pb[c][k].y, fbB, __uint_as_float(o[4 * k + 3]) * faB));
+                            if (rA < nrows) st_global_f2(dst + (int64_t)rA * D + col, va);
+                            if (rB < nrows) st_global_f2(dst + (int64_t)rB * D + col, vb);
+                        }
+                    }
+                    continue;
+                }
                 // all of this half's TMEM columns first (one wait), then the stores
                 uint32_t o[D / 32][16];
 #pragma unroll
@@ -588,16 +623,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 #pragma unroll
                     for (int k = 0; k < 4; ++k) {
                         const int col = c * 32 + 8 * k + 2 * (lane & 3);
-                        float2 va = make_float2(__uint_as_float(o[c][4 * k]) * faA, __uint_as_float(o[c][4 * k + 1]) * faA);
-                        float2 vb = make_float2(__uint_as_float(o[c][4 * k + 2]) * faB, __uint_as_float(o[c][4 * k + 3]) * faB);
-                        if (split_head) {
-                            const float2 pa = __ldcg(reinterpret_cast<const float2*>(src + (int64_t)rA * D + col));
-                            const float2 pb = __ldcg(reinterpret_cast<const float2*>(src + (int64_t)rB * D + col));
-                            va.x = fmaf(pa.x, fbA, va.x);
-                            va.y = fmaf(pa.y, fbA, va.y);
-                            vb.x = fmaf(pb.x, fbB, vb.x);
-                            vb.y = fmaf(pb.y, fbB, vb.y);
-                        }
+                        const float2 va = make_float2(__uint_as_float(o[c][4 * k]) * faA, __uint_as_float(o[c][4 * k + 1]) * faA);
+                        const float2 vb = make_float2(__uint_as_float(o[c][4 * k + 2]) * faB, __uint_as_float(o[c][4 * k + 3]) * faB);
                         if (split_tail) {
                             // published to another CTA behind a fence: ordinary stores
                             *reinterpret_cast<float2*>(dst + (int64_t)rA * D + col) = va;
