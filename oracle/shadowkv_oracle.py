@@ -25,7 +25,7 @@ from __future__ import annotations
 
 import hashlib
 import struct
-from typing import Any, Dict, List, Optional, Tuple
+from typing import Any, Dict, List, Optional, Sequence, Tuple
 
 import numpy as np
 
@@ -584,3 +584,70 @@ def packed_attention(q: np.ndarray, cache: OraclePackedKV, scale: Optional[float
     """Oracle for attention read from the packed cache: ``unpack()`` then dense attention."""
     k, v = unpack(cache)
     return attention(q, k, v, scale)
+
+
+# --------------------------------------------------------------------------------------
+# cross-layer budget enforcement  (shadowinfer/shadowkv/kv_cache_manager.py:129-200, 301-322)
+# --------------------------------------------------------------------------------------
+def manager_usage(layers: Sequence[Dict[str, Any]]) -> int:
+    """``KVCacheManager.get_memory_usage`` (kv_cache_manager.py:301-322) for layers that hold a
+    cache entry (``counted``): packed resident bytes plus the retained dense shadow bytes."""
+    total = 0
+    for L in layers:
+        if L.get("counted", True):
+            total += L["cache"].resident_bytes() + int(L.get("dense_bytes", 0))
+    return total
+
+
+def enforce_global_budget(layers: Sequence[Dict[str, Any]], budget_bytes: Optional[int], sink_tokens: int = 0) -> int:
+    """Cross-layer eviction by ascending importance (kv_cache_manager.py:129-200).
+
+    ``layers`` in the manager's importance-matrix insertion order, each a dict with
+    ``cache`` (OraclePackedKV, evicted in place), ``importance`` (float [S, H]), ``counted``
+    (the layer holds a cache entry, so its bytes count in the usage), ``candidate`` (it has
+    an importance matrix; default True) and ``dense_bytes`` (retained dense shadow, released
+    first under pressure).  Returns the number of candidates processed, as the reference does.
+    """
+    if budget_bytes is None or budget_bytes <= 0 or not layers:
+        return 0
+    target = int(budget_bytes * 0.9)
+    if manager_usage(layers) > target:                 # _release_dense_shadows (:202-222)
+        for L in layers:
+            if L.get("counted", True):
+                L["dense_bytes"] = 0
+    if manager_usage(layers) <= target:
+        return 0
+    # candidates in (layer order, token, head) order, stably sorted by importance (:152-165)
+    values, owner, token, head = [], [], [], []
+    for li, L in enumerate(layers):
+        if not L.get("candidate", True):
+            continue
+        imp = np.asarray(L["importance"], dtype=np.float32)
+        S, H = imp.shape
+        for t in range(sink_tokens, S):
+            values.append(imp[t])
+            owner.append(np.full(H, li))
+            token.append(np.full(H, t))
+            head.append(np.arange(H))
+    if not values:
+        return 0
+    values = np.concatenate(values)
+    owner, token, head = np.concatenate(owner), np.concatenate(token), np.concatenate(head)
+    order = np.argsort(values, kind="stable")
+    n = len(order)
+    idx = 0
+    evicted_total = 0
+    while manager_usage(layers) > target and idx < n:   # batched eviction loop (:167-194)
+        usage = manager_usage(layers)
+        remaining = usage - target
+        avg_entry = max(1, usage // max(1, n))
+        batch = max(1, min(n - idx, remaining // avg_entry + 1))
+        chunk = order[idx: idx + batch]
+        idx += batch
+        for li, L in enumerate(layers):
+            sel = chunk[owner[chunk] == li]
+            if len(sel) == 0:
+                continue
+            evict(L["cache"], set(zip(token[sel].tolist(), head[sel].tolist())))
+            evicted_total += len(sel)
+    return evicted_total

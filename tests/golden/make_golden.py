@@ -253,6 +253,49 @@ def attention_case(R, case, gen, B, H, S, D):
     PINS["cases"][case] = {"kind": "attention", "B": B, "H": H, "S": S, "D": D}
 
 
+def global_budget_case(R, case, gen, B, H, S, D, layers, budget_frac, sink, *, probs=(0.2, 0.3, 0.25, 0.2, 0.05),
+                       group=16, dense=(), packed_only=(), no_importance=(), ties=False, budget_abs=None):
+    """KVCacheManager.enforce_global_budget over several packed layers (kv_cache_manager.py:129-200)."""
+    from shadowinfer.core.structs import KVCacheEntry
+    from shadowinfer.shadowkv.kv_cache_manager import KVCacheManager
+    mgr = KVCacheManager(num_layers=layers)
+    packs = []
+    for L in range(layers):
+        k, v = kv(gen, B, H, S, D)
+        codes = codes_of(gen, S, H, probs)
+        imp = torch.rand(S, H, generator=gen)
+        if ties:
+            imp = torch.round(imp * 4) / 4
+        imp[:sink] = 1.0
+        plan = R.plan.PrecisionPlan.from_codes(codes)
+        packed = R.pkc.PackedKVCache.pack(k, v, None, group_size=group, plan=plan)["packed_kv"]
+        if L in packed_only:
+            mgr.store_packed(L, packed)
+        else:
+            mgr.store(L, KVCacheEntry(k_tensor=k if L in dense else None, v_tensor=v if L in dense else None,
+                                      precision="mixed", packed_kv=packed))
+        if L not in no_importance:
+            mgr.set_importance_matrix(L, imp)
+        put(case, f"L{L}.k", k); put(case, f"L{L}.v", v); put(case, f"L{L}.codes", codes); put(case, f"L{L}.imp", imp)
+        packs.append(packed)
+    before = mgr.get_memory_usage()
+    budget = budget_abs if budget_abs is not None else int(before * budget_frac)
+    evicted = mgr.enforce_global_budget(budget, sink)
+    for L, packed in enumerate(packs):
+        remaining = np.zeros((S, H), dtype=np.uint8)
+        for d in packed.packed_data.values():
+            for t, h in d["indices"]:
+                remaining[t, h] = 1
+        put(case, f"L{L}.remaining", remaining)
+    PINS["cases"][case] = {
+        "kind": "global_budget", "B": B, "H": H, "S": S, "D": D, "group": group, "layers": layers,
+        "sink": sink, "budget": budget, "dense": list(dense), "packed_only": list(packed_only),
+        "no_importance": list(no_importance), "usage_before": before, "evicted": evicted,
+        "usage_after": mgr.get_memory_usage(),
+        "resident_after": [p.resident_bytes() for p in packs],
+    }
+
+
 def full_pins(R):
     """cfg1 / cfg2 pipelines at full size: digests only."""
     c1 = W.CONFIGS["cfg1"]
@@ -355,6 +398,13 @@ def main():
     sensitivity_case(R, "sensitivity", gen)
     attention_case(R, "attention_b1", gen, 1, 2, 64, 64)
     attention_case(R, "attention_b2_d128", gen, 2, 1, 80, 128)
+    global_budget_case(R, "gb_two_fp32_dense", gen, 1, 2, 16, 64, 2, 0.0, 2, probs=(1.0, 0, 0, 0, 0),
+                       dense=(0, 1), budget_abs=20000)
+    global_budget_case(R, "gb_mixed_ties", gen, 2, 3, 24, 64, 3, 0.55, 3, ties=True, packed_only=(2,))
+    global_budget_case(R, "gb_noncandidate_layer", gen, 1, 4, 20, 128, 3, 0.6, 2, no_importance=(1,), dense=(0,))
+    global_budget_case(R, "gb_floor", gen, 1, 2, 12, 64, 2, 0.02, 2)
+    global_budget_case(R, "gb_no_pressure", gen, 1, 2, 12, 64, 2, 2.0, 0)
+    global_budget_case(R, "gb_b2_group32", gen, 2, 2, 40, 128, 2, 0.4, 4, group=32, probs=(0.1, 0.3, 0.3, 0.25, 0.05))
     full_pins(R)
     np.savez_compressed(SMALL_NPZ, **ARR)
     with open(PINS_JSON, "w") as f:

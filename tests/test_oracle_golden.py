@@ -161,3 +161,35 @@ def test_full_cfg2_pins(golden_pins):
     assert O.evict(cache, emask) == pin["removed"]
     assert packed_summary(cache.packed_data, cache.memory_bytes()) == pin["after_evict"]
     assert cache.resident_bytes() == pin["resident_after_evict"]
+
+
+def _gb_layers(pin, arrays):
+    """Oracle layer list of a global-budget fixture (the manager's layer order)."""
+    layers = []
+    for L in range(pin["layers"]):
+        k, v = arrays[f"L{L}.k"], arrays[f"L{L}.v"]
+        cache = O.pack(k, v, O.plan_from_codes(arrays[f"L{L}.codes"]), pin["group"])
+        layers.append({
+            "cache": cache, "importance": arrays[f"L{L}.imp"],
+            "counted": L not in pin["packed_only"], "candidate": L not in pin["no_importance"],
+            "dense_bytes": (k.nbytes + v.nbytes) if L in pin["dense"] else 0,
+        })
+    return layers
+
+
+@pytest.mark.parametrize("case", _cases(_pins(), "global_budget"))
+def test_global_budget(case, golden_small):
+    """KVCacheManager.enforce_global_budget: processed count, usage and surviving entries."""
+    pin = _pins()["cases"][case]
+    a = case_arrays(golden_small, case)
+    layers = _gb_layers(pin, a)
+    assert O.manager_usage(layers) == pin["usage_before"]
+    assert O.enforce_global_budget(layers, pin["budget"], pin["sink"]) == pin["evicted"]
+    assert O.manager_usage(layers) == pin["usage_after"]
+    for L, layer in enumerate(layers):
+        present = np.zeros_like(a[f"L{L}.remaining"])
+        for d in layer["cache"].packed_data.values():
+            for t, h in d["indices"]:
+                present[t, h] = 1
+        np.testing.assert_array_equal(present, a[f"L{L}.remaining"])
+        assert layer["cache"].resident_bytes() == pin["resident_after"][L]
