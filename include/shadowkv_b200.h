@@ -172,6 +172,28 @@ int skv_attend_kv_tiles(const void* q, int B, int H, int S_q, int D, int S_kv, c
                         const int32_t* counts, float scale, const void* scratch, size_t scratch_bytes, float* out,
                         int32_t* error_flag, void* stream);
 
+/* ---- cross-layer budget: KVCacheManager.enforce_global_budget
+ * (shadowinfer/shadowkv/kv_cache_manager.py:129-200).  The reference sorts every non-sink
+ * (layer, token, head) by importance and evicts from the front in batches, re-reading usage
+ * after each batch; these three calls give the bytes freed by the first k candidates and the
+ * candidates themselves without a sort. */
+
+/* One layer's candidates, tokens sink..S_m-1 (token-major, then head) of an importance matrix
+ * float [S_m, H_m]: score[i] = importance, weight[i] = entry_cost[code] of the cache entry in
+ * slot int32 [S_c, H_c] (slot may be NULL; 0 when absent or outside the cache).  Writes
+ * (S_m - sink) * H_m values (nothing when sink >= S_m). */
+int skv_budget_candidates(const float* importance, int S_m, int H_m, const int32_t* slot, int S_c, int H_c,
+                          int sink_tokens, const int64_t* entry_cost /* host [4] */, float* score,
+                          int64_t* weight, void* stream);
+/* k-th smallest key (score, position) of n candidates (1 <= k <= n, n < 2^31) and the summed
+ * weight of the k smallest: result int64[2] (device) = {weight sum, key}; -1 on an internal
+ * timeout.  Ties in score keep list order, as the reference's stable sort does. */
+size_t skv_rank_select_scratch_bytes(int64_t n);
+int skv_rank_select(const float* score, const int64_t* weight, int64_t n, int64_t k, void* scratch,
+                    size_t scratch_bytes, int64_t* result, void* stream);
+/* mask[i] = 1 for the candidates at or below the key in result (from skv_rank_select). */
+int skv_mark_smallest(const float* score, int64_t n, const int64_t* result, uint8_t* mask, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

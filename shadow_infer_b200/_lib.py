@@ -82,6 +82,11 @@ _SIGNATURES = {
                                    c_void_p, c_size_t, c_void_p]),
     "skv_attend_kv_tiles": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_int, c_void_p, c_void_p, ctypes.c_float,
                                     c_void_p, c_size_t, c_void_p, c_void_p, c_void_p]),
+    "skv_budget_candidates": (c_int, [c_void_p, c_int, c_int, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p,
+                                      c_void_p, c_void_p]),
+    "skv_rank_select_scratch_bytes": (c_size_t, [c_int64]),
+    "skv_rank_select": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_size_t, c_void_p, c_void_p]),
+    "skv_mark_smallest": (c_int, [c_void_p, c_int64, c_void_p, c_void_p, c_void_p]),
     "skv_evict_scratch_bytes": (c_size_t, [c_int64]),
     "skv_evict_count": (c_int, [ctypes.POINTER(SkvBucket), c_void_p, c_int, c_int, c_void_p, c_void_p, c_size_t,
                                 c_void_p]),

@@ -124,13 +124,6 @@ struct AdmitArgs {
     long long delta[3];      // cost[c] - cost[c+1], c = 0..2
 };
 
-__device__ __forceinline__ uint32_t score_bits(float f) {
-    if (f != f) return 0xFFFFFFFFu;       // NaN sorts last
-    if (f == 0.0f) f = 0.0f;              // -0.0 ties with +0.0
-    const uint32_t u = __float_as_uint(f);
-    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-}
-
 __device__ __forceinline__ bool eligible(const AdmitArgs& a, int64_t i) {
     if (i / a.H < a.sink) return false;
     if (a.prot && a.prot[i]) return false;
@@ -187,34 +180,8 @@ struct AdmitPlanDigits {
     int idx_bits;
 };
 
-// Bounded grid barrier (cooperative launch guarantees every block is resident).  The arrival
-// counter only grows within a launch (zeroed by the host with the header): barrier number k
-// completes when it reaches k * nblocks.  Returns false, and records the failure, if the
-// other blocks do not arrive within the limit.
-__device__ bool grid_barrier(AdmitScratch* sc, unsigned nblocks, unsigned& epoch) {
-    __shared__ int s_ok;
-    __syncthreads();
-    ++epoch;
-    if (threadIdx.x == 0) {
-        const unsigned target = epoch * nblocks;
-        __threadfence();
-        atomicAdd(&sc->bar_count, 1u);
-        volatile unsigned* cnt = &sc->bar_count;
-        int ok = 1;
-        long long it = 0;
-        while (*cnt < target) {
-            if (++it > (1ll << 24) || *reinterpret_cast<volatile int*>(&sc->err)) {
-                atomicExch(&sc->err, 1);
-                ok = 0;
-                break;
-            }
-            if (it > 256) __nanosleep(32);
-        }
-        __threadfence();
-        s_ok = ok;
-    }
-    __syncthreads();
-    return s_ok != 0;
+__device__ __forceinline__ bool grid_barrier(AdmitScratch* sc, unsigned nblocks, unsigned& epoch) {
+    return grid_sync_bounded(&sc->bar_count, &sc->err, nblocks, epoch);
 }
 
 __device__ __forceinline__ long long block_sum_ll(long long v, long long* s_red) {

@@ -50,6 +50,45 @@ __device__ __forceinline__ float group_max(float x, int width) {
     return x;
 }
 
+// Order-preserving 32-bit image of a float score for radix selection: ascending images are
+// ascending scores (the order a stable float sort uses), -0.0 ties with +0.0, NaN sorts last.
+__device__ __forceinline__ uint32_t score_bits(float f) {
+    if (f != f) return 0xFFFFFFFFu;
+    if (f == 0.0f) f = 0.0f;
+    const uint32_t u = __float_as_uint(f);
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+// Bounded grid barrier for cooperative launches (every block resident).  `count` only grows
+// within a launch (zeroed before it): barrier number `epoch` completes when it reaches
+// epoch * nblocks.  Returns false, and records the failure in *err, if the other blocks do
+// not arrive within the limit or another block has failed.
+__device__ __forceinline__ bool grid_sync_bounded(unsigned* count, int* err, unsigned nblocks, unsigned& epoch) {
+    __shared__ int s_ok;
+    __syncthreads();
+    ++epoch;
+    if (threadIdx.x == 0) {
+        const unsigned target = epoch * nblocks;
+        __threadfence();
+        atomicAdd(count, 1u);
+        volatile unsigned* cnt = count;
+        int ok = 1;
+        long long it = 0;
+        while (*cnt < target) {
+            if (++it > (1ll << 24) || *reinterpret_cast<volatile int*>(err)) {
+                atomicExch(err, 1);
+                ok = 0;
+                break;
+            }
+            if (it > 256) __nanosleep(32);
+        }
+        __threadfence();
+        s_ok = ok;
+    }
+    __syncthreads();
+    return s_ok != 0;
+}
+
 __device__ __forceinline__ long long warp_sum_ll(long long x) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);

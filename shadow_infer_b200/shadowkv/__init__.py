@@ -1,5 +1,13 @@
 """ShadowKV packed-KV data plane on B200 (drop-in for ``shadowinfer.shadowkv``'s data plane)."""
 
+from .kv_cache_manager import (
+    EvictionPolicy,
+    ImportanceAgeEvictionPolicy,
+    KVCacheEntry,
+    KVCacheManager,
+    LeastImportantEvictionPolicy,
+    TokenHeadScore,
+)
 from .packed_attention import packed_attention
 from .packed_kv_cache import PackedKVCache
 from .precision_plan import (
@@ -16,5 +24,6 @@ from .rd_allocator import admit_budget, admit_codes, entry_bytes, kv_sensitivity
 __all__ = [
     "PackedKVCache", "PrecisionPlan", "map_to_codes", "codes_to_map", "PRECISION_ORDER", "PRECISION_CODES",
     "CODE_PRECISIONS", "EVICTED", "admit_codes", "admit_budget", "entry_bytes", "kv_sensitivity",
-    "predict_codes_bytes", "packed_attention",
+    "predict_codes_bytes", "packed_attention", "KVCacheManager", "KVCacheEntry", "TokenHeadScore",
+    "EvictionPolicy", "LeastImportantEvictionPolicy", "ImportanceAgeEvictionPolicy",
 ]
