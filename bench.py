@@ -23,7 +23,8 @@ kernel), timed with CUDA events around each launch in the timed region.
 The line also carries ``attention``: packed attention over one cfg3 layer
 (B=1, H=32, S=4096, D=128, codes 20/50/30 % fp16/int8/int4), heads sharded over
 the ranks with an NCCL all-gather of the outputs, as tokens/s of the 32-layer
-stack and as tensor-core roofline of the kernel.
+stack and as tensor-core roofline of the kernel; and ``global_budget``:
+KVCacheManager.enforce_global_budget over 8 packed layers of that shape.
 """
 
 from __future__ import annotations
@@ -51,7 +52,7 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
     ap.add_argument("--ref-heads", type=int, default=8, help="head slice timed by the CPU reference arm")
-    ap.add_argument("--no-attention", action="store_true", help="skip the packed-attention measurement")
+    ap.add_argument("--no-attention", action="store_true", help="skip the packed-attention and global-budget phases")
     return ap.parse_args()
 
 
@@ -326,6 +327,83 @@ def attention_phase(args, world, rank, dev, dist, lib, tensor_peak):
     return res
 
 
+# --------------------------------------------------------------------------- global budget
+def budget_phase(args, world, rank, dev, lib):
+    """KVCacheManager.enforce_global_budget over 8 packed layers of cfg3's shape.
+
+    Each step re-packs the 8 layers (outside the timed region), then times one
+    enforce_global_budget call (budget = 70 % of the usage, 4 sink tokens) with CUDA events:
+    candidate listing, the device selection for each batch the reference's loop visits, and
+    the in-place eviction of every layer.
+    """
+    import torch
+
+    from shadow_infer_b200 import workloads as W
+    from shadow_infer_b200.shadowkv import KVCacheEntry, KVCacheManager, PackedKVCache, PrecisionPlan
+    from shadow_infer_b200.shadowkv.shadowkv_agent import allocate_precision_codes
+
+    c = W.CONFIGS["cfg3"]
+    B, H, S, D, layers, sink = c["B"], c["H"], c["S"], c["D"], 8, 4
+    kvs, imps, plans = [], [], []
+    for L in range(layers):
+        k, v = W.kv_tensors(B, H, S, D, 1000 * rank + L)
+        imp = W.importance_map(S, H, 1000 * rank + L, c["fractions"]).to(dev)
+        kvs.append((k.to(dev), v.to(dev)))
+        imps.append(imp)
+        plans.append(PrecisionPlan.from_codes(allocate_precision_codes(imp, "balanced")))
+
+    def fresh():
+        mgr = KVCacheManager(num_layers=layers)
+        for L in range(layers):
+            cache = PackedKVCache.pack(kvs[L][0], kvs[L][1], None, c["group"], plan=plans[L])["packed_kv"]
+            mgr.store(L, KVCacheEntry(k_tensor=None, v_tensor=None, precision="mixed", packed_kv=cache))
+            mgr.set_importance_matrix(L, imps[L])
+        return mgr
+
+    steps = max(3, min(args.steps, 10))
+    n_cand = layers * (S - sink) * H
+    mgr = fresh()
+    budget = int(mgr.get_memory_usage() * 0.7)
+    for _ in range(2):
+        fresh().enforce_global_budget(budget, sink)
+    times, processed, launches = [], 0, 0
+    for _ in range(steps):
+        mgr = fresh()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        n0 = lib.skv_launch_count()
+        e0.record()
+        processed = mgr.enforce_global_budget(budget, sink)
+        e1.record()
+        torch.cuda.synchronize()
+        launches = lib.skv_launch_count() - n0
+        times.append(e0.elapsed_time(e1))
+    ms = statistics.median(times)
+    res = {
+        "metric": "enforce_global_budget candidates/s (8 layers, cfg3 shape)",
+        "value": n_cand / (ms / 1e3), "unit": "candidates/s", "ms_per_call": ms, "steps": steps,
+        "config": {"workload": "8 packed layers B1 H32 S4096 D128 (codes 20/50/30 fp16/int8/int4), "
+                               "budget 70% of usage, 4 sink tokens", "candidates": n_cand,
+                   "processed": processed},
+        "gpu_launches": launches,
+    }
+    if world == 1 and rank == 0:
+        import numpy as np
+        from oracle import shadowkv_oracle as O
+
+        k, v = kvs[0]
+        codes = plans[0].codes.cpu().numpy()
+        layer = {"cache": O.pack(k.cpu().numpy(), v.cpu().numpy(), O.plan_from_codes(codes), c["group"]),
+                 "importance": imps[0].cpu().numpy(), "counted": True}
+        bud = int(O.manager_usage([layer]) * 0.7)
+        t = time.perf_counter()
+        O.enforce_global_budget([layer], bud, sink)
+        dt = time.perf_counter() - t
+        res["cpu_baseline"] = {"value": (S - sink) * H / dt, "unit": "candidates/s", "cores": 1, "kind": "port",
+                               "sample": "numpy oracle of enforce_global_budget on one layer of the workload"}
+    return res
+
+
 def tensor_peak():
     path = os.path.join(REPO, "MEASURED_PEAKS.json")
     try:
@@ -474,6 +552,7 @@ def run_b200(args):
     e2e_ms = float(e2e_ms.item())
     h2d = (hk.numel() + hv.numel() + himp.numel()) * 4 + hreuse.numel()
     attn = attention_phase(args, world, rank, dev, dist, lib, tensor_peak()) if not args.no_attention else None
+    gbudget = budget_phase(args, world, rank, dev, lib) if not args.no_attention else None
     if sampler:
         sampler.stop()
 
@@ -505,6 +584,7 @@ def run_b200(args):
         "gpu_launches": launches,
         "clocks": sampler.summary() if sampler else None,
         "attention": attn,
+        "global_budget": gbudget,
     }
     if world == 1:
         run = reference_sample(I, args.ref_heads)
