@@ -23,8 +23,10 @@ kernel), timed with CUDA events around each launch in the timed region.
 The line also carries ``attention``: packed attention over one cfg3 layer
 (B=1, H=32, S=4096, D=128, codes 20/50/30 % fp16/int8/int4), heads sharded over
 the ranks with an NCCL all-gather of the outputs, as tokens/s of the 32-layer
-stack and as tensor-core roofline of the kernel; and ``global_budget``:
-KVCacheManager.enforce_global_budget over 8 packed layers of that shape.
+stack and as tensor-core roofline of the kernel; ``global_budget``:
+KVCacheManager.enforce_global_budget over 8 packed layers of that shape; and
+``paged_store``: the PagedKVStore append-mode run of the reference's own paged
+benchmark shape plus its gather / append kernels at the cfg2 layer shape.
 """
 
 from __future__ import annotations
@@ -52,7 +54,11 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
     ap.add_argument("--ref-heads", type=int, default=8, help="head slice timed by the CPU reference arm")
-    ap.add_argument("--no-attention", action="store_true", help="skip the packed-attention and global-budget phases")
+    ap.add_argument("--no-attention", action="store_true",
+                    help="skip the packed-attention, global-budget and paged-store phases")
+    ap.add_argument("--phase", choices=("all", "paged", "paged-kernels"), default="all",
+                    help="'paged' / 'paged-kernels': print only the paged-store phase (all of it / its kernels "
+                         "at the cfg2 shape) as the JSON line; for profiling")
     return ap.parse_args()
 
 
@@ -404,6 +410,121 @@ def budget_phase(args, world, rank, dev, lib):
     return res
 
 
+def paged_phase(args, world, rank, dev, lib, run_mode=True):
+    """PagedKVStore (kv_execution="paged"), two measurements.
+
+    * append-mode run: the reference's own paged benchmark shape (B=4, H=8, D=64, 8 layers,
+      32-token fp16 pages, 16 steps of 128 new tokens; per step and layer gather the past,
+      then append the new tokens), through the public API, timed with CUDA events around
+      the whole run (host work included: the GPU waits on it);
+    * gather / append kernels at the cfg2 layer shape (B=1, H=32, S=8192, D=128, fp16
+      pages): one gather of the full store and one append of all 8192 tokens, each over
+      more than L2's worth of bytes, CUDA events around each launch.
+    """
+    import torch
+
+    from shadow_infer_b200.shadowkv import PagedKVStore
+
+    B, H, D, L, P, n_steps, chunk = 4, 8, 64, 8, 32, 16, 128
+    S = n_steps * chunk
+    g = torch.Generator().manual_seed(2026 + rank)
+    kf = (torch.randn(B, H, S, D, generator=g) * 2.0).to(dev)
+    vf = (torch.randn(B, H, S, D, generator=g) * 2.0).to(dev)
+    reps = max(3, min(args.steps, 5))
+    res = {}
+
+    def run():
+        stores = [PagedKVStore(B, H, D, page_size=P, device=dev) for _ in range(L)]
+        for step in range(n_steps):
+            a = step * chunk
+            for st in stores:
+                if step:
+                    st.gather()
+                st.append(kf[:, :, a:a + chunk], vf[:, :, a:a + chunk], "fp16")
+        return stores
+
+    if run_mode:
+        for _ in range(2):
+            run()
+        times = []
+        n0 = lib.skv_launch_count()
+        for _ in range(reps):
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            run()
+            e1.record()
+            torch.cuda.synchronize()
+            times.append(e0.elapsed_time(e1))
+        launches = (lib.skv_launch_count() - n0) // reps
+        ms = statistics.median(times)
+        res.update({
+            "metric": "paged append-mode run tokens/s (AR014 shape: 8 layers, 16 steps x 128 tokens, "
+                      "gather + append)",
+            "value": L * S / (ms / 1e3), "unit": "tokens/s", "ms_per_run": ms, "runs": reps,
+            "config": {"workload": "B4 H8 D64, 8 layers, 32-token fp16 pages, 16 steps of 128 tokens",
+                       "gathers_per_run": L * (n_steps - 1), "appends_per_run": L * n_steps},
+            "gpu_launches_per_run": launches,
+        })
+
+    # kernels at the cfg2 layer shape
+    B2, H2, S2, D2 = 1, 32, 8192, 128
+    k2 = (torch.randn(B2, H2, S2, D2, generator=g) * 2.0).to(dev)
+    v2 = (torch.randn(B2, H2, S2, D2, generator=g) * 2.0).to(dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    gather_ms, append_ms = [], []
+    for i in range(2 + reps):
+        st = PagedKVStore(B2, H2, D2, page_size=32, device=dev)
+        flush.fill_(i & 0xFF)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        st._kernel_events = (e0, e1)
+        st.append(k2, v2, "fp16")
+        flush.fill_(i & 0xFF)
+        e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        st._kernel_events = (e2, e3)
+        st.gather()
+        torch.cuda.synchronize()
+        if i >= 2:
+            append_ms.append(e0.elapsed_time(e1))
+            gather_ms.append(e2.elapsed_time(e3))
+    peak, peak_kind = hbm_peak()
+    n_el = B2 * H2 * S2 * D2
+    g_bytes = 2 * n_el * (2 + 4)            # fp16 pages read, fp32 K/V written
+    a_bytes = 2 * n_el * (4 + 2)            # fp32 rows read, fp16 pages written
+    g_ms, a_ms = statistics.mean(gather_ms), statistics.mean(append_ms)
+    res.update({
+        "gather": {"workload": "B1 H32 S8192 D128 fp16 pages (256 pages of 32)", "ms": g_ms,
+                   "GB/s": g_bytes / (g_ms / 1e3) / 1e9,
+                   "roofline": {"kernel": "paged_gather_kernel", "bound": "hbm",
+                                "achieved": g_bytes / (g_ms / 1e3) / 1e9, "peak": peak, "unit": "GB/s",
+                                "frac": g_bytes / (g_ms / 1e3) / 1e9 / peak, "peak_source": f"{peak_kind} hbm_gbs",
+                                "algorithmic_bytes": g_bytes,
+                                "traffic": committed_traffic("paged_gather_kernel_cfg2.md")}},
+        "append": {"workload": "one append of 8192 tokens into 256 new fp16 pages", "ms": a_ms,
+                   "GB/s": a_bytes / (a_ms / 1e3) / 1e9,
+                   "roofline": {"kernel": "paged_write_kernel", "bound": "hbm",
+                                "achieved": a_bytes / (a_ms / 1e3) / 1e9, "peak": peak, "unit": "GB/s",
+                                "frac": a_bytes / (a_ms / 1e3) / 1e9 / peak, "peak_source": f"{peak_kind} hbm_gbs",
+                                "algorithmic_bytes": a_bytes,
+                                "traffic": committed_traffic("paged_write_kernel_cfg2.md")}},
+    })
+    if run_mode and world == 1 and rank == 0:
+        from oracle.paged_store_oracle import OraclePagedStore
+
+        kc, vc = kf.cpu().numpy(), vf.cpu().numpy()
+        t = time.perf_counter()
+        st = OraclePagedStore(B, H, D, page_size=P)
+        for step in range(n_steps):
+            a = step * chunk
+            if step:
+                st.gather()
+            st.append(kc[:, :, a:a + chunk], vc[:, :, a:a + chunk], "fp16")
+        dt = time.perf_counter() - t
+        res["cpu_baseline"] = {"value": S / dt, "unit": "tokens/s", "cores": 1, "kind": "port",
+                               "sample": "numpy oracle of the append-mode run on one of the 8 layers"}
+    return res
+
+
 def tensor_peak():
     path = os.path.join(REPO, "MEASURED_PEAKS.json")
     try:
@@ -433,6 +554,13 @@ def run_b200(args):
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     lib = _lib.load()
+    if args.phase != "all":
+        res = paged_phase(args, world, rank, dev, lib, run_mode=args.phase == "paged")
+        if world > 1:
+            dist.destroy_process_group()
+        if rank == 0:
+            print(json.dumps({"phase": args.phase, "paged_store": res}), flush=True)
+        return 0
 
     # every rank packs its own layer: seed = rank
     I = W.cfg2_inputs(seed=rank)
@@ -553,6 +681,7 @@ def run_b200(args):
     h2d = (hk.numel() + hv.numel() + himp.numel()) * 4 + hreuse.numel()
     attn = attention_phase(args, world, rank, dev, dist, lib, tensor_peak()) if not args.no_attention else None
     gbudget = budget_phase(args, world, rank, dev, lib) if not args.no_attention else None
+    paged = paged_phase(args, world, rank, dev, lib) if not args.no_attention else None
     if sampler:
         sampler.stop()
 
@@ -585,6 +714,7 @@ def run_b200(args):
         "clocks": sampler.summary() if sampler else None,
         "attention": attn,
         "global_budget": gbudget,
+        "paged_store": paged,
     }
     if world == 1:
         run = reference_sample(I, args.ref_heads)

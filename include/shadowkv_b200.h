@@ -194,6 +194,58 @@ int skv_rank_select(const float* score, const int64_t* weight, int64_t n, int64_
 /* mask[i] = 1 for the candidates at or below the key in result (from skv_rank_select). */
 int skv_mark_smallest(const float* score, int64_t n, const int64_t* result, uint8_t* mask, void* stream);
 
+/* ---------------------------------------------------------------------------------------
+ * Paged KV store  (shadowinfer/shadowkv/paged_kv_store.py)
+ *
+ * A page holds the rows of one precision for consecutive tokens.  Payload slab
+ * [B, H, cap, row]: row = D float | D half | D int8 | ceil(D/2) int4 bytes ((q+8) high nibble
+ * first, a zero nibble after an odd last value); scales float [B, H, cap] (int8) or
+ * [B, H, cap, D/G] (int4, G the effective group of packed_kv_cache.py:307).
+ * ------------------------------------------------------------------------------------- */
+typedef struct skv_page_desc {
+    void* k;              /* payload row of the page's first token in block (b, h) = (0, 0) */
+    void* v;
+    float* scale_k;       /* scale row of that token (NULL for fp32 / fp16 pages) */
+    float* scale_v;
+    int64_t start_token;  /* global position of the page's first token */
+    int32_t num_tokens;   /* tokens in the page */
+    int32_t row_stride;   /* rows from one (b, h) block to the next (the slab's cap) */
+    int32_t precision;    /* 0 fp32, 1 fp16, 2 int8, 3 int4 */
+    int32_t reserved[3];
+} skv_page_desc;          /* 64 bytes */
+
+typedef struct skv_page_write {
+    skv_page_desc page;   /* destination page, num_tokens as after the write */
+    int64_t src_token;    /* first source token of the run */
+    int32_t dst_row;      /* first row inside the page */
+    int32_t rows;         /* rows to write (>= 1) */
+    int32_t table_pos;    /* page-table entry that receives `page` after the launch, or -1 */
+    int32_t reserved;
+} skv_page_write;         /* 88 bytes */
+
+/* PagedKVStore._quantize_chunk + the page merge of append / the row copy of rewrite_tokens
+ * (paged_kv_store.py:189-224, :248-307, :408-448): quantises K/V float [B, H, T_src, D] rows
+ * [src_token, src_token + rows) of every write into its page's rows [dst_row, dst_row + rows),
+ * bit-identical to Quantizer.quantize_int8 / quantize_int4 per (b, h, token) row.  `writes` is
+ * HOST memory, read during the call; `table` (device, may be NULL) receives each write's
+ * page descriptor at table_pos. */
+int skv_paged_write(const float* k, const float* v, int B, int H, int64_t T_src, int D, int int4_group_size,
+                    const skv_page_write* writes, int n_writes, skv_page_desc* table, void* stream);
+
+/* PagedKVStore.gather  (paged_kv_store.py:326-402): dense float K/V [B, H, s_out, D] from the
+ * n_pages descriptors of `table` (device, token order, non-overlapping); tokens no page holds
+ * are zero.  max_span_tokens >= max over pages j of (start_j - end_{j-1}) + num_tokens_j and
+ * >= s_out - end_last. */
+int skv_paged_gather(const skv_page_desc* table, int n_pages, int B, int H, int D, int int4_group_size,
+                     int64_t s_out, int64_t max_span_tokens, float* k_out, float* v_out, void* stream);
+
+/* The head-row zeroing of PagedKVStore._plan_eviction  (paged_kv_store.py:662-672):
+ * items int32 [n_items, 3] (device) = {table entry, row inside the page, head}; zeroes that
+ * row of K and V in every batch (0x88 bytes for int4 pages).  *error_flag (device int32) is
+ * set to 1 if an item lies outside the table or its page. */
+int skv_paged_clear_heads(const skv_page_desc* table, int n_pages, const int32_t* items, int64_t n_items, int B,
+                          int H, int D, int* error_flag, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

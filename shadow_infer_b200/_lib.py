@@ -92,6 +92,11 @@ _SIGNATURES = {
                                 c_void_p]),
     "skv_evict_compact": (c_int, [ctypes.POINTER(SkvBucket), ctypes.POINTER(SkvBucket), c_void_p, c_void_p, c_int,
                                   c_int, c_int, c_int, c_int, c_void_p, c_size_t, c_void_p]),
+    "skv_paged_write": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int64, c_int, c_int, c_void_p, c_int, c_void_p,
+                                c_void_p]),
+    "skv_paged_gather": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_int, c_int64, c_int64, c_void_p, c_void_p,
+                                 c_void_p]),
+    "skv_paged_clear_heads": (c_int, [c_void_p, c_int, c_void_p, c_int64, c_int, c_int, c_int, c_void_p, c_void_p]),
 }
 
 EXPORTED_SYMBOLS = tuple(_SIGNATURES.keys())

@@ -10,6 +10,7 @@ from .kv_cache_manager import (
 )
 from .packed_attention import packed_attention
 from .packed_kv_cache import PackedKVCache
+from .paged_kv_store import PagedKVStore
 from .precision_plan import (
     CODE_PRECISIONS,
     EVICTED,
@@ -25,5 +26,5 @@ __all__ = [
     "PackedKVCache", "PrecisionPlan", "map_to_codes", "codes_to_map", "PRECISION_ORDER", "PRECISION_CODES",
     "CODE_PRECISIONS", "EVICTED", "admit_codes", "admit_budget", "entry_bytes", "kv_sensitivity",
     "predict_codes_bytes", "packed_attention", "KVCacheManager", "KVCacheEntry", "TokenHeadScore",
-    "EvictionPolicy", "LeastImportantEvictionPolicy", "ImportanceAgeEvictionPolicy",
+    "EvictionPolicy", "LeastImportantEvictionPolicy", "ImportanceAgeEvictionPolicy", "PagedKVStore",
 ]

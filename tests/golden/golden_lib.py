@@ -76,3 +76,67 @@ def load_small() -> Dict[str, np.ndarray]:
 def case_arrays(small: Dict[str, np.ndarray], case: str) -> Dict[str, np.ndarray]:
     pre = case + "/"
     return {k[len(pre):]: v for k, v in small.items() if k.startswith(pre)}
+
+
+# ------------------------------------------------------------------------------ paged store
+def paged_inputs(seed: int, B: int, H: int, T: int, D: int):
+    """Seeded K/V ``[B,H,T,D]`` fp32 for the paged-store scripts: N(0, 2^2) values, about 3% of
+    the (b, h, t) rows exactly zero (scale 0 -> 1) and a few values large enough to overflow fp16."""
+    rng = np.random.default_rng(seed)
+    out = []
+    for _ in range(2):
+        x = (rng.standard_normal((B, H, T, D)) * 2.0).astype(np.float32)
+        x[rng.random((B, H, T)) < 0.03] = 0.0
+        x[rng.random((B, H, T, D)) < 0.002] *= np.float32(4.0e4)
+        out.append(x)
+    return out[0], out[1]
+
+
+def paged_bad_inputs(kind: str, seed: int, B: int, H: int, D: int):
+    """Inputs that every append/rewrite must refuse with ValueError (paged_kv_store.py:149-183)."""
+    k, v = paged_inputs(seed, B, H, 3, D)
+    if kind == "heads":
+        k, v = paged_inputs(seed, B, H + 1, 3, D)
+    elif kind == "dim":
+        k, v = paged_inputs(seed, B, H, 3, D + 1)
+    elif kind == "batch":
+        k, v = paged_inputs(seed, B + 1, H, 3, D)
+    elif kind == "ndim":
+        k = k[..., 0]
+    elif kind == "kv_mismatch":
+        v = v[:, :, :2]
+    return k, v
+
+
+def state_digest(page_digests) -> str:
+    """One SHA-256 over the per-page tensor digests of a store state."""
+    return hashlib.sha256(json.dumps(page_digests).encode()).hexdigest()
+
+
+def paged_apply(store, op, B: int, H: int, D: int, conv):
+    """Apply one scripted operation (as recorded in the fixtures) to a paged store; ``conv``
+    turns the numpy inputs into what the store takes.  Returns the operation's return value."""
+    name = op[0]
+    if name == "append":
+        _, T, prec, seed = op
+        k, v = paged_inputs(seed, B, H, T, D)
+        return store.append(conv(k), conv(v), prec)
+    if name == "append_bad":
+        _, kind, prec, seed = op
+        k, v = paged_bad_inputs(kind, seed, B, H, D)
+        return store.append(conv(k), conv(v), prec)
+    if name == "rewrite":
+        _, start, T, prec, seed = op
+        k, v = paged_inputs(seed, B, H, T, D)
+        return store.rewrite_tokens(start, conv(k), conv(v), prec)
+    if name == "rewrite_bad":
+        _, start, kind, prec, seed = op
+        k, v = paged_bad_inputs(kind, seed, B, H, D)
+        return store.rewrite_tokens(start, conv(k), conv(v), prec)
+    if name == "evict":
+        return store.evict_tokens({(int(t), int(h)) for t, h in op[1]})
+    if name == "clear":
+        return store.clear()
+    if name == "validate":
+        return store.validate_against(*op[1:])
+    raise ValueError(f"unknown scripted operation {name}")

@@ -32,7 +32,8 @@ REPO = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, REPO)
 sys.path.insert(0, HERE)
 
-from golden_lib import PINS_JSON, SMALL_NPZ, array_digest, packed_summary, to_numpy  # noqa: E402
+from golden_lib import (PINS_JSON, SMALL_NPZ, array_digest, packed_summary, paged_apply,  # noqa: E402
+                        state_digest, to_numpy)
 
 from shadow_infer_b200 import workloads as W  # noqa: E402
 
@@ -44,8 +45,9 @@ def _import_reference(path: str):
     sys.path.insert(0, path)
     from shadowinfer.shadowkv import rd_allocator, precision_plan, packed_kv_cache  # noqa
     from shadowinfer.shadowkv.shadowkv_agent import ShadowKVAgent  # noqa
+    from shadowinfer.shadowkv import paged_kv_store  # noqa
     return types.SimpleNamespace(
-        rd=rd_allocator, plan=precision_plan, pkc=packed_kv_cache, Agent=ShadowKVAgent
+        rd=rd_allocator, plan=precision_plan, pkc=packed_kv_cache, Agent=ShadowKVAgent, paged=paged_kv_store
     )
 
 
@@ -296,6 +298,139 @@ def global_budget_case(R, case, gen, B, H, S, D, layers, budget_frac, sink, *, p
     }
 
 
+def _paged_op(store, op, B, H, D):
+    return paged_apply(store, op, B, H, D, torch.from_numpy)
+
+
+def paged_state(store):
+    from oracle.paged_store_oracle import store_state
+    st = store_state(store, to_numpy)
+    st["pages_digest"] = state_digest(st.pop("page_digests"))
+    return st
+
+
+def paged_case(R, case, B, H, D, P, G, ops):
+    """Replay an operation script on the reference PagedKVStore (paged_kv_store.py) and pin its
+    return values / ValueErrors, page layout, slot pool, counters, ledgers, page-tensor digests
+    and gather digests after every operation."""
+    store = R.paged.PagedKVStore(B, H, D, page_size=P, device="cpu", int4_group_size=G)
+    results = []
+    for op in ops:
+        try:
+            ret, err = _paged_op(store, op, B, H, D), False
+        except ValueError:
+            ret, err = None, True
+        k, v = store.gather()
+        results.append({"ret": ret, "error": err, "state": paged_state(store),
+                        "gather": [array_digest(k), array_digest(v)], "S_out": int(k.shape[2])})
+    PINS["cases"][case] = {"kind": "paged", "B": B, "H": H, "D": D, "P": P, "G": G, "ops": ops,
+                           "results": results}
+
+
+def paged_random_ops(R, B, H, D, P, G, n_ops, seed):
+    """A seeded random script: appends of random lengths and precisions (sticky), evictions of
+    full tokens / single heads / absent pairs, rewrites inside and across pages (many valid,
+    some refused), invalid inputs and one clear.  Chosen against a live reference store."""
+    rng = np.random.default_rng(seed)
+    store = R.paged.PagedKVStore(B, H, D, page_size=P, device="cpu", int4_group_size=G)
+    ops, prec = [], "fp16"
+    for i in range(n_ops):
+        r = rng.random()
+        s = int(seed * 1000 + i)
+        if r < 0.45 or store.max_seq == 0:
+            if rng.random() < 0.4:
+                prec = PRECISIONS[int(rng.integers(4))]
+            T = int(rng.choice([0, 1, 2, P - 1, P, P + 1, 2 * P + 3, int(rng.integers(1, 3 * P))]))
+            op = ["append", max(T, 0), prec, s]
+        elif r < 0.68:
+            S = store.max_seq
+            pairs = set()
+            for _ in range(int(rng.integers(1, 4))):
+                t = int(rng.integers(0, S + 2))
+                if rng.random() < 0.5:
+                    pairs.update((t, h) for h in range(H))
+                else:
+                    pairs.add((t, int(rng.integers(0, H + 1))))
+            op = ["evict", sorted([list(p) for p in pairs])]
+        elif r < 0.92:
+            live = [store.pages[sl] for sl in store._order]
+            if live and rng.random() < 0.8:
+                pg = live[int(rng.integers(len(live)))]
+                a = pg.start_token + int(rng.integers(pg.num_tokens))
+                span = pg.end_token - a + (int(rng.integers(0, P)) if rng.random() < 0.3 else 0)
+                T = int(rng.integers(1, span + 1))
+                p = pg.precision if rng.random() < 0.9 else PRECISIONS[int(rng.integers(4))]
+                op = ["rewrite", a, T, p, s]
+            else:
+                op = ["rewrite", int(rng.integers(-1, store.max_seq + 2)), int(rng.integers(0, 4)), prec, s]
+        elif r < 0.97:
+            kind = ["precision", "heads", "dim", "batch", "ndim", "kv_mismatch"][int(rng.integers(6))]
+            p = "bf16" if kind == "precision" else prec
+            op = ["append_bad", kind, p, s] if rng.random() < 0.5 else ["rewrite_bad", 0, kind, p, s]
+        else:
+            op = ["clear"]
+        try:
+            _paged_op(store, op, B, H, D)
+        except ValueError:
+            pass
+        ops.append(op)
+    return ops
+
+
+def paged_cases(R):
+    full = lambda *ts: [[t, h] for t in ts for h in range(4)]  # noqa: E731  (H = 4 scripts)
+    a = lambda T, p, s: ["append", T, p, s]  # noqa: E731
+    paged_case(R, "paged_fp16_evict", 2, 4, 32, 8, 16, [
+        a(5, "fp16", 1), a(5, "fp16", 2), a(5, "fp16", 3), a(4, "fp16", 4),
+        ["evict", full(2, 4, 5, 17) + [[10, 0], [10, 1], [12, 2], [12, 3]]],
+        ["evict", [[5, 0], [5, 3], [24, 0], [0, 7]]],
+        ["evict", [[10, 2], [10, 3]]],
+        ["rewrite", 0, 2, "fp16", 5], ["rewrite", 9, 3, "fp16", 6],
+        a(2, "fp16", 7), ["evict", full(18, 19, 20)], a(3, "fp16", 8),
+    ])
+    paged_case(R, "paged_int8_rewrite", 2, 4, 32, 8, 16, [
+        a(8, "int8", 11), a(8, "int8", 12), a(8, "int8", 13), a(2, "int8", 14),
+        ["rewrite", 4, 16, "int8", 15], ["rewrite", 0, 4, "fp16", 16], ["rewrite", 20, 8, "int8", 17],
+        ["rewrite", -1, 2, "int8", 18], ["rewrite", 3, 0, "int8", 19], ["rewrite", 26, 1, "int8", 20],
+        a(3, "int4", 21), ["rewrite", 24, 3, "int8", 22], ["rewrite", 0, 29, "int8", 23],
+        ["rewrite", 0, 26, "int8", 24], ["validate", 2, 4, 32], ["validate", 2, 5, 32],
+        ["rewrite_bad", 0, "heads", "int8", 25], ["append_bad", "precision", "bf16", 26],
+        ["append_bad", "kv_mismatch", "int8", 27], ["append", 0, "int8", 28],
+    ])
+    paged_case(R, "paged_mixed_pool", 2, 4, 32, 4, 16, [
+        a(4, "fp16", 31), a(4, "int8", 32), a(3, "int4", 33), a(5, "fp32", 34), a(2, "fp16", 35),
+        ["evict", full(4, 5, 6, 7)], a(3, "int8", 36), ["evict", full(0)],
+        ["evict", [[9, 1], [9, 3]]], ["evict", full(21, 20)], a(6, "int4", 37),
+        ["rewrite", 8, 3, "int4", 38], ["evict", [[8, 0], [9, 0], [9, 2], [10, 0]]],
+        ["rewrite", 12, 4, "fp32", 39], ["clear"], a(5, "int4", 40),
+    ])
+    paged_case(R, "paged_tail_contiguous", 1, 4, 64, 8, 16, [
+        a(19, "fp16", 41), ["evict", full(17, 18)], a(2, "fp16", 42), ["evict", full(19, 20)],
+        ["evict", full(0, 1, 2, 3, 4, 5, 6, 7)], a(9, "int8", 43), ["evict", full(8, 9, 10)],
+    ])
+    paged_case(R, "paged_int4_d40_group_fallback", 2, 2, 40, 8, 16, [
+        a(5, "int4", 51), a(7, "int4", 52), a(3, "int8", 53), ["rewrite", 2, 8, "int4", 54],
+        ["evict", [[3, 1], [6, 0], [6, 1], [13, 0]]], a(4, "int4", 55),
+    ])
+    paged_case(R, "paged_int4_d33_odd", 1, 3, 33, 5, 16, [
+        a(7, "int4", 61), a(4, "fp16", 62), a(6, "int4", 63), ["evict", [[1, 2], [12, 0], [12, 1], [12, 2], [14, 1]]],
+        ["rewrite", 11, 1, "int4", 64], a(3, "int8", 65),
+    ])
+    paged_case(R, "paged_int4_d48_group24", 1, 2, 48, 6, 24, [
+        a(10, "int4", 71), ["rewrite", 2, 5, "int4", 72], ["evict", [[4, 0], [7, 0], [7, 1]]], a(9, "int4", 73),
+    ])
+    paged_case(R, "paged_int4_d64_group4", 1, 2, 64, 16, 4, [
+        a(20, "int4", 81), a(7, "int8", 82), ["rewrite", 5, 11, "int4", 83], ["evict", [[3, 1], [17, 0], [17, 1]]],
+    ])
+    for name, (B, H, D, P, G, n, seed) in {
+        "paged_random_b2_d64": (2, 3, 64, 8, 16, 48, 7),
+        "paged_random_b1_d128_g32": (1, 4, 128, 16, 32, 48, 8),
+        "paged_random_b3_d32_p3": (3, 2, 32, 3, 8, 48, 9),
+        "paged_random_b1_d96_p1": (1, 2, 96, 1, 16, 30, 10),
+    }.items():
+        paged_case(R, name, B, H, D, P, G, paged_random_ops(R, B, H, D, P, G, n, seed))
+
+
 def full_pins(R):
     """cfg1 / cfg2 pipelines at full size: digests only."""
     c1 = W.CONFIGS["cfg1"]
@@ -405,6 +540,7 @@ def main():
     global_budget_case(R, "gb_floor", gen, 1, 2, 12, 64, 2, 0.02, 2)
     global_budget_case(R, "gb_no_pressure", gen, 1, 2, 12, 64, 2, 2.0, 0)
     global_budget_case(R, "gb_b2_group32", gen, 2, 2, 40, 128, 2, 0.4, 4, group=32, probs=(0.1, 0.3, 0.3, 0.25, 0.05))
+    paged_cases(R)
     full_pins(R)
     np.savez_compressed(SMALL_NPZ, **ARR)
     with open(PINS_JSON, "w") as f:

@@ -193,3 +193,25 @@ def test_global_budget(case, golden_small):
                 present[t, h] = 1
         np.testing.assert_array_equal(present, a[f"L{L}.remaining"])
         assert layer["cache"].resident_bytes() == pin["resident_after"][L]
+
+
+@pytest.mark.parametrize("case", _cases(_pins(), "paged"))
+def test_paged_store(case):
+    """PagedKVStore scripts: return values / ValueErrors, page layout, slot pool, counters,
+    ledgers, page-tensor digests and gather digests after every operation."""
+    from golden_lib import array_digest as dig, paged_apply, state_digest
+    from oracle.paged_store_oracle import OraclePagedStore, store_state
+    pin = _pins()["cases"][case]
+    B, H, D = pin["B"], pin["H"], pin["D"]
+    store = OraclePagedStore(B, H, D, page_size=pin["P"], int4_group_size=pin["G"])
+    for i, (op, want) in enumerate(zip(pin["ops"], pin["results"])):
+        try:
+            ret, err = paged_apply(store, op, B, H, D, lambda x: x), False
+        except ValueError:
+            ret, err = None, True
+        assert (ret, err) == (want["ret"], want["error"]), (i, op)
+        st = store_state(store)
+        st["pages_digest"] = state_digest(st.pop("page_digests"))
+        assert st == want["state"], (i, op)
+        k, v = store.gather()
+        assert [dig(k), dig(v)] == want["gather"] and k.shape[2] == want["S_out"], (i, op)
