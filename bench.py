@@ -502,11 +502,11 @@ def paged_phase(args, world, rank, dev, lib, run_mode=True):
                                 "traffic": committed_traffic("paged_gather_kernel_cfg2.md")}},
         "append": {"workload": "one append of 8192 tokens into 256 new fp16 pages", "ms": a_ms,
                    "GB/s": a_bytes / (a_ms / 1e3) / 1e9,
-                   "roofline": {"kernel": "paged_write_kernel", "bound": "hbm",
+                   "roofline": {"kernel": "paged_write_vec_kernel", "bound": "hbm",
                                 "achieved": a_bytes / (a_ms / 1e3) / 1e9, "peak": peak, "unit": "GB/s",
                                 "frac": a_bytes / (a_ms / 1e3) / 1e9 / peak, "peak_source": f"{peak_kind} hbm_gbs",
                                 "algorithmic_bytes": a_bytes,
-                                "traffic": committed_traffic("paged_write_kernel_cfg2.md")}},
+                                "traffic": committed_traffic("paged_write_vec_kernel_cfg2.md")}},
     })
     if run_mode and world == 1 and rank == 0:
         from oracle.paged_store_oracle import OraclePagedStore

@@ -202,6 +202,8 @@ int skv_mark_smallest(const float* score, int64_t n, const int64_t* result, uint
  * first, a zero nibble after an odd last value); scales float [B, H, cap] (int8) or
  * [B, H, cap, D/G] (int4, G the effective group of packed_kv_cache.py:307).
  * ------------------------------------------------------------------------------------- */
+/* Page payload pointers should be 16-byte aligned and scale pointers 4-byte aligned (the
+ * kernels use 16-byte vectors then, value-by-value access otherwise). */
 typedef struct skv_page_desc {
     void* k;              /* payload row of the page's first token in block (b, h) = (0, 0) */
     void* v;

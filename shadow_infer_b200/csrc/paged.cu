@@ -125,6 +125,124 @@ __global__ void __launch_bounds__(256) paged_write_kernel(const float* __restric
               p, D, G, ngroups, gsm, lane);
 }
 
+// Vector path (D in {32, 64, 128, 256}; int4 groups a multiple of V): the rows of one
+// (write, b, h) run are contiguous in the source and in the page, so a warp walks them as one
+// flat array, V consecutive values per lane and 32*V values (whole rows) per pass.  The lanes
+// of a row (D/V of them) and of an int4 group (G/V) are aligned lane blocks, reduced with xor
+// shuffles.  A warp takes PPW passes of K and V, all loads issued before the first store.
+template <int V, int PPW, int N>
+__global__ void __launch_bounds__(256) paged_write_vec_kernel(const float* __restrict__ k,
+                                                             const float* __restrict__ v, int BH, int64_t T_src,
+                                                             int D, int G, const __grid_constant__ PagedWrites<N> ws,
+                                                             skv_page_desc* __restrict__ table) {
+    const skv_page_write& w = ws.w[blockIdx.y];
+    if (blockIdx.x == 0 && threadIdx.x == 0 && table != nullptr && w.table_pos >= 0) table[w.table_pos] = w.page;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t n_el = (int64_t)w.rows * D;
+    const int passes = (int)((n_el + 32 * V - 1) / (32 * V));
+    const int tasks_per_bh = (passes + PPW - 1) / PPW;
+    const int64_t task = (int64_t)blockIdx.x * kPagedWarps + warp;
+    if (task >= (int64_t)tasks_per_bh * BH) return;
+    const int bh = (int)(task / tasks_per_bh), pass0 = (int)(task % tasks_per_bh) * PPW;
+    const int p = w.page.precision;
+    const int lpr = D / V;                     // lanes per row
+    const int lpg = G / V;                     // lanes per int4 group
+    const int ng = D / G;
+    const int64_t src0 = ((int64_t)bh * T_src + w.src_token) * D;
+    const int64_t row0 = (int64_t)bh * w.page.row_stride + w.dst_row;   // page row of the run's first token
+    float xk[PPW][V], xv[PPW][V];
+#pragma unroll
+    for (int i = 0; i < PPW; ++i) {
+        const int64_t e = (int64_t)(pass0 + i) * 32 * V + lane * V;
+#pragma unroll
+        for (int j = 0; j < V; j += 4) {
+            float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = a;
+            if (e < n_el) {
+                a = __ldg(reinterpret_cast<const float4*>(k + src0 + e + j));
+                b = __ldg(reinterpret_cast<const float4*>(v + src0 + e + j));
+            }
+            xk[i][j] = a.x; xk[i][j + 1] = a.y; xk[i][j + 2] = a.z; xk[i][j + 3] = a.w;
+            xv[i][j] = b.x; xv[i][j + 1] = b.y; xv[i][j + 2] = b.z; xv[i][j + 3] = b.w;
+        }
+    }
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {
+        uint8_t* dst = static_cast<uint8_t*>(t ? w.page.v : w.page.k);
+        float* sc = t ? w.page.scale_v : w.page.scale_k;
+#pragma unroll
+        for (int i = 0; i < PPW; ++i) {
+            const float* x = t ? xv[i] : xk[i];
+            const int64_t e = (int64_t)(pass0 + i) * 32 * V + lane * V;
+            const bool on = e < n_el;
+            const int64_t r = e / D;                   // run row
+            const int col = (int)(e - r * D);
+            const int64_t prow = row0 + r;            // page row (b, h block included)
+            if (p == 0) {
+                if (on) {
+#pragma unroll
+                    for (int j = 0; j < V; j += 4)
+                        reinterpret_cast<float4*>(dst + (prow * D + col + j) * 4)[0] =
+                            make_float4(x[j], x[j + 1], x[j + 2], x[j + 3]);
+                }
+            } else if (p == 1) {
+                uint32_t h[V / 2];
+#pragma unroll
+                for (int j = 0; j < V / 2; ++j) {
+                    const __half2 hv = __floats2half2_rn(x[2 * j], x[2 * j + 1]);
+                    h[j] = *reinterpret_cast<const uint32_t*>(&hv);
+                }
+                if (on) {
+                    if (V == 4) {
+                        *reinterpret_cast<uint2*>(dst + (prow * D + col) * 2) = make_uint2(h[0], h[1]);
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < V / 2; j += 4)
+                            *reinterpret_cast<uint4*>(dst + (prow * D + col + 2 * j) * 2) =
+                                make_uint4(h[j], h[j + 1], h[j + 2], h[j + 3]);
+                    }
+                }
+            } else {
+                const bool i4 = p == 3;
+                float m = 0.0f;
+#pragma unroll
+                for (int j = 0; j < V; ++j) m = fmaxf(m, fabsf(x[j]));
+                m = group_max(m, i4 ? lpg : lpr);    // every lane runs the shuffles
+                const float s = quant_scale(m, i4 ? 7.0f : 127.0f), rc = __frcp_rn(s);
+                int q[V];
+#pragma unroll
+                for (int j = 0; j < V; ++j) q[j] = quant_value_fast(x[j], s, rc, i4 ? -8 : -128, i4 ? 7 : 127);
+                if (on) {
+                    if (!i4) {
+#pragma unroll
+                        for (int j = 0; j < V; j += 4) {
+                            const uint32_t wd = ((uint32_t)(q[j] & 0xFF)) | ((uint32_t)(q[j + 1] & 0xFF) << 8) |
+                                                ((uint32_t)(q[j + 2] & 0xFF) << 16) |
+                                                ((uint32_t)(q[j + 3] & 0xFF) << 24);
+                            *reinterpret_cast<uint32_t*>(dst + prow * D + col + j) = wd;
+                        }
+                        if (col == 0) sc[prow] = s;
+                    } else {
+                        uint32_t bytes[V / 2];
+#pragma unroll
+                        for (int j = 0; j < V / 2; ++j)
+                            bytes[j] = (((uint32_t)(q[2 * j] + 8) & 15u) << 4) | ((uint32_t)(q[2 * j + 1] + 8) & 15u);
+                        uint8_t* d = dst + (prow * D + col) / 2;
+                        if (V == 4) {
+                            *reinterpret_cast<uint16_t*>(d) = (uint16_t)(bytes[0] | (bytes[1] << 8));
+                        } else {
+#pragma unroll
+                            for (int j = 0; j < V / 2; j += 4)
+                                *reinterpret_cast<uint32_t*>(d + j) =
+                                    bytes[j] | (bytes[j + 1] << 8) | (bytes[j + 2] << 16) | (bytes[j + 3] << 24);
+                        }
+                        if (col % G == 0) sc[prow * ng + col / G] = s;
+                    }
+                }
+            }
+        }
+    }
+}
+
 // ------------------------------------------------------------------------------------ gather
 __device__ __forceinline__ void st8(float* dst, const float (&x)[8]) {
     float4* d = reinterpret_cast<float4*>(dst);
@@ -236,7 +354,11 @@ __global__ void __launch_bounds__(256) paged_gather_kernel(const skv_page_desc* 
     const int64_t row0 = (int64_t)bh * s_pg.row_stride + (t0 - pstart);
     const int64_t o = ((int64_t)bh * s_out + t0) * D;
     const int64_t n = (b - t0) * D;
-    if (VEC) {
+    // 16-byte vector loads need 16-byte aligned payloads (4-byte scales); other pages decode
+    // value by value
+    const bool aligned = ((reinterpret_cast<uintptr_t>(s_pg.k) | reinterpret_cast<uintptr_t>(s_pg.v)) & 15) == 0 &&
+                         ((reinterpret_cast<uintptr_t>(s_pg.scale_k) | reinterpret_cast<uintptr_t>(s_pg.scale_v)) & 3) == 0;
+    if (VEC && aligned) {
         for (int64_t e = (int64_t)threadIdx.x * 8; e < n; e += (int64_t)blockDim.x * 8) {
             const int64_t r = e / D;
             const int col = (int)(e - r * D);
@@ -320,21 +442,49 @@ int skv_paged_write(const float* k, const float* v, int B, int H, int64_t T_src,
         const int n = n_writes - base < kPagedManyWrites ? n_writes - base : kPagedManyWrites;
         int max_rows = 0;
         for (int i = 0; i < n; ++i) max_rows = writes[base + i].rows > max_rows ? writes[base + i].rows : max_rows;
-        const int64_t gx = ((int64_t)max_rows * BH + kPagedWarps - 1) / kPagedWarps;
+        // vector path: whole rows per warp pass, int4 groups on aligned lane blocks
+        const int V = D == 256 ? 8 : 4;
+        bool vec = (D == 32 || D == 64 || D == 128 || D == 256) && G % V == 0;
+        // 16-byte vectors: source rows and page payloads must start on 16-byte boundaries
+        vec = vec && ((reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v)) & 15) == 0;
+        for (int i = 0; i < n && vec; ++i) {
+            const skv_page_desc& pg = writes[base + i].page;
+            vec = ((reinterpret_cast<uintptr_t>(pg.k) | reinterpret_cast<uintptr_t>(pg.v)) & 15) == 0 &&
+                  ((reinterpret_cast<uintptr_t>(pg.scale_k) | reinterpret_cast<uintptr_t>(pg.scale_v)) & 3) == 0;
+        }
+        int64_t gx;
+        if (vec) {
+            const int ppw = V == 8 ? 2 : 4;
+            const int64_t passes = ((int64_t)max_rows * D + 32 * V - 1) / (32 * V);
+            gx = (((passes + ppw - 1) / ppw) * BH + kPagedWarps - 1) / kPagedWarps;
+        } else {
+            gx = ((int64_t)max_rows * BH + kPagedWarps - 1) / kPagedWarps;
+        }
         if (gx > 0x7fffffff) return fail(SKV_ERR_TOO_LARGE, "paged_write: grid too large");
         const dim3 grid((unsigned)gx, (unsigned)n);
+        const int threads = kPagedWarps * kWarp;
         if (n <= kPagedFewWrites) {
             PagedWrites<kPagedFewWrites> ws;
             for (int i = 0; i < n; ++i) ws.w[i] = writes[base + i];
-            paged_write_kernel<kPagedFewWrites><<<grid, kPagedWarps * kWarp, smem, st>>>(k, v, BH, T_src, D, G, ws,
-                                                                                        table);
+            if (!vec)
+                paged_write_kernel<kPagedFewWrites><<<grid, threads, smem, st>>>(k, v, BH, T_src, D, G, ws, table);
+            else if (V == 4)
+                paged_write_vec_kernel<4, 4, kPagedFewWrites><<<grid, threads, 0, st>>>(k, v, BH, T_src, D, G, ws, table);
+            else
+                paged_write_vec_kernel<8, 2, kPagedFewWrites><<<grid, threads, 0, st>>>(k, v, BH, T_src, D, G, ws, table);
         } else {
             static PagedWrites<kPagedManyWrites> ws;   // 22.5 KB: kept off the host stack
             static std::mutex mu;
             std::lock_guard<std::mutex> lock(mu);
             for (int i = 0; i < n; ++i) ws.w[i] = writes[base + i];
-            paged_write_kernel<kPagedManyWrites><<<grid, kPagedWarps * kWarp, smem, st>>>(k, v, BH, T_src, D, G, ws,
-                                                                                         table);
+            if (!vec)
+                paged_write_kernel<kPagedManyWrites><<<grid, threads, smem, st>>>(k, v, BH, T_src, D, G, ws, table);
+            else if (V == 4)
+                paged_write_vec_kernel<4, 4, kPagedManyWrites><<<grid, threads, 0, st>>>(k, v, BH, T_src, D, G, ws,
+                                                                                        table);
+            else
+                paged_write_vec_kernel<8, 2, kPagedManyWrites><<<grid, threads, 0, st>>>(k, v, BH, T_src, D, G, ws,
+                                                                                        table);
         }
         const int rc = check_launch("paged_write");
         if (rc != SKV_OK) return rc;
@@ -360,7 +510,8 @@ int skv_paged_gather(const skv_page_desc* table, int n_pages, int B, int H, int 
     }
     const dim3 grid((unsigned)n_pages + 1, (unsigned)(B * H), (unsigned)parts);
     cudaStream_t st = as_stream(stream);
-    if (D % 8 == 0 && G % 8 == 0)
+    const bool out_aligned = ((reinterpret_cast<uintptr_t>(k_out) | reinterpret_cast<uintptr_t>(v_out)) & 15) == 0;
+    if (D % 8 == 0 && G % 8 == 0 && out_aligned)
         paged_gather_kernel<true><<<grid, 256, 0, st>>>(table, n_pages, D, G, s_out, part, k_out, v_out);
     else
         paged_gather_kernel<false><<<grid, 256, 0, st>>>(table, n_pages, D, G, s_out, part, k_out, v_out);

@@ -26,7 +26,9 @@ memory returns to the allocator when no page of that slab remains).
 from __future__ import annotations
 
 import bisect
+import ctypes
 import operator
+import struct
 from typing import Any, Dict, List, Optional, Set, Tuple
 
 import numpy as np
@@ -38,6 +40,7 @@ from .._device import as_device, compute_device, device_ctx, on
 _PRECISIONS = ("fp32", "fp16", "int8", "int4")
 _CODE = {"fp32": 0, "fp16": 1, "int8": 2, "int4": 3}
 _PAYLOAD_DTYPE = {"fp32": torch.float32, "fp16": torch.float16, "int8": torch.int8, "int4": torch.uint8}
+_PAYLOAD_BYTES = {"fp32": 4, "fp16": 2, "int8": 1, "int4": 1}
 _RESIDENT_TOKEN_HEAD = 48          # metadata bytes per (batch, head, token) (paged_kv_store.py:545-554)
 _RESIDENT_SLOT = 16                # page-table bytes per pool slot
 
@@ -46,21 +49,57 @@ _DESC = np.dtype([("k", "<u8"), ("v", "<u8"), ("scale_k", "<u8"), ("scale_v", "<
 _WRITE = np.dtype([("page", _DESC), ("src_token", "<i8"), ("dst_row", "<i4"), ("rows", "<i4"),
                    ("table_pos", "<i4"), ("reserved", "<i4")])
 assert _DESC.itemsize == 64 and _WRITE.itemsize == 88
+# the same records as flat structs (faster than numpy field access for a few records)
+_DESC_S = struct.Struct("<QQQQqiiiiii")
+_WRITE_S = struct.Struct("<QQQQqiiiiiiqiiii")
+assert _DESC_S.size == 64 and _WRITE_S.size == 88
 
 
 class _Chunk:
-    """Slabs of the pages one append opens: K, V payload ``[n, B, H, cap, row]`` and, for int8 /
-    int4, fp32 scales ``[n, B, H, cap, 1]`` / ``[n, B, H, cap, G, 1]``; host copies of their base
-    addresses and strides so page descriptors are plain arithmetic."""
+    """Slabs of the pages one append opens, in ONE device allocation: K and V payload
+    ``[n, B, H, cap, row]`` and, for int8 / int4, fp32 scales ``[n, B, H, cap, 1]`` /
+    ``[n, B, H, cap, G, 1]``, each part 256-byte aligned.  Base addresses and strides are
+    kept on the host so page descriptors are plain arithmetic; the typed tensors are built
+    only when a page's tensors are looked at."""
 
-    __slots__ = ("t", "ptr", "page_bytes", "row_bytes", "cap")
+    __slots__ = ("buf", "parts", "ptr", "page_bytes", "row_bytes", "cap", "_t")
 
-    def __init__(self, tensors: Tuple[Optional[torch.Tensor], ...]) -> None:
-        self.t = tensors
-        self.ptr = tuple(0 if x is None else x.data_ptr() for x in tensors)
-        self.page_bytes = tuple(0 if x is None else x.stride(0) * x.element_size() for x in tensors)
-        self.row_bytes = tuple(0 if x is None else x.stride(3) * x.element_size() for x in tensors)
-        self.cap = tensors[0].shape[3]
+    def __init__(self, precision: str, n: int, B: int, H: int, P: int, D: int, groups: int,
+                 dev: torch.device) -> None:
+        dt = _PAYLOAD_DTYPE[precision]
+        esz = _PAYLOAD_BYTES[precision]
+        row = (D + 1) // 2 if precision == "int4" else D
+        parts: List[Optional[Tuple[torch.dtype, Tuple[int, ...], int]]] = [(dt, (n, B, H, P, row), row * esz)] * 2
+        if precision == "int8":
+            parts += [(torch.float32, (n, B, H, P, 1), 4)] * 2
+        elif precision == "int4":
+            parts += [(torch.float32, (n, B, H, P, groups, 1), 4 * groups)] * 2
+        else:
+            parts += [None, None]
+        offs, total = [], 0
+        for part in parts:
+            offs.append(total)
+            if part is not None:
+                total += -(-(n * B * H * P * part[2]) // 256) * 256
+        self.buf = torch.empty(max(total, 256), dtype=torch.uint8, device=dev)
+        base = self.buf.data_ptr()
+        self.parts = [None if part is None else (part[0], part[1], off) for part, off in zip(parts, offs)]
+        self.ptr = tuple(0 if part is None else base + off for part, off in zip(parts, offs))
+        self.page_bytes = tuple(0 if part is None else B * H * P * part[2] for part in parts)
+        self.row_bytes = tuple(0 if part is None else part[2] for part in parts)
+        self.cap = P
+        self._t: List[Optional[torch.Tensor]] = [None, None, None, None]
+
+    def tensor(self, i: int) -> Optional[torch.Tensor]:
+        """Part ``i`` (0 K, 1 V, 2 K scales, 3 V scales) as a typed tensor ``[n, B, H, cap, ...]``."""
+        part = self.parts[i]
+        if part is None:
+            return None
+        if self._t[i] is None:
+            dt, shape, off = part
+            nbytes = self.page_bytes[i] * shape[0]
+            self._t[i] = self.buf[off:off + nbytes].view(dt).view(shape)
+        return self._t[i]
 
 
 class _Page:
@@ -73,6 +112,7 @@ class _Page:
     __slots__ = ("precision", "start_token", "num_tokens", "sealed", "_chunk", "_idx", "_row0", "_host_device",
                  "_ver", "_host")
 
+
     def __init__(self, precision: str, chunk: _Chunk, idx: int, row0: int, start_token: int, num_tokens: int,
                  sealed: bool, host_device: Optional[torch.device]) -> None:
         self.precision = precision
@@ -84,19 +124,21 @@ class _Page:
         self.sealed = sealed
         self._host_device = host_device
         self._ver = 0
-        self._host: List[Optional[Tuple[int, torch.Tensor]]] = [None, None, None, None]
+        self._host: Optional[List[Optional[Tuple[int, torch.Tensor]]]] = None
 
     @property
     def end_token(self) -> int:
         return self.start_token + self.num_tokens
 
     def _view(self, i: int) -> Optional[torch.Tensor]:
-        t = self._chunk.t[i]
+        t = self._chunk.tensor(i)
         if t is None:
             return None
         v = t[self._idx, :, :, self._row0:self._row0 + self.num_tokens]
         if self._host_device is None:
             return v
+        if self._host is None:
+            self._host = [None, None, None, None]
         cached = self._host[i]
         if cached is not None and cached[0] == self._ver:
             return cached[1]
@@ -123,15 +165,16 @@ class _Page:
     def scale_v(self) -> Optional[torch.Tensor]:
         return self._view(3)
 
-    def _desc(self, out: np.ndarray) -> None:
-        """Fill one ``skv_page_desc`` record for the page's current rows."""
+    def _fields(self) -> Tuple[int, int, int, int, int, int, int, int]:
+        """The ``skv_page_desc`` fields of the page's current rows: k, v, scale_k, scale_v,
+        start_token, num_tokens, row_stride, precision."""
         c = self._chunk
-        for i, name in enumerate(("k", "v", "scale_k", "scale_v")):
-            out[name] = c.ptr[i] + self._idx * c.page_bytes[i] + self._row0 * c.row_bytes[i] if c.ptr[i] else 0
-        out["start_token"] = self.start_token
-        out["num_tokens"] = self.num_tokens
-        out["row_stride"] = c.cap
-        out["precision"] = _CODE[self.precision]
+        i, r = self._idx, self._row0
+        p = c.ptr
+        return (p[0] + i * c.page_bytes[0] + r * c.row_bytes[0], p[1] + i * c.page_bytes[1] + r * c.row_bytes[1],
+                p[2] + i * c.page_bytes[2] + r * c.row_bytes[2] if p[2] else 0,
+                p[3] + i * c.page_bytes[3] + r * c.row_bytes[3] if p[3] else 0,
+                self.start_token, self.num_tokens, c.cap, _CODE[self.precision])
 
 
 def _as_index(x: Any) -> Optional[int]:
@@ -271,12 +314,15 @@ class PagedKVStore:
         B, H, T = int(k_new.shape[0]), int(k_new.shape[1]), int(k_new.shape[2])
 
         def rows_stride(t: torch.Tensor) -> Optional[int]:
-            if t.device != dev or t.dtype != torch.float32 or t.stride(3) != 1 or t.stride(2) != D:
+            if t.dtype != torch.float32 or not t.is_cuda or t.get_device() != dev.index or t.data_ptr() % 16:
+                return None
+            st = t.stride()
+            if st[3] != 1 or st[2] != D:
                 return None
             if B * H == 1:
                 return T
-            s = t.stride(0) if H == 1 else t.stride(1)
-            if H > 1 and B > 1 and t.stride(0) != H * s:
+            s = st[0] if H == 1 else st[1]
+            if H > 1 and B > 1 and st[0] != H * s:
                 return None
             return s // D if s % D == 0 and s // D >= T else None
 
@@ -290,22 +336,9 @@ class PagedKVStore:
         return None if self._dev.type == "cuda" else self._dev
 
     def _new_chunk(self, precision: str, n_pages: int, dev: torch.device) -> _Chunk:
-        """Slabs of ``n_pages`` new pages, one allocation per tensor kind."""
-        B, H, P, D = self.batch_size, self.num_heads, self.page_size, self.head_dim
-        row = (D + 1) // 2 if precision == "int4" else D
-        dt = _PAYLOAD_DTYPE[precision]
-        k = torch.empty(n_pages, B, H, P, row, dtype=dt, device=dev)
-        v = torch.empty(n_pages, B, H, P, row, dtype=dt, device=dev)
-        if precision == "int8":
-            sk = torch.empty(n_pages, B, H, P, 1, dtype=torch.float32, device=dev)
-            sv = torch.empty(n_pages, B, H, P, 1, dtype=torch.float32, device=dev)
-        elif precision == "int4":
-            ng = D // self._int4_effective_group
-            sk = torch.empty(n_pages, B, H, P, ng, 1, dtype=torch.float32, device=dev)
-            sv = torch.empty(n_pages, B, H, P, ng, 1, dtype=torch.float32, device=dev)
-        else:
-            sk = sv = None
-        return _Chunk((k, v, sk, sv))
+        """Slabs of ``n_pages`` new pages (one allocation)."""
+        return _Chunk(precision, n_pages, self.batch_size, self.num_heads, self.page_size, self.head_dim,
+                      self.head_dim // self._int4_effective_group, dev)
 
     def _table_capacity(self, n: int, dev: torch.device) -> torch.Tensor:
         """The device page table, grown (contents kept) to hold ``n`` descriptors."""
@@ -324,13 +357,16 @@ class PagedKVStore:
         table = self._table_capacity(max(n, 1), dev)
         if n == 0:
             return
-        arr = np.zeros(n, dtype=_DESC)
+        buf = bytearray(64 * n)
         for i, slot in enumerate(self._order):
-            self.pages[slot]._desc(arr[i:i + 1])
-        table[:n * 64].copy_(torch.from_numpy(arr.view(np.uint8)))
+            _DESC_S.pack_into(buf, 64 * i, *self.pages[slot]._fields(), 0, 0, 0)
+        table[:n * 64].copy_(torch.frombuffer(buf, dtype=torch.uint8))
 
-    def _launch_writes(self, k: torch.Tensor, v: torch.Tensor, t_src: int, writes: np.ndarray, dev: torch.device,
+    def _launch_writes(self, k: torch.Tensor, v: torch.Tensor, t_src: int, writes: bytearray, dev: torch.device,
                        update_table: bool) -> None:
+        """One ``skv_paged_write`` over ``writes`` (packed ``skv_page_write`` records)."""
+        n = len(writes) // 88
+        rec = (ctypes.c_char * len(writes)).from_buffer(writes)
         lib = _lib.load()
         table = self._table_capacity(len(self._order), dev) if update_table else None
         ev = self._kernel_events
@@ -338,7 +374,7 @@ class PagedKVStore:
             if ev is not None:
                 ev[0].record()
             st = lib.skv_paged_write(_lib.ptr(k), _lib.ptr(v), self.batch_size, self.num_heads, t_src,
-                                     self.head_dim, self.int4_group_size, writes.ctypes.data, len(writes),
+                                     self.head_dim, self.int4_group_size, ctypes.addressof(rec), n,
                                      _lib.ptr(table), _lib.stream_of(dev))
             if ev is not None:
                 ev[1].record()
@@ -398,44 +434,35 @@ class PagedKVStore:
             if page._row0 + page.num_tokens + first > page._chunk.cap:
                 self._relocate(page, dev)
         n_new = -(-(tokens - first) // P)
-        writes = np.zeros((1 if first else 0) + n_new, dtype=_WRITE)
+        writes = bytearray(88 * ((1 if first else 0) + n_new))
         if first:
             page = self.pages[slot]
-            w = writes[0:1]
-            w["src_token"], w["dst_row"], w["rows"], w["table_pos"] = 0, page.num_tokens, first, len(self._order) - 1
+            dst_row = page.num_tokens
             page.num_tokens += first
             page.sealed = page.num_tokens == P
             page._ver += 1
-            page._desc(w["page"])
+            _WRITE_S.pack_into(writes, 0, *page._fields(), 0, 0, 0, 0, dst_row, first, len(self._order) - 1, 0)
             self._max_rows = max(self._max_rows, page.num_tokens)
             self._max_seq += first
         if n_new:
             chunk = self._new_chunk(precision, n_new, dev)
             prev_end = self.pages[self._order[-1]].end_token if self._order else 0
-            start0, pos0 = self._max_seq, len(self._order)
-            idx = np.arange(n_new, dtype=np.int64)
-            takes = np.minimum(P, tokens - first - idx * P)
-            w = writes[1 if first else 0:]
-            pg = w["page"]
-            for i, name in enumerate(("k", "v", "scale_k", "scale_v")):
-                if chunk.ptr[i]:
-                    pg[name] = chunk.ptr[i] + idx * chunk.page_bytes[i]
-            pg["start_token"] = start0 + idx * P
-            pg["num_tokens"] = takes
-            pg["row_stride"] = P
-            pg["precision"] = _CODE[precision]
-            w["src_token"] = first + idx * P
-            w["rows"] = takes
-            w["table_pos"] = pos0 + idx
+            start0, pos0, code = self._max_seq, len(self._order), _CODE[precision]
+            (pk, pv, psk, psv), (bk, bv, bsk, bsv) = chunk.ptr, chunk.page_bytes
             host = self._host_device()
-            for i, take in enumerate(takes.tolist()):
+            off = 88 if first else 0
+            for i in range(n_new):
+                take = min(P, tokens - first - i * P)
                 s = self._alloc_slot()
                 self._order.append(s)
                 self.pages[s] = _Page(precision, chunk, i, 0, start0 + i * P, take, take == P, host)
+                _WRITE_S.pack_into(writes, off + 88 * i, pk + i * bk, pv + i * bv, psk + i * bsk if psk else 0,
+                                   psv + i * bsv if psv else 0, start0 + i * P, take, P, code, 0, 0, 0,
+                                   first + i * P, 0, take, pos0 + i, 0)
             if start0 != prev_end:
                 self._contiguous = False
                 self._max_hole = max(self._max_hole, start0 - prev_end)
-            self._max_rows = max(self._max_rows, int(takes[0]))
+            self._max_rows = max(self._max_rows, min(P, tokens - first))
             self._max_seq += tokens - first
         self._launch_writes(k, v, t_src, writes, dev, update_table=True)
         self._appended_tokens += tokens
@@ -444,7 +471,8 @@ class PagedKVStore:
         """Give an open page (a survivor run that starts inside its slab) a slab of its own."""
         chunk = self._new_chunk(page.precision, 1, dev)
         n = page.num_tokens
-        for src, dst in zip(page._chunk.t, chunk.t):
+        for i in range(4):
+            src, dst = page._chunk.tensor(i), chunk.tensor(i)
             if src is not None:
                 dst[0, :, :, :n].copy_(src[page._idx, :, :, page._row0:page._row0 + n])
         page._chunk, page._idx, page._row0 = chunk, 0, 0
@@ -502,11 +530,9 @@ class PagedKVStore:
         hits = self._plan_rewrite(start, end, precision)
         dev = self._compute_device(k_new, v_new)
         k, v, t_src = self._sources(k_new, v_new, dev)
-        writes = np.zeros(len(hits), dtype=_WRITE)
+        writes = bytearray(88 * len(hits))
         for i, (page, a, b) in enumerate(hits):
-            w = writes[i:i + 1]
-            page._desc(w["page"])
-            w["src_token"], w["dst_row"], w["rows"], w["table_pos"] = a - start, a - page.start_token, b - a, -1
+            _WRITE_S.pack_into(writes, 88 * i, *page._fields(), 0, 0, 0, a - start, a - page.start_token, b - a, -1, 0)
             page._ver += 1
         self._launch_writes(k, v, t_src, writes, dev, update_table=False)
         self._rewritten_tokens += end - start

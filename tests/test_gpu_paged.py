@@ -104,6 +104,8 @@ def _random_script(rng, store, B, H, D, P, n_ops):
     (2, 2, 33, 5, 16, 50, 5),      # odd head_dim: scalar gather path, padded int4 rows
     (1, 2, 64, 12, 4, 50, 6),      # int4 groups of 4 lanes
     (1, 2, 48, 9, 24, 50, 7),      # int4 groups of 24 (shared-memory group maxima)
+    (1, 2, 256, 8, 16, 40, 8),     # 8 values per lane in the vector write path
+    (2, 2, 32, 4, 8, 40, 9),       # four rows per warp pass
 ])
 def test_random_scripts_match_oracle(skv, B, H, D, P, G, n_ops, seed):
     rng = np.random.default_rng(seed)
@@ -239,3 +241,26 @@ def test_clear_heads_flags_items_outside_the_table(skv):
         flag.zero_()
     after = store.gather()
     assert torch.equal(before[0], after[0]) and torch.equal(before[1], after[1])
+
+
+def test_misaligned_and_strided_sources(skv):
+    """A token slice of a larger tensor is read in place; a source that is not 16-byte aligned
+    is copied first; both give the rows an aligned contiguous tensor gives."""
+    B, H, T, D = 2, 3, 37, 64
+    k, v = _kv(21, B=B, H=H, S=T, D=D)
+    base_k = torch.zeros(B * H * T * D + 1, device="cuda")
+    base_v = torch.zeros_like(base_k)
+    base_k[1:] = k.reshape(-1)
+    base_v[1:] = v.reshape(-1)
+    odd_k, odd_v = base_k[1:].view(B, H, T, D), base_v[1:].view(B, H, T, D)
+    for precision in PRECISIONS:
+        a = skv.PagedKVStore(B, H, D, page_size=8, device="cuda")
+        b = skv.PagedKVStore(B, H, D, page_size=8, device="cuda")
+        c = skv.PagedKVStore(B, H, D, page_size=8, device="cuda")
+        a.append(k, v, precision)
+        b.append(odd_k, odd_v, precision)
+        c.append(k[:, :, :20], v[:, :, :20], precision)
+        c.append(k[:, :, 20:], v[:, :, 20:], precision)
+        ga, gb, gc = a.gather(), b.gather(), c.gather()
+        assert torch.equal(ga[0], gb[0]) and torch.equal(ga[1], gb[1]), precision
+        assert torch.equal(ga[0], gc[0]) and torch.equal(ga[1], gc[1]), precision

@@ -10,7 +10,7 @@ import torch
 
 from shadow_infer_b200 import _lib
 from shadow_infer_b200.shadowkv import PagedKVStore
-from shadow_infer_b200.shadowkv.paged_kv_store import _DESC, _WRITE
+from shadow_infer_b200.shadowkv.paged_kv_store import _DESC, _DESC_S, _WRITE, _WRITE_S
 
 
 def _store(**kw):
@@ -70,8 +70,13 @@ def test_zero_token_append_is_a_noop_and_rewrite_range_checks():
 
 
 def test_record_layouts_match_the_c_structs():
-    assert _DESC.itemsize == 64 and _WRITE.itemsize == 88
+    assert _DESC.itemsize == 64 and _WRITE.itemsize == 88 and _DESC_S.size == 64 and _WRITE_S.size == 88
     assert _WRITE.fields["src_token"][1] == 64 and _WRITE.fields["table_pos"][1] == 80
+    rec = np.frombuffer(_WRITE_S.pack(1, 2, 3, 4, 5, 6, 7, 3, 0, 0, 0, 8, 9, 10, 11, 0), dtype=_WRITE)[0]
+    assert (rec["page"]["k"], rec["page"]["scale_v"], rec["page"]["start_token"], rec["page"]["num_tokens"]) == \
+        (1, 4, 5, 6)
+    assert (rec["page"]["row_stride"], rec["page"]["precision"], rec["src_token"], rec["dst_row"], rec["rows"],
+            rec["table_pos"]) == (7, 3, 8, 9, 10, 11)
 
 
 def test_abi_page_write_checks():
