@@ -24,9 +24,11 @@ The line also carries ``attention``: packed attention over one cfg3 layer
 (B=1, H=32, S=4096, D=128, codes 20/50/30 % fp16/int8/int4), heads sharded over
 the ranks with an NCCL all-gather of the outputs, as tokens/s of the 32-layer
 stack and as tensor-core roofline of the kernel; ``global_budget``:
-KVCacheManager.enforce_global_budget over 8 packed layers of that shape; and
+KVCacheManager.enforce_global_budget over 8 packed layers of that shape;
 ``paged_store``: the PagedKVStore append-mode run of the reference's own paged
-benchmark shape plus its gather / append kernels at the cfg2 layer shape.
+benchmark shape plus its gather / append kernels at the cfg2 layer shape; and
+``decisions``: decide_reuse_per_token over the cfg2 layer and
+compute_irap_importance over cfg3-shaped attention probabilities.
 """
 
 from __future__ import annotations
@@ -56,9 +58,9 @@ def parse_args():
     ap.add_argument("--ref-heads", type=int, default=8, help="head slice timed by the CPU reference arm")
     ap.add_argument("--no-attention", action="store_true",
                     help="skip the packed-attention, global-budget and paged-store phases")
-    ap.add_argument("--phase", choices=("all", "paged", "paged-kernels"), default="all",
-                    help="'paged' / 'paged-kernels': print only the paged-store phase (all of it / its kernels "
-                         "at the cfg2 shape) as the JSON line; for profiling")
+    ap.add_argument("--phase", choices=("all", "paged", "paged-kernels", "decisions"), default="all",
+                    help="'paged' / 'paged-kernels' / 'decisions': print only that phase (the paged store, its "
+                         "kernels at the cfg2 shape, the decision inputs) as the JSON line; for profiling")
     return ap.parse_args()
 
 
@@ -525,6 +527,126 @@ def paged_phase(args, world, rank, dev, lib, run_mode=True):
     return res
 
 
+def decision_phase(args, world, rank, dev, lib):
+    """Decision inputs: decide_reuse_per_token over the cfg2 layer (current vs previous K/V,
+    B=1, H=32, S=8192, D=128) and compute_irap_importance over cfg3-shaped attention
+    probabilities (B=1, H=32, 4096 x 4096, 2.1 GB, with the previous step's EMA), CUDA events
+    around each call (every launch of it inside), inputs resident and larger than L2."""
+    import torch
+
+    from shadow_infer_b200 import workloads as W
+    from shadow_infer_b200.shadowkv import compute_irap_importance
+    from shadow_infer_b200.shadowkv.shadowkv_agent import decide_reuse_mask
+
+    I = W.cfg2_inputs(seed=rank)
+    k, v = I["k"].to(dev), I["v"].to(dev)
+    kp, vp = I["k_prev"].to(dev), I["v_prev"].to(dev)
+    imp = I["importance"].to(dev)
+    B, H, S, D = k.shape
+    reps = max(3, min(args.steps, 10))
+
+    def timed(fn):
+        out, ts = None, []
+        for i in range(2 + reps):
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            out = fn()
+            e1.record()
+            torch.cuda.synchronize()
+            if i >= 2:
+                ts.append(e0.elapsed_time(e1))
+        return out, statistics.median(ts)
+
+    from shadow_infer_b200 import _lib
+    from shadow_infer_b200.shadowkv.shadowkv_agent import reuse_threshold
+
+    n0 = lib.skv_launch_count()
+    (mask, stats), reuse_ms = timed(lambda: decide_reuse_mask(k, v, kp, vp, 4, 16, 0.2, "balanced", imp))
+    reuse_launches = (lib.skv_launch_count() - n0) // (2 + reps)
+    reuse_bytes = 4 * B * H * S * D * 4 + S * H * 4 + S * H
+    # the kernel alone: the C-ABI call with the buffers already allocated
+    m_out = torch.empty(S, H, dtype=torch.uint8, device=dev)
+    cnt = torch.empty(4, dtype=torch.int64, device=dev)
+    eff = reuse_threshold(4, 16, 0.2, "balanced")
+    stream = _lib.stream_of(dev)
+
+    def reuse_kernel():
+        _lib.check(lib.skv_reuse_decide(_lib.ptr(k), _lib.ptr(v), _lib.ptr(kp), _lib.ptr(vp), B, H, S, D,
+                                        _lib.ptr(imp), eff, _lib.ptr(m_out), None, _lib.ptr(cnt), stream), "bench")
+
+    _, reuse_kms = timed(reuse_kernel)
+    c3 = W.CONFIGS["cfg3"]
+    Hq, Sq = c3["H"], c3["S"]
+    g = torch.Generator(device=dev).manual_seed(77 + rank)
+    logits = torch.randn(1, Hq, Sq, Sq, device=dev, generator=g)
+    logits[:, :, : (3 * Sq) // 4] *= 6.0
+    probs = torch.softmax(logits, dim=-1)
+    del logits
+    prev = torch.rand(Sq, Hq, device=dev, generator=g) / Sq
+    n0 = lib.skv_launch_count()
+    (imp3, ema3, da), irap_ms = timed(lambda: compute_irap_importance(probs, prev, 0.9, 0.3, 4, 1, 32))
+    irap_launches = (lib.skv_launch_count() - n0) // (2 + reps)
+    irap_bytes = probs.numel() * 4
+    # the launches alone: the C-ABI call with scratch and outputs already allocated
+    scr = torch.empty(lib.skv_irap_scratch_bytes(1, Hq, Sq, Sq), dtype=torch.uint8, device=dev)
+    o_imp = torch.empty(Sq, Hq, device=dev)
+    o_ema = torch.empty(Sq, Hq, device=dev)
+    o_dp = torch.empty(2, dtype=torch.float64, device=dev)
+
+    def irap_kernels():
+        _lib.check(lib.skv_irap_importance(_lib.ptr(probs), 1, Hq, Sq, Sq, 0, _lib.ptr(prev), Sq, 0.9, 0.3, 4,
+                                           1.0 + 0.1 * (1 / 32), _lib.ptr(scr), scr.numel(), _lib.ptr(o_imp),
+                                           _lib.ptr(o_ema), _lib.ptr(o_dp), stream), "bench")
+
+    _, irap_kms = timed(irap_kernels)
+    peak, peak_kind = hbm_peak()
+    res = {
+        "reuse_decision": {
+            "workload": "cfg2 layer B1 H32 S8192 D128, current vs previous K/V, balanced, step 4/16",
+            "ms": reuse_ms, "GB/s": reuse_bytes / (reuse_ms / 1e3) / 1e9, "gpu_launches": reuse_launches,
+            "kernel_ms": reuse_kms, "reuse_ratio": stats["reuse_ratio"],
+            "roofline": {"kernel": "reuse_decide_kernel", "bound": "hbm", "algorithmic_bytes": reuse_bytes,
+                         "achieved": reuse_bytes / (reuse_kms / 1e3) / 1e9, "peak": peak, "unit": "GB/s",
+                         "frac": reuse_bytes / (reuse_kms / 1e3) / 1e9 / peak, "peak_source": f"{peak_kind} hbm_gbs",
+                         "traffic": committed_traffic("reuse_decide_kernel_cfg2.md")},
+        },
+        "irap_importance": {
+            "workload": f"attention probabilities [1,{Hq},{Sq},{Sq}] fp32 (cfg3 layer) with the previous EMA",
+            "ms": irap_ms, "GB/s": irap_bytes / (irap_ms / 1e3) / 1e9, "gpu_launches": irap_launches,
+            "kernels_ms": irap_kms,
+            "roofline": {"kernel": "irap_pass_kernel + columns, delta and rank kernels (one ABI call)",
+                         "bound": "hbm", "algorithmic_bytes": irap_bytes,
+                         "achieved": irap_bytes / (irap_kms / 1e3) / 1e9, "peak": peak, "unit": "GB/s",
+                         "frac": irap_bytes / (irap_kms / 1e3) / 1e9 / peak, "peak_source": f"{peak_kind} hbm_gbs",
+                         "traffic": committed_traffic("irap_pass_kernel_cfg3.md")},
+        },
+    }
+    if world == 1 and rank == 0:
+        import numpy as np
+
+        from oracle import decision_oracle as DO
+
+        hs = 2
+        kk, vv, kkp, vvp = (t[:, :hs].cpu().numpy() for t in (k, v, kp, vp))
+        ii = imp[:, :hs].cpu().numpy()
+        t0 = time.perf_counter()
+        DO.decide_reuse_per_token(kk, vv, kkp, vvp, 4, 16, 0.2, "balanced", ii)
+        dt_r = time.perf_counter() - t0
+        pw = probs[:, :1].cpu().numpy()
+        t0 = time.perf_counter()
+        DO.compute_irap_importance(pw, prev[:, :1].cpu().numpy(), 0.9, 0.3, 4, 1, 32)
+        dt_i = time.perf_counter() - t0
+        res["reuse_decision"]["cpu_baseline"] = {
+            "value": (reuse_bytes * hs / H) / dt_r / 1e9, "unit": "GB/s", "cores": 1, "kind": "port",
+            "sample": f"numpy oracle on heads 0..{hs - 1} of the cfg2 layer"}
+        res["irap_importance"]["cpu_baseline"] = {
+            "value": (irap_bytes / Hq) / dt_i / 1e9, "unit": "GB/s", "cores": 1, "kind": "port",
+            "sample": "numpy oracle on head 0 of the cfg3 probabilities"}
+        del np
+    return res
+
+
 def tensor_peak():
     path = os.path.join(REPO, "MEASURED_PEAKS.json")
     try:
@@ -555,11 +677,14 @@ def run_b200(args):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     lib = _lib.load()
     if args.phase != "all":
-        res = paged_phase(args, world, rank, dev, lib, run_mode=args.phase == "paged")
+        if args.phase == "decisions":
+            res = decision_phase(args, world, rank, dev, lib)
+        else:
+            res = paged_phase(args, world, rank, dev, lib, run_mode=args.phase == "paged")
         if world > 1:
             dist.destroy_process_group()
         if rank == 0:
-            print(json.dumps({"phase": args.phase, "paged_store": res}), flush=True)
+            print(json.dumps({"phase": args.phase, "result": res}), flush=True)
         return 0
 
     # every rank packs its own layer: seed = rank
@@ -682,6 +807,7 @@ def run_b200(args):
     attn = attention_phase(args, world, rank, dev, dist, lib, tensor_peak()) if not args.no_attention else None
     gbudget = budget_phase(args, world, rank, dev, lib) if not args.no_attention else None
     paged = paged_phase(args, world, rank, dev, lib) if not args.no_attention else None
+    decisions = decision_phase(args, world, rank, dev, lib) if not args.no_attention else None
     if sampler:
         sampler.stop()
 
@@ -715,6 +841,7 @@ def run_b200(args):
         "attention": attn,
         "global_budget": gbudget,
         "paged_store": paged,
+        "decisions": decisions,
     }
     if world == 1:
         run = reference_sample(I, args.ref_heads)

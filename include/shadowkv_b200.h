@@ -248,6 +248,31 @@ int skv_paged_gather(const skv_page_desc* table, int n_pages, int B, int H, int 
 int skv_paged_clear_heads(const skv_page_desc* table, int n_pages, const int32_t* items, int64_t n_items, int B,
                           int H, int D, int* error_flag, void* stream);
 
+/* ---------------------------------------------------------------------------------------
+ * Decision inputs of the agent
+ * ------------------------------------------------------------------------------------- */
+/* ShadowKVAgent.decide_reuse_per_token  (shadowinfer/shadowkv/shadowkv_agent.py:1165-1256):
+ * K/V float [B,H,S,D] of the current and previous step, importance float [S,H];
+ * effective_threshold = base(mode) * (1 - 0.5*progress) * (1 - 0.3*qdrift) as the reference
+ * computes it on the host.  mask uint8 [S,H] = drift < max(thr * (1 - 0.3*clamp(imp,0,1)), 1e-5);
+ * drift float [S,H] (may be NULL); counts int64[4] (device) = {full-reuse tokens, partial,
+ * none, reused entries}. */
+int skv_reuse_decide(const float* k_cur, const float* v_cur, const float* k_prev, const float* v_prev, int B, int H,
+                     int S, int D, const float* importance, double effective_threshold, uint8_t* mask, float* drift,
+                     int64_t* counts, void* stream);
+
+/* compute_irap_importance  (shadowinfer/shadowkv/importance_model.py:37-134) with the agent's input
+ * contract (shadowkv_agent.py:894-965): scores float [B,H,Sq,Sk]; input_mode 0 = probabilities
+ * used as given, 1 = logits (softmax of the NaN-cleaned rows), 2 = probabilities divided by
+ * their row sum clamped to 1e-10.  ema_prev float [S_prev,H] or NULL (cold start).
+ * importance, ema float [Sk,H]; delta_parts double[2] (device) = {sum (ema - prev)^2,
+ * sum prev^2} for delta_a.  Ties in the EMA rank by token index. */
+size_t skv_irap_scratch_bytes(int B, int H, int Sq, int Sk);
+int skv_irap_importance(const float* scores, int B, int H, int Sq, int Sk, int input_mode, const float* ema_prev,
+                        int S_prev, double irap_decay, double entropy_weight, int sink_tokens, double layer_factor,
+                        void* scratch, size_t scratch_bytes, float* importance, float* ema, double* delta_parts,
+                        void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -97,6 +97,12 @@ _SIGNATURES = {
     "skv_paged_gather": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_int, c_int64, c_int64, c_void_p, c_void_p,
                                  c_void_p]),
     "skv_paged_clear_heads": (c_int, [c_void_p, c_int, c_void_p, c_int64, c_int, c_int, c_int, c_void_p, c_void_p]),
+    "skv_reuse_decide": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p,
+                                 ctypes.c_double, c_void_p, c_void_p, c_void_p, c_void_p]),
+    "skv_irap_scratch_bytes": (c_size_t, [c_int, c_int, c_int, c_int]),
+    "skv_irap_importance": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_int, c_void_p, c_int, ctypes.c_double,
+                                    ctypes.c_double, c_int, ctypes.c_double, c_void_p, c_size_t, c_void_p, c_void_p,
+                                    c_void_p, c_void_p]),
 }
 
 EXPORTED_SYMBOLS = tuple(_SIGNATURES.keys())

@@ -8,6 +8,7 @@ from .kv_cache_manager import (
     LeastImportantEvictionPolicy,
     TokenHeadScore,
 )
+from .importance_model import compute_irap_importance
 from .packed_attention import packed_attention
 from .packed_kv_cache import PackedKVCache
 from .paged_kv_store import PagedKVStore
@@ -27,4 +28,5 @@ __all__ = [
     "CODE_PRECISIONS", "EVICTED", "admit_codes", "admit_budget", "entry_bytes", "kv_sensitivity",
     "predict_codes_bytes", "packed_attention", "KVCacheManager", "KVCacheEntry", "TokenHeadScore",
     "EvictionPolicy", "LeastImportantEvictionPolicy", "ImportanceAgeEvictionPolicy", "PagedKVStore",
+    "compute_irap_importance",
 ]

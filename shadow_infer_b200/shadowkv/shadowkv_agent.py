@@ -1,11 +1,13 @@
 """Data-plane methods of ``ShadowKVAgent`` (shadowinfer/shadowkv/shadowkv_agent.py).
 
-Only the hot-path methods of the reference agent are provided --
+Only the data-plane methods of the reference agent are provided --
 ``allocate_precision_codes`` (:1028-1059), ``_admit_precision_codes``
-(:679-743), ``compress_kv`` (:1445-1584) and ``_compress_kv_with_plan``
-(:1698-1809) -- with the reference's signatures and return dictionaries.  The
-agent's policy logic (IRAP importance, reuse decisions, stats, prefetch,
-``on_step``) is outside this package.
+(:679-743), ``compress_kv`` (:1445-1584), ``_compress_kv_with_plan``
+(:1698-1809), and the decision inputs ``decide_reuse_per_token`` (:1165-1256),
+``_compute_importance_matrix`` / ``_compute_importance_with_state`` (:899-965,
+IRAP importance) and ``_row_normalize`` (:893-897) -- with the reference's
+signatures and return values.  The agent's policy logic (stats, prefetch,
+``on_step`` orchestration) is outside this package.
 
 ``compress_kv`` builds the plan on the GPU and runs ONE fused kernel that
 writes both the packed buckets and the dense working copy (``k``/``v`` of the
@@ -15,12 +17,13 @@ zeros for evicted entries, previous-step rows for reused entries).
 
 from __future__ import annotations
 
-from typing import Any, Dict, Optional, Set, Tuple
+from typing import Any, Dict, List, Optional, Set, Tuple
 
 import torch
 
 from .. import _lib
 from .._device import back, compute_device, on, device_ctx
+from .importance_model import INPUT_LOGITS, INPUT_UNNORMALISED, irap_importance
 from .packed_kv_cache import PackedKVCache, run_pack
 from .precision_plan import PRECISION_ORDER, PrecisionPlan
 from .rd_allocator import admit_codes, kv_sensitivity, predict_codes_bytes
@@ -39,6 +42,59 @@ def allocate_precision_codes(importance_map: torch.Tensor, mode: str) -> torch.T
                                     _lib.stream_of(dev))
     _lib.check(st, "allocate_precision_codes")
     return back(out, importance_map.device)
+
+
+_REUSE_BASE = {"aggressive": 0.20, "balanced": 0.15, "conservative": 0.10}
+
+
+def reuse_threshold(step_id: int, total_steps: int, qdrift_drift_score: float, mode: str) -> float:
+    """Effective drift threshold before the importance term (shadowkv_agent.py:1222-1231)."""
+    progress = step_id / max(total_steps, 1)
+    adaptive = _REUSE_BASE.get(mode, 0.15) * (1.0 - 0.5 * progress)
+    return adaptive * (1.0 - qdrift_drift_score * 0.3)
+
+
+def decide_reuse_mask(
+    kv_current_k: torch.Tensor,
+    kv_current_v: torch.Tensor,
+    kv_previous_k: torch.Tensor,
+    kv_previous_v: torch.Tensor,
+    step_id: int,
+    total_steps: int,
+    qdrift_drift_score: float,
+    mode: str,
+    importance_map: torch.Tensor,
+    return_drift: bool = False,
+):
+    """``decide_reuse_per_token`` as a device mask: (bool ``[seq, heads]``, stats[, drift ``[seq,
+    heads]``]) on the compute device, without building the ``{(t, h): bool}`` dict.
+
+    drift = (|k - k_prev| / (|k| + 1e-8) + |v - v_prev| / (|v| + 1e-8)) / 2 per (token, head),
+    norms over (batch, head_dim); reuse where drift < max(thr * (1 - 0.3 * clamp(imp, 0, 1)), 1e-5).
+    """
+    B, H, S, D = (int(x) for x in kv_current_k.shape)
+    for t in (kv_current_v, kv_previous_k, kv_previous_v):
+        if tuple(t.shape) != (B, H, S, D):
+            raise ValueError("current and previous K/V must have the same [batch, heads, seq, head_dim] shape")
+    if tuple(importance_map.shape) != (S, H):
+        raise ValueError(f"importance_map must be [seq, heads] = [{S}, {H}], got {tuple(importance_map.shape)}")
+    dev = compute_device(kv_current_k, kv_current_v, kv_previous_k, kv_previous_v, importance_map)
+    kc, vc, kp, vp = (on(t.detach(), dev, torch.float32) for t in (kv_current_k, kv_current_v, kv_previous_k,
+                                                                   kv_previous_v))
+    imp = on(importance_map.detach(), dev, torch.float32)
+    mask = torch.empty(S, H, dtype=torch.bool, device=dev)
+    drift = torch.empty(S, H, dtype=torch.float32, device=dev) if return_drift else None
+    counts = torch.empty(4, dtype=torch.int64, device=dev)
+    eff = reuse_threshold(step_id, total_steps, qdrift_drift_score, mode)
+    lib = _lib.load()
+    with device_ctx(dev):
+        st = lib.skv_reuse_decide(_lib.ptr(kc), _lib.ptr(vc), _lib.ptr(kp), _lib.ptr(vp), B, H, S, D, _lib.ptr(imp),
+                                  eff, _lib.ptr(mask), _lib.ptr(drift), _lib.ptr(counts), _lib.stream_of(dev))
+    _lib.check(st, "decide_reuse_per_token")
+    full, partial, none, reused = counts.tolist()
+    stats = {"full_reuse_count": float(full), "partial_reuse_count": float(partial),
+             "no_reuse_count": float(none), "reuse_ratio": float(reused / max(S * H, 1))}
+    return (mask, stats, drift) if return_drift else (mask, stats)
 
 
 class ShadowKVAgent:
@@ -73,6 +129,67 @@ class ShadowKVAgent:
 
     def allocate_precision_codes(self, importance_map: torch.Tensor, mode: str) -> torch.Tensor:
         return allocate_precision_codes(importance_map, mode)
+
+    # ---------------------------------------------------------------- decision inputs
+    def decide_reuse_per_token(
+        self,
+        kv_current_k: torch.Tensor,
+        kv_current_v: torch.Tensor,
+        kv_previous_k: torch.Tensor,
+        kv_previous_v: torch.Tensor,
+        step_id: int,
+        total_steps: int,
+        qdrift_drift_score: float,
+        mode: str,
+        importance_map: torch.Tensor,
+    ) -> Tuple[Dict[Tuple[int, int], bool], Dict[str, float]]:
+        """Per-(token, head) KV reuse decision (shadowkv_agent.py:1165-1256): the drift and the
+        threshold comparison run on the GPU (``decide_reuse_mask``); the returned dict and stats
+        are the reference's."""
+        mask, stats = decide_reuse_mask(kv_current_k, kv_current_v, kv_previous_k, kv_previous_v, step_id,
+                                        total_steps, qdrift_drift_score, mode, importance_map)
+        S, H = mask.shape
+        flags: List[bool] = mask.reshape(-1).tolist()
+        keys = [(t, h) for t in range(S) for h in range(H)]
+        return dict(zip(keys, flags)), stats
+
+    @staticmethod
+    def _row_normalize(tensor: torch.Tensor) -> torch.Tensor:
+        """Row-sum correction of probability inputs (shadowkv_agent.py:893-897)."""
+        return tensor / tensor.sum(dim=-1, keepdim=True).clamp(min=1e-10)
+
+    def _compute_importance_with_state(
+        self,
+        attention_scores: torch.Tensor,
+        layer_index: int,
+        num_layers: int,
+        attn_is_probabilities: bool = False,
+        received_ema=None,
+        irap_decay: float = 0.9,
+        entropy_weight: float = 0.3,
+        sink_tokens: int = 4,
+    ) -> Tuple[torch.Tensor, torch.Tensor, Optional[float]]:
+        """Importance + new EMA state + delta A (shadowkv_agent.py:940-965): probabilities get the
+        row-sum correction, logits a softmax of the NaN-cleaned rows, both fused into the IRAP
+        pass on the GPU."""
+        mode = INPUT_UNNORMALISED if attn_is_probabilities else INPUT_LOGITS
+        return irap_importance(attention_scores, mode, received_ema, irap_decay, entropy_weight, sink_tokens,
+                               layer_index, num_layers)
+
+    def _compute_importance_matrix(
+        self,
+        attention_scores: torch.Tensor,
+        layer_index: int,
+        num_layers: int,
+        attn_is_probabilities: bool = False,
+        received_ema=None,
+        irap_decay: float = 0.9,
+        entropy_weight: float = 0.3,
+        sink_tokens: int = 4,
+    ) -> torch.Tensor:
+        """Importance ``[seq_k, heads]`` only (shadowkv_agent.py:899-938)."""
+        return self._compute_importance_with_state(attention_scores, layer_index, num_layers, attn_is_probabilities,
+                                                   received_ema, irap_decay, entropy_weight, sink_tokens)[0]
 
     def _admit_precision_codes(
         self,

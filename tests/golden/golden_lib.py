@@ -140,3 +140,46 @@ def paged_apply(store, op, B: int, H: int, D: int, conv):
     if name == "validate":
         return store.validate_against(*op[1:])
     raise ValueError(f"unknown scripted operation {name}")
+
+
+# ---------------------------------------------------------------------- decision inputs
+def irap_scores(seed: int, B: int, H: int, Sq: int, Sk: int, kind: str = "probs", sharpen: float = 6.0,
+                bad: bool = False) -> np.ndarray:
+    """Seeded attention input ``[B,H,Sq,Sk]`` fp32: ``logits`` = N(0,1) with 3/4 of the query
+    rows sharpened; ``probs`` = their row softmax; ``raw`` = unnormalised non-negative rows
+    (some all-zero).  ``bad`` plants NaN / +-inf entries."""
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal((B, H, Sq, Sk)).astype(np.float64)
+    x[:, :, : (3 * Sq) // 4] *= sharpen
+    if kind == "probs":
+        e = np.exp(x - x.max(axis=-1, keepdims=True))
+        x = e / e.sum(axis=-1, keepdims=True)
+    elif kind == "raw":
+        x = np.abs(x) * rng.random((B, H, Sq, 1))
+        x[:, :, rng.random(Sq) < 0.05] = 0.0
+    x = x.astype(np.float32)
+    if bad:
+        flat = x.reshape(-1)
+        idx = rng.choice(flat.size, size=max(3, flat.size // 2000), replace=False)
+        flat[idx[0::3]] = np.nan
+        flat[idx[1::3]] = np.inf
+        flat[idx[2::3]] = -np.inf
+    return x
+
+
+def reuse_inputs(seed: int, B: int, H: int, S: int, D: int):
+    """Seeded (k_cur, v_cur, k_prev, v_prev, importance): the previous step's K/V drift by a
+    per-(token, head) relative amount spread around the reuse thresholds; a few rows exactly
+    zero; importance in [-0.1, 1.1] (clamped by the reference)."""
+    rng = np.random.default_rng(seed)
+    k = rng.standard_normal((B, H, S, D)).astype(np.float32)
+    v = rng.standard_normal((B, H, S, D)).astype(np.float32)
+    rk = np.abs(rng.normal(0.0, 0.12, (1, H, S, 1))).astype(np.float32)
+    rv = np.abs(rng.normal(0.0, 0.12, (1, H, S, 1))).astype(np.float32)
+    kp = (k + rk * rng.standard_normal((B, H, S, D)).astype(np.float32)).astype(np.float32)
+    vp = (v + rv * rng.standard_normal((B, H, S, D)).astype(np.float32)).astype(np.float32)
+    zero = rng.random((H, S)) < 0.01
+    k[:, zero] = 0.0
+    kp[:, zero] = 0.0
+    imp = (rng.random((S, H)) * 1.2 - 0.1).astype(np.float32)
+    return k, v, kp, vp, imp

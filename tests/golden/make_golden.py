@@ -32,8 +32,8 @@ REPO = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, REPO)
 sys.path.insert(0, HERE)
 
-from golden_lib import (PINS_JSON, SMALL_NPZ, array_digest, packed_summary, paged_apply,  # noqa: E402
-                        state_digest, to_numpy)
+from golden_lib import (PINS_JSON, SMALL_NPZ, array_digest, irap_scores, packed_summary,  # noqa: E402
+                        paged_apply, reuse_inputs, state_digest, to_numpy)
 
 from shadow_infer_b200 import workloads as W  # noqa: E402
 
@@ -45,9 +45,10 @@ def _import_reference(path: str):
     sys.path.insert(0, path)
     from shadowinfer.shadowkv import rd_allocator, precision_plan, packed_kv_cache  # noqa
     from shadowinfer.shadowkv.shadowkv_agent import ShadowKVAgent  # noqa
-    from shadowinfer.shadowkv import paged_kv_store  # noqa
+    from shadowinfer.shadowkv import paged_kv_store, importance_model  # noqa
     return types.SimpleNamespace(
-        rd=rd_allocator, plan=precision_plan, pkc=packed_kv_cache, Agent=ShadowKVAgent, paged=paged_kv_store
+        rd=rd_allocator, plan=precision_plan, pkc=packed_kv_cache, Agent=ShadowKVAgent, paged=paged_kv_store,
+        imp=importance_model,
     )
 
 
@@ -431,6 +432,82 @@ def paged_cases(R):
         paged_case(R, name, B, H, D, P, G, paged_random_ops(R, B, H, D, P, G, n, seed))
 
 
+def reuse_decision_case(R, case, seed, B, H, S, D, step_id, total_steps, drift, mode):
+    """ShadowKVAgent.decide_reuse_per_token (shadowkv_agent.py:1165-1256): the reuse dict as an
+    array, the stats, and the drift / threshold the reference compares (replayed with the
+    reference's own torch lines, to tell near-threshold entries)."""
+    k, v, kp, vp, imp = (torch.from_numpy(x) for x in reuse_inputs(seed, B, H, S, D))
+    mask, stats = R.Agent.decide_reuse_per_token(None, k, v, kp, vp, step_id, total_steps, drift, mode, imp)
+    arr = np.zeros((S, H), dtype=np.uint8)
+    for (t, h), on in mask.items():
+        arr[t, h] = 1 if on else 0
+    dk = torch.norm(k - kp, dim=(0, 3)) / (torch.norm(k, dim=(0, 3)) + 1e-8)
+    dv = torch.norm(v - vp, dim=(0, 3)) / (torch.norm(v, dim=(0, 3)) + 1e-8)
+    delta = ((dk + dv) / 2.0).t().double()
+    progress = step_id / max(total_steps, 1)
+    base = {"aggressive": 0.20, "balanced": 0.15, "conservative": 0.10}.get(mode, 0.15)
+    eff = base * (1.0 - 0.5 * progress) * (1.0 - drift * 0.3)
+    thr = torch.clamp(eff * (1.0 - 0.3 * imp.double().clamp(0.0, 1.0)), min=1e-5)
+    put(case, "mask", arr)
+    put(case, "ref_delta", delta)
+    put(case, "ref_thr", thr)
+    PINS["cases"][case] = {"kind": "reuse_decision", "seed": seed, "B": B, "H": H, "S": S, "D": D,
+                           "step_id": step_id, "total_steps": total_steps, "drift": drift, "mode": mode,
+                           "stats": stats}
+
+
+def irap_case(R, case, seed, B, H, Sq, Sk, *, kind="probs", contract=None, prev_len=None, decay=0.9, beta=0.3,
+              sink=4, layer_index=0, num_layers=1, bad=False):
+    """compute_irap_importance (importance_model.py:37-134), called directly on probabilities
+    (contract None) or through the agent's contract normalisation
+    (_compute_importance_with_state, shadowkv_agent.py:940-965; contract 'probs' / 'logits').
+    ``prev_len``: a previous EMA state of that many tokens (grown / truncated to Sk)."""
+    scores = torch.from_numpy(irap_scores(seed, B, H, Sq, Sk, kind=kind, bad=bad))
+    prev = None
+    if prev_len is not None:
+        g = np.random.default_rng(seed + 7)
+        prev = torch.from_numpy((g.random((prev_len, H)) / Sk).astype(np.float32))
+        put(case, "prev", prev)
+    if contract is None:
+        imp, ema, da = R.imp.compute_irap_importance(scores, received_ema_prev=prev, irap_decay=decay,
+                                                     entropy_weight=beta, sink_tokens=sink,
+                                                     layer_index=layer_index, num_layers=num_layers)
+        w = torch.nan_to_num(scores, nan=0.0, posinf=0.0, neginf=0.0)
+    else:
+        imp, ema, da = R.Agent._compute_importance_with_state(
+            R.Agent, scores, layer_index, num_layers, attn_is_probabilities=contract == "probs",
+            received_ema=prev, irap_decay=decay, entropy_weight=beta, sink_tokens=sink)
+        if contract == "probs":
+            w = R.Agent._row_normalize(scores)
+        else:
+            w = torch.nn.functional.softmax(torch.nan_to_num(scores), dim=-1)
+        w = torch.nan_to_num(w, nan=0.0, posinf=0.0, neginf=0.0)
+    put(case, "importance", imp)
+    put(case, "ema", ema)
+    put(case, "ref_received", w.mean(dim=(0, 2)).t())
+    PINS["cases"][case] = {"kind": "irap", "seed": seed, "B": B, "H": H, "Sq": Sq, "Sk": Sk, "score_kind": kind,
+                           "contract": contract, "prev_len": prev_len, "decay": decay, "beta": beta,
+                           "sink": sink, "layer_index": layer_index, "num_layers": num_layers, "bad": bad,
+                           "delta_a": da}
+
+
+def decision_cases(R):
+    reuse_decision_case(R, "reuse_dec_b1_d128", 501, 1, 8, 256, 128, 3, 16, 0.2, "balanced")
+    reuse_decision_case(R, "reuse_dec_b2_d64_aggr", 502, 2, 4, 200, 64, 0, 10, 0.0, "aggressive")
+    reuse_decision_case(R, "reuse_dec_b1_d96_cons_late", 503, 1, 6, 150, 96, 9, 10, 0.9, "conservative")
+    reuse_decision_case(R, "reuse_dec_b3_d32_unknown_mode", 504, 3, 3, 77, 32, 5, 0, 0.5, "custom")
+    irap_case(R, "irap_probs_cold", 601, 1, 8, 128, 128)
+    irap_case(R, "irap_probs_ema_grow", 602, 1, 8, 128, 128, prev_len=96, decay=0.8, layer_index=2, num_layers=4)
+    irap_case(R, "irap_probs_ema_shrink", 603, 2, 4, 100, 100, prev_len=130, beta=0.0, sink=0)
+    irap_case(R, "irap_nonsquare_q_lt_k", 604, 1, 4, 48, 160, beta=1.0, sink=200)
+    irap_case(R, "irap_nonsquare_q_gt_k", 605, 2, 3, 90, 64, prev_len=64, layer_index=3, num_layers=3)
+    irap_case(R, "irap_bad_values", 606, 1, 4, 64, 64, bad=True, prev_len=64)
+    irap_case(R, "irap_contract_probs_raw", 607, 1, 8, 128, 128, kind="raw", contract="probs", prev_len=128)
+    irap_case(R, "irap_contract_logits", 608, 2, 8, 128, 128, kind="logits", contract="logits", bad=True)
+    irap_case(R, "irap_contract_logits_ema", 609, 1, 16, 256, 256, kind="logits", contract="logits",
+              prev_len=200, decay=0.95, beta=0.5, layer_index=1, num_layers=2)
+
+
 def full_pins(R):
     """cfg1 / cfg2 pipelines at full size: digests only."""
     c1 = W.CONFIGS["cfg1"]
@@ -541,6 +618,7 @@ def main():
     global_budget_case(R, "gb_no_pressure", gen, 1, 2, 12, 64, 2, 2.0, 0)
     global_budget_case(R, "gb_b2_group32", gen, 2, 2, 40, 128, 2, 0.4, 4, group=32, probs=(0.1, 0.3, 0.3, 0.25, 0.05))
     paged_cases(R)
+    decision_cases(R)
     full_pins(R)
     np.savez_compressed(SMALL_NPZ, **ARR)
     with open(PINS_JSON, "w") as f:

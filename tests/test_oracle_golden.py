@@ -215,3 +215,42 @@ def test_paged_store(case):
         assert st == want["state"], (i, op)
         k, v = store.gather()
         assert [dig(k), dig(v)] == want["gather"] and k.shape[2] == want["S_out"], (i, op)
+
+
+@pytest.mark.parametrize("case", _cases(_pins(), "reuse_decision"))
+def test_reuse_decision(case, golden_small):
+    """decide_reuse_per_token: drift within 1e-6 relative of the reference's float32 drift; the
+    mask equal wherever the reference's drift is not within that band of its threshold."""
+    from golden_lib import reuse_inputs
+    from oracle import decision_oracle as DO
+    pin = _pins()["cases"][case]
+    a = case_arrays(golden_small, case)
+    k, v, kp, vp, imp = reuse_inputs(pin["seed"], pin["B"], pin["H"], pin["S"], pin["D"])
+    mask, stats, delta = DO.decide_reuse_per_token(k, v, kp, vp, pin["step_id"], pin["total_steps"], pin["drift"],
+                                                   pin["mode"], imp)
+    np.testing.assert_allclose(delta.T.astype(np.float64), a["ref_delta"], rtol=1e-6, atol=0)
+    near = np.abs(a["ref_delta"] - a["ref_thr"]) <= 1e-6 * a["ref_thr"]
+    assert np.array_equal(mask[~near], a["mask"].astype(bool)[~near])
+    if not near.any():
+        assert stats == pin["stats"]
+
+
+@pytest.mark.parametrize("case", _cases(_pins(), "irap"))
+def test_irap_importance(case, golden_small):
+    """compute_irap_importance (direct or through the agent's contract): importance within the
+    reference's own 1e-6, EMA within 1e-6 relative, delta_a within 1e-5 relative."""
+    from golden_lib import irap_scores
+    from oracle import decision_oracle as DO
+    pin = _pins()["cases"][case]
+    a = case_arrays(golden_small, case)
+    x = irap_scores(pin["seed"], pin["B"], pin["H"], pin["Sq"], pin["Sk"], kind=pin["score_kind"], bad=pin["bad"])
+    if pin["contract"] is not None:
+        x = DO.irap_inputs(x, pin["contract"] == "probs")
+    imp, ema, da = DO.compute_irap_importance(x, a.get("prev"), pin["decay"], pin["beta"], pin["sink"],
+                                              pin["layer_index"], pin["num_layers"])
+    assert np.abs(imp - a["importance"]).max() <= 1e-6
+    np.testing.assert_allclose(ema, a["ema"], rtol=1e-6, atol=1e-12)
+    if pin["delta_a"] is None:
+        assert da is None
+    else:
+        assert abs(da - pin["delta_a"]) <= 1e-5 * abs(pin["delta_a"])
