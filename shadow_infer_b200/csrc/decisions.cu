@@ -263,12 +263,57 @@ __device__ __forceinline__ float warp_sum8(float (&v)[8], int lane) {
     return c;
 }
 
+// Four query rows (of one batch) of one thread's four keys: loads all four rows first, then
+// folds each value into the column sums (compensated float32) and the rows' entropy terms.
+// FULL: the block's whole key tile is in range and 16-byte aligned (no per-value checks).
+template <int MODE, bool FULL>
+__device__ __forceinline__ void irap_rows4(const float* __restrict__ row0, int64_t row_stride, int nr,
+                                           const float2* __restrict__ st_row, int k0, int Sk, float (&col)[4],
+                                           float (&comp)[4], float (&rc)[4], float (&rl)[4]) {
+    constexpr int U = 4;
+    float v[U][4];
+    float2 st[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+        st[u] = make_float2(0.0f, 1.0f);
+        if (u < nr) {
+            const float* row = row0 + u * row_stride;
+            if (MODE) st[u] = st_row[u];
+            if (FULL) {
+                const float4 a = __ldg(reinterpret_cast<const float4*>(row + k0));
+                v[u][0] = a.x; v[u][1] = a.y; v[u][2] = a.z; v[u][3] = a.w;
+            } else {
+#pragma unroll
+                for (int i = 0; i < 4; ++i) v[u][i] = k0 + i < Sk ? __ldg(row + k0 + i) : 0.0f;
+            }
+        }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+        if (u < nr) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                if (FULL || k0 + i < Sk) {
+                    const float w = irap_weight<MODE>(v[u][i], st[u]);
+                    const float y = __fsub_rn(w, comp[i]);        // Kahan step: col += w
+                    const float t = __fadd_rn(col[i], y);
+                    comp[i] = __fsub_rn(__fsub_rn(t, col[i]), y);
+                    col[i] = t;
+                    const float c = fmaxf(w, 1e-10f);
+                    rc[u] += c;
+                    rl[u] = fmaf(c, lg2_approx(c), rl[u]);        // sum c log2 c; MUFU error ~2^-22
+                }
+            }
+        }
+    }
+}
+
 // grid (nkt, nqb, H), 256 threads: keys [kt*1024, +1024), query rows [qb*128, +128), all batches.
 // colpart[(qb*H + h)*Sk + k] = sum over the block's rows of w (compensated float32 sum per
 // column, one rounding to float64 per block); rowpart[(h*Sq + q)*nkt + kt] = (sum c, sum c ln c)
 // over the block's keys and all batches.  Four query rows are loaded before any is reduced.
 template <int MODE>
-__global__ void __launch_bounds__(256) irap_pass_kernel(const float* __restrict__ x, IrapGeom g,
+__global__ void __launch_bounds__(256, 4) irap_pass_kernel(const float* __restrict__ x, IrapGeom g,
                                                        const float2* __restrict__ stats, double* __restrict__ colpart,
                                                        double2* __restrict__ rowpart) {
     constexpr int U = 4;
@@ -278,52 +323,19 @@ __global__ void __launch_bounds__(256) irap_pass_kernel(const float* __restrict_
     const int k0 = kt * kIrapTile + threadIdx.x * 4;
     const int q0 = qb * kIrapRows;
     const int nq = min(kIrapRows, g.Sq - q0);
-    // a whole tile of aligned columns: unchecked 16-byte loads
     const bool full = (g.Sk & 3) == 0 && (kt + 1) * kIrapTile <= g.Sk;
     float col[4] = {0.f, 0.f, 0.f, 0.f}, comp[4] = {0.f, 0.f, 0.f, 0.f};
     for (int qi = 0; qi < nq; qi += U) {
         const int nr = min(U, nq - qi);
-        float rc[U], rl[U];
-#pragma unroll
-        for (int u = 0; u < U; ++u) rc[u] = rl[u] = 0.0f;
+        float rc[U] = {0.f, 0.f, 0.f, 0.f}, rl[U] = {0.f, 0.f, 0.f, 0.f};
         for (int b = 0; b < g.B; ++b) {
-            float v[U][4];
-            float2 st[U];
-#pragma unroll
-            for (int u = 0; u < U; ++u) {
-                st[u] = make_float2(0.0f, 1.0f);
-                if (u < nr) {
-                    const int64_t r = ((int64_t)b * g.H + h) * g.Sq + q0 + qi + u;
-                    const float* row = x + r * g.Sk;
-                    if (MODE) st[u] = stats[r];
-                    if (full) {
-                        const float4 a = __ldg(reinterpret_cast<const float4*>(row + k0));
-                        v[u][0] = a.x; v[u][1] = a.y; v[u][2] = a.z; v[u][3] = a.w;
-                    } else {
-#pragma unroll
-                        for (int i = 0; i < 4; ++i) v[u][i] = k0 + i < g.Sk ? __ldg(row + k0 + i) : 0.0f;
-                    }
-                }
-            }
-#pragma unroll
-            for (int u = 0; u < U; ++u) {
-                if (u < nr) {
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        if (full || k0 + i < g.Sk) {
-                            const float w = irap_weight<MODE>(v[u][i], st[u]);
-                            // Kahan step: col += w
-                            const float y = __fsub_rn(w, comp[i]);
-                            const float t = __fadd_rn(col[i], y);
-                            comp[i] = __fsub_rn(__fsub_rn(t, col[i]), y);
-                            col[i] = t;
-                            const float c = fmaxf(w, 1e-10f);
-                            rc[u] += c;
-                            rl[u] = fmaf(c, lg2_approx(c), rl[u]);   // sum c log2 c; MUFU error ~2^-22
-                        }
-                    }
-                }
-            }
+            const int64_t r = ((int64_t)b * g.H + h) * g.Sq + q0 + qi;      // first of the 4 rows
+            const float* row0 = x + r * g.Sk;
+            const float2* st_row = MODE ? stats + r : nullptr;
+            if (full)
+                irap_rows4<MODE, true>(row0, g.Sk, nr, st_row, k0, g.Sk, col, comp, rc, rl);
+            else
+                irap_rows4<MODE, false>(row0, g.Sk, nr, st_row, k0, g.Sk, col, comp, rc, rl);
         }
         // the 4 rows' (sum c, sum c log2 c) over the warp; value 2u is row u's sum c, 2u+1 its log sum
         float v8[8] = {rc[0], rl[0], rc[1], rl[1], rc[2], rl[2], rc[3], rl[3]};
