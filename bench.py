@@ -332,7 +332,62 @@ def attention_phase(args, world, rank, dev, dist, lib, tensor_peak):
                                "kind": "port",
                                "sample": "oracle unpack + float64 numpy attention of head 0 of the layer, "
                                          "extrapolated x32 heads x32 layers"}
+    res["gqa_block"] = gqa_block_attention(args, rank, dev, tensor_peak, k, v, codes, c["group"]) if world == 1 else None
     return res
+
+
+def gqa_block_attention(args, rank, dev, tensor_peak, k, v, codes, group):
+    """Blockwise decoding shape of the grouped-query model path: a 256-token block's queries
+    (32 query heads) attend to the packed cfg3 prefix (8 KV heads of it, 4096 tokens) plus the
+    block's own K/V (the reference's cat(past, new) + repeat_kv + attention,
+    diffusion_llama.py:376-390).  Events around the two launches; the reference arm for it is
+    unpack + cat + repeat_kv + torch attention (fp32) on the same device."""
+    import torch
+
+    from shadow_infer_b200.shadowkv import PackedKVCache, PrecisionPlan, packed_attention
+
+    H_kv, rep, W_blk = 8, 4, 256
+    B, _, S, D = k.shape
+    cache = PackedKVCache.pack(k[:, :H_kv].contiguous().to(dev), v[:, :H_kv].contiguous().to(dev), None, group,
+                               plan=PrecisionPlan.from_codes(codes[:, :H_kv].contiguous()))["packed_kv"]
+    g = torch.Generator(device=dev).manual_seed(5 + rank)
+    q = torch.randn(B, H_kv * rep, W_blk, D, device=dev, generator=g).half()
+    kn = torch.randn(B, H_kv, W_blk, D, device=dev, generator=g)
+    vn = torch.randn(B, H_kv, W_blk, D, device=dev, generator=g)
+    packed_attention(q, cache, k_new=kn, v_new=vn)
+    reps = max(3, min(args.steps, 20))
+    ev = [tuple(torch.cuda.Event(enable_timing=True) for _ in range(3)) for _ in range(reps + 3)]
+    for i in range(reps + 3):
+        packed_attention(q, cache, check=False, events=ev[i], k_new=kn, v_new=vn)
+    torch.cuda.synchronize()
+    ms = statistics.mean(a.elapsed_time(c) for a, _, c in ev[3:])
+    kms = statistics.mean(b.elapsed_time(c) for _, b, c in ev[3:])
+    flops = 4.0 * B * H_kv * rep * W_blk * (S + W_blk) * D
+
+    def torch_path():
+        pk, pv = cache.unpack()
+        ka = torch.cat((pk, kn), dim=2).repeat_interleave(rep, dim=1)
+        va = torch.cat((pv, vn), dim=2).repeat_interleave(rep, dim=1)
+        return torch.softmax(q.float() @ ka.transpose(-2, -1) / D ** 0.5, dim=-1) @ va
+
+    for _ in range(2):
+        torch_path()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        torch_path()
+    e1.record()
+    torch.cuda.synchronize()
+    return {
+        "workload": f"block of {W_blk} queries x {H_kv * rep} heads over a packed prefix of {S} tokens x {H_kv} KV "
+                    f"heads (codes 20/50/30) + the block's own K/V, D={D}",
+        "ms": ms, "attention_kernel_ms": kms,
+        "roofline": {"kernel": "packed_attention_kernel (GQA, dense tail rows)", "bound": "tensor",
+                     "achieved": flops / (kms / 1e3) / 1e12, "peak": tensor_peak[0], "unit": "TFLOP/s",
+                     "frac": flops / (kms / 1e3) / 1e12 / tensor_peak[0], "flops_per_launch": flops},
+        "torch_unpack_cat_attention_ms": e0.elapsed_time(e1) / reps,
+    }
 
 
 # --------------------------------------------------------------------------- global budget

@@ -172,6 +172,24 @@ int skv_attend_kv_tiles(const void* q, int B, int H, int S_q, int D, int S_kv, c
                         const int32_t* counts, float scale, const void* scratch, size_t scratch_bytes, float* out,
                         int32_t* error_flag, void* stream);
 
+/* Grouped-query attention over a packed cache plus this step's own dense K/V: the attention
+ * of shadowinfer/models/diffusion_llama.py:376-390 and simple_diffusion_llm.py:160-169
+ * (cat(past, new) -> repeat_kv -> softmax(q k^T * scale) v) with the past read from the packed
+ * buckets.  q fp16 [B, H_q, S_q, D]; the cache has H_kv heads (H_q % H_kv == 0, query head h
+ * reads KV head h / (H_q / H_kv)); rows/counts from skv_head_index over the cache's S_kv
+ * tokens; k_new / v_new float [B, H_kv, S_new, D] (16-byte aligned; NULL when S_new == 0).
+ * Scratch: skv_packed_attention_scratch_bytes(B, H_kv, S_kv + S_new, D). */
+int skv_stage_kv_tiles_gqa(const skv_bucket* buckets, int B, int H_kv, int S_kv, int D, int int4_group,
+                           const int32_t* rows, const int32_t* counts, const float* k_new, const float* v_new,
+                           int S_new, void* scratch, size_t scratch_bytes, void* stream);
+int skv_attend_kv_tiles_gqa(const void* q, int B, int H_q, int S_q, int D, int H_kv, int S_kv, const int32_t* rows,
+                            const int32_t* counts, int S_new, float scale, const void* scratch, size_t scratch_bytes,
+                            float* out, int32_t* error_flag, void* stream);
+int skv_packed_attention_gqa(const void* q, int B, int H_q, int S_q, int D, const skv_bucket* buckets, int H_kv,
+                             int S_kv, int int4_group, const int32_t* rows, const int32_t* counts,
+                             const float* k_new, const float* v_new, int S_new, float scale, void* scratch,
+                             size_t scratch_bytes, float* out, int32_t* error_flag, void* stream);
+
 /* ---- cross-layer budget: KVCacheManager.enforce_global_budget
  * (shadowinfer/shadowkv/kv_cache_manager.py:129-200).  The reference sorts every non-sink
  * (layer, token, head) by importance and evicts from the front in batches, re-reading usage

@@ -580,10 +580,23 @@ def attention(q: np.ndarray, k: np.ndarray, v: np.ndarray, scale: Optional[float
     return out
 
 
-def packed_attention(q: np.ndarray, cache: OraclePackedKV, scale: Optional[float] = None) -> np.ndarray:
-    """Oracle for attention read from the packed cache: ``unpack()`` then dense attention."""
+def repeat_kv(x: np.ndarray, n_rep: int) -> np.ndarray:
+    """``[B, H_kv, S, D] -> [B, H_kv * n_rep, S, D]``, head h of the result = head h // n_rep
+    (diffusion_llama.py:300-308)."""
+    return np.repeat(x, n_rep, axis=1)
+
+
+def packed_attention(q: np.ndarray, cache: OraclePackedKV, scale: Optional[float] = None,
+                     k_new: Optional[np.ndarray] = None, v_new: Optional[np.ndarray] = None) -> np.ndarray:
+    """Oracle for attention read from the packed cache: ``unpack()``, this step's own K/V appended
+    (``cat((past, new), dim=2)``), KV heads repeated to the query heads, then dense attention
+    (diffusion_llama.py:376-390, simple_diffusion_llm.py:160-169)."""
     k, v = unpack(cache)
-    return attention(q, k, v, scale)
+    if k_new is not None:
+        k = np.concatenate([k, k_new.astype(np.float32)], axis=2)
+        v = np.concatenate([v, v_new.astype(np.float32)], axis=2)
+    n_rep = q.shape[1] // k.shape[1]
+    return attention(q, repeat_kv(k, n_rep), repeat_kv(v, n_rep), scale)
 
 
 # --------------------------------------------------------------------------------------

@@ -89,13 +89,16 @@ struct AttnParams {
     const __half* q;           // [B, H, S_q, D]
     float* out;                // [B, H, S_q, D]
     Buckets bk;
-    const int32_t* rows;       // [H, S_kv] slot values of the stored entries, grouped by precision
-    const int32_t* counts;     // [H, 5]: stored entries per precision, evicted entries
-    uint8_t* stage;            // [B, H, ntmax, 2 (K, V), staged_tile_bytes(D)]
+    const int32_t* rows;       // [H_kv, S_kv] slot values of the stored entries, grouped by precision
+    const int32_t* counts;     // [H_kv, 5]: stored entries per precision, evicted entries
+    const float* k_new;        // [B, H_kv, S_new, D] dense rows attended after the packed ones (or NULL)
+    const float* v_new;
+    uint8_t* stage;            // [B, H_kv, ntmax, 2 (K, V), staged_tile_bytes(D)]
     float* part_o;             // [slots, kUnitRows, D]: unnormalised O of a unit's second part
     float2* part_ml;           // [slots, kUnitRows]: its (reference max, sum) per query row
     int* part_flag;            // [slots]: softmax warps that have published their rows
     int B, H, S_q, S_kv, G, ntmax, QP, slots;
+    int H_kv, rep, S_new;      // query head h reads KV head h / rep (grouped-query attention)
     float scale_log2;          // softmax scale * log2(e)
     int* err;
 };
@@ -126,7 +129,7 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* e
 }
 
 __device__ __forceinline__ int64_t staged_offset(const AttnParams& p, int b, int h, int j, int kv, int tile_bytes) {
-    return ((((int64_t)b * p.H + h) * p.ntmax + j) * 2 + kv) * tile_bytes;
+    return ((((int64_t)b * p.H_kv + h) * p.ntmax + j) * 2 + kv) * tile_bytes;
 }
 
 // ------------------------------------------------------------------------------ staging
@@ -225,6 +228,22 @@ __device__ __forceinline__ void load_raw_row(const AttnParams& p, int b, int32_t
     if (r.code == 0) r.code = 1;
 }
 
+// One lane's share of dense fp32 row r of (b, KV head h) of k_new / v_new, converted to fp16.
+template <int D>
+__device__ __forceinline__ void load_dense_row(const AttnParams& p, int b, int h, int r, int l8, RawRow<D / 64>& raw) {
+    constexpr int NA = D / 64;
+    raw.code = 1;
+    const int64_t row = (((int64_t)b * p.H_kv + h) * p.S_new + r) * D;
+#pragma unroll
+    for (int a = 0; a < NA; ++a) {
+        const int d0 = a * 64 + l8 * 8;
+        const uint4* pk = reinterpret_cast<const uint4*>(p.k_new + row + d0);
+        const uint4* pv = reinterpret_cast<const uint4*>(p.v_new + row + d0);
+        raw.k[a] = f32x8_bits_to_half(__ldg(pk), __ldg(pk + 1));
+        raw.v[a] = f32x8_bits_to_half(__ldg(pv), __ldg(pv + 1));
+    }
+}
+
 // Converts one lane's share of a K and a V row to fp16 and stores it, 128B-swizzled, at row
 // `r` of the staged tiles (zeros for a padding row).
 template <int D>
@@ -248,7 +267,8 @@ __device__ __forceinline__ void store_row(const RawRow<D / 64>& raw, int r, int 
     }
 }
 
-// One CTA per (KV tile j, head h, batch b); tiles past the head's stored rows exit at once.
+// One CTA per (KV tile j, KV head h, batch b); tiles past the head's rows exit at once.  A
+// head's rows are its stored packed entries, then the S_new dense rows of k_new / v_new.
 // Eight lanes per row (one 16-byte chunk of each atom per lane), 32 rows per pass, 4 passes.
 // The row-list entries are fetched together with the head's counts (entries past the stored
 // rows are discarded afterwards), so a CTA waits for two memory round trips, not three.
@@ -268,13 +288,19 @@ __global__ void __launch_bounds__(kStageThreads, 3) stage_tiles_kernel(AttnParam
     }
     const int* cnt = p.counts + (int64_t)h * 5;
     const int n_stored = __ldg(cnt) + __ldg(cnt + 1) + __ldg(cnt + 2) + __ldg(cnt + 3);
-    if (j * kBN >= n_stored) return;
+    const int n_rows = n_stored + p.S_new;
+    if (j * kBN >= n_rows) return;
     uint8_t* ktile = p.stage + staged_offset(p, b, h, j, 0, staged_tile_bytes(D));
     uint8_t* vtile = ktile + staged_tile_bytes(D);
     RawRow<NA> raw[kPasses];
 #pragma unroll
-    for (int i = 0; i < kPasses; ++i)
-        load_raw_row<D>(p, b, j * kBN + i * kRowsPerPass + rsub < n_stored ? e[i] : -1, l8, raw[i]);
+    for (int i = 0; i < kPasses; ++i) {
+        const int idx = j * kBN + i * kRowsPerPass + rsub;
+        if (idx >= n_stored && idx < n_rows)
+            load_dense_row<D>(p, b, h, idx - n_stored, l8, raw[i]);
+        else
+            load_raw_row<D>(p, b, idx < n_stored ? e[i] : -1, l8, raw[i]);
+    }
 #pragma unroll
     for (int i = 0; i < kPasses; ++i) store_row<D>(raw[i], i * kRowsPerPass + rsub, l8, ktile, vtile);
 }
@@ -396,8 +422,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         long long acc = 0;
         int ntm = 0;
         for (int hh = 0; hh < p.H; ++hh) {
-            const int* c = p.counts + (int64_t)hh * 5;
-            const int n = (c[0] + c[1] + c[2] + c[3] + kBN - 1) / kBN;
+            const int* c = p.counts + (int64_t)(hh / p.rep) * 5;
+            const int n = (c[0] + c[1] + c[2] + c[3] + p.S_new + kBN - 1) / kBN;
             hp[hh] = acc;
             acc += n;
             ntm = max(ntm, n);
@@ -447,8 +473,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         int si = 0;                                      // segments so far
         bool ok = true;
         while (ok && sched.next(sg)) {
-            const int* cnt = p.counts + (int64_t)sg.h * 5;
-            const int n_stored = cnt[0] + cnt[1] + cnt[2] + cnt[3];
+            const int* cnt = p.counts + (int64_t)(sg.h / p.rep) * 5;
+            const int n_stored = cnt[0] + cnt[1] + cnt[2] + cnt[3] + p.S_new;     // packed + dense rows
             const int n_ev = cnt[4];
             const bool first_part = sg.j0 == 0;
             if (sg.j0 > 0 && sg.j1 < sg.nt) {            // cannot happen with the schedule above
@@ -674,7 +700,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                     for (int a = 0; a < NA; ++a)
                         tma_load_2d(smem + L::kQ + t * TB + a * kBM * 128, &qmap, a * 64, qrow + t * kBM, q_full);
                 ++nq;
-                const uint8_t* gkv = p.stage + staged_offset(p, sg.b, sg.h, 0, 0, TB);
+                const uint8_t* gkv = p.stage + staged_offset(p, sg.b, sg.h / p.rep, 0, 0, TB);
                 for (int j = sg.j0; j < sg.j1; ++j, ++g) {
                     const int s = (int)(g & 1);
                     if (g >= 2 && !mbar_wait_spin(&k_empty[s], (uint32_t)(((g >> 1) - 1) & 1), p.err, kErrKEmpty)) {
@@ -917,11 +943,17 @@ size_t skv_packed_attention_scratch_bytes(int B, int H, int S_kv, int D) {
 
 namespace {
 
-int attn_params(const void* q, int B, int H, int S_q, int D, const skv_bucket* buckets, int S_kv, int int4_group,
-                const int32_t* rows, const int32_t* counts, float scale, void* scratch, size_t scratch_bytes,
-                float* out, int32_t* error_flag, AttnParams& prm, const char* what) {
+int attn_params(const void* q, int B, int H, int S_q, int D, const skv_bucket* buckets, int H_kv, int S_kv,
+                int int4_group, const int32_t* rows, const int32_t* counts, const float* k_new, const float* v_new,
+                int S_new, float scale, void* scratch, size_t scratch_bytes, float* out, int32_t* error_flag,
+                AttnParams& prm, const char* what) {
     if (!rows || !counts || !scratch) return fail(SKV_ERR_INVALID_ARGUMENT, "%s: null pointer", what);
-    if (B <= 0 || H <= 0 || S_q <= 0 || S_kv <= 0) return fail(SKV_ERR_INVALID_ARGUMENT, "%s: bad shape", what);
+    if (B <= 0 || H <= 0 || S_q <= 0 || S_kv <= 0 || H_kv <= 0 || S_new < 0)
+        return fail(SKV_ERR_INVALID_ARGUMENT, "%s: bad shape", what);
+    if (H % H_kv) return fail(SKV_ERR_SHAPE, "%s: %d query heads do not group over %d KV heads", what, H, H_kv);
+    if (S_new > 0 && (!k_new || !v_new)) return fail(SKV_ERR_INVALID_ARGUMENT, "%s: null new K/V", what);
+    if (S_new > 0 && ((reinterpret_cast<uintptr_t>(k_new) | reinterpret_cast<uintptr_t>(v_new)) & 15))
+        return fail(SKV_ERR_UNSUPPORTED, "%s: new K/V not 16-byte aligned", what);
     if (D != 64 && D != 128) return fail(SKV_ERR_UNSUPPORTED, "%s: head_dim %d (64 or 128 supported)", what, D);
     const int G = int4_group > 0 && D % int4_group == 0 ? int4_group : D;
     if (G % 8) return fail(SKV_ERR_UNSUPPORTED, "%s: int4 group %d must be a multiple of 8", what, G);
@@ -934,7 +966,7 @@ int attn_params(const void* q, int B, int H, int S_q, int D, const skv_bucket* b
     }
     if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(out) | reinterpret_cast<uintptr_t>(scratch)) & 15)
         return fail(SKV_ERR_UNSUPPORTED, "%s: q/out/scratch not 16-byte aligned", what);
-    const size_t need = skv_packed_attention_scratch_bytes(B, H, S_kv, D);
+    const size_t need = skv_packed_attention_scratch_bytes(B, H_kv, S_kv + S_new, D);
     if (scratch_bytes < need)
         return fail(SKV_ERR_SCRATCH, "%s: scratch of %zu bytes, %zu needed", what, scratch_bytes, need);
     if ((long long)B * H * S_q >= (1ll << 31) || H > kMaxHeads)
@@ -946,10 +978,15 @@ int attn_params(const void* q, int B, int H, int S_q, int D, const skv_bucket* b
         for (int p = 0; p < kNumBuckets; ++p) prm.bk.b[p] = buckets[p];
     prm.rows = rows;
     prm.counts = counts;
+    prm.k_new = S_new > 0 ? k_new : nullptr;
+    prm.v_new = S_new > 0 ? v_new : nullptr;
+    prm.H_kv = H_kv;
+    prm.rep = H / H_kv;
+    prm.S_new = S_new;
     prm.stage = reinterpret_cast<uint8_t*>(scratch);
-    prm.ntmax = (S_kv + kBN - 1) / kBN;
+    prm.ntmax = (S_kv + S_new + kBN - 1) / kBN;
     prm.slots = sm_count();
-    uint8_t* part = prm.stage + (size_t)B * H * prm.ntmax * 2 * staged_tile_bytes(D);
+    uint8_t* part = prm.stage + (size_t)B * H_kv * prm.ntmax * 2 * staged_tile_bytes(D);
     prm.part_o = reinterpret_cast<float*>(part);
     part += (size_t)prm.slots * kUnitRows * D * sizeof(float);
     prm.part_ml = reinterpret_cast<float2*>(part);
@@ -970,19 +1007,26 @@ int attn_params(const void* q, int B, int H, int S_q, int D, const skv_bucket* b
 
 extern "C" {
 
-int skv_stage_kv_tiles(const skv_bucket* buckets, int B, int H, int S_kv, int D, int int4_group, const int32_t* rows,
-                       const int32_t* counts, void* scratch, size_t scratch_bytes, void* stream) {
+int skv_stage_kv_tiles_gqa(const skv_bucket* buckets, int B, int H_kv, int S_kv, int D, int int4_group,
+                           const int32_t* rows, const int32_t* counts, const float* k_new, const float* v_new,
+                           int S_new, void* scratch, size_t scratch_bytes, void* stream) {
     if (!buckets) return fail(SKV_ERR_INVALID_ARGUMENT, "stage_kv_tiles: null pointer");
     AttnParams prm;
-    const int st = attn_params(nullptr, B, H, 1, D, buckets, S_kv, int4_group, rows, counts, 1.0f, scratch,
-                               scratch_bytes, nullptr, nullptr, prm, "stage_kv_tiles");
+    const int st = attn_params(nullptr, B, H_kv, 1, D, buckets, H_kv, S_kv, int4_group, rows, counts, k_new, v_new,
+                               S_new, 1.0f, scratch, scratch_bytes, nullptr, nullptr, prm, "stage_kv_tiles");
     if (st != SKV_OK) return st;
-    const dim3 grid((unsigned)prm.ntmax, (unsigned)H, (unsigned)B);
+    const dim3 grid((unsigned)prm.ntmax, (unsigned)H_kv, (unsigned)B);
     if (D == 128)
         stage_tiles_kernel<128><<<grid, kStageThreads, 0, as_stream(stream)>>>(prm);
     else
         stage_tiles_kernel<64><<<grid, kStageThreads, 0, as_stream(stream)>>>(prm);
     return check_launch("stage_kv_tiles");
+}
+
+int skv_stage_kv_tiles(const skv_bucket* buckets, int B, int H, int S_kv, int D, int int4_group, const int32_t* rows,
+                       const int32_t* counts, void* scratch, size_t scratch_bytes, void* stream) {
+    return skv_stage_kv_tiles_gqa(buckets, B, H, S_kv, D, int4_group, rows, counts, nullptr, nullptr, 0, scratch,
+                                  scratch_bytes, stream);
 }
 
 }  // extern "C"
@@ -1036,13 +1080,16 @@ int launch_attention(const AttnParams& prm, cudaStream_t s) {
 
 extern "C" {
 
-int skv_attend_kv_tiles(const void* q, int B, int H, int S_q, int D, int S_kv, const int32_t* rows,
-                        const int32_t* counts, float scale, const void* scratch, size_t scratch_bytes, float* out,
-                        int32_t* error_flag, void* stream) {
+int skv_attend_kv_tiles_gqa(const void* q, int B, int H_q, int S_q, int D, int H_kv, int S_kv, const int32_t* rows,
+                            const int32_t* counts, int S_new, float scale, const void* scratch, size_t scratch_bytes,
+                            float* out, int32_t* error_flag, void* stream) {
     if (!q || !out || !error_flag) return fail(SKV_ERR_INVALID_ARGUMENT, "attend_kv_tiles: null pointer");
     AttnParams prm;
-    const int st = attn_params(q, B, H, S_q, D, nullptr, S_kv, 0, rows, counts, scale, const_cast<void*>(scratch),
-                               scratch_bytes, out, error_flag, prm, "attend_kv_tiles");
+    // the dense rows are already staged: only their count matters here (a non-null placeholder
+    // passes the argument checks and is never read)
+    const float* staged = S_new > 0 ? reinterpret_cast<const float*>(scratch) : nullptr;
+    const int st = attn_params(q, B, H_q, S_q, D, nullptr, H_kv, S_kv, 0, rows, counts, staged, staged, S_new, scale,
+                               const_cast<void*>(scratch), scratch_bytes, out, error_flag, prm, "attend_kv_tiles");
     if (st != SKV_OK) return st;
     cudaStream_t s = as_stream(stream);
     if (cudaMemsetAsync(error_flag, 0, sizeof(int32_t), s) != cudaSuccess)
@@ -1050,14 +1097,31 @@ int skv_attend_kv_tiles(const void* q, int B, int H, int S_q, int D, int S_kv, c
     return D == 128 ? launch_attention<128>(prm, s) : launch_attention<64>(prm, s);
 }
 
+int skv_attend_kv_tiles(const void* q, int B, int H, int S_q, int D, int S_kv, const int32_t* rows,
+                        const int32_t* counts, float scale, const void* scratch, size_t scratch_bytes, float* out,
+                        int32_t* error_flag, void* stream) {
+    return skv_attend_kv_tiles_gqa(q, B, H, S_q, D, H, S_kv, rows, counts, 0, scale, scratch, scratch_bytes, out,
+                                   error_flag, stream);
+}
+
+int skv_packed_attention_gqa(const void* q, int B, int H_q, int S_q, int D, const skv_bucket* buckets, int H_kv,
+                             int S_kv, int int4_group, const int32_t* rows, const int32_t* counts,
+                             const float* k_new, const float* v_new, int S_new, float scale, void* scratch,
+                             size_t scratch_bytes, float* out, int32_t* error_flag, void* stream) {
+    if (!q || !buckets || !out || !error_flag) return fail(SKV_ERR_INVALID_ARGUMENT, "packed_attention: null pointer");
+    if (H_kv <= 0 || H_q % H_kv) return fail(SKV_ERR_SHAPE, "packed_attention: %d query heads over %d KV heads", H_q, H_kv);
+    const int st = skv_stage_kv_tiles_gqa(buckets, B, H_kv, S_kv, D, int4_group, rows, counts, k_new, v_new, S_new,
+                                          scratch, scratch_bytes, stream);
+    if (st != SKV_OK) return st;
+    return skv_attend_kv_tiles_gqa(q, B, H_q, S_q, D, H_kv, S_kv, rows, counts, S_new, scale, scratch, scratch_bytes,
+                                   out, error_flag, stream);
+}
+
 int skv_packed_attention(const void* q, int B, int H, int S_q, int D, const skv_bucket* buckets, int S_kv,
                          int int4_group, const int32_t* rows, const int32_t* counts, float scale, void* scratch,
                          size_t scratch_bytes, float* out, int32_t* error_flag, void* stream) {
-    if (!q || !buckets || !out || !error_flag) return fail(SKV_ERR_INVALID_ARGUMENT, "packed_attention: null pointer");
-    const int st = skv_stage_kv_tiles(buckets, B, H, S_kv, D, int4_group, rows, counts, scratch, scratch_bytes, stream);
-    if (st != SKV_OK) return st;
-    return skv_attend_kv_tiles(q, B, H, S_q, D, S_kv, rows, counts, scale, scratch, scratch_bytes, out, error_flag,
-                               stream);
+    return skv_packed_attention_gqa(q, B, H, S_q, D, buckets, H, S_kv, int4_group, rows, counts, nullptr, nullptr, 0,
+                                    scale, scratch, scratch_bytes, out, error_flag, stream);
 }
 
 }  // extern "C"

@@ -29,51 +29,75 @@ def packed_attention(
     scale: Optional[float] = None,
     check: bool = True,
     events: Optional[tuple] = None,
+    k_new: Optional[torch.Tensor] = None,
+    v_new: Optional[torch.Tensor] = None,
 ) -> torch.Tensor:
-    """Non-causal attention of ``q`` [B, H, S_q, D] over a packed cache; returns fp32 [B, H, S_q, D].
+    """Non-causal attention of ``q`` [B, H_q, S_q, D] over a packed cache; returns fp32 [B, H_q, S_q, D].
 
     ``scale`` defaults to ``1/sqrt(D)``.  ``q`` is used in fp16 (the tensor-core operand type).
     With ``check`` the call synchronises and raises ``RuntimeError`` if the kernel
     reported a pipeline timeout.  ``events``: three CUDA events recorded before the staging
     kernel, between the two kernels and after the attention kernel (timing hook).
+
+    Grouped-query attention: the cache holds H_kv heads and query head h reads KV head
+    ``h // (H_q / H_kv)`` (the reference's ``_repeat_kv`` order, diffusion_llama.py:300-308).
+    ``k_new`` / ``v_new`` [B, H_kv, S_new, D]: this step's own K/V, attended together with the
+    cached rows -- the reference's ``cat((past_k, k), dim=2)`` before the attention
+    (simple_diffusion_llm.py:160-169, diffusion_llama.py:376-390) -- staged straight from the
+    dense tensors.
     """
     if q.dim() != 4:
         raise ValueError(f"q must be 4-D [batch, heads, seq, head_dim], got shape {tuple(q.shape)}")
     B, H, S_q, D = (int(x) for x in q.shape)
     c = kv_cache
-    if (B, H, D) != (c.batch_size, c.num_heads, c.head_dim):
+    H_kv = int(c.num_heads)
+    if B != c.batch_size or D != c.head_dim or H_kv <= 0 or H % H_kv:
         raise ValueError(
             "q shape mismatch for packed attention: "
             f"q=(batch={B}, heads={H}, head_dim={D}) cache=({c.batch_size},{c.num_heads},{c.head_dim})"
         )
+    if (k_new is None) != (v_new is None):
+        raise ValueError("k_new and v_new must be given together")
+    S_new = 0
+    if k_new is not None:
+        if k_new.dim() != 4 or tuple(k_new.shape) != tuple(v_new.shape) or \
+                (int(k_new.shape[0]), int(k_new.shape[1]), int(k_new.shape[3])) != (B, H_kv, D):
+            raise ValueError(
+                f"k_new/v_new must be [batch, kv_heads, tokens, head_dim] = [{B}, {H_kv}, T, {D}], "
+                f"got {tuple(k_new.shape)} and {tuple(v_new.shape)}"
+            )
+        S_new = int(k_new.shape[2])
     if scale is None:
         scale = 1.0 / math.sqrt(D)
-    if not c.packed_data:
+    if not c.packed_data and S_new == 0:
         # every token-head evicted: unpack() would give zero K/V, so the output is zero
         return torch.zeros(B, H, S_q, D, dtype=torch.float32, device=q.device)
     dev = c._ensure_state()
     qd = on(q.detach(), dev, torch.float16)
+    kn = on(k_new.detach(), dev, torch.float32) if S_new else None
+    vn = on(v_new.detach(), dev, torch.float32) if S_new else None
     rows, counts = c._head_index(dev)
     out = torch.empty(B, H, S_q, D, dtype=torch.float32, device=dev)
     err = torch.empty(1, dtype=torch.int32, device=dev)
     arr, _, _ = c._device_arr(dev)
     lib = _lib.load()
-    tiles = scratch(lib.skv_packed_attention_scratch_bytes(B, H, c.seq_len, D), dev)
+    tiles = scratch(lib.skv_packed_attention_scratch_bytes(B, H_kv, c.seq_len + S_new, D), dev)
     stream = _lib.stream_of(dev)
+    g = c._int4_group_of()
     with device_ctx(dev):
         if events is None:
-            st = lib.skv_packed_attention(_lib.ptr(qd), B, H, S_q, D, arr, c.seq_len, c._int4_group_of(),
-                                          _lib.ptr(rows), _lib.ptr(counts), float(scale), _lib.ptr(tiles),
-                                          tiles.numel(), _lib.ptr(out), _lib.ptr(err), stream)
+            st = lib.skv_packed_attention_gqa(_lib.ptr(qd), B, H, S_q, D, arr, H_kv, c.seq_len, g, _lib.ptr(rows),
+                                              _lib.ptr(counts), _lib.ptr(kn), _lib.ptr(vn), S_new, float(scale),
+                                              _lib.ptr(tiles), tiles.numel(), _lib.ptr(out), _lib.ptr(err), stream)
         else:
             events[0].record()
-            st = lib.skv_stage_kv_tiles(arr, B, H, c.seq_len, D, c._int4_group_of(), _lib.ptr(rows),
-                                        _lib.ptr(counts), _lib.ptr(tiles), tiles.numel(), stream)
+            st = lib.skv_stage_kv_tiles_gqa(arr, B, H_kv, c.seq_len, D, g, _lib.ptr(rows), _lib.ptr(counts),
+                                            _lib.ptr(kn), _lib.ptr(vn), S_new, _lib.ptr(tiles), tiles.numel(), stream)
             _lib.check(st, "packed_attention")
             events[1].record()
-            st = lib.skv_attend_kv_tiles(_lib.ptr(qd), B, H, S_q, D, c.seq_len, _lib.ptr(rows), _lib.ptr(counts),
-                                         float(scale), _lib.ptr(tiles), tiles.numel(), _lib.ptr(out), _lib.ptr(err),
-                                         stream)
+            st = lib.skv_attend_kv_tiles_gqa(_lib.ptr(qd), B, H, S_q, D, H_kv, c.seq_len, _lib.ptr(rows),
+                                             _lib.ptr(counts), S_new, float(scale), _lib.ptr(tiles), tiles.numel(),
+                                             _lib.ptr(out), _lib.ptr(err), stream)
             events[2].record()
     _lib.check(st, "packed_attention")
     if check:

@@ -46,9 +46,10 @@ def _import_reference(path: str):
     from shadowinfer.shadowkv import rd_allocator, precision_plan, packed_kv_cache  # noqa
     from shadowinfer.shadowkv.shadowkv_agent import ShadowKVAgent  # noqa
     from shadowinfer.shadowkv import paged_kv_store, importance_model  # noqa
+    from shadowinfer.models import diffusion_llama  # noqa
     return types.SimpleNamespace(
         rd=rd_allocator, plan=precision_plan, pkc=packed_kv_cache, Agent=ShadowKVAgent, paged=paged_kv_store,
-        imp=importance_model,
+        imp=importance_model, llama=diffusion_llama,
     )
 
 
@@ -254,6 +255,30 @@ def attention_case(R, case, gen, B, H, S, D):
     put(case, "k", k); put(case, "v", v); put(case, "codes", codes); put(case, "q", q)
     put(case, "out", out)
     PINS["cases"][case] = {"kind": "attention", "B": B, "H": H, "S": S, "D": D}
+
+
+def attention_gqa_case(R, case, gen, B, H_kv, n_rep, S_past, S_new, S_q, D, probs=(0.1, 0.3, 0.3, 0.25, 0.05)):
+    """The model attention over a packed past plus this step's own K/V, as DiffusionLlamaAttention
+    runs it (diffusion_llama.py:376-390: cat(past, new), _repeat_kv, softmax(q k^T / sqrt(D)) v),
+    with the past from the reference PackedKVCache (pack -> unpack)."""
+    k, v = kv(gen, B, H_kv, S_past, D)
+    codes = codes_of(gen, S_past, H_kv, probs)
+    packed = R.pkc.PackedKVCache.pack(k, v, R.plan.codes_to_map(codes), group_size=16)["packed_kv"]
+    k_new = torch.randn(B, H_kv, S_new, D, generator=gen)
+    v_new = torch.randn(B, H_kv, S_new, D, generator=gen)
+    q = torch.randn(B, H_kv * n_rep, S_q, D, generator=gen).to(torch.float16)
+    past_k, past_v = packed.unpack()
+    k_all = torch.cat((past_k, k_new), dim=2)
+    v_all = torch.cat((past_v, v_new), dim=2)
+    k_exp = R.llama._repeat_kv(k_all, n_rep)
+    v_exp = R.llama._repeat_kv(v_all, n_rep)
+    scores = torch.matmul(q.float(), k_exp.transpose(-2, -1)) / (D ** 0.5)
+    out = torch.matmul(torch.softmax(scores, dim=-1), v_exp)
+    for name, x in (("k", k), ("v", v), ("codes", codes), ("k_new", k_new), ("v_new", v_new), ("q", q),
+                    ("out", out)):
+        put(case, name, x)
+    PINS["cases"][case] = {"kind": "attention_gqa", "B": B, "H_kv": H_kv, "n_rep": n_rep, "S_past": S_past,
+                           "S_new": S_new, "S_q": S_q, "D": D}
 
 
 def global_budget_case(R, case, gen, B, H, S, D, layers, budget_frac, sink, *, probs=(0.2, 0.3, 0.25, 0.2, 0.05),
@@ -619,6 +644,11 @@ def main():
     global_budget_case(R, "gb_b2_group32", gen, 2, 2, 40, 128, 2, 0.4, 4, group=32, probs=(0.1, 0.3, 0.3, 0.25, 0.05))
     paged_cases(R)
     decision_cases(R)
+    g2 = torch.Generator().manual_seed(20261202)
+    attention_gqa_case(R, "attn_gqa_rep4_d64", g2, 1, 2, 4, 100, 40, 40, 64)
+    attention_gqa_case(R, "attn_gqa_rep2_d128_b2", g2, 2, 2, 2, 96, 40, 40, 128)
+    attention_gqa_case(R, "attn_new_rows_rep1", g2, 1, 3, 1, 70, 33, 50, 64)
+    attention_gqa_case(R, "attn_gqa_past_all_evicted", g2, 1, 2, 2, 20, 17, 30, 64, probs=(0, 0, 0, 0, 1.0))
     full_pins(R)
     np.savez_compressed(SMALL_NPZ, **ARR)
     with open(PINS_JSON, "w") as f:

@@ -135,3 +135,60 @@ def test_attention_shape_errors(skv):
         skv.packed_attention(torch.zeros(1, 3, 8, 128, dtype=torch.float16, device="cuda"), cache)
     with pytest.raises(ValueError, match="4-D"):
         skv.packed_attention(torch.zeros(2, 8, 128, dtype=torch.float16, device="cuda"), cache)
+
+
+# ---------------------------------------------------------------- grouped-query + this step's K/V
+@pytest.mark.parametrize("case", sorted(c for c, v in load_pins()["cases"].items() if v["kind"] == "attention_gqa"))
+def test_gqa_attention_matches_reference_fixture(case, skv, golden_small):
+    """DiffusionLlamaAttention over cat(packed past, new K/V) with repeated KV heads, as the
+    reference computes it (recorded by make_golden.py)."""
+    a = case_arrays(golden_small, case)
+    cache = _pack(skv, a["k"], a["v"], a["codes"])
+    out = skv.packed_attention(torch.from_numpy(a["q"]).cuda(), cache, k_new=torch.from_numpy(a["k_new"]).cuda(),
+                               v_new=torch.from_numpy(a["v_new"]).cuda())
+    assert out.shape == a["out"].shape
+    assert rel_l2(out.cpu().numpy(), a["out"]) < REL_L2_TOL
+
+
+GQA_CASES = [
+    # B, H_kv, n_rep, S_past, S_new, S_q, D, code probabilities
+    (1, 4, 4, 500, 128, 128, 128, (0.1, 0.3, 0.3, 0.2, 0.1)),     # new rows fill a whole tile
+    (2, 2, 2, 257, 100, 100, 64, (0.0, 0.3, 0.4, 0.3, 0.0)),      # packed rows end mid-tile
+    (1, 8, 1, 300, 1, 64, 128, (0.2, 0.2, 0.2, 0.2, 0.2)),        # one new row
+    (1, 2, 8, 64, 300, 300, 128, (0.0, 1.0, 0.0, 0.0, 0.0)),      # more new rows than cached
+    (1, 4, 2, 200, 0, 150, 64, (0.1, 0.2, 0.3, 0.3, 0.1)),        # GQA without new rows
+    (1, 3, 2, 50, 64, 77, 64, (0.0, 0.0, 0.0, 0.0, 1.0)),         # every cached entry evicted
+]
+
+
+@pytest.mark.parametrize("B,H_kv,rep,S,SN,SQ,D,probs", GQA_CASES)
+def test_gqa_attention_matches_oracle(skv, B, H_kv, rep, S, SN, SQ, D, probs):
+    rng = np.random.default_rng(S * 7 + SN * 3 + rep)
+    k = rng.standard_normal((B, H_kv, S, D)).astype(np.float32)
+    v = rng.standard_normal((B, H_kv, S, D)).astype(np.float32)
+    codes = rng.choice(5, size=(S, H_kv), p=probs).astype(np.int8)
+    kn = rng.standard_normal((B, H_kv, SN, D)).astype(np.float32)
+    vn = rng.standard_normal((B, H_kv, SN, D)).astype(np.float32)
+    q = rng.standard_normal((B, H_kv * rep, SQ, D)).astype(np.float16)
+    cache = _pack(skv, k, v, codes)
+    out = skv.packed_attention(torch.from_numpy(q).cuda(), cache,
+                               k_new=torch.from_numpy(kn).cuda() if SN else None,
+                               v_new=torch.from_numpy(vn).cuda() if SN else None).cpu().numpy()
+    ref = O.packed_attention(q.astype(np.float32), O.pack(k, v, O.plan_from_codes(codes), 16),
+                             k_new=kn if SN else None, v_new=vn if SN else None)
+    assert rel_l2(out, ref) < REL_L2_TOL
+    err = np.linalg.norm(out - ref, axis=-1) / np.maximum(np.linalg.norm(ref, axis=-1), 1e-30)
+    assert float(err.max()) < 1e-2
+
+
+def test_gqa_argument_checks(skv):
+    k = torch.randn(1, 2, 40, 64, device="cuda")
+    cache = skv.PackedKVCache.pack(k, k, None, 16, plan=skv.PrecisionPlan.from_codes(
+        torch.ones(40, 2, dtype=torch.int8, device="cuda")))["packed_kv"]
+    with pytest.raises(ValueError, match="mismatch"):
+        skv.packed_attention(torch.randn(1, 3, 8, 64, device="cuda"), cache)          # 3 heads over 2
+    with pytest.raises(ValueError, match="k_new"):
+        skv.packed_attention(torch.randn(1, 4, 8, 64, device="cuda"), cache, k_new=torch.randn(1, 2, 5, 64))
+    with pytest.raises(ValueError, match="k_new/v_new"):
+        skv.packed_attention(torch.randn(1, 4, 8, 64, device="cuda"), cache, k_new=torch.randn(1, 4, 5, 64),
+                             v_new=torch.randn(1, 4, 5, 64))

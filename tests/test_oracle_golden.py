@@ -254,3 +254,14 @@ def test_irap_importance(case, golden_small):
         assert da is None
     else:
         assert abs(da - pin["delta_a"]) <= 1e-5 * abs(pin["delta_a"])
+
+
+@pytest.mark.parametrize("case", _cases(_pins(), "attention_gqa"))
+def test_attention_gqa(case, golden_small):
+    """Grouped-query attention over a packed past plus this step's K/V (DiffusionLlamaAttention)."""
+    a = case_arrays(golden_small, case)
+    cache = O.pack(a["k"], a["v"], O.plan_from_codes(a["codes"]), 16)
+    out = O.packed_attention(a["q"].astype(np.float32), cache, k_new=a["k_new"], v_new=a["v_new"])
+    ref = a["out"].astype(np.float64)
+    rel = np.linalg.norm(out - ref) / np.linalg.norm(ref)
+    assert rel < 1e-5, rel
