@@ -65,6 +65,7 @@ enum AttnError { kErrNone = 0, kErrKFull = 1, kErrKEmpty = 2, kErrSFull = 3, kEr
 __host__ __device__ constexpr int staged_tile_bytes(int D) { return (D / 64) * kBN * 128; }
 
 constexpr int kMaxHeads = 256;     // heads per launch (the schedule keeps a per-head prefix in smem)
+constexpr int kMaxPartners = 8;    // CTAs that can hold later parts of one unit (merged by its first part)
 constexpr int kUnitRows = 2 * kBM;  // queries per work unit
 
 template <int D>
@@ -373,6 +374,53 @@ __device__ __forceinline__ bool wait_flag(const int* flag, int target, int* err,
     }
 }
 
+// Epilogue of a unit's first part when its later parts sit in np >= 2 other CTAs: rows rA and
+// rB of this lane's 16x256b share, O = O_this * fa + sum_i O_i * 2^(m_i - m) / l_total, one
+// partner at a time.  Kept out of line: the path is rare and its registers stay out of the
+// softmax loop.
+template <int D>
+__device__ __noinline__ void merge_parts(const AttnParams& p, uint32_t tO, int hf, int rA, int rB, float faA,
+                                         float faB, float mA, float mB, float iA, float iB, int np, int slot, int rt,
+                                         int lane, int nrows, float* dst, uint64_t* o_empty) {
+#pragma unroll 1
+    for (int c = 0; c < D / 32; ++c) {
+        uint32_t o[16];
+        tmem_ld16x256b_x4(tO + c * 32 + ((uint32_t)(hf * 16) << 16), o);
+        tmem_wait_ld();
+        if (hf == 1 && c == D / 32 - 1) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(o_empty);
+        }
+        float2 va[4], vb[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            va[k] = make_float2(__uint_as_float(o[4 * k]) * faA, __uint_as_float(o[4 * k + 1]) * faA);
+            vb[k] = make_float2(__uint_as_float(o[4 * k + 2]) * faB, __uint_as_float(o[4 * k + 3]) * faB);
+        }
+        for (int i = 0; i < np; ++i) {
+            const size_t si2 = (size_t)(slot + i) * kUnitRows + rt;
+            const float fA = ex2(__ldcg(p.part_ml + si2 + rA).x - mA) * iA;
+            const float fB = ex2(__ldcg(p.part_ml + si2 + rB).x - mB) * iB;
+            const float* srci = p.part_o + si2 * D;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const int col = c * 32 + 8 * k + 2 * (lane & 3);
+                const float2 xa = __ldcg(reinterpret_cast<const float2*>(srci + (int64_t)rA * D + col));
+                const float2 xb = __ldcg(reinterpret_cast<const float2*>(srci + (int64_t)rB * D + col));
+                va[k] = make_float2(fmaf(xa.x, fA, va[k].x), fmaf(xa.y, fA, va[k].y));
+                vb[k] = make_float2(fmaf(xb.x, fB, vb[k].x), fmaf(xb.y, fB, vb[k].y));
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const int col = c * 32 + 8 * k + 2 * (lane & 3);
+            if (rA < nrows) st_global_f2(dst + (int64_t)rA * D + col, va[k]);
+            if (rB < nrows) st_global_f2(dst + (int64_t)rB * D + col, vb[k]);
+        }
+    }
+}
+
 // Persistent, cooperatively launched (one CTA per SM, all resident): warps 0-7 softmax,
 // warp 8 loader, warp 9 MMA issuer, as described at the top of this file, looping over the
 // CTA's segments.  Barrier phases run on across segments (per step for the KV ring, S and P;
@@ -446,12 +494,15 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     sched.QP = p.QP;
     sched.per_batch = (long long)p.QP * hp[p.H];
     sched.pos = sched.end = 0;
+    // CTA c takes steps [c*T/G, (c+1)*T/G).  G keeps at least ceil(max_nt / kMaxPartners) steps
+    // per CTA, so a unit spans at most kMaxPartners + 1 CTAs
+    const long long T = sched.per_batch * p.B;
+    int G = 0;
     {
-        const long long T = sched.per_batch * p.B;
         const int ntm = misc[0];
         if (T > 0) {
-            const long long cap = T / ntm;
-            const int G = (int)min((long long)gridDim.x, cap);
+            const long long cap = T / ((ntm + kMaxPartners - 1) / kMaxPartners);
+            G = (int)min((long long)gridDim.x, cap);
             if ((int)blockIdx.x < G) {
                 sched.pos = (long long)blockIdx.x * T / G;
                 sched.end = ((long long)blockIdx.x + 1) * T / G;
@@ -477,11 +528,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             const int n_stored = cnt[0] + cnt[1] + cnt[2] + cnt[3] + p.S_new;     // packed + dense rows
             const int n_ev = cnt[4];
             const bool first_part = sg.j0 == 0;
-            if (sg.j0 > 0 && sg.j1 < sg.nt) {            // cannot happen with the schedule above
-                atomicCAS(p.err, 0, (int)kErrSchedule);
-                ok = false;
-                break;
-            }
             // evicted rows (logit 0, no value) are counted once, by the unit's first part
             float m_ref = first_part && n_ev > 0 ? 0.0f : -INFINITY;
             float l = first_part ? (float)n_ev : 0.0f;
@@ -559,30 +605,50 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             // ---------------------------------------------------------------- epilogue
             if (!warp_wait(&o_full[t], (uint32_t)(si & 1), p.err, kErrOFull)) { ok = false; break; }
             tc_fence_after();
-            const bool split_tail = sg.j0 > 0;                   // second part: publish, unnormalised
-            const bool split_head = first_part && sg.j1 < sg.nt; // first part: merge the second
+            const bool split_tail = sg.j0 > 0;                   // a later part: publish, unnormalised
+            const bool split_head = first_part && sg.j1 < sg.nt; // first part: merge the later parts
+            // later parts live in CTAs blockIdx.x + 1 .. + np (each publishes into its own slot)
+            int np = 0;
+            if (split_head) {
+                const long long ue = ((long long)blockIdx.x + 1) * T / G + (sg.nt - sg.j1);   // unit end
+                while (np < kMaxPartners && ((long long)blockIdx.x + 1 + np) * T / G < ue) ++np;
+            }
             const int slot = blockIdx.x + 1;
             float mB = -INFINITY, lB = 0.0f;
-            if (split_head) {
+            for (int i = 0; i < np; ++i) {
                 int got = 1;
-                if (lane == 0) got = wait_flag(p.part_flag + slot, kSoftmaxWarps, p.err, kErrPartial) ? 1 : 0;
+                if (lane == 0) got = wait_flag(p.part_flag + slot + i, kSoftmaxWarps, p.err, kErrPartial) ? 1 : 0;
                 got = __shfl_sync(0xffffffffu, got, 0);
                 __syncwarp();
                 if (!got) { ok = false; break; }
+            }
+            if (!ok) break;
+            if (np == 1) {
                 const float2 ml = __ldcg(p.part_ml + (size_t)slot * kUnitRows + rt + lane);
                 mB = ml.x;
                 lB = ml.y;
             }
             // per-row factors (thread = row): O = O_this * fa + O_other * fb
             float fa = 1.0f, fb = 0.0f;
-            if (!split_tail) {
+            float mall = m_ref, inv_all = 0.0f;                  // np >= 2: common max and 1 / total
+            if (!split_tail && np <= 1) {
                 const float m = fmaxf(m_ref, mB);
                 fa = m_ref == -INFINITY ? 0.0f : ex2(m_ref - m);
-                fb = split_head ? ex2(mB - m) : 0.0f;
+                fb = np == 1 ? ex2(mB - m) : 0.0f;
                 const float lt = l * fa + lB * fb;
                 const float inv = lt > 0.0f ? 1.0f / lt : 0.0f;
                 fa *= inv;
                 fb *= inv;
+            } else if (!split_tail) {
+                for (int i = 0; i < np; ++i)
+                    mall = fmaxf(mall, __ldcg(p.part_ml + (size_t)(slot + i) * kUnitRows + rt + lane).x);
+                float lt = m_ref == -INFINITY ? 0.0f : l * ex2(m_ref - mall);
+                for (int i = 0; i < np; ++i) {
+                    const float2 ml = __ldcg(p.part_ml + (size_t)(slot + i) * kUnitRows + rt + lane);
+                    lt += ml.y * ex2(ml.x - mall);
+                }
+                inv_all = lt > 0.0f ? 1.0f / lt : 0.0f;
+                fa = m_ref == -INFINITY ? 0.0f : ex2(m_ref - mall) * inv_all;
             }
             const int row0 = sg.qp * kUnitRows + rt;             // query row within the head
             float* dst = split_tail ? p.part_o + ((size_t)blockIdx.x * kUnitRows + rt) * D
@@ -597,7 +663,15 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                 const int rA = hf * 16 + (lane >> 2), rB = rA + 8;
                 const float faA = __shfl_sync(0xffffffffu, fa, rA), faB = __shfl_sync(0xffffffffu, fa, rB);
                 const float fbA = __shfl_sync(0xffffffffu, fb, rA), fbB = __shfl_sync(0xffffffffu, fb, rB);
-                if (split_head) {
+                if (np >= 2) {
+                    // a unit spread over three or more CTAs (small grids of units)
+                    const float mA = __shfl_sync(0xffffffffu, mall, rA), mBr = __shfl_sync(0xffffffffu, mall, rB);
+                    const float iA = __shfl_sync(0xffffffffu, inv_all, rA), iB = __shfl_sync(0xffffffffu, inv_all, rB);
+                    merge_parts<D>(p, tO, hf, rA, rB, faA, faB, mA, mBr, iA, iB, np, slot, rt, lane, nrows, dst,
+                                   &o_empty[t]);
+                    continue;
+                }
+                if (np == 1) {
                     // a unit cut between two CTAs, merged here (once per CTA at most): all of this
                     // half's partial values first, so their loads overlap, then O chunk by chunk
                     float2 pa[D / 32][4], pb[D / 32][4];

@@ -114,24 +114,38 @@ __device__ __forceinline__ uint32_t pack_u4(int a, int b, uint32_t c) {
 
 constexpr float kRoundMagic = 12582912.0f;   // 1.5 * 2^23: adding it rounds |y| < 2^22 to an integer
 
-// q[i] = clamp(rint(fl(x[i] / s)), lo, hi) for 16 values; qf[i] = (float)q[i].
+// max that propagates NaN (so a NaN deviation still sends the values to the exact path)
+__device__ __forceinline__ float max_nan(float a, float b) {
+    float d;
+    asm("max.NaN.f32 %0, %1, %2;" : "=f"(d) : "f"(a), "f"(b));
+    return d;
+}
+
+// q[i] = clamp(rint(fl(x[i] / s)), lo, hi) + OFF for 16 values; qf[i] = the rounded value without
+// OFF.  OFF (8 for int4 nibbles) rides in the rounding constant: the integer part of
+// y + 1.5*2^23 + OFF is rint(y) + OFF.  Values are rounded from y = x * rcp(s); if any lies within
+// 1e-4 of a half-integer (or is not finite) all 16 take the exact IEEE division.  Out-of-range
+// codes are clamped by the saturating packs that consume q.
+template <int OFF>
 __device__ __forceinline__ void quant16(const float (&x)[16], float s, float r, int lo, int hi, int (&q)[16],
                                         float (&qf)[16]) {
-    bool slow = false;
+    constexpr float kM = kRoundMagic + (float)OFF;
+    float dev = 0.0f;
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
         const float y = __fmul_rn(x[i], r);
-        const float t = __fadd_rn(y, kRoundMagic);
-        const float rf = __fsub_rn(t, kRoundMagic);
-        slow |= !(fabsf(__fsub_rn(y, rf)) < 0.4999f);
+        const float t = __fadd_rn(y, kM);
+        const float rf = __fsub_rn(t, kM);
+        dev = max_nan(dev, fabsf(__fsub_rn(y, rf)));
         q[i] = __float_as_int(t) - 0x4B400000;
         qf[i] = rf;
     }
-    if (slow) {
+    if (!(dev < 0.4999f)) {
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-            q[i] = quant_value(x[i], s, lo, hi);
-            qf[i] = (float)q[i];
+            const int v = quant_value(x[i], s, lo, hi);
+            q[i] = v + OFF;
+            qf[i] = (float)v;
         }
     }
 }
@@ -172,15 +186,15 @@ __device__ __forceinline__ void pack_lane(const float (&x)[16], int code, int64_
         const float s = quant_scale(i4 ? m_grp : m_row, i4 ? 7.0f : 127.0f);
         const float r = __frcp_rn(s);
         int q[16];
-        quant16(x, s, r, i4 ? -8 : -128, i4 ? 7 : 127, q, dense);
         if (i4) {
+            quant16<8>(x, s, r, -8, 7, q, dense);         // q = code + 8, the stored nibble
             uint32_t w[2];
 #pragma unroll
             for (int k = 0; k < 2; ++k) {
-                uint32_t a = pack_u4(q[8 * k + 6] + 8, q[8 * k + 7] + 8, 0u);
-                a = pack_u4(q[8 * k + 4] + 8, q[8 * k + 5] + 8, a);
-                a = pack_u4(q[8 * k + 2] + 8, q[8 * k + 3] + 8, a);
-                w[k] = pack_u4(q[8 * k] + 8, q[8 * k + 1] + 8, a);
+                uint32_t a = pack_u4(q[8 * k + 6], q[8 * k + 7], 0u);
+                a = pack_u4(q[8 * k + 4], q[8 * k + 5], a);
+                a = pack_u4(q[8 * k + 2], q[8 * k + 3], a);
+                w[k] = pack_u4(q[8 * k], q[8 * k + 1], a);
             }
             const int64_t rb = (int64_t)B * D / 2;
             *reinterpret_cast<uint2*>(reinterpret_cast<uint8_t*>(payload) + pos * rb + (int64_t)b * (D / 2) + l * 8) =
@@ -188,6 +202,7 @@ __device__ __forceinline__ void pack_lane(const float (&x)[16], int code, int64_
             const int lpg = G >> 4;   // lanes per int4 group
             if ((l & (lpg - 1)) == 0) scale[row * (D / G) + (l * 16) / G] = s;
         } else {
+            quant16<0>(x, s, r, -128, 127, q, dense);
             uint32_t w[4];
 #pragma unroll
             for (int k = 0; k < 4; ++k) w[k] = pack_s8(q[4 * k + 1], q[4 * k], pack_s8(q[4 * k + 3], q[4 * k + 2], 0u));

@@ -107,6 +107,23 @@ def test_attention_more_units_than_sms(skv):
     _check(skv, k, v, codes, q)
 
 
+@pytest.mark.parametrize("B,H,S,SQ,D,evict", [
+    (1, 1, 4096, 256, 128, 0.0),    # one unit of 32 tiles over 8 CTAs: 7 later parts merged
+    (1, 2, 2000, 100, 64, 0.2),     # two units, ragged queries, evicted rows in multi-part units
+    (2, 3, 1100, 300, 128, 0.05),   # 12 units of 9 tiles: parts of 2-3 CTAs
+])
+def test_attention_units_spread_over_many_ctas(skv, B, H, S, SQ, D, evict):
+    """Few units with many KV tiles: the steps are spread over more CTAs than units, so a
+    unit's first part merges the partial results of several later parts."""
+    rng = np.random.default_rng(S + H)
+    k = rng.standard_normal((B, H, S, D)).astype(np.float32)
+    v = rng.standard_normal((B, H, S, D)).astype(np.float32)
+    p_keep = (1.0 - evict) / 3
+    codes = rng.choice(5, size=(S, H), p=(0.0, p_keep, p_keep, p_keep, evict)).astype(np.int8)
+    q = (rng.standard_normal((B, H, SQ, D)) * 2.0).astype(np.float16)
+    _check(skv, k, v, codes, q)
+
+
 def test_attention_all_evicted_head_and_after_evict(skv):
     rng = np.random.default_rng(5)
     B, H, S, D = 1, 3, 200, 128
