@@ -22,7 +22,8 @@ kernel), timed with CUDA events around each launch in the timed region.
 
 The line also carries ``attention``: packed attention over one cfg3 layer
 (B=1, H=32, S=4096, D=128, codes 20/50/30 % fp16/int8/int4), heads sharded over
-the ranks with an NCCL all-gather of the outputs, as tokens/s of the 32-layer
+the ranks, the outputs all-gathered by the kernel's own stores into every rank's
+buffer (CUDA IPC mappings, NVLink), as tokens/s of the 32-layer
 stack and as tensor-core roofline of the kernel; ``global_budget``:
 KVCacheManager.enforce_global_budget over 8 packed layers of that shape;
 ``paged_store``: the PagedKVStore append-mode run of the reference's own paged
@@ -231,8 +232,9 @@ def run_reference(args):
 def attention_phase(args, world, rank, dev, dist, lib, tensor_peak):
     """Packed attention on one cfg3 layer, heads sharded over ranks, outputs all-gathered.
 
-    One step = the layer's attention (this rank's heads) + an NCCL all-gather of the fp32
-    outputs on a side stream, so the gather of one step overlaps the next step's kernel.
+    One step = the layer's attention over this rank's heads; with N > 1 its epilogue stores
+    every output row into all ranks' fp32 [B, H, S, D] buffers (CUDA IPC mappings over NVLink),
+    so the all-gather runs inside the kernel, overlapped with the attention math.
     """
     import torch
 
@@ -253,23 +255,18 @@ def attention_phase(args, world, rank, dev, dist, lib, tensor_peak):
     cache = PackedKVCache.pack(k.to(dev), v.to(dev), None, c["group"], plan=PrecisionPlan.from_codes(codes))["packed_kv"]
     qd = q[:, h0:h0 + hs].contiguous().to(dev)
     packed_attention(qd, cache)                        # builds the head index, checks the error word
-    from shadow_infer_b200.shadowkv.sharding import all_gather_heads
-    gathered = torch.empty(B, H, S, D, dtype=torch.float32, device=dev)
-    comm = torch.cuda.Stream(device=dev)
+    # N > 1: the all-gather of the head-sharded outputs is fused into the attention epilogue --
+    # every finished row is stored into all ranks' [B, H, S, D] buffers over NVLink
+    from shadow_infer_b200.shadowkv.sharding import PeerOutputs
+    peers = PeerOutputs((B, H, S, D), device=dev) if world > 1 else None
     steps = max(3, min(args.steps, 32))
     kev = [tuple(torch.cuda.Event(enable_timing=True) for _ in range(3)) for _ in range(steps)]
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
 
     def step(i=None):
         # events: before the staging kernel, between the two kernels, after the attention kernel
-        out = packed_attention(qd, cache, check=False, events=kev[i] if i is not None else None)
-        if world > 1:
-            done = torch.cuda.Event()
-            done.record()
-            with torch.cuda.stream(comm):
-                comm.wait_event(done)
-                all_gather_heads(out, out=gathered)
-            out.record_stream(comm)
-        return out
+        return packed_attention(qd, cache, check=False, events=kev[i] if i is not None else None,
+                                peer_outputs=peers, head_offset=h0)
 
     for _ in range(3):
         step()
@@ -282,14 +279,13 @@ def attention_phase(args, world, rank, dev, dist, lib, tensor_peak):
     t0.record()
     for i in range(steps):
         step(i)
-    if world > 1:
-        tail = torch.cuda.Event()
-        tail.record(comm)
-        torch.cuda.current_stream().wait_event(tail)
     t1.record()
     torch.cuda.synchronize()
     launches = lib.skv_launch_count() - n0
-    packed_attention(qd, cache)                        # error word of the last launch
+    packed_attention(qd, cache, peer_outputs=peers, head_offset=h0)   # error word of the last launch
+    if world > 1:
+        dist.barrier()
+        peers.close()
     ms = torch.tensor([t0.elapsed_time(t1) / steps], device=dev, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(ms, op=dist.ReduceOp.MAX)
@@ -303,7 +299,9 @@ def attention_phase(args, world, rank, dev, dist, lib, tensor_peak):
     res = {
         "metric": "packed-attn tokens/s (32-layer stack, cfg3)",
         "value": B * S / (L * ms / 1e3), "unit": "tokens/s", "ms_per_layer": ms, "steps": steps,
-        "scaling": "strong (heads sharded over GPUs, NCCL all-gather of outputs)",
+        "scaling": "strong (heads sharded over GPUs; outputs all-gathered by the attention epilogue's "
+                   "stores into every rank's buffer over NVLink)",
+        "attention_ctas": sms,
         "config": {"workload": "cfg3: packed K/V codes 20/50/30 fp16/int8/int4, fp16 queries, non-causal",
                    "B": B, "H": H, "S_q": S, "S_kv": S, "D": D, "layers": L, "heads_per_gpu": hs},
         "roofline": {"kernel": "packed_attention_kernel", "bound": "tensor",

@@ -184,11 +184,31 @@ int skv_stage_kv_tiles_gqa(const skv_bucket* buckets, int B, int H_kv, int S_kv,
                            int S_new, void* scratch, size_t scratch_bytes, void* stream);
 int skv_attend_kv_tiles_gqa(const void* q, int B, int H_q, int S_q, int D, int H_kv, int S_kv, const int32_t* rows,
                             const int32_t* counts, int S_new, float scale, const void* scratch, size_t scratch_bytes,
-                            float* out, int32_t* error_flag, void* stream);
+                            float* out, int32_t* error_flag, int max_ctas, void* stream);
+/* The attention with its outputs stored into n_peers buffers [B, H_out, S_q, D] (device array of
+ * device pointers: every rank's output buffer, mapped into this process), this call's query heads
+ * at [head_offset, head_offset + H_q): the head-sharded all-gather of the outputs fused into the
+ * epilogue (plain stores over NVLink; no multicast).  The buffers are complete once every
+ * rank's call has finished. */
+int skv_attend_kv_tiles_peers(const void* q, int B, int H_q, int S_q, int D, int H_kv, int S_kv, const int32_t* rows,
+                              const int32_t* counts, int S_new, float scale, const void* scratch,
+                              size_t scratch_bytes, float* const* out_peers, int n_peers, int head_offset,
+                              int H_out, int32_t* error_flag, int max_ctas, void* stream);
+/* Peer mappings for out_peers (CUDA IPC between the processes of one node).  export: the
+ * skv_ipc_handle_bytes() handle of the allocation holding ptr and ptr's byte offset in it.
+ * open (on the device that will launch the kernel): maps another process's exported buffer
+ * with peer access from the current device; *ptr = mapping + offset, *base is what
+ * skv_ipc_close takes.  A process opens each peer allocation once. */
+int skv_ipc_handle_bytes(void);
+int skv_ipc_export(const void* ptr, void* handle, int64_t* offset);
+int skv_ipc_open(const void* handle, int64_t offset, void** base, void** ptr);
+int skv_ipc_close(void* base);
+/* max_ctas: CTAs of the persistent attention kernel (0 = one per SM); fewer leave SMs free for
+ * work that should run beside it (e.g. the NCCL all-gather of the previous layer's outputs). */
 int skv_packed_attention_gqa(const void* q, int B, int H_q, int S_q, int D, const skv_bucket* buckets, int H_kv,
                              int S_kv, int int4_group, const int32_t* rows, const int32_t* counts,
                              const float* k_new, const float* v_new, int S_new, float scale, void* scratch,
-                             size_t scratch_bytes, float* out, int32_t* error_flag, void* stream);
+                             size_t scratch_bytes, float* out, int32_t* error_flag, int max_ctas, void* stream);
 
 /* ---- cross-layer budget: KVCacheManager.enforce_global_budget
  * (shadowinfer/shadowkv/kv_cache_manager.py:129-200).  The reference sorts every non-sink

@@ -85,10 +85,17 @@ _SIGNATURES = {
     "skv_stage_kv_tiles_gqa": (c_int, [ctypes.POINTER(SkvBucket), c_int, c_int, c_int, c_int, c_int, c_void_p,
                                        c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_size_t, c_void_p]),
     "skv_attend_kv_tiles_gqa": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_int,
-                                        ctypes.c_float, c_void_p, c_size_t, c_void_p, c_void_p, c_void_p]),
+                                        ctypes.c_float, c_void_p, c_size_t, c_void_p, c_void_p, c_int, c_void_p]),
+    "skv_attend_kv_tiles_peers": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_void_p, c_void_p,
+                                          c_int, ctypes.c_float, c_void_p, c_size_t, c_void_p, c_int, c_int, c_int,
+                                          c_void_p, c_int, c_void_p]),
+    "skv_ipc_handle_bytes": (c_int, []),
+    "skv_ipc_export": (c_int, [c_void_p, c_void_p, ctypes.POINTER(c_int64)]),
+    "skv_ipc_open": (c_int, [c_void_p, c_int64, ctypes.POINTER(c_void_p), ctypes.POINTER(c_void_p)]),
+    "skv_ipc_close": (c_int, [c_void_p]),
     "skv_packed_attention_gqa": (c_int, [c_void_p, c_int, c_int, c_int, c_int, ctypes.POINTER(SkvBucket), c_int, c_int,
                                          c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int, ctypes.c_float,
-                                         c_void_p, c_size_t, c_void_p, c_void_p, c_void_p]),
+                                         c_void_p, c_size_t, c_void_p, c_void_p, c_int, c_void_p]),
     "skv_budget_candidates": (c_int, [c_void_p, c_int, c_int, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p,
                                       c_void_p, c_void_p]),
     "skv_rank_select_scratch_bytes": (c_size_t, [c_int64]),

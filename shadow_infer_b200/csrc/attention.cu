@@ -68,7 +68,7 @@ constexpr int kMaxHeads = 256;     // heads per launch (the schedule keeps a per
 constexpr int kMaxPartners = 8;    // CTAs that can hold later parts of one unit (merged by its first part)
 constexpr int kUnitRows = 2 * kBM;  // queries per work unit
 
-template <int D>
+template <int D, bool PEERS = false>
 struct AttnLayout {
     static constexpr int NA = D / 64;                   // 128-byte swizzle atoms per row
     static constexpr int kTile = staged_tile_bytes(D);  // one 128-row tile (Q, K or V)
@@ -77,13 +77,17 @@ struct AttnLayout {
     static constexpr int kV = kK + 2 * kTile;           // two V stages
     static constexpr int kBar = kV + 2 * kTile;
     static constexpr int kNumBars = 24;
-    static constexpr int kHP = kBar + kNumBars * 8;     // int64 [kMaxHeads + 1]: prefix of KV tiles per head
-    static constexpr int kMisc = kHP + (kMaxHeads + 1) * 8;
+    static constexpr int kHP = kBar + kNumBars * 8;     // int32 [kMaxHeads + 1]: prefix of KV tiles per head
+    // PEERS: per softmax warp, 8 output rows staged for the bulk stores into every rank's buffer
+    static constexpr int kOut = (kHP + (kMaxHeads + 1) * 4 + 127) / 128 * 128;
+    static constexpr int kOutRows = 8;
+    static constexpr int kMisc = kOut + (PEERS ? kSoftmaxWarps * kOutRows * D * 4 : 0);
     static constexpr int kTmemSlot = kMisc + 16;
     static constexpr int kBytes = kTmemSlot + 16;
     // + slack to align the base to 1024 B; at least 120 KB so that one CTA occupies an SM and
     // its 512-column TMEM allocation never waits for another CTA's
     static constexpr int kAlloc = (kBytes + 1024) > 120 * 1024 ? (kBytes + 1024) : 120 * 1024;
+    static_assert(kAlloc <= 227 * 1024, "attention shared memory beyond the per-CTA limit");
 };
 
 struct AttnParams {
@@ -100,6 +104,10 @@ struct AttnParams {
     int* part_flag;            // [slots]: softmax warps that have published their rows
     int B, H, S_q, S_kv, G, ntmax, QP, slots;
     int H_kv, rep, S_new;      // query head h reads KV head h / rep (grouped-query attention)
+    // outputs written straight into n_peers buffers [B, H_out, S_q, D] (this rank's heads at
+    // head_off; peers' memory over NVLink), or into `out` [B, H, S_q, D] when n_peers == 0
+    float* const* peers;
+    int n_peers, head_off, H_out;
     float scale_log2;          // softmax scale * log2(e)
     int* err;
 };
@@ -318,7 +326,7 @@ struct Segment {
 };
 
 struct Schedule {
-    const long long* hp;       // [H + 1] prefix of KV tiles per head
+    const int* hp;             // [H + 1] prefix of KV tiles per head
     int H, QP;
     long long per_batch;       // QP * hp[H]
     long long pos, end;
@@ -374,14 +382,96 @@ __device__ __forceinline__ bool wait_flag(const int* flag, int target, int* err,
     }
 }
 
+// One float2 of the final output at element offset idx of the [B, H_out, S_q, D] layout: into
+// every peer's buffer, or into `out`.
+template <bool PEERS>
+__device__ __forceinline__ void out_store(const AttnParams& p, int64_t idx, float2 v) {
+    if (!PEERS) {
+        st_global_f2(p.out + idx, v);
+        return;
+    }
+    for (int r = 0; r < p.n_peers; ++r) st_global_f2(p.peers[r] + idx, v);
+}
+
+// Peer epilogue: a softmax warp stages 8 finished output rows -- contiguous in every rank's
+// buffer -- in its shared-memory slot and sends them with one bulk copy per rank, so whole rows
+// cross NVLink as large writes and the warp does not stall on remote stores.
+// stage_acquire: the copies that read the slot last time have read it (the slot may be rewritten).
+__device__ __forceinline__ void stage_acquire(int lane) {
+    if (lane == 0) bulk_wait_read0();
+    __syncwarp();
+}
+// this lane's two values of chunk c, part k of slot row (lane >> 2) (the 16x256b share)
+template <int D>
+__device__ __forceinline__ void stage_put(float* slot, int lane, int c, int k, float2 v) {
+    *reinterpret_cast<float2*>(slot + (lane >> 2) * D + c * 32 + 8 * k + 2 * (lane & 3)) = v;
+}
+// slot rows [0, n) -> element idx of every rank's buffer
+template <int D>
+__device__ __noinline__ void stage_flush(const AttnParams& p, const float* slot, int lane, int64_t idx, int n) {
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (n <= 0) return;
+    for (int r = 0; r < p.n_peers; ++r) {
+        float* g = p.peers[r] + idx;
+        if ((reinterpret_cast<uintptr_t>(g) & 15) == 0) {
+            if (lane == 0) bulk_s2g(g, slot, (uint32_t)(n * D * 4));
+        } else {
+            for (int e = lane; e < n * D; e += 32) g[e] = slot[e];
+        }
+    }
+    if (lane == 0) bulk_commit();
+}
+
 // Epilogue of a unit's first part when its later parts sit in np >= 2 other CTAs: rows rA and
 // rB of this lane's 16x256b share, O = O_this * fa + sum_i O_i * 2^(m_i - m) / l_total, one
 // partner at a time.  Kept out of line: the path is rare and its registers stay out of the
 // softmax loop.
-template <int D>
+template <int D, bool PEERS>
 __device__ __noinline__ void merge_parts(const AttnParams& p, uint32_t tO, int hf, int rA, int rB, float faA,
                                          float faB, float mA, float mB, float iA, float iB, int np, int slot, int rt,
-                                         int lane, int nrows, float* dst, uint64_t* o_empty) {
+                                         int lane, int nrows, int64_t obase, uint64_t* o_empty, float* oslot) {
+    if constexpr (PEERS) {
+        // rows rA (slot pass 0) then rows rB (pass 1), each staged whole and bulk-stored
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+            const int r = half ? rB : rA;
+            const float fr = half ? faB : faA, mr = half ? mB : mA, ir = half ? iB : iA;
+            stage_acquire(lane);
+#pragma unroll 1
+            for (int c = 0; c < D / 32; ++c) {
+                uint32_t o[16];
+                tmem_ld16x256b_x4(tO + c * 32 + ((uint32_t)(hf * 16) << 16), o);
+                tmem_wait_ld();
+                if (hf == 1 && half == 1 && c == D / 32 - 1) {
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(o_empty);
+                }
+                float2 v[4];
+#pragma unroll
+                for (int k = 0; k < 4; ++k)
+                    v[k] = make_float2(__uint_as_float(o[4 * k + 2 * half]) * fr,
+                                       __uint_as_float(o[4 * k + 2 * half + 1]) * fr);
+                for (int i = 0; i < np; ++i) {
+                    const size_t si2 = (size_t)(slot + i) * kUnitRows + rt;
+                    const float f = ex2(__ldcg(p.part_ml + si2 + r).x - mr) * ir;
+                    const float* srci = p.part_o + si2 * D;
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        const int col = c * 32 + 8 * k + 2 * (lane & 3);
+                        const float2 x = __ldcg(reinterpret_cast<const float2*>(srci + (int64_t)r * D + col));
+                        v[k] = make_float2(fmaf(x.x, f, v[k].x), fmaf(x.y, f, v[k].y));
+                    }
+                }
+#pragma unroll
+                for (int k = 0; k < 4; ++k) stage_put<D>(oslot, lane, c, k, v[k]);
+            }
+            const int r0 = hf * 16 + half * 8;
+            stage_flush<D>(p, oslot, lane, obase + (int64_t)r0 * D, min(8, nrows - r0));
+        }
+        return;
+    }
 #pragma unroll 1
     for (int c = 0; c < D / 32; ++c) {
         uint32_t o[16];
@@ -415,8 +505,8 @@ __device__ __noinline__ void merge_parts(const AttnParams& p, uint32_t tO, int h
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
             const int col = c * 32 + 8 * k + 2 * (lane & 3);
-            if (rA < nrows) st_global_f2(dst + (int64_t)rA * D + col, va[k]);
-            if (rB < nrows) st_global_f2(dst + (int64_t)rB * D + col, vb[k]);
+            if (rA < nrows) out_store<PEERS>(p, obase + (int64_t)rA * D + col, va[k]);
+            if (rB < nrows) out_store<PEERS>(p, obase + (int64_t)rB * D + col, vb[k]);
         }
     }
 }
@@ -426,10 +516,10 @@ __device__ __noinline__ void merge_parts(const AttnParams& p, uint32_t tO, int h
 // CTA's segments.  Barrier phases run on across segments (per step for the KV ring, S and P;
 // per segment for Q and O), so the next unit's Q load and first S MMAs overlap the previous
 // unit's epilogue.
-template <int D>
+template <int D, bool PEERS>
 __global__ void __launch_bounds__(kAttnThreads, 1)
-    packed_attention_kernel(const __grid_constant__ CUtensorMap qmap, AttnParams p) {
-    using L = AttnLayout<D>;
+    packed_attention_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ AttnParams p) {
+    using L = AttnLayout<D, PEERS>;
     constexpr int NA = L::NA;
     constexpr uint32_t TB = L::kTile;
     extern __shared__ uint8_t smem_raw[];
@@ -448,7 +538,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     uint64_t* o_full = bars + 14;       // [2] per query tile, commit after the segment's last P*V
     uint64_t* o_empty = bars + 16;      // [2] per query tile, 4 softmax warps (O read out)
     uint64_t* drain = bars + 18;        // commit, drain before TMEM release
-    long long* hp = reinterpret_cast<long long*>(smem + L::kHP);
+    int* hp = reinterpret_cast<int*>(smem + L::kHP);
     int* misc = reinterpret_cast<int*>(smem + L::kMisc);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kTmemSlot);
 
@@ -467,7 +557,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         }
         mbar_init(drain, 1);
         fence_mbarrier_init();
-        long long acc = 0;
+        int acc = 0;            // below 2^31: H * ntmax is checked on the host
         int ntm = 0;
         for (int hh = 0; hh < p.H; ++hh) {
             const int* c = p.counts + (int64_t)(hh / p.rep) * 5;
@@ -651,10 +741,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                 fa = m_ref == -INFINITY ? 0.0f : ex2(m_ref - mall) * inv_all;
             }
             const int row0 = sg.qp * kUnitRows + rt;             // query row within the head
+            const int64_t obase = (((int64_t)sg.b * p.H_out + p.head_off + sg.h) * p.S_q + row0) * D;
             float* dst = split_tail ? p.part_o + ((size_t)blockIdx.x * kUnitRows + rt) * D
                                     : p.out + (((int64_t)sg.b * p.H + sg.h) * p.S_q + row0) * D;
             const float* src = p.part_o + ((size_t)slot * kUnitRows + rt) * D;
             const int nrows = split_tail ? 32 : min(32, p.S_q - row0);
+            // PEERS: this warp's staging slot (8 output rows)
+            float* oslot = PEERS ? reinterpret_cast<float*>(smem + L::kOut) + warp * L::kOutRows * D : nullptr;
             // O is read in the 16x256b shape: four threads hold 32 contiguous bytes of a row, so
             // each store instruction writes whole sectors without a shared-memory transpose
             // (shared memory bandwidth stays with the tensor cores)
@@ -667,11 +760,47 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                     // a unit spread over three or more CTAs (small grids of units)
                     const float mA = __shfl_sync(0xffffffffu, mall, rA), mBr = __shfl_sync(0xffffffffu, mall, rB);
                     const float iA = __shfl_sync(0xffffffffu, inv_all, rA), iB = __shfl_sync(0xffffffffu, inv_all, rB);
-                    merge_parts<D>(p, tO, hf, rA, rB, faA, faB, mA, mBr, iA, iB, np, slot, rt, lane, nrows, dst,
-                                   &o_empty[t]);
+                    merge_parts<D, PEERS>(p, tO, hf, rA, rB, faA, faB, mA, mBr, iA, iB, np, slot, rt, lane, nrows, obase,
+                                          &o_empty[t], oslot);
                     continue;
                 }
                 if (np == 1) {
+                    if constexpr (PEERS) {
+                        // rows rA, then rows rB, staged whole: per pass this row's partial values
+                        // first (their loads overlap), then O chunk by chunk (read once per pass)
+#pragma unroll
+                        for (int half = 0; half < 2; ++half) {
+                            const int r = half ? rB : rA;
+                            const float fbr = half ? fbB : fbA, far = half ? faB : faA;
+                            float2 px[D / 32][4];
+#pragma unroll
+                            for (int c = 0; c < D / 32; ++c)
+#pragma unroll
+                                for (int k = 0; k < 4; ++k)
+                                    px[c][k] = __ldcg(reinterpret_cast<const float2*>(
+                                        src + (int64_t)r * D + c * 32 + 8 * k + 2 * (lane & 3)));
+                            stage_acquire(lane);
+#pragma unroll
+                            for (int c = 0; c < D / 32; ++c) {
+                                uint32_t o[16];
+                                tmem_ld16x256b_x4(tO + c * 32 + ((uint32_t)(hf * 16) << 16), o);
+                                tmem_wait_ld();
+                                if (hf == 1 && half == 1 && c == D / 32 - 1) {
+                                    tc_fence_before();
+                                    __syncwarp();
+                                    if (lane == 0) mbar_arrive(&o_empty[t]);
+                                }
+#pragma unroll
+                                for (int k = 0; k < 4; ++k)
+                                    stage_put<D>(oslot, lane, c, k,
+                                                 make_float2(fmaf(px[c][k].x, fbr, __uint_as_float(o[4 * k + 2 * half]) * far),
+                                                             fmaf(px[c][k].y, fbr, __uint_as_float(o[4 * k + 2 * half + 1]) * far)));
+                            }
+                            const int r0 = hf * 16 + half * 8;
+                            stage_flush<D>(p, oslot, lane, obase + (int64_t)r0 * D, min(8, nrows - r0));
+                        }
+                        continue;
+                    }
                     // a unit cut between two CTAs, merged here (once per CTA at most): all of this
                     // half's partial values first, so their loads overlap, then O chunk by chunk
                     float2 pa[D / 32][4], pb[D / 32][4];
@@ -700,11 +829,41 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                                                           fmaf(pa[c][k].y, fbA, __uint_as_float(o[4 * k + 1]) * faA));
                             const float2 vb = make_float2(fmaf(pb[c][k].x, fbB, __uint_as_float(o[4 * k + 2]) * faB),
                                                           fmaf(pb[c][k].y, fbB, __uint_as_float(o[4 * k + 3]) * faB));
-                            if (rA < nrows) st_global_f2(dst + (int64_t)rA * D + col, va);
-                            if (rB < nrows) st_global_f2(dst + (int64_t)rB * D + col, vb);
+                            if (rA < nrows) out_store<PEERS>(p, obase + (int64_t)rA * D + col, va);
+                            if (rB < nrows) out_store<PEERS>(p, obase + (int64_t)rB * D + col, vb);
                         }
                     }
                     continue;
+                }
+                if constexpr (PEERS) {
+                    if (!split_tail) {
+                        // rows rA, then rows rB, staged whole; O read chunk by chunk per pass so
+                        // that few registers stay live beside the bulk-store issue
+#pragma unroll
+                        for (int half = 0; half < 2; ++half) {
+                            const float fr = half ? faB : faA;
+                            stage_acquire(lane);
+#pragma unroll
+                            for (int c = 0; c < D / 32; ++c) {
+                                uint32_t o[16];
+                                tmem_ld16x256b_x4(tO + c * 32 + ((uint32_t)(hf * 16) << 16), o);
+                                tmem_wait_ld();
+                                if (hf == 1 && half == 1 && c == D / 32 - 1) {
+                                    tc_fence_before();
+                                    __syncwarp();
+                                    if (lane == 0) mbar_arrive(&o_empty[t]);
+                                }
+#pragma unroll
+                                for (int k = 0; k < 4; ++k)
+                                    stage_put<D>(oslot, lane, c, k,
+                                                 make_float2(__uint_as_float(o[4 * k + 2 * half]) * fr,
+                                                             __uint_as_float(o[4 * k + 2 * half + 1]) * fr));
+                            }
+                            const int r0 = hf * 16 + half * 8;
+                            stage_flush<D>(p, oslot, lane, obase + (int64_t)r0 * D, min(8, nrows - r0));
+                        }
+                        continue;
+                    }
                 }
                 // all of this half's TMEM columns first (one wait), then the stores
                 uint32_t o[D / 32][16];
@@ -730,8 +889,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                             *reinterpret_cast<float2*>(dst + (int64_t)rA * D + col) = va;
                             *reinterpret_cast<float2*>(dst + (int64_t)rB * D + col) = vb;
                         } else {
-                            if (rA < nrows) st_global_f2(dst + (int64_t)rA * D + col, va);
-                            if (rB < nrows) st_global_f2(dst + (int64_t)rB * D + col, vb);
+                            if (rA < nrows) out_store<PEERS>(p, obase + (int64_t)rA * D + col, va);
+                            if (rB < nrows) out_store<PEERS>(p, obase + (int64_t)rB * D + col, vb);
                         }
                     }
                 }
@@ -752,9 +911,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             const int bb = (int)(u / ((long long)p.QP * p.H));
             if (hp[hh + 1] != hp[hh]) continue;
             const int row0 = qp * kUnitRows + rt;
-            float* dst = p.out + (((int64_t)bb * p.H + hh) * p.S_q + row0) * D;
+            const int64_t ob = (((int64_t)bb * p.H_out + p.head_off + hh) * p.S_q + row0) * D;
             for (int r = 0; r < min(32, p.S_q - row0); ++r)
-                for (int d = lane; d < D; d += 32) dst[(int64_t)r * D + d] = 0.0f;
+                for (int d = 2 * lane; d < D; d += 64) out_store<PEERS>(p, ob + (int64_t)r * D + d, make_float2(0.0f, 0.0f));
+        }
+        if constexpr (PEERS) {
+            // the staged rows' bulk stores have completed before the CTA (and its shared memory) ends
+            if (lane == 0) bulk_wait0();
+            __syncwarp();
         }
     } else if (warp == kLoadWarp) {
         // ------------------------------------------------------------------ loader
@@ -1020,7 +1184,8 @@ namespace {
 int attn_params(const void* q, int B, int H, int S_q, int D, const skv_bucket* buckets, int H_kv, int S_kv,
                 int int4_group, const int32_t* rows, const int32_t* counts, const float* k_new, const float* v_new,
                 int S_new, float scale, void* scratch, size_t scratch_bytes, float* out, int32_t* error_flag,
-                AttnParams& prm, const char* what) {
+                AttnParams& prm, const char* what, int max_ctas = 0, float* const* peers = nullptr,
+                int n_peers = 0, int head_off = 0, int H_out = 0) {
     if (!rows || !counts || !scratch) return fail(SKV_ERR_INVALID_ARGUMENT, "%s: null pointer", what);
     if (B <= 0 || H <= 0 || S_q <= 0 || S_kv <= 0 || H_kv <= 0 || S_new < 0)
         return fail(SKV_ERR_INVALID_ARGUMENT, "%s: bad shape", what);
@@ -1043,8 +1208,10 @@ int attn_params(const void* q, int B, int H, int S_q, int D, const skv_bucket* b
     const size_t need = skv_packed_attention_scratch_bytes(B, H_kv, S_kv + S_new, D);
     if (scratch_bytes < need)
         return fail(SKV_ERR_SCRATCH, "%s: scratch of %zu bytes, %zu needed", what, scratch_bytes, need);
-    if ((long long)B * H * S_q >= (1ll << 31) || H > kMaxHeads)
-        return fail(SKV_ERR_TOO_LARGE, "%s: B*H*S_q must stay below 2^31 and H <= %d", what, kMaxHeads);
+    if ((long long)B * H * S_q >= (1ll << 31) || H > kMaxHeads ||
+        (long long)H * ((S_kv + S_new + kBN - 1) / kBN) >= (1ll << 31))
+        return fail(SKV_ERR_TOO_LARGE, "%s: B*H*S_q and H*ceil((S_kv+S_new)/128) must stay below 2^31, H <= %d",
+                    what, kMaxHeads);
     memset(&prm, 0, sizeof(prm));
     prm.q = reinterpret_cast<const __half*>(q);
     prm.out = out;
@@ -1056,10 +1223,14 @@ int attn_params(const void* q, int B, int H, int S_q, int D, const skv_bucket* b
     prm.v_new = S_new > 0 ? v_new : nullptr;
     prm.H_kv = H_kv;
     prm.rep = H / H_kv;
+    prm.peers = n_peers > 0 ? peers : nullptr;
+    prm.n_peers = n_peers > 0 ? n_peers : 0;
+    prm.head_off = n_peers > 0 ? head_off : 0;
+    prm.H_out = n_peers > 0 ? H_out : H;
     prm.S_new = S_new;
     prm.stage = reinterpret_cast<uint8_t*>(scratch);
     prm.ntmax = (S_kv + S_new + kBN - 1) / kBN;
-    prm.slots = sm_count();
+    prm.slots = max_ctas > 0 && max_ctas < sm_count() ? max_ctas : sm_count();
     uint8_t* part = prm.stage + (size_t)B * H_kv * prm.ntmax * 2 * staged_tile_bytes(D);
     prm.part_o = reinterpret_cast<float*>(part);
     part += (size_t)prm.slots * kUnitRows * D * sizeof(float);
@@ -1138,12 +1309,13 @@ int launch_attention(const AttnParams& prm, cudaStream_t s) {
     if (r != CUDA_SUCCESS) return fail(SKV_ERR_CUDA, "attend_kv_tiles: tensor map encoding failed (%d)", (int)r);
     if (cudaMemsetAsync(prm.part_flag, 0, (size_t)prm.slots * sizeof(int), s) != cudaSuccess)
         return fail(SKV_ERR_CUDA, "attend_kv_tiles: memset failed");
-    const int smem = AttnLayout<D>::kAlloc;
-    cudaFuncSetAttribute(packed_attention_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    const int smem = prm.n_peers > 0 ? AttnLayout<D, true>::kAlloc : AttnLayout<D, false>::kAlloc;
+    void* kern = prm.n_peers > 0 ? reinterpret_cast<void*>(packed_attention_kernel<D, true>)
+                                 : reinterpret_cast<void*>(packed_attention_kernel<D, false>);
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     AttnParams a = prm;
     void* args[] = {&qmap, &a};
-    const cudaError_t e = cudaLaunchCooperativeKernel(reinterpret_cast<void*>(packed_attention_kernel<D>),
-                                                      dim3((unsigned)prm.slots), dim3(kAttnThreads), args,
+    const cudaError_t e = cudaLaunchCooperativeKernel(kern, dim3((unsigned)prm.slots), dim3(kAttnThreads), args,
                                                       (size_t)smem, s);
     if (e != cudaSuccess)
         return fail(SKV_ERR_CUDA, "attend_kv_tiles: cooperative launch failed: %s", cudaGetErrorString(e));
@@ -1154,16 +1326,40 @@ int launch_attention(const AttnParams& prm, cudaStream_t s) {
 
 extern "C" {
 
+int skv_attend_kv_tiles_peers(const void* q, int B, int H_q, int S_q, int D, int H_kv, int S_kv, const int32_t* rows,
+                              const int32_t* counts, int S_new, float scale, const void* scratch,
+                              size_t scratch_bytes, float* const* out_peers, int n_peers, int head_offset,
+                              int H_out, int32_t* error_flag, int max_ctas, void* stream) {
+    if (!q || !out_peers || !error_flag || n_peers <= 0)
+        return fail(SKV_ERR_INVALID_ARGUMENT, "attend_kv_tiles_peers: null pointer or no peers");
+    if (n_peers > 64 || head_offset < 0 || H_out < head_offset + H_q)
+        return fail(SKV_ERR_SHAPE, "attend_kv_tiles_peers: heads %d at %d of %d, %d peers", H_q, head_offset, H_out,
+                    n_peers);
+    AttnParams prm;
+    const float* staged = S_new > 0 ? reinterpret_cast<const float*>(scratch) : nullptr;
+    // `out` is not used with peers; a non-null placeholder passes the shared checks
+    float* placeholder = reinterpret_cast<float*>(const_cast<void*>(scratch));
+    const int st = attn_params(q, B, H_q, S_q, D, nullptr, H_kv, S_kv, 0, rows, counts, staged, staged, S_new, scale,
+                               const_cast<void*>(scratch), scratch_bytes, placeholder, error_flag, prm,
+                               "attend_kv_tiles_peers", max_ctas, out_peers, n_peers, head_offset, H_out);
+    if (st != SKV_OK) return st;
+    cudaStream_t s = as_stream(stream);
+    if (cudaMemsetAsync(error_flag, 0, sizeof(int32_t), s) != cudaSuccess)
+        return fail(SKV_ERR_CUDA, "attend_kv_tiles_peers: memset failed");
+    return D == 128 ? launch_attention<128>(prm, s) : launch_attention<64>(prm, s);
+}
+
 int skv_attend_kv_tiles_gqa(const void* q, int B, int H_q, int S_q, int D, int H_kv, int S_kv, const int32_t* rows,
                             const int32_t* counts, int S_new, float scale, const void* scratch, size_t scratch_bytes,
-                            float* out, int32_t* error_flag, void* stream) {
+                            float* out, int32_t* error_flag, int max_ctas, void* stream) {
     if (!q || !out || !error_flag) return fail(SKV_ERR_INVALID_ARGUMENT, "attend_kv_tiles: null pointer");
     AttnParams prm;
     // the dense rows are already staged: only their count matters here (a non-null placeholder
     // passes the argument checks and is never read)
     const float* staged = S_new > 0 ? reinterpret_cast<const float*>(scratch) : nullptr;
     const int st = attn_params(q, B, H_q, S_q, D, nullptr, H_kv, S_kv, 0, rows, counts, staged, staged, S_new, scale,
-                               const_cast<void*>(scratch), scratch_bytes, out, error_flag, prm, "attend_kv_tiles");
+                               const_cast<void*>(scratch), scratch_bytes, out, error_flag, prm, "attend_kv_tiles",
+                               max_ctas);
     if (st != SKV_OK) return st;
     cudaStream_t s = as_stream(stream);
     if (cudaMemsetAsync(error_flag, 0, sizeof(int32_t), s) != cudaSuccess)
@@ -1175,27 +1371,27 @@ int skv_attend_kv_tiles(const void* q, int B, int H, int S_q, int D, int S_kv, c
                         const int32_t* counts, float scale, const void* scratch, size_t scratch_bytes, float* out,
                         int32_t* error_flag, void* stream) {
     return skv_attend_kv_tiles_gqa(q, B, H, S_q, D, H, S_kv, rows, counts, 0, scale, scratch, scratch_bytes, out,
-                                   error_flag, stream);
+                                   error_flag, 0, stream);
 }
 
 int skv_packed_attention_gqa(const void* q, int B, int H_q, int S_q, int D, const skv_bucket* buckets, int H_kv,
                              int S_kv, int int4_group, const int32_t* rows, const int32_t* counts,
                              const float* k_new, const float* v_new, int S_new, float scale, void* scratch,
-                             size_t scratch_bytes, float* out, int32_t* error_flag, void* stream) {
+                             size_t scratch_bytes, float* out, int32_t* error_flag, int max_ctas, void* stream) {
     if (!q || !buckets || !out || !error_flag) return fail(SKV_ERR_INVALID_ARGUMENT, "packed_attention: null pointer");
     if (H_kv <= 0 || H_q % H_kv) return fail(SKV_ERR_SHAPE, "packed_attention: %d query heads over %d KV heads", H_q, H_kv);
     const int st = skv_stage_kv_tiles_gqa(buckets, B, H_kv, S_kv, D, int4_group, rows, counts, k_new, v_new, S_new,
                                           scratch, scratch_bytes, stream);
     if (st != SKV_OK) return st;
     return skv_attend_kv_tiles_gqa(q, B, H_q, S_q, D, H_kv, S_kv, rows, counts, S_new, scale, scratch, scratch_bytes,
-                                   out, error_flag, stream);
+                                   out, error_flag, max_ctas, stream);
 }
 
 int skv_packed_attention(const void* q, int B, int H, int S_q, int D, const skv_bucket* buckets, int S_kv,
                          int int4_group, const int32_t* rows, const int32_t* counts, float scale, void* scratch,
                          size_t scratch_bytes, float* out, int32_t* error_flag, void* stream) {
     return skv_packed_attention_gqa(q, B, H, S_q, D, buckets, H, S_kv, int4_group, rows, counts, nullptr, nullptr, 0,
-                                    scale, scratch, scratch_bytes, out, error_flag, stream);
+                                    scale, scratch, scratch_bytes, out, error_flag, 0, stream);
 }
 
 }  // extern "C"

@@ -53,6 +53,20 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
                  : "memory");
 }
 
+// Bulk async copy this CTA's shared memory -> global (local or a peer GPU's memory; no tensor
+// map, no multicast), tracked in the issuing thread's bulk groups.  Both addresses 16-byte
+// aligned, `bytes` a multiple of 16.  The source may be rewritten after bulk_wait_read0().
+__device__ __forceinline__ void bulk_s2g(void* dst, const void* src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst), "r"(smem_u32(src)),
+                 "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// every committed group of this thread has finished reading shared memory
+__device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// every committed group of this thread has completed (its writes performed)
+__device__ __forceinline__ void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
 // try_wait with a suspend-time hint: the thread sleeps in hardware until the phase completes
 // or `hint_ns` passes, instead of spinning and taking issue slots from its SMSP neighbours.
 __device__ __forceinline__ bool mbar_try_wait_hint(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {

@@ -31,6 +31,9 @@ def packed_attention(
     events: Optional[tuple] = None,
     k_new: Optional[torch.Tensor] = None,
     v_new: Optional[torch.Tensor] = None,
+    max_ctas: int = 0,
+    peer_outputs=None,
+    head_offset: int = 0,
 ) -> torch.Tensor:
     """Non-causal attention of ``q`` [B, H_q, S_q, D] over a packed cache; returns fp32 [B, H_q, S_q, D].
 
@@ -44,7 +47,13 @@ def packed_attention(
     ``k_new`` / ``v_new`` [B, H_kv, S_new, D]: this step's own K/V, attended together with the
     cached rows -- the reference's ``cat((past_k, k), dim=2)`` before the attention
     (simple_diffusion_llm.py:160-169, diffusion_llama.py:376-390) -- staged straight from the
-    dense tensors.
+    dense tensors.  ``max_ctas`` caps the persistent attention kernel's CTAs (0: one per SM), to
+    leave SMs to work that should run beside it, such as an NCCL all-gather on another stream.
+
+    ``peer_outputs`` (a ``sharding.PeerOutputs`` of shape [B, H_total, S_q, D]): the kernel stores
+    each finished output row into every rank's buffer, at heads ``[head_offset, head_offset +
+    H_q)``, over NVLink -- the all-gather of head-sharded outputs fused into the attention
+    epilogue.  Returns the local buffer, complete once every rank's call has finished.
     """
     if q.dim() != 4:
         raise ValueError(f"q must be 4-D [batch, heads, seq, head_dim], got shape {tuple(q.shape)}")
@@ -84,11 +93,37 @@ def packed_attention(
     tiles = scratch(lib.skv_packed_attention_scratch_bytes(B, H_kv, c.seq_len + S_new, D), dev)
     stream = _lib.stream_of(dev)
     g = c._int4_group_of()
+    if peer_outputs is not None:
+        Bp, Hp, Sp, Dp = peer_outputs.shape
+        if (Bp, Sp, Dp) != (B, S_q, D) or not 0 <= head_offset <= Hp - H:
+            raise ValueError(f"peer output buffers {peer_outputs.shape} cannot take heads "
+                             f"[{head_offset}, {head_offset + H}) of q {tuple(q.shape)}")
+        with device_ctx(dev):
+            if events is not None:
+                events[0].record()
+            st = lib.skv_stage_kv_tiles_gqa(arr, B, H_kv, c.seq_len, D, g, _lib.ptr(rows), _lib.ptr(counts),
+                                            _lib.ptr(kn), _lib.ptr(vn), S_new, _lib.ptr(tiles), tiles.numel(), stream)
+            _lib.check(st, "packed_attention")
+            if events is not None:
+                events[1].record()
+            st = lib.skv_attend_kv_tiles_peers(_lib.ptr(qd), B, H, S_q, D, H_kv, c.seq_len, _lib.ptr(rows),
+                                               _lib.ptr(counts), S_new, float(scale), _lib.ptr(tiles), tiles.numel(),
+                                               _lib.ptr(peer_outputs.ptrs), peer_outputs.world, int(head_offset), Hp,
+                                               _lib.ptr(err), int(max_ctas), stream)
+            if events is not None:
+                events[2].record()
+        _lib.check(st, "packed_attention")
+        if check:
+            code = int(err.item())
+            if code:
+                raise RuntimeError(f"packed_attention: a pipeline wait timed out inside the kernel (code {code})")
+        return peer_outputs.local
     with device_ctx(dev):
         if events is None:
             st = lib.skv_packed_attention_gqa(_lib.ptr(qd), B, H, S_q, D, arr, H_kv, c.seq_len, g, _lib.ptr(rows),
                                               _lib.ptr(counts), _lib.ptr(kn), _lib.ptr(vn), S_new, float(scale),
-                                              _lib.ptr(tiles), tiles.numel(), _lib.ptr(out), _lib.ptr(err), stream)
+                                              _lib.ptr(tiles), tiles.numel(), _lib.ptr(out), _lib.ptr(err),
+                                              int(max_ctas), stream)
         else:
             events[0].record()
             st = lib.skv_stage_kv_tiles_gqa(arr, B, H_kv, c.seq_len, D, g, _lib.ptr(rows), _lib.ptr(counts),
@@ -97,7 +132,7 @@ def packed_attention(
             events[1].record()
             st = lib.skv_attend_kv_tiles_gqa(_lib.ptr(qd), B, H, S_q, D, H_kv, c.seq_len, _lib.ptr(rows),
                                              _lib.ptr(counts), S_new, float(scale), _lib.ptr(tiles), tiles.numel(),
-                                             _lib.ptr(out), _lib.ptr(err), stream)
+                                             _lib.ptr(out), _lib.ptr(err), int(max_ctas), stream)
             events[2].record()
     _lib.check(st, "packed_attention")
     if check:

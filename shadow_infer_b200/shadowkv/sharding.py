@@ -12,12 +12,19 @@ steps remain:
   single-GPU admission exactly.
 * ``all_gather_heads`` -- the attention outputs ``[B, H/n, S, D]`` of all ranks
   assembled into ``[B, H, S, D]`` (one NCCL all-gather).
+* ``PeerOutputs`` -- the fused alternative: every rank's ``[B, H, S, D]`` output buffer is
+  mapped into all ranks (CUDA IPC), and the attention kernel's epilogue stores each finished
+  row straight into every rank's buffer over NVLink (``packed_attention(...,
+  peer_outputs=...)``), so the exchange overlaps the attention itself and no NCCL kernel
+  competes with it for SMs.
 
 The collectives go through ``torch.distributed``, so the same code runs on a gloo
 (CPU) group in tests.
 """
 
 from __future__ import annotations
+
+import ctypes
 
 from typing import Optional, Tuple
 
@@ -94,3 +101,71 @@ def admit_codes_sharded(
     out, predicted, evicted = admit(codes, imp, sens, budget_bytes, batch, head_dim, sink_tokens, rd_allocation,
                                     allow_eviction, prot, group_size)
     return out[:, r * h:(r + 1) * h].contiguous(), predicted, evicted
+
+
+class PeerOutputs:
+    """One float32 output buffer ``shape`` = [B, H, S_q, D] per rank, each mapped into every rank
+    of ``group`` through CUDA IPC.  ``ptrs`` is a device int64 array of the ranks' buffer
+    addresses as seen from this process, in rank order; ``local`` is this rank's buffer.  A
+    kernel that stores into all of them leaves every rank with the full result once all ranks'
+    kernels have finished (the caller synchronises the ranks, e.g. with
+    ``torch.distributed.barrier``, before reading ``local``).
+    Collective: every rank of ``group`` constructs it with the same shape, each on its own GPU.
+
+    The peer buffers are opened by the library (``skv_ipc_open``) on THIS rank's device, which
+    enables peer access from it to the owner's GPU; only the handle bytes travel through the
+    process group.
+    """
+
+    def __init__(self, shape, group=None, device=None) -> None:
+        from .. import _lib
+        from .._device import device_ctx
+
+        n, r = _world(group)
+        dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+        self.world, self.rank = n, r
+        self.local = torch.zeros(tuple(shape), dtype=torch.float32, device=dev)
+        lib = _lib.load()
+        hb = lib.skv_ipc_handle_bytes()
+        handle = ctypes.create_string_buffer(hb)
+        offset = ctypes.c_int64(0)
+        with device_ctx(dev):
+            _lib.check(lib.skv_ipc_export(_lib.ptr(self.local), handle, ctypes.byref(offset)), "PeerOutputs")
+        mine = (bytes(handle.raw), int(offset.value), int(self.local.numel()))
+        entries = [None] * n
+        dist.all_gather_object(entries, mine, group=group)
+        self._lib = lib
+        self._bases = []
+        ptrs = []
+        with device_ctx(dev):
+            for i, (h, off, numel) in enumerate(entries):
+                if numel != self.local.numel():
+                    self.close()
+                    raise ValueError(f"PeerOutputs: rank {i} has {numel} elements, this rank {self.local.numel()}")
+                if i == r:
+                    ptrs.append(self.local.data_ptr())
+                    continue
+                base = ctypes.c_void_p()
+                p = ctypes.c_void_p()
+                st = lib.skv_ipc_open(ctypes.create_string_buffer(h, hb), off, ctypes.byref(base), ctypes.byref(p))
+                if st != 0:
+                    self.close()
+                _lib.check(st, "PeerOutputs")
+                self._bases.append(base.value)
+                ptrs.append(int(p.value))
+        self.ptrs = torch.tensor(ptrs, dtype=torch.int64, device=dev)
+
+    @property
+    def shape(self):
+        return tuple(self.local.shape)
+
+    def close(self) -> None:
+        """Unmap the peer buffers (call on every rank after a barrier: no kernel may still be
+        storing into them, and no rank may still be reading its own)."""
+        from .. import _lib
+        from .._device import device_ctx
+
+        bases, self._bases = self._bases, []
+        with device_ctx(self.local.device):
+            for b in bases:
+                _lib.check(self._lib.skv_ipc_close(b), "PeerOutputs.close")

@@ -209,3 +209,110 @@ def test_gqa_argument_checks(skv):
     with pytest.raises(ValueError, match="k_new/v_new"):
         skv.packed_attention(torch.randn(1, 4, 8, 64, device="cuda"), cache, k_new=torch.randn(1, 4, 5, 64),
                              v_new=torch.randn(1, 4, 5, 64))
+
+
+def test_attention_with_fewer_ctas(skv):
+    """A capped persistent grid (SMs left to other work) gives the same result."""
+    rng = np.random.default_rng(77)
+    B, H, S, SQ, D = 1, 4, 700, 300, 128
+    k = rng.standard_normal((B, H, S, D)).astype(np.float32)
+    v = rng.standard_normal((B, H, S, D)).astype(np.float32)
+    codes = rng.choice(5, size=(S, H), p=(0.0, 0.3, 0.4, 0.25, 0.05)).astype(np.int8)
+    q = torch.from_numpy(rng.standard_normal((B, H, SQ, D)).astype(np.float16)).cuda()
+    cache = _pack(skv, k, v, codes)
+    ref = O.packed_attention(q.cpu().numpy().astype(np.float32), O.pack(k, v, O.plan_from_codes(codes), 16))
+    for ctas in (1, 7, 37, 132):
+        out = skv.packed_attention(q, cache, max_ctas=ctas).cpu().numpy()
+        assert rel_l2(out, ref) < REL_L2_TOL, ctas
+
+
+class _TwoBuffers:
+    """Two output buffers on one GPU standing in for two ranks' IPC-mapped buffers."""
+
+    def __init__(self, shape, local):
+        self.bufs = [torch.zeros(shape, dtype=torch.float32, device="cuda") for _ in range(2)]
+        self.local = self.bufs[local]
+        self.shape = tuple(shape)
+        self.world = 2
+        self.ptrs = torch.tensor([b.data_ptr() for b in self.bufs], dtype=torch.int64, device="cuda")
+
+
+def _sharded_problem(seed, B, H, S, SQ, D):
+    rng = np.random.default_rng(seed)
+    k = rng.standard_normal((B, H, S, D)).astype(np.float32)
+    v = rng.standard_normal((B, H, S, D)).astype(np.float32)
+    codes = rng.choice(5, size=(S, H), p=(0.05, 0.25, 0.4, 0.25, 0.05)).astype(np.int8)
+    q = rng.standard_normal((B, H, SQ, D)).astype(np.float16)
+    return k, v, codes, q
+
+
+def test_attention_stores_into_peer_buffers(skv):
+    """The fused all-gather epilogue: each head shard's call stores its rows into every buffer,
+    so after both shards both buffers hold all heads (identical bits) and match the oracle."""
+    B, H, S, SQ, D = 2, 6, 500, 260, 128
+    k, v, codes, q = _sharded_problem(5, B, H, S, SQ, D)
+    ref = O.packed_attention(q.astype(np.float32), O.pack(k, v, O.plan_from_codes(codes), 16))
+    peers = _TwoBuffers((B, H, SQ, D), 0)
+    for h0, h1 in ((0, 4), (4, 6)):
+        cache = _pack(skv, np.ascontiguousarray(k[:, h0:h1]), np.ascontiguousarray(v[:, h0:h1]),
+                      np.ascontiguousarray(codes[:, h0:h1]))
+        got = skv.packed_attention(torch.from_numpy(np.ascontiguousarray(q[:, h0:h1])).cuda(), cache,
+                                   peer_outputs=peers, head_offset=h0)
+        assert got.data_ptr() == peers.local.data_ptr()
+    torch.cuda.synchronize()
+    assert torch.equal(peers.bufs[0], peers.bufs[1])
+    assert rel_l2(peers.bufs[0].cpu().numpy(), ref) < REL_L2_TOL
+    with pytest.raises(ValueError, match="peer output buffers"):
+        skv.packed_attention(torch.from_numpy(np.ascontiguousarray(q[:, :4])).cuda(), cache, peer_outputs=peers,
+                             head_offset=3)
+
+
+def _peer_worker(rank, world, port, ret):
+    import os
+    import sys
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        repo = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+        sys.path.insert(0, repo)
+        import shadow_infer_b200.shadowkv as skv
+        from shadow_infer_b200.shadowkv.sharding import PeerOutputs, head_range
+        B, H, S, SQ, D = 1, 8, 700, 300, 128
+        k, v, codes, q = _sharded_problem(9, B, H, S, SQ, D)
+        h0, h1 = head_range(H, world, rank)
+        peers = PeerOutputs((B, H, SQ, D), device=f"cuda:{rank}")
+        cache = _pack(skv, np.ascontiguousarray(k[:, h0:h1]), np.ascontiguousarray(v[:, h0:h1]),
+                      np.ascontiguousarray(codes[:, h0:h1]))
+        out = skv.packed_attention(torch.from_numpy(np.ascontiguousarray(q[:, h0:h1])).cuda(), cache,
+                                   peer_outputs=peers, head_offset=h0)
+        torch.cuda.synchronize()
+        dist.barrier()                          # every rank's stores have landed
+        full = out.cpu()
+        dist.barrier()                          # nobody unmaps a buffer another rank still reads
+        peers.close()
+        allf = [torch.empty_like(full) for _ in range(world)]
+        dist.all_gather(allf, full)
+        ref = O.packed_attention(q.astype(np.float32), O.pack(k, v, O.plan_from_codes(codes), 16))
+        ret[rank] = bool(all(torch.equal(f, full) for f in allf)) and rel_l2(full.numpy(), ref) < REL_L2_TOL
+    finally:
+        dist.destroy_process_group()
+
+
+def test_attention_peer_outputs_two_gpus(skv):
+    """Two ranks (one process per GPU), heads sharded, outputs exchanged by the kernel's own
+    stores into the CUDA IPC mappings of each other's buffers."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import socket
+    import torch.multiprocessing as mp
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    ctx = mp.get_context("spawn")
+    ret = ctx.Manager().dict()
+    mp.start_processes(_peer_worker, args=(2, port, ret), nprocs=2, join=True, start_method="spawn")
+    assert ret.get(0) and ret.get(1)
