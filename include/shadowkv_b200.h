@@ -115,6 +115,20 @@ int skv_pack(const float* k, const float* v, int B, int H, int S, int D, int gro
              const int32_t* slot, const skv_bucket* buckets /* [4] */,
              float* dense_k, float* dense_v, const float* k_prev, const float* v_prev,
              const uint8_t* reuse_mask, void* stream);
+/* skv_pack with the buckets laid out in ONE allocation on the device, so that the launch needs
+ * no host copy of the plan's counts (the host reads them afterwards, while the kernel runs):
+ * a one-thread kernel writes the skv_bucket[4] of `slab` for the DEVICE counts[0..3] (the
+ * plan's, skv_plan_bucket) into `desc` (device, 192 bytes, 16-byte aligned) -- per precision
+ * in code order its k, v (scale_k, scale_v) tensors in the reference layout, each at a 256-byte
+ * boundary; bucket c's flat indices are flat_all[sum(counts[:c]) ...] -- and the pack kernel
+ * reads them there.  If the layout needs more than slab_bytes, the descriptors are empty and
+ * nothing is written (the caller packs again into a larger slab).  skv_pack_slab_bytes: the
+ * bytes that layout needs, for HOST counts.  D in {64, 128, 256}, int4 group a multiple of 16,
+ * K/V 16-byte and the slab 256-byte aligned (else SKV_ERR_UNSUPPORTED); no dense copy. */
+int64_t skv_pack_slab_bytes(const int64_t* counts, int B, int D, int group_size);
+int skv_pack_slab(const float* k, const float* v, int B, int H, int S, int D, int group_size, const int32_t* slot,
+                  const int64_t* counts, const int64_t* flat_all, void* slab, int64_t slab_bytes, void* desc,
+                  void* stream);
 
 /* PackedKVCache.unpack / _dequantize_int4_bucket
  * (shadowinfer/shadowkv/packed_kv_cache.py:535-577, :636-656) -> zero-filled

@@ -16,9 +16,13 @@ import torch
 _NULL_CTX = contextlib.nullcontext()
 
 
+_get_device = getattr(torch._C, "_cuda_getDevice", None)
+
+
 def device_ctx(dev: torch.device):
     """``torch.cuda.device(dev)`` only when ``dev`` is not already the current device."""
-    return _NULL_CTX if torch.cuda.current_device() == dev.index else torch.cuda.device(dev)
+    cur = _get_device() if _get_device is not None and torch.cuda.is_initialized() else torch.cuda.current_device()
+    return _NULL_CTX if cur == dev.index else torch.cuda.device(dev)
 
 
 def mask_u8(mask: torch.Tensor, rows: int, cols: int, dev: torch.device) -> Optional[torch.Tensor]:

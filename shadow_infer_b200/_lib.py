@@ -89,6 +89,9 @@ _SIGNATURES = {
     "skv_attend_kv_tiles_peers": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_void_p, c_void_p,
                                           c_int, ctypes.c_float, c_void_p, c_size_t, c_void_p, c_int, c_int, c_int,
                                           c_void_p, c_int, c_void_p]),
+    "skv_pack_slab_bytes": (c_int64, [ctypes.POINTER(c_int64), c_int, c_int, c_int]),
+    "skv_pack_slab": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p,
+                              c_void_p, c_int64, c_void_p, c_void_p]),
     "skv_ipc_handle_bytes": (c_int, []),
     "skv_ipc_export": (c_int, [c_void_p, c_void_p, ctypes.POINTER(c_int64)]),
     "skv_ipc_open": (c_int, [c_void_p, c_int64, ctypes.POINTER(c_void_p), ctypes.POINTER(c_void_p)]),
@@ -170,7 +173,13 @@ def ptr(t: Optional[torch.Tensor]) -> Optional[int]:
     return t.data_ptr()
 
 
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def stream_of(device: torch.device) -> int:
+    """The ``cudaStream_t`` of the current stream of ``device`` (without building a Stream object)."""
+    if _raw_stream is not None:
+        return _raw_stream(device.index if device.index is not None else torch.cuda.current_device())
     return torch.cuda.current_stream(device).cuda_stream
 
 

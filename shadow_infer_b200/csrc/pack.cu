@@ -21,6 +21,8 @@
 // at most ~2.3e-5 for |y| <= 128, so elsewhere both round identically).  Packing uses
 // cvt.pack.sat (int8: saturating s8; int4: saturating u4 of q + 8, high nibble first).
 // Built without fast-math.
+#include <string.h>
+
 #include "skv_common.cuh"
 
 namespace skv {
@@ -234,12 +236,15 @@ __device__ __forceinline__ void row_group_max(const float (&x)[16], int G, float
 // token rows of K and of V are contiguous in memory: they are fetched with coalesced 128-bit
 // loads into the warp's staging buffer, then each lane quantises its 16 values, K first,
 // then V (one tensor live at a time keeps the register count low).  DENSE adds the
-// compress_kv working copy, staged back and stored coalesced.
-template <int LPR, bool DENSE>
+// compress_kv working copy, staged back and stored coalesced.  DDESC: the bucket descriptors
+// are read from device memory (`dbk`, written by pack_layout_kernel); a bucket without payload
+// there (a slab that was too small) receives no stores.
+template <int LPR, bool DENSE, bool DDESC = false>
 __global__ void __launch_bounds__(256, 4) pack16_kernel(
     const float* __restrict__ k, const float* __restrict__ v, int B, int H, int S, int G,
     const int32_t* __restrict__ slot, Buckets bk, float* __restrict__ dense_k, float* __restrict__ dense_v,
-    const float* __restrict__ k_prev, const float* __restrict__ v_prev, const uint8_t* __restrict__ reuse) {
+    const float* __restrict__ k_prev, const float* __restrict__ v_prev, const uint8_t* __restrict__ reuse,
+    const Buckets* __restrict__ dbk = nullptr) {
     constexpr int D = LPR * 16;
     constexpr int RPW = 32 / LPR;
     constexpr int CPR = D / 4;
@@ -273,7 +278,11 @@ __global__ void __launch_bounds__(256, 4) pack16_kernel(
         float mr, mg;
         row_group_max<LPR>(x, G, mr, mg);
         float dn[16];
-        if (active && sl >= 0) {
+        if (DDESC && active && sl >= 0) {
+            const int code = slot_code(sl);
+            const skv_bucket bc = dbk->b[code];
+            if (bc.k) pack_lane<LPR>(x, code, slot_pos(sl), b, B, G, bc, tensor == 1, mr, mg, dn, l);
+        } else if (active && sl >= 0) {
             const int code = slot_code(sl);
             pack_lane<LPR>(x, code, slot_pos(sl), b, B, G, bk.b[code], tensor == 1, mr, mg, dn, l);
         } else {
@@ -555,6 +564,53 @@ static dim3 grid_rows(int B, int H, int S, int lpr) {
     return dim3((unsigned)(B * H), (unsigned)((S + rows_per_block - 1) / rows_per_block));
 }
 
+// Bucket layout of one allocation ("slab"), the same arithmetic on host and device: per
+// precision in code order its k, v (and scale_k, scale_v) tensors in the reference layout,
+// each starting on a 256-byte boundary.  Returns the slab bytes needed.
+__host__ __device__ inline int64_t slab_layout(const int64_t* counts, int B, int D, int G, int64_t (*off)[4]) {
+    int64_t total = 0;
+    for (int c = 0; c < kNumBuckets; ++c) {
+        const int64_t n = counts[c];
+        int64_t nb[4] = {0, 0, 0, 0};
+        if (c == 0) nb[0] = nb[1] = n * B * D * 4;
+        else if (c == 1) nb[0] = nb[1] = n * B * D * 2;
+        else if (c == 2) { nb[0] = nb[1] = n * B * D; nb[2] = nb[3] = n * B * 4; }
+        else { nb[0] = nb[1] = n * ((B * D + 1) / 2); nb[2] = nb[3] = n * B * (D / G) * 4; }
+        for (int t = 0; t < 4; ++t) {
+            off[c][t] = -1;
+            if (n == 0 || nb[t] == 0) continue;
+            off[c][t] = total;
+            total += (nb[t] + 255) / 256 * 256;
+        }
+    }
+    return total;
+}
+
+// One thread: the descriptors of `slab` for the plan's device counts (bucket c's entries are
+// flat_all[sum(counts[:c]) : +counts[c]]).  A slab smaller than the layout gets empty
+// descriptors, and the pack kernel then writes nothing.
+__global__ void pack_layout_kernel(const int64_t* __restrict__ counts, int B, int D, int G, uint8_t* slab,
+                                   int64_t slab_bytes, const int64_t* flat_all, Buckets* __restrict__ out) {
+    if (threadIdx.x != 0 || blockIdx.x != 0) return;
+    int64_t cnt[kNumBuckets];
+    for (int c = 0; c < kNumBuckets; ++c) cnt[c] = counts[c];
+    int64_t off[kNumBuckets][4];
+    const int64_t total = slab_layout(cnt, B, D, G, off);
+    const bool fits = total <= slab_bytes;
+    int64_t start = 0;
+    for (int c = 0; c < kNumBuckets; ++c) {
+        skv_bucket d;
+        d.k = fits && off[c][0] >= 0 ? slab + off[c][0] : nullptr;
+        d.v = fits && off[c][1] >= 0 ? slab + off[c][1] : nullptr;
+        d.scale_k = fits && off[c][2] >= 0 ? reinterpret_cast<float*>(slab + off[c][2]) : nullptr;
+        d.scale_v = fits && off[c][3] >= 0 ? reinterpret_cast<float*>(slab + off[c][3]) : nullptr;
+        d.flat = const_cast<int64_t*>(flat_all) + start;
+        d.count = fits ? cnt[c] : 0;
+        out->b[c] = d;
+        start += cnt[c];
+    }
+}
+
 static int check_buckets(const skv_bucket* bk, const char* what) {
     if (!bk) return fail(SKV_ERR_INVALID_ARGUMENT, "%s: null bucket array", what);
     for (int p = 0; p < kNumBuckets; ++p) {
@@ -616,6 +672,45 @@ int skv_pack(const float* k, const float* v, int B, int H, int S, int D, int gro
                                                    reuse_mask);
     }
     return check_launch("pack");
+}
+
+int64_t skv_pack_slab_bytes(const int64_t* counts, int B, int D, int group_size) {
+    if (!counts || B <= 0 || D <= 0 || group_size <= 0) return -1;
+    int64_t off[kNumBuckets][4];
+    return slab_layout(counts, B, D, int4_group(D, group_size), off);
+}
+
+int skv_pack_slab(const float* k, const float* v, int B, int H, int S, int D, int group_size, const int32_t* slot,
+                  const int64_t* counts, const int64_t* flat_all, void* slab, int64_t slab_bytes, void* desc,
+                  void* stream) {
+    if (B <= 0 || H <= 0 || S <= 0 || D <= 0 || slab_bytes < 0)
+        return fail(SKV_ERR_INVALID_ARGUMENT, "pack_slab: bad shape or size");
+    if (!k || !v || !slot || !counts || !flat_all || !slab || !desc)
+        return fail(SKV_ERR_INVALID_ARGUMENT, "pack_slab: null pointer");
+    if ((int64_t)S * H > (int64_t(1) << 29)) return fail(SKV_ERR_TOO_LARGE, "pack_slab: S*H above 2^29");
+    if (group_size <= 0) return fail(SKV_ERR_GROUP_SIZE, "pack_slab: group_size must be >= 1");
+    const int G = int4_group(D, group_size);
+    const int lpr = fast_lpr(D, G);
+    if (!lpr || !is_aligned16(k) || !is_aligned16(v) || (reinterpret_cast<uintptr_t>(slab) & 255) ||
+        (reinterpret_cast<uintptr_t>(desc) & 15))
+        return fail(SKV_ERR_UNSUPPORTED, "pack_slab: needs D in {64,128,256}, a group multiple of 16, 16-byte "
+                                         "aligned K/V, a 256-byte aligned slab");
+    cudaStream_t s = as_stream(stream);
+    Buckets* dbk = reinterpret_cast<Buckets*>(desc);
+    pack_layout_kernel<<<1, 32, 0, s>>>(counts, B, D, G, reinterpret_cast<uint8_t*>(slab), slab_bytes, flat_all, dbk);
+    int st = check_launch("pack_slab layout");
+    if (st) return st;
+    Buckets none;
+    memset(&none, 0, sizeof(none));
+    const dim3 grid = grid_rows(B, H, S, lpr);
+#define SKV_PACK16D(L)                                                                                          \
+    pack16_kernel<L, false, true><<<grid, 256, 0, s>>>(k, v, B, H, S, G, slot, none, nullptr, nullptr, nullptr, \
+                                                       nullptr, nullptr, dbk)
+    if (lpr == 4) SKV_PACK16D(4);
+    else if (lpr == 8) SKV_PACK16D(8);
+    else SKV_PACK16D(16);
+#undef SKV_PACK16D
+    return check_launch("pack_slab");
 }
 
 int skv_unpack(const skv_bucket* buckets, const int32_t* slot, int B, int H, int S, int D, int int4_group,

@@ -23,7 +23,7 @@ on the current CUDA device and copied back.
 
 from __future__ import annotations
 
-from typing import Any, Callable, Dict, List, Optional, Set, Tuple
+from typing import Any, Callable, Dict, List, Optional, Set, Tuple, Sequence
 
 import torch
 
@@ -96,54 +96,167 @@ def _int4_group(head_dim: int, group_size: int) -> int:
     return group_size if head_dim % group_size == 0 else head_dim
 
 
-def _alloc_bucket(code: int, n: int, B: int, D: int, G: int, dev: torch.device) -> Dict[str, torch.Tensor]:
-    """Bucket tensors in the reference layout (packed_kv_cache.py:265-363)."""
+_F32, _F16, _I8, _U8 = torch.float32, torch.float16, torch.int8, torch.uint8
+_ALIGN = 256
+
+
+def _bucket_parts(code: int, n: int, B: int, D: int, G: int):
+    """(key, dtype, shape, bytes) of a bucket's tensors in the reference layout
+    (packed_kv_cache.py:265-363); ``scale_*`` absent (None) for fp32 / fp16."""
     if code == 0:
-        return {"k": torch.empty(n, B, D, dtype=torch.float32, device=dev),
-                "v": torch.empty(n, B, D, dtype=torch.float32, device=dev), "scale_k": None, "scale_v": None}
+        return (("k", _F32, (n, B, D), n * B * D * 4), ("v", _F32, (n, B, D), n * B * D * 4))
     if code == 1:
-        return {"k": torch.empty(n, B, D, dtype=torch.float16, device=dev),
-                "v": torch.empty(n, B, D, dtype=torch.float16, device=dev), "scale_k": None, "scale_v": None}
+        return (("k", _F16, (n, B, D), n * B * D * 2), ("v", _F16, (n, B, D), n * B * D * 2))
     if code == 2:
-        return {"k": torch.empty(n, B, D, dtype=torch.int8, device=dev),
-                "v": torch.empty(n, B, D, dtype=torch.int8, device=dev),
-                "scale_k": torch.empty(n, B, 1, dtype=torch.float32, device=dev),
-                "scale_v": torch.empty(n, B, 1, dtype=torch.float32, device=dev)}
+        return (("k", _I8, (n, B, D), n * B * D), ("v", _I8, (n, B, D), n * B * D),
+                ("scale_k", _F32, (n, B, 1), n * B * 4), ("scale_v", _F32, (n, B, 1), n * B * 4))
     rb = (B * D + 1) // 2
     ng = D // G
-    return {"k": torch.empty(n * rb, dtype=torch.uint8, device=dev),
-            "v": torch.empty(n * rb, dtype=torch.uint8, device=dev),
-            "scale_k": torch.empty(n * B, ng, 1, dtype=torch.float32, device=dev),
-            "scale_v": torch.empty(n * B, ng, 1, dtype=torch.float32, device=dev)}
+    return (("k", _U8, (n * rb,), n * rb), ("v", _U8, (n * rb,), n * rb),
+            ("scale_k", _F32, (n * B, ng, 1), n * B * ng * 4), ("scale_v", _F32, (n * B, ng, 1), n * B * ng * 4))
+
+
+def _alloc_bucket(code: int, n: int, B: int, D: int, G: int, dev: torch.device) -> Dict[str, torch.Tensor]:
+    """Bucket tensors in the reference layout (packed_kv_cache.py:265-363)."""
+    out = {"scale_k": None, "scale_v": None}
+    for key, dt, shape, _ in _bucket_parts(code, n, B, D, G):
+        out[key] = torch.empty(shape, dtype=dt, device=dev)
+    return out
+
+
+_DISCARD: Dict[Any, torch.Tensor] = {}
+
+
+def _discard_stats(dev: torch.device) -> torch.Tensor:
+    """Per-device int64[2] that takes reuse statistics nobody asked for (never read)."""
+    t = _DISCARD.get(dev.index)
+    if t is None:
+        t = _DISCARD[dev.index] = torch.empty(2, dtype=torch.int64, device=dev)
+    return t
 
 
 def _nbytes(t: Optional[torch.Tensor]) -> int:
     return 0 if t is None else t.numel() * t.element_size()
 
 
+# Slab bytes to try for the next pack of a shape, per (device, B, H, S, D, int4 group): the last
+# exact layout plus an eighth, so that packing launches before the plan's counts reach the host.
+_SLAB_HINT: Dict[Tuple[int, int, int, int, int, int], int] = {}
+
+
+def _slab_layout(counts: Sequence[int], B: int, D: int, G: int):
+    """Per code: None or ((key, dtype, shape, offset, bytes), ...); and the slab bytes.  The
+    arithmetic of the library's slab_layout (each tensor at a 256-byte boundary)."""
+    layout = []
+    total = 0
+    for code in range(4):
+        n = counts[code]
+        if n == 0:
+            layout.append(None)
+            continue
+        parts = []
+        for key, dt, shape, nb in _bucket_parts(code, n, B, D, G):
+            parts.append((key, dt, shape, total, nb))
+            total += (nb + _ALIGN - 1) // _ALIGN * _ALIGN
+        layout.append(parts)
+    return layout, total
+
+
+def _slab_views(slab: torch.Tensor, layout, counts: Sequence[int], plan: PrecisionPlan):
+    """Bucket dicts of typed views into ``slab`` for ``layout``."""
+    typed: Dict[torch.dtype, torch.Tensor] = {}
+    buckets: List[Optional[Dict[str, Any]]] = []
+    start = 0
+    flat_all = plan._flat_all
+    for code in range(4):
+        parts = layout[code]
+        n = counts[code]
+        if parts is None:
+            buckets.append(None)
+            start += n
+            continue
+        b: Dict[str, Any] = {"scale_k": None, "scale_v": None}
+        for key, dt, shape, off, nb in parts:
+            t = typed.get(dt)
+            if t is None:
+                t = typed[dt] = slab.view(dt)
+            es = t.element_size()
+            stride = (shape[1] * shape[2], shape[2], 1) if len(shape) == 3 else (1,)
+            b[key] = t.as_strided(shape, stride, off // es)
+        b["flat"] = flat_all[start:start + n]
+        b["count"] = n
+        start += n
+        buckets.append(b)
+    return buckets
+
+
+def _bucket_array(slab_base: int, layout, counts: Sequence[int], plan: PrecisionPlan):
+    arr = _lib.Buckets4()
+    flat_base = plan._flat_all.data_ptr()
+    start = 0
+    for code in range(4):
+        parts = layout[code]
+        n = counts[code]
+        if parts is not None:
+            a = [slab_base + off for _, _, _, off, _ in parts]
+            arr[code] = _lib.SkvBucket(a[0], a[1], a[2] if len(a) > 2 else None, a[3] if len(a) > 2 else None,
+                                       flat_base + 8 * start, n)
+        start += n
+    return arr
+
+
 def run_pack(k: torch.Tensor, v: torch.Tensor, plan: PrecisionPlan, group_size: int, dense: bool = False,
              k_prev: Optional[torch.Tensor] = None, v_prev: Optional[torch.Tensor] = None,
-             events: Optional[Tuple[Any, Any]] = None,
-             ) -> Tuple[List[Optional[Dict[str, torch.Tensor]]], Optional[torch.Tensor], Optional[torch.Tensor]]:
-    """Launch ``skv_pack`` for ``plan``; returns device buckets (+ dense working copy).
+             events: Optional[Tuple[Any, Any]] = None, want_arr: bool = False,
+             ):
+    """Launch ``skv_pack`` for ``plan``; returns device buckets (+ dense working copy), and with
+    ``want_arr`` also the ``skv_bucket[4]`` array of those buckets.
 
-    ``events``: optional pair of CUDA events recorded immediately around the kernel launch.
+    All buckets live in one allocation (each tensor 256-byte aligned in it).  When the plan's
+    counts are still on their way to the host and a slab size is known for this shape, the
+    kernel is launched at once on a layout the device computes from the counts
+    (``skv_pack_slab``) and the host reads the counts while it runs; a slab that turns out too
+    small receives nothing and the buckets are packed again into an exact one.  Otherwise the
+    layout is computed here and the kernel gets it directly.  The typed tensor views are made
+    after the launch.  ``events``: optional pair of CUDA events recorded around the launch.
     """
     B, H, S, D = k.shape
     dev = plan.compute_device
     G = _int4_group(D, group_size)
     kd = on(k.detach(), dev, torch.float32)
     vd = on(v.detach(), dev, torch.float32)
-    buckets: List[Optional[Dict[str, torch.Tensor]]] = []
-    for code in range(4):
-        n = plan.counts[code]
-        if n == 0:
-            buckets.append(None)
-            continue
-        b = _alloc_bucket(code, n, B, D, G, dev)
-        b["flat"] = plan.bucket_flat(code)
-        b["count"] = n
-        buckets.append(b)
+    lib = _lib.load()
+    key = (dev.index, B, H, S, D, G)
+    hint = None
+    if plan._counts is None and not dense and D in (64, 128, 256) and G % 16 == 0:
+        hint = _SLAB_HINT.get(key)
+    if hint is not None:
+        slab = torch.empty(hint + _ALIGN, dtype=torch.uint8, device=dev)      # + the descriptors
+        base = slab.data_ptr()
+        with device_ctx(dev):
+            if events is not None:
+                events[0].record()
+            st = lib.skv_pack_slab(_lib.ptr(kd), _lib.ptr(vd), B, H, S, D, group_size, _lib.ptr(plan.slot),
+                                   _lib.ptr(plan.counts_device), _lib.ptr(plan._flat_all), base, hint, base + hint,
+                                   _lib.stream_of(dev))
+            if events is not None:
+                events[1].record()
+        _lib.check(st, "PackedKVCache.pack")
+        counts = plan._host_counts()
+        layout, total = _slab_layout(counts, B, D, G)
+        _SLAB_HINT[key] = (total + total // 8 + _ALIGN - 1) // _ALIGN * _ALIGN or _ALIGN
+        if total <= hint:
+            buckets = _slab_views(slab, layout, counts, plan)
+            if want_arr:
+                return buckets, None, None, _bucket_array(base, layout, counts, plan)
+            return buckets, None, None
+        # the layout did not fit: the device wrote nothing; pack into an exact slab below
+    counts = plan._host_counts()
+    layout, total = _slab_layout(counts, B, D, G)
+    _SLAB_HINT[key] = (total + total // 8 + _ALIGN - 1) // _ALIGN * _ALIGN or _ALIGN
+    slab = torch.empty(max(total, _ALIGN), dtype=torch.uint8, device=dev)
+    base = slab.data_ptr()
+    arr = _bucket_array(base, layout, counts, plan)
     dk = dv = None
     kp = vp = None
     if dense:
@@ -152,8 +265,6 @@ def run_pack(k: torch.Tensor, v: torch.Tensor, plan: PrecisionPlan, group_size: 
         if k_prev is not None and plan.reuse_mask_device is not None:
             kp = on(k_prev.detach(), dev, torch.float32)
             vp = on(v_prev.detach(), dev, torch.float32)
-    lib = _lib.load()
-    arr = _lib.buckets(buckets)
     with device_ctx(dev):
         if events is not None:
             events[0].record()
@@ -163,6 +274,9 @@ def run_pack(k: torch.Tensor, v: torch.Tensor, plan: PrecisionPlan, group_size: 
         if events is not None:
             events[1].record()
     _lib.check(st, "PackedKVCache.pack")
+    buckets = _slab_views(slab, layout, counts, plan)
+    if want_arr:
+        return buckets, dk, dv, arr
     return buckets, dk, dv
 
 
@@ -187,7 +301,7 @@ class PackedKVCache:
         self._count: Dict[str, int] = {}
         self._dev: Optional[torch.device] = None
         self._hidx: Optional[Tuple[torch.Tensor, torch.Tensor]] = None   # per-head row lists (attention)
-        self._arr_cache = None                                           # (key, dev, skv_bucket[4], list, direct)
+        self._arr_cache = None     # (packed_data, dev, skv_bucket[4], device buckets, direct, snapshot)
 
     # ------------------------------------------------------------------------------ pack
     @classmethod
@@ -237,11 +351,12 @@ class PackedKVCache:
             )
         if not isinstance(plan, PrecisionPlan):
             plan = PrecisionPlan.from_codes(plan.codes, device=plan.codes.device)
-        buckets, _, _ = run_pack(k_tensor, v_tensor, plan, group_size, events=self._pack_events)
-        self._adopt(buckets, plan.slot, shared_slot=True, group_size=group_size)
+        buckets, _, _, arr = run_pack(k_tensor, v_tensor, plan, group_size, events=self._pack_events, want_arr=True)
+        self._adopt(buckets, plan.slot, shared_slot=True, group_size=group_size, arr=arr)
 
-    def _adopt(self, buckets, slot: torch.Tensor, shared_slot: bool, group_size: int) -> None:
-        """Install device buckets as ``packed_data`` (on the cache's device)."""
+    def _adopt(self, buckets, slot: torch.Tensor, shared_slot: bool, group_size: int, arr=None) -> None:
+        """Install device buckets as ``packed_data`` (on the cache's device); ``arr``: their
+        ``skv_bucket[4]``, kept as the kernels' view when the payload stays on that device."""
         self._dev = slot.device
         self._slot = slot
         self._slot_owned = not shared_slot
@@ -270,6 +385,10 @@ class PackedKVCache:
             for key in ("k", "v", "scale_k", "scale_v"):
                 total += _nbytes(data[key])
         self._memory_bytes = total
+        if arr is not None and all(b is None or all(b[x] is dict.__getitem__(self.packed_data[p], x)
+                                                    for x in ("k", "v", "scale_k", "scale_v"))
+                                   for p, b in zip(PRECISION_ORDER, buckets)):
+            self._arr_cache = (self.packed_data, self._dev, arr, buckets, True, self._arr_snapshot())
 
     def _indices_fn(self, p: str) -> Callable[[], List[Tuple[int, int]]]:
         flat, S = self._flat[p], self.seq_len
@@ -311,15 +430,36 @@ class PackedKVCache:
         self._dev = dev
         return dev
 
+    def _arr_snapshot(self):
+        """(precision, bucket dict, ((key, tensor, address), ...)) of the current payload."""
+        snap = []
+        for p, d in self.packed_data.items():
+            ts = []
+            for x in ("k", "v", "scale_k", "scale_v"):
+                t = dict.get(d, x)
+                ts.append((x, t, None if t is None else t.data_ptr()))
+            snap.append((p, d, tuple(ts)))
+        return tuple(snap)
+
+    def _arr_valid(self, snap) -> bool:
+        """The payload is still the snapshot's: same buckets, tensor objects and addresses."""
+        pd = self.packed_data
+        if len(pd) != len(snap):
+            return False
+        for p, d, ts in snap:
+            if pd.get(p) is not d:
+                return False
+            for x, t, a in ts:
+                if dict.get(d, x) is not t or (t is not None and t.data_ptr() != a):
+                    return False
+        return True
+
     def _device_arr(self, dev: torch.device):
         """``skv_bucket[4]`` of this cache for ``dev`` plus a flag: True when the kernels work on
-        the ``packed_data`` tensors themselves (no copy-back needed).  Cached while those
-        tensor objects stay the same."""
-        key = tuple(None if d is None else tuple(None if t is None else (id(t), t.data_ptr())
-                                                 for t in (d.get("k"), d.get("v"), d.get("scale_k"), d.get("scale_v")))
-                    for d in (self.packed_data.get(p) for p in PRECISION_ORDER))
+        the ``packed_data`` tensors themselves (no copy-back needed).  Cached while the payload
+        (bucket dicts, tensor objects and their addresses) stays the same."""
         cached = self._arr_cache
-        if cached is not None and cached[0] == key and cached[1] == dev:
+        if cached is not None and cached[0] is self.packed_data and cached[1] == dev and self._arr_valid(cached[5]):
             return cached[2], cached[3], cached[4]
         bk = self._device_buckets(dev)
         direct = True
@@ -329,7 +469,7 @@ class PackedKVCache:
             data = self.packed_data[p]
             direct &= all(b[x] is data[x] for x in ("k", "v", "scale_k", "scale_v"))
         arr = _lib.buckets(bk)
-        self._arr_cache = (key, dev, arr, bk, direct)
+        self._arr_cache = (self.packed_data, dev, arr, bk, direct, self._arr_snapshot())
         return arr, bk, direct
 
     def _device_buckets(self, dev: torch.device) -> List[Optional[Dict[str, Any]]]:
@@ -576,7 +716,7 @@ class PackedKVCache:
         mask = self._entry_mask_from_reuse(reuse_mask, dev)
         cur_arr, cur_b, direct = self._device_arr(dev)
         prev_arr, _, _ = prev._device_arr(dev)
-        stats_d = torch.empty(2, dtype=torch.int64, device=dev)
+        stats_d = torch.empty(2, dtype=torch.int64, device=dev) if return_stats else _discard_stats(dev)
         lib = _lib.load()
         with device_ctx(dev):
             st = lib.skv_apply_reuse(cur_arr, _lib.ptr(self._slot), self.seq_len, prev_arr,

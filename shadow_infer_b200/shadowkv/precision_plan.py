@@ -20,7 +20,7 @@ from typing import Any, Dict, List, Optional, Tuple
 import torch
 
 from .. import _lib
-from .._device import as_device, compute_device, device_ctx, mask_u8, on, scratch
+from .._device import as_device, compute_device, device_ctx, mask_u8, on
 
 PRECISION_ORDER: Tuple[str, ...] = ("fp32", "fp16", "int8", "int4")
 EVICTED = "evicted"
@@ -105,6 +105,10 @@ def reuse_mask_tensor(reuse_mask: Any, seq_len: int, num_heads: int, dev: torch.
     return full.view(seq_len, num_heads).to(dev, non_blocking=True)
 
 
+# pinned int64[6] host buffers for plan counts, returned here once read
+_PINNED: List[torch.Tensor] = []
+
+
 def _entries(flat: torch.Tensor, seq_len: int) -> List[Tuple[int, int]]:
     f = flat.detach().to("cpu")
     return list(zip((f % seq_len).tolist(), torch.div(f, seq_len, rounding_mode="floor").tolist()))
@@ -120,7 +124,7 @@ class PrecisionPlan:
     """
 
     __slots__ = ("_seq_len", "_num_heads", "_codes", "_device", "_dev", "_flat_all", "_counts", "_slot",
-                 "_reuse_flat_dev", "_reuse_mask_dev", "_lazy", "_frozen")
+                 "_reuse_flat_dev", "_reuse_mask_dev", "_lazy", "_frozen", "_counts_dev", "_pending")
 
     def __init__(self, *args, **kwargs):
         raise TypeError("use PrecisionPlan.build(...) or PrecisionPlan.from_codes(...)")
@@ -164,45 +168,75 @@ class PrecisionPlan:
         codes_d = on(codes_nom, dev)
         mask_d = reuse_mask_tensor(reuse_mask, seq_len, num_heads, dev)
         n = seq_len * num_heads
+        lib = _lib.load()
+        nbytes = lib.skv_plan_scratch_bytes(seq_len, num_heads)
         flat_all = torch.empty(n, dtype=torch.int64, device=dev)
         slot = torch.empty(n, dtype=torch.int32, device=dev)
         reuse_all = torch.empty(n if mask_d is not None else 0, dtype=torch.int64, device=dev)
         counts_d = torch.empty(6, dtype=torch.int64, device=dev)
-        lib = _lib.load()
-        nbytes = lib.skv_plan_scratch_bytes(seq_len, num_heads)
-        scr = scratch(nbytes, dev)
+        scr = torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=dev)
         with device_ctx(dev):
-            st = lib.skv_plan_bucket(_lib.ptr(codes_d), _lib.ptr(mask_d), seq_len, num_heads, _lib.ptr(flat_all),
-                                     _lib.ptr(slot), _lib.ptr(reuse_all) if mask_d is not None else None,
-                                     _lib.ptr(counts_d), _lib.ptr(scr), scr.numel(), _lib.stream_of(dev))
+            st = lib.skv_plan_bucket(_lib.ptr(codes_d), _lib.ptr(mask_d), seq_len, num_heads, flat_all.data_ptr(),
+                                     slot.data_ptr(), reuse_all.data_ptr() if mask_d is not None else None,
+                                     counts_d.data_ptr(), scr.data_ptr(), scr.numel(), _lib.stream_of(dev))
         _lib.check(st, "PrecisionPlan.from_codes")
-        counts = [int(c) for c in counts_d.tolist()]
+        # the counts travel to a pinned host buffer behind an event: nothing waits for them
+        # until a host-side field needs them (packing launches on the device counts)
+        counts_h = _PINNED.pop() if _PINNED else torch.empty(6, dtype=torch.int64, pin_memory=True)
+        with device_ctx(dev):
+            counts_h.copy_(counts_d, non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record()
         plan = object.__new__(cls)
-        plan._frozen = False
-        plan._seq_len = seq_len
-        plan._num_heads = num_heads
-        plan._codes = codes_nom
-        plan._device = device
-        plan._dev = dev
-        plan._flat_all = flat_all
-        plan._counts = counts
-        plan._slot = slot
-        plan._reuse_flat_dev = reuse_all[: counts[5]] if mask_d is not None else reuse_all
-        plan._reuse_mask_dev = mask_d if (mask_d is not None and counts[5] > 0) else None
-        plan._lazy = {}
-        plan._frozen = True
+        st = object.__setattr__
+        st(plan, "_seq_len", seq_len)
+        st(plan, "_num_heads", num_heads)
+        st(plan, "_codes", codes_nom)
+        st(plan, "_device", device)
+        st(plan, "_dev", dev)
+        st(plan, "_flat_all", flat_all)
+        st(plan, "_counts", None)
+        st(plan, "_counts_dev", counts_d)
+        st(plan, "_pending", (ev, counts_h, reuse_all, mask_d))
+        st(plan, "_slot", slot)
+        st(plan, "_reuse_flat_dev", None)
+        st(plan, "_reuse_mask_dev", None)
+        st(plan, "_lazy", {})
+        st(plan, "_frozen", True)
         return plan
+
+    def _host_counts(self) -> List[int]:
+        """Counts per code 0..4 and the reuse count, waiting for the plan kernel if needed."""
+        c = self._counts
+        if c is None:
+            ev, counts_h, reuse_all, mask_d = self._pending
+            ev.synchronize()
+            c = counts_h.tolist()
+            if len(_PINNED) < 64:
+                _PINNED.append(counts_h)
+            st = object.__setattr__
+            st(self, "_counts", c)
+            st(self, "_reuse_flat_dev", reuse_all[: c[5]] if mask_d is not None else reuse_all)
+            st(self, "_reuse_mask_dev", mask_d if (mask_d is not None and c[5] > 0) else None)
+            st(self, "_pending", None)
+        return c
+
+    @property
+    def counts_device(self) -> torch.Tensor:
+        """Device int64 ``[6]``: entries per code 0..4, then reuse entries (no host sync)."""
+        return self._counts_dev
 
     # -- device-side state used by PackedKVCache / compress ------------------------------
     def bucket_flat(self, code: int) -> torch.Tensor:
         """Device int64 ``h*S+t`` of the entries with ``code`` (bucket order)."""
-        start = sum(self._counts[:code])
-        return self._flat_all[start:start + self._counts[code]]
+        c = self._host_counts()
+        start = sum(c[:code])
+        return self._flat_all[start:start + c[code]]
 
     @property
     def counts(self) -> List[int]:
         """Entries per code 0..4 (fp32, fp16, int8, int4, evicted)."""
-        return list(self._counts[:5])
+        return self._host_counts()[:5]
 
     @property
     def slot(self) -> torch.Tensor:
@@ -215,6 +249,7 @@ class PrecisionPlan:
 
     @property
     def reuse_mask_device(self) -> Optional[torch.Tensor]:
+        self._host_counts()
         return self._reuse_mask_dev
 
     # -- reference fields ----------------------------------------------------------------
@@ -243,19 +278,20 @@ class PrecisionPlan:
     @property
     def groups(self) -> Dict[str, List[Tuple[int, int]]]:
         if "groups" not in self._lazy:
-            self._lazy["groups"] = {p: _entries(self.bucket_flat(c), self._seq_len) if self._counts[c] else []
+            self._lazy["groups"] = {p: _entries(self.bucket_flat(c), self._seq_len) if self._host_counts()[c] else []
                                     for c, p in enumerate(PRECISION_ORDER)}
         return self._lazy["groups"]
 
     @property
     def evicted_entries(self) -> List[Tuple[int, int]]:
         if "evicted" not in self._lazy:
-            self._lazy["evicted"] = _entries(self.bucket_flat(4), self._seq_len) if self._counts[4] else []
+            self._lazy["evicted"] = _entries(self.bucket_flat(4), self._seq_len) if self._host_counts()[4] else []
         return self._lazy["evicted"]
 
     @property
     def reuse_flat(self) -> torch.Tensor:
         if "reuse_flat" not in self._lazy:
+            self._host_counts()
             t = self._reuse_flat_dev
             self._lazy["reuse_flat"] = t if t.device == self._device else t.to(self._device)
         return self._lazy["reuse_flat"]
@@ -263,7 +299,8 @@ class PrecisionPlan:
     @property
     def reuse_entries(self) -> List[Tuple[int, int]]:
         if "reuse_entries" not in self._lazy:
-            self._lazy["reuse_entries"] = _entries(self._reuse_flat_dev, self._seq_len) if self._counts[5] else []
+            c = self._host_counts()
+            self._lazy["reuse_entries"] = _entries(self._reuse_flat_dev, self._seq_len) if c[5] else []
         return self._lazy["reuse_entries"]
 
     @property
@@ -273,6 +310,7 @@ class PrecisionPlan:
             digest = hashlib.sha256()
             digest.update(struct.pack("<QQ", self._seq_len, self._num_heads))
             digest.update(self._codes.detach().to("cpu").contiguous().numpy().tobytes())
+            self._host_counts()
             digest.update(self._reuse_flat_dev.detach().to("cpu").contiguous().numpy().tobytes())
             self._lazy["fingerprint"] = digest.hexdigest()
         return self._lazy["fingerprint"]
@@ -283,5 +321,5 @@ class PrecisionPlan:
 
     def __repr__(self) -> str:
         return (f"PrecisionPlan(seq_len={self._seq_len}, num_heads={self._num_heads}, "
-                f"counts={dict(zip(PRECISION_ORDER + (EVICTED,), self._counts[:5]))}, "
-                f"reuse={self._counts[5]})")
+                f"counts={dict(zip(PRECISION_ORDER + (EVICTED,), self._host_counts()[:5]))}, "
+                f"reuse={self._host_counts()[5]})")

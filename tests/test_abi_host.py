@@ -114,3 +114,25 @@ def test_lazy_bucket_dict_behaves_like_dict():
     assert b.get("missing", 5) == 5
     assert isinstance(b, dict)
 
+
+
+@pytest.mark.parametrize("B,D,group", [(1, 128, 16), (8, 128, 16), (2, 64, 32), (1, 256, 16), (3, 96, 48)])
+def test_slab_layout_agrees_with_library(B, D, group):
+    """The host bucket layout of one pack slab and the library's (device) layout need the same
+    bytes for any counts: the host makes its tensor views from the former while the kernel
+    writes through the latter."""
+    import ctypes
+    from shadow_infer_b200 import _lib
+    from shadow_infer_b200.shadowkv.packed_kv_cache import _int4_group, _slab_layout
+    lib = _lib.load()
+    rng = np.random.default_rng(B * 1000 + D)
+    G = _int4_group(D, group)
+    for _ in range(50):
+        counts = [int(x) for x in rng.integers(0, 5000, size=6)]
+        counts[rng.integers(0, 4)] = 0                       # an empty bucket
+        layout, total = _slab_layout(counts, B, D, G)
+        arr = (ctypes.c_int64 * 6)(*counts)
+        assert lib.skv_pack_slab_bytes(arr, B, D, group) == total
+        for parts in layout:
+            for _, _, _, off, nb in parts or ():
+                assert off % 256 == 0 and off + nb <= total

@@ -168,9 +168,8 @@ def test_admit_does_not_mutate_input(skv):
     assert torch.equal(codes, before)
 
 
-def test_allocate_and_sensitivity(golden_small):
+def test_allocate_and_sensitivity(skv, golden_small):
     from shadow_infer_b200.shadowkv.shadowkv_agent import allocate_precision_codes
-    import shadow_infer_b200.shadowkv as skv
     a = case_arrays(golden_small, "allocate")
     for mode in ("aggressive", "balanced", "conservative", "unknown"):
         assert eq(allocate_precision_codes(cu(a["importance"]), mode), a[f"codes.{mode}"]), mode
@@ -249,3 +248,52 @@ def test_oracle_agrees_at_random_shapes(skv):
         ku, vu = cache.unpack()
         ko, vo = O.unpack(ref)
         assert eq(ku, ko) and eq(vu, vo), trial
+
+
+def _bucket_bytes(cache):
+    out = {}
+    for p, d in cache.packed_data.items():
+        for key in ("k", "v", "scale_k", "scale_v"):
+            t = d[key]
+            out[(p, key)] = None if t is None else (tuple(t.shape), t.dtype, t.cpu().numpy().tobytes())
+    return out
+
+
+def test_pack_before_counts_reach_host(skv):
+    """Packing launched on the device layout (the plan's counts still in flight) equals packing
+    on the host layout, also when the slab guessed from the previous pack is too small (the
+    device writes nothing and the buckets are packed again)."""
+    from shadow_infer_b200 import _lib
+    from shadow_infer_b200.shadowkv import packed_kv_cache as PKC
+    rng = np.random.default_rng(31)
+    B, H, S, D = 2, 8, 300, 128
+    k, v = cu(rng.standard_normal((B, H, S, D)).astype(np.float32)), cu(rng.standard_normal((B, H, S, D)).astype(np.float32))
+    lib = _lib.load()
+    PKC._SLAB_HINT.clear()
+    for probs in ((0.0, 0.1, 0.3, 0.5, 0.1), (0.7, 0.2, 0.1, 0.0, 0.0), (0.7, 0.2, 0.1, 0.0, 0.0),
+                  (0.0, 0.0, 0.0, 1.0, 0.0), (0.0, 0.0, 0.0, 0.0, 1.0)):
+        codes = cu(rng.choice(5, size=(S, H), p=probs).astype(np.int8))
+        exact_plan = skv.PrecisionPlan.from_codes(codes)
+        exact_plan.counts                                  # counts on the host: host layout
+        want = skv.PackedKVCache.pack(k, v, None, 16, plan=exact_plan)["packed_kv"]
+        hint = PKC._SLAB_HINT.get((0, B, H, S, D, 16))
+        lazy_plan = skv.PrecisionPlan.from_codes(codes)    # counts in flight: device layout
+        n0 = lib.skv_launch_count()
+        got = skv.PackedKVCache.pack(k, v, None, 16, plan=lazy_plan)["packed_kv"]
+        launches = lib.skv_launch_count() - n0
+        assert launches == 2                               # layout + pack, the hint fits (same counts)
+        assert _bucket_bytes(got) == _bucket_bytes(want)
+        assert got.memory_bytes() == want.memory_bytes()
+        ku, vu = got.unpack()
+        kw, vw = want.unpack()
+        assert torch.equal(ku, kw) and torch.equal(vu, vw)
+        # a slab that is too small: shrink the hint below this layout, then pack again
+        PKC._SLAB_HINT[(0, B, H, S, D, 16)] = 256
+        small_plan = skv.PrecisionPlan.from_codes(codes)
+        n0 = lib.skv_launch_count()
+        again = skv.PackedKVCache.pack(k, v, None, 16, plan=small_plan)["packed_kv"]
+        launches = lib.skv_launch_count() - n0
+        stored = sum(1 for p in again.packed_data)
+        assert launches == (3 if stored else 2)            # layout + empty pack + exact pack
+        assert _bucket_bytes(again) == _bucket_bytes(want)
+        assert hint is not None
