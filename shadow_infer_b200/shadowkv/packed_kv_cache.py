@@ -210,7 +210,19 @@ def run_pack(k: torch.Tensor, v: torch.Tensor, plan: PrecisionPlan, group_size: 
              events: Optional[Tuple[Any, Any]] = None, want_arr: bool = False,
              ):
     """Launch ``skv_pack`` for ``plan``; returns device buckets (+ dense working copy), and with
-    ``want_arr`` also the ``skv_bucket[4]`` array of those buckets.
+    ``want_arr`` also the ``skv_bucket[4]`` array of those buckets (see ``pack_slab``)."""
+    slab, layout, counts, arr, dk, dv = pack_slab(k, v, plan, group_size, dense, k_prev, v_prev, events)
+    buckets = _slab_views(slab, layout, counts, plan)
+    if want_arr:
+        return buckets, dk, dv, arr
+    return buckets, dk, dv
+
+
+def pack_slab(k: torch.Tensor, v: torch.Tensor, plan: PrecisionPlan, group_size: int, dense: bool = False,
+              k_prev: Optional[torch.Tensor] = None, v_prev: Optional[torch.Tensor] = None,
+              events: Optional[Tuple[Any, Any]] = None):
+    """Launch ``skv_pack`` for ``plan``; returns ``(slab, layout, counts, skv_bucket[4], dense_k,
+    dense_v)`` -- the buckets as one allocation and its layout (``_slab_layout``), no views.
 
     All buckets live in one allocation (each tensor 256-byte aligned in it).  When the plan's
     counts are still on their way to the host and a slab size is known for this shape, the
@@ -218,7 +230,8 @@ def run_pack(k: torch.Tensor, v: torch.Tensor, plan: PrecisionPlan, group_size: 
     (``skv_pack_slab``) and the host reads the counts while it runs; a slab that turns out too
     small receives nothing and the buckets are packed again into an exact one.  Otherwise the
     layout is computed here and the kernel gets it directly.  The typed tensor views are made
-    after the launch.  ``events``: optional pair of CUDA events recorded around the launch.
+    by the caller (``_slab_views``) after the launch.  ``events``: optional pair of CUDA events
+    recorded around the launch.
     """
     B, H, S, D = k.shape
     dev = plan.compute_device
@@ -246,10 +259,7 @@ def run_pack(k: torch.Tensor, v: torch.Tensor, plan: PrecisionPlan, group_size: 
         layout, total = _slab_layout(counts, B, D, G)
         _SLAB_HINT[key] = (total + total // 8 + _ALIGN - 1) // _ALIGN * _ALIGN or _ALIGN
         if total <= hint:
-            buckets = _slab_views(slab, layout, counts, plan)
-            if want_arr:
-                return buckets, None, None, _bucket_array(base, layout, counts, plan)
-            return buckets, None, None
+            return slab, layout, counts, _bucket_array(base, layout, counts, plan), None, None
         # the layout did not fit: the device wrote nothing; pack into an exact slab below
     counts = plan._host_counts()
     layout, total = _slab_layout(counts, B, D, G)
@@ -274,10 +284,7 @@ def run_pack(k: torch.Tensor, v: torch.Tensor, plan: PrecisionPlan, group_size: 
         if events is not None:
             events[1].record()
     _lib.check(st, "PackedKVCache.pack")
-    buckets = _slab_views(slab, layout, counts, plan)
-    if want_arr:
-        return buckets, dk, dv, arr
-    return buckets, dk, dv
+    return slab, layout, counts, arr, dk, dv
 
 
 class PackedKVCache:
@@ -293,7 +300,9 @@ class PackedKVCache:
         self.seq_len = seq_len
         self.head_dim = head_dim
         self.device = device
-        self.packed_data: Dict[str, Dict[str, Any]] = {}
+        self._packed_data: Dict[str, Dict[str, Any]] = {}
+        # (slab, layout, counts, plan, group_size) of a pack whose packed_data views are not made yet
+        self._pending = None
         self._memory_bytes = 0
         self._slot: Optional[torch.Tensor] = None       # device int32 [S*H]
         self._slot_owned = False
@@ -302,6 +311,20 @@ class PackedKVCache:
         self._dev: Optional[torch.device] = None
         self._hidx: Optional[Tuple[torch.Tensor, torch.Tensor]] = None   # per-head row lists (attention)
         self._arr_cache = None     # (packed_data, dev, skv_bucket[4], device buckets, direct, snapshot)
+
+    @property
+    def packed_data(self) -> Dict[str, Dict[str, Any]]:
+        """Per-precision bucket dicts (reference schema); after ``pack`` the tensor views into the
+        bucket allocation are made on first access."""
+        if self._pending is not None:
+            self._materialise()
+        return self._packed_data
+
+    @packed_data.setter
+    def packed_data(self, value: Dict[str, Dict[str, Any]]) -> None:
+        self._pending = None
+        self._packed_data = value
+        self._arr_cache = None
 
     # ------------------------------------------------------------------------------ pack
     @classmethod
@@ -351,8 +374,33 @@ class PackedKVCache:
             )
         if not isinstance(plan, PrecisionPlan):
             plan = PrecisionPlan.from_codes(plan.codes, device=plan.codes.device)
-        buckets, _, _, arr = run_pack(k_tensor, v_tensor, plan, group_size, events=self._pack_events, want_arr=True)
-        self._adopt(buckets, plan.slot, shared_slot=True, group_size=group_size, arr=arr)
+        slab, layout, counts, arr, _, _ = pack_slab(k_tensor, v_tensor, plan, group_size, events=self._pack_events)
+        self._adopt_pending(slab, layout, counts, plan, group_size, arr)
+
+    def _adopt_pending(self, slab: torch.Tensor, layout, counts: Sequence[int], plan: PrecisionPlan,
+                       group_size: int, arr) -> None:
+        """Install a freshly packed slab: counts, bytes and the kernels' bucket array now, the
+        ``packed_data`` views on first access (``_materialise``)."""
+        self._dev = plan.slot.device
+        self._slot = plan.slot
+        self._slot_owned = False
+        self._hidx = None
+        self._packed_data = {}
+        self._flat = {}
+        self._count = {PRECISION_ORDER[c]: counts[c] for c in range(4) if counts[c]}
+        self._memory_bytes = sum(nb for parts in layout if parts for _, _, _, _, nb in parts)
+        self._pending = (slab, layout, counts, plan, group_size)
+        self._arr_cache = (None, self._dev, arr, None, True, None)
+
+    def _materialise(self) -> None:
+        """Make the ``packed_data`` views of a pending slab (keeps the kernels' bucket array)."""
+        slab, layout, counts, plan, group_size = self._pending
+        self._pending = None
+        arr = self._arr_cache[2]
+        hidx = self._hidx
+        self._adopt(_slab_views(slab, layout, counts, plan), plan.slot, shared_slot=True, group_size=group_size,
+                    arr=arr)
+        self._hidx = hidx
 
     def _adopt(self, buckets, slot: torch.Tensor, shared_slot: bool, group_size: int, arr=None) -> None:
         """Install device buckets as ``packed_data`` (on the cache's device); ``arr``: their
@@ -362,7 +410,8 @@ class PackedKVCache:
         self._slot_owned = not shared_slot
         self._hidx = None
         self._arr_cache = None
-        self.packed_data = {}
+        self._pending = None
+        self._packed_data = {}
         self._flat = {}
         self._count = {}
         total = 0
@@ -385,10 +434,10 @@ class PackedKVCache:
             for key in ("k", "v", "scale_k", "scale_v"):
                 total += _nbytes(data[key])
         self._memory_bytes = total
-        if arr is not None and all(b is None or all(b[x] is dict.__getitem__(self.packed_data[p], x)
+        if arr is not None and all(b is None or all(b[x] is dict.__getitem__(self._packed_data[p], x)
                                                     for x in ("k", "v", "scale_k", "scale_v"))
                                    for p, b in zip(PRECISION_ORDER, buckets)):
-            self._arr_cache = (self.packed_data, self._dev, arr, buckets, True, self._arr_snapshot())
+            self._arr_cache = (self._packed_data, self._dev, arr, buckets, True, self._arr_snapshot())
 
     def _indices_fn(self, p: str) -> Callable[[], List[Tuple[int, int]]]:
         flat, S = self._flat[p], self.seq_len
@@ -459,6 +508,8 @@ class PackedKVCache:
         the ``packed_data`` tensors themselves (no copy-back needed).  Cached while the payload
         (bucket dicts, tensor objects and their addresses) stays the same."""
         cached = self._arr_cache
+        if self._pending is not None and cached is not None and cached[1] == dev:
+            return cached[2], None, True                   # views not made yet: the pack's own array
         if cached is not None and cached[0] is self.packed_data and cached[1] == dev and self._arr_valid(cached[5]):
             return cached[2], cached[3], cached[4]
         bk = self._device_buckets(dev)
@@ -498,7 +549,15 @@ class PackedKVCache:
             self._hidx = (rows, counts)
         return self._hidx
 
+    def _has_int4(self) -> bool:
+        return "int4" in self._count if self._pending is not None else "int4" in self.packed_data
+
+    def _has_buckets(self) -> bool:
+        return bool(self._count) if self._pending is not None else bool(self.packed_data)
+
     def _int4_group_of(self) -> int:
+        if self._pending is not None:
+            return _int4_group(self.head_dim, self._pending[4]) if "int4" in self._count else self.head_dim
         d = self.packed_data.get("int4")
         return int(d["group_size"]) if d is not None else self.head_dim
 
@@ -506,7 +565,7 @@ class PackedKVCache:
     def unpack(self) -> Tuple[torch.Tensor, torch.Tensor]:
         """Zero-filled float32 ``[B,H,S,D]`` K and V from all buckets (packed_kv_cache.py:535-577)."""
         shape = (self.batch_size, self.num_heads, self.seq_len, self.head_dim)
-        if not self.packed_data:
+        if not (self._count if self._pending is not None else self.packed_data):
             k_out = torch.zeros(shape, dtype=torch.float32, device=self.device)
             return k_out, torch.zeros_like(k_out)
         dev = self._ensure_state()
@@ -700,16 +759,14 @@ class PackedKVCache:
                 f"current=({self.batch_size},{self.num_heads},{self.head_dim}) "
                 f"previous=({prev.batch_size},{prev.num_heads},{prev.head_dim})"
             )
-        cur4 = self.packed_data.get("int4")
-        prev4 = prev.packed_data.get("int4")
-        if cur4 is not None and prev4 is not None and cur4["group_size"] != prev4["group_size"]:
+        if self._has_int4() and prev._has_int4() and self._int4_group_of() != prev._int4_group_of():
             raise ValueError(
                 "INT4 group_size mismatch for reuse: "
-                f"current={cur4['group_size']} previous={prev4['group_size']}"
+                f"current={self._int4_group_of()} previous={prev._int4_group_of()}"
             )
         stats = {"applied": 0, "skipped_precision": 0}
         empty_mask = reuse_mask is None or (not torch.is_tensor(reuse_mask) and not reuse_mask)
-        if empty_mask or not prev.packed_data or not self.packed_data:
+        if empty_mask or not prev._has_buckets() or not self._has_buckets():
             return stats if return_stats else None
         dev = self._ensure_state()
         prev._ensure_state()

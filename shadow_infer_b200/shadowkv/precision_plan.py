@@ -105,8 +105,8 @@ def reuse_mask_tensor(reuse_mask: Any, seq_len: int, num_heads: int, dev: torch.
     return full.view(seq_len, num_heads).to(dev, non_blocking=True)
 
 
-# pinned int64[6] host buffers for plan counts, returned here once read
-_PINNED: List[torch.Tensor] = []
+# (pinned int64[6] host buffer, event) pairs for plan counts, returned here once read
+_PINNED: List[Tuple[torch.Tensor, Any]] = []
 
 
 def _entries(flat: torch.Tensor, seq_len: int) -> List[Tuple[int, int]]:
@@ -163,9 +163,13 @@ class PrecisionPlan:
         if seq_len <= 0 or num_heads <= 0:
             raise ValueError(f"seq_len and num_heads must be positive, got {seq_len}, {num_heads}")
         device = codes.device if device is None else as_device(device)
-        codes_nom = codes.detach().to(device=device, dtype=torch.int8).contiguous()
-        dev = compute_device(codes_nom)
-        codes_d = on(codes_nom, dev)
+        if codes.dtype is torch.int8 and codes.is_cuda and codes.device == device and codes.is_contiguous():
+            codes_nom = codes_d = codes                  # already what the kernel reads
+            dev = codes.device
+        else:
+            codes_nom = codes.detach().to(device=device, dtype=torch.int8).contiguous()
+            dev = compute_device(codes_nom)
+            codes_d = on(codes_nom, dev)
         mask_d = reuse_mask_tensor(reuse_mask, seq_len, num_heads, dev)
         n = seq_len * num_heads
         lib = _lib.load()
@@ -182,10 +186,10 @@ class PrecisionPlan:
         _lib.check(st, "PrecisionPlan.from_codes")
         # the counts travel to a pinned host buffer behind an event: nothing waits for them
         # until a host-side field needs them (packing launches on the device counts)
-        counts_h = _PINNED.pop() if _PINNED else torch.empty(6, dtype=torch.int64, pin_memory=True)
+        counts_h, ev = _PINNED.pop() if _PINNED else (torch.empty(6, dtype=torch.int64, pin_memory=True),
+                                                      torch.cuda.Event())
         with device_ctx(dev):
             counts_h.copy_(counts_d, non_blocking=True)
-            ev = torch.cuda.Event()
             ev.record()
         plan = object.__new__(cls)
         st = object.__setattr__
@@ -213,7 +217,7 @@ class PrecisionPlan:
             ev.synchronize()
             c = counts_h.tolist()
             if len(_PINNED) < 64:
-                _PINNED.append(counts_h)
+                _PINNED.append((counts_h, ev))
             st = object.__setattr__
             st(self, "_counts", c)
             st(self, "_reuse_flat_dev", reuse_all[: c[5]] if mask_d is not None else reuse_all)

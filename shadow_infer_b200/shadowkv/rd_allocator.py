@@ -91,13 +91,17 @@ def admit_codes_device(
     S, H = int(codes.shape[0]), int(codes.shape[1])
     dev = compute_device(codes, importance, sensitivity)
     cd = on(codes.detach(), dev, torch.int8)
-    imp = importance.detach()[:S, :H]
+    imp = importance.detach()
     if tuple(imp.shape) != (S, H):
-        raise ValueError(f"importance must cover codes {(S, H)}, got {tuple(importance.shape)}")
+        imp = imp[:S, :H]
+        if tuple(imp.shape) != (S, H):
+            raise ValueError(f"importance must cover codes {(S, H)}, got {tuple(importance.shape)}")
     imp = on(imp, dev, torch.float32)
     sens = None
     if sensitivity is not None:
-        s = sensitivity.detach()[:S, :H]
+        s = sensitivity.detach()
+        if tuple(s.shape) != (S, H):
+            s = s[:S, :H]
         if tuple(s.shape) == (S, H):
             sens = on(s, dev, torch.float32)
     prot = None
