@@ -36,11 +36,36 @@ __device__ __forceinline__ bool aligned16(const void* a, const void* b, const vo
              reinterpret_cast<uintptr_t>(d)) & 15) == 0;
 }
 
-// One warp per 32 consecutive entries.  Rows to copy are grouped by precision; the 16-byte
-// chunks of all selected rows of a group are spread over the lanes, so a warp has up to 32
-// independent copies in flight instead of one row at a time.
-__global__ void __launch_bounds__(256) reuse_kernel(Buckets cur, const int32_t* __restrict__ cur_slot,
-                                                    int S, Buckets prev, const int32_t* __restrict__ prev_slot,
+// Copy of one small row (payload of K and V, bytes a multiple of 16 and at most kLaneRowBytes)
+// by a single lane: every 16-byte load is issued before the first store.
+constexpr int kLaneRowBytes = 64;
+
+__device__ __forceinline__ void lane_copy_row(uint8_t* __restrict__ dk, uint8_t* __restrict__ dv,
+                                              const uint8_t* __restrict__ sk, const uint8_t* __restrict__ sv,
+                                              int chunks) {
+    uint4 a[kLaneRowBytes / 16], b[kLaneRowBytes / 16];
+#pragma unroll
+    for (int i = 0; i < kLaneRowBytes / 16; ++i)
+        if (i < chunks) {
+            a[i] = __ldg(reinterpret_cast<const uint4*>(sk) + i);
+            b[i] = __ldg(reinterpret_cast<const uint4*>(sv) + i);
+        }
+#pragma unroll
+    for (int i = 0; i < kLaneRowBytes / 16; ++i)
+        if (i < chunks) {
+            reinterpret_cast<uint4*>(dk)[i] = a[i];
+            reinterpret_cast<uint4*>(dv)[i] = b[i];
+        }
+}
+
+// One warp per 32 consecutive entries; the reuse flag and both slots of an entry are loaded
+// together.  A row of at most 128 bytes (int8/int4 at small batch) is copied by its own lane,
+// scales with it; larger rows are grouped by precision and their 16-byte chunks spread over
+// the lanes, so a warp has up to 32 independent copies in flight.
+__global__ void __launch_bounds__(256, 3) reuse_kernel(const __grid_constant__ Buckets cur,
+                                                       const int32_t* __restrict__ cur_slot, int S,
+                                                       const __grid_constant__ Buckets prev,
+                                                       const int32_t* __restrict__ prev_slot,
                                                     int S_prev, const uint8_t* __restrict__ mask, int B,
                                                     int H, int D, int NG, long long* __restrict__ stats) {
     const int lane = threadIdx.x & 31;
@@ -51,21 +76,69 @@ __global__ void __launch_bounds__(256) reuse_kernel(Buckets cur, const int32_t* 
          base += nwarps * 32) {
         const int64_t e = base + lane;
         int32_t cs = -1, ps = -1;
-        bool copy = false;
-        if (e < n && mask[e]) {
+        bool flag = false;
+        if (e < n) {
+            const int64_t t = e / H;
+            flag = mask[e] != 0;
             cs = cur_slot[e];
-            if (cs >= 0) {
-                const int64_t t = e / H, h = e - t * H;
-                ps = t < S_prev ? prev_slot[t * H + h] : -1;
-                if (ps >= 0) {
-                    if (slot_code(ps) == slot_code(cs)) copy = true;
-                    else skipped += 1;
+            ps = t < S_prev ? prev_slot[e] : -1;           // same H: entry (t, h) sits at t*H + h
+        }
+        bool copy = false;
+        if (flag && cs >= 0 && ps >= 0) {
+            if (slot_code(ps) == slot_code(cs)) copy = true;
+            else skipped += 1;
+        }
+        applied += copy ? 1 : 0;
+        const int code_l = copy ? slot_code(cs) : 0;
+        // small rows: this lane copies its own entry
+        bool wide = copy;
+        if (copy) {
+            const int64_t rb = payload_row_bytes(code_l, B, D);
+            const int64_t sf = scale_row_floats(code_l, B, D, NG);
+            const skv_bucket& cb = cur.b[code_l];
+            const skv_bucket& pb = prev.b[code_l];
+            if (rb <= kLaneRowBytes && (rb & 15) == 0 && aligned16(cb.k, cb.v, pb.k, pb.v)) {
+                wide = false;
+                const int64_t cp = slot_pos(cs), pp = slot_pos(ps);
+                // scales of up to 8 floats as 16-byte vectors, loaded with the payload
+                const bool vec = sf > 0 && (sf & 3) == 0 && sf <= 8 &&
+                                 aligned16(pb.scale_k + pp * sf, pb.scale_v + pp * sf, cb.scale_k + cp * sf,
+                                           cb.scale_v + cp * sf);
+                float4 k0 = make_float4(0.f, 0.f, 0.f, 0.f), v0 = k0, k1 = k0, v1 = k0;
+                if (vec) {
+                    const float4* ssk = reinterpret_cast<const float4*>(pb.scale_k + pp * sf);
+                    const float4* ssv = reinterpret_cast<const float4*>(pb.scale_v + pp * sf);
+                    k0 = __ldg(ssk);
+                    v0 = __ldg(ssv);
+                    if (sf > 4) {
+                        k1 = __ldg(ssk + 1);
+                        v1 = __ldg(ssv + 1);
+                    }
+                }
+                lane_copy_row(reinterpret_cast<uint8_t*>(cb.k) + cp * rb, reinterpret_cast<uint8_t*>(cb.v) + cp * rb,
+                              reinterpret_cast<const uint8_t*>(pb.k) + pp * rb,
+                              reinterpret_cast<const uint8_t*>(pb.v) + pp * rb, (int)(rb / 16));
+                if (vec) {
+                    float4* dsk = reinterpret_cast<float4*>(cb.scale_k + cp * sf);
+                    float4* dsv = reinterpret_cast<float4*>(cb.scale_v + cp * sf);
+                    dsk[0] = k0;
+                    dsv[0] = v0;
+                    if (sf > 4) {
+                        dsk[1] = k1;
+                        dsv[1] = v1;
+                    }
+                } else {
+                    for (int64_t i = 0; i < sf; ++i) {
+                        cb.scale_k[cp * sf + i] = pb.scale_k[pp * sf + i];
+                        cb.scale_v[cp * sf + i] = pb.scale_v[pp * sf + i];
+                    }
                 }
             }
         }
-        applied += copy ? 1 : 0;
+        if (!__any_sync(0xffffffffu, wide)) continue;
+        // larger rows: grouped by precision, chunks spread over the lanes
         for (int code = 0; code < kNumBuckets; ++code) {
-            const unsigned m = __ballot_sync(0xffffffffu, copy && slot_code(cs) == code);
+            const unsigned m = __ballot_sync(0xffffffffu, wide && code_l == code);
             if (!m) continue;
             const int nrows = __popc(m);
             const int64_t rb = payload_row_bytes(code, B, D);
