@@ -125,9 +125,11 @@ __device__ __forceinline__ float max_nan(float a, float b) {
 
 // q[i] = clamp(rint(fl(x[i] / s)), lo, hi) + OFF for 16 values; qf[i] = the rounded value without
 // OFF.  OFF (8 for int4 nibbles) rides in the rounding constant: the integer part of
-// y + 1.5*2^23 + OFF is rint(y) + OFF.  Values are rounded from y = x * rcp(s); if any lies within
-// 1e-4 of a half-integer (or is not finite) all 16 take the exact IEEE division.  Out-of-range
-// codes are clamped by the saturating packs that consume q.
+// y + 1.5*2^23 + OFF is rint(y) + OFF.  Values are rounded from the exact product y = x * rcp(s)
+// (one fma with the constant), and the deviation y - rint(y) comes from a second fma; if any value
+// lies within 1e-4 of a half-integer (or is not finite) all 16 take the exact IEEE division.  Away
+// from ties rint(x * rcp(s)) == rint(fl(x / s)): the two differ by far less than 1e-4 for the
+// |q| <= 128 range.  Out-of-range codes are clamped by the saturating packs that consume q.
 template <int OFF>
 __device__ __forceinline__ void quant16(const float (&x)[16], float s, float r, int lo, int hi, int (&q)[16],
                                         float (&qf)[16]) {
@@ -135,10 +137,9 @@ __device__ __forceinline__ void quant16(const float (&x)[16], float s, float r, 
     float dev = 0.0f;
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
-        const float y = __fmul_rn(x[i], r);
-        const float t = __fadd_rn(y, kM);
+        const float t = __fmaf_rn(x[i], r, kM);
         const float rf = __fsub_rn(t, kM);
-        dev = max_nan(dev, fabsf(__fsub_rn(y, rf)));
+        dev = max_nan(dev, fabsf(__fmaf_rn(x[i], r, -rf)));
         q[i] = __float_as_int(t) - 0x4B400000;
         qf[i] = rf;
     }
