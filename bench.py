@@ -820,6 +820,31 @@ def run_b200(args):
         run_pack(k, v, plan_last, 16, events=ev)
     torch.cuda.synchronize()
     pack_ms = [a.elapsed_time(b) for a, b in pev[2:]]
+    # every call of the step alone, the same way: each after two L2-flushing fills (~80 us of GPU
+    # work, during which the host enqueues the call), events around the call
+    def alone(fn, n=8):
+        evp = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n)]
+        for i, (a, b) in enumerate(evp):
+            flush.fill_(i & 0xFF)
+            flush.fill_((i + 1) & 0xFF)
+            a.record()
+            fn()
+            b.record()
+        torch.cuda.synchronize()
+        return statistics.mean(a.elapsed_time(b) for a, b in evp[2:])
+    codes_l = allocate_precision_codes(imp, "balanced")
+    sens_l = kv_sensitivity(k, v)
+    adm_l = admit_codes_device(codes_l, imp, sens_l, budget, B, D, sink, True, True)[0]
+    cache_l = PackedKVCache.pack(k, v, None, 16, plan=PrecisionPlan.from_codes(adm_l, reuse_mask=reuse))["packed_kv"]
+    kernel_ms = {
+        "allocate": alone(lambda: allocate_precision_codes(imp, "balanced")),
+        "sensitivity": alone(lambda: kv_sensitivity(k, v)),
+        "admission": alone(lambda: admit_codes_device(codes_l, imp, sens_l, budget, B, D, sink, True, True)),
+        "plan": alone(lambda: PrecisionPlan.from_codes(adm_l, reuse_mask=reuse)),
+        "pack": statistics.mean(pack_ms),
+        "reuse": alone(lambda: cache_l.apply_reuse_mask(prev, reuse)),
+        "unpack": alone(lambda: cache_l.unpack()),
+    }
     del flush
     tmax = torch.tensor([elapsed_ms], device=dev, dtype=torch.float64)
     if world > 1:
@@ -910,6 +935,13 @@ def run_b200(args):
                 "ms_per_step": e2e_ms / e2e_steps},
         "gpu_launches": launches,
         "clocks": sampler.summary() if sampler else None,
+        "kernels": {name: {"avg_ms": ms, "algorithmic_bytes": parts[name],
+                           "achieved_gbs": parts[name] / (ms / 1e3) / 1e9,
+                           "frac": parts[name] / (ms / 1e3) / 1e9 / peak}
+                    for name, ms in kernel_ms.items()},
+        "kernels_timing": "each call of the step alone through its public API, events around it, after two "
+                          "256 MB L2-flushing fills (8 calls, first 2 dropped; pack: the roofline's launches); "
+                          "frac of measured HBM",
         "attention": attn,
         "global_budget": gbudget,
         "paged_store": paged,
