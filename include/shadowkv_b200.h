@@ -137,7 +137,8 @@ int skv_unpack(const skv_bucket* buckets /* [4] */, const int32_t* slot, int B, 
                int D, int int4_group, float* k_out, float* v_out, void* stream);
 
 /* PackedKVCache.apply_reuse_mask  (shadowinfer/shadowkv/packed_kv_cache.py:753-854)
- * stats[0] = applied, stats[1] = skipped_precision (device int64[2], overwritten). */
+ * stats[0] = applied, stats[1] = skipped_precision (device int64[2], overwritten), or NULL
+ * when the counts are not wanted. */
 int skv_apply_reuse(const skv_bucket* cur /* [4] */, const int32_t* cur_slot, int S,
                     const skv_bucket* prev /* [4] */, const int32_t* prev_slot, int S_prev,
                     const uint8_t* reuse_mask, int B, int H, int D, int int4_group,

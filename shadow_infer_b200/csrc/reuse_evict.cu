@@ -194,6 +194,7 @@ __global__ void __launch_bounds__(256, 3) reuse_kernel(const __grid_constant__ B
             }
         }
     }
+    if (!stats) return;                                 // statistics not requested
     applied = warp_sum_ll(applied);
     skipped = warp_sum_ll(skipped);
     if (lane == 0) {
@@ -346,12 +347,12 @@ extern "C" {
 int skv_apply_reuse(const skv_bucket* cur, const int32_t* cur_slot, int S, const skv_bucket* prev,
                     const int32_t* prev_slot, int S_prev, const uint8_t* reuse_mask, int B, int H, int D,
                     int int4_group, int64_t* stats, void* stream) {
-    if (!cur || !prev || !cur_slot || !prev_slot || !reuse_mask || !stats)
+    if (!cur || !prev || !cur_slot || !prev_slot || !reuse_mask)
         return fail(SKV_ERR_INVALID_ARGUMENT, "apply_reuse: null pointer");
     if (B <= 0 || H <= 0 || S <= 0 || S_prev <= 0 || D <= 0)
         return fail(SKV_ERR_INVALID_ARGUMENT, "apply_reuse: bad shape");
     cudaStream_t s = as_stream(stream);
-    if (cudaMemsetAsync(stats, 0, 2 * sizeof(int64_t), s) != cudaSuccess)
+    if (stats && cudaMemsetAsync(stats, 0, 2 * sizeof(int64_t), s) != cudaSuccess)
         return fail(SKV_ERR_CUDA, "apply_reuse: memset failed");
     const int G = int4_group > 0 && D % int4_group == 0 ? int4_group : D;
     Buckets c, p;

@@ -124,17 +124,6 @@ def _alloc_bucket(code: int, n: int, B: int, D: int, G: int, dev: torch.device) 
     return out
 
 
-_DISCARD: Dict[Any, torch.Tensor] = {}
-
-
-def _discard_stats(dev: torch.device) -> torch.Tensor:
-    """Per-device int64[2] that takes reuse statistics nobody asked for (never read)."""
-    t = _DISCARD.get(dev.index)
-    if t is None:
-        t = _DISCARD[dev.index] = torch.empty(2, dtype=torch.int64, device=dev)
-    return t
-
-
 def _nbytes(t: Optional[torch.Tensor]) -> int:
     return 0 if t is None else t.numel() * t.element_size()
 
@@ -773,7 +762,7 @@ class PackedKVCache:
         mask = self._entry_mask_from_reuse(reuse_mask, dev)
         cur_arr, cur_b, direct = self._device_arr(dev)
         prev_arr, _, _ = prev._device_arr(dev)
-        stats_d = torch.empty(2, dtype=torch.int64, device=dev) if return_stats else _discard_stats(dev)
+        stats_d = torch.empty(2, dtype=torch.int64, device=dev) if return_stats else None
         lib = _lib.load()
         with device_ctx(dev):
             st = lib.skv_apply_reuse(cur_arr, _lib.ptr(self._slot), self.seq_len, prev_arr,
