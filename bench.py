@@ -845,6 +845,25 @@ def run_b200(args):
         "reuse": alone(lambda: cache_l.apply_reuse_mask(prev, reuse)),
         "unpack": alone(lambda: cache_l.unpack()),
     }
+    # evict: 25 % of the (t, h) entries (seeded Bernoulli mask) from a freshly packed copy of the
+    # layer each time; the pack is queued before the fills and is not timed
+    gen = torch.Generator(device="cpu").manual_seed(7)
+    evict_mask = (torch.rand(S, H, generator=gen) < 0.25).to(dev)
+    plan_e = PrecisionPlan.from_codes(adm_l)
+    eve = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(8)]
+    evict_after = 0
+    for i, (a, b) in enumerate(eve):
+        ce = PackedKVCache.pack(k, v, None, 16, plan=plan_e)["packed_kv"]
+        flush.fill_(i & 0xFF)
+        flush.fill_((i + 1) & 0xFF)
+        a.record()
+        ce.evict(evict_mask)
+        b.record()
+        evict_after = ce.memory_bytes()
+    torch.cuda.synchronize()
+    kernel_ms["evict"] = statistics.mean(a.elapsed_time(b) for a, b in eve[2:])
+    parts_k = dict(parts)
+    parts_k["evict"] = S * H + 2 * evict_after
     del flush
     tmax = torch.tensor([elapsed_ms], device=dev, dtype=torch.float64)
     if world > 1:
@@ -935,13 +954,15 @@ def run_b200(args):
                 "ms_per_step": e2e_ms / e2e_steps},
         "gpu_launches": launches,
         "clocks": sampler.summary() if sampler else None,
-        "kernels": {name: {"avg_ms": ms, "algorithmic_bytes": parts[name],
-                           "achieved_gbs": parts[name] / (ms / 1e3) / 1e9,
-                           "frac": parts[name] / (ms / 1e3) / 1e9 / peak}
+        "kernels": {name: {"avg_ms": ms, "algorithmic_bytes": parts_k[name],
+                           "achieved_gbs": parts_k[name] / (ms / 1e3) / 1e9,
+                           "frac": parts_k[name] / (ms / 1e3) / 1e9 / peak}
                     for name, ms in kernel_ms.items()},
         "kernels_timing": "each call of the step alone through its public API, events around it, after two "
-                          "256 MB L2-flushing fills (8 calls, first 2 dropped; pack: the roofline's launches); "
-                          "frac of measured HBM",
+                          "256 MB L2-flushing fills (8 calls, first 2 dropped; pack: the roofline's launches; "
+                          "evict: 25 % of the entries of a freshly packed copy, bytes = mask + 2 x packed bytes "
+                          "after, count + compaction with the host read of the kept counts between); frac of "
+                          "measured HBM",
         "attention": attn,
         "global_budget": gbudget,
         "paged_store": paged,

@@ -261,6 +261,41 @@ __global__ void __launch_bounds__(kEvThreads) evict_count_kernel(Buckets src, co
     }
 }
 
+// Rows of `cpr` 16-byte chunks (K and V tensors alike) of tile entries li -> new[li] (-1: not
+// kept): chunk c of the tile is chunk c % cpr of entry c / cpr; each thread takes every
+// kEvThreads-th chunk, four at a time with their loads issued first.
+__device__ __forceinline__ void copy_rows16(uint8_t* __restrict__ dk, uint8_t* __restrict__ dv,
+                                            const uint8_t* __restrict__ sk, const uint8_t* __restrict__ sv,
+                                            int cpr, int64_t first, int in_tile, const int32_t* s_new) {
+    const int total = in_tile * cpr;
+    for (int c0 = threadIdx.x; c0 < total; c0 += 4 * kEvThreads) {
+        uint4 a[4], b[4];
+        int64_t d_off[4];
+        bool ok[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int c = c0 + u * kEvThreads;
+            const int li = c < total ? c / cpr : 0;
+            const int32_t np = c < total ? s_new[li] : -1;
+            ok[u] = np >= 0;
+            d_off[u] = 0;
+            if (ok[u]) {
+                const int off = (c - li * cpr) * 16;
+                const int64_t s_off = (first + li) * (int64_t)cpr * 16 + off;
+                d_off[u] = (int64_t)np * cpr * 16 + off;
+                a[u] = __ldg(reinterpret_cast<const uint4*>(sk + s_off));
+                b[u] = __ldg(reinterpret_cast<const uint4*>(sv + s_off));
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+            if (ok[u]) {
+                *reinterpret_cast<uint4*>(dk + d_off[u]) = a[u];
+                *reinterpret_cast<uint4*>(dv + d_off[u]) = b[u];
+            }
+    }
+}
+
 __global__ void __launch_bounds__(kEvThreads) evict_compact_kernel(
     Buckets src, Buckets dst, const uint8_t* __restrict__ mask, int32_t* __restrict__ slot, int B, int S,
     int H, int D, int NG, int max_tiles, const int* __restrict__ tile_kept) {
@@ -312,22 +347,45 @@ __global__ void __launch_bounds__(kEvThreads) evict_compact_kernel(
         }
     }
     __syncthreads();
-    // move the kept rows, one warp per entry
+    // move the kept rows: the 16-byte chunks of every row of the tile are spread over the
+    // block's threads, four chunk copies in flight per thread (loads before stores)
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
     const int64_t rb = payload_row_bytes(p, B, D);
     const int64_t sf = scale_row_floats(p, B, D, NG);
-    const int64_t in_tile = count - first < kEvTile ? count - first : kEvTile;
-    for (int li = w; li < in_tile; li += kEvThreads / 32) {
-        const int32_t np = s_new[li];
-        if (np < 0) continue;
-        const int64_t op = first + li;
-        warp_copy(reinterpret_cast<uint8_t*>(dst.b[p].k) + np * rb,
-                  reinterpret_cast<const uint8_t*>(src.b[p].k) + op * rb, rb, lane);
-        warp_copy(reinterpret_cast<uint8_t*>(dst.b[p].v) + np * rb,
-                  reinterpret_cast<const uint8_t*>(src.b[p].v) + op * rb, rb, lane);
-        for (int64_t i = lane; i < sf; i += 32) {
-            dst.b[p].scale_k[np * sf + i] = src.b[p].scale_k[op * sf + i];
-            dst.b[p].scale_v[np * sf + i] = src.b[p].scale_v[op * sf + i];
+    const int in_tile = (int)(count - first < kEvTile ? count - first : kEvTile);
+    const skv_bucket& sb = src.b[p];
+    const skv_bucket& db = dst.b[p];
+    if ((rb & 15) == 0 && aligned16(sb.k, sb.v, db.k, db.v)) {
+        copy_rows16(reinterpret_cast<uint8_t*>(db.k), reinterpret_cast<uint8_t*>(db.v),
+                    reinterpret_cast<const uint8_t*>(sb.k), reinterpret_cast<const uint8_t*>(sb.v), (int)(rb / 16),
+                    first, in_tile, s_new);
+    } else {
+        for (int li = w; li < in_tile; li += kEvThreads / 32) {
+            const int32_t np = s_new[li];
+            if (np < 0) continue;
+            const int64_t op = first + li;
+            warp_copy(reinterpret_cast<uint8_t*>(db.k) + np * rb, reinterpret_cast<const uint8_t*>(sb.k) + op * rb,
+                      rb, lane);
+            warp_copy(reinterpret_cast<uint8_t*>(db.v) + np * rb, reinterpret_cast<const uint8_t*>(sb.v) + op * rb,
+                      rb, lane);
+        }
+    }
+    if (sf) {
+        if (((sf * 4) & 15) == 0 && aligned16(sb.scale_k, sb.scale_v, db.scale_k, db.scale_v)) {
+            copy_rows16(reinterpret_cast<uint8_t*>(db.scale_k), reinterpret_cast<uint8_t*>(db.scale_v),
+                        reinterpret_cast<const uint8_t*>(sb.scale_k), reinterpret_cast<const uint8_t*>(sb.scale_v),
+                        (int)(sf * 4 / 16), first, in_tile, s_new);
+        } else {
+            const int total = in_tile * (int)sf;
+            for (int e = threadIdx.x; e < total; e += kEvThreads) {
+                const int li = e / (int)sf;
+                const int32_t np = s_new[li];
+                if (np < 0) continue;
+                const int64_t i = e - (int64_t)li * sf;
+                const int64_t op = first + li;
+                db.scale_k[np * sf + i] = sb.scale_k[op * sf + i];
+                db.scale_v[np * sf + i] = sb.scale_v[op * sf + i];
+            }
         }
     }
 }
