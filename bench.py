@@ -257,16 +257,38 @@ def attention_phase(args, world, rank, dev, dist, lib, tensor_peak):
     packed_attention(qd, cache)                        # builds the head index, checks the error word
     # N > 1: the all-gather of the head-sharded outputs is fused into the attention epilogue --
     # every finished row is stored into all ranks' [B, H, S, D] buffers over NVLink
-    from shadow_infer_b200.shadowkv.sharding import PeerOutputs
-    peers = PeerOutputs((B, H, S, D), device=dev) if world > 1 else None
+    # (all ranks agree: if any rank cannot map its peers' buffers, every rank falls back to the
+    # NCCL all-gather after the kernel, so that all ranks keep taking the same collective steps)
+    from shadow_infer_b200.shadowkv.sharding import PeerOutputs, all_gather_heads
+    peers, exchange = None, "none"
+    if world > 1:
+        err = None
+        try:
+            peers = PeerOutputs((B, H, S, D), device=dev)
+        except Exception as e:          # noqa: BLE001 - reported in the line, then the fallback runs
+            err = f"{type(e).__name__}: {e}"
+        flag = torch.tensor([0 if err else 1], device=dev, dtype=torch.int32)
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+        if int(flag.item()) == 1:
+            exchange = "fused epilogue stores into every rank's buffer (CUDA IPC, NVLink)"
+        else:
+            if peers is not None:
+                dist.barrier()
+                peers.close()
+                peers = None
+            exchange = "NCCL all-gather after the kernel (peer mapping failed" + (f": {err})" if err else " on a peer)")
+    gathered = torch.empty(B, H, S, D, dtype=torch.float32, device=dev) if world > 1 and peers is None else None
     steps = max(3, min(args.steps, 32))
     kev = [tuple(torch.cuda.Event(enable_timing=True) for _ in range(3)) for _ in range(steps)]
     sms = torch.cuda.get_device_properties(dev).multi_processor_count
 
     def step(i=None):
         # events: before the staging kernel, between the two kernels, after the attention kernel
-        return packed_attention(qd, cache, check=False, events=kev[i] if i is not None else None,
-                                peer_outputs=peers, head_offset=h0)
+        out = packed_attention(qd, cache, check=False, events=kev[i] if i is not None else None,
+                               peer_outputs=peers, head_offset=h0)
+        if gathered is not None:
+            all_gather_heads(out, out=gathered)
+        return out
 
     for _ in range(3):
         step()
@@ -285,7 +307,8 @@ def attention_phase(args, world, rank, dev, dist, lib, tensor_peak):
     packed_attention(qd, cache, peer_outputs=peers, head_offset=h0)   # error word of the last launch
     if world > 1:
         dist.barrier()
-        peers.close()
+        if peers is not None:
+            peers.close()
     ms = torch.tensor([t0.elapsed_time(t1) / steps], device=dev, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(ms, op=dist.ReduceOp.MAX)
@@ -299,8 +322,8 @@ def attention_phase(args, world, rank, dev, dist, lib, tensor_peak):
     res = {
         "metric": "packed-attn tokens/s (32-layer stack, cfg3)",
         "value": B * S / (L * ms / 1e3), "unit": "tokens/s", "ms_per_layer": ms, "steps": steps,
-        "scaling": "strong (heads sharded over GPUs; outputs all-gathered by the attention epilogue's "
-                   "stores into every rank's buffer over NVLink)",
+        "scaling": "strong (heads sharded over GPUs; outputs all-gathered to every rank)",
+        "exchange": exchange,
         "attention_ctas": sms,
         "config": {"workload": "cfg3: packed K/V codes 20/50/30 fp16/int8/int4, fp16 queries, non-causal",
                    "B": B, "H": H, "S_q": S, "S_kv": S, "D": D, "layers": L, "heads_per_gpu": hs},

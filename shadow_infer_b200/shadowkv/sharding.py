@@ -130,12 +130,19 @@ class PeerOutputs:
         handle = ctypes.create_string_buffer(hb)
         offset = ctypes.c_int64(0)
         with device_ctx(dev):
-            _lib.check(lib.skv_ipc_export(_lib.ptr(self.local), handle, ctypes.byref(offset)), "PeerOutputs")
-        mine = (bytes(handle.raw), int(offset.value), int(self.local.numel()))
+            st = lib.skv_ipc_export(_lib.ptr(self.local), handle, ctypes.byref(offset))
+        # every rank takes part in the exchange, also after a failed export (it sends None), so
+        # that a failure raises on all ranks instead of leaving the others in the collective
+        mine = (bytes(handle.raw), int(offset.value), int(self.local.numel())) if st == 0 else None
+        export_error = None if st == 0 else _lib.last_error()
         entries = [None] * n
         dist.all_gather_object(entries, mine, group=group)
         self._lib = lib
         self._bases = []
+        failed = [i for i, e in enumerate(entries) if e is None]
+        if failed:
+            raise RuntimeError(f"PeerOutputs: ranks {failed} could not export their buffer"
+                               + (f" ({export_error})" if export_error else ""))
         ptrs = []
         with device_ctx(dev):
             for i, (h, off, numel) in enumerate(entries):
