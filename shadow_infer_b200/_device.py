@@ -51,9 +51,13 @@ def as_device(device: Any) -> torch.device:
 
 
 def on(t: Optional[torch.Tensor], dev: torch.device, dtype: Optional[torch.dtype] = None) -> Optional[torch.Tensor]:
-    """``t`` contiguous on ``dev`` (and ``dtype``), copying only when needed."""
+    """``t`` contiguous on ``dev`` (and ``dtype``), copying only when needed; detached from autograd
+    (the kernels read the storage only)."""
     if t is None:
         return None
+    if (dtype is None or t.dtype is dtype) and t.is_cuda and t.get_device() == dev.index and t.is_contiguous():
+        return t.detach() if t.requires_grad else t  # already what the kernel reads
+    t = t.detach()
     if dtype is not None and t.dtype != dtype:
         t = t.to(dtype)
     if t.device != dev:
@@ -63,6 +67,8 @@ def on(t: Optional[torch.Tensor], dev: torch.device, dtype: Optional[torch.dtype
 
 def back(t: torch.Tensor, device: torch.device) -> torch.Tensor:
     """Move a result to the caller's device."""
+    if isinstance(device, torch.device) and device.type == "cuda" and device.index == t.get_device():
+        return t
     return t if t.device == device else t.to(device)
 
 

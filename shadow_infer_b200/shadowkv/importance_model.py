@@ -65,11 +65,11 @@ def irap_importance(
         return empty, empty.clone(), (None if received_ema_prev is None else 0.0)
     if B == 0 or Sq == 0:
         raise ValueError("weights must have at least one batch row and one query row")
-    x = on(scores.detach(), dev, torch.float32)
+    x = on(scores, dev, torch.float32)
     prev = None
     s_prev = 0
     if received_ema_prev is not None:
-        prev = on(received_ema_prev.detach(), dev, torch.float32)
+        prev = on(received_ema_prev, dev, torch.float32)
         if prev.dim() != 2:
             raise ValueError(f"received_ema_prev must be 2-D [seq, heads], got {prev.dim()}-D")
         if prev.shape[1] != H:

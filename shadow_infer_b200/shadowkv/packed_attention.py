@@ -82,9 +82,9 @@ def packed_attention(
         # every token-head evicted: unpack() would give zero K/V, so the output is zero
         return torch.zeros(B, H, S_q, D, dtype=torch.float32, device=q.device)
     dev = c._ensure_state()
-    qd = on(q.detach(), dev, torch.float16)
-    kn = on(k_new.detach(), dev, torch.float32) if S_new else None
-    vn = on(v_new.detach(), dev, torch.float32) if S_new else None
+    qd = on(q, dev, torch.float16)
+    kn = on(k_new, dev, torch.float32) if S_new else None
+    vn = on(v_new, dev, torch.float32) if S_new else None
     rows, counts = c._head_index(dev)
     out = torch.empty(B, H, S_q, D, dtype=torch.float32, device=dev)
     err = torch.empty(1, dtype=torch.int32, device=dev)

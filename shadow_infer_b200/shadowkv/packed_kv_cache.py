@@ -225,8 +225,8 @@ def pack_slab(k: torch.Tensor, v: torch.Tensor, plan: PrecisionPlan, group_size:
     B, H, S, D = k.shape
     dev = plan.compute_device
     G = _int4_group(D, group_size)
-    kd = on(k.detach(), dev, torch.float32)
-    vd = on(v.detach(), dev, torch.float32)
+    kd = on(k, dev, torch.float32)
+    vd = on(v, dev, torch.float32)
     lib = _lib.load()
     key = (dev.index, B, H, S, D, G)
     hint = None
@@ -262,8 +262,8 @@ def pack_slab(k: torch.Tensor, v: torch.Tensor, plan: PrecisionPlan, group_size:
         dk = torch.empty(B, H, S, D, dtype=torch.float32, device=dev)
         dv = torch.empty(B, H, S, D, dtype=torch.float32, device=dev)
         if k_prev is not None and plan.reuse_mask_device is not None:
-            kp = on(k_prev.detach(), dev, torch.float32)
-            vp = on(v_prev.detach(), dev, torch.float32)
+            kp = on(k_prev, dev, torch.float32)
+            vp = on(v_prev, dev, torch.float32)
     with device_ctx(dev):
         if events is not None:
             events[0].record()

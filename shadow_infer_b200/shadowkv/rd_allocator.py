@@ -49,8 +49,8 @@ def kv_sensitivity(k: torch.Tensor, v: torch.Tensor) -> torch.Tensor:
         raise ValueError("k and v must have identical shapes")
     B, H, S, D = k.shape
     dev = compute_device(k, v)
-    kd = on(k.detach(), dev, torch.float32)
-    vd = on(v.detach(), dev, torch.float32)
+    kd = on(k, dev, torch.float32)
+    vd = on(v, dev, torch.float32)
     out = torch.empty(S, H, dtype=torch.float32, device=dev)
     lib = _lib.load()
     with device_ctx(dev):
@@ -62,7 +62,7 @@ def kv_sensitivity(k: torch.Tensor, v: torch.Tensor) -> torch.Tensor:
 def predict_codes_bytes(codes: torch.Tensor, batch: int, head_dim: int, group_size: int = 16) -> int:
     """Byte prediction of dense codes (rd_allocator.py:170-187)."""
     dev = compute_device(codes)
-    cd = on(codes.detach(), dev, torch.int8)
+    cd = on(codes, dev, torch.int8)
     out = torch.empty(1, dtype=torch.int64, device=dev)
     lib = _lib.load()
     with device_ctx(dev):
@@ -90,7 +90,7 @@ def admit_codes_device(
         raise ValueError(f"codes must be 2-D [seq, heads], got shape {tuple(codes.shape)}")
     S, H = int(codes.shape[0]), int(codes.shape[1])
     dev = compute_device(codes, importance, sensitivity)
-    cd = on(codes.detach(), dev, torch.int8)
+    cd = on(codes, dev, torch.int8)
     imp = importance.detach()
     if tuple(imp.shape) != (S, H):
         imp = imp[:S, :H]

@@ -34,7 +34,7 @@ _MODES = {"aggressive": 0, "balanced": 1, "conservative": 2}
 def allocate_precision_codes(importance_map: torch.Tensor, mode: str) -> torch.Tensor:
     """Threshold bands (float64 compares) -> ``int8 [seq, heads]`` codes (shadowkv_agent.py:1028-1059)."""
     dev = compute_device(importance_map)
-    imp = on(importance_map.detach(), dev, torch.float32)
+    imp = on(importance_map, dev, torch.float32)
     out = torch.empty(imp.shape, dtype=torch.int8, device=dev)
     lib = _lib.load()
     with device_ctx(dev):
@@ -79,9 +79,9 @@ def decide_reuse_mask(
     if tuple(importance_map.shape) != (S, H):
         raise ValueError(f"importance_map must be [seq, heads] = [{S}, {H}], got {tuple(importance_map.shape)}")
     dev = compute_device(kv_current_k, kv_current_v, kv_previous_k, kv_previous_v, importance_map)
-    kc, vc, kp, vp = (on(t.detach(), dev, torch.float32) for t in (kv_current_k, kv_current_v, kv_previous_k,
+    kc, vc, kp, vp = (on(t, dev, torch.float32) for t in (kv_current_k, kv_current_v, kv_previous_k,
                                                                    kv_previous_v))
-    imp = on(importance_map.detach(), dev, torch.float32)
+    imp = on(importance_map, dev, torch.float32)
     mask = torch.empty(S, H, dtype=torch.bool, device=dev)
     drift = torch.empty(S, H, dtype=torch.float32, device=dev) if return_drift else None
     counts = torch.empty(4, dtype=torch.int64, device=dev)
