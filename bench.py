@@ -18,7 +18,8 @@ from pinned host buffers (K, V, importance, reuse mask copied in; the packed
 payload copied out).  ``roofline`` covers the pack kernel (the dominant
 kernel), timed with CUDA events around each launch in the timed region.
 ``--impl reference`` times the CPU restatement of the reference algorithm
-(``oracle/``) on a head slice of the same workload, on rank 0 only.
+(``oracle/``) over the same layer, its heads split over one single-threaded
+worker process per host core (up to 8), on rank 0 only.
 
 The line also carries ``attention``: packed attention over one cfg3 layer
 (B=1, H=32, S=4096, D=128, codes 20/50/30 % fp16/int8/int4), heads sharded over
@@ -160,22 +161,24 @@ def step_bytes(B, H, S, D, packed_bytes, n_kept, n_reuse_rows_bytes, n_reuse):
 
 
 # ------------------------------------------------------------------------------- reference
-def reference_sample(I, heads: int):
-    """The CPU oracle pipeline on the first ``heads`` heads of the workload; returns (seconds, bytes)."""
+def reference_sample(I, heads: int, h0: int = 0):
+    """The CPU oracle pipeline on heads [h0, h0 + heads) of the workload (the budget scaled to the
+    slice); returns a callable that runs one step and returns (seconds, algorithmic bytes)."""
     import numpy as np
     from oracle import shadowkv_oracle as O
 
-    k = np.ascontiguousarray(I["k"][:, :heads].numpy())
-    v = np.ascontiguousarray(I["v"][:, :heads].numpy())
-    imp = np.ascontiguousarray(I["importance"][:, :heads].numpy())
-    reuse = np.ascontiguousarray(I["reuse"][:, :heads].numpy())
+    sl = slice(h0, h0 + heads)
+    k = np.ascontiguousarray(I["k"][:, sl].numpy())
+    v = np.ascontiguousarray(I["v"][:, sl].numpy())
+    imp = np.ascontiguousarray(I["importance"][:, sl].numpy())
+    reuse = np.ascontiguousarray(I["reuse"][:, sl].numpy())
     B, H, S, D = k.shape
     budget = I["budget"] * heads // I["k"].shape[1]
     codes0 = O.allocate_precision_codes(imp, "balanced")
     adm, _, _ = O.admit_codes(codes0, imp, O.kv_sensitivity(k, v), budget, B, D, sink_tokens=4,
                               allow_eviction=True)
-    prev = O.pack(np.ascontiguousarray(I["k_prev"][:, :heads].numpy()),
-                  np.ascontiguousarray(I["v_prev"][:, :heads].numpy()), O.plan_from_codes(adm), 16)
+    prev = O.pack(np.ascontiguousarray(I["k_prev"][:, sl].numpy()),
+                  np.ascontiguousarray(I["v_prev"][:, sl].numpy()), O.plan_from_codes(adm), 16)
 
     def run():
         t0 = time.perf_counter()
@@ -197,31 +200,72 @@ def reference_sample(I, heads: int):
     return run
 
 
+_REF_RUN = None
+
+
+def _ref_worker_init(heads: int, h0: int) -> None:
+    """Reference-arm worker: one thread, its own copy of the cfg2 inputs, one head slice."""
+    global _REF_RUN
+    import torch
+    torch.set_num_threads(1)
+    from shadow_infer_b200 import workloads as W
+    I = W.cfg2_inputs()
+    _REF_RUN = reference_sample(I, heads, h0)
+    del I
+
+
+def _ref_worker_step(_):
+    return _REF_RUN()
+
+
 def run_reference(args):
+    """The CPU restatement of the reference path over the whole cfg2 layer, its heads split over
+    one single-threaded worker process per host core (up to 8, heads dividing evenly); a step is
+    every worker's pass over its slice, timed on the wall clock around all of them."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
+    import multiprocessing as mp
     from shadow_infer_b200 import workloads as W
 
-    I = W.cfg2_inputs()
-    run = reference_sample(I, args.ref_heads)
-    for _ in range(args.warmup):
-        run()
-    times, nbytes = [], 0
-    for _ in range(args.steps):
-        dt, nbytes = run()
-        times.append(dt)
+    H = W.CONFIGS["cfg2"]["H"]
+    workers = 1
+    for w in (8, 4, 2, 1):
+        if w <= (os.cpu_count() or 1) and H % w == 0:
+            workers = w
+            break
+    heads = H // workers
+    for var in ("OMP_NUM_THREADS", "OPENBLAS_NUM_THREADS", "MKL_NUM_THREADS"):
+        os.environ[var] = "1"           # inherited by the workers: one thread each
+    ctx = mp.get_context("spawn")
+    # one single-process pool per slice, so that each worker's initializer builds its own slice
+    pools = [ctx.Pool(1, initializer=_ref_worker_init, initargs=(heads, i * heads)) for i in range(workers)]
+    try:
+        def step():
+            t0 = time.perf_counter()
+            res = [p.apply_async(_ref_worker_step, (0,)) for p in pools]
+            out = [r.get() for r in res]
+            return time.perf_counter() - t0, sum(b for _, b in out)
+        for _ in range(max(args.warmup, 1)):
+            step()
+        times, nbytes = [], 0
+        for _ in range(args.steps):
+            dt, nbytes = step()
+            times.append(dt)
+    finally:
+        for p in pools:
+            p.close()
+            p.join()
     total = sum(times)
     value = nbytes * args.steps / total / 1e9
-    sample = (f"CPU oracle (numpy restatement of the reference path) on heads 0..{args.ref_heads - 1} of cfg2 "
-              f"(B1 S8192 D128), per step")
+    sample = (f"CPU oracle (numpy restatement of the reference path) on the whole cfg2 layer (B1 H{H} S8192 "
+              f"D128), {workers} single-threaded worker processes of {heads} heads each, per step")
     line = {
         "metric": METRIC, "value": value, "unit": "GB/s", "impl": "reference", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * total / args.steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "cfg2 data-plane step (head slice)", "B": 1, "H": args.ref_heads, "S": 8192,
-                   "D": 128},
-        "cpu_baseline": {"value": value, "unit": "GB/s", "cores": 1, "kind": "port", "sample": sample},
+        "config": {"workload": "cfg2 data-plane step", "B": 1, "H": H, "S": 8192, "D": 128},
+        "cpu_baseline": {"value": value, "unit": "GB/s", "cores": workers, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
