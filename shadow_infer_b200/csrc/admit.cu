@@ -49,13 +49,9 @@ __global__ void __launch_bounds__(256) sensitivity_kernel(const float* __restric
 // D == 128: grid x over token chunks (8 warps * RPW rows), y over heads; each warp keeps
 // 2*RPW 128-bit loads in flight per batch.
 template <int RPW>
-__global__ void __launch_bounds__(256) sensitivity_d128_kernel(const float* __restrict__ k,
-                                                               const float* __restrict__ v, int B, int H,
-                                                               int S, float* __restrict__ sens) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int h = blockIdx.y;
-    const int t0 = (blockIdx.x * 8 + warp) * RPW;
-    if (t0 >= S) return;
+__device__ __forceinline__ void sensitivity_d128_rows(const float* __restrict__ k, const float* __restrict__ v,
+                                                      int B, int H, int S, int h, int t0, int lane,
+                                                      float* __restrict__ sens) {
     float mk[RPW], mv[RPW];
 #pragma unroll
     for (int i = 0; i < RPW; ++i) mk[i] = mv[i] = 0.0f;
@@ -83,6 +79,22 @@ __global__ void __launch_bounds__(256) sensitivity_d128_kernel(const float* __re
         const float c = warp_max(mv[i]);
         if (lane == i && t0 + i < S)
             sens[(int64_t)(t0 + i) * H + h] = __fdiv_rn(__fadd_rn(__fmul_rn(a, a), __fmul_rn(c, c)), 2.0f);
+    }
+}
+
+// Resident grid (a whole number of blocks per SM) walking the (head, 32-row chunk) items in
+// head-major order, so that consecutive items read consecutive memory; 8 warps x RPW rows each.
+template <int RPW>
+__global__ void __launch_bounds__(256) sensitivity_d128_kernel(const float* __restrict__ k,
+                                                               const float* __restrict__ v, int B, int H,
+                                                               int S, float* __restrict__ sens) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int nchunks = (S + 8 * RPW - 1) / (8 * RPW);
+    const long long items = (long long)H * nchunks;
+    for (long long it = blockIdx.x; it < items; it += gridDim.x) {
+        const int h = (int)(it / nchunks);
+        const int t0 = ((int)(it - (long long)h * nchunks) * 8 + warp) * RPW;
+        if (t0 < S) sensitivity_d128_rows<RPW>(k, v, B, H, S, h, t0, lane, sens);
     }
 }
 
@@ -481,7 +493,13 @@ int skv_kv_sensitivity(const float* k, const float* v, int B, int H, int S, int 
     if (B <= 0 || H <= 0 || S <= 0 || D <= 0) return fail(SKV_ERR_INVALID_ARGUMENT, "kv_sensitivity: bad shape");
     if (D == 128 && ((reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v)) & 15) == 0) {
         constexpr int kRPW = 4;
-        const dim3 grid((unsigned)((S + 8 * kRPW - 1) / (8 * kRPW)), (unsigned)H);
+        const long long items = (long long)H * ((S + 8 * kRPW - 1) / (8 * kRPW));
+        static int per_sm = 0;          // resident blocks per SM (same on every B200 of the process)
+        if (per_sm == 0 && (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, sensitivity_d128_kernel<kRPW>,
+                                                                           256, 0) != cudaSuccess || per_sm < 1))
+            per_sm = 4;
+        const long long resident = (long long)sm_count() * per_sm;
+        const int grid = (int)(items < resident ? items : resident);
         sensitivity_d128_kernel<kRPW><<<grid, 256, 0, as_stream(stream)>>>(k, v, B, H, S, sensitivity);
         return check_launch("kv_sensitivity");
     }

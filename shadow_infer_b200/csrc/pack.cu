@@ -461,7 +461,7 @@ __device__ __forceinline__ void unpack_lane(int code, int64_t pos, int b, int B,
 }
 
 template <int LPR>
-__global__ void __launch_bounds__(256, 4) unpack16_kernel(Buckets bk, const int32_t* __restrict__ slot, int B, int H,
+__global__ void __launch_bounds__(256, 5) unpack16_kernel(Buckets bk, const int32_t* __restrict__ slot, int B, int H,
                                                           int S, int G, float* __restrict__ k_out,
                                                           float* __restrict__ v_out) {
     constexpr int D = LPR * 16;
@@ -470,26 +470,34 @@ __global__ void __launch_bounds__(256, 4) unpack16_kernel(Buckets bk, const int3
     __shared__ float4 s_stage[8][kStageF4];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int l = lane % LPR, rsub = lane / LPR;
-    const int bh = blockIdx.x;
-    const int h = bh % H, b = bh / H;
-    const int t0 = (blockIdx.y * 8 + warp) * RPW;
-    if (t0 >= S) return;
-    const int rows = min(RPW, S - t0);
-    const int t = t0 + rsub;
-    const bool active = rsub < rows;
-    const int32_t sl = active ? slot[(int64_t)t * H + h] : -1;
-    const int code = sl < 0 ? kCodeEvicted : slot_code(sl);
-    const int64_t pos = sl < 0 ? 0 : slot_pos(sl);
-    const int64_t base = ((int64_t)bh * S + t0) * D;
-    float4* st = s_stage[warp];
+    // resident grid: each block walks (token chunk, b*h) items, b*h fastest -- the items in flight
+    // cover every head of the same token range, whose bucket rows (token-major) are contiguous
+    // (the host keeps the item count below 2^31)
+    const int BH = B * H;
+    const int items = BH * ((S + 8 * RPW - 1) / (8 * RPW));
+    for (int it = blockIdx.x; it < items; it += gridDim.x) {
+        const int bh = it % BH;
+        const int h = bh % H, b = bh / H;
+        const int t0 = ((it / BH) * 8 + warp) * RPW;
+        if (t0 >= S) continue;
+        const int rows = min(RPW, S - t0);
+        const int t = t0 + rsub;
+        const bool active = rsub < rows;
+        const int32_t sl = active ? slot[(int64_t)t * H + h] : -1;
+        const int code = sl < 0 ? kCodeEvicted : slot_code(sl);
+        const int64_t pos = sl < 0 ? 0 : slot_pos(sl);
+        const int64_t base = ((int64_t)bh * S + t0) * D;
+        float4* st = s_stage[warp];
 #pragma unroll 1
-    for (int tensor = 0; tensor < 2; ++tensor) {
-        float y[16];
-        unpack_lane<LPR>(code, pos, b, B, G, bk.b[code < kCodeEvicted ? code : 0], tensor == 1, y, l);
-        if (tensor) __syncwarp();        // the K rows have left the staging buffer
-        if (active) stage_put<D>(st, rsub, l, y);
-        __syncwarp();
-        stage_out<D, RPW>(st, (tensor ? v_out : k_out) + base, rows, lane);
+        for (int tensor = 0; tensor < 2; ++tensor) {
+            float y[16];
+            unpack_lane<LPR>(code, pos, b, B, G, bk.b[code < kCodeEvicted ? code : 0], tensor == 1, y, l);
+            if (tensor) __syncwarp();        // the K rows have left the staging buffer
+            if (active) stage_put<D>(st, rsub, l, y);
+            __syncwarp();
+            stage_out<D, RPW>(st, (tensor ? v_out : k_out) + base, rows, lane);
+        }
+        __syncwarp();        // the next item rewrites this warp's staging buffer
     }
 }
 
@@ -563,6 +571,26 @@ static bool buckets_aligned(const skv_bucket* bk) {
 static dim3 grid_rows(int B, int H, int S, int lpr) {
     const int rows_per_block = 8 * (32 / lpr);
     return dim3((unsigned)(B * H), (unsigned)((S + rows_per_block - 1) / rows_per_block));
+}
+
+// Resident blocks per SM of a 256-thread kernel (the launch-time occupancy).
+template <typename Kernel>
+static int resident_per_sm(Kernel kernel) {
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, 256, 0) != cudaSuccess || n < 1) n = 1;
+    return n;
+}
+
+// Grid of the unpack kernels: one resident wave (per_sm blocks on every SM), each block walking
+// its share of the (token chunk, b*h) items -- no block launch per 32-row chunk, no tail wave
+// (63 -> 58 us on the cfg2 layer).  Pack keeps one block per chunk: its blocks hold 32 KB of
+// staging and 64 registers per thread (4 per SM), and a block that walks items serialises their
+// load latency (66 -> 70 us when looped).
+static dim3 grid_items(int B, int H, int S, int lpr, int per_sm) {
+    const int rows_per_block = 8 * (32 / lpr);
+    const long long items = (long long)B * H * ((S + rows_per_block - 1) / rows_per_block);
+    const long long resident = (long long)sm_count() * per_sm;
+    return dim3((unsigned)(items < resident ? items : resident));
 }
 
 // Bucket layout of one allocation ("slab"), the same arithmetic on host and device: per
@@ -725,11 +753,17 @@ int skv_unpack(const skv_bucket* buckets, const int32_t* slot, int B, int H, int
     for (int p = 0; p < kNumBuckets; ++p) bk.b[p] = buckets[p];
     cudaStream_t s = as_stream(stream);
     const bool aligned = is_aligned16(k_out) && is_aligned16(v_out) && buckets_aligned(buckets);
-    switch (aligned ? fast_lpr(D, G) : 0) {
-        case 4: unpack16_kernel<4><<<grid_rows(B, H, S, 4), 256, 0, s>>>(bk, slot, B, H, S, G, k_out, v_out); break;
-        case 8: unpack16_kernel<8><<<grid_rows(B, H, S, 8), 256, 0, s>>>(bk, slot, B, H, S, G, k_out, v_out); break;
+    const bool items_ok = (long long)B * H * ((S + 15) / 16) < (1ll << 31);   // 32-bit item index
+    switch (aligned && items_ok ? fast_lpr(D, G) : 0) {
+#define SKV_UNPACK16(L)                                                                                     \
+    do {                                                                                                    \
+        static const int per_sm = resident_per_sm(unpack16_kernel<L>);                                     \
+        unpack16_kernel<L><<<grid_items(B, H, S, L, per_sm), 256, 0, s>>>(bk, slot, B, H, S, G, k_out, v_out); \
+    } while (0)
+        case 4: SKV_UNPACK16(4); break;
+        case 8: SKV_UNPACK16(8); break;
         case 16:
-            unpack16_kernel<16><<<grid_rows(B, H, S, 16), 256, 0, s>>>(bk, slot, B, H, S, G, k_out, v_out);
+            SKV_UNPACK16(16);
             break;
         default: {
             const int64_t total = (int64_t)B * H * S * D;
@@ -738,6 +772,7 @@ int skv_unpack(const skv_bucket* buckets, const int32_t* slot, int B, int H, int
             unpack_generic_kernel<<<blocks, 256, 0, s>>>(bk, slot, B, H, S, D, G, k_out, v_out);
         }
     }
+#undef SKV_UNPACK16
     return check_launch("unpack");
 }
 
