@@ -995,6 +995,7 @@ def run_b200(args):
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record(cs)
+    s_in.wait_event(e0)                            # no copy of the timed steps starts before e0
     d2h = 0
     for _ in range(e2e_steps):
         d2h = e2e_step()
