@@ -635,9 +635,17 @@ class PackedKVCache:
         ``token_head_set``: set of ``(t, h)`` or a bool ``[S, H]`` mask.  Returns
         the number of entries removed; buckets that become empty are deleted.
         """
-        if token_head_set is None or not self.packed_data:
+        if token_head_set is None:
             return 0
         if not torch.is_tensor(token_head_set) and not token_head_set:
+            return 0
+        if self._pending is not None:
+            if not self._count:
+                return 0
+            removed = self._evict_pending(token_head_set)
+            if removed is not None:
+                return removed
+        if not self.packed_data:
             return 0
         dev = self._ensure_state()
         mask = self._entry_mask(token_head_set, dev)
@@ -702,6 +710,49 @@ class PackedKVCache:
                 data.set_lazy("byte_offsets", self._offsets_fn(p))
         self._memory_bytes = self._compute_data_bytes()
         return removed
+
+    def _evict_pending(self, token_head_set: Any) -> Optional[int]:
+        """``evict`` of a cache whose ``packed_data`` views are not made yet: the pack's own bucket
+        array is the source and the survivors are installed directly, so the views of the buckets
+        being replaced are never built.  Returns None (nothing changed) when a stored bucket loses
+        no entry -- the general path then keeps that bucket as it is."""
+        dev = self._dev
+        slab, layout, counts, plan, group_size = self._pending
+        src_arr = self._arr_cache[2]
+        mask = self._entry_mask(token_head_set, dev)
+        lib = _lib.load()
+        scr = scratch(lib.skv_evict_scratch_bytes(max(counts[:4])), dev)
+        kept_d = torch.empty(5, dtype=torch.int64, device=dev)
+        stream = _lib.stream_of(dev)
+        with device_ctx(dev):
+            st = lib.skv_evict_count(src_arr, _lib.ptr(mask), self.seq_len, self.num_heads, _lib.ptr(kept_d),
+                                     _lib.ptr(scr), scr.numel(), stream)
+        _lib.check(st, "PackedKVCache.evict")
+        kept = kept_d.tolist()
+        if kept[4] == 0:
+            return 0
+        if any(0 < kept[c] == counts[c] for c in range(4)):
+            return None
+        if not self._slot_owned:
+            self._slot = self._slot.clone()
+            self._slot_owned = True
+        G = _int4_group(self.head_dim, group_size)
+        dst: List[Optional[Dict[str, Any]]] = []
+        for code in range(4):
+            if counts[code] == 0 or kept[code] == 0:
+                dst.append(None)
+                continue
+            nb = _alloc_bucket(code, kept[code], self.batch_size, self.head_dim, G, dev)
+            nb["flat"] = torch.empty(kept[code], dtype=torch.int64, device=dev)
+            nb["count"] = kept[code]
+            dst.append(nb)
+        with device_ctx(dev):
+            st = lib.skv_evict_compact(src_arr, _lib.buckets(dst), _lib.ptr(mask), _lib.ptr(self._slot),
+                                       self.batch_size, self.seq_len, self.num_heads, self.head_dim, G,
+                                       _lib.ptr(scr), scr.numel(), stream)
+        _lib.check(st, "PackedKVCache.evict")
+        self._adopt(dst, self._slot, shared_slot=False, group_size=group_size)
+        return kept[4]
 
     def _entry_mask(self, entries: Any, dev: torch.device) -> torch.Tensor:
         S, H = self.seq_len, self.num_heads
