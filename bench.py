@@ -3,40 +3,43 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
 
-One STEP is one pass of the data plane over one layer of the cfg2 workload
-(B=1, H=32, S=8192, D=128 fp32 K/V, inputs resident in HBM):
+One STEP is one layer of the long-context workload (cfg5: B=1, H=32, S=32768, D=128, fp32 K/V
+with 1 % x8 outliers and 4 outlier channels x10 per head in K, codes 10/30/60 % fp16/int8/int4,
+fp16 queries), through the packed-KV path, inputs resident in HBM:
 
-    allocate_precision_codes -> kv_sensitivity -> admit_codes (30 % fp16 budget,
-    hard eviction, 4 sink tokens) -> PrecisionPlan.from_codes (50 % reuse mask)
-    -> PackedKVCache.pack -> apply_reuse_mask (previous step's cache) -> unpack
+    allocate_precision_codes -> PrecisionPlan.from_codes -> PackedKVCache.pack (compress+pack)
+    -> unpack -> packed_attention (non-causal, scale 1/sqrt(128), read from the packed buckets)
 
-``value`` is algorithmic bytes per step / device time (GB/s).  With N GPUs
-(torchrun) every rank packs its own layer (layers are independent objects, so
-there is no collective on the data path): weak scaling, value = N layers'
-bytes / max-over-ranks time.  ``e2e`` is the same step through the public API
-from pinned host buffers (K, V, importance, reuse mask copied in; the packed
-payload copied out).  ``roofline`` covers the pack kernel (the dominant
-kernel), timed with CUDA events around each launch in the timed region.
-``--impl reference`` times the CPU restatement of the reference algorithm
-(``oracle/``) over the same layer, its heads split over one single-threaded
-worker process per host core (up to 8), on rank 0 only.
+With N GPUs (torchrun) the layer's heads are sharded: rank g owns heads [g*32/N, (g+1)*32/N),
+packs, unpacks and attends over them, and the attention epilogue stores every finished output
+row into all ranks' [B, H, S, D] buffers (CUDA IPC mappings over NVLink), so every rank ends the
+step holding the whole layer's output (a one-element NCCL all-reduce after the kernel marks that
+point).  Strong scaling: the job is one layer per step at every N.  ``value`` = tokens/s of the
+32-layer stack = B*S / (32 * max-over-ranks step time).  ``roofline`` is the attention kernel
+(tensor-bound, CUDA events around each launch in the timed region); ``data_plane`` gives the
+compress+pack and unpack GB/s of the layer with their HBM rooflines; ``check`` compares the
+gathered output of every rank with the oracle on sampled rows of sampled heads and with the
+single-GPU call on the rank's own heads.  ``e2e`` is the same step from pinned host K, V,
+importance and queries, with this rank's heads of the output read back.
 
-The line also carries ``attention``: packed attention over one cfg3 layer
-(B=1, H=32, S=4096, D=128, codes 20/50/30 % fp16/int8/int4), heads sharded over
-the ranks, the outputs all-gathered by the kernel's own stores into every rank's
-buffer (CUDA IPC mappings, NVLink), as tokens/s of the 32-layer
-stack and as tensor-core roofline of the kernel; ``global_budget``:
-KVCacheManager.enforce_global_budget over 8 packed layers of that shape;
-``paged_store``: the PagedKVStore append-mode run of the reference's own paged
-benchmark shape plus its gather / append kernels at the cfg2 layer shape; and
-``decisions``: decide_reuse_per_token over the cfg2 layer and
-compute_irap_importance over cfg3-shaped attention probabilities.
+Sub-objects: ``cfg2_step`` (the budget data plane: codes, sensitivity, budget admission with hard
+eviction -- an all-gather of the [S, H/N] inputs and the same admission on every rank at N > 1 --
+plan, pack, reuse, unpack, heads sharded), ``attention_cfg3`` (one 4096-token layer), ``denoise_cfg4``
+(the batched denoising loop: B=8, S=2048, 32 layers x 16 steps of drift, reuse decision, re-pack,
+reuse, eviction of the 25 % lowest-importance entries and attention, heads sharded), and at N=1
+``global_budget``, ``paged_store`` and ``decisions``.
+
+``--impl reference`` times the CPU restatement of the reference path (``oracle/``) on the same
+step: each of up to 32 single-threaded worker processes (one per host core) packs, unpacks and
+attends one head (attention on a bounded sample of query rows), and the layer time is
+extrapolated from the sample; rank 0 only.
 """
 
 from __future__ import annotations
 
 import argparse
 import json
+import math
 import os
 import statistics
 import subprocess
@@ -49,31 +52,48 @@ sys.path.insert(0, REPO)
 
 METRIC = "packed-KV GB/s (compress+pack, unpack) & packed-attn tokens/s at 1/2/4/8 B200, % roofline"
 FALLBACK_HBM_GBS = 6650.0
+FALLBACK_TFLOPS = 1590.0
+STACK_LAYERS = 32          # tokens/s are quoted for the 32-layer stack of the 7B-shaped model
 
 
 def parse_args():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
-    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
-    ap.add_argument("--ref-heads", type=int, default=8, help="head slice timed by the CPU reference arm")
-    ap.add_argument("--no-attention", action="store_true",
-                    help="skip the packed-attention, global-budget and paged-store phases")
-    ap.add_argument("--phase", choices=("all", "paged", "paged-kernels", "decisions"), default="all",
-                    help="'paged' / 'paged-kernels' / 'decisions': print only that phase (the paged store, its "
-                         "kernels at the cfg2 shape, the decision inputs) as the JSON line; for profiling")
+    ap.add_argument("--ref-rows", type=int, default=128, help="query rows per head timed by the CPU reference")
+    ap.add_argument("--no-extras", action="store_true", help="the headline step only (no sub-objects)")
+    ap.add_argument("--phase", choices=("all", "long-slice", "cfg2", "paged", "paged-kernels", "decisions"),
+                    default="all",
+                    help="print only that phase as the JSON line (for profiling): 'long-slice' = the step on a "
+                         "4-head slice of the long-context layer (one GPU's share at N=8), 'cfg2' = the budget "
+                         "data-plane step, 'paged' / 'paged-kernels' / 'decisions' as named")
     return ap.parse_args()
 
 
 # ----------------------------------------------------------------------------------- peaks
-def hbm_peak():
-    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+def _peaks():
     try:
-        with open(path) as f:
-            return float(json.load(f)["hbm_gbs"]), "measured"
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+            return json.load(f)
     except Exception:
-        return FALLBACK_HBM_GBS, "fallback"
+        return None
+
+
+def hbm_peak():
+    p = _peaks()
+    if p and "hbm_gbs" in p:
+        return float(p["hbm_gbs"]), "measured"
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+def tensor_peaks():
+    """(burst, sustained, source) dense bf16 TFLOP/s (fp16 runs at the same rate)."""
+    p = _peaks()
+    if p and "bf16_tflops" in p:
+        return float(p["bf16_tflops"]), float(p.get("bf16_tflops_sustained", p["bf16_tflops"])), "measured"
+    return FALLBACK_TFLOPS, 1400.0, "fallback"
 
 
 def committed_traffic(name: str):
@@ -143,147 +163,678 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(self.rows)}
 
 
-# ------------------------------------------------------------------------- algorithmic bytes
-def step_bytes(B, H, S, D, packed_bytes, n_kept, n_reuse_rows_bytes, n_reuse):
-    """Algorithmic HBM bytes of one data-plane step, per kernel."""
-    N = S * H
-    fp32 = 2 * B * H * S * D * 4
-    parts = {
-        "allocate": 4 * N + N,
-        "sensitivity": fp32 + 4 * N,
-        "admission": 9 * N + 4 * N,
-        "plan": N + N + 8 * N + 4 * N + 8 * n_reuse,
-        "pack": fp32 + N + packed_bytes + 8 * n_kept,
-        "reuse": N + 2 * n_reuse_rows_bytes,
-        "unpack": packed_bytes + 8 * n_kept + fp32,
-    }
-    return parts
-
-
 # ------------------------------------------------------------------------------- reference
-def reference_sample(I, heads: int, h0: int = 0):
-    """The CPU oracle pipeline on heads [h0, h0 + heads) of the workload (the budget scaled to the
-    slice); returns a callable that runs one step and returns (seconds, algorithmic bytes)."""
+def long_context_sample(h: int, rows_n: int):
+    """The CPU oracle (numpy restatement of the reference path) on head ``h`` of the long-context
+    layer; returns a callable that runs one pass and returns (seconds of codes + plan + pack +
+    unpack of the head, seconds of the attention of ``rows_n`` sampled query rows over it)."""
     import numpy as np
     from oracle import shadowkv_oracle as O
+    from shadow_infer_b200 import workloads as W
 
-    sl = slice(h0, h0 + heads)
-    k = np.ascontiguousarray(I["k"][:, sl].numpy())
-    v = np.ascontiguousarray(I["v"][:, sl].numpy())
-    imp = np.ascontiguousarray(I["importance"][:, sl].numpy())
-    reuse = np.ascontiguousarray(I["reuse"][:, sl].numpy())
-    B, H, S, D = k.shape
-    budget = I["budget"] * heads // I["k"].shape[1]
-    codes0 = O.allocate_precision_codes(imp, "balanced")
-    adm, _, _ = O.admit_codes(codes0, imp, O.kv_sensitivity(k, v), budget, B, D, sink_tokens=4,
-                              allow_eviction=True)
-    prev = O.pack(np.ascontiguousarray(I["k_prev"][:, sl].numpy()),
-                  np.ascontiguousarray(I["v_prev"][:, sl].numpy()), O.plan_from_codes(adm), 16)
+    L = W.cfg5_layer(h, h + 1)
+    k, v = L["k"].numpy(), L["v"].numpy()
+    imp = np.ascontiguousarray(L["importance"][:, h:h + 1].numpy())
+    rows = W.sample_rows(k.shape[2], rows_n, h).numpy()
+    q = np.ascontiguousarray(L["q"][:, :, rows].float().numpy())
 
     def run():
         t0 = time.perf_counter()
         codes = O.allocate_precision_codes(imp, "balanced")
-        sens = O.kv_sensitivity(k, v)
-        a, _, _ = O.admit_codes(codes, imp, sens, budget, B, D, sink_tokens=4, allow_eviction=True)
-        plan = O.plan_from_codes(a, reuse)
-        cache = O.pack(k, v, plan, 16)
-        st = O.apply_reuse_mask(cache, prev, reuse)
-        O.unpack(cache)
-        dt = time.perf_counter() - t0
-        kept = sum(len(d["indices"]) for d in cache.packed_data.values())
-        flagged = reuse & (a < 4)   # previous cache holds the same codes: every flagged entry is copied
-        assert st["applied"] == int(flagged.sum())
-        reuse_bytes = int(O.code_costs(B, D, 16)[a[flagged].astype(np.int64)].sum())
-        parts = step_bytes(B, H, S, D, cache.memory_bytes(), kept, reuse_bytes, int(reuse.sum()))
-        return dt, sum(parts.values())
+        cache = O.pack(k, v, O.plan_from_codes(codes), 16)
+        ku, vu = O.unpack(cache)
+        t1 = time.perf_counter()
+        O.attention(q, ku, vu)
+        return t1 - t0, time.perf_counter() - t1
 
-    return run
+    return run, len(rows)
+
+
+def long_context_cpu_rate(t_pu: float, t_attn: float, rows: int, heads_per_worker: int) -> float:
+    """tokens/s of the 32-layer stack from one head's sample: the layer takes ``heads_per_worker``
+    heads' worth of (pack + unpack + attention of all S query rows), attention scaled from the
+    sampled rows (every query row costs the same in non-causal attention)."""
+    from shadow_infer_b200 import workloads as W
+    c = W.CONFIGS["cfg5"]
+    t_layer = heads_per_worker * (t_pu + t_attn * c["S"] / rows)
+    return c["B"] * c["S"] / (STACK_LAYERS * t_layer)
 
 
 _REF_RUN = None
 
 
-def _ref_worker_init(heads: int, h0: int) -> None:
-    """Reference-arm worker: one thread, its own copy of the cfg2 inputs, one head slice."""
+def _ref_worker_init(h: int, rows_n: int) -> None:
+    """Reference-arm worker: one thread, its own head of the long-context layer."""
     global _REF_RUN
     import torch
     torch.set_num_threads(1)
-    from shadow_infer_b200 import workloads as W
-    I = W.cfg2_inputs()
-    _REF_RUN = reference_sample(I, heads, h0)
-    del I
+    _REF_RUN = long_context_sample(h, rows_n)
 
 
 def _ref_worker_step(_):
-    return _REF_RUN()
+    run, rows = _REF_RUN
+    t_pu, t_attn = run()
+    return t_pu, t_attn, rows
 
 
 def run_reference(args):
-    """The CPU restatement of the reference path over the whole cfg2 layer, its heads split over
-    one single-threaded worker process per host core (up to 8, heads dividing evenly); a step is
-    every worker's pass over its slice, timed on the wall clock around all of them."""
+    """The CPU restatement of the reference path over the long-context layer: one single-threaded
+    worker process per host core (up to one per head), each packing, unpacking and attending its
+    own head (attention of a bounded sample of query rows); a step is every worker's pass, and
+    the layer time is the slowest worker's time scaled to all query rows and to the heads each
+    worker would take."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
     import multiprocessing as mp
     from shadow_infer_b200 import workloads as W
 
-    H = W.CONFIGS["cfg2"]["H"]
-    workers = 1
-    for w in (8, 4, 2, 1):
-        if w <= (os.cpu_count() or 1) and H % w == 0:
-            workers = w
-            break
-    heads = H // workers
+    c = W.CONFIGS["cfg5"]
+    H = c["H"]
+    workers = max(1, min(os.cpu_count() or 1, H))
+    per_worker = -(-H // workers)
     for var in ("OMP_NUM_THREADS", "OPENBLAS_NUM_THREADS", "MKL_NUM_THREADS"):
         os.environ[var] = "1"           # inherited by the workers: one thread each
     ctx = mp.get_context("spawn")
-    # one single-process pool per slice, so that each worker's initializer builds its own slice
-    pools = [ctx.Pool(1, initializer=_ref_worker_init, initargs=(heads, i * heads)) for i in range(workers)]
+    pools = [ctx.Pool(1, initializer=_ref_worker_init, initargs=(h, args.ref_rows)) for h in range(workers)]
     try:
         def step():
             t0 = time.perf_counter()
             res = [p.apply_async(_ref_worker_step, (0,)) for p in pools]
             out = [r.get() for r in res]
-            return time.perf_counter() - t0, sum(b for _, b in out)
+            return time.perf_counter() - t0, out
         for _ in range(max(args.warmup, 1)):
             step()
-        times, nbytes = [], 0
+        rates, walls, rows = [], [], 0
         for _ in range(args.steps):
-            dt, nbytes = step()
-            times.append(dt)
+            wall, out = step()
+            t_pu = max(o[0] for o in out)
+            t_attn = max(o[1] for o in out)
+            rows = out[0][2]
+            rates.append(long_context_cpu_rate(t_pu, t_attn, rows, per_worker))
+            walls.append(wall)
     finally:
         for p in pools:
             p.close()
             p.join()
-    total = sum(times)
-    value = nbytes * args.steps / total / 1e9
-    sample = (f"CPU oracle (numpy restatement of the reference path) on the whole cfg2 layer (B1 H{H} S8192 "
-              f"D128), {workers} single-threaded worker processes of {heads} heads each, per step")
+    value = statistics.median(rates)
+    t_layer = c["B"] * c["S"] / (STACK_LAYERS * value)
+    sample = (f"CPU oracle (numpy restatement of the reference path) on the long-context layer: {workers} "
+              f"single-threaded worker processes, each on its own head: codes + plan + pack + unpack of the whole "
+              f"head (32768 tokens) and float64 attention of {rows} sampled query rows over it; layer time = "
+              f"{per_worker} head(s) per worker x (pack/unpack + attention scaled to all 32768 rows), slowest "
+              f"worker, median over steps; tokens/s of the 32-layer stack")
     line = {
-        "metric": METRIC, "value": value, "unit": "GB/s", "impl": "reference", "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * total / args.steps,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "cfg2 data-plane step", "B": 1, "H": H, "S": 8192, "D": 128},
-        "cpu_baseline": {"value": value, "unit": "GB/s", "cores": workers, "kind": "port", "sample": sample},
-        "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "metric": METRIC, "value": value, "unit": "tokens/s", "impl": "reference", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * t_layer,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": long_context_config(),
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": workers, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "sample_wall_s_per_step": statistics.median(walls),
     }
     print(json.dumps(line), flush=True)
     return 0
 
 
-# ------------------------------------------------------------------------------- attention
-def attention_phase(args, world, rank, dev, dist, lib, tensor_peak):
-    """Packed attention on one cfg3 layer, heads sharded over ranks, outputs all-gathered.
+# ------------------------------------------------------------------------------- helpers
+def rel_l2(a, b) -> float:
+    import numpy as np
+    a = np.asarray(a, dtype=np.float64)
+    b = np.asarray(b, dtype=np.float64)
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
 
-    One step = the layer's attention over this rank's heads; with N > 1 its epilogue stores
-    every output row into all ranks' fp32 [B, H, S, D] buffers (CUDA IPC mappings over NVLink),
-    so the all-gather runs inside the kernel, overlapped with the attention math.
-    """
+
+def make_peers(world, dev, dist, shape, count=1):
+    """``count`` PeerOutputs of ``shape`` (every rank's fp32 buffer mapped into all ranks), or
+    (None, reason) on every rank if any rank cannot map its peers' buffers -- the ranks agree
+    through a MIN all-reduce so that all of them keep taking the same collective steps."""
+    import torch
+    from shadow_infer_b200.shadowkv.sharding import PeerOutputs
+    if world == 1:
+        return None, "none"
+    bufs, err = [], None
+    try:
+        for _ in range(count):
+            bufs.append(PeerOutputs(shape, device=dev))
+    except Exception as e:          # noqa: BLE001 - reported in the line, then the fallback runs
+        err = f"{type(e).__name__}: {e}"
+    flag = torch.tensor([0 if err else 1], device=dev, dtype=torch.int32)
+    dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+    if int(flag.item()) == 1:
+        return bufs, "fused epilogue stores into every rank's buffer (CUDA IPC, NVLink)"
+    dist.barrier()
+    for b in bufs:
+        b.close()
+    return None, "NCCL all-gather after the kernel (peer mapping failed" + (f": {err})" if err else " on a peer)")
+
+
+def close_peers(bufs, dist):
+    if bufs:
+        dist.barrier()
+        for b in bufs:
+            b.close()
+
+
+def max_over_ranks(x: float, world, dist, dev) -> float:
+    import torch
+    t = torch.tensor([x], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def sum_over_ranks(x: float, world, dist, dev) -> float:
+    import torch
+    t = torch.tensor([x], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+class Flush:
+    """Kernel-alone timing: each call runs after two 256 MB fills (more than L2, and ~80 us of GPU
+    work during which the host enqueues the call), CUDA events around the call."""
+
+    def __init__(self, dev):
+        import torch
+        self.buf = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+
+    def time(self, fn, n=8, events=False):
+        import torch
+        evp = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n)]
+        for i, (a, b) in enumerate(evp):
+            self.buf.fill_(i & 0xFF)
+            self.buf.fill_((i + 1) & 0xFF)
+            if events:
+                fn((a, b))
+            else:
+                a.record()
+                fn()
+                b.record()
+        torch.cuda.synchronize()
+        return statistics.mean(a.elapsed_time(b) for a, b in evp[2:])
+
+
+def long_context_config(heads=None, world=1):
+    from shadow_infer_b200 import workloads as W
+    c = W.CONFIGS["cfg5"]
+    H = heads or c["H"]
+    return {"workload": "cfg5 long-context layer: allocate codes (10/30/60 % fp16/int8/int4), plan, compress+pack, "
+                        "unpack, packed attention (non-causal, fp16 queries, scale 1/sqrt(128)); heads sharded "
+                        "over the GPUs, outputs gathered to every GPU",
+            "B": c["B"], "H": H, "S": c["S"], "D": c["D"], "heads_per_gpu": H // world,
+            "layers_quoted": STACK_LAYERS, "tokens_per_s": f"B*S / ({STACK_LAYERS} x layer step time)",
+            "l2": "inputs larger than L2 (K+V 1 GiB fp32 per layer; 134 MB per GPU at 8 GPUs)"}
+
+
+def check_long_context(out_full, local_fn, h0, hs, S, world, rank, dev, dist, layer_fn, codes_fn, seed_base):
+    """Every rank checks the gathered output it holds: its own heads against the single-GPU call
+    (no peer buffers, relative L2 <= 1e-5) and sampled query rows of sampled heads of every rank's
+    slice against the oracle (relative L2 <= 1e-3).  The verdict is reduced over the ranks."""
+    import numpy as np
+    import torch
+    from oracle import shadowkv_oracle as O
+    from shadow_infer_b200 import workloads as W
+
+    local = local_fn()
+    own = out_full[:, h0:h0 + hs]
+    own_rel = float(((own - local).double().norm() / local.double().norm().clamp_min(1e-30)).item())
+    H = hs * world
+    if world == 1:
+        heads = sorted({0, max(H // 2 - 3, 0), H - 1})
+    else:
+        heads = sorted({((rank + j) % world) * hs + (5 * rank + 3 * j) % hs for j in range(min(world, 3))})
+    worst = 0.0
+    for h in heads:
+        Lh = layer_fn(h)
+        codes_o = codes_fn(Lh, h)
+        ch = O.pack(Lh["k"].numpy(), Lh["v"].numpy(), O.plan_from_codes(codes_o), 16)
+        rows = W.sample_rows(S, 32, seed_base + h)
+        want = O.packed_attention(Lh["q"][:, :, rows].float().numpy(), ch)
+        got = out_full[:, h:h + 1, rows.to(dev)].cpu().numpy()
+        worst = max(worst, rel_l2(got, want))
+    t = torch.tensor([own_rel, worst, float(len(heads))], device=dev, dtype=torch.float64)
+    if world > 1:
+        n = t[2:].clone()
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dist.all_reduce(n, op=dist.ReduceOp.SUM)
+        t[2] = n[0]
+    own_rel, worst, n_heads = (float(x) for x in t.tolist())
+    ok = own_rel <= 1e-5 and worst <= 1e-3 and np.isfinite(worst)
+    return {"result": "ok" if ok else "FAILED", "own_heads_vs_single_gpu_max_rel_l2": own_rel,
+            "sampled_heads_vs_oracle_max_rel_l2": worst, "heads_checked_all_ranks": int(n_heads),
+            "rows_per_head": 32, "tolerance": {"own_heads": 1e-5, "oracle": 1e-3}}
+
+
+def long_context_phase(args, world, rank, dev, dist, lib, heads_total=None, extras=True):
+    """The headline step (module docstring) on heads [rank*H/N, (rank+1)*H/N) of the layer."""
     import torch
 
     from shadow_infer_b200 import workloads as W
     from shadow_infer_b200.shadowkv import PackedKVCache, PrecisionPlan, packed_attention
+    from shadow_infer_b200.shadowkv.packed_kv_cache import run_pack
+    from shadow_infer_b200.shadowkv.sharding import all_gather_heads
+    from shadow_infer_b200.shadowkv.shadowkv_agent import allocate_precision_codes
+
+    c = W.CONFIGS["cfg5"]
+    B, S, D, grp = c["B"], c["S"], c["D"], c["group"]
+    H = heads_total or c["H"]
+    if H % world:
+        raise ValueError(f"{H} heads do not shard over {world} GPUs")
+    hs, h0 = H // world, rank * (H // world)
+    L = W.cfg5_layer(h0, h0 + hs)
+    imp_h = L["importance"][:, h0:h0 + hs].contiguous()
+    k, v, imp, q = L["k"].to(dev), L["v"].to(dev), imp_h.to(dev), L["q"].to(dev)
+    n_bufs = 2 if extras else 1
+    peers, exchange = make_peers(world, dev, dist, (B, H, S, D), count=n_bufs)
+    gathered = ([torch.empty(B, H, S, D, dtype=torch.float32, device=dev) for _ in range(n_bufs)]
+                if world > 1 and peers is None else None)
+    bar = torch.ones(1, device=dev)
+    cs = torch.cuda.current_stream(dev)
+
+    def step(kk, vv, ii, qq, ev=None, j=0, before_barrier=None):
+        if ev:
+            ev[0].record()
+        codes = allocate_precision_codes(ii, "balanced")
+        plan = PrecisionPlan.from_codes(codes)
+        if ev:
+            ev[1].record()
+        cache = PackedKVCache.pack(kk, vv, None, grp, plan=plan)["packed_kv"]
+        if ev:
+            ev[2].record()
+        cache.unpack()
+        if ev:
+            ev[3].record()
+        out = packed_attention(qq, cache, check=False, events=ev[4:7] if ev else None,
+                               peer_outputs=peers[j % n_bufs] if peers else None, head_offset=h0)
+        if gathered is not None:
+            out = all_gather_heads(out, out=gathered[j % n_bufs])
+        if before_barrier is not None:
+            before_barrier()
+        if world > 1:
+            dist.all_reduce(bar)       # every rank's stores into every buffer have landed
+        if ev:
+            ev[7].record()
+        return cache, out
+
+    for _ in range(args.warmup):
+        step(k, v, imp, q)
+    steps = args.steps
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(8)] for _ in range(steps)]
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    n0 = lib.skv_launch_count()
+    t0.record()
+    for i in range(steps):
+        cache, out = step(k, v, imp, q, ev=evs[i])
+    t1.record()
+    torch.cuda.synchronize()
+    launches = lib.skv_launch_count() - n0
+    ms = max_over_ranks(t0.elapsed_time(t1) / steps, world, dist, dev)
+    parts = {name: statistics.mean(e[a].elapsed_time(e[b]) for e in evs)
+             for name, a, b in (("codes_plan", 0, 1), ("compress_pack", 1, 2), ("unpack", 2, 3),
+                                ("head_index", 3, 4), ("staging", 4, 5), ("attention", 5, 6),
+                                ("exchange_barrier", 6, 7))}
+    attn_ms = parts["attention"]
+    # per-launch error word of the attention (the timed launches ran with check=False)
+    packed_attention(q, cache, peer_outputs=peers[0] if peers else None, head_offset=h0)
+    if world > 1:
+        dist.all_reduce(bar)
+    torch.cuda.synchronize()
+    full = (peers[0].local if peers else (gathered[0] if gathered is not None else out))
+
+    def codes_fn(Lh, h):
+        from oracle import shadowkv_oracle as O
+        return O.allocate_precision_codes(Lh["importance"][:, h:h + 1].numpy(), "balanced")
+
+    check = check_long_context(full, lambda: packed_attention(q, cache), h0, hs, S, world, rank, dev, dist,
+                               lambda h: W.cfg5_layer(h, h + 1), codes_fn, 100)
+    fast = fast_k_compare(q, cache, flops=4.0 * B * hs * S * S * D, reps=3)
+
+    # ---- data plane of the layer: compress+pack and unpack alone (L2 flushed before each call)
+    fl = Flush(dev)
+    plan = PrecisionPlan.from_codes(allocate_precision_codes(imp, "balanced"))
+    pack_ms = fl.time(lambda ev: run_pack(k, v, plan, grp, events=ev), events=True)
+    unpack_ms = fl.time(lambda: cache.unpack())
+    kept = int(sum(cache._count.values()))
+    P = cache.memory_bytes()
+    fp32 = 2 * B * hs * S * D * 4
+    N = S * hs
+    pack_bytes = fp32 + N + P + 8 * kept
+    unpack_bytes = P + 8 * kept + fp32
+    hbm, hbm_src = hbm_peak()
+    burst, sustained, t_src = tensor_peaks()
+    flops = 4.0 * B * hs * S * S * D
+    pack_gbs = sum_over_ranks(pack_bytes, world, dist, dev) / (max_over_ranks(pack_ms, world, dist, dev) / 1e3) / 1e9
+    unpack_gbs = sum_over_ranks(unpack_bytes, world, dist, dev) / (max_over_ranks(unpack_ms, world, dist, dev) / 1e3) / 1e9
+    pk_in = sum_over_ranks(pack_bytes, world, dist, dev) / (max_over_ranks(parts["compress_pack"], world, dist, dev) / 1e3) / 1e9
+    up_in = sum_over_ranks(unpack_bytes, world, dist, dev) / (max_over_ranks(parts["unpack"], world, dist, dev) / 1e3) / 1e9
+    achieved = flops / (attn_ms / 1e3) / 1e12
+    res = {
+        "value": B * S / (STACK_LAYERS * ms / 1e3), "unit": "tokens/s", "ms_per_step": ms, "steps": steps,
+        "config": long_context_config(H if heads_total else None, world),
+        "roofline": {"kernel": "packed_attention_kernel", "bound": "tensor", "achieved": achieved,
+                     "peak": sustained, "unit": "TFLOP/s", "frac": achieved / sustained,
+                     "peak_source": f"{t_src} bf16_tflops_sustained: the kernel runs {attn_ms:.1f} ms launches back "
+                                    f"to back through the timed region, under the power cap like the sustained "
+                                    f"GEMM loop",
+                     "frac_of_burst": achieved / burst, "burst_peak": burst,
+                     "flops_per_launch": flops, "avg_launch_ms": attn_ms,
+                     "traffic": committed_traffic("packed_attention_kernel_cfg5.md"),
+                     "timing": "CUDA events on the launching stream around each attention launch of the timed steps"},
+        "step_breakdown_ms": parts,
+        "data_plane": {
+            "per_layer_bytes": {"compress_pack": pack_bytes, "unpack": unpack_bytes, "packed": P, "kept": kept},
+            "compress_pack": {"GB/s": pack_gbs, "ms": pack_ms, "in_step_GB/s": pk_in,
+                              "roofline": {"kernel": "pack16_kernel", "bound": "hbm", "achieved": pack_gbs / world,
+                                           "peak": hbm, "unit": "GB/s", "frac": pack_gbs / world / hbm,
+                                           "peak_source": f"{hbm_src} hbm_gbs",
+                                           "traffic": committed_traffic("pack16_kernel_cfg5.md")}},
+            "unpack": {"GB/s": unpack_gbs, "ms": unpack_ms, "in_step_GB/s": up_in,
+                       "roofline": {"kernel": "unpack16_kernel", "bound": "hbm", "achieved": unpack_gbs / world,
+                                    "peak": hbm, "unit": "GB/s", "frac": unpack_gbs / world / hbm,
+                                    "peak_source": f"{hbm_src} hbm_gbs",
+                                    "traffic": committed_traffic("unpack16_kernel_cfg5.md")}},
+            "stack_of_32_layers_ms": {"compress_pack": 32 * pack_ms, "unpack": 32 * unpack_ms},
+            "timing": "GB/s of the whole job (all ranks' bytes / slowest rank); each call alone after two 256 MB "
+                      "L2-flushing fills, events around the pack kernels and around unpack; in_step: events "
+                      "around the calls inside the timed steps",
+        },
+        "check": check,
+        "fast_k": fast,
+        "exchange": exchange,
+        "gpu_launches": launches,
+    }
+    if extras and world == 1:
+        res["vs_sdpa"] = sdpa_compare(args, dev, cache, q, parts["staging"] + attn_ms, reps=3)
+    if extras:
+        res["e2e"] = long_context_e2e(args, world, rank, dev, dist, L, imp_h, step, peers, gathered, h0, hs)
+        if world == 1 and rank == 0:
+            run, rows = long_context_sample(0, args.ref_rows)
+            run()
+            samples = [run() for _ in range(3)]
+            t_pu = statistics.median(s[0] for s in samples)
+            t_attn = statistics.median(s[1] for s in samples)
+            res["cpu_baseline"] = {
+                "value": long_context_cpu_rate(t_pu, t_attn, rows, c["H"]), "unit": "tokens/s", "cores": 1,
+                "kind": "port",
+                "sample": f"numpy oracle on head 0 of the layer (codes, plan, pack, unpack of all 32768 tokens; "
+                          f"float64 attention of {rows} sampled query rows), median of 3, scaled to 32 heads and "
+                          f"all query rows; tokens/s of the 32-layer stack"}
+    close_peers(peers, dist)
+    return res
+
+
+def long_context_e2e(args, world, rank, dev, dist, L, imp_h, step, peers, gathered, h0, hs):
+    """The step from pinned host buffers through the public API: step i+1's K, V, importance and
+    queries travel host -> device on one copy stream and step i's output (this rank's heads of the
+    gathered output) device -> host on another while step i computes; device inputs and output
+    buffers are double-buffered; every copy lies inside the timed region."""
+    import torch
+    hosts = [L["k"].pin_memory(), L["v"].pin_memory(), imp_h.pin_memory(), L["q"].pin_memory()]
+    B, _, S, D = L["k"].shape
+    out_host = [torch.empty(B, hs, S, D, dtype=torch.float32).pin_memory() for _ in range(2)]
+    dbuf = [tuple(torch.empty(t.shape, dtype=t.dtype, device=dev) for t in hosts) for _ in range(2)]
+    cs = torch.cuda.current_stream(dev)
+    s_in, s_out = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
+    in_ready = [torch.cuda.Event() for _ in range(2)]
+    in_free = [torch.cuda.Event() for _ in range(2)]
+    out_read = [torch.cuda.Event() for _ in range(2)]
+    state = {"n": 0}
+
+    def e2e_step():
+        j = state["n"]
+        state["n"] += 1
+        b = j % 2
+        with torch.cuda.stream(s_in):
+            s_in.wait_event(in_free[b])              # the compute that read buffer b is done
+            for d, h in zip(dbuf[b], hosts):
+                d.copy_(h, non_blocking=True)
+            in_ready[b].record(s_in)
+        cs.wait_event(in_ready[b])
+        # output buffer b was last read back two steps ago: no rank may write it again before that
+        # read is done (the wait precedes this step's barrier, which every rank's next write follows)
+        _, out = step(*dbuf[b], j=j, before_barrier=(lambda: cs.wait_event(out_read[(j - 1) % 2])) if j else None)
+        in_free[b].record(cs)
+        done = torch.cuda.Event()
+        done.record(cs)
+        with torch.cuda.stream(s_out):
+            s_out.wait_event(done)
+            src = out[:, h0:h0 + hs] if out.shape[1] != hs else out
+            out_host[b].copy_(src, non_blocking=True)
+            out.record_stream(s_out)
+            out_read[b].record(s_out)
+
+    n = max(3, min(args.steps, 10))
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(cs)
+    s_in.wait_event(e0)                            # no copy of the timed steps starts before e0
+    for _ in range(n):
+        e2e_step()
+    cs.wait_stream(s_in)
+    cs.wait_stream(s_out)
+    e1.record(cs)
+    torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1) / n, world, dist, dev)
+    h2d = sum(t.numel() * t.element_size() for t in hosts)
+    d2h = out_host[0].numel() * 4
+    from shadow_infer_b200 import workloads as W
+    c = W.CONFIGS["cfg5"]
+    return {"value": c["B"] * c["S"] / (STACK_LAYERS * ms / 1e3), "unit": "tokens/s",
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": n, "ms_per_step": ms,
+            "per_rank": "each rank copies its heads' K, V, queries and the importance slice in and reads its heads "
+                        "of the gathered output back",
+            "pipelining": "inputs of step i+1 in and step i's output out on two copy streams while step i computes "
+                          "(PCIe is full duplex); double-buffered"}
+
+
+# ------------------------------------------------------------------------ cfg2 data plane
+def step_bytes(B, H, S, D, packed_bytes, n_kept, n_reuse_rows_bytes, n_reuse, admission_entries=None):
+    """Algorithmic HBM bytes of one budget data-plane step over H heads, per call (admission over
+    ``admission_entries`` entries: the whole layer, which every rank admits)."""
+    N = S * H
+    fp32 = 2 * B * H * S * D * 4
+    NA = N if admission_entries is None else admission_entries
+    return {
+        "allocate": 4 * N + N,
+        "sensitivity": fp32 + 4 * N,
+        "admission": 9 * NA + 4 * NA,
+        "plan": N + N + 8 * N + 4 * N + 8 * n_reuse,
+        "pack": fp32 + N + packed_bytes + 8 * n_kept,
+        "reuse": N + 2 * n_reuse_rows_bytes,
+        "unpack": packed_bytes + 8 * n_kept + fp32,
+    }
+
+
+def cfg2_phase(args, world, rank, dev, dist, lib):
+    """The budget data plane on one cfg2 layer (B=1, H=32, S=8192, D=128), heads sharded:
+
+        allocate_precision_codes -> kv_sensitivity -> admit_codes (30 % fp16 budget, hard eviction,
+        4 sinks; at N > 1 ``admit_codes_sharded``: NCCL all-gather of the [S, H/N] codes, importance
+        and sensitivity, the same admission on every rank, own columns kept) -> PrecisionPlan.from_codes
+        (50 % reuse mask) -> PackedKVCache.pack -> apply_reuse_mask (previous step's cache) -> unpack
+
+    through the drop-in calls (``admit_codes`` returns Python ints, so it synchronises).  GB/s =
+    the job's algorithmic bytes (admission counted once) / slowest rank's step time.  ``check``:
+    every rank's admitted columns, predicted bytes and eviction count equal the single-GPU
+    admission of the whole layer, and the ranks' packed bytes add up to the whole layer's."""
+    import torch
+
+    from shadow_infer_b200 import workloads as W
+    from shadow_infer_b200.shadowkv import PackedKVCache, PrecisionPlan, kv_sensitivity
+    from shadow_infer_b200.shadowkv.rd_allocator import admit_codes, entry_bytes, predict_codes_bytes
+    from shadow_infer_b200.shadowkv.sharding import admit_codes_sharded
+    from shadow_infer_b200.shadowkv.shadowkv_agent import allocate_precision_codes
+
+    I = W.cfg2_inputs()
+    B, H, S, D = I["k"].shape
+    if H % world:
+        raise ValueError(f"{H} heads do not shard over {world} GPUs")
+    hs, h0 = H // world, rank * (H // world)
+    sl = slice(h0, h0 + hs)
+    k, v = I["k"][:, sl].contiguous().to(dev), I["v"][:, sl].contiguous().to(dev)
+    imp, reuse = I["importance"][:, sl].contiguous().to(dev), I["reuse"][:, sl].contiguous().to(dev)
+    budget, sink = I["budget"], I["sink_tokens"]
+
+    def admit(codes, ii, sens):
+        if world > 1:
+            return admit_codes_sharded(codes, ii, sens, budget, B, D, sink, True, True)
+        return admit_codes(codes, ii, sens, budget, B, D, sink, True, True)
+
+    codes0 = allocate_precision_codes(imp, "balanced")
+    adm, pred, ev = admit(codes0, imp, kv_sensitivity(k, v))
+    prev = PackedKVCache.pack(I["k_prev"][:, sl].contiguous().to(dev), I["v_prev"][:, sl].contiguous().to(dev),
+                              None, 16, plan=PrecisionPlan.from_codes(adm))["packed_kv"]
+
+    def step():
+        codes = allocate_precision_codes(imp, "balanced")
+        sens = kv_sensitivity(k, v)
+        a, _, _ = admit(codes, imp, sens)
+        plan = PrecisionPlan.from_codes(a, reuse_mask=reuse)
+        cache = PackedKVCache.pack(k, v, None, 16, plan=plan)["packed_kv"]
+        cache.apply_reuse_mask(prev, reuse)
+        cache.unpack()
+        return cache, a
+
+    cache, a = step()
+    stats = cache.apply_reuse_mask(prev, reuse, return_stats=True)
+    kept = sum(cache._count.values())
+    per_code = [int(entry_bytes(p, B, D, 16)) for p in ("fp32", "fp16", "int8", "int4")]
+    slot = cache._slot
+    flagged = reuse.reshape(-1).bool() & (slot >= 0)
+    reused_bytes = sum(int(((slot & 3) == c)[flagged].sum().item()) * per_code[c] for c in range(4))
+    assert stats["applied"] == int(flagged.sum().item())
+    parts = step_bytes(B, hs, S, D, cache.memory_bytes(), kept, reused_bytes, int(reuse.sum().item()),
+                       admission_entries=S * H if rank == 0 else 0)
+    nbytes = sum_over_ranks(sum(parts.values()), world, dist, dev)
+
+    # check: the sharded admission equals the single-GPU admission of the whole layer
+    kf, vf = I["k"].to(dev), I["v"].to(dev)
+    impf = I["importance"].to(dev)
+    full, pred_f, ev_f = admit_codes(allocate_precision_codes(impf, "balanced"), impf, kv_sensitivity(kf, vf),
+                                     budget, B, D, sink, True, True)
+    del kf, vf
+    same = bool(torch.equal(full[:, sl], a)) and (pred, ev) == (pred_f, ev_f)
+    mem_sum = sum_over_ranks(cache.memory_bytes(), world, dist, dev)
+    ok = sum_over_ranks(0.0 if same else 1.0, world, dist, dev) == 0 and \
+        int(mem_sum) == int(predict_codes_bytes(full, B, D, 16))
+
+    for _ in range(args.warmup):
+        step()
+    steps = max(3, min(args.steps, 50))
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n0 = lib.skv_launch_count()
+    h0_wall = time.perf_counter()
+    t0.record()
+    for _ in range(steps):
+        step()
+    t1.record()
+    torch.cuda.synchronize()
+    host_ms = (time.perf_counter() - h0_wall) * 1e3 / steps
+    launches = (lib.skv_launch_count() - n0) // steps
+    ms = max_over_ranks(t0.elapsed_time(t1) / steps, world, dist, dev)
+    peak, peak_kind = hbm_peak()
+    kernels = cfg2_calls(k, v, imp, reuse, prev, budget, sink, parts, dev, peak) if world == 1 else None
+    return {
+        "metric": "budget data-plane step GB/s (cfg2 layer, heads sharded)",
+        "value": nbytes / (ms / 1e3) / 1e9, "unit": "GB/s", "ms_per_step": ms, "steps": steps,
+        "frac_of_hbm_per_gpu": nbytes / world / (ms / 1e3) / 1e9 / peak, "peak_source": f"{peak_kind} hbm_gbs",
+        "host_wall_ms_per_step": host_ms, "gpu_launches_per_step": launches,
+        "config": {"workload": "cfg2 layer: codes, sensitivity, budget admission (30 % fp16, hard eviction, 4 "
+                               "sinks), plan (50 % reuse), compress+pack, reuse, unpack", "B": B, "H": H, "S": S,
+                   "D": D, "heads_per_gpu": hs, "budget_bytes": budget,
+                   "admission": "admit_codes_sharded (NCCL all-gather + the same admission on every rank)"
+                                if world > 1 else "admit_codes",
+                   "bytes_per_step_rank0": parts},
+        "check": {"result": "ok" if ok else "FAILED", "predicted": pred, "evicted": ev,
+                  "what": "admitted columns, predicted bytes and evictions equal the single-GPU admission of the "
+                          "whole layer; packed bytes of all ranks add up to the whole layer's"},
+        "kernels": kernels,
+        "kernels_timing": "each call of the step alone through its public API, events around it, after two 256 MB "
+                          "L2-flushing fills (8 calls, first 2 dropped; pack: events around its kernels; evict: 25 % "
+                          "of the entries of a freshly packed copy, bytes = mask + 2 x packed bytes after); frac of "
+                          "measured HBM" if kernels else None,
+    }
+
+
+def cfg2_calls(k, v, imp, reuse, prev, budget, sink, parts, dev, peak):
+    """Every call of the budget step alone (one GPU), with its algorithmic bytes and HBM fraction."""
+    import torch
+
+    from shadow_infer_b200.shadowkv import PackedKVCache, PrecisionPlan, kv_sensitivity
+    from shadow_infer_b200.shadowkv.packed_kv_cache import run_pack
+    from shadow_infer_b200.shadowkv.rd_allocator import admit_codes
+    from shadow_infer_b200.shadowkv.shadowkv_agent import allocate_precision_codes
+
+    B, H, S, D = k.shape
+    fl = Flush(dev)
+    codes = allocate_precision_codes(imp, "balanced")
+    sens = kv_sensitivity(k, v)
+    adm = admit_codes(codes, imp, sens, budget, B, D, sink, True, True)[0]
+    plan = PrecisionPlan.from_codes(adm, reuse_mask=reuse)
+    cache = PackedKVCache.pack(k, v, None, 16, plan=plan)["packed_kv"]
+    ms = {
+        "allocate": fl.time(lambda: allocate_precision_codes(imp, "balanced")),
+        "sensitivity": fl.time(lambda: kv_sensitivity(k, v)),
+        "admission": fl.time(lambda: admit_codes(codes, imp, sens, budget, B, D, sink, True, True)),
+        "plan": fl.time(lambda: PrecisionPlan.from_codes(adm, reuse_mask=reuse)),
+        "pack": fl.time(lambda ev: run_pack(k, v, plan, 16, events=ev), events=True),
+        "reuse": fl.time(lambda: cache.apply_reuse_mask(prev, reuse)),
+        "unpack": fl.time(lambda: cache.unpack()),
+    }
+    gen = torch.Generator(device="cpu").manual_seed(7)
+    evict_mask = (torch.rand(S, H, generator=gen) < 0.25).to(dev)
+    plan_e = PrecisionPlan.from_codes(adm)
+    fresh = []
+    after = [0]
+
+    def evict_call():
+        ce = fresh.pop()
+        ce.evict(evict_mask)
+        after[0] = ce.memory_bytes()
+
+    def evict_timed(ev):
+        fresh.append(PackedKVCache.pack(k, v, None, 16, plan=plan_e)["packed_kv"])
+        fl.buf.fill_(1)
+        fl.buf.fill_(2)
+        ev[0].record()
+        evict_call()
+        ev[1].record()
+
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(8)]
+    for e in evs:
+        evict_timed(e)
+    torch.cuda.synchronize()
+    ms["evict"] = statistics.mean(a.elapsed_time(b) for a, b in evs[2:])
+    nbytes = dict(parts)
+    nbytes["evict"] = S * H + 2 * after[0]
+    return {name: {"avg_ms": t, "algorithmic_bytes": nbytes[name], "achieved_gbs": nbytes[name] / (t / 1e3) / 1e9,
+                   "frac": nbytes[name] / (t / 1e3) / 1e9 / peak} for name, t in ms.items()}
+
+
+# ------------------------------------------------------------------------------- attention
+def attention_phase(args, world, rank, dev, dist, lib):
+    """Packed attention on one cfg3 layer (B=1, H=32, S=4096, D=128, codes 20/50/30 %), heads
+    sharded over ranks; at N > 1 the epilogue stores every output row into all ranks' fp32
+    [B, H, S, D] buffers over NVLink (the all-gather inside the kernel), then a one-element
+    all-reduce marks the point where every rank holds the whole output.  ``check`` as for the
+    headline step."""
+    import torch
+
+    from shadow_infer_b200 import workloads as W
+    from shadow_infer_b200.shadowkv import PackedKVCache, PrecisionPlan, packed_attention
+    from shadow_infer_b200.shadowkv.sharding import all_gather_heads
     from shadow_infer_b200.shadowkv.shadowkv_agent import allocate_precision_codes
 
     c = W.CONFIGS["cfg3"]
@@ -294,44 +845,25 @@ def attention_phase(args, world, rank, dev, dist, lib, tensor_peak):
     k, v = W.kv_tensors(B, H, S, D, 0)
     imp = W.importance_map(S, H, 0, c["fractions"])
     q = W.queries(B, H, S, D, 0)
-    k, v = k[:, h0:h0 + hs].contiguous(), v[:, h0:h0 + hs].contiguous()
-    codes = allocate_precision_codes(imp[:, h0:h0 + hs].contiguous().to(dev), "balanced")
-    cache = PackedKVCache.pack(k.to(dev), v.to(dev), None, c["group"], plan=PrecisionPlan.from_codes(codes))["packed_kv"]
+    codes_all = allocate_precision_codes(imp.to(dev), "balanced").cpu()
+    ks, vs = k[:, h0:h0 + hs].contiguous(), v[:, h0:h0 + hs].contiguous()
+    codes = codes_all[:, h0:h0 + hs].contiguous().to(dev)
+    cache = PackedKVCache.pack(ks.to(dev), vs.to(dev), None, c["group"], plan=PrecisionPlan.from_codes(codes))["packed_kv"]
     qd = q[:, h0:h0 + hs].contiguous().to(dev)
     packed_attention(qd, cache)                        # builds the head index, checks the error word
-    # N > 1: the all-gather of the head-sharded outputs is fused into the attention epilogue --
-    # every finished row is stored into all ranks' [B, H, S, D] buffers over NVLink
-    # (all ranks agree: if any rank cannot map its peers' buffers, every rank falls back to the
-    # NCCL all-gather after the kernel, so that all ranks keep taking the same collective steps)
-    from shadow_infer_b200.shadowkv.sharding import PeerOutputs, all_gather_heads
-    peers, exchange = None, "none"
-    if world > 1:
-        err = None
-        try:
-            peers = PeerOutputs((B, H, S, D), device=dev)
-        except Exception as e:          # noqa: BLE001 - reported in the line, then the fallback runs
-            err = f"{type(e).__name__}: {e}"
-        flag = torch.tensor([0 if err else 1], device=dev, dtype=torch.int32)
-        dist.all_reduce(flag, op=dist.ReduceOp.MIN)
-        if int(flag.item()) == 1:
-            exchange = "fused epilogue stores into every rank's buffer (CUDA IPC, NVLink)"
-        else:
-            if peers is not None:
-                dist.barrier()
-                peers.close()
-                peers = None
-            exchange = "NCCL all-gather after the kernel (peer mapping failed" + (f": {err})" if err else " on a peer)")
+    peers, exchange = make_peers(world, dev, dist, (B, H, S, D))
     gathered = torch.empty(B, H, S, D, dtype=torch.float32, device=dev) if world > 1 and peers is None else None
+    bar = torch.ones(1, device=dev)
     steps = max(3, min(args.steps, 32))
     kev = [tuple(torch.cuda.Event(enable_timing=True) for _ in range(3)) for _ in range(steps)]
-    sms = torch.cuda.get_device_properties(dev).multi_processor_count
 
     def step(i=None):
-        # events: before the staging kernel, between the two kernels, after the attention kernel
         out = packed_attention(qd, cache, check=False, events=kev[i] if i is not None else None,
-                               peer_outputs=peers, head_offset=h0)
+                               peer_outputs=peers[0] if peers else None, head_offset=h0)
         if gathered is not None:
-            all_gather_heads(out, out=gathered)
+            out = all_gather_heads(out, out=gathered)
+        if world > 1:
+            dist.all_reduce(bar)
         return out
 
     for _ in range(3):
@@ -339,69 +871,115 @@ def attention_phase(args, world, rank, dev, dist, lib, tensor_peak):
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
-    t0 = torch.cuda.Event(enable_timing=True)
-    t1 = torch.cuda.Event(enable_timing=True)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     n0 = lib.skv_launch_count()
     t0.record()
     for i in range(steps):
-        step(i)
+        out = step(i)
     t1.record()
     torch.cuda.synchronize()
     launches = lib.skv_launch_count() - n0
-    packed_attention(qd, cache, peer_outputs=peers, head_offset=h0)   # error word of the last launch
+    packed_attention(qd, cache, peer_outputs=peers[0] if peers else None, head_offset=h0)   # error word
     if world > 1:
-        dist.barrier()
-        if peers is not None:
-            peers.close()
-    ms = torch.tensor([t0.elapsed_time(t1) / steps], device=dev, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
-    ms = float(ms.item())
+        dist.all_reduce(bar)
+    torch.cuda.synchronize()
+    full = out
+
+    def layer_fn(h):
+        return {"k": k[:, h:h + 1], "v": v[:, h:h + 1], "q": q[:, h:h + 1]}
+
+    check = check_long_context(full, lambda: packed_attention(qd, cache), h0, hs, S, world, rank, dev, dist,
+                               layer_fn, lambda Lh, h: codes_all[:, h:h + 1].numpy(), 200)
+    close_peers(peers, dist)
+    ms = max_over_ranks(t0.elapsed_time(t1) / steps, world, dist, dev)
     stage_ms = statistics.mean(a.elapsed_time(b) for a, b, _ in kev)
-    kms = statistics.mean(b.elapsed_time(c) for _, b, c in kev)
+    kms = statistics.mean(b.elapsed_time(c_) for _, b, c_ in kev)
     flops_rank = 4.0 * B * hs * S * S * D
-    # staging kernel: reads the packed rows, writes fp16 K/V tiles (evicted entries skipped)
     stored = int(sum(cache._count.values()))
     stage_bytes = cache.memory_bytes() + stored * 4 + stored * 2 * B * D * 2
+    burst, sustained, t_src = tensor_peaks()
     res = {
         "metric": "packed-attn tokens/s (32-layer stack, cfg3)",
         "value": B * S / (L * ms / 1e3), "unit": "tokens/s", "ms_per_layer": ms, "steps": steps,
-        "scaling": "strong (heads sharded over GPUs; outputs all-gathered to every rank)",
+        "scaling": "strong (heads sharded over GPUs; outputs gathered to every rank)",
         "exchange": exchange,
-        "attention_ctas": sms,
         "config": {"workload": "cfg3: packed K/V codes 20/50/30 fp16/int8/int4, fp16 queries, non-causal",
                    "B": B, "H": H, "S_q": S, "S_kv": S, "D": D, "layers": L, "heads_per_gpu": hs},
         "roofline": {"kernel": "packed_attention_kernel", "bound": "tensor",
-                     "achieved": flops_rank / (kms / 1e3) / 1e12, "peak": tensor_peak[0], "unit": "TFLOP/s",
-                     "frac": flops_rank / (kms / 1e3) / 1e12 / tensor_peak[0],
-                     "peak_source": tensor_peak[1], "avg_launch_ms": kms, "flops_per_launch": flops_rank,
+                     "achieved": flops_rank / (kms / 1e3) / 1e12, "peak": burst, "unit": "TFLOP/s",
+                     "frac": flops_rank / (kms / 1e3) / 1e12 / burst,
+                     "peak_source": f"{t_src} bf16_tflops (burst: 0.1-0.3 ms launches)", "avg_launch_ms": kms,
+                     "flops_per_launch": flops_rank,
                      "traffic": committed_traffic("packed_attention_kernel_cfg3.md")},
         "staging": {"kernel": "stage_tiles_kernel", "bound": "hbm", "avg_launch_ms": stage_ms,
                     "algorithmic_bytes": stage_bytes, "achieved_gbs": stage_bytes / (stage_ms / 1e3) / 1e9,
                     "traffic": committed_traffic("stage_tiles_kernel_cfg3.md")},
+        "check": check,
         "gpu_launches": launches,
         "output_dtype": "f32",
     }
+    res["fast_k"] = fast_k_compare(qd, cache, flops_rank, reps=10)
     if world == 1 and rank == 0:
-        import numpy as np
-        from oracle import shadowkv_oracle as O
-
-        ko, vo = k[:, :1].numpy().copy(), v[:, :1].numpy().copy()
-        co = codes[:, :1].cpu().numpy()
-        cache_o = O.pack(ko, vo, O.plan_from_codes(co), c["group"])
-        qo = q[:, :1].float().numpy()
-        t = time.perf_counter()
-        O.packed_attention(qo, cache_o)
-        dt = time.perf_counter() - t
-        res["cpu_baseline"] = {"value": B * S / (dt * H * L), "unit": "tokens/s", "cores": os.cpu_count(),
-                               "kind": "port",
-                               "sample": "oracle unpack + float64 numpy attention of head 0 of the layer, "
-                                         "extrapolated x32 heads x32 layers"}
-    res["gqa_block"] = gqa_block_attention(args, rank, dev, tensor_peak, k, v, codes, c["group"]) if world == 1 else None
+        res["vs_sdpa"] = sdpa_compare(args, dev, cache, qd, stage_ms + kms)
+        res["gqa_block"] = gqa_block_attention(args, rank, dev, ks, vs, codes, c["group"])
     return res
 
 
-def gqa_block_attention(args, rank, dev, tensor_peak, k, v, codes, group):
+def fast_k_compare(q, cache, flops, reps=3):
+    """The attention with K in fp16 only (``fast_k``, one MMA chain) against the default hi + lo
+    K on the same layer: kernel time and the relative L2 difference of the outputs (the default
+    is within ~3e-4 of the oracle, so the difference is the fast path's extra error)."""
+    import torch
+    from shadow_infer_b200.shadowkv import packed_attention
+    ref = packed_attention(q, cache)
+    out = packed_attention(q, cache, fast_k=True)
+    diff = float(((out - ref).double().norm() / ref.double().norm()).item())
+    evs = [tuple(torch.cuda.Event(enable_timing=True) for _ in range(3)) for _ in range(reps)]
+    for e in evs:
+        packed_attention(q, cache, check=False, events=e, fast_k=True)
+    torch.cuda.synchronize()
+    ms = statistics.mean(b.elapsed_time(c_) for _, b, c_ in evs)
+    burst, sustained, _ = tensor_peaks()
+    return {"attention_ms": ms, "achieved_tflops": flops / (ms / 1e3) / 1e12,
+            "frac_of_burst": flops / (ms / 1e3) / 1e12 / burst, "rel_l2_vs_default": diff,
+            "what": "K staged in fp16 only (SKV_ATTN_FAST_K): one QK MMA chain instead of hi + lo"}
+
+
+def sdpa_compare(args, dev, cache, qd, ours_ms, reps=None):
+    """The unfused library path the packed kernel replaces, on the same layer and device: unpack to
+    fp32, convert to fp16 and torch's scaled_dot_product_attention (fp16, non-causal)."""
+    import torch
+    import torch.nn.functional as F
+
+    def lib_path():
+        ku, vu = cache.unpack()
+        return F.scaled_dot_product_attention(qd, ku.half(), vu.half())
+
+    def sdpa_only(kh, vh):
+        return F.scaled_dot_product_attention(qd, kh, vh)
+
+    ku, vu = cache.unpack()
+    kh, vh = ku.half(), vu.half()
+    for _ in range(3):
+        lib_path()
+        sdpa_only(kh, vh)
+    torch.cuda.synchronize()
+    reps = reps or max(3, min(args.steps, 20))
+    times = {}
+    for name, fn in (("unpack_plus_sdpa_ms", lib_path), ("sdpa_alone_ms", lambda: sdpa_only(kh, vh))):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        times[name] = e0.elapsed_time(e1) / reps
+    times["packed_staging_plus_attention_ms"] = ours_ms
+    times["speedup_vs_unpack_plus_sdpa"] = times["unpack_plus_sdpa_ms"] / ours_ms
+    return times
+
+
+def gqa_block_attention(args, rank, dev, k, v, codes, group):
     """Blockwise decoding shape of the grouped-query model path: a 256-token block's queries
     (32 query heads) attend to the packed cfg3 prefix (8 KV heads of it, 4096 tokens) plus the
     block's own K/V (the reference's cat(past, new) + repeat_kv + attention,
@@ -411,6 +989,7 @@ def gqa_block_attention(args, rank, dev, tensor_peak, k, v, codes, group):
 
     from shadow_infer_b200.shadowkv import PackedKVCache, PrecisionPlan, packed_attention
 
+    tensor_peak = tensor_peaks()[0::2]
     H_kv, rep, W_blk = 8, 4, 256
     B, _, S, D = k.shape
     cache = PackedKVCache.pack(k[:, :H_kv].contiguous().to(dev), v[:, :H_kv].contiguous().to(dev), None, group,
@@ -452,6 +1031,120 @@ def gqa_block_attention(args, rank, dev, tensor_peak, k, v, codes, group):
                      "achieved": flops / (kms / 1e3) / 1e12, "peak": tensor_peak[0], "unit": "TFLOP/s",
                      "frac": flops / (kms / 1e3) / 1e12 / tensor_peak[0], "flops_per_launch": flops},
         "torch_unpack_cat_attention_ms": e0.elapsed_time(e1) / reps,
+    }
+
+
+# ------------------------------------------------------------------- batched denoising loop
+def denoise_phase(args, world, rank, dev, dist, lib):
+    """The batched denoising loop (cfg4: B=8, S=2048, H=32, D=128, 32 layers, 16 steps), heads
+    sharded over the ranks.  Per step and layer:
+
+        K_t = K_{t-1} + drift, V likewise (per (token, head) a relative drift r ~ |N(0, 0.074)|,
+        drawn on the device before the timed events) -> decide_reuse_mask (drift < 0.05: the
+        reference's rule at its conservative threshold on the last step, importance term off)
+        -> PrecisionPlan.from_codes (the layer's codes, that reuse mask) -> pack -> apply_reuse_mask
+        from the layer's previous cache -> evict the layer's 25 % lowest-importance non-sink
+        entries -> packed_attention (outputs gathered to every rank) -> the cache is next step's
+        previous cache.
+
+    Timed with CUDA events around each layer step (drift synthesis excluded), summed, slowest
+    rank.  tokens/s = B * S * steps / time of the 16 x 32 layer steps."""
+    import torch
+
+    from shadow_infer_b200 import workloads as W
+    from shadow_infer_b200.shadowkv import PackedKVCache, PrecisionPlan, packed_attention
+    from shadow_infer_b200.shadowkv.sharding import all_gather_heads
+    from shadow_infer_b200.shadowkv.shadowkv_agent import allocate_precision_codes, decide_reuse_mask
+
+    c = W.CONFIGS["cfg4"]
+    B, H, S, D, Lyr, T = c["B"], c["H"], c["S"], c["D"], c["layers"], c["steps"]
+    if H % world:
+        raise ValueError(f"{H} heads do not shard over {world} GPUs")
+    hs, h0 = H // world, rank * (H // world)
+    g = torch.Generator(device=dev).manual_seed(4000 + rank)
+
+    def kv0():
+        x = torch.randn(B, hs, S, D, device=dev, generator=g)
+        return torch.where(torch.rand(x.shape, device=dev, generator=g) < 0.01, x * 8, x)
+
+    kprev, vprev, qs, codes, emask, prev = [], [], [], [], [], []
+    zeros = torch.zeros(S, hs, device=dev)
+    for layer in range(Lyr):
+        imp = W.importance_map(S, H, 10_000 + layer, c["fractions"])
+        cl = allocate_precision_codes(imp[:, h0:h0 + hs].contiguous().to(dev), "balanced")
+        codes.append(cl)
+        emask.append(W.lowest_importance_mask(imp, c["evict_frac"], 4)[:, h0:h0 + hs].contiguous().to(dev))
+        k0, v0 = kv0(), kv0()
+        kprev.append(k0)
+        vprev.append(v0)
+        qs.append(torch.randn(B, hs, S, D, device=dev, generator=g).half())
+        prev.append(PackedKVCache.pack(k0, v0, None, c["group"], plan=PrecisionPlan.from_codes(cl))["packed_kv"])
+    peers, exchange = make_peers(world, dev, dist, (B, H, S, D))
+    gathered = torch.empty(B, H, S, D, dtype=torch.float32, device=dev) if world > 1 and peers is None else None
+    bar = torch.ones(1, device=dev)
+    r_scale = 0.074 / math.sqrt(D)
+
+    def drifted(x):
+        r = torch.randn(1, hs, S, 1, device=dev, generator=g).abs_() * r_scale
+        return x + torch.randn(x.shape, device=dev, generator=g) * r * torch.linalg.vector_norm(x, dim=-1, keepdim=True)
+
+    def layer_step(layer, k1, v1):
+        mask, st = decide_reuse_mask(k1, v1, kprev[layer], vprev[layer], 16, 16, 0.0, "conservative", zeros)
+        plan = PrecisionPlan.from_codes(codes[layer], reuse_mask=mask)
+        cur = PackedKVCache.pack(k1, v1, None, c["group"], plan=plan)["packed_kv"]
+        applied = cur.apply_reuse_mask(prev[layer], mask, return_stats=True)["applied"]
+        removed = cur.evict(emask[layer])
+        out = packed_attention(qs[layer], cur, check=False, peer_outputs=peers[0] if peers else None,
+                               head_offset=h0)
+        if gathered is not None:
+            all_gather_heads(out, out=gathered)
+        if world > 1:
+            dist.all_reduce(bar)
+        return cur, st["reuse_ratio"], applied, removed
+
+    for _ in range(3):                                 # warm-up on layer 0, state untouched
+        layer_step(0, drifted(kprev[0]), drifted(vprev[0]))
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    evs = []
+    ratios, applied_n, removed_n = [], 0, 0
+    n0 = lib.skv_launch_count()
+    w0 = time.perf_counter()
+    for t in range(1, T + 1):
+        for layer in range(Lyr):
+            k1, v1 = drifted(kprev[layer]), drifted(vprev[layer])
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            cur, ratio, applied, removed = layer_step(layer, k1, v1)
+            b.record()
+            evs.append((a, b))
+            prev[layer], kprev[layer], vprev[layer] = cur, k1, v1
+            ratios.append(ratio)
+            applied_n += applied
+            removed_n += removed
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - w0
+    launches = lib.skv_launch_count() - n0
+    packed_attention(qs[0], prev[0], peer_outputs=peers[0] if peers else None, head_offset=h0)   # error word
+    if world > 1:
+        dist.all_reduce(bar)
+    torch.cuda.synchronize()
+    close_peers(peers, dist)
+    total_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in evs), world, dist, dev)
+    flops = 4.0 * B * H * S * S * D * Lyr * T
+    return {
+        "metric": "batched denoising loop tokens/s (cfg4: 16 steps x 32 layers)",
+        "value": B * S * T / (total_ms / 1e3), "unit": "tokens/s", "ms_per_layer_step": total_ms / (Lyr * T),
+        "loop_ms": total_ms, "host_wall_s": wall,
+        "attention_tflops_whole_loop": flops / (total_ms / 1e3) / 1e12,
+        "reuse_ratio_mean": statistics.mean(ratios), "reused_entries_rank0": applied_n,
+        "evicted_entries_rank0": removed_n, "gpu_launches": launches, "exchange": exchange,
+        "scaling": "strong (heads sharded over GPUs; outputs gathered to every rank)",
+        "config": {"workload": "cfg4: per step and layer drift -> reuse decision (drift < 0.05) -> re-pack -> reuse "
+                               "-> evict 25 % lowest importance -> packed attention", "B": B, "H": H, "S": S, "D": D,
+                   "layers": Lyr, "steps": T, "heads_per_gpu": hs, "codes": "25/50/25 fp16/int8/int4",
+                   "data": "K, V, Q and the drift drawn on the device (seeded), importance from workloads"},
     }
 
 
@@ -767,25 +1460,12 @@ def decision_phase(args, world, rank, dev, lib):
     return res
 
 
-def tensor_peak():
-    path = os.path.join(REPO, "MEASURED_PEAKS.json")
-    try:
-        with open(path) as f:
-            return float(json.load(f)["bf16_tflops"]), "measured bf16_tflops (burst; fp16 runs at the same rate)"
-    except Exception:
-        return 1590.0, "fallback"
-
-
 # ------------------------------------------------------------------------------------ b200
 def run_b200(args):
     import torch
     import torch.distributed as dist
 
     from shadow_infer_b200 import _lib
-    from shadow_infer_b200 import workloads as W
-    from shadow_infer_b200.shadowkv import PackedKVCache, PrecisionPlan, kv_sensitivity
-    from shadow_infer_b200.shadowkv.rd_allocator import admit_codes_device
-    from shadow_infer_b200.shadowkv.shadowkv_agent import allocate_precision_codes
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -794,282 +1474,68 @@ def run_b200(args):
     dev = torch.device("cuda", local)
     if world > 1:
         import datetime
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
     lib = _lib.load()
     if args.phase != "all":
-        if args.phase == "decisions":
+        if args.phase == "long-slice":
+            res = long_context_phase(args, world, rank, dev, dist, lib, heads_total=4 * world, extras=False)
+        elif args.phase == "cfg2":
+            res = cfg2_phase(args, world, rank, dev, dist, lib)
+        elif args.phase == "decisions":
             res = decision_phase(args, world, rank, dev, lib)
         else:
             res = paged_phase(args, world, rank, dev, lib, run_mode=args.phase == "paged")
         if world > 1:
+            dist.barrier()
             dist.destroy_process_group()
         if rank == 0:
             print(json.dumps({"phase": args.phase, "result": res}), flush=True)
         return 0
 
-    # every rank packs its own layer: seed = rank
-    I = W.cfg2_inputs(seed=rank)
-    B, H, S, D = I["k"].shape
-    k, v = I["k"].to(dev), I["v"].to(dev)
-    imp, reuse = I["importance"].to(dev), I["reuse"].to(dev)
-    budget, sink = I["budget"], I["sink_tokens"]
-
-    codes0 = allocate_precision_codes(imp, "balanced")
-    adm, _ = admit_codes_device(codes0, imp, kv_sensitivity(k, v), budget, B, D, sink, True, True)
-    prev = PackedKVCache.pack(I["k_prev"].to(dev), I["v_prev"].to(dev), None, 16,
-                              plan=PrecisionPlan.from_codes(adm))["packed_kv"]
-
-    def step(kk, vv, ii, rr):
-        codes = allocate_precision_codes(ii, "balanced")
-        sens = kv_sensitivity(kk, vv)
-        a, res = admit_codes_device(codes, ii, sens, budget, B, D, sink, True, True)
-        plan = PrecisionPlan.from_codes(a, reuse_mask=rr)
-        cache = PackedKVCache.pack(kk, vv, None, 16, plan=plan)["packed_kv"]
-        cache.apply_reuse_mask(prev, rr)
-        ku, vu = cache.unpack()
-        return cache, res, ku, vu
-
-    # algorithmic bytes of the step (fixed across steps: same inputs)
-    cache, res, _, _ = step(k, v, imp, reuse)
-    stats = cache.apply_reuse_mask(prev, reuse, return_stats=True)
-    kept = sum(cache._count.values())
-    from shadow_infer_b200.shadowkv.rd_allocator import entry_bytes
-    per_code = {p: int(entry_bytes(p, B, D, 16)) for p in ("fp32", "fp16", "int8", "int4")}
-    # reused rows: entries present in both caches with the same precision; same codes here, so
-    # every flagged stored entry is copied
-    reused_bytes = 0
-    slot = cache._slot
-    flagged = reuse.reshape(-1).bool() & (slot >= 0)
-    for code, p in enumerate(("fp32", "fp16", "int8", "int4")):
-        reused_bytes += int(((slot & 3) == code)[flagged].sum().item()) * per_code[p]
-    assert stats["applied"] == int(flagged.sum().item())
-    parts = step_bytes(B, H, S, D, cache.memory_bytes(), kept, reused_bytes, int(reuse.sum().item()))
-    nbytes = sum(parts.values())
-
     sampler = ClockSampler(local) if rank == 0 else None
     if sampler:
         sampler.start()
-    for _ in range(args.warmup):
-        step(k, v, imp, reuse)
-    # pack-kernel events inside the timed region
-    n_ev = args.steps
-    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n_ev)]
-    t0 = torch.cuda.Event(enable_timing=True)
-    t1 = torch.cuda.Event(enable_timing=True)
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    launches0 = lib.skv_launch_count()
-    t0.record()
-    for i in range(args.steps):
-        PackedKVCache._pack_events = evs[i]
-        step(k, v, imp, reuse)
-    PackedKVCache._pack_events = None
-    t1.record()
-    torch.cuda.synchronize()
-    launches = lib.skv_launch_count() - launches0
-    if world > 1:
-        dist.barrier()
-    elapsed_ms = t0.elapsed_time(t1)
-    pack_ms_in_step = [a.elapsed_time(b) for a, b in evs]
-    # the pack kernel alone, back to back on this step's plan: an L2 flush (a 256 MB fill, ~40 us
-    # of GPU work) precedes each launch, so the host's bucket allocation and launch call overlap
-    # GPU work and the event pair holds the kernel only (inside a step the GPU idles on the host
-    # between the plan's count read-back and the launch, and that gap lands in the events)
-    from shadow_infer_b200.shadowkv.packed_kv_cache import run_pack
-    plan_last = PrecisionPlan.from_codes(admit_codes_device(allocate_precision_codes(imp, "balanced"), imp,
-                                                            kv_sensitivity(k, v), budget, B, D, sink, True,
-                                                            True)[0], reuse_mask=reuse)
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
-    pev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(10)]
-    for i, ev in enumerate(pev):
-        flush.fill_(i & 0xFF)
-        run_pack(k, v, plan_last, 16, events=ev)
-    torch.cuda.synchronize()
-    pack_ms = [a.elapsed_time(b) for a, b in pev[2:]]
-    # every call of the step alone, the same way: each after two L2-flushing fills (~80 us of GPU
-    # work, during which the host enqueues the call), events around the call
-    def alone(fn, n=8):
-        evp = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n)]
-        for i, (a, b) in enumerate(evp):
-            flush.fill_(i & 0xFF)
-            flush.fill_((i + 1) & 0xFF)
-            a.record()
-            fn()
-            b.record()
-        torch.cuda.synchronize()
-        return statistics.mean(a.elapsed_time(b) for a, b in evp[2:])
-    codes_l = allocate_precision_codes(imp, "balanced")
-    sens_l = kv_sensitivity(k, v)
-    adm_l = admit_codes_device(codes_l, imp, sens_l, budget, B, D, sink, True, True)[0]
-    cache_l = PackedKVCache.pack(k, v, None, 16, plan=PrecisionPlan.from_codes(adm_l, reuse_mask=reuse))["packed_kv"]
-    kernel_ms = {
-        "allocate": alone(lambda: allocate_precision_codes(imp, "balanced")),
-        "sensitivity": alone(lambda: kv_sensitivity(k, v)),
-        "admission": alone(lambda: admit_codes_device(codes_l, imp, sens_l, budget, B, D, sink, True, True)),
-        "plan": alone(lambda: PrecisionPlan.from_codes(adm_l, reuse_mask=reuse)),
-        "pack": statistics.mean(pack_ms),
-        "reuse": alone(lambda: cache_l.apply_reuse_mask(prev, reuse)),
-        "unpack": alone(lambda: cache_l.unpack()),
-    }
-    # evict: 25 % of the (t, h) entries (seeded Bernoulli mask) from a freshly packed copy of the
-    # layer each time; the pack is queued before the fills and is not timed
-    gen = torch.Generator(device="cpu").manual_seed(7)
-    evict_mask = (torch.rand(S, H, generator=gen) < 0.25).to(dev)
-    plan_e = PrecisionPlan.from_codes(adm_l)
-    eve = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(8)]
-    evict_after = 0
-    for i, (a, b) in enumerate(eve):
-        ce = PackedKVCache.pack(k, v, None, 16, plan=plan_e)["packed_kv"]
-        flush.fill_(i & 0xFF)
-        flush.fill_((i + 1) & 0xFF)
-        a.record()
-        ce.evict(evict_mask)
-        b.record()
-        evict_after = ce.memory_bytes()
-    torch.cuda.synchronize()
-    kernel_ms["evict"] = statistics.mean(a.elapsed_time(b) for a, b in eve[2:])
-    parts_k = dict(parts)
-    parts_k["evict"] = S * H + 2 * evict_after
-    del flush
-    tmax = torch.tensor([elapsed_ms], device=dev, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(tmax, op=dist.ReduceOp.MAX)
-    elapsed_ms = float(tmax.item())
-    ms_per_step = elapsed_ms / args.steps
-    value = world * nbytes * args.steps / (elapsed_ms / 1e3) / 1e9
-
-    # ---- e2e: pinned host buffers through the public API
-    hk = I["k"].pin_memory()
-    hv = I["v"].pin_memory()
-    himp = I["importance"].pin_memory()
-    hreuse = I["reuse"].pin_memory()
-    # Steps are pipelined over full-duplex PCIe: step i+1's inputs travel host -> device on one
-    # copy stream and step i's packed payload device -> host on another while the data plane
-    # computes on the current stream; device inputs and the host result buffer are double-
-    # buffered.  Every step's copies lie inside the timed region.
-    out_host = [torch.empty(cache.memory_bytes() + 64, dtype=torch.uint8).pin_memory() for _ in range(2)]
-    res_host = [torch.empty(2, dtype=torch.int64).pin_memory() for _ in range(2)]
-    dbuf = [tuple(torch.empty(t.shape, dtype=t.dtype, device=dev) for t in (hk, hv, himp, hreuse)) for _ in range(2)]
-    cs = torch.cuda.current_stream(dev)
-    s_in, s_out = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
-    in_ready = [torch.cuda.Event() for _ in range(2)]
-    in_free = [torch.cuda.Event() for _ in range(2)]
-    n_e2e = [0]
-
-    def e2e_step():
-        j = n_e2e[0] % 2
-        n_e2e[0] += 1
-        with torch.cuda.stream(s_in):
-            s_in.wait_event(in_free[j])            # the compute that read buffer j is done
-            for d, h in zip(dbuf[j], (hk, hv, himp, hreuse)):
-                d.copy_(h, non_blocking=True)
-            in_ready[j].record(s_in)
-        cs.wait_event(in_ready[j])
-        c, r, _, _ = step(*dbuf[j])
-        in_free[j].record(cs)
-        done = torch.cuda.Event()
-        done.record(cs)
-        off = 0
-        with torch.cuda.stream(s_out):
-            s_out.wait_event(done)
-            for d in c.packed_data.values():
-                for key in ("k", "v", "scale_k", "scale_v"):
-                    t = d[key]
-                    if t is None:
-                        continue
-                    nb = t.numel() * t.element_size()
-                    out_host[j][off:off + nb].copy_(t.reshape(-1).view(torch.uint8), non_blocking=True)
-                    t.record_stream(s_out)
-                    off += nb
-            res_host[j].copy_(r, non_blocking=True)
-            r.record_stream(s_out)
-        return off
-
-    e2e_steps = max(3, min(args.steps, 30))
-    for _ in range(3):
-        e2e_step()
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    e0.record(cs)
-    s_in.wait_event(e0)                            # no copy of the timed steps starts before e0
-    d2h = 0
-    for _ in range(e2e_steps):
-        d2h = e2e_step()
-    cs.wait_stream(s_in)
-    cs.wait_stream(s_out)
-    e1.record(cs)
-    torch.cuda.synchronize()
-    e2e_ms = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
-    e2e_ms = float(e2e_ms.item())
-    h2d = (hk.numel() + hv.numel() + himp.numel()) * 4 + hreuse.numel()
-    attn = attention_phase(args, world, rank, dev, dist, lib, tensor_peak()) if not args.no_attention else None
-    gbudget = budget_phase(args, world, rank, dev, lib) if not args.no_attention else None
-    paged = paged_phase(args, world, rank, dev, lib) if not args.no_attention else None
-    decisions = decision_phase(args, world, rank, dev, lib) if not args.no_attention else None
+    head = long_context_phase(args, world, rank, dev, dist, lib)
+    clocks = sampler.summary() if sampler else None
+    torch.cuda.empty_cache()
+    extras = {}
+    if not args.no_extras:
+        extras["cfg2_step"] = cfg2_phase(args, world, rank, dev, dist, lib)
+        torch.cuda.empty_cache()
+        extras["attention_cfg3"] = attention_phase(args, world, rank, dev, dist, lib)
+        torch.cuda.empty_cache()
+        extras["denoise_cfg4"] = denoise_phase(args, world, rank, dev, dist, lib)
+        torch.cuda.empty_cache()
+        if world == 1:
+            extras["global_budget"] = budget_phase(args, world, rank, dev, lib)
+            extras["paged_store"] = paged_phase(args, world, rank, dev, lib)
+            extras["decisions"] = decision_phase(args, world, rank, dev, lib)
     if sampler:
         sampler.stop()
-
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
     if rank != 0:
         return 0
-
-    peak, peak_kind = hbm_peak()
-    pack_avg_ms = statistics.mean(pack_ms)
-    achieved = parts["pack"] / (pack_avg_ms / 1e3) / 1e9
-    traffic = committed_traffic("pack16_kernel_cfg2.md")
     line = {
-        "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "cfg2 data-plane step: codes, sensitivity, budget admission + hard eviction, "
-                               "plan, compress+pack, reuse (50%), unpack",
-                   "B": B, "H": H, "S": S, "D": D, "layers_per_gpu": 1, "budget_bytes": budget,
-                   "l2": "inputs larger than L2 (K+V 268 MB per layer)",
-                   "bytes_per_step": parts},
-        "roofline": {"kernel": "pack16_kernel", "bound": "hbm", "achieved": achieved, "peak": peak,
-                     "unit": "GB/s", "frac": achieved / peak, "peak_source": f"{peak_kind} hbm_gbs",
-                     "traffic": traffic, "algorithmic_bytes": parts["pack"], "avg_launch_ms": pack_avg_ms,
-                     "timing": "events around 8 back-to-back launches on the step's plan, each after a 256 MB "
-                               "L2-flushing fill",
-                     "in_step_avg_launch_ms": statistics.mean(pack_ms_in_step)},
-        "e2e": {"value": world * nbytes * e2e_steps / (e2e_ms / 1e3) / 1e9, "unit": "GB/s",
-                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h + 16, "steps": e2e_steps,
-                "ms_per_step": e2e_ms / e2e_steps,
-                "pipelining": "inputs of step i+1 in and step i's packed payload out on two copy streams "
-                              "while step i computes (PCIe is full duplex); double-buffered"},
-        "gpu_launches": launches,
-        "clocks": sampler.summary() if sampler else None,
-        "kernels": {name: {"avg_ms": ms, "algorithmic_bytes": parts_k[name],
-                           "achieved_gbs": parts_k[name] / (ms / 1e3) / 1e9,
-                           "frac": parts_k[name] / (ms / 1e3) / 1e9 / peak}
-                    for name, ms in kernel_ms.items()},
-        "kernels_timing": "each call of the step alone through its public API, events around it, after two "
-                          "256 MB L2-flushing fills (8 calls, first 2 dropped; pack: the roofline's launches; "
-                          "evict: 25 % of the entries of a freshly packed copy, bytes = mask + 2 x packed bytes "
-                          "after, count + compaction with the host read of the kept counts between); frac of "
-                          "measured HBM",
-        "attention": attn,
-        "global_budget": gbudget,
-        "paged_store": paged,
-        "decisions": decisions,
+        "metric": METRIC, "value": head["value"], "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": head["ms_per_step"], "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+        "config": head["config"],
+        "roofline": head["roofline"],
+        "e2e": head.get("e2e"),
+        "gpu_launches": head["gpu_launches"],
+        "clocks": clocks,
+        "check": head["check"],
+        "data_plane": head["data_plane"],
+        "step_breakdown_ms": head["step_breakdown_ms"],
+        "exchange": head["exchange"],
+        "dtype_note": "attention in fp16 tensor-core operands with fp32 accumulation and softmax; the data plane "
+                      "quantises fp32 K/V to fp16/int8/int4 bit-exactly",
     }
-    if world == 1:
-        run = reference_sample(I, args.ref_heads)
-        run()
-        samples = [run() for _ in range(3)]
-        ref_val = sum(b for _, b in samples) / sum(t for t, _ in samples) / 1e9
-        line["cpu_baseline"] = {
-            "value": ref_val, "unit": "GB/s", "cores": 1, "kind": "port",
-            "sample": f"numpy oracle pipeline on heads 0..{args.ref_heads - 1} of the cfg2 layer, 3 runs",
-        }
+    if "cpu_baseline" in head:
+        line["cpu_baseline"] = head["cpu_baseline"]
+    line.update(extras)
     print(json.dumps(line), flush=True)
     return 0
 

@@ -169,7 +169,9 @@ int skv_head_index(const int32_t* slot, int S, int H, int32_t* rows, int32_t* co
  * attention (shadowinfer/models/simple_diffusion_llm.py:165-169), without materialising the
  * dense fp32 K/V.  The packed rows of each head are dequantised once into fp16 tensor-core tiles
  * in `scratch` (at least skv_packed_attention_scratch_bytes bytes, 16-byte aligned), which
- * every query tile of the head then reads.
+ * every query tile of the head then reads: K as an fp16 pair hi + lo (hi = RNE(k), lo =
+ * RNE(k - hi)) contracted with Q in two MMA chains, so K enters the scores with ~22 bits
+ * (tiles of fp16 entries only are exact and skip the lo chain); V in fp16.
  * q fp16 [B,H,S_q,D], out fp32 [B,H,S_q,D]; D = 64 or 128; error_flag (device int32) is cleared
  * and set non-zero if a pipeline wait timed out (results then invalid). */
 size_t skv_packed_attention_scratch_bytes(int B, int H, int S_kv, int D);
@@ -196,10 +198,10 @@ int skv_attend_kv_tiles(const void* q, int B, int H, int S_q, int D, int S_kv, c
  * Scratch: skv_packed_attention_scratch_bytes(B, H_kv, S_kv + S_new, D). */
 int skv_stage_kv_tiles_gqa(const skv_bucket* buckets, int B, int H_kv, int S_kv, int D, int int4_group,
                            const int32_t* rows, const int32_t* counts, const float* k_new, const float* v_new,
-                           int S_new, void* scratch, size_t scratch_bytes, void* stream);
+                           int S_new, void* scratch, size_t scratch_bytes, int flags, void* stream);
 int skv_attend_kv_tiles_gqa(const void* q, int B, int H_q, int S_q, int D, int H_kv, int S_kv, const int32_t* rows,
                             const int32_t* counts, int S_new, float scale, const void* scratch, size_t scratch_bytes,
-                            float* out, int32_t* error_flag, int max_ctas, void* stream);
+                            float* out, int32_t* error_flag, int max_ctas, int flags, void* stream);
 /* The attention with its outputs stored into n_peers buffers [B, H_out, S_q, D] (device array of
  * device pointers: every rank's output buffer, mapped into this process), this call's query heads
  * at [head_offset, head_offset + H_q): the head-sharded all-gather of the outputs fused into the
@@ -208,7 +210,7 @@ int skv_attend_kv_tiles_gqa(const void* q, int B, int H_q, int S_q, int D, int H
 int skv_attend_kv_tiles_peers(const void* q, int B, int H_q, int S_q, int D, int H_kv, int S_kv, const int32_t* rows,
                               const int32_t* counts, int S_new, float scale, const void* scratch,
                               size_t scratch_bytes, float* const* out_peers, int n_peers, int head_offset,
-                              int H_out, int32_t* error_flag, int max_ctas, void* stream);
+                              int H_out, int32_t* error_flag, int max_ctas, int flags, void* stream);
 /* Peer mappings for out_peers (CUDA IPC between the processes of one node).  export: the
  * skv_ipc_handle_bytes() handle of the allocation holding ptr and ptr's byte offset in it.
  * open (on the device that will launch the kernel): maps another process's exported buffer
@@ -219,11 +221,20 @@ int skv_ipc_export(const void* ptr, void* handle, int64_t* offset);
 int skv_ipc_open(const void* handle, int64_t offset, void** base, void** ptr);
 int skv_ipc_close(void* base);
 /* max_ctas: CTAs of the persistent attention kernel (0 = one per SM); fewer leave SMs free for
- * work that should run beside it (e.g. the NCCL all-gather of the previous layer's outputs). */
+ * work that should run beside it (e.g. the NCCL all-gather of the previous layer's outputs).
+ * flags (the _gqa / _peers entry points; staging and attention take the same flags):
+ *   0                -- K staged as hi + lo fp16 tiles and contracted in two MMA chains (~22 bits;
+ *                       the default, which meets relative L2 1e-3 against the fp32 reference also
+ *                       with channel outliers in K);
+ *   SKV_ATTN_FAST_K  -- K in fp16 only (one MMA chain, two K stages): faster, but K enters the
+ *                       scores with fp16's 2^-11 relative error, which outlier channels of K turn
+ *                       into ~2e-3 relative L2 on the long-context workload. */
+#define SKV_ATTN_FAST_K 1
 int skv_packed_attention_gqa(const void* q, int B, int H_q, int S_q, int D, const skv_bucket* buckets, int H_kv,
                              int S_kv, int int4_group, const int32_t* rows, const int32_t* counts,
                              const float* k_new, const float* v_new, int S_new, float scale, void* scratch,
-                             size_t scratch_bytes, float* out, int32_t* error_flag, int max_ctas, void* stream);
+                             size_t scratch_bytes, float* out, int32_t* error_flag, int max_ctas, int flags,
+                             void* stream);
 
 /* ---- cross-layer budget: KVCacheManager.enforce_global_budget
  * (shadowinfer/shadowkv/kv_cache_manager.py:129-200).  The reference sorts every non-sink

@@ -27,6 +27,8 @@ SKV_ERR_TOO_LARGE = 5
 SKV_ERR_CUDA = 6
 SKV_ERR_UNSUPPORTED = 7
 
+SKV_ATTN_FAST_K = 1   # attention flag: K in fp16 only (include/shadowkv_b200.h)
+
 c_void_p = ctypes.c_void_p
 c_int = ctypes.c_int
 c_int64 = ctypes.c_int64
@@ -83,12 +85,13 @@ _SIGNATURES = {
     "skv_attend_kv_tiles": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_int, c_void_p, c_void_p, ctypes.c_float,
                                     c_void_p, c_size_t, c_void_p, c_void_p, c_void_p]),
     "skv_stage_kv_tiles_gqa": (c_int, [ctypes.POINTER(SkvBucket), c_int, c_int, c_int, c_int, c_int, c_void_p,
-                                       c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_size_t, c_void_p]),
+                                       c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_size_t, c_int, c_void_p]),
     "skv_attend_kv_tiles_gqa": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_int,
-                                        ctypes.c_float, c_void_p, c_size_t, c_void_p, c_void_p, c_int, c_void_p]),
+                                        ctypes.c_float, c_void_p, c_size_t, c_void_p, c_void_p, c_int, c_int,
+                                        c_void_p]),
     "skv_attend_kv_tiles_peers": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_void_p, c_void_p,
                                           c_int, ctypes.c_float, c_void_p, c_size_t, c_void_p, c_int, c_int, c_int,
-                                          c_void_p, c_int, c_void_p]),
+                                          c_void_p, c_int, c_int, c_void_p]),
     "skv_pack_slab_bytes": (c_int64, [ctypes.POINTER(c_int64), c_int, c_int, c_int]),
     "skv_pack_slab": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p,
                               c_void_p, c_int64, c_void_p, c_void_p]),
@@ -98,7 +101,7 @@ _SIGNATURES = {
     "skv_ipc_close": (c_int, [c_void_p]),
     "skv_packed_attention_gqa": (c_int, [c_void_p, c_int, c_int, c_int, c_int, ctypes.POINTER(SkvBucket), c_int, c_int,
                                          c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int, ctypes.c_float,
-                                         c_void_p, c_size_t, c_void_p, c_void_p, c_int, c_void_p]),
+                                         c_void_p, c_size_t, c_void_p, c_void_p, c_int, c_int, c_void_p]),
     "skv_budget_candidates": (c_int, [c_void_p, c_int, c_int, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p,
                                       c_void_p, c_void_p]),
     "skv_rank_select_scratch_bytes": (c_size_t, [c_int64]),

@@ -11,9 +11,11 @@
 //   1. stage_tiles_kernel (skv_stage_kv_tiles), one CTA per (128-row KV tile, head, batch):
 //      gathers the tile's rows from the fp32/fp16/int8/int4 buckets and dequantises them ONCE
 //      into fp16 K and V tiles in exactly the byte layout the tensor cores read (128B-swizzled
-//      atoms of 128 rows x 64 values).  fp32 -> fp16 RNE; fp16 copied; int8 and int4 computed
-//      in fp32 as the reference dequantises (q * scale), then rounded.  Evicted entries are
-//      not staged.  Every query tile of the head reuses the staged tiles (from L2), so the
+//      atoms of 128 rows x 64 values).  K is staged as a pair of fp16 tiles, hi = RNE(k) and
+//      lo = RNE(k - hi), whose sum carries ~22 significant bits of the fp32 value the
+//      reference dequantises (q * scale for int8 / int4, computed in fp32 as the reference
+//      does); V as one fp16 tile (RNE).  A tile whose rows are all fp16 entries is exact in
+//      fp16 and gets no lo tile.  Evicted entries are not staged.  Every query tile of the head reuses the staged tiles (from L2), so the
 //      packed bytes are read and converted once per head instead of once per query tile.
 //   2. packed_attention_kernel (skv_attend_kv_tiles): persistent, one CTA per SM, launched
 //      cooperatively.  A work unit is 256 queries (two 128-row tiles) of one head; the units'
@@ -24,11 +26,12 @@
 //                 and sum (lazy rescale of O_t when the max grows by more than 2^8), and writes
 //                 P_t (fp16) back into TMEM over the first half of S_t's columns; at the end of
 //                 a unit, normalises O_t and stores it.
-//      warp 8     loader: Q tiles by TMA (128B swizzle, no multicast) and the staged K and V
-//                 tiles by bulk asynchronous copies into a two-stage shared-memory ring.
+//      warp 8     loader: Q tiles by TMA (128B swizzle, no multicast), the staged K hi/lo pair
+//                 by one bulk asynchronous copy into a single stage, the V tiles into a
+//                 two-stage ring.
 //      warp 9     MMA issuer (tcgen05.mma kind::f16, M=128, fp32 accumulate):
-//                 S_t = Q_t K_j^T (both operands in shared memory) and O_t += P_t V_j (P read
-//                 from TMEM), interleaved PV_0(j), S_0(j+1), PV_1(j), S_1(j+1) so that the
+//                 S_t = Q_t K_j,hi^T + Q_t K_j,lo^T (both operands in shared memory; the lo
+//                 chain is skipped for exact tiles) and O_t += P_t V_j (P read from TMEM), interleaved PV_0(j), S_0(j+1), PV_1(j), S_1(j+1) so that the
 //                 tensor cores work on one query tile while the other tile's softmax runs.
 //      TMEM: S_0 | S_1 | O_0 | O_1 (128 + 128 + D + D columns).
 // Evicted entries never enter a tile: their contribution (count * 2^(0 - m)) is added to the
@@ -73,7 +76,7 @@ struct AttnLayout {
     static constexpr int NA = D / 64;                   // 128-byte swizzle atoms per row
     static constexpr int kTile = staged_tile_bytes(D);  // one 128-row tile (Q, K or V)
     static constexpr int kQ = 0;                        // two query tiles
-    static constexpr int kK = kQ + 2 * kTile;           // two K stages
+    static constexpr int kK = kQ + 2 * kTile;           // K: one stage of hi + lo tiles, or two hi stages
     static constexpr int kV = kK + 2 * kTile;           // two V stages
     static constexpr int kBar = kV + 2 * kTile;
     static constexpr int kNumBars = 24;
@@ -110,6 +113,7 @@ struct AttnParams {
     int n_peers, head_off, H_out;
     float scale_log2;          // softmax scale * log2(e)
     int* err;
+    int klo;                   // 1: K staged and contracted as hi + lo (one K stage); 0: hi only (two stages)
 };
 
 __device__ __forceinline__ float ex2(float x) {
@@ -137,38 +141,56 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* e
     return __all_sync(0xffffffffu, ok);
 }
 
+// Staged tiles of (batch b, KV head h, tile j): K hi, K lo, V (kStagedTiles of them).
+constexpr int kStagedTiles = 3;
+constexpr int kTileKHi = 0, kTileKLo = 1, kTileV = 2;
 __device__ __forceinline__ int64_t staged_offset(const AttnParams& p, int b, int h, int j, int kv, int tile_bytes) {
-    return ((((int64_t)b * p.H_kv + h) * p.ntmax + j) * 2 + kv) * tile_bytes;
+    return ((((int64_t)b * p.H_kv + h) * p.ntmax + j) * kStagedTiles + kv) * tile_bytes;
+}
+
+// Rows [c0, c1) of a head's row list are its fp16 entries (the list holds fp32, fp16, int8,
+// int4 entries in that order, then the dense new rows).  A tile inside them is exact in fp16.
+struct HeadRows {
+    int f16_begin, f16_end, n_rows;
+    __device__ __forceinline__ void load(const AttnParams& p, int h);
+    int klo;
+    __device__ __forceinline__ bool exact(int j) const {
+        const int lo = j * kBN, hi = min(lo + kBN, n_rows);
+        return !klo || (lo >= f16_begin && hi <= f16_end);
+    }
+};
+__device__ __forceinline__ void HeadRows::load(const AttnParams& p, int h) {
+    const int* c = p.counts + (int64_t)(h / p.rep) * 5;
+    const int c0 = __ldg(c), c1 = __ldg(c + 1), c2 = __ldg(c + 2), c3 = __ldg(c + 3);
+    f16_begin = c0;
+    f16_end = c0 + c1;
+    n_rows = c0 + c1 + c2 + c3 + p.S_new;
+    klo = p.klo;
 }
 
 // ------------------------------------------------------------------------------ staging
-// Eight int4 codes (one word, high nibble first per byte) times a group scale, computed in
-// fp32 exactly as the reference dequantises ((nibble - 8) * scale), then rounded to fp16.
-__device__ __forceinline__ uint4 int4x8_to_half(uint32_t w, float s) {
-    float v[8];
+// Eight int4 codes (one word, high nibble first per byte) times a group scale, in fp32 exactly
+// as the reference dequantises ((nibble - 8) * scale).
+__device__ __forceinline__ void int4x8_to_f32(uint32_t w, float s, float (&v)[8]) {
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
         const uint32_t byte = (w >> (8 * i)) & 0xFFu;
         v[2 * i] = __fmul_rn(__int_as_float(0x4B000000 | (byte >> 4)) - 8388616.0f, s);
         v[2 * i + 1] = __fmul_rn(__int_as_float(0x4B000000 | (byte & 0xF)) - 8388616.0f, s);
     }
-    uint4 r;
-    r.x = half2_bits(__floats2half2_rn(v[0], v[1]));
-    r.y = half2_bits(__floats2half2_rn(v[2], v[3]));
-    r.z = half2_bits(__floats2half2_rn(v[4], v[5]));
-    r.w = half2_bits(__floats2half2_rn(v[6], v[7]));
-    return r;
 }
 
 // Eight int8 codes times the row scale, in fp32 exactly as the reference dequantises
-// (q * scale), then rounded to fp16.  (q ^ 0x80) | 0x4B000000 is 2^23 + q + 128.
-__device__ __forceinline__ uint4 int8x8_scaled_to_half(uint32_t w0, uint32_t w1, float s) {
-    float v[8];
+// (q * scale).  (q ^ 0x80) | 0x4B000000 is 2^23 + q + 128.
+__device__ __forceinline__ void int8x8_to_f32(uint32_t w0, uint32_t w1, float s, float (&v)[8]) {
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
         v[i] = __fmul_rn(__int_as_float(0x4B000000 | (((w0 >> (8 * i)) & 0xFFu) ^ 0x80u)) - 8388736.0f, s);
         v[4 + i] = __fmul_rn(__int_as_float(0x4B000000 | (((w1 >> (8 * i)) & 0xFFu) ^ 0x80u)) - 8388736.0f, s);
     }
+}
+
+__device__ __forceinline__ uint4 f32x8_to_half(const float (&v)[8]) {
     uint4 r;
     r.x = half2_bits(__floats2half2_rn(v[0], v[1]));
     r.y = half2_bits(__floats2half2_rn(v[2], v[3]));
@@ -177,23 +199,41 @@ __device__ __forceinline__ uint4 int8x8_scaled_to_half(uint32_t w0, uint32_t w1,
     return r;
 }
 
-__device__ __forceinline__ uint4 f32x8_bits_to_half(const uint4& a, const uint4& b) {
-    uint4 r;
-    r.x = half2_bits(__floats2half2_rn(__uint_as_float(a.x), __uint_as_float(a.y)));
-    r.y = half2_bits(__floats2half2_rn(__uint_as_float(a.z), __uint_as_float(a.w)));
-    r.z = half2_bits(__floats2half2_rn(__uint_as_float(b.x), __uint_as_float(b.y)));
-    r.w = half2_bits(__floats2half2_rn(__uint_as_float(b.z), __uint_as_float(b.w)));
-    return r;
+// hi = RNE(v), lo = RNE(v - hi) for eight fp32 values (v - hi is exact in fp32).  A K element
+// in fp16 alone is off by up to 2^-11 of itself, and channel outliers of K (a few channels ten
+// times larger than the rest) make that the dominant error of the attention; hi + lo keeps
+// the contraction within ~2^-22.
+__device__ __forceinline__ void f32x8_split(const float (&v)[8], uint4& hi, uint4& lo) {
+    uint32_t h[4], l[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const __half2 hh = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
+        const float2 hf = __half22float2(hh);
+        h[i] = half2_bits(hh);
+        l[i] = half2_bits(__floats2half2_rn(v[2 * i] - hf.x, v[2 * i + 1] - hf.y));
+    }
+    hi = make_uint4(h[0], h[1], h[2], h[3]);
+    lo = make_uint4(l[0], l[1], l[2], l[3]);
+}
+
+__device__ __forceinline__ void f32x8_load(const float* src, float (&v)[8]) {
+    const float4 a = __ldg(reinterpret_cast<const float4*>(src));
+    const float4 b = __ldg(reinterpret_cast<const float4*>(src) + 1);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
 }
 
 // Raw packed bytes of one lane's share of one K row and one V row: chunk `l8` (8 values)
 // of each 64-value atom, plus the row/group scales.  Loaded for several rows before any is
-// converted, so each lane keeps several memory requests in flight.
+// converted, so each lane keeps several memory requests in flight.  fp32 rows (packed fp32
+// entries and the dense new rows) carry V converted at load and a pointer to their K row,
+// which is read when the row is stored (it is split into hi + lo there).
 template <int NA>
 struct RawRow {
-    uint4 k[NA], v[NA];         // fp16 (fp32 rows are converted on load), int8 8 bytes, int4 4 bytes
+    uint4 k[NA], v[NA];         // fp16, int8 8 bytes, int4 4 bytes (unused for K of fp32 rows)
     float sk[NA], sv[NA];
-    int code;                   // 1..3 (fp32 rows arrive as 1), or -1 for a padding row
+    const float* kf;            // fp32 rows: K row
+    int code;                   // 0 fp32 row, 1..3 packed fp16 / int8 / int4, -1 padding row
 };
 
 template <int D>
@@ -203,15 +243,15 @@ __device__ __forceinline__ void load_raw_row(const AttnParams& p, int b, int32_t
     if (e < 0) return;
     const int64_t row = (int64_t)slot_pos(e) * p.B + b;
     const skv_bucket& bb = p.bk.b[r.code];
+    if (r.code == 0) r.kf = reinterpret_cast<const float*>(bb.k) + row * D;
 #pragma unroll
     for (int a = 0; a < NA; ++a) {
         const int d0 = a * 64 + l8 * 8;
         if (r.code == 0) {
-            // rare: converted at once (RNE), which keeps the raw buffer at 16 bytes per chunk
-            const uint4* pk = reinterpret_cast<const uint4*>(reinterpret_cast<const float*>(bb.k) + row * D + d0);
-            const uint4* pv = reinterpret_cast<const uint4*>(reinterpret_cast<const float*>(bb.v) + row * D + d0);
-            r.k[a] = f32x8_bits_to_half(__ldg(pk), __ldg(pk + 1));
-            r.v[a] = f32x8_bits_to_half(__ldg(pv), __ldg(pv + 1));
+            // rare: V converted at once (RNE), K read again when stored
+            float x[8];
+            f32x8_load(reinterpret_cast<const float*>(bb.v) + row * D + d0, x);
+            r.v[a] = f32x8_to_half(x);
         } else if (r.code == 1) {
             r.k[a] = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const __half*>(bb.k) + row * D + d0));
             r.v[a] = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const __half*>(bb.v) + row * D + d0));
@@ -234,45 +274,56 @@ __device__ __forceinline__ void load_raw_row(const AttnParams& p, int b, int32_t
             r.sv[a] = __ldg(bb.scale_v + row * NG + g);
         }
     }
-    if (r.code == 0) r.code = 1;
 }
 
-// One lane's share of dense fp32 row r of (b, KV head h) of k_new / v_new, converted to fp16.
+// One lane's share of dense fp32 row r of (b, KV head h) of k_new / v_new: V converted to fp16,
+// K kept as a pointer (split when stored).
 template <int D>
 __device__ __forceinline__ void load_dense_row(const AttnParams& p, int b, int h, int r, int l8, RawRow<D / 64>& raw) {
     constexpr int NA = D / 64;
-    raw.code = 1;
+    raw.code = 0;
     const int64_t row = (((int64_t)b * p.H_kv + h) * p.S_new + r) * D;
+    raw.kf = p.k_new + row;
 #pragma unroll
     for (int a = 0; a < NA; ++a) {
-        const int d0 = a * 64 + l8 * 8;
-        const uint4* pk = reinterpret_cast<const uint4*>(p.k_new + row + d0);
-        const uint4* pv = reinterpret_cast<const uint4*>(p.v_new + row + d0);
-        raw.k[a] = f32x8_bits_to_half(__ldg(pk), __ldg(pk + 1));
-        raw.v[a] = f32x8_bits_to_half(__ldg(pv), __ldg(pv + 1));
+        float x[8];
+        f32x8_load(p.v_new + row + a * 64 + l8 * 8, x);
+        raw.v[a] = f32x8_to_half(x);
     }
 }
 
-// Converts one lane's share of a K and a V row to fp16 and stores it, 128B-swizzled, at row
-// `r` of the staged tiles (zeros for a padding row).
+// Converts one lane's share of a K and a V row and stores it, 128B-swizzled, at row `r` of the
+// staged tiles: K as hi (and, unless the tile is exact, lo), V in fp16 (zeros for a padding row).
 template <int D>
-__device__ __forceinline__ void store_row(const RawRow<D / 64>& raw, int r, int l8, uint8_t* ktile, uint8_t* vtile) {
+__device__ __forceinline__ void store_row(const RawRow<D / 64>& raw, int r, int l8, uint8_t* khi, uint8_t* klo,
+                                          uint8_t* vtile, bool want_lo) {
     constexpr int NA = D / 64;
 #pragma unroll
     for (int a = 0; a < NA; ++a) {
-        uint4 hk = make_uint4(0, 0, 0, 0), hv = make_uint4(0, 0, 0, 0);
-        if (raw.code == 1) {
+        uint4 hk = make_uint4(0, 0, 0, 0), lk = make_uint4(0, 0, 0, 0), hv = make_uint4(0, 0, 0, 0);
+        float x[8];
+        if (raw.code == 0) {
+            f32x8_load(raw.kf + a * 64 + l8 * 8, x);
+            f32x8_split(x, hk, lk);
+            hv = raw.v[a];
+        } else if (raw.code == 1) {
             hk = raw.k[a];
             hv = raw.v[a];
         } else if (raw.code == 2) {
-            hk = int8x8_scaled_to_half(raw.k[a].x, raw.k[a].y, raw.sk[0]);
-            hv = int8x8_scaled_to_half(raw.v[a].x, raw.v[a].y, raw.sv[0]);
+            int8x8_to_f32(raw.k[a].x, raw.k[a].y, raw.sk[0], x);
+            f32x8_split(x, hk, lk);
+            int8x8_to_f32(raw.v[a].x, raw.v[a].y, raw.sv[0], x);
+            hv = f32x8_to_half(x);
         } else if (raw.code == 3) {
-            hk = int4x8_to_half(raw.k[a].x, raw.sk[a]);
-            hv = int4x8_to_half(raw.v[a].x, raw.sv[a]);
+            int4x8_to_f32(raw.k[a].x, raw.sk[a], x);
+            f32x8_split(x, hk, lk);
+            int4x8_to_f32(raw.v[a].x, raw.sv[a], x);
+            hv = f32x8_to_half(x);
         }
-        *reinterpret_cast<uint4*>(ktile + a * kBN * 128 + sw128_offset(r, l8)) = hk;
-        *reinterpret_cast<uint4*>(vtile + a * kBN * 128 + sw128_offset(r, l8)) = hv;
+        const int off = a * kBN * 128 + sw128_offset(r, l8);
+        *reinterpret_cast<uint4*>(khi + off) = hk;
+        if (want_lo) *reinterpret_cast<uint4*>(klo + off) = lk;
+        *reinterpret_cast<uint4*>(vtile + off) = hv;
     }
 }
 
@@ -282,7 +333,7 @@ __device__ __forceinline__ void store_row(const RawRow<D / 64>& raw, int r, int 
 // The row-list entries are fetched together with the head's counts (entries past the stored
 // rows are discarded afterwards), so a CTA waits for two memory round trips, not three.
 template <int D>
-__global__ void __launch_bounds__(kStageThreads, 3) stage_tiles_kernel(AttnParams p) {
+__global__ void __launch_bounds__(kStageThreads, 2) stage_tiles_kernel(AttnParams p) {
     constexpr int NA = D / 64;
     constexpr int kRowsPerPass = kStageThreads / 8;
     constexpr int kPasses = kBN / kRowsPerPass;
@@ -295,23 +346,26 @@ __global__ void __launch_bounds__(kStageThreads, 3) stage_tiles_kernel(AttnParam
         const int idx = j * kBN + i * kRowsPerPass + rsub;
         e[i] = idx < p.S_kv ? __ldg(hrows + idx) : -1;
     }
-    const int* cnt = p.counts + (int64_t)h * 5;
-    const int n_stored = __ldg(cnt) + __ldg(cnt + 1) + __ldg(cnt + 2) + __ldg(cnt + 3);
-    const int n_rows = n_stored + p.S_new;
-    if (j * kBN >= n_rows) return;
-    uint8_t* ktile = p.stage + staged_offset(p, b, h, j, 0, staged_tile_bytes(D));
-    uint8_t* vtile = ktile + staged_tile_bytes(D);
+    HeadRows hr;
+    hr.load(p, h);
+    const int n_stored = hr.n_rows - p.S_new;
+    if (j * kBN >= hr.n_rows) return;
+    const bool want_lo = !hr.exact(j);
+    const int TB = staged_tile_bytes(D);
+    uint8_t* khi = p.stage + staged_offset(p, b, h, j, kTileKHi, TB);
+    uint8_t* klo = khi + (kTileKLo - kTileKHi) * TB;
+    uint8_t* vtile = khi + (kTileV - kTileKHi) * TB;
     RawRow<NA> raw[kPasses];
 #pragma unroll
     for (int i = 0; i < kPasses; ++i) {
         const int idx = j * kBN + i * kRowsPerPass + rsub;
-        if (idx >= n_stored && idx < n_rows)
+        if (idx >= n_stored && idx < hr.n_rows)
             load_dense_row<D>(p, b, h, idx - n_stored, l8, raw[i]);
         else
             load_raw_row<D>(p, b, idx < n_stored ? e[i] : -1, l8, raw[i]);
     }
 #pragma unroll
-    for (int i = 0; i < kPasses; ++i) store_row<D>(raw[i], i * kRowsPerPass + rsub, l8, ktile, vtile);
+    for (int i = 0; i < kPasses; ++i) store_row<D>(raw[i], i * kRowsPerPass + rsub, l8, khi, klo, vtile, want_lo);
 }
 
 // ------------------------------------------------------------------------------ attention
@@ -529,9 +583,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBar);
     uint64_t* q_full = bars;            // expect_tx arrive + TMA bytes, per segment
     uint64_t* q_empty = bars + 1;       // commit after the segment's last S MMAs
-    uint64_t* k_full = bars + 2;        // [2] ring stages
+    uint64_t* k_full = bars + 2;        // [0]: the single K stage (hi + lo tiles)
     uint64_t* v_full = bars + 4;        // [2]
-    uint64_t* k_empty = bars + 6;       // [2] commit
+    uint64_t* k_empty = bars + 6;       // [0]: commit after the step's last S MMAs
     uint64_t* v_empty = bars + 8;       // [2] commit
     uint64_t* s_full = bars + 10;       // [2] per query tile, commit
     uint64_t* p_full = bars + 12;       // [2] per query tile, 4 softmax warps
@@ -939,21 +993,30 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                         tma_load_2d(smem + L::kQ + t * TB + a * kBM * 128, &qmap, a * 64, qrow + t * kBM, q_full);
                 ++nq;
                 const uint8_t* gkv = p.stage + staged_offset(p, sg.b, sg.h / p.rep, 0, 0, TB);
+                HeadRows hr;
+                hr.load(p, sg.h);
                 for (int j = sg.j0; j < sg.j1; ++j, ++g) {
                     const int s = (int)(g & 1);
-                    if (g >= 2 && !mbar_wait_spin(&k_empty[s], (uint32_t)(((g >> 1) - 1) & 1), p.err, kErrKEmpty)) {
+                    // K: one stage holding the hi tile and, unless the tile is exact, the lo tile;
+                    // hi tiles only (fast K): a two-stage ring
+                    const int ks = p.klo ? 0 : s;
+                    const bool kwait = p.klo ? g >= 1 : g >= 2;
+                    const uint32_t kpar = p.klo ? (uint32_t)((g - 1) & 1) : (uint32_t)(((g >> 1) - 1) & 1);
+                    if (kwait && !mbar_wait_spin(&k_empty[ks], kpar, p.err, kErrKEmpty)) {
                         ok = false;
                         break;
                     }
-                    mbar_arrive_expect_tx(&k_full[s], TB);
-                    bulk_g2s(smem + L::kK + s * TB, gkv + (int64_t)j * 2 * TB, TB, &k_full[s]);
-                    ++nk[s];
+                    const uint32_t kbytes = hr.exact(j) ? TB : 2 * TB;
+                    mbar_arrive_expect_tx(&k_full[ks], kbytes);
+                    bulk_g2s(smem + L::kK + ks * TB, gkv + ((int64_t)j * kStagedTiles + kTileKHi) * TB, kbytes,
+                             &k_full[ks]);
+                    ++nk[ks];
                     if (g >= 2 && !mbar_wait_spin(&v_empty[s], (uint32_t)(((g >> 1) - 1) & 1), p.err, kErrVEmpty)) {
                         ok = false;
                         break;
                     }
                     mbar_arrive_expect_tx(&v_full[s], TB);
-                    bulk_g2s(smem + L::kV + s * TB, gkv + ((int64_t)j * 2 + 1) * TB, TB, &v_full[s]);
+                    bulk_g2s(smem + L::kV + s * TB, gkv + ((int64_t)j * kStagedTiles + kTileV) * TB, TB, &v_full[s]);
                     ++nv[s];
                 }
                 ++si;
@@ -972,13 +1035,25 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             const uint32_t idesc_s = idesc_f16_f32(kBM, kBN, false, false);
             const uint32_t idesc_o = idesc_f16_f32(kBM, D, false, true);
             const uint32_t q_base = smem_u32(smem + L::kQ);
-            auto issue_s = [&](int t, long long g) {
-                const uint32_t k_base = smem_u32(smem + L::kK + (int)(g & 1) * TB);
+            // K stage of step g and the parity of its full barrier
+            auto kstage = [&](long long g) { return p.klo ? 0 : (int)(g & 1); };
+            auto kparity = [&](long long g) { return p.klo ? (uint32_t)(g & 1) : (uint32_t)((g >> 1) & 1); };
+            // S_t = Q_t K_hi^T, then += Q_t K_lo^T unless the tile is exact in fp16
+            auto issue_s = [&](int t, long long g, bool lo) {
+                const uint32_t k_base = smem_u32(smem + L::kK + kstage(g) * TB);
 #pragma unroll
                 for (int k = 0; k < D / 16; ++k) {
                     const uint32_t off = (k >> 2) * (kBN * 128) + (k & 3) * 32;
                     umma_f16(tmem + t * kBN, smem_desc_sw128(q_base + t * TB + off, 16, 1024),
                              smem_desc_sw128(k_base + off, 16, 1024), idesc_s, k > 0 ? 1u : 0u);
+                }
+                if (lo) {
+#pragma unroll
+                    for (int k = 0; k < D / 16; ++k) {
+                        const uint32_t off = (k >> 2) * (kBN * 128) + (k & 3) * 32;
+                        umma_f16(tmem + t * kBN, smem_desc_sw128(q_base + t * TB + off, 16, 1024),
+                                 smem_desc_sw128(k_base + TB + off, 16, 1024), idesc_s, 1u);
+                    }
                 }
             };
             auto issue_pv = [&](int t, long long g, bool acc) {
@@ -995,24 +1070,28 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             bool ok = true, issued = false;
             while (ok && sched.next(sg)) {
                 const int len = sg.j1 - sg.j0;
+                HeadRows hr;
+                hr.load(p, sg.h);
                 if (!mbar_wait_spin(q_full, (uint32_t)(si & 1), p.err, kErrQFull) ||
-                    !mbar_wait_spin(&k_full[g & 1], (uint32_t)((g >> 1) & 1), p.err, kErrKFull)) {
+                    !mbar_wait_spin(&k_full[kstage(g)], kparity(g), p.err, kErrKFull)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
                 // S of the segment's first step; P_t of the previous segment's last step has
                 // been read by its P_t V, issued before (the tensor pipe runs in issue order)
-                issue_s(0, g);
+                const bool lo0 = !hr.exact(sg.j0);
+                issue_s(0, g, lo0);
                 umma_commit(&s_full[0]);
-                issue_s(1, g);
+                issue_s(1, g, lo0);
                 umma_commit(&s_full[1]);
-                umma_commit(&k_empty[g & 1]);
+                umma_commit(&k_empty[kstage(g)]);
                 if (len == 1) umma_commit(q_empty);
                 issued = true;
                 for (int j = 0; j < len; ++j, ++g) {
-                    const int s = (int)(g & 1), s1 = (int)((g + 1) & 1);
+                    const int s = (int)(g & 1);
                     const bool more = j + 1 < len;
+                    const bool lo1 = more && !hr.exact(sg.j0 + j + 1);
                     if (!mbar_wait_spin(&v_full[s], (uint32_t)((g >> 1) & 1), p.err, kErrVFull) ||
                         !mbar_wait_spin(&p_full[0], (uint32_t)(g & 1), p.err, kErrPFull) ||
                         (j == 0 && si > 0 && !mbar_wait_spin(&o_empty[0], (uint32_t)((si - 1) & 1), p.err, kErrOEmpty))) {
@@ -1023,13 +1102,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                     issue_pv(0, g, j > 0);
                     if (!more) umma_commit(&o_full[0]);
                     if (more) {
-                        if (!mbar_wait_spin(&k_full[s1], (uint32_t)(((g + 1) >> 1) & 1), p.err, kErrKFull)) {
+                        if (!mbar_wait_spin(&k_full[kstage(g + 1)], kparity(g + 1), p.err, kErrKFull)) {
                             ok = false;
                             break;
                         }
                         tc_fence_after();
                         // issued after P_0 V: the tensor pipe has read P_0 before S_0 is rewritten
-                        issue_s(0, g + 1);
+                        issue_s(0, g + 1, lo1);
                         umma_commit(&s_full[0]);
                     }
                     if (!mbar_wait_spin(&p_full[1], (uint32_t)(g & 1), p.err, kErrPFull) ||
@@ -1042,9 +1121,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                     umma_commit(&v_empty[s]);
                     if (!more) umma_commit(&o_full[1]);
                     if (more) {
-                        issue_s(1, g + 1);
+                        issue_s(1, g + 1, lo1);
                         umma_commit(&s_full[1]);
-                        umma_commit(&k_empty[s1]);
+                        umma_commit(&k_empty[kstage(g + 1)]);
                         if (j + 2 == len) umma_commit(q_empty);
                     }
                 }
@@ -1171,7 +1250,7 @@ size_t skv_packed_attention_scratch_bytes(int B, int H, int S_kv, int D) {
     if (B <= 0 || H <= 0 || S_kv <= 0 || (D != 64 && D != 128)) return 0;
     const size_t ntmax = (size_t)(S_kv + kBN - 1) / kBN;
     const size_t slots = (size_t)sm_count();
-    return (size_t)B * H * ntmax * 2 * staged_tile_bytes(D)           // staged K/V tiles
+    return (size_t)B * H * ntmax * kStagedTiles * staged_tile_bytes(D)   // staged K hi, K lo, V tiles
            + slots * kUnitRows * D * sizeof(float)                    // partial O
            + slots * kUnitRows * sizeof(float2)                       // partial (max, sum)
            + ((slots * sizeof(int) + 255) & ~size_t(255));            // partial flags
@@ -1185,8 +1264,9 @@ int attn_params(const void* q, int B, int H, int S_q, int D, const skv_bucket* b
                 int int4_group, const int32_t* rows, const int32_t* counts, const float* k_new, const float* v_new,
                 int S_new, float scale, void* scratch, size_t scratch_bytes, float* out, int32_t* error_flag,
                 AttnParams& prm, const char* what, int max_ctas = 0, float* const* peers = nullptr,
-                int n_peers = 0, int head_off = 0, int H_out = 0) {
+                int n_peers = 0, int head_off = 0, int H_out = 0, int flags = 0) {
     if (!rows || !counts || !scratch) return fail(SKV_ERR_INVALID_ARGUMENT, "%s: null pointer", what);
+    if (flags & ~SKV_ATTN_FAST_K) return fail(SKV_ERR_INVALID_ARGUMENT, "%s: unknown flags 0x%x", what, flags);
     if (B <= 0 || H <= 0 || S_q <= 0 || S_kv <= 0 || H_kv <= 0 || S_new < 0)
         return fail(SKV_ERR_INVALID_ARGUMENT, "%s: bad shape", what);
     if (H % H_kv) return fail(SKV_ERR_SHAPE, "%s: %d query heads do not group over %d KV heads", what, H, H_kv);
@@ -1231,7 +1311,7 @@ int attn_params(const void* q, int B, int H, int S_q, int D, const skv_bucket* b
     prm.stage = reinterpret_cast<uint8_t*>(scratch);
     prm.ntmax = (S_kv + S_new + kBN - 1) / kBN;
     prm.slots = max_ctas > 0 && max_ctas < sm_count() ? max_ctas : sm_count();
-    uint8_t* part = prm.stage + (size_t)B * H_kv * prm.ntmax * 2 * staged_tile_bytes(D);
+    uint8_t* part = prm.stage + (size_t)B * H_kv * prm.ntmax * kStagedTiles * staged_tile_bytes(D);
     prm.part_o = reinterpret_cast<float*>(part);
     part += (size_t)prm.slots * kUnitRows * D * sizeof(float);
     prm.part_ml = reinterpret_cast<float2*>(part);
@@ -1245,6 +1325,7 @@ int attn_params(const void* q, int B, int H, int S_q, int D, const skv_bucket* b
     prm.QP = (S_q + kUnitRows - 1) / kUnitRows;
     prm.scale_log2 = scale * 1.4426950408889634f;
     prm.err = error_flag;
+    prm.klo = (flags & SKV_ATTN_FAST_K) ? 0 : 1;
     return SKV_OK;
 }
 
@@ -1254,11 +1335,12 @@ extern "C" {
 
 int skv_stage_kv_tiles_gqa(const skv_bucket* buckets, int B, int H_kv, int S_kv, int D, int int4_group,
                            const int32_t* rows, const int32_t* counts, const float* k_new, const float* v_new,
-                           int S_new, void* scratch, size_t scratch_bytes, void* stream) {
+                           int S_new, void* scratch, size_t scratch_bytes, int flags, void* stream) {
     if (!buckets) return fail(SKV_ERR_INVALID_ARGUMENT, "stage_kv_tiles: null pointer");
     AttnParams prm;
     const int st = attn_params(nullptr, B, H_kv, 1, D, buckets, H_kv, S_kv, int4_group, rows, counts, k_new, v_new,
-                               S_new, 1.0f, scratch, scratch_bytes, nullptr, nullptr, prm, "stage_kv_tiles");
+                               S_new, 1.0f, scratch, scratch_bytes, nullptr, nullptr, prm, "stage_kv_tiles", 0,
+                               nullptr, 0, 0, 0, flags);
     if (st != SKV_OK) return st;
     const dim3 grid((unsigned)prm.ntmax, (unsigned)H_kv, (unsigned)B);
     if (D == 128)
@@ -1271,7 +1353,7 @@ int skv_stage_kv_tiles_gqa(const skv_bucket* buckets, int B, int H_kv, int S_kv,
 int skv_stage_kv_tiles(const skv_bucket* buckets, int B, int H, int S_kv, int D, int int4_group, const int32_t* rows,
                        const int32_t* counts, void* scratch, size_t scratch_bytes, void* stream) {
     return skv_stage_kv_tiles_gqa(buckets, B, H, S_kv, D, int4_group, rows, counts, nullptr, nullptr, 0, scratch,
-                                  scratch_bytes, stream);
+                                  scratch_bytes, 0, stream);
 }
 
 }  // extern "C"
@@ -1329,7 +1411,7 @@ extern "C" {
 int skv_attend_kv_tiles_peers(const void* q, int B, int H_q, int S_q, int D, int H_kv, int S_kv, const int32_t* rows,
                               const int32_t* counts, int S_new, float scale, const void* scratch,
                               size_t scratch_bytes, float* const* out_peers, int n_peers, int head_offset,
-                              int H_out, int32_t* error_flag, int max_ctas, void* stream) {
+                              int H_out, int32_t* error_flag, int max_ctas, int flags, void* stream) {
     if (!q || !out_peers || !error_flag || n_peers <= 0)
         return fail(SKV_ERR_INVALID_ARGUMENT, "attend_kv_tiles_peers: null pointer or no peers");
     if (n_peers > 64 || head_offset < 0 || H_out < head_offset + H_q)
@@ -1341,7 +1423,7 @@ int skv_attend_kv_tiles_peers(const void* q, int B, int H_q, int S_q, int D, int
     float* placeholder = reinterpret_cast<float*>(const_cast<void*>(scratch));
     const int st = attn_params(q, B, H_q, S_q, D, nullptr, H_kv, S_kv, 0, rows, counts, staged, staged, S_new, scale,
                                const_cast<void*>(scratch), scratch_bytes, placeholder, error_flag, prm,
-                               "attend_kv_tiles_peers", max_ctas, out_peers, n_peers, head_offset, H_out);
+                               "attend_kv_tiles_peers", max_ctas, out_peers, n_peers, head_offset, H_out, flags);
     if (st != SKV_OK) return st;
     cudaStream_t s = as_stream(stream);
     if (cudaMemsetAsync(error_flag, 0, sizeof(int32_t), s) != cudaSuccess)
@@ -1351,7 +1433,7 @@ int skv_attend_kv_tiles_peers(const void* q, int B, int H_q, int S_q, int D, int
 
 int skv_attend_kv_tiles_gqa(const void* q, int B, int H_q, int S_q, int D, int H_kv, int S_kv, const int32_t* rows,
                             const int32_t* counts, int S_new, float scale, const void* scratch, size_t scratch_bytes,
-                            float* out, int32_t* error_flag, int max_ctas, void* stream) {
+                            float* out, int32_t* error_flag, int max_ctas, int flags, void* stream) {
     if (!q || !out || !error_flag) return fail(SKV_ERR_INVALID_ARGUMENT, "attend_kv_tiles: null pointer");
     AttnParams prm;
     // the dense rows are already staged: only their count matters here (a non-null placeholder
@@ -1359,7 +1441,7 @@ int skv_attend_kv_tiles_gqa(const void* q, int B, int H_q, int S_q, int D, int H
     const float* staged = S_new > 0 ? reinterpret_cast<const float*>(scratch) : nullptr;
     const int st = attn_params(q, B, H_q, S_q, D, nullptr, H_kv, S_kv, 0, rows, counts, staged, staged, S_new, scale,
                                const_cast<void*>(scratch), scratch_bytes, out, error_flag, prm, "attend_kv_tiles",
-                               max_ctas);
+                               max_ctas, nullptr, 0, 0, 0, flags);
     if (st != SKV_OK) return st;
     cudaStream_t s = as_stream(stream);
     if (cudaMemsetAsync(error_flag, 0, sizeof(int32_t), s) != cudaSuccess)
@@ -1371,27 +1453,28 @@ int skv_attend_kv_tiles(const void* q, int B, int H, int S_q, int D, int S_kv, c
                         const int32_t* counts, float scale, const void* scratch, size_t scratch_bytes, float* out,
                         int32_t* error_flag, void* stream) {
     return skv_attend_kv_tiles_gqa(q, B, H, S_q, D, H, S_kv, rows, counts, 0, scale, scratch, scratch_bytes, out,
-                                   error_flag, 0, stream);
+                                   error_flag, 0, 0, stream);
 }
 
 int skv_packed_attention_gqa(const void* q, int B, int H_q, int S_q, int D, const skv_bucket* buckets, int H_kv,
                              int S_kv, int int4_group, const int32_t* rows, const int32_t* counts,
                              const float* k_new, const float* v_new, int S_new, float scale, void* scratch,
-                             size_t scratch_bytes, float* out, int32_t* error_flag, int max_ctas, void* stream) {
+                             size_t scratch_bytes, float* out, int32_t* error_flag, int max_ctas, int flags,
+                             void* stream) {
     if (!q || !buckets || !out || !error_flag) return fail(SKV_ERR_INVALID_ARGUMENT, "packed_attention: null pointer");
     if (H_kv <= 0 || H_q % H_kv) return fail(SKV_ERR_SHAPE, "packed_attention: %d query heads over %d KV heads", H_q, H_kv);
     const int st = skv_stage_kv_tiles_gqa(buckets, B, H_kv, S_kv, D, int4_group, rows, counts, k_new, v_new, S_new,
-                                          scratch, scratch_bytes, stream);
+                                          scratch, scratch_bytes, flags, stream);
     if (st != SKV_OK) return st;
     return skv_attend_kv_tiles_gqa(q, B, H_q, S_q, D, H_kv, S_kv, rows, counts, S_new, scale, scratch, scratch_bytes,
-                                   out, error_flag, max_ctas, stream);
+                                   out, error_flag, max_ctas, flags, stream);
 }
 
 int skv_packed_attention(const void* q, int B, int H, int S_q, int D, const skv_bucket* buckets, int S_kv,
                          int int4_group, const int32_t* rows, const int32_t* counts, float scale, void* scratch,
                          size_t scratch_bytes, float* out, int32_t* error_flag, void* stream) {
     return skv_packed_attention_gqa(q, B, H, S_q, D, buckets, H, S_kv, int4_group, rows, counts, nullptr, nullptr, 0,
-                                    scale, scratch, scratch_bytes, out, error_flag, 0, stream);
+                                    scale, scratch, scratch_bytes, out, error_flag, 0, 0, stream);
 }
 
 }  // extern "C"

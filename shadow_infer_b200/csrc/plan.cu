@@ -7,7 +7,8 @@
 //  * skv_plan_bucket         -- PrecisionPlan.from_codes (precision_plan.py:113-177): a
 //                               stable 5-way partition of the int8 [S,H] codes in
 //                               token-major order plus the reuse-list compaction, done as
-//                               a tile-count pass and a scan+scatter pass (no sort).
+//                               a tile-count pass, a scan over the tile counts and a
+//                               scatter pass (no sort).
 #include <math.h>
 
 #include <mutex>
@@ -157,54 +158,82 @@ __global__ void __launch_bounds__(kPlanThreads) plan_count_kernel(
         field(tl, th, threadIdx.x);
 }
 
-__global__ void __launch_bounds__(kPlanThreads) plan_scatter_kernel(
-    const int8_t* __restrict__ codes, const uint8_t* __restrict__ reuse, int64_t n, int S, int H,
-    const int* __restrict__ tile_counts, int num_tiles, int64_t* __restrict__ flat_out,
-    int32_t* __restrict__ slot_out, int64_t* __restrict__ reuse_out, int64_t* __restrict__ counts) {
-    // 1. prefix of previous tiles and totals, per category
-    __shared__ long long s_red[kPlanThreads / 32][2 * kPlanCats];
-    __shared__ long long s_prefix[kPlanCats], s_total[kPlanCats], s_base[kPlanCats];
-    long long pre[kPlanCats], tot[kPlanCats];
-#pragma unroll
-    for (int k = 0; k < kPlanCats; ++k) pre[k] = tot[k] = 0;
-    for (int t = threadIdx.x; t < num_tiles; t += kPlanThreads) {
+// Exclusive prefix over the tiles of each category's tile count, in place, and the category
+// totals into counts[0..5]: one block walks the tiles kPrefixThreads at a time with a running
+// carry, so every scatter block then reads its own prefix only (the work grows linearly with
+// the number of tiles).  Prefixes stay below 2^31: S*H is limited to 2^29.
+constexpr int kPrefixThreads = 1024;
+__global__ void __launch_bounds__(kPrefixThreads) plan_prefix_kernel(int* __restrict__ tile_counts, int num_tiles,
+                                                                      int64_t* __restrict__ counts) {
+    __shared__ int s_warp[kPrefixThreads / 32][kPlanCats];
+    __shared__ int s_chunk[kPlanCats];
+    __shared__ long long s_carry[kPlanCats];
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    if (threadIdx.x < kPlanCats) s_carry[threadIdx.x] = 0;
+    __syncthreads();
+    for (int base = 0; base < num_tiles; base += kPrefixThreads) {
+        const int t = base + threadIdx.x;
+        int v[kPlanCats], incl[kPlanCats];
 #pragma unroll
         for (int k = 0; k < kPlanCats; ++k) {
-            const long long v = tile_counts[(int64_t)t * kPlanStride + k];
-            tot[k] += v;
-            if (t < (int)blockIdx.x) pre[k] += v;
+            v[k] = t < num_tiles ? tile_counts[(int64_t)t * kPlanStride + k] : 0;
+            incl[k] = v[k];
         }
-    }
-    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
 #pragma unroll
-    for (int k = 0; k < kPlanCats; ++k) {
-        const long long a = warp_sum_ll(pre[k]);
-        const long long b = warp_sum_ll(tot[k]);
-        if (lane == 0) {
-            s_red[w][k] = a;
-            s_red[w][kPlanCats + k] = b;
+        for (int o = 1; o < 32; o <<= 1) {
+#pragma unroll
+            for (int k = 0; k < kPlanCats; ++k) {
+                const int x = __shfl_up_sync(0xffffffffu, incl[k], o);
+                if (lane >= o) incl[k] += x;
+            }
         }
-    }
-    __syncthreads();
-    if (threadIdx.x < kPlanCats) {
-        long long a = 0, b = 0;
-        for (int q = 0; q < kPlanThreads / 32; ++q) {
-            a += s_red[q][threadIdx.x];
-            b += s_red[q][kPlanCats + threadIdx.x];
+        if (lane == 31) {
+#pragma unroll
+            for (int k = 0; k < kPlanCats; ++k) s_warp[w][k] = incl[k];
         }
-        s_prefix[threadIdx.x] = a;
-        s_total[threadIdx.x] = b;
+        __syncthreads();
+        if (w == 0) {
+            // exclusive scan of the 32 warp totals of each category; the last lane holds the chunk total
+#pragma unroll
+            for (int k = 0; k < kPlanCats; ++k) {
+                const int x = s_warp[lane][k];
+                int y = x;
+#pragma unroll
+                for (int o = 1; o < 32; o <<= 1) {
+                    const int z = __shfl_up_sync(0xffffffffu, y, o);
+                    if (lane >= o) y += z;
+                }
+                s_warp[lane][k] = y - x;
+                if (lane == 31) s_chunk[k] = y;
+            }
+        }
+        __syncthreads();
+        if (t < num_tiles) {
+#pragma unroll
+            for (int k = 0; k < kPlanCats; ++k)
+                tile_counts[(int64_t)t * kPlanStride + k] = (int)(s_carry[k] + s_warp[w][k] + incl[k] - v[k]);
+        }
+        __syncthreads();
+        if (threadIdx.x < kPlanCats) s_carry[threadIdx.x] += s_chunk[threadIdx.x];
+        __syncthreads();
     }
-    __syncthreads();
+    if (threadIdx.x < kPlanCats) counts[threadIdx.x] = s_carry[threadIdx.x];
+}
+
+__global__ void __launch_bounds__(kPlanThreads) plan_scatter_kernel(
+    const int8_t* __restrict__ codes, const uint8_t* __restrict__ reuse, int64_t n, int S, int H,
+    const int* __restrict__ tile_prefix, const int64_t* __restrict__ counts, int64_t* __restrict__ flat_out,
+    int32_t* __restrict__ slot_out, int64_t* __restrict__ reuse_out) {
+    // 1. this tile's prefix per category (plan_prefix_kernel) and the bucket bases in flat_out
+    __shared__ long long s_prefix[kPlanCats], s_base[kPlanCats];
+    if (threadIdx.x < kPlanCats) s_prefix[threadIdx.x] = tile_prefix[(int64_t)blockIdx.x * kPlanStride + threadIdx.x];
     if (threadIdx.x == 0) {
         long long base = 0;
         for (int k = 0; k < 5; ++k) {
             s_base[k] = base;
-            base += s_total[k];
+            base += counts[k];
         }
         s_base[5] = 0;
-        if (blockIdx.x == 0)
-            for (int k = 0; k < kPlanCats; ++k) counts[k] = s_total[k];
     }
     __syncthreads();
 
@@ -292,15 +321,18 @@ int skv_plan_bucket_static(const int8_t* codes, const uint8_t* reuse_mask, int S
     int* tc = nullptr;
     int st = static_plan_scratch(&tc);
     if (st) return st;
-    // every tile count read by plan_scatter_kernel is written by plan_count_kernel of the
-    // same call, so nothing left over from an earlier call needs clearing
+    // every tile count the prefix and scatter kernels read is written by plan_count_kernel of
+    // the same call, so nothing left over from an earlier call needs clearing
     const int tiles = (int)((n + kPlanTile - 1) / kPlanTile);
     cudaStream_t s = as_stream(stream);
     plan_count_kernel<<<tiles, kPlanThreads, 0, s>>>(codes, reuse_mask, n, tc);
     st = check_launch("plan_count");
     if (st) return st;
-    plan_scatter_kernel<<<tiles, kPlanThreads, 0, s>>>(codes, reuse_mask, n, S, H, tc, tiles, flat_out, slot_out,
-                                                       reuse_flat_out, counts);
+    plan_prefix_kernel<<<1, kPrefixThreads, 0, s>>>(tc, tiles, counts);
+    st = check_launch("plan_prefix");
+    if (st) return st;
+    plan_scatter_kernel<<<tiles, kPlanThreads, 0, s>>>(codes, reuse_mask, n, S, H, tc, counts, flat_out, slot_out,
+                                                       reuse_flat_out);
     return check_launch("plan_scatter");
 }
 
@@ -357,8 +389,11 @@ int skv_plan_bucket(const int8_t* codes, const uint8_t* reuse_mask, int S, int H
     plan_count_kernel<<<tiles, kPlanThreads, 0, s>>>(codes, reuse_mask, n, tc);
     int st = check_launch("plan_count");
     if (st) return st;
-    plan_scatter_kernel<<<tiles, kPlanThreads, 0, s>>>(codes, reuse_mask, n, S, H, tc, tiles, flat_out,
-                                                       slot_out, reuse_flat_out, counts);
+    plan_prefix_kernel<<<1, kPrefixThreads, 0, s>>>(tc, tiles, counts);
+    st = check_launch("plan_prefix");
+    if (st) return st;
+    plan_scatter_kernel<<<tiles, kPlanThreads, 0, s>>>(codes, reuse_mask, n, S, H, tc, counts, flat_out, slot_out,
+                                                       reuse_flat_out);
     return check_launch("plan_scatter");
 }
 

@@ -9,7 +9,7 @@ from .kv_cache_manager import (
     TokenHeadScore,
 )
 from .importance_model import compute_irap_importance
-from .packed_attention import packed_attention
+from .packed_attention import packed_attention, packed_block_forward
 from .packed_kv_cache import PackedKVCache
 from .paged_kv_store import PagedKVStore
 from .precision_plan import (
@@ -26,7 +26,7 @@ from .rd_allocator import admit_budget, admit_codes, entry_bytes, kv_sensitivity
 __all__ = [
     "PackedKVCache", "PrecisionPlan", "map_to_codes", "codes_to_map", "PRECISION_ORDER", "PRECISION_CODES",
     "CODE_PRECISIONS", "EVICTED", "admit_codes", "admit_budget", "entry_bytes", "kv_sensitivity",
-    "predict_codes_bytes", "packed_attention", "KVCacheManager", "KVCacheEntry", "TokenHeadScore",
+    "predict_codes_bytes", "packed_attention", "packed_block_forward", "KVCacheManager", "KVCacheEntry", "TokenHeadScore",
     "EvictionPolicy", "LeastImportantEvictionPolicy", "ImportanceAgeEvictionPolicy", "PagedKVStore",
     "compute_irap_importance",
 ]

@@ -34,6 +34,8 @@ def packed_attention(
     max_ctas: int = 0,
     peer_outputs=None,
     head_offset: int = 0,
+    attention_mask: Optional[torch.Tensor] = None,
+    fast_k: bool = False,
 ) -> torch.Tensor:
     """Non-causal attention of ``q`` [B, H_q, S_q, D] over a packed cache; returns fp32 [B, H_q, S_q, D].
 
@@ -53,7 +55,22 @@ def packed_attention(
     ``peer_outputs`` (a ``sharding.PeerOutputs`` of shape [B, H_total, S_q, D]): the kernel stores
     each finished output row into every rank's buffer, at heads ``[head_offset, head_offset +
     H_q)``, over NVLink -- the all-gather of head-sharded outputs fused into the attention
-    epilogue.  Returns the local buffer, complete once every rank's call has finished.
+    epilogue.  Returns the local buffer, complete only once EVERY rank's call has finished: the
+    caller synchronises all ranks (a stream-ordered collective such as a one-element NCCL
+    all-reduce after the call, or a stream synchronize plus ``torch.distributed.barrier``)
+    before reading it, and again before the next call that writes the same buffers, so that
+    no rank overwrites a buffer another rank is still reading.
+
+    Precision: Q, V and the softmax weights P are fp16 tensor-core operands, K enters as an fp16
+    pair hi + lo (~22 bits) contracted in two MMA chains, accumulation and softmax are fp32:
+    relative L2 <= 1e-3 against the reference's fp32 attention, also when K has outlier
+    channels.  ``fast_k=True`` stages K in fp16 only (one MMA chain): faster, with fp16's 2^-11
+    relative error on every K element, which channel outliers of K turn into ~2e-3.
+
+    ``attention_mask``: accepted for the reference's signature; like
+    ``SimpleDiffusionLLM._compute_block`` (simple_diffusion_llm.py:140-142), which raises when an
+    additive mask meets a KV cache, a mask together with a packed past raises ``ValueError``
+    (the packed path always attends over a past).
     """
     if q.dim() != 4:
         raise ValueError(f"q must be 4-D [batch, heads, seq, head_dim], got shape {tuple(q.shape)}")
@@ -67,6 +84,8 @@ def packed_attention(
         )
     if (k_new is None) != (v_new is None):
         raise ValueError("k_new and v_new must be given together")
+    if attention_mask is not None:
+        raise ValueError("attention_mask is not supported together with kv_cache")
     S_new = 0
     if k_new is not None:
         if k_new.dim() != 4 or tuple(k_new.shape) != tuple(v_new.shape) or \
@@ -93,6 +112,7 @@ def packed_attention(
     tiles = scratch(lib.skv_packed_attention_scratch_bytes(B, H_kv, c.seq_len + S_new, D), dev)
     stream = _lib.stream_of(dev)
     g = c._int4_group_of()
+    flags = _lib.SKV_ATTN_FAST_K if fast_k else 0
     if peer_outputs is not None:
         Bp, Hp, Sp, Dp = peer_outputs.shape
         if (Bp, Sp, Dp) != (B, S_q, D) or not 0 <= head_offset <= Hp - H:
@@ -102,14 +122,15 @@ def packed_attention(
             if events is not None:
                 events[0].record()
             st = lib.skv_stage_kv_tiles_gqa(arr, B, H_kv, c.seq_len, D, g, _lib.ptr(rows), _lib.ptr(counts),
-                                            _lib.ptr(kn), _lib.ptr(vn), S_new, _lib.ptr(tiles), tiles.numel(), stream)
+                                            _lib.ptr(kn), _lib.ptr(vn), S_new, _lib.ptr(tiles), tiles.numel(), flags,
+                                            stream)
             _lib.check(st, "packed_attention")
             if events is not None:
                 events[1].record()
             st = lib.skv_attend_kv_tiles_peers(_lib.ptr(qd), B, H, S_q, D, H_kv, c.seq_len, _lib.ptr(rows),
                                                _lib.ptr(counts), S_new, float(scale), _lib.ptr(tiles), tiles.numel(),
                                                _lib.ptr(peer_outputs.ptrs), peer_outputs.world, int(head_offset), Hp,
-                                               _lib.ptr(err), int(max_ctas), stream)
+                                               _lib.ptr(err), int(max_ctas), flags, stream)
             if events is not None:
                 events[2].record()
         _lib.check(st, "packed_attention")
@@ -123,16 +144,17 @@ def packed_attention(
             st = lib.skv_packed_attention_gqa(_lib.ptr(qd), B, H, S_q, D, arr, H_kv, c.seq_len, g, _lib.ptr(rows),
                                               _lib.ptr(counts), _lib.ptr(kn), _lib.ptr(vn), S_new, float(scale),
                                               _lib.ptr(tiles), tiles.numel(), _lib.ptr(out), _lib.ptr(err),
-                                              int(max_ctas), stream)
+                                              int(max_ctas), flags, stream)
         else:
             events[0].record()
             st = lib.skv_stage_kv_tiles_gqa(arr, B, H_kv, c.seq_len, D, g, _lib.ptr(rows), _lib.ptr(counts),
-                                            _lib.ptr(kn), _lib.ptr(vn), S_new, _lib.ptr(tiles), tiles.numel(), stream)
+                                            _lib.ptr(kn), _lib.ptr(vn), S_new, _lib.ptr(tiles), tiles.numel(), flags,
+                                            stream)
             _lib.check(st, "packed_attention")
             events[1].record()
             st = lib.skv_attend_kv_tiles_gqa(_lib.ptr(qd), B, H, S_q, D, H_kv, c.seq_len, _lib.ptr(rows),
                                              _lib.ptr(counts), S_new, float(scale), _lib.ptr(tiles), tiles.numel(),
-                                             _lib.ptr(out), _lib.ptr(err), int(max_ctas), stream)
+                                             _lib.ptr(out), _lib.ptr(err), int(max_ctas), flags, stream)
             events[2].record()
     _lib.check(st, "packed_attention")
     if check:
@@ -140,3 +162,29 @@ def packed_attention(
         if code:
             raise RuntimeError(f"packed_attention: a pipeline wait timed out inside the kernel (code {code})")
     return back(out, q.device)
+
+
+def packed_block_forward(block, hidden: torch.Tensor, kv_cache: PackedKVCache, fast_k: bool = False):
+    """``DiffusionTransformerBlock._compute_block`` (shadowinfer/models/simple_diffusion_llm.py:
+    122-180) for ``kv_execution="packed"``: the block's own modules (``ln1``, ``q_proj`` /
+    ``k_proj`` / ``v_proj`` / ``o_proj``, ``ln2``, ``up_proj`` / ``down_proj``; ``num_heads``,
+    ``head_dim``, ``hidden_dim``) run as in the reference, and the attention over
+    ``cat((past, new), dim=2)`` reads the past from the packed cache through ``packed_attention``
+    (the past is never unpacked, pytorch_backend.py:302-304).
+
+    ``hidden`` [B, S, hidden_dim].  Returns ``(hidden_out, k_new, v_new)``: the reference's
+    first three results (its ``k_full`` / ``v_full`` / attention weights are not formed).
+    """
+    import torch.nn.functional as F
+
+    batch, seq_len, _ = hidden.shape
+    nh, hd = int(block.num_heads), int(block.head_dim)
+    normed = block.ln1(hidden)
+    q = block.q_proj(normed).view(batch, seq_len, nh, hd).transpose(1, 2)
+    k = block.k_proj(normed).view(batch, seq_len, nh, hd).transpose(1, 2)
+    v = block.v_proj(normed).view(batch, seq_len, nh, hd).transpose(1, 2)
+    attn = packed_attention(q, kv_cache, k_new=k, v_new=v, fast_k=fast_k)
+    attn_out = attn.transpose(1, 2).contiguous().view(batch, seq_len, int(block.hidden_dim))
+    hidden = hidden + block.o_proj(attn_out)
+    hidden = hidden + block.down_proj(F.gelu(block.up_proj(block.ln2(hidden))))
+    return hidden, k, v

@@ -144,11 +144,12 @@ class PeerOutputs:
             raise RuntimeError(f"PeerOutputs: ranks {failed} could not export their buffer"
                                + (f" ({export_error})" if export_error else ""))
         ptrs = []
+        error = None
         with device_ctx(dev):
             for i, (h, off, numel) in enumerate(entries):
                 if numel != self.local.numel():
-                    self.close()
-                    raise ValueError(f"PeerOutputs: rank {i} has {numel} elements, this rank {self.local.numel()}")
+                    error = ValueError(f"PeerOutputs: rank {i} has {numel} elements, this rank {self.local.numel()}")
+                    break
                 if i == r:
                     ptrs.append(self.local.data_ptr())
                     continue
@@ -156,10 +157,20 @@ class PeerOutputs:
                 p = ctypes.c_void_p()
                 st = lib.skv_ipc_open(ctypes.create_string_buffer(h, hb), off, ctypes.byref(base), ctypes.byref(p))
                 if st != 0:
-                    self.close()
-                _lib.check(st, "PeerOutputs")
+                    error = RuntimeError(f"PeerOutputs: opening rank {i}'s buffer failed: {_lib.last_error()}")
+                    break
                 self._bases.append(base.value)
                 ptrs.append(int(p.value))
+        # every rank learns whether every rank mapped all its peers, so that a failure on one rank
+        # raises on all of them together instead of leaving the others blocked in a later collective
+        opened = [None] * n
+        dist.all_gather_object(opened, None if error is None else str(error), group=group)
+        failed = [i for i, e in enumerate(opened) if e is not None]
+        if failed:
+            self.close()
+            if error is not None:
+                raise error
+            raise RuntimeError(f"PeerOutputs: ranks {failed} could not map their peers' buffers ({opened[failed[0]]})")
         self.ptrs = torch.tensor(ptrs, dtype=torch.int64, device=dev)
 
     @property

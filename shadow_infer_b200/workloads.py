@@ -62,6 +62,109 @@ def kv_tensors(
     return k.contiguous(), v.contiguous()
 
 
+def _head_seed(seed: int, h: int, salt: int = 0) -> int:
+    return int(seed) * 1_000_003 + int(salt) * 7_919 + int(h)
+
+
+def kv_heads(
+    B: int, S: int, D: int, seed: int, h0: int, h1: int,
+    outlier_frac: float = 0.01, outlier_scale: float = 8.0,
+    outlier_channels: int = 0, outlier_channel_scale: float = 10.0,
+) -> Tuple[torch.Tensor, torch.Tensor]:
+    """K, V ~ N(0,1) fp32 [B, h1-h0, S, D] for heads [h0, h1) of a layer, each head drawn from
+    its own generator, so that any head slice is generated alone with the same bits as in the
+    whole layer (the long-context and batched workloads, whose layers are 1 GB / 537 MB of
+    fp32 K/V).  Per head, in order: K, V, the 1 % Bernoulli x8 outlier masks of K and V, and
+    ``outlier_channels`` channels of K scaled by ``outlier_channel_scale``."""
+    ks, vs = [], []
+    for h in range(h0, h1):
+        g = torch.Generator().manual_seed(_head_seed(seed, h))
+        k = torch.randn(B, S, D, generator=g)
+        v = torch.randn(B, S, D, generator=g)
+        if outlier_frac > 0:
+            k = torch.where(torch.rand(B, S, D, generator=g) < outlier_frac, k * outlier_scale, k)
+            v = torch.where(torch.rand(B, S, D, generator=g) < outlier_frac, v * outlier_scale, v)
+        if outlier_channels > 0:
+            ch = torch.randperm(D, generator=g)[:outlier_channels]
+            k[:, :, ch] *= outlier_channel_scale
+        ks.append(k)
+        vs.append(v)
+    return torch.stack(ks, dim=1).contiguous(), torch.stack(vs, dim=1).contiguous()
+
+
+def queries_heads(B: int, S: int, D: int, seed: int, h0: int, h1: int) -> torch.Tensor:
+    """fp16 queries ~N(0,1) [B, h1-h0, S, D] for heads [h0, h1), one generator per head."""
+    qs = []
+    for h in range(h0, h1):
+        g = torch.Generator().manual_seed(_head_seed(seed, h, salt=31337))
+        qs.append(torch.randn(B, S, D, generator=g).to(torch.float16))
+    return torch.stack(qs, dim=1).contiguous()
+
+
+def drift_noise(B: int, S: int, D: int, seed: int, step: int, h0: int, h1: int,
+                sigma: float = 0.074, eps: float = 1.0) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Per-step drift of the batched denoising loop: for each (token, head) a relative drift
+    r ~ |N(0, sigma)| shared by its K and V rows, applied as ``x + r * eps * ||x_row|| / sqrt(D) *
+    n`` with n ~ N(0, 1) per element; returns the unit-row noise ``n`` scaled by ``r * eps /
+    sqrt(D)`` (multiply by the row norm to apply).  [B, h1-h0, S, D] fp32 for K and for V."""
+    nk, nv = [], []
+    for h in range(h0, h1):
+        g = torch.Generator().manual_seed(_head_seed(seed, h, salt=1000 + step))
+        r = torch.randn(S, generator=g).abs() * sigma * eps / math.sqrt(D)
+        nk.append(torch.randn(B, S, D, generator=g) * r[None, :, None])
+        nv.append(torch.randn(B, S, D, generator=g) * r[None, :, None])
+    return torch.stack(nk, dim=1).contiguous(), torch.stack(nv, dim=1).contiguous()
+
+
+def cfg5_layer(h0: int = 0, h1: Optional[int] = None, layer: int = 0) -> Dict[str, torch.Tensor]:
+    """Heads [h0, h1) of one long-context layer (cfg5, seed = layer): K, V fp32 [1, h, 32768, 128]
+    with 1 % x8 outliers and 4 outlier channels x10 per head in K, the layer's importance
+    [S, H] (all heads; codes 10/30/60 % fp16/int8/int4, 4 fp16 sinks) and fp16 queries."""
+    c = CONFIGS["cfg5"]
+    h1 = c["H"] if h1 is None else h1
+    k, v = kv_heads(c["B"], c["S"], c["D"], layer, h0, h1, outlier_channels=c["outlier_channels"],
+                    outlier_channel_scale=c["outlier_channel_scale"])
+    return {"k": k, "v": v, "importance": importance_map(c["S"], c["H"], layer, c["fractions"]),
+            "q": queries_heads(c["B"], c["S"], c["D"], layer, h0, h1), "group": c["group"]}
+
+
+def cfg4_layer(h0: int = 0, h1: Optional[int] = None, layer: int = 0) -> Dict[str, torch.Tensor]:
+    """Heads [h0, h1) of one batched-denoising layer (cfg4, seed = layer) at step 0: K, V fp32
+    [8, h, 2048, 128], the layer's importance [S, H] (codes 25/50/25 %) and fp16 queries."""
+    c = CONFIGS["cfg4"]
+    h1 = c["H"] if h1 is None else h1
+    k, v = kv_heads(c["B"], c["S"], c["D"], 10_000 + layer, h0, h1)
+    return {"k": k, "v": v, "importance": importance_map(c["S"], c["H"], 10_000 + layer, c["fractions"]),
+            "q": queries_heads(c["B"], c["S"], c["D"], 10_000 + layer, h0, h1), "group": c["group"]}
+
+
+def apply_drift(x: torch.Tensor, noise: torch.Tensor) -> torch.Tensor:
+    """``x + noise * ||x_row||`` (row = the head_dim vector of one (batch, head, token))."""
+    return x + noise * torch.linalg.vector_norm(x, dim=-1, keepdim=True)
+
+
+def lowest_importance_mask(importance: torch.Tensor, frac: float, sink_tokens: int = 4) -> torch.Tensor:
+    """bool [S, H]: the ``floor(frac * n)`` entries of lowest importance among the n non-sink
+    (t >= sink_tokens) entries, ties in row-major (token, head) order -- the eviction set of
+    the batched denoising loop."""
+    S, H = importance.shape
+    flat = importance.reshape(-1).to(torch.float64).clone()
+    flat[: min(sink_tokens, S) * H] = float("inf")
+    n = int(math.floor(frac * (S - min(sink_tokens, S)) * H))
+    order = torch.argsort(flat, stable=True)
+    mask = torch.zeros(S * H, dtype=torch.bool, device=importance.device)
+    mask[order[:n]] = True
+    return mask.reshape(S, H)
+
+
+def sample_rows(S: int, n: int, seed: int) -> torch.Tensor:
+    """int64 [n]: sorted distinct query rows of a sequence of S, always holding the first and the
+    last row (sampled rows of a non-causal attention are checked against the oracle)."""
+    g = torch.Generator().manual_seed(int(seed) + 4242)
+    mid = torch.randperm(max(S - 2, 0), generator=g)[: max(n - 2, 0)] + 1
+    return torch.unique(torch.cat([torch.tensor([0, S - 1]), mid])).to(torch.int64)
+
+
 def importance_map(
     S: int, H: int, seed: int, fractions=(0.25, 0.50, 0.25), sink_tokens: int = 4
 ) -> torch.Tensor:

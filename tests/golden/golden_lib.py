@@ -183,3 +183,31 @@ def reuse_inputs(seed: int, B: int, H: int, S: int, D: int):
     kp[:, zero] = 0.0
     imp = (rng.random((S, H)) * 1.2 - 0.1).astype(np.float32)
     return k, v, kp, vp, imp
+
+
+BLOCK_PARAM_ORDER = ("ln1.weight", "ln1.bias", "q_proj.weight", "q_proj.bias", "k_proj.weight", "k_proj.bias",
+                     "v_proj.weight", "v_proj.bias", "o_proj.weight", "o_proj.bias", "ln2.weight", "ln2.bias",
+                     "up_proj.weight", "up_proj.bias", "down_proj.weight", "down_proj.bias")
+
+
+def block_params(seed: int, hidden: int, inter: int) -> Dict[str, Any]:
+    """Seeded parameters of one diffusion transformer block (the attribute names and shapes of
+    shadowinfer/models/simple_diffusion_llm.py:26-52), drawn in BLOCK_PARAM_ORDER so that the
+    fixture generator and the GPU test build the same block without storing weights."""
+    import torch
+    g = torch.Generator().manual_seed(int(seed))
+    shapes = {"ln1": (hidden,), "ln2": (hidden,), "q_proj": (hidden, hidden), "k_proj": (hidden, hidden),
+              "v_proj": (hidden, hidden), "o_proj": (hidden, hidden), "up_proj": (inter, hidden),
+              "down_proj": (hidden, inter)}
+    out = {}
+    for name in BLOCK_PARAM_ORDER:
+        mod, kind = name.split(".")
+        shp = shapes[mod]
+        if mod.startswith("ln"):
+            base = 1.0 if kind == "weight" else 0.0
+            out[name] = base + 0.1 * torch.randn(shp, generator=g)
+        elif kind == "weight":
+            out[name] = torch.randn(shp, generator=g) / (shp[1] ** 0.5)
+        else:
+            out[name] = 0.02 * torch.randn(shp[0], generator=g)
+    return out

@@ -32,8 +32,8 @@ REPO = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, REPO)
 sys.path.insert(0, HERE)
 
-from golden_lib import (PINS_JSON, SMALL_NPZ, array_digest, irap_scores, packed_summary,  # noqa: E402
-                        paged_apply, reuse_inputs, state_digest, to_numpy)
+from golden_lib import (BLOCK_PARAM_ORDER, PINS_JSON, SMALL_NPZ, array_digest, block_params,  # noqa: E402
+                        irap_scores, packed_summary, paged_apply, reuse_inputs, state_digest, to_numpy)
 
 from shadow_infer_b200 import workloads as W  # noqa: E402
 
@@ -46,10 +46,10 @@ def _import_reference(path: str):
     from shadowinfer.shadowkv import rd_allocator, precision_plan, packed_kv_cache  # noqa
     from shadowinfer.shadowkv.shadowkv_agent import ShadowKVAgent  # noqa
     from shadowinfer.shadowkv import paged_kv_store, importance_model  # noqa
-    from shadowinfer.models import diffusion_llama  # noqa
+    from shadowinfer.models import diffusion_llama, simple_diffusion_llm  # noqa
     return types.SimpleNamespace(
         rd=rd_allocator, plan=precision_plan, pkc=packed_kv_cache, Agent=ShadowKVAgent, paged=paged_kv_store,
-        imp=importance_model, llama=diffusion_llama,
+        imp=importance_model, llama=diffusion_llama, sdl=simple_diffusion_llm,
     )
 
 
@@ -594,12 +594,144 @@ def full_pins(R):
     print("cfg2 done", pred, ev, stats, removed)
 
 
+def _sampled_attention(q, ku, vu, rows):
+    """The reference model's attention lines (simple_diffusion_llm.py:165-169, fp32) on the query
+    rows ``rows`` only: non-causal attention is row-independent, so these are exactly those rows
+    of the full output."""
+    qf = q[:, :, rows].float()
+    scores = torch.matmul(qf, ku.transpose(-2, -1)) / (qf.shape[-1] ** 0.5)
+    return torch.matmul(torch.softmax(scores, dim=-1), vu)
+
+
+def long_pins(R):
+    """Head slices of the long-context layer (cfg5: S=32768, codes 10/30/60, channel outliers) and
+    of the batched denoising layer (cfg4: B=8, one drift step with reuse and eviction): digests
+    of the reference's plan / pack / reuse / evict / unpack, and its attention on sampled rows."""
+    c5 = W.CONFIGS["cfg5"]
+    h0, h1 = 0, 2
+    L = W.cfg5_layer(h0, h1)
+    imp = L["importance"][:, h0:h1].contiguous()
+    codes = R.Agent.allocate_precision_codes(None, imp, "balanced")
+    plan = R.plan.PrecisionPlan.from_codes(codes)
+    packed = R.pkc.PackedKVCache.pack(L["k"], L["v"], None, group_size=c5["group"], plan=plan)["packed_kv"]
+    ku, vu = packed.unpack()
+    rows = W.sample_rows(c5["S"], 64, 5)
+    out = _sampled_attention(L["q"], ku, vu, rows)
+    put("cfg5_slice", "rows", rows)
+    put("cfg5_slice", "out", out)
+    PINS["full"]["cfg5_slice"] = {
+        "heads": [h0, h1], "k": array_digest(L["k"]), "v": array_digest(L["v"]), "q": array_digest(L["q"]),
+        "importance": array_digest(L["importance"]), "codes": array_digest(codes),
+        "counts": {p: len(plan.groups[p]) for p in PRECISIONS}, "fingerprint": plan.fingerprint,
+        "packed": packed_summary(packed.packed_data, packed.memory_bytes()),
+        "data_plane_bytes": packed.data_plane_bytes(), "resident_bytes": packed.resident_bytes(),
+        "unpack_k": array_digest(ku), "unpack_v": array_digest(vu),
+    }
+    print("cfg5 slice done", PINS["full"]["cfg5_slice"]["counts"], packed.memory_bytes())
+
+    c4 = W.CONFIGS["cfg4"]
+    B, S, D = c4["B"], c4["S"], c4["D"]
+    h0, h1 = 0, 4
+    L = W.cfg4_layer(h0, h1)
+    imp = L["importance"][:, h0:h1].contiguous()
+    codes = R.Agent.allocate_precision_codes(None, imp, "balanced")
+    prev = R.pkc.PackedKVCache.pack(L["k"], L["v"], None, group_size=16,
+                                    plan=R.plan.PrecisionPlan.from_codes(codes))["packed_kv"]
+    nk, nv = W.drift_noise(B, S, D, 10_000, 1, h0, h1)
+    k1, v1 = W.apply_drift(L["k"], nk), W.apply_drift(L["v"], nv)
+    # drift < 0.05: the conservative threshold at the last step, importance term off
+    reuse_dict, rstats = R.Agent.decide_reuse_per_token(None, k1, v1, L["k"], L["v"], 16, 16, 0.0, "conservative",
+                                                        torch.zeros(S, h1 - h0))
+    reuse = torch.zeros(S, h1 - h0, dtype=torch.bool)
+    for (t, h), f in reuse_dict.items():
+        reuse[t, h] = f
+    plan = R.plan.PrecisionPlan.from_codes(codes, reuse_mask=reuse_dict)
+    cur = R.pkc.PackedKVCache.pack(k1, v1, None, group_size=16, plan=plan)["packed_kv"]
+    summary_pack = packed_summary(cur.packed_data, cur.memory_bytes())
+    stats = cur.apply_reuse_mask(prev, reuse_dict, return_stats=True)
+    summary_reuse = packed_summary(cur.packed_data, cur.memory_bytes())
+    emask = W.lowest_importance_mask(imp, c4["evict_frac"], 4)
+    ts, hs = torch.nonzero(emask, as_tuple=True)
+    removed = cur.evict(set(zip(ts.tolist(), hs.tolist())))
+    ku, vu = cur.unpack()
+    rows = W.sample_rows(S, 16, 4)
+    out = _sampled_attention(L["q"], ku, vu, rows)
+    put("cfg4_slice", "rows", rows)
+    put("cfg4_slice", "out", out)
+    put("cfg4_slice", "reuse", reuse)
+    PINS["full"]["cfg4_slice"] = {
+        "heads": [h0, h1], "k1": array_digest(k1), "v1": array_digest(v1), "q": array_digest(L["q"]),
+        "codes": array_digest(codes), "reuse": array_digest(reuse), "reuse_decision": rstats,
+        "fingerprint": plan.fingerprint, "packed": summary_pack, "reuse_stats": stats,
+        "after_reuse": summary_reuse, "evict_mask": array_digest(emask), "removed": removed,
+        "after_evict": packed_summary(cur.packed_data, cur.memory_bytes()),
+        "resident_after_evict": cur.resident_bytes(),
+        "unpack_k": array_digest(ku), "unpack_v": array_digest(vu),
+    }
+    print("cfg4 slice done", rstats, stats, removed)
+
+
+def block_case(R, case, gen, B, H, D, S_past, S_new, inter, probs=(0.1, 0.3, 0.3, 0.25, 0.05), seed=77):
+    """One reference DiffusionTransformerBlock._compute_block forward over a past KV cache that
+    comes from the reference PackedKVCache (pack -> unpack, the kv_execution="packed" backend's
+    path, pytorch_backend.py:302-304): this block's hidden output, its own K/V and the attention
+    output (attention weights times the concatenated V)."""
+    hidden_dim = H * D
+    block = R.sdl.DiffusionTransformerBlock(hidden_dim, H, D, inter, torch.device("cpu"), torch.float32)
+    params = block_params(seed, hidden_dim, inter)
+    with torch.no_grad():
+        named = dict(block.named_parameters())
+        assert set(named) == set(BLOCK_PARAM_ORDER)
+        for name in BLOCK_PARAM_ORDER:
+            named[name].copy_(params[name])
+    k, v = kv(gen, B, H, S_past, D)
+    codes = codes_of(gen, S_past, H, probs)
+    packed = R.pkc.PackedKVCache.pack(k, v, R.plan.codes_to_map(codes), group_size=16)["packed_kv"]
+    past = packed.unpack()
+    hidden = torch.randn(B, S_new, hidden_dim, generator=gen)
+    with torch.no_grad():
+        out, k_new, v_new, k_full, v_full, attn_w = block._compute_block(hidden, past)
+        attn_out = torch.matmul(attn_w, v_full)
+        q = block.q_proj(block.ln1(hidden)).view(B, S_new, H, D).transpose(1, 2)
+    for name, x in (("k", k), ("v", v), ("codes", codes), ("hidden", hidden), ("out", out), ("k_new", k_new),
+                    ("v_new", v_new), ("attn_out", attn_out), ("q", q)):
+        put(case, name, x)
+    PINS["cases"][case] = {"kind": "block", "B": B, "H": H, "D": D, "S_past": S_past, "S_new": S_new,
+                           "inter": inter, "seed": seed,
+                           "params": {n: array_digest(params[n]) for n in BLOCK_PARAM_ORDER}}
+
+
+def block_cases(R):
+    g3 = torch.Generator().manual_seed(20261203)
+    block_case(R, "block_b2_h2_d64", g3, 2, 2, 64, 200, 80, 256)
+    block_case(R, "block_b1_h2_d128", g3, 1, 2, 128, 300, 130, 512, seed=78)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="path of the shadow-infer source tree")
+    ap.add_argument("--only-long", action="store_true",
+                    help="keep the existing fixtures and (re)record only the cfg5 / cfg4 head-slice pins")
+    ap.add_argument("--only-block", action="store_true",
+                    help="keep the existing fixtures and (re)record only the model-block forward cases")
     args = ap.parse_args()
     torch.set_num_threads(os.cpu_count() or 1)
     R = _import_reference(args.reference)
+    if args.only_long or args.only_block:
+        with np.load(SMALL_NPZ, allow_pickle=False) as z:
+            drop = (("cfg5_slice/", "cfg4_slice/") if args.only_long else ()) + (("block_",) if args.only_block else ())
+            ARR.update({k: z[k] for k in z.files if not k.startswith(drop)})
+        with open(PINS_JSON) as f:
+            PINS.update(json.load(f))
+        if args.only_long:
+            long_pins(R)
+        if args.only_block:
+            block_cases(R)
+        np.savez_compressed(SMALL_NPZ, **ARR)
+        with open(PINS_JSON, "w") as f:
+            json.dump(PINS, f, indent=1, sort_keys=True)
+        print("wrote", SMALL_NPZ, os.path.getsize(SMALL_NPZ), PINS_JSON)
+        return
     gen = torch.Generator().manual_seed(20261201)
     mixed = (0.15, 0.3, 0.25, 0.2, 0.1)
     pack_case(R, "pack_b1_d64", gen, 1, 4, 16, 64, mixed)
@@ -650,6 +782,8 @@ def main():
     attention_gqa_case(R, "attn_new_rows_rep1", g2, 1, 3, 1, 70, 33, 50, 64)
     attention_gqa_case(R, "attn_gqa_past_all_evicted", g2, 1, 2, 2, 20, 17, 30, 64, probs=(0, 0, 0, 0, 1.0))
     full_pins(R)
+    long_pins(R)
+    block_cases(R)
     np.savez_compressed(SMALL_NPZ, **ARR)
     with open(PINS_JSON, "w") as f:
         json.dump(PINS, f, indent=1, sort_keys=True)

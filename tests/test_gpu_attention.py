@@ -316,3 +316,30 @@ def test_attention_peer_outputs_two_gpus(skv):
     ret = ctx.Manager().dict()
     mp.start_processes(_peer_worker, args=(2, port, ret), nprocs=2, join=True, start_method="spawn")
     assert ret.get(0) and ret.get(1)
+
+
+@pytest.mark.parametrize("B,H,S,SQ,D,probs,qs", CASES[:4])
+def test_attention_fast_k_matches_oracle(skv, B, H, S, SQ, D, probs, qs):
+    """K in fp16 only (one MMA chain, two K stages): within 1e-3 on N(0,1) data, and never
+    closer to the oracle than the default hi + lo K."""
+    rng = np.random.default_rng(S * 31 + D)
+    k = rng.standard_normal((B, H, S, D)).astype(np.float32)
+    v = rng.standard_normal((B, H, S, D)).astype(np.float32)
+    k[rng.random(k.shape) < 0.01] *= 8
+    codes = rng.choice(5, size=(S, H), p=probs).astype(np.int8)
+    q = (rng.standard_normal((B, H, SQ, D)) * qs).astype(np.float16)
+    cache = _pack(skv, k, v, codes)
+    ref = O.packed_attention(q.astype(np.float32), O.pack(k, v, O.plan_from_codes(codes), 16))
+    fast = skv.packed_attention(torch.from_numpy(q).cuda(), cache, fast_k=True).cpu().numpy()
+    exact = skv.packed_attention(torch.from_numpy(q).cuda(), cache).cpu().numpy()
+    assert rel_l2(fast, ref) < REL_L2_TOL
+    assert rel_l2(exact, ref) <= rel_l2(fast, ref) * 1.05 + 1e-6
+
+
+def test_attention_mask_with_packed_past_raises(skv):
+    rng = np.random.default_rng(3)
+    k = rng.standard_normal((1, 2, 40, 64)).astype(np.float32)
+    cache = _pack(skv, k, k, np.full((40, 2), 2, dtype=np.int8))
+    q = torch.zeros(1, 2, 8, 64, dtype=torch.float16, device="cuda")
+    with pytest.raises(ValueError, match="attention_mask is not supported together with kv_cache"):
+        skv.packed_attention(q, cache, attention_mask=torch.zeros(8, 40, device="cuda"))

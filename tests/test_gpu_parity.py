@@ -297,3 +297,47 @@ def test_pack_before_counts_reach_host(skv):
         assert launches == (3 if stored else 2)            # layout + empty pack + exact pack
         assert _bucket_bytes(again) == _bucket_bytes(want)
         assert hint is not None
+
+
+@pytest.mark.parametrize("case", ["one_bucket_touched", "bucket_emptied_others_touched",
+                                  "bucket_emptied_other_untouched", "every_bucket_touched"])
+def test_evict_fresh_pack_paths(case, skv, monkeypatch):
+    """evict on a freshly packed cache takes the pack's own bucket array (fast path) unless a
+    non-empty bucket loses no entry, when it hands over to the general path; both must equal the
+    oracle: removed count, packed bytes and index lists, memory accounting and the unpack."""
+    calls = []
+    orig = skv.PackedKVCache._evict_pending
+
+    def spy(self, entries):
+        r = orig(self, entries)
+        calls.append(r)
+        return r
+
+    monkeypatch.setattr(skv.PackedKVCache, "_evict_pending", spy)
+    rng = np.random.default_rng(len(case))
+    B, H, S, D = 2, 3, 40, 64
+    k = rng.standard_normal((B, H, S, D)).astype(np.float32)
+    v = rng.standard_normal((B, H, S, D)).astype(np.float32)
+    codes = rng.integers(1, 4, size=(S, H)).astype(np.int8)       # fp16 / int8 / int4 buckets
+    sel = {
+        "one_bucket_touched": codes == 2,                         # int8 only
+        "bucket_emptied_others_touched": (codes == 3) | ((codes != 3) & (rng.random((S, H)) < 0.3)),
+        "bucket_emptied_other_untouched": (codes == 3) | ((codes == 1) & (rng.random((S, H)) < 0.5)),
+        "every_bucket_touched": rng.random((S, H)) < 0.25,
+    }[case]
+    if case == "one_bucket_touched":
+        sel = sel & (rng.random((S, H)) < 0.5)
+    fast = case in ("bucket_emptied_others_touched", "every_bucket_touched")
+    cache = skv.PackedKVCache.pack(cu(k), cu(v), None, 16, plan=skv.PrecisionPlan.from_codes(cu(codes)))["packed_kv"]
+    ref = O.pack(k, v, O.plan_from_codes(codes), 16)
+    removed = cache.evict(cu(sel))
+    assert removed == O.evict(ref, sel) == int(sel.sum())
+    assert calls == ([removed] if fast else [None])
+    assert packed_summary(cache.packed_data, cache.memory_bytes()) == packed_summary(ref.packed_data,
+                                                                                     ref.memory_bytes())
+    assert cache.memory_bytes() == ref.memory_bytes() and cache.resident_bytes() == ref.resident_bytes()
+    ku, vu = cache.unpack()
+    ko, vo = O.unpack(ref)
+    assert eq(ku, ko) and eq(vu, vo)
+    # idempotent: the same set again removes nothing
+    assert cache.evict(cu(sel)) == 0

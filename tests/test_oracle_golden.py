@@ -265,3 +265,84 @@ def test_attention_gqa(case, golden_small):
     ref = a["out"].astype(np.float64)
     rel = np.linalg.norm(out - ref) / np.linalg.norm(ref)
     assert rel < 1e-5, rel
+
+
+def _sampled_oracle_attention(q_rows, cache):
+    """Oracle attention of the query rows ``q_rows`` [B, H, n, D] over the whole packed cache."""
+    return O.packed_attention(q_rows.astype(np.float32), cache)
+
+
+def test_long_context_slice_pins(golden_pins, golden_small):
+    """Heads 0-1 of the long-context layer (S=32768, codes 10/30/60, 4 outlier channels x10):
+    the oracle reproduces the reference's plan, packed bytes, unpack and sampled attention."""
+    from shadow_infer_b200 import workloads as W
+    pin = golden_pins["full"]["cfg5_slice"]
+    h0, h1 = pin["heads"]
+    L = W.cfg5_layer(h0, h1)
+    assert array_digest(L["k"]) == pin["k"] and array_digest(L["v"]) == pin["v"]
+    assert array_digest(L["q"]) == pin["q"] and array_digest(L["importance"]) == pin["importance"]
+    imp = np.ascontiguousarray(L["importance"][:, h0:h1].numpy())
+    codes = O.allocate_precision_codes(imp, "balanced")
+    assert array_digest(codes) == pin["codes"]
+    plan = O.plan_from_codes(codes)
+    assert plan["fingerprint"] == pin["fingerprint"]
+    cache = O.pack(L["k"].numpy(), L["v"].numpy(), plan, 16)
+    assert packed_summary(cache.packed_data, cache.memory_bytes()) == pin["packed"]
+    assert cache.data_plane_bytes() == pin["data_plane_bytes"] and cache.resident_bytes() == pin["resident_bytes"]
+    ku, vu = O.unpack(cache)
+    assert array_digest(ku) == pin["unpack_k"] and array_digest(vu) == pin["unpack_v"]
+    a = case_arrays(golden_small, "cfg5_slice")
+    out = _sampled_oracle_attention(L["q"].numpy()[:, :, a["rows"]], cache)
+    assert np.linalg.norm(out - a["out"]) / np.linalg.norm(out) < 1e-5
+
+
+def test_batched_denoise_slice_pins(golden_pins, golden_small):
+    """Heads 0-3 of a batched denoising layer (B=8, S=2048): one drift step, the reuse decision
+    (drift < 0.05), re-pack, reuse from the previous cache, eviction of the 25 % lowest-importance
+    entries and the unpack, against the reference's digests."""
+    import torch
+    from oracle import decision_oracle as DO
+    from shadow_infer_b200 import workloads as W
+    pin = golden_pins["full"]["cfg4_slice"]
+    a = case_arrays(golden_small, "cfg4_slice")
+    h0, h1 = pin["heads"]
+    c = W.CONFIGS["cfg4"]
+    L = W.cfg4_layer(h0, h1)
+    nk, nv = W.drift_noise(c["B"], c["S"], c["D"], 10_000, 1, h0, h1)
+    k1, v1 = W.apply_drift(L["k"], nk), W.apply_drift(L["v"], nv)
+    assert array_digest(k1) == pin["k1"] and array_digest(v1) == pin["v1"] and array_digest(L["q"]) == pin["q"]
+    imp = np.ascontiguousarray(L["importance"][:, h0:h1].numpy())
+    codes = O.allocate_precision_codes(imp, "balanced")
+    assert array_digest(codes) == pin["codes"]
+    mask, stats, drift = DO.decide_reuse_per_token(k1.numpy(), v1.numpy(), L["k"].numpy(), L["v"].numpy(), 16, 16,
+                                                   0.0, "conservative", np.zeros_like(imp))
+    # equal wherever the drift is not within 1e-6 of the 0.05 threshold (float32 reduction order)
+    far = np.abs(drift.T.astype(np.float64) - 0.05) > 1e-6
+    assert np.array_equal(mask[far], a["reuse"][far])
+    reuse = a["reuse"]
+    prev = O.pack(L["k"].numpy(), L["v"].numpy(), O.plan_from_codes(codes), 16)
+    plan = O.plan_from_codes(codes, reuse)
+    assert plan["fingerprint"] == pin["fingerprint"]
+    cache = O.pack(k1.numpy(), v1.numpy(), plan, 16)
+    assert packed_summary(cache.packed_data, cache.memory_bytes()) == pin["packed"]
+    assert O.apply_reuse_mask(cache, prev, reuse) == pin["reuse_stats"]
+    assert packed_summary(cache.packed_data, cache.memory_bytes()) == pin["after_reuse"]
+    emask = W.lowest_importance_mask(torch.from_numpy(imp), c["evict_frac"], 4).numpy()
+    assert array_digest(emask) == pin["evict_mask"]
+    assert O.evict(cache, emask) == pin["removed"]
+    assert packed_summary(cache.packed_data, cache.memory_bytes()) == pin["after_evict"]
+    assert cache.resident_bytes() == pin["resident_after_evict"]
+    ku, vu = O.unpack(cache)
+    assert array_digest(ku) == pin["unpack_k"] and array_digest(vu) == pin["unpack_v"]
+    out = _sampled_oracle_attention(L["q"].numpy()[:, :, a["rows"]], cache)
+    assert np.linalg.norm(out - a["out"]) / np.linalg.norm(out) < 1e-5
+
+
+@pytest.mark.parametrize("case", _cases(_pins(), "block"))
+def test_model_block_attention(case, golden_small):
+    """The reference block forward over a packed past (kv_execution="packed"): the oracle's
+    attention of the block's own queries over unpack() + this step's K/V equals the reference's."""
+    a = case_arrays(golden_small, case)
+    cache = O.pack(a["k"], a["v"], O.plan_from_codes(a["codes"]), 16)
+    out = O.packed_attention(a["q"], cache, k_new=a["k_new"], v_new=a["v_new"])
+    assert np.linalg.norm(out - a["attn_out"]) / np.linalg.norm(a["attn_out"]) < 1e-5
