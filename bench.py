@@ -1533,8 +1533,9 @@ def run_b200(args):
         "dtype_note": "attention in fp16 tensor-core operands with fp32 accumulation and softmax; the data plane "
                       "quantises fp32 K/V to fp16/int8/int4 bit-exactly",
     }
-    if "cpu_baseline" in head:
-        line["cpu_baseline"] = head["cpu_baseline"]
+    for key in ("cpu_baseline", "fast_k", "vs_sdpa"):
+        if key in head:
+            line[key] = head[key]
     line.update(extras)
     print(json.dumps(line), flush=True)
     return 0

@@ -169,9 +169,11 @@ int skv_head_index(const int32_t* slot, int S, int H, int32_t* rows, int32_t* co
  * attention (shadowinfer/models/simple_diffusion_llm.py:165-169), without materialising the
  * dense fp32 K/V.  The packed rows of each head are dequantised once into fp16 tensor-core tiles
  * in `scratch` (at least skv_packed_attention_scratch_bytes bytes, 16-byte aligned), which
- * every query tile of the head then reads: K as an fp16 pair hi + lo (hi = RNE(k), lo =
- * RNE(k - hi)) contracted with Q in two MMA chains, so K enters the scores with ~22 bits
- * (tiles of fp16 entries only are exact and skip the lo chain); V in fp16.
+ * every query tile of the head then reads: K and V in fp16, plus, for the 16 channels of
+ * largest max |K| in each KV head, lo = RNE(k - RNE(k)) in a tile of its own, which one extra
+ * MMA (K = 16) contracts with the same channels of Q -- channel outliers of K would otherwise
+ * make fp16's 2^-11 rounding of K the dominant error (tiles of fp16 entries only are exact and
+ * skip it).  The scratch also holds the per-head channel maxima and selection.
  * q fp16 [B,H,S_q,D], out fp32 [B,H,S_q,D]; D = 64 or 128; error_flag (device int32) is cleared
  * and set non-zero if a pipeline wait timed out (results then invalid). */
 size_t skv_packed_attention_scratch_bytes(int B, int H, int S_kv, int D);
@@ -223,10 +225,10 @@ int skv_ipc_close(void* base);
 /* max_ctas: CTAs of the persistent attention kernel (0 = one per SM); fewer leave SMs free for
  * work that should run beside it (e.g. the NCCL all-gather of the previous layer's outputs).
  * flags (the _gqa / _peers entry points; staging and attention take the same flags):
- *   0                -- K staged as hi + lo fp16 tiles and contracted in two MMA chains (~22 bits;
- *                       the default, which meets relative L2 1e-3 against the fp32 reference also
- *                       with channel outliers in K);
- *   SKV_ATTN_FAST_K  -- K in fp16 only (one MMA chain, two K stages): faster, but K enters the
+ *   0                -- the default: the 16 largest channels of K per KV head also contribute their
+ *                       fp16 lo part (one extra K = 16 MMA per score tile), which keeps relative L2
+ *                       within 1e-3 of the fp32 reference also with channel outliers in K;
+ *   SKV_ATTN_FAST_K  -- K in fp16 only: no channel selection and no extra MMA, but K enters the
  *                       scores with fp16's 2^-11 relative error, which outlier channels of K turn
  *                       into ~2e-3 relative L2 on the long-context workload. */
 #define SKV_ATTN_FAST_K 1

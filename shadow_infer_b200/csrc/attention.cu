@@ -67,6 +67,9 @@ enum AttnError { kErrNone = 0, kErrKFull = 1, kErrKEmpty = 2, kErrSFull = 3, kEr
 // Bytes of one staged K (or V) tile: D/64 swizzle atoms of 128 rows x 128 bytes.
 __host__ __device__ constexpr int staged_tile_bytes(int D) { return (D / 64) * kBN * 128; }
 
+constexpr int kLoCh = 16;                       // channels of K with a lo part: one MMA K-step of fp16
+constexpr int kLoTile = kBN * kLoCh * 2;        // their lo tile: 128 rows x 32 bytes (32-byte swizzle)
+
 constexpr int kMaxHeads = 256;     // heads per launch (the schedule keeps a per-head prefix in smem)
 constexpr int kMaxPartners = 8;    // CTAs that can hold later parts of one unit (merged by its first part)
 constexpr int kUnitRows = 2 * kBM;  // queries per work unit
@@ -76,14 +79,16 @@ struct AttnLayout {
     static constexpr int NA = D / 64;                   // 128-byte swizzle atoms per row
     static constexpr int kTile = staged_tile_bytes(D);  // one 128-row tile (Q, K or V)
     static constexpr int kQ = 0;                        // two query tiles
-    static constexpr int kK = kQ + 2 * kTile;           // K: one stage of hi + lo tiles, or two hi stages
+    static constexpr int kK = kQ + 2 * kTile;           // two K stages
     static constexpr int kV = kK + 2 * kTile;           // two V stages
-    static constexpr int kBar = kV + 2 * kTile;
+    static constexpr int kQc = kV + 2 * kTile;          // two tiles of the queries' selected channels (32B swizzle)
+    static constexpr int kKc = kQc + 2 * kLoTile;       // two stages of K lo of the selected channels
+    static constexpr int kBar = kKc + 2 * kLoTile;
     static constexpr int kNumBars = 24;
     static constexpr int kHP = kBar + kNumBars * 8;     // int32 [kMaxHeads + 1]: prefix of KV tiles per head
-    // PEERS: per softmax warp, 8 output rows staged for the bulk stores into every rank's buffer
+    // PEERS: per softmax warp, kOutRows output rows staged for the bulk stores into every rank's buffer
     static constexpr int kOut = (kHP + (kMaxHeads + 1) * 4 + 127) / 128 * 128;
-    static constexpr int kOutRows = 8;
+    static constexpr int kOutRows = 4;
     static constexpr int kMisc = kOut + (PEERS ? kSoftmaxWarps * kOutRows * D * 4 : 0);
     static constexpr int kTmemSlot = kMisc + 16;
     static constexpr int kBytes = kTmemSlot + 16;
@@ -113,7 +118,9 @@ struct AttnParams {
     int n_peers, head_off, H_out;
     float scale_log2;          // softmax scale * log2(e)
     int* err;
-    int klo;                   // 1: K staged and contracted as hi + lo (one K stage); 0: hi only (two stages)
+    int klo;                   // 1: the head's kLoCh largest channels of K also contribute their lo part
+    unsigned* chmax;           // [H_kv, D] max |K| per channel (float bits), channel selection input
+    int* sel;                  // [H_kv, kLoCh] the selected channels, ascending
 };
 
 __device__ __forceinline__ float ex2(float x) {
@@ -141,19 +148,32 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* e
     return __all_sync(0xffffffffu, ok);
 }
 
-// Staged tiles of (batch b, KV head h, tile j): K hi, K lo, V (kStagedTiles of them).
-constexpr int kStagedTiles = 3;
-constexpr int kTileKHi = 0, kTileKLo = 1, kTileV = 2;
-__device__ __forceinline__ int64_t staged_offset(const AttnParams& p, int b, int h, int j, int kv, int tile_bytes) {
-    return ((((int64_t)b * p.H_kv + h) * p.ntmax + j) * kStagedTiles + kv) * tile_bytes;
+// Channel-selective lo part of K.  fp16 K is off by up to 2^-11 of every element; a few channels
+// of much larger magnitude than the rest (channel outliers of K) make that the dominant error of
+// the scores.  Per KV head the kLoCh channels of largest max |K| get lo = RNE(k - RNE(k)) staged
+// in a small tile of their own, and one extra MMA (K = kLoCh) adds Q[:, sel] K_lo^T to the scores,
+// so these channels enter with ~22 bits and the rest with fp16's 11 (kLoCh, kLoTile above).
+// Staged tiles of (batch b, KV head h, tile j), contiguous: K (fp16), V (fp16), K lo of the
+// selected channels.
+__host__ __device__ constexpr int staged_set_bytes(int D) { return 2 * staged_tile_bytes(D) + kLoTile; }
+constexpr int kSetKHi = 0, kSetV = 1;           // in units of staged_tile_bytes; the lo tile follows V
+__device__ __forceinline__ int64_t staged_offset(const AttnParams& p, int b, int h, int j, int D) {
+    return (((int64_t)b * p.H_kv + h) * p.ntmax + j) * staged_set_bytes(D);
+}
+
+// Byte offset of 16-byte chunk `chunk` (0..1) of row `row` of a 32-byte-swizzled K-major tile
+// (rows 32 bytes apart; the chunk index is XORed with bit 2 of the row, the pattern of the
+// SWIZZLE_32B shared-memory descriptor and tensor map).
+__device__ __forceinline__ uint32_t sw32_offset(int row, int chunk) {
+    return (uint32_t)(row * 32 + ((chunk ^ ((row >> 2) & 1)) << 4));
 }
 
 // Rows [c0, c1) of a head's row list are its fp16 entries (the list holds fp32, fp16, int8,
 // int4 entries in that order, then the dense new rows).  A tile inside them is exact in fp16.
 struct HeadRows {
     int f16_begin, f16_end, n_rows;
-    __device__ __forceinline__ void load(const AttnParams& p, int h);
     int klo;
+    __device__ __forceinline__ void load(const AttnParams& p, int h);
     __device__ __forceinline__ bool exact(int j) const {
         const int lo = j * kBN, hi = min(lo + kBN, n_rows);
         return !klo || (lo >= f16_begin && hi <= f16_end);
@@ -292,38 +312,90 @@ __device__ __forceinline__ void load_dense_row(const AttnParams& p, int b, int h
     }
 }
 
-// Converts one lane's share of a K and a V row and stores it, 128B-swizzled, at row `r` of the
-// staged tiles: K as hi (and, unless the tile is exact, lo), V in fp16 (zeros for a padding row).
+// The eight fp32 K values of atom `a` of one lane's share of a row (zeros for a padding row).
 template <int D>
-__device__ __forceinline__ void store_row(const RawRow<D / 64>& raw, int r, int l8, uint8_t* khi, uint8_t* klo,
-                                          uint8_t* vtile, bool want_lo) {
+__device__ __forceinline__ void raw_k_f32(const RawRow<D / 64>& raw, int a, int l8, float (&x)[8]) {
+    if (raw.code == 0) {
+        f32x8_load(raw.kf + a * 64 + l8 * 8, x);
+    } else if (raw.code == 1) {
+        const uint32_t w[4] = {raw.k[a].x, raw.k[a].y, raw.k[a].z, raw.k[a].w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            __half2 h2;
+            memcpy(&h2, &w[i], 4);
+            const float2 f = __half22float2(h2);
+            x[2 * i] = f.x;
+            x[2 * i + 1] = f.y;
+        }
+    } else if (raw.code == 2) {
+        int8x8_to_f32(raw.k[a].x, raw.k[a].y, raw.sk[0], x);
+    } else if (raw.code == 3) {
+        int4x8_to_f32(raw.k[a].x, raw.sk[a], x);
+    } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) x[i] = 0.0f;
+    }
+}
+
+// Converts one lane's share of a K and a V row to fp16 and stores it, 128B-swizzled, at row `r`
+// of the staged tiles (zeros for a padding row); with `want_lo`, the lo parts of the selected
+// channels that fall in this lane's chunks go to the lo tile (bit i of lo_bits[a]: selected
+// channel i lies in chunk a; its position inside the chunk is lo_pos[i]).
+template <int D>
+__device__ __forceinline__ void store_row(const RawRow<D / 64>& raw, int r, int l8, uint8_t* ktile, uint8_t* vtile,
+                                          uint8_t* lotile, bool want_lo, const uint32_t (&lo_bits)[D / 64],
+                                          const int8_t* lo_pos) {
     constexpr int NA = D / 64;
 #pragma unroll
     for (int a = 0; a < NA; ++a) {
-        uint4 hk = make_uint4(0, 0, 0, 0), lk = make_uint4(0, 0, 0, 0), hv = make_uint4(0, 0, 0, 0);
         float x[8];
-        if (raw.code == 0) {
-            f32x8_load(raw.kf + a * 64 + l8 * 8, x);
-            f32x8_split(x, hk, lk);
-            hv = raw.v[a];
-        } else if (raw.code == 1) {
-            hk = raw.k[a];
+        raw_k_f32<D>(raw, a, l8, x);
+        uint4 hv = make_uint4(0, 0, 0, 0);
+        if (raw.code == 0 || raw.code == 1) {
             hv = raw.v[a];
         } else if (raw.code == 2) {
-            int8x8_to_f32(raw.k[a].x, raw.k[a].y, raw.sk[0], x);
-            f32x8_split(x, hk, lk);
-            int8x8_to_f32(raw.v[a].x, raw.v[a].y, raw.sv[0], x);
-            hv = f32x8_to_half(x);
+            float y[8];
+            int8x8_to_f32(raw.v[a].x, raw.v[a].y, raw.sv[0], y);
+            hv = f32x8_to_half(y);
         } else if (raw.code == 3) {
-            int4x8_to_f32(raw.k[a].x, raw.sk[a], x);
-            f32x8_split(x, hk, lk);
-            int4x8_to_f32(raw.v[a].x, raw.sv[a], x);
-            hv = f32x8_to_half(x);
+            float y[8];
+            int4x8_to_f32(raw.v[a].x, raw.sv[a], y);
+            hv = f32x8_to_half(y);
         }
+        const uint4 hk = raw.code == 1 ? raw.k[a] : f32x8_to_half(x);
         const int off = a * kBN * 128 + sw128_offset(r, l8);
-        *reinterpret_cast<uint4*>(khi + off) = hk;
-        if (want_lo) *reinterpret_cast<uint4*>(klo + off) = lk;
+        *reinterpret_cast<uint4*>(ktile + off) = hk;
         *reinterpret_cast<uint4*>(vtile + off) = hv;
+        if (want_lo) {
+            for (uint32_t bits = lo_bits[a]; bits; bits &= bits - 1) {
+                const int i = __ffs(bits) - 1;
+                const float v = x[lo_pos[i]];
+                const __half lo = __float2half_rn(v - __half2float(__float2half_rn(v)));
+                *reinterpret_cast<__half*>(lotile + sw32_offset(r, i >> 3) + (i & 7) * 2) = lo;
+            }
+        }
+    }
+}
+
+// The selected channels of KV head h (shared memory) and this lane's share of them: bit i of
+// lo_bits[a] is set when selected channel i lies in chunk (a, l8); lo_pos[i] is its position in
+// the chunk.
+template <int D>
+__device__ __forceinline__ void lo_share(const AttnParams& p, int h, int l8, int* s_sel, uint32_t (&lo_bits)[D / 64],
+                                         int8_t* s_pos) {
+    if (threadIdx.x < kLoCh) {
+        const int c = p.klo ? __ldg(p.sel + (int64_t)h * kLoCh + threadIdx.x) : 0;
+        s_sel[threadIdx.x] = c;
+        s_pos[threadIdx.x] = (int8_t)(c & 7);
+    }
+    __syncthreads();
+#pragma unroll
+    for (int a = 0; a < D / 64; ++a) {
+        uint32_t bits = 0;
+#pragma unroll
+        for (int i = 0; i < kLoCh; ++i)
+            if ((s_sel[i] >> 3) == a * 8 + l8) bits |= 1u << i;
+        lo_bits[a] = bits;
     }
 }
 
@@ -337,6 +409,8 @@ __global__ void __launch_bounds__(kStageThreads, 2) stage_tiles_kernel(AttnParam
     constexpr int NA = D / 64;
     constexpr int kRowsPerPass = kStageThreads / 8;
     constexpr int kPasses = kBN / kRowsPerPass;
+    __shared__ int s_sel[kLoCh];
+    __shared__ int8_t s_pos[kLoCh];
     const int j = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
     const int rsub = threadIdx.x >> 3, l8 = threadIdx.x & 7;
     const int32_t* hrows = p.rows + (int64_t)h * p.S_kv;
@@ -351,10 +425,12 @@ __global__ void __launch_bounds__(kStageThreads, 2) stage_tiles_kernel(AttnParam
     const int n_stored = hr.n_rows - p.S_new;
     if (j * kBN >= hr.n_rows) return;
     const bool want_lo = !hr.exact(j);
+    uint32_t lo_bits[NA];
+    lo_share<D>(p, h, l8, s_sel, lo_bits, s_pos);
     const int TB = staged_tile_bytes(D);
-    uint8_t* khi = p.stage + staged_offset(p, b, h, j, kTileKHi, TB);
-    uint8_t* klo = khi + (kTileKLo - kTileKHi) * TB;
-    uint8_t* vtile = khi + (kTileV - kTileKHi) * TB;
+    uint8_t* ktile = p.stage + staged_offset(p, b, h, j, D);
+    uint8_t* vtile = ktile + TB;
+    uint8_t* lotile = ktile + 2 * TB;
     RawRow<NA> raw[kPasses];
 #pragma unroll
     for (int i = 0; i < kPasses; ++i) {
@@ -365,7 +441,82 @@ __global__ void __launch_bounds__(kStageThreads, 2) stage_tiles_kernel(AttnParam
             load_raw_row<D>(p, b, idx < n_stored ? e[i] : -1, l8, raw[i]);
     }
 #pragma unroll
-    for (int i = 0; i < kPasses; ++i) store_row<D>(raw[i], i * kRowsPerPass + rsub, l8, khi, klo, vtile, want_lo);
+    for (int i = 0; i < kPasses; ++i)
+        store_row<D>(raw[i], i * kRowsPerPass + rsub, l8, ktile, vtile, lotile, want_lo, lo_bits, s_pos);
+}
+
+// Max |K| per channel of each KV head over all its rows and batches (float bits, atomicMax on
+// non-negative floats orders like the values): the input of the channel selection.  Same grid
+// and row mapping as the staging; `chmax` is cleared before the launch.
+template <int D>
+__global__ void __launch_bounds__(kStageThreads, 2) chan_max_kernel(AttnParams p) {
+    constexpr int NA = D / 64;
+    constexpr int kRowsPerPass = kStageThreads / 8;
+    constexpr int kPasses = kBN / kRowsPerPass;
+    __shared__ unsigned s_max[D];
+    const int j = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+    const int rsub = threadIdx.x >> 3, l8 = threadIdx.x & 7;
+    HeadRows hr;
+    hr.load(p, h);
+    const int n_stored = hr.n_rows - p.S_new;
+    if (j * kBN >= hr.n_rows) return;
+    for (int d = threadIdx.x; d < D; d += kStageThreads) s_max[d] = 0u;
+    __syncthreads();
+    const int32_t* hrows = p.rows + (int64_t)h * p.S_kv;
+    float m[NA][8];
+#pragma unroll
+    for (int a = 0; a < NA; ++a)
+#pragma unroll
+        for (int i = 0; i < 8; ++i) m[a][i] = 0.0f;
+#pragma unroll
+    for (int i = 0; i < kPasses; ++i) {
+        const int idx = j * kBN + i * kRowsPerPass + rsub;
+        RawRow<NA> raw;
+        if (idx >= n_stored && idx < hr.n_rows)
+            load_dense_row<D>(p, b, h, idx - n_stored, l8, raw);
+        else
+            load_raw_row<D>(p, b, idx < n_stored ? __ldg(hrows + idx) : -1, l8, raw);
+#pragma unroll
+        for (int a = 0; a < NA; ++a) {
+            float x[8];
+            raw_k_f32<D>(raw, a, l8, x);
+#pragma unroll
+            for (int t = 0; t < 8; ++t) m[a][t] = fmaxf(m[a][t], fabsf(x[t]));
+        }
+    }
+#pragma unroll
+    for (int a = 0; a < NA; ++a)
+#pragma unroll
+        for (int t = 0; t < 8; ++t)
+            if (m[a][t] > 0.0f) atomicMax(&s_max[a * 64 + l8 * 8 + t], __float_as_uint(m[a][t]));
+    __syncthreads();
+    for (int d = threadIdx.x; d < D; d += kStageThreads)
+        if (s_max[d]) atomicMax(p.chmax + (int64_t)h * D + d, s_max[d]);
+}
+
+// Per KV head, the kLoCh channels of largest max |K| (ties: lower channel first), written in
+// ascending channel order.  One block of D threads per head.
+template <int D>
+__global__ void __launch_bounds__(D) chan_select_kernel(AttnParams p) {
+    __shared__ unsigned s_v[D];
+    __shared__ int s_flag[D];
+    const int h = blockIdx.x, d = threadIdx.x;
+    const unsigned v = p.chmax[(int64_t)h * D + d];
+    s_v[d] = v;
+    __syncthreads();
+    int rank = 0;
+    for (int e = 0; e < D; ++e) {
+        const unsigned w = s_v[e];
+        rank += (w > v || (w == v && e < d)) ? 1 : 0;
+    }
+    const bool chosen = rank < kLoCh;
+    s_flag[d] = chosen ? 1 : 0;
+    __syncthreads();
+    if (chosen) {
+        int pos = 0;
+        for (int e = 0; e < d; ++e) pos += s_flag[e];
+        p.sel[(int64_t)h * kLoCh + pos] = d;
+    }
 }
 
 // ------------------------------------------------------------------------------ attention
@@ -447,18 +598,21 @@ __device__ __forceinline__ void out_store(const AttnParams& p, int64_t idx, floa
     for (int r = 0; r < p.n_peers; ++r) st_global_f2(p.peers[r] + idx, v);
 }
 
-// Peer epilogue: a softmax warp stages 8 finished output rows -- contiguous in every rank's
+// Peer epilogue: a softmax warp stages 4 finished output rows -- contiguous in every rank's
 // buffer -- in its shared-memory slot and sends them with one bulk copy per rank, so whole rows
-// cross NVLink as large writes and the warp does not stall on remote stores.
+// cross NVLink as large writes and the warp does not stall on remote stores.  The 16x256b TMEM
+// share gives a warp 8 rows per pass (lane >> 2); the slot takes them in two halves, lanes
+// 16 * sub .. 16 * sub + 15 (rows 4 * sub .. 4 * sub + 3), each pass reading O again.
 // stage_acquire: the copies that read the slot last time have read it (the slot may be rewritten).
 __device__ __forceinline__ void stage_acquire(int lane) {
     if (lane == 0) bulk_wait_read0();
     __syncwarp();
 }
-// this lane's two values of chunk c, part k of slot row (lane >> 2) (the 16x256b share)
+// this lane's two values of chunk c, part k of slot row (lane >> 2) & 3, when its row is in half `sub`
 template <int D>
-__device__ __forceinline__ void stage_put(float* slot, int lane, int c, int k, float2 v) {
-    *reinterpret_cast<float2*>(slot + (lane >> 2) * D + c * 32 + 8 * k + 2 * (lane & 3)) = v;
+__device__ __forceinline__ void stage_put(float* slot, int lane, int sub, int c, int k, float2 v) {
+    if ((lane >> 4) == sub)
+        *reinterpret_cast<float2*>(slot + ((lane >> 2) & 3) * D + c * 32 + 8 * k + 2 * (lane & 3)) = v;
 }
 // slot rows [0, n) -> element idx of every rank's buffer
 template <int D>
@@ -486,9 +640,10 @@ __device__ __noinline__ void merge_parts(const AttnParams& p, uint32_t tO, int h
                                          float faB, float mA, float mB, float iA, float iB, int np, int slot, int rt,
                                          int lane, int nrows, int64_t obase, uint64_t* o_empty, float* oslot) {
     if constexpr (PEERS) {
-        // rows rA (slot pass 0) then rows rB (pass 1), each staged whole and bulk-stored
-#pragma unroll
-        for (int half = 0; half < 2; ++half) {
+        // rows rA (slot passes 0, 1) then rows rB (passes 2, 3), each staged and bulk-stored
+#pragma unroll 1
+        for (int pass = 0; pass < 4; ++pass) {
+            const int half = pass >> 1, sub = pass & 1;
             const int r = half ? rB : rA;
             const float fr = half ? faB : faA, mr = half ? mB : mA, ir = half ? iB : iA;
             stage_acquire(lane);
@@ -497,7 +652,7 @@ __device__ __noinline__ void merge_parts(const AttnParams& p, uint32_t tO, int h
                 uint32_t o[16];
                 tmem_ld16x256b_x4(tO + c * 32 + ((uint32_t)(hf * 16) << 16), o);
                 tmem_wait_ld();
-                if (hf == 1 && half == 1 && c == D / 32 - 1) {
+                if (hf == 1 && pass == 3 && c == D / 32 - 1) {
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(o_empty);
@@ -519,10 +674,10 @@ __device__ __noinline__ void merge_parts(const AttnParams& p, uint32_t tO, int h
                     }
                 }
 #pragma unroll
-                for (int k = 0; k < 4; ++k) stage_put<D>(oslot, lane, c, k, v[k]);
+                for (int k = 0; k < 4; ++k) stage_put<D>(oslot, lane, sub, c, k, v[k]);
             }
-            const int r0 = hf * 16 + half * 8;
-            stage_flush<D>(p, oslot, lane, obase + (int64_t)r0 * D, min(8, nrows - r0));
+            const int r0 = hf * 16 + half * 8 + sub * 4;
+            stage_flush<D>(p, oslot, lane, obase + (int64_t)r0 * D, min(4, nrows - r0));
         }
         return;
     }
@@ -583,15 +738,16 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBar);
     uint64_t* q_full = bars;            // expect_tx arrive + TMA bytes, per segment
     uint64_t* q_empty = bars + 1;       // commit after the segment's last S MMAs
-    uint64_t* k_full = bars + 2;        // [0]: the single K stage (hi + lo tiles)
+    uint64_t* k_full = bars + 2;        // [2] ring stages (K tile + lo tile of the selected channels)
     uint64_t* v_full = bars + 4;        // [2]
-    uint64_t* k_empty = bars + 6;       // [0]: commit after the step's last S MMAs
+    uint64_t* k_empty = bars + 6;       // [2] commit
     uint64_t* v_empty = bars + 8;       // [2] commit
     uint64_t* s_full = bars + 10;       // [2] per query tile, commit
     uint64_t* p_full = bars + 12;       // [2] per query tile, 4 softmax warps
     uint64_t* o_full = bars + 14;       // [2] per query tile, commit after the segment's last P*V
     uint64_t* o_empty = bars + 16;      // [2] per query tile, 4 softmax warps (O read out)
     uint64_t* drain = bars + 18;        // commit, drain before TMEM release
+    uint64_t* qc_full = bars + 19;      // loader warp: the segment's Q_c tiles are in shared memory
     int* hp = reinterpret_cast<int*>(smem + L::kHP);
     int* misc = reinterpret_cast<int*>(smem + L::kMisc);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kTmemSlot);
@@ -610,6 +766,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             mbar_init(&o_empty[s], 4);
         }
         mbar_init(drain, 1);
+        mbar_init(qc_full, 1);
         fence_mbarrier_init();
         int acc = 0;            // below 2^31: H * ntmax is checked on the host
         int ntm = 0;
@@ -820,9 +977,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                 }
                 if (np == 1) {
                     if constexpr (PEERS) {
-                        // rows rA, then rows rB, staged whole: per pass this row's partial values
-                        // first (their loads overlap), then O chunk by chunk (read once per pass)
-#pragma unroll
+                        // rows rA, then rows rB, each in two slot halves: per row the partial
+                        // values first (their loads overlap), then O chunk by chunk per pass
+#pragma unroll 1
                         for (int half = 0; half < 2; ++half) {
                             const int r = half ? rB : rA;
                             const float fbr = half ? fbB : fbA, far = half ? faB : faA;
@@ -833,25 +990,28 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                                 for (int k = 0; k < 4; ++k)
                                     px[c][k] = __ldcg(reinterpret_cast<const float2*>(
                                         src + (int64_t)r * D + c * 32 + 8 * k + 2 * (lane & 3)));
-                            stage_acquire(lane);
+#pragma unroll 1
+                            for (int sub = 0; sub < 2; ++sub) {
+                                stage_acquire(lane);
 #pragma unroll
-                            for (int c = 0; c < D / 32; ++c) {
-                                uint32_t o[16];
-                                tmem_ld16x256b_x4(tO + c * 32 + ((uint32_t)(hf * 16) << 16), o);
-                                tmem_wait_ld();
-                                if (hf == 1 && half == 1 && c == D / 32 - 1) {
-                                    tc_fence_before();
-                                    __syncwarp();
-                                    if (lane == 0) mbar_arrive(&o_empty[t]);
+                                for (int c = 0; c < D / 32; ++c) {
+                                    uint32_t o[16];
+                                    tmem_ld16x256b_x4(tO + c * 32 + ((uint32_t)(hf * 16) << 16), o);
+                                    tmem_wait_ld();
+                                    if (hf == 1 && half == 1 && sub == 1 && c == D / 32 - 1) {
+                                        tc_fence_before();
+                                        __syncwarp();
+                                        if (lane == 0) mbar_arrive(&o_empty[t]);
+                                    }
+#pragma unroll
+                                    for (int k = 0; k < 4; ++k)
+                                        stage_put<D>(oslot, lane, sub, c, k,
+                                                     make_float2(fmaf(px[c][k].x, fbr, __uint_as_float(o[4 * k + 2 * half]) * far),
+                                                                 fmaf(px[c][k].y, fbr, __uint_as_float(o[4 * k + 2 * half + 1]) * far)));
                                 }
-#pragma unroll
-                                for (int k = 0; k < 4; ++k)
-                                    stage_put<D>(oslot, lane, c, k,
-                                                 make_float2(fmaf(px[c][k].x, fbr, __uint_as_float(o[4 * k + 2 * half]) * far),
-                                                             fmaf(px[c][k].y, fbr, __uint_as_float(o[4 * k + 2 * half + 1]) * far)));
+                                const int r0 = hf * 16 + half * 8 + sub * 4;
+                                stage_flush<D>(p, oslot, lane, obase + (int64_t)r0 * D, min(4, nrows - r0));
                             }
-                            const int r0 = hf * 16 + half * 8;
-                            stage_flush<D>(p, oslot, lane, obase + (int64_t)r0 * D, min(8, nrows - r0));
                         }
                         continue;
                     }
@@ -891,10 +1051,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                 }
                 if constexpr (PEERS) {
                     if (!split_tail) {
-                        // rows rA, then rows rB, staged whole; O read chunk by chunk per pass so
-                        // that few registers stay live beside the bulk-store issue
-#pragma unroll
-                        for (int half = 0; half < 2; ++half) {
+                        // rows rA, then rows rB, each in two slot halves; O read chunk by chunk
+                        // per pass so that few registers stay live beside the bulk-store issue
+#pragma unroll 1
+                        for (int pass = 0; pass < 4; ++pass) {
+                            const int half = pass >> 1, sub = pass & 1;
                             const float fr = half ? faB : faA;
                             stage_acquire(lane);
 #pragma unroll
@@ -902,19 +1063,19 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                                 uint32_t o[16];
                                 tmem_ld16x256b_x4(tO + c * 32 + ((uint32_t)(hf * 16) << 16), o);
                                 tmem_wait_ld();
-                                if (hf == 1 && half == 1 && c == D / 32 - 1) {
+                                if (hf == 1 && pass == 3 && c == D / 32 - 1) {
                                     tc_fence_before();
                                     __syncwarp();
                                     if (lane == 0) mbar_arrive(&o_empty[t]);
                                 }
 #pragma unroll
                                 for (int k = 0; k < 4; ++k)
-                                    stage_put<D>(oslot, lane, c, k,
+                                    stage_put<D>(oslot, lane, sub, c, k,
                                                  make_float2(__uint_as_float(o[4 * k + 2 * half]) * fr,
                                                              __uint_as_float(o[4 * k + 2 * half + 1]) * fr));
                             }
-                            const int r0 = hf * 16 + half * 8;
-                            stage_flush<D>(p, oslot, lane, obase + (int64_t)r0 * D, min(8, nrows - r0));
+                            const int r0 = hf * 16 + half * 8 + sub * 4;
+                            stage_flush<D>(p, oslot, lane, obase + (int64_t)r0 * D, min(4, nrows - r0));
                         }
                         continue;
                     }
@@ -976,51 +1137,97 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         }
     } else if (warp == kLoadWarp) {
         // ------------------------------------------------------------------ loader
-        if (lane == 0) {
-            Segment sg;
-            long long g = 0;
-            int si = 0, nq = 0;
-            int nk[2] = {0, 0}, nv[2] = {0, 0};          // copies issued per stage
-            bool ok = true;
-            while (ok && sched.next(sg)) {
-                if (si > 0 && !mbar_wait_spin(q_empty, (uint32_t)((si - 1) & 1), p.err, kErrQEmpty)) break;
+        // Lane 0 issues every copy; with the lo correction the whole warp then gathers the
+        // segment's Q_c tiles (the queries' selected channels) from the Q tiles once they land.
+        Segment sg;
+        long long g = 0;
+        int si = 0, nq = 0;
+        int nk[2] = {0, 0}, nv[2] = {0, 0};          // copies issued per stage (lane 0)
+        bool ok = true;
+        // lane 0 waits, the warp agrees on the outcome
+        auto lane0_wait = [&](uint64_t* bar, uint32_t parity, int code) -> bool {
+            int r = 1;
+            if (lane == 0) r = mbar_wait_spin(bar, parity, p.err, code) ? 1 : 0;
+            return __shfl_sync(0xffffffffu, r, 0) != 0;
+        };
+        while (ok && sched.next(sg)) {
+            if (si > 0 && !lane0_wait(q_empty, (uint32_t)((si - 1) & 1), kErrQEmpty)) break;
+            const int qrow = (sg.b * p.H + sg.h) * p.S_q + sg.qp * kUnitRows;
+            if (lane == 0) {
                 mbar_arrive_expect_tx(q_full, 2 * TB);
-                const int qrow = (sg.b * p.H + sg.h) * p.S_q + sg.qp * kUnitRows;
 #pragma unroll
                 for (int t = 0; t < 2; ++t)
 #pragma unroll
                     for (int a = 0; a < NA; ++a)
                         tma_load_2d(smem + L::kQ + t * TB + a * kBM * 128, &qmap, a * 64, qrow + t * kBM, q_full);
-                ++nq;
-                const uint8_t* gkv = p.stage + staged_offset(p, sg.b, sg.h / p.rep, 0, 0, TB);
-                HeadRows hr;
-                hr.load(p, sg.h);
-                for (int j = sg.j0; j < sg.j1; ++j, ++g) {
-                    const int s = (int)(g & 1);
-                    // K: one stage holding the hi tile and, unless the tile is exact, the lo tile;
-                    // hi tiles only (fast K): a two-stage ring
-                    const int ks = p.klo ? 0 : s;
-                    const bool kwait = p.klo ? g >= 1 : g >= 2;
-                    const uint32_t kpar = p.klo ? (uint32_t)((g - 1) & 1) : (uint32_t)(((g >> 1) - 1) & 1);
-                    if (kwait && !mbar_wait_spin(&k_empty[ks], kpar, p.err, kErrKEmpty)) {
-                        ok = false;
-                        break;
-                    }
-                    const uint32_t kbytes = hr.exact(j) ? TB : 2 * TB;
-                    mbar_arrive_expect_tx(&k_full[ks], kbytes);
-                    bulk_g2s(smem + L::kK + ks * TB, gkv + ((int64_t)j * kStagedTiles + kTileKHi) * TB, kbytes,
-                             &k_full[ks]);
-                    ++nk[ks];
-                    if (g >= 2 && !mbar_wait_spin(&v_empty[s], (uint32_t)(((g >> 1) - 1) & 1), p.err, kErrVEmpty)) {
-                        ok = false;
-                        break;
-                    }
+            }
+            ++nq;
+            const uint8_t* gkv = p.stage + staged_offset(p, sg.b, sg.h / p.rep, 0, D);
+            HeadRows hr;
+            hr.load(p, sg.h);
+            const int selc = p.klo && lane < kLoCh ? __ldg(p.sel + (int64_t)(sg.h / p.rep) * kLoCh + lane) : 0;
+            for (int j = sg.j0; j < sg.j1; ++j, ++g) {
+                const int s = (int)(g & 1);
+                const uint8_t* set = gkv + (int64_t)j * staged_set_bytes(D);
+                if (g >= 2 && !lane0_wait(&k_empty[s], (uint32_t)(((g >> 1) - 1) & 1), kErrKEmpty)) {
+                    ok = false;
+                    break;
+                }
+                if (lane == 0) {
+                    // K and, unless the tile is exact in fp16, the lo tile of the selected channels
+                    const bool lo = !hr.exact(j);
+                    mbar_arrive_expect_tx(&k_full[s], lo ? TB + kLoTile : TB);
+                    bulk_g2s(smem + L::kK + s * TB, set, TB, &k_full[s]);
+                    if (lo) bulk_g2s(smem + L::kKc + s * kLoTile, set + 2 * TB, kLoTile, &k_full[s]);
+                    ++nk[s];
+                }
+                if (g >= 2 && !lane0_wait(&v_empty[s], (uint32_t)(((g >> 1) - 1) & 1), kErrVEmpty)) {
+                    ok = false;
+                    break;
+                }
+                if (lane == 0) {
                     mbar_arrive_expect_tx(&v_full[s], TB);
-                    bulk_g2s(smem + L::kV + s * TB, gkv + ((int64_t)j * kStagedTiles + kTileV) * TB, TB, &v_full[s]);
+                    bulk_g2s(smem + L::kV + s * TB, set + TB, TB, &v_full[s]);
                     ++nv[s];
                 }
-                ++si;
+                if (j == sg.j0 && p.klo) {
+                    // Q_c: the selected channels of both query tiles, 32-byte-swizzled rows.  The
+                    // previous segment's S MMAs (the last readers of Q_c) completed before q_empty.
+                    if (!warp_wait(q_full, (uint32_t)(si & 1), p.err, kErrQFull)) {
+                        ok = false;
+                        break;
+                    }
+                    int sc[kLoCh];
+#pragma unroll
+                    for (int i = 0; i < kLoCh; ++i) sc[i] = __shfl_sync(0xffffffffu, selc, i) & (D - 1);  // in the tile
+#pragma unroll 1
+                    for (int t = 0; t < 2; ++t) {
+                        const uint8_t* qt = smem + L::kQ + t * TB;
+                        uint8_t* qc = smem + L::kQc + t * kLoTile;
+#pragma unroll 1
+                        for (int r = lane; r < kBM; r += 32) {
+                            uint32_t w[kLoCh / 2];
+#pragma unroll
+                            for (int i = 0; i < kLoCh; i += 2) {
+                                const int c0 = sc[i], c1 = sc[i + 1];
+                                const uint32_t lo16 = *reinterpret_cast<const uint16_t*>(
+                                    qt + (c0 >> 6) * (kBM * 128) + sw128_offset(r, (c0 & 63) >> 3) + (c0 & 7) * 2);
+                                const uint32_t hi16 = *reinterpret_cast<const uint16_t*>(
+                                    qt + (c1 >> 6) * (kBM * 128) + sw128_offset(r, (c1 & 63) >> 3) + (c1 & 7) * 2);
+                                w[i / 2] = lo16 | (hi16 << 16);
+                            }
+                            *reinterpret_cast<uint4*>(qc + sw32_offset(r, 0)) = make_uint4(w[0], w[1], w[2], w[3]);
+                            *reinterpret_cast<uint4*>(qc + sw32_offset(r, 1)) = make_uint4(w[4], w[5], w[6], w[7]);
+                        }
+                    }
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(qc_full);
+                }
             }
+            ++si;
+        }
+        if (lane == 0) {
             // every copy issued lands before the CTA can exit (a no-op when the MMA consumed them)
             if (nq) mbar_wait_spin(q_full, (uint32_t)((nq - 1) & 1), p.err, kErrCopy);
             for (int s = 0; s < 2; ++s) {
@@ -1035,10 +1242,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             const uint32_t idesc_s = idesc_f16_f32(kBM, kBN, false, false);
             const uint32_t idesc_o = idesc_f16_f32(kBM, D, false, true);
             const uint32_t q_base = smem_u32(smem + L::kQ);
+            const uint32_t qc_base = smem_u32(smem + L::kQc);
             // K stage of step g and the parity of its full barrier
-            auto kstage = [&](long long g) { return p.klo ? 0 : (int)(g & 1); };
-            auto kparity = [&](long long g) { return p.klo ? (uint32_t)(g & 1) : (uint32_t)((g >> 1) & 1); };
-            // S_t = Q_t K_hi^T, then += Q_t K_lo^T unless the tile is exact in fp16
+            auto kstage = [&](long long g) { return (int)(g & 1); };
+            auto kparity = [&](long long g) { return (uint32_t)((g >> 1) & 1); };
+            // S_t = Q_t K^T (fp16), then += Q_c,t K_lo^T over the selected channels (one K = 16 step)
+            // unless the tile is exact in fp16
             auto issue_s = [&](int t, long long g, bool lo) {
                 const uint32_t k_base = smem_u32(smem + L::kK + kstage(g) * TB);
 #pragma unroll
@@ -1047,14 +1256,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                     umma_f16(tmem + t * kBN, smem_desc_sw128(q_base + t * TB + off, 16, 1024),
                              smem_desc_sw128(k_base + off, 16, 1024), idesc_s, k > 0 ? 1u : 0u);
                 }
-                if (lo) {
-#pragma unroll
-                    for (int k = 0; k < D / 16; ++k) {
-                        const uint32_t off = (k >> 2) * (kBN * 128) + (k & 3) * 32;
-                        umma_f16(tmem + t * kBN, smem_desc_sw128(q_base + t * TB + off, 16, 1024),
-                                 smem_desc_sw128(k_base + TB + off, 16, 1024), idesc_s, 1u);
-                    }
-                }
+                if (lo)
+                    umma_f16(tmem + t * kBN, smem_desc_sw32(qc_base + t * kLoTile, 16, 256),
+                             smem_desc_sw32(smem_u32(smem + L::kKc + kstage(g) * kLoTile), 16, 256), idesc_s, 1u);
             };
             auto issue_pv = [&](int t, long long g, bool acc) {
                 const uint32_t v_base = smem_u32(smem + L::kV + (int)(g & 1) * TB);
@@ -1073,6 +1277,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                 HeadRows hr;
                 hr.load(p, sg.h);
                 if (!mbar_wait_spin(q_full, (uint32_t)(si & 1), p.err, kErrQFull) ||
+                    (p.klo && !mbar_wait_spin(qc_full, (uint32_t)(si & 1), p.err, kErrQFull)) ||
                     !mbar_wait_spin(&k_full[kstage(g)], kparity(g), p.err, kErrKFull)) {
                     ok = false;
                     break;
@@ -1246,11 +1451,18 @@ int skv_head_index(const int32_t* slot, int S, int H, int32_t* rows, int32_t* co
     return check_launch("head_index");
 }
 
+// Bytes of the per-KV-head channel maxima (uint32 [H, D]) and selected channels (int32 [H, kLoCh]),
+// each rounded up to 256 bytes.
+static size_t chan_bytes(int H, int D) {
+    return (((size_t)H * D * 4 + 255) & ~size_t(255)) + (((size_t)H * kLoCh * 4 + 255) & ~size_t(255));
+}
+
 size_t skv_packed_attention_scratch_bytes(int B, int H, int S_kv, int D) {
     if (B <= 0 || H <= 0 || S_kv <= 0 || (D != 64 && D != 128)) return 0;
     const size_t ntmax = (size_t)(S_kv + kBN - 1) / kBN;
     const size_t slots = (size_t)sm_count();
-    return (size_t)B * H * ntmax * kStagedTiles * staged_tile_bytes(D)   // staged K hi, K lo, V tiles
+    return (size_t)B * H * ntmax * staged_set_bytes(D)                // staged K, V, K lo tiles
+           + chan_bytes(H, D)                                          // channel maxima, selection
            + slots * kUnitRows * D * sizeof(float)                    // partial O
            + slots * kUnitRows * sizeof(float2)                       // partial (max, sum)
            + ((slots * sizeof(int) + 255) & ~size_t(255));            // partial flags
@@ -1311,7 +1523,10 @@ int attn_params(const void* q, int B, int H, int S_q, int D, const skv_bucket* b
     prm.stage = reinterpret_cast<uint8_t*>(scratch);
     prm.ntmax = (S_kv + S_new + kBN - 1) / kBN;
     prm.slots = max_ctas > 0 && max_ctas < sm_count() ? max_ctas : sm_count();
-    uint8_t* part = prm.stage + (size_t)B * H_kv * prm.ntmax * kStagedTiles * staged_tile_bytes(D);
+    uint8_t* part = prm.stage + (size_t)B * H_kv * prm.ntmax * staged_set_bytes(D);
+    prm.chmax = reinterpret_cast<unsigned*>(part);
+    prm.sel = reinterpret_cast<int*>(part + (((size_t)H_kv * D * 4 + 255) & ~size_t(255)));
+    part += chan_bytes(H_kv, D);
     prm.part_o = reinterpret_cast<float*>(part);
     part += (size_t)prm.slots * kUnitRows * D * sizeof(float);
     prm.part_ml = reinterpret_cast<float2*>(part);
@@ -1343,10 +1558,28 @@ int skv_stage_kv_tiles_gqa(const skv_bucket* buckets, int B, int H_kv, int S_kv,
                                nullptr, 0, 0, 0, flags);
     if (st != SKV_OK) return st;
     const dim3 grid((unsigned)prm.ntmax, (unsigned)H_kv, (unsigned)B);
+    cudaStream_t s = as_stream(stream);
+    if (prm.klo) {
+        // the kLoCh channels of largest max |K| per KV head, whose lo parts are staged
+        if (cudaMemsetAsync(prm.chmax, 0, (size_t)H_kv * D * 4, s) != cudaSuccess)
+            return fail(SKV_ERR_CUDA, "stage_kv_tiles: memset failed");
+        if (D == 128)
+            chan_max_kernel<128><<<grid, kStageThreads, 0, s>>>(prm);
+        else
+            chan_max_kernel<64><<<grid, kStageThreads, 0, s>>>(prm);
+        int e = check_launch("stage_kv_tiles (channel maxima)");
+        if (e) return e;
+        if (D == 128)
+            chan_select_kernel<128><<<H_kv, 128, 0, s>>>(prm);
+        else
+            chan_select_kernel<64><<<H_kv, 64, 0, s>>>(prm);
+        e = check_launch("stage_kv_tiles (channel selection)");
+        if (e) return e;
+    }
     if (D == 128)
-        stage_tiles_kernel<128><<<grid, kStageThreads, 0, as_stream(stream)>>>(prm);
+        stage_tiles_kernel<128><<<grid, kStageThreads, 0, s>>>(prm);
     else
-        stage_tiles_kernel<64><<<grid, kStageThreads, 0, as_stream(stream)>>>(prm);
+        stage_tiles_kernel<64><<<grid, kStageThreads, 0, s>>>(prm);
     return check_launch("stage_kv_tiles");
 }
 

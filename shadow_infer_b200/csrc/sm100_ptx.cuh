@@ -250,6 +250,18 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr, uint32_t lbo
     return d;
 }
 
+// Shared-memory matrix descriptor with 32-byte swizzle (layout type 6, version 1): K-major rows
+// of 32 bytes, 8-row groups `sbo_bytes` apart (the chunk index XORed with bit 2 of the row).
+__device__ __forceinline__ uint64_t smem_desc_sw32(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr >> 4) & 0x3FFF);
+    d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFF) << 16;
+    d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFF) << 32;
+    d |= (uint64_t)1 << 46;   // version
+    d |= (uint64_t)6 << 61;   // SWIZZLE_32B
+    return d;
+}
+
 // Byte offset of 16-byte chunk `chunk` (0..7) of row `row` inside a 128B-swizzled atom
 // whose rows are 128 bytes apart.
 __device__ __forceinline__ uint32_t sw128_offset(int row, int chunk) {

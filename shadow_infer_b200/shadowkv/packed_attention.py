@@ -61,11 +61,12 @@ def packed_attention(
     before reading it, and again before the next call that writes the same buffers, so that
     no rank overwrites a buffer another rank is still reading.
 
-    Precision: Q, V and the softmax weights P are fp16 tensor-core operands, K enters as an fp16
-    pair hi + lo (~22 bits) contracted in two MMA chains, accumulation and softmax are fp32:
-    relative L2 <= 1e-3 against the reference's fp32 attention, also when K has outlier
-    channels.  ``fast_k=True`` stages K in fp16 only (one MMA chain): faster, with fp16's 2^-11
-    relative error on every K element, which channel outliers of K turn into ~2e-3.
+    Precision: Q, K, V and the softmax weights P are fp16 tensor-core operands with fp32
+    accumulation and softmax; the 16 channels of largest max |K| in each KV head also contribute
+    the lo part of K (k - fp16(k)) through one extra K = 16 MMA, so channel outliers of K (a few
+    channels ten times larger than the rest) do not turn fp16's 2^-11 rounding into the dominant
+    error: relative L2 <= 1e-3 against the reference's fp32 attention.  ``fast_k=True`` skips the
+    channel selection and the lo part (K in fp16 only; ~2e-3 with outlier channels).
 
     ``attention_mask``: accepted for the reference's signature; like
     ``SimpleDiffusionLLM._compute_block`` (simple_diffusion_llm.py:140-142), which raises when an
