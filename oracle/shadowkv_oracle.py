@@ -580,6 +580,20 @@ def attention(q: np.ndarray, k: np.ndarray, v: np.ndarray, scale: Optional[float
     return out
 
 
+def attention_f32(q: np.ndarray, k: np.ndarray, v: np.ndarray, scale: Optional[float] = None) -> np.ndarray:
+    """The same attention in the reference's own float32 arithmetic (simple_diffusion_llm.py:165-169:
+    fp32 matmuls and softmax).  The CPU baselines time this one -- it runs at the speed of the
+    reference's torch CPU path -- while the float64 ``attention`` above is the parity checker."""
+    D = q.shape[-1]
+    if scale is None:
+        scale = 1.0 / np.sqrt(D)
+    s = np.matmul(q.astype(np.float32), np.swapaxes(k.astype(np.float32), -1, -2)) * np.float32(scale)
+    s -= s.max(axis=-1, keepdims=True)
+    np.exp(s, out=s)
+    s /= s.sum(axis=-1, keepdims=True)
+    return np.matmul(s, v.astype(np.float32))
+
+
 def repeat_kv(x: np.ndarray, n_rep: int) -> np.ndarray:
     """``[B, H_kv, S, D] -> [B, H_kv * n_rep, S, D]``, head h of the result = head h // n_rep
     (diffusion_llama.py:300-308)."""

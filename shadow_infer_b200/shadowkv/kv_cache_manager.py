@@ -104,6 +104,69 @@ class ImportanceAgeEvictionPolicy(EvictionPolicy):
         return _select_lowest(entries, self._score, budget_bytes, current_usage_bytes, estimated_entry_bytes)
 
 
+def _policy_keys(entries: List[TokenHeadScore], policy: EvictionPolicy):
+    """float64 sort keys of the built-in policies, the same IEEE values the reference computes
+    (``importance`` or ``importance * (1 - age_decay) ** age``, the power taken by Python per
+    distinct age)."""
+    import numpy as np
+    n = len(entries)
+    imp = np.fromiter((e.importance for e in entries), dtype=np.float64, count=n)
+    if isinstance(policy, ImportanceAgeEvictionPolicy):
+        ages = np.fromiter((e.age for e in entries), dtype=np.int64, count=n)
+        uniq, inv = np.unique(ages, return_inverse=True)
+        factor = np.array([(1.0 - policy.age_decay) ** int(a) for a in uniq], dtype=np.float64)
+        imp = imp * factor[inv]
+    return imp
+
+
+def _select_lowest_device(entries: List[TokenHeadScore], policy: EvictionPolicy, budget_bytes: int,
+                          current_usage_bytes: int, estimated_entry_bytes: int, packed: Any) -> List[TokenHeadScore]:
+    """The built-in policies' selection (eviction_policy.py:40-98: the ``num_to_evict`` entries
+    of smallest key in a stable sort) without the Python sort, and the in-place eviction of the
+    chosen entries from ``packed``.  Keys that float32 holds exactly (finite, no -0.0) are
+    selected on the GPU by the rank select of ``enforce_global_budget`` (score = key, position =
+    list order, the stable sort's tie order); other keys by a float64 stable argsort.  Returns the
+    chosen entries."""
+    import numpy as np
+    if current_usage_bytes <= budget_bytes or not entries:
+        return []
+    n = len(entries)
+    target_reduction = current_usage_bytes - budget_bytes
+    k = min(n, max(1, int(target_reduction // max(1, estimated_entry_bytes))))
+    keys = _policy_keys(entries, policy)
+    dev = packed._ensure_state() if packed.packed_data else compute_device()
+    k32 = keys.astype(np.float32)
+    exact = bool(np.all(np.isfinite(keys)) and np.array_equal(k32.astype(np.float64), keys) and
+                 not np.any((keys == 0) & np.signbit(keys)))
+    if exact and n < (1 << 31):
+        lib = _lib.load()
+        score = torch.from_numpy(k32).to(dev)
+        weight = torch.ones(n, dtype=torch.int64, device=dev)
+        res = torch.empty(2, dtype=torch.int64, device=dev)
+        mask = torch.empty(n, dtype=torch.uint8, device=dev)
+        scr = scratch(lib.skv_rank_select_scratch_bytes(n), dev)
+        stream = _lib.stream_of(dev)
+        with device_ctx(dev):
+            _lib.check(lib.skv_rank_select(_lib.ptr(score), _lib.ptr(weight), n, k, _lib.ptr(scr), scr.numel(),
+                                           _lib.ptr(res), stream), "_enforce_budget")
+            _lib.check(lib.skv_mark_smallest(_lib.ptr(score), n, _lib.ptr(res), _lib.ptr(mask), stream),
+                       "_enforce_budget")
+        chosen_idx = torch.nonzero(mask, as_tuple=True)[0].cpu().numpy()
+        if int(res[0].item()) < 0:
+            raise RuntimeError("_enforce_budget: the selection kernel's grid barrier timed out")
+    else:
+        chosen_idx = np.sort(np.argsort(keys, kind="stable")[:k])
+    chosen = [entries[i] for i in chosen_idx.tolist()]
+    S, H = int(packed.seq_len), int(packed.num_heads)
+    tok = np.fromiter((e.token_idx for e in chosen), dtype=np.int64, count=len(chosen))
+    head = np.fromiter((e.head_idx for e in chosen), dtype=np.int64, count=len(chosen))
+    inside = (tok >= 0) & (tok < S) & (head >= 0) & (head < H)
+    ev = torch.zeros(S * H, dtype=torch.bool)
+    ev[torch.from_numpy(tok[inside] * H + head[inside])] = True
+    packed.evict(ev.view(S, H).to(dev))
+    return chosen
+
+
 def _resident_entry_cost(packed: Any) -> List[int]:
     """Resident bytes one stored entry of each precision takes in ``packed``: its K/V payload,
     its scales and the per-entry metadata (the quantities ``resident_bytes`` sums)."""
@@ -306,7 +369,16 @@ class KVCacheManager:
             estimated_entry_bytes = max(1, int(packed.memory_bytes()) // total_entries)
         else:
             estimated_entry_bytes = (getattr(packed, "batch_size", 1) or 1) * (getattr(packed, "head_dim", 1) or 1)
-        to_evict = self.eviction_policy.select_for_eviction(
+        policy = self.eviction_policy
+        if type(policy) in (LeastImportantEvictionPolicy, ImportanceAgeEvictionPolicy) and \
+                getattr(packed, "_slot", None) is not None:
+            chosen = _select_lowest_device(list(meta.values()), policy, self.memory_budget_bytes, current_usage,
+                                           estimated_entry_bytes, packed)
+            if chosen:
+                for e in chosen:
+                    e.importance = -1.0
+            return
+        to_evict = policy.select_for_eviction(
             list(meta.values()), budget_bytes=self.memory_budget_bytes, current_usage_bytes=current_usage,
             estimated_entry_bytes=estimated_entry_bytes)
         if to_evict:

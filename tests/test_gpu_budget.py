@@ -109,3 +109,48 @@ def test_global_budget_no_candidates_and_no_budget(skv):
     before = cache.resident_bytes()
     assert mgr.enforce_global_budget(1, sink_tokens=2) == 12  # floor: every non-sink processed
     assert cache.resident_bytes() < before
+
+
+@pytest.mark.parametrize("policy_name,ties", [("least", False), ("least", True), ("age", False)])
+def test_per_layer_budget_device_selection(policy_name, ties):
+    """KVCacheManager._enforce_budget with the built-in policies selects on the GPU (or by a float64
+    argsort when float32 cannot hold the keys) exactly the entries the policy's stable sort picks."""
+    import copy
+    import numpy as np
+    from shadow_infer_b200.shadowkv import (ImportanceAgeEvictionPolicy, KVCacheEntry, KVCacheManager,
+                                            LeastImportantEvictionPolicy, PackedKVCache, PrecisionPlan,
+                                            TokenHeadScore)
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    rng = np.random.default_rng(31 + ties)
+    B, H, S, D = 1, 4, 300, 64
+    k = torch.from_numpy(rng.standard_normal((B, H, S, D)).astype(np.float32)).cuda()
+    codes = torch.from_numpy(rng.integers(1, 4, size=(S, H)).astype(np.int8)).cuda()
+    imp = rng.random((S, H)).astype(np.float32)
+    if ties:
+        imp = np.round(imp * 8) / 8                      # many equal keys: list order decides
+    policy = (LeastImportantEvictionPolicy() if policy_name == "least" else ImportanceAgeEvictionPolicy(0.03))
+
+    def build():
+        cache = PackedKVCache.pack(k, k, None, 16, plan=PrecisionPlan.from_codes(codes))["packed_kv"]
+        meta = {(t, h): TokenHeadScore(0, t, h, importance=float(imp[t, h]), age=int((t * 7 + h) % 11))
+                for t in range(S) for h in range(H)}
+        m = KVCacheManager(num_layers=1, eviction_policy=policy)
+        m.store(0, KVCacheEntry(k_tensor=None, v_tensor=None, precision="mixed", packed_kv=cache))
+        m.set_token_head_meta(0, meta)
+        return m, cache, meta
+
+    m, cache, meta = build()
+    usage = m.get_memory_usage()
+    est = max(1, int(cache.memory_bytes()) // (S * H))
+    want = policy.select_for_eviction(list(copy.deepcopy(meta).values()), int(usage * 0.6), usage, est)
+    m.memory_budget_bytes = int(usage * 0.6)
+    m._enforce_budget(0)
+    got = {(0, t, h) for (t, h), e in meta.items() if e.importance == -1.0}
+    assert got == want and len(want) > 0
+    ref = PackedKVCache.pack(k, k, None, 16, plan=PrecisionPlan.from_codes(codes))["packed_kv"]
+    ref.evict({(t, h) for _, t, h in want})
+    assert cache.memory_bytes() == ref.memory_bytes()
+    ku, _ = cache.unpack()
+    kr, _ = ref.unpack()
+    assert torch.equal(ku, kr)
