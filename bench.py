@@ -509,7 +509,7 @@ def long_context_phase(args, world, rank, dev, dist, lib, heads_total=None, extr
 
     check = check_long_context(full, lambda: packed_attention(q, cache), h0, hs, S, world, rank, dev, dist,
                                lambda h: W.cfg5_layer(h, h + 1), codes_fn, 100)
-    fast = fast_k_compare(q, cache, flops=4.0 * B * hs * S * S * D, reps=3)
+    variants = {v: variant_compare(v, q, cache, flops=4.0 * B * hs * S * S * D, reps=3) for v in ATTN_VARIANTS}
 
     # ---- data plane of the layer: compress+pack and unpack alone (L2 flushed before each call)
     fl = Flush(dev)
@@ -561,7 +561,7 @@ def long_context_phase(args, world, rank, dev, dist, lib, heads_total=None, extr
                       "around the calls inside the timed steps",
         },
         "check": check,
-        "fast_k": fast,
+        "attention_variants": variants,
         "exchange": exchange,
         "gpu_launches": launches,
     }
@@ -935,31 +935,41 @@ def attention_phase(args, world, rank, dev, dist, lib):
         "gpu_launches": launches,
         "output_dtype": "f32",
     }
-    res["fast_k"] = fast_k_compare(qd, cache, flops_rank, reps=10)
+    for v in ATTN_VARIANTS:
+        res[v] = variant_compare(v, qd, cache, flops_rank, reps=10)
     if world == 1 and rank == 0:
         res["vs_sdpa"] = sdpa_compare(args, dev, cache, qd, stage_ms + kms)
         res["gqa_block"] = gqa_block_attention(args, rank, dev, ks, vs, codes, c["group"])
     return res
 
 
-def fast_k_compare(q, cache, flops, reps=3):
-    """The attention with K in fp16 only (``fast_k``, one MMA chain) against the default hi + lo
-    K on the same layer: kernel time and the relative L2 difference of the outputs (the default
-    is within ~3e-4 of the oracle, so the difference is the fast path's extra error)."""
+ATTN_VARIANTS = {
+    "fast_k": ({"fast_k": True}, "K staged in fp16 only (SKV_ATTN_FAST_K): one QK MMA chain, no lo correction"),
+    "one_tile": ({"one_tile": True}, "one query tile of 128 rows per work unit, two score buffers (SKV_ATTN_ONE_TILE)"),
+    "fma_exp": ({"fma_exp": True},
+                "a quarter of the softmax exponentials by a polynomial on the FMA pipe (SKV_ATTN_FMA_EXP)"),
+}
+
+
+def variant_compare(name, q, cache, flops, reps=3):
+    """One optional attention pipeline (``ATTN_VARIANTS``) on the same layer as the default:
+    kernel time and the relative L2 difference of its output to the default's (the default is
+    within ~3e-4 of the oracle, so the difference bounds the variant's extra error)."""
     import torch
     from shadow_infer_b200.shadowkv import packed_attention
+    kw, what = ATTN_VARIANTS[name]
     ref = packed_attention(q, cache)
-    out = packed_attention(q, cache, fast_k=True)
+    out = packed_attention(q, cache, **kw)
     diff = float(((out - ref).double().norm() / ref.double().norm()).item())
+    del ref, out
     evs = [tuple(torch.cuda.Event(enable_timing=True) for _ in range(3)) for _ in range(reps)]
     for e in evs:
-        packed_attention(q, cache, check=False, events=e, fast_k=True)
+        packed_attention(q, cache, check=False, events=e, **kw)
     torch.cuda.synchronize()
     ms = statistics.mean(b.elapsed_time(c_) for _, b, c_ in evs)
-    burst, sustained, _ = tensor_peaks()
+    burst, _, _ = tensor_peaks()
     return {"attention_ms": ms, "achieved_tflops": flops / (ms / 1e3) / 1e12,
-            "frac_of_burst": flops / (ms / 1e3) / 1e12 / burst, "rel_l2_vs_default": diff,
-            "what": "K staged in fp16 only (SKV_ATTN_FAST_K): one QK MMA chain instead of hi + lo"}
+            "frac_of_burst": flops / (ms / 1e3) / 1e12 / burst, "rel_l2_vs_default": diff, "what": what}
 
 
 def sdpa_compare(args, dev, cache, qd, ours_ms, reps=None):
@@ -1109,7 +1119,7 @@ def denoise_phase(args, world, rank, dev, dist, lib):
         mask, st = decide_reuse_mask(k1, v1, kprev[layer], vprev[layer], 16, 16, 0.0, "conservative", zeros)
         plan = PrecisionPlan.from_codes(codes[layer], reuse_mask=mask)
         cur = PackedKVCache.pack(k1, v1, None, c["group"], plan=plan)["packed_kv"]
-        applied = cur.apply_reuse_mask(prev[layer], mask, return_stats=True)["applied"]
+        cur.apply_reuse_mask(prev[layer], mask)
         removed = cur.evict(emask[layer])
         out = packed_attention(qs[layer], cur, check=False, peer_outputs=peers[0] if peers else None,
                                head_offset=h0)
@@ -1117,15 +1127,16 @@ def denoise_phase(args, world, rank, dev, dist, lib):
             all_gather_heads(out, out=gathered)
         if world > 1:
             dist.all_reduce(bar)
-        return cur, st["reuse_ratio"], applied, removed
+        return cur, st, removed
 
     for _ in range(3):                                 # warm-up on layer 0, state untouched
         layer_step(0, drifted(kprev[0]), drifted(vprev[0]))
+    # the reuse statistics are read after the loop (reading them per step would wait for the GPU)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     evs = []
-    ratios, applied_n, removed_n = [], 0, 0
+    stats, removed_n = [], 0
     n0 = lib.skv_launch_count()
     w0 = time.perf_counter()
     for t in range(1, T + 1):
@@ -1133,12 +1144,11 @@ def denoise_phase(args, world, rank, dev, dist, lib):
             k1, v1 = drifted(kprev[layer]), drifted(vprev[layer])
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             a.record()
-            cur, ratio, applied, removed = layer_step(layer, k1, v1)
+            cur, st, removed = layer_step(layer, k1, v1)
             b.record()
             evs.append((a, b))
             prev[layer], kprev[layer], vprev[layer] = cur, k1, v1
-            ratios.append(ratio)
-            applied_n += applied
+            stats.append(st)
             removed_n += removed
     torch.cuda.synchronize()
     wall = time.perf_counter() - w0
@@ -1155,7 +1165,7 @@ def denoise_phase(args, world, rank, dev, dist, lib):
         "value": B * S * T / (total_ms / 1e3), "unit": "tokens/s", "ms_per_layer_step": total_ms / (Lyr * T),
         "loop_ms": total_ms, "host_wall_s": wall,
         "attention_tflops_whole_loop": flops / (total_ms / 1e3) / 1e12,
-        "reuse_ratio_mean": statistics.mean(ratios), "reused_entries_rank0": applied_n,
+        "reuse_ratio_mean": statistics.mean(st["reuse_ratio"] for st in stats),
         "evicted_entries_rank0": removed_n, "gpu_launches": launches, "exchange": exchange,
         "scaling": "strong (heads sharded over GPUs; outputs gathered to every rank)",
         "config": {"workload": "cfg4: per step and layer drift -> reuse decision (drift < 0.05) -> re-pack -> reuse "
@@ -1552,7 +1562,7 @@ def run_b200(args):
         "dtype_note": "attention in fp16 tensor-core operands with fp32 accumulation and softmax; the data plane "
                       "quantises fp32 K/V to fp16/int8/int4 bit-exactly",
     }
-    for key in ("cpu_baseline", "fast_k", "vs_sdpa"):
+    for key in ("cpu_baseline", "attention_variants", "vs_sdpa"):
         if key in head:
             line[key] = head[key]
     line.update(extras)

@@ -232,6 +232,16 @@ int skv_ipc_close(void* base);
  *                       scores with fp16's 2^-11 relative error, which outlier channels of K turn
  *                       into ~2e-3 relative L2 on the long-context workload. */
 #define SKV_ATTN_FAST_K 1
+/*   SKV_ATTN_ONE_TILE -- the single-query-tile pipeline (units of 128 queries, two score buffers,
+ *                       the next step's scores computed during this step's softmax) instead of the
+ *                       default two-tile one (units of 256 queries, one score buffer per tile):
+ *                       slower on long sequences (twice the K/V tile traffic), slightly faster on
+ *                       short query blocks. */
+#define SKV_ATTN_ONE_TILE 2
+/*   SKV_ATTN_FMA_EXP  -- two-tile pipeline: one column pair in four computes its softmax
+ *                       exponentials with a polynomial on the FMA pipe (relative error <= 7.5e-5)
+ *                       instead of the MUFU. */
+#define SKV_ATTN_FMA_EXP 4
 int skv_packed_attention_gqa(const void* q, int B, int H_q, int S_q, int D, const skv_bucket* buckets, int H_kv,
                              int S_kv, int int4_group, const int32_t* rows, const int32_t* counts,
                              const float* k_new, const float* v_new, int S_new, float scale, void* scratch,

@@ -28,6 +28,8 @@ SKV_ERR_CUDA = 6
 SKV_ERR_UNSUPPORTED = 7
 
 SKV_ATTN_FAST_K = 1   # attention flag: K in fp16 only (include/shadowkv_b200.h)
+SKV_ATTN_ONE_TILE = 2  # attention flag: the single-query-tile pipeline
+SKV_ATTN_FMA_EXP = 4   # attention flag: a quarter of the softmax exponentials on the FMA pipe
 
 c_void_p = ctypes.c_void_p
 c_int = ctypes.c_int

@@ -11,28 +11,34 @@
 //   1. stage_tiles_kernel (skv_stage_kv_tiles), one CTA per (128-row KV tile, head, batch):
 //      gathers the tile's rows from the fp32/fp16/int8/int4 buckets and dequantises them ONCE
 //      into fp16 K and V tiles in exactly the byte layout the tensor cores read (128B-swizzled
-//      atoms of 128 rows x 64 values).  K is staged as a pair of fp16 tiles, hi = RNE(k) and
-//      lo = RNE(k - hi), whose sum carries ~22 significant bits of the fp32 value the
-//      reference dequantises (q * scale for int8 / int4, computed in fp32 as the reference
-//      does); V as one fp16 tile (RNE).  A tile whose rows are all fp16 entries is exact in
-//      fp16 and gets no lo tile.  Evicted entries are not staged.  Every query tile of the head reuses the staged tiles (from L2), so the
-//      packed bytes are read and converted once per head instead of once per query tile.
+//      atoms of 128 rows x 64 values), K and V with RNE (fp32 -> fp16) of the value the reference
+//      dequantises (q * scale for int8 / int4, computed in fp32 as the reference does).  Beside
+//      them, per KV head, the lo part RNE(k - RNE(k)) of the 16 channels of largest max |K|
+//      (channel-selective lo, see kLoCh), unless the tile is all fp16 entries and so exact.
+//      Evicted entries are not staged.  Every query tile of the head reuses the staged tiles
+//      (from L2), so the packed bytes are read and converted once per head instead of once per
+//      query tile.
 //   2. packed_attention_kernel (skv_attend_kv_tiles): persistent, one CTA per SM, launched
-//      cooperatively.  A work unit is 256 queries (two 128-row tiles) of one head; the units'
-//      KV steps are split evenly over the CTAs (a unit cut between two CTAs is merged through
-//      a partial (O, max, sum) in scratch).  Per CTA:
+//      cooperatively.  A work unit is 256 queries (two 128-row tiles) of one head.  Whole units
+//      go round-robin over the CTAs (the units in flight share one or two heads' tiles in L2);
+//      the last one to two rounds are split evenly by KV steps (a unit cut between two CTAs is
+//      merged through a partial (O, max, sum) in scratch).  Per CTA:
 //      warps 0-7  softmax, two groups of four: group t owns query tile t, thread i of the group
 //                 owns query row i = TMEM lane i.  Reads S_t from TMEM, keeps the running max
 //                 and sum (lazy rescale of O_t when the max grows by more than 2^8), and writes
 //                 P_t (fp16) back into TMEM over the first half of S_t's columns; at the end of
 //                 a unit, normalises O_t and stores it.
-//      warp 8     loader: Q tiles by TMA (128B swizzle, no multicast), the staged K hi/lo pair
-//                 by one bulk asynchronous copy into a single stage, the V tiles into a
-//                 two-stage ring.
+//      warp 8     loader: Q tiles by TMA (128B swizzle, no multicast), the staged K (+ lo) and
+//                 V tiles by bulk asynchronous copies into two-stage rings, and the queries'
+//                 selected channels Q_c gathered from the Q tiles.
 //      warp 9     MMA issuer (tcgen05.mma kind::f16, M=128, fp32 accumulate):
-//                 S_t = Q_t K_j,hi^T + Q_t K_j,lo^T (both operands in shared memory; the lo
-//                 chain is skipped for exact tiles) and O_t += P_t V_j (P read from TMEM), interleaved PV_0(j), S_0(j+1), PV_1(j), S_1(j+1) so that the
-//                 tensor cores work on one query tile while the other tile's softmax runs.
+//                 S_t = Q_t K_j^T (+ Q_c,t K_lo,j^T over the selected channels; both operands in
+//                 shared memory) and O_t += P_t V_j (P read from TMEM), interleaved PV_0(j),
+//                 S_0(j+1), PV_1(j), S_1(j+1) so that the tensor cores work on one query tile
+//                 while the other tile's softmax runs.  One thread issues every MMA: the issue
+//                 of a tcgen05.mma costs about as long as its execution at N = 128, so two issuers
+//                 (one per group) interleave their tiles' MMAs in the pipe, and a hand-over
+//                 between them leaves the pipe idle for the hand-over's latency (measured).
 //      TMEM: S_0 | S_1 | O_0 | O_1 (128 + 128 + D + D columns).
 // Evicted entries never enter a tile: their contribution (count * 2^(0 - m)) is added to the
 // softmax denominator analytically.  Every mbarrier wait is bounded; a timeout sets the error
@@ -62,7 +68,7 @@ constexpr float kRescaleThreshold = 8.0f;   // log2 units
 
 enum AttnError { kErrNone = 0, kErrKFull = 1, kErrKEmpty = 2, kErrSFull = 3, kErrPFull = 4, kErrOFull = 5,
                  kErrDrain = 6, kErrQFull = 7, kErrVFull = 8, kErrVEmpty = 9, kErrCopy = 10, kErrQEmpty = 11,
-                 kErrOEmpty = 12, kErrPartial = 13, kErrSchedule = 14 };
+                 kErrOEmpty = 12, kErrPartial = 13, kErrSchedule = 14, kErrTurn = 15 };
 
 // Bytes of one staged K (or V) tile: D/64 swizzle atoms of 128 rows x 128 bytes.
 __host__ __device__ constexpr int staged_tile_bytes(int D) { return (D / 64) * kBN * 128; }
@@ -72,6 +78,8 @@ constexpr int kLoTile = kBN * kLoCh * 2;        // their lo tile: 128 rows x 32 
 
 constexpr int kMaxHeads = 256;     // heads per launch (the schedule keeps a per-head prefix in smem)
 constexpr int kMaxPartners = 8;    // CTAs that can hold later parts of one unit (merged by its first part)
+// bytes of the schedule's shared state (SchedSmem: 48 bytes of fields, the two prefixes)
+constexpr int kSchedSmemBytes = (48 + (kMaxHeads + 1) * 4 + (kMaxHeads + 1) * 2 + 15) / 16 * 16;
 constexpr int kUnitRows = 2 * kBM;  // queries per work unit
 
 template <int D, bool PEERS = false>
@@ -85,9 +93,9 @@ struct AttnLayout {
     static constexpr int kKc = kQc + 2 * kLoTile;       // two stages of K lo of the selected channels
     static constexpr int kBar = kKc + 2 * kLoTile;
     static constexpr int kNumBars = 24;
-    static constexpr int kHP = kBar + kNumBars * 8;     // int32 [kMaxHeads + 1]: prefix of KV tiles per head
+    static constexpr int kSch = kBar + kNumBars * 8;    // SchedSmem (defined below)
     // PEERS: per softmax warp, kOutRows output rows staged for the bulk stores into every rank's buffer
-    static constexpr int kOut = (kHP + (kMaxHeads + 1) * 4 + 127) / 128 * 128;
+    static constexpr int kOut = (kSch + kSchedSmemBytes + 127) / 128 * 128;
     static constexpr int kOutRows = 4;
     static constexpr int kMisc = kOut + (PEERS ? kSoftmaxWarps * kOutRows * D * 4 : 0);
     static constexpr int kTmemSlot = kMisc + 16;
@@ -119,6 +127,8 @@ struct AttnParams {
     float scale_log2;          // softmax scale * log2(e)
     int* err;
     int klo;                   // 1: the head's kLoCh largest channels of K also contribute their lo part
+    int one_tile;              // 1: the single-query-tile kernel (units of 128 queries); 0: two tiles (256)
+    int emu;                   // two-tile kernel: a quarter of the exponentials on the FMA pipe
     unsigned* chmax;           // [H_kv, D] max |K| per channel (float bits), channel selection input
     int* sel;                  // [H_kv, kLoCh] the selected channels, ascending
 };
@@ -256,7 +266,7 @@ struct RawRow {
     int code;                   // 0 fp32 row, 1..3 packed fp16 / int8 / int4, -1 padding row
 };
 
-template <int D>
+template <int D, bool WANT_V = true>
 __device__ __forceinline__ void load_raw_row(const AttnParams& p, int b, int32_t e, int l8, RawRow<D / 64>& r) {
     constexpr int NA = D / 64;
     r.code = e < 0 ? -1 : slot_code(e);
@@ -269,41 +279,49 @@ __device__ __forceinline__ void load_raw_row(const AttnParams& p, int b, int32_t
         const int d0 = a * 64 + l8 * 8;
         if (r.code == 0) {
             // rare: V converted at once (RNE), K read again when stored
-            float x[8];
-            f32x8_load(reinterpret_cast<const float*>(bb.v) + row * D + d0, x);
-            r.v[a] = f32x8_to_half(x);
+            if (WANT_V) {
+                float x[8];
+                f32x8_load(reinterpret_cast<const float*>(bb.v) + row * D + d0, x);
+                r.v[a] = f32x8_to_half(x);
+            }
         } else if (r.code == 1) {
             r.k[a] = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const __half*>(bb.k) + row * D + d0));
-            r.v[a] = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const __half*>(bb.v) + row * D + d0));
+            if (WANT_V)
+                r.v[a] = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const __half*>(bb.v) + row * D + d0));
         } else if (r.code == 2) {
             const uint2 wk = __ldg(reinterpret_cast<const uint2*>(reinterpret_cast<const int8_t*>(bb.k) + row * D + d0));
-            const uint2 wv = __ldg(reinterpret_cast<const uint2*>(reinterpret_cast<const int8_t*>(bb.v) + row * D + d0));
             r.k[a] = make_uint4(wk.x, wk.y, 0, 0);
-            r.v[a] = make_uint4(wv.x, wv.y, 0, 0);
+            if (WANT_V) {
+                const uint2 wv = __ldg(reinterpret_cast<const uint2*>(reinterpret_cast<const int8_t*>(bb.v) + row * D + d0));
+                r.v[a] = make_uint4(wv.x, wv.y, 0, 0);
+            }
             if (a == 0) {
                 r.sk[0] = __ldg(bb.scale_k + row);
-                r.sv[0] = __ldg(bb.scale_v + row);
+                if (WANT_V) r.sv[0] = __ldg(bb.scale_v + row);
             }
         } else {
             const int64_t off = (int64_t)slot_pos(e) * ((int64_t)p.B * D / 2) + (int64_t)b * (D / 2) + d0 / 2;
             r.k[a].x = __ldg(reinterpret_cast<const uint32_t*>(reinterpret_cast<const uint8_t*>(bb.k) + off));
-            r.v[a].x = __ldg(reinterpret_cast<const uint32_t*>(reinterpret_cast<const uint8_t*>(bb.v) + off));
             const int NG = D / p.G;
             const int g = d0 / p.G;
             r.sk[a] = __ldg(bb.scale_k + row * NG + g);
-            r.sv[a] = __ldg(bb.scale_v + row * NG + g);
+            if (WANT_V) {
+                r.v[a].x = __ldg(reinterpret_cast<const uint32_t*>(reinterpret_cast<const uint8_t*>(bb.v) + off));
+                r.sv[a] = __ldg(bb.scale_v + row * NG + g);
+            }
         }
     }
 }
 
 // One lane's share of dense fp32 row r of (b, KV head h) of k_new / v_new: V converted to fp16,
 // K kept as a pointer (split when stored).
-template <int D>
+template <int D, bool WANT_V = true>
 __device__ __forceinline__ void load_dense_row(const AttnParams& p, int b, int h, int r, int l8, RawRow<D / 64>& raw) {
     constexpr int NA = D / 64;
     raw.code = 0;
     const int64_t row = (((int64_t)b * p.H_kv + h) * p.S_new + r) * D;
     raw.kf = p.k_new + row;
+    if (!WANT_V) return;
 #pragma unroll
     for (int a = 0; a < NA; ++a) {
         float x[8];
@@ -468,18 +486,28 @@ __global__ void __launch_bounds__(kStageThreads, 2) chan_max_kernel(AttnParams p
     for (int a = 0; a < NA; ++a)
 #pragma unroll
         for (int i = 0; i < 8; ++i) m[a][i] = 0.0f;
+    // all rows' K bytes in flight before any is reduced (V is not read)
+    int32_t e[kPasses];
 #pragma unroll
     for (int i = 0; i < kPasses; ++i) {
         const int idx = j * kBN + i * kRowsPerPass + rsub;
-        RawRow<NA> raw;
+        e[i] = idx < n_stored ? __ldg(hrows + idx) : -1;
+    }
+    RawRow<NA> raw[kPasses];
+#pragma unroll
+    for (int i = 0; i < kPasses; ++i) {
+        const int idx = j * kBN + i * kRowsPerPass + rsub;
         if (idx >= n_stored && idx < hr.n_rows)
-            load_dense_row<D>(p, b, h, idx - n_stored, l8, raw);
+            load_dense_row<D, false>(p, b, h, idx - n_stored, l8, raw[i]);
         else
-            load_raw_row<D>(p, b, idx < n_stored ? __ldg(hrows + idx) : -1, l8, raw);
+            load_raw_row<D, false>(p, b, e[i], l8, raw[i]);
+    }
+#pragma unroll
+    for (int i = 0; i < kPasses; ++i) {
 #pragma unroll
         for (int a = 0; a < NA; ++a) {
             float x[8];
-            raw_k_f32<D>(raw, a, l8, x);
+            raw_k_f32<D>(raw[i], a, l8, x);
 #pragma unroll
             for (int t = 0; t < 8; ++t) m[a][t] = fmaxf(m[a][t], fabsf(x[t]));
         }
@@ -530,25 +558,124 @@ struct Segment {
     int b, h, qp, j0, j1, nt;
 };
 
-struct Schedule {
-    const int* hp;             // [H + 1] prefix of KV tiles per head
-    int H, QP;
-    long long per_batch;       // QP * hp[H]
-    long long pos, end;
+// The schedule's shared state, written by one thread before the CTA's first barrier: per-head
+// prefixes hp[h] = KV tiles of heads before h and hn[h] = heads before h that have any tile, and
+// the split of the work over the grid (below).  Each thread keeps only its cursor in registers.
+struct SchedSmem {
+    long long per_batch;       // steps of one batch entry: QP * hp[H]
+    long long P0, T_sk;        // first step and step count of the stream-K tail
+    int H, QP, G, G_sk;        // heads, query blocks per head, CTAs, CTAs sharing the tail (0: none)
+    int unit_end;              // data-parallel units: [0, unit_end)
+    int ntm;                   // largest tile count of a head
+    int hp[kMaxHeads + 1];
+    uint16_t hn[kMaxHeads + 1];
+};
 
-    __device__ bool next(Segment& s) {
-        if (pos >= end) return false;
-        const long long bb = pos / per_batch;
-        const long long r = pos - bb * per_batch;
-        // largest h with QP * hp[h] <= r; heads without tiles are skipped by construction
-        int lo = 0, hi = H - 1;
+// Work of one CTA.  Units (batch, head, query block) are ordered batch-major, then head, then
+// query block; a unit is nt steps (one per KV tile of its head).
+//  * Data-parallel rounds: CTA c takes whole units c, c + G, c + 2G, ... for the first
+//    `rounds` x G units, so the G units in flight at any time are consecutive -- they share one
+//    or two heads' staged K/V, which stays in L2 instead of every CTA streaming its own head.
+//  * Stream-K tail (the last one to two rounds of units): their steps are split contiguously,
+//    CTA c taking steps [bound(c), bound(c + 1)); a unit cut at a CTA boundary has its first part
+//    in the lower CTA, which merges the later parts published by the CTAs above it.  G_sk keeps at
+//    least ceil(max_nt / kMaxPartners) steps per CTA, so a unit spans at most kMaxPartners + 1.
+static_assert(sizeof(SchedSmem) <= kSchedSmemBytes, "schedule state beyond its shared-memory slot");
+
+struct Schedule {
+    const SchedSmem* c;
+    int unit;                  // next data-parallel unit of this CTA (steps of G)
+    long long pos, end;        // this CTA's tail steps
+
+    __device__ long long bound(long long cta) const { return c->P0 + cta * c->T_sk / c->G_sk; }
+
+    // (b, h, qp, nt) of unit u and its first step
+    __device__ static long long unit_start(const SchedSmem* c, long long u, int& b, int& h, int& qp, int& nt) {
+        const long long upb = (long long)c->QP * c->hn[c->H];
+        const long long bb = u / upb;
+        const long long r = u - bb * upb;
+        const int k = (int)(r / c->QP);
+        // largest h with hn[h] <= k: the k-th head that has tiles
+        int lo = 0, hi = c->H - 1;
         while (lo < hi) {
             const int mid = (lo + hi + 1) >> 1;
-            if ((long long)QP * hp[mid] <= r) lo = mid;
+            if (c->hn[mid] <= k) lo = mid;
             else hi = mid - 1;
         }
-        const int nt = (int)(hp[lo + 1] - hp[lo]);
-        const long long r2 = r - (long long)QP * hp[lo];
+        b = (int)bb;
+        h = lo;
+        qp = (int)(r - (long long)k * c->QP);
+        nt = c->hp[lo + 1] - c->hp[lo];
+        return bb * c->per_batch + (long long)c->QP * c->hp[lo] + (long long)qp * nt;
+    }
+
+    // one thread: head prefixes and the split (before the CTA's first barrier)
+    __device__ static void setup(SchedSmem* c, const AttnParams& p) {
+        int acc = 0, heads = 0, ntm = 0;    // acc below 2^31: H * ntmax is checked on the host
+        for (int hh = 0; hh < p.H; ++hh) {
+            const int* cn = p.counts + (int64_t)(hh / p.rep) * 5;
+            const int n = (cn[0] + cn[1] + cn[2] + cn[3] + p.S_new + kBN - 1) / kBN;
+            c->hp[hh] = acc;
+            c->hn[hh] = (uint16_t)heads;
+            acc += n;
+            heads += n > 0;
+            ntm = max(ntm, n);
+        }
+        c->hp[p.H] = acc;
+        c->hn[p.H] = (uint16_t)heads;
+        c->ntm = ntm;
+        c->H = p.H;
+        c->QP = p.QP;
+        c->G = (int)gridDim.x;
+        c->per_batch = (long long)p.QP * acc;
+        const long long T = c->per_batch * p.B;
+        const long long U = (long long)p.B * p.QP * heads;     // below 2^31: B * H * S_q is checked
+        const long long rounds = U / c->G >= 2 ? U / c->G - 1 : 0;
+        c->unit_end = (int)(rounds * c->G);
+        c->P0 = T;
+        if (c->unit_end < U) {
+            int b, h, qp, nt;
+            c->P0 = unit_start(c, c->unit_end, b, h, qp, nt);
+        }
+        c->T_sk = T - c->P0;
+        c->G_sk = 0;
+        if (c->T_sk > 0) {
+            const long long cap = max(1ll, c->T_sk / ((ntm + kMaxPartners - 1) / kMaxPartners));
+            c->G_sk = (int)min((long long)c->G, cap);
+        }
+    }
+
+    __device__ void init(const SchedSmem* c_) {
+        c = c_;
+        unit = blockIdx.x;
+        pos = end = 0;
+        if ((int)blockIdx.x < c->G_sk) {
+            pos = bound(blockIdx.x);
+            end = bound((long long)blockIdx.x + 1);
+        }
+    }
+
+    // out of line (once per segment): its registers stay out of the roles' loops
+    __device__ __noinline__ bool next(Segment& s) {
+        if (unit < c->unit_end) {
+            unit_start(c, unit, s.b, s.h, s.qp, s.nt);
+            s.j0 = 0;
+            s.j1 = s.nt;
+            unit += c->G;
+            return true;
+        }
+        if (pos >= end) return false;
+        const long long bb = pos / c->per_batch;
+        const long long r = pos - bb * c->per_batch;
+        // largest h with QP * hp[h] <= r; heads without tiles are skipped by construction
+        int lo = 0, hi = c->H - 1;
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if ((long long)c->QP * c->hp[mid] <= r) lo = mid;
+            else hi = mid - 1;
+        }
+        const int nt = c->hp[lo + 1] - c->hp[lo];
+        const long long r2 = r - (long long)c->QP * c->hp[lo];
         s.b = (int)bb;
         s.h = lo;
         s.nt = nt;
@@ -558,6 +685,15 @@ struct Schedule {
         s.j1 = s.j0 + (int)(e - pos);
         pos = e;
         return true;
+    }
+
+    // CTAs above this one holding later parts of a unit whose first part ends this CTA's tail
+    __device__ __noinline__ int partners(const Segment& s) const {
+        const long long ue = bound((long long)blockIdx.x + 1) + (s.nt - s.j1);   // unit end
+        int np = 0;
+        while (np < kMaxPartners && (int)blockIdx.x + 1 + np < c->G_sk && bound((long long)blockIdx.x + 1 + np) < ue)
+            ++np;
+        return np;
     }
 };
 
@@ -634,7 +770,7 @@ __device__ __noinline__ void stage_flush(const AttnParams& p, const float* slot,
 // Epilogue of a unit's first part when its later parts sit in np >= 2 other CTAs: rows rA and
 // rB of this lane's 16x256b share, O = O_this * fa + sum_i O_i * 2^(m_i - m) / l_total, one
 // partner at a time.  Kept out of line: the path is rare and its registers stay out of the
-// softmax loop.
+// softmax loop.  `o_empty` (may be null) gets the warp's arrival once O has been read out.
 template <int D, bool PEERS>
 __device__ __noinline__ void merge_parts(const AttnParams& p, uint32_t tO, int hf, int rA, int rB, float faA,
                                          float faB, float mA, float mB, float iA, float iB, int np, int slot, int rt,
@@ -652,7 +788,7 @@ __device__ __noinline__ void merge_parts(const AttnParams& p, uint32_t tO, int h
                 uint32_t o[16];
                 tmem_ld16x256b_x4(tO + c * 32 + ((uint32_t)(hf * 16) << 16), o);
                 tmem_wait_ld();
-                if (hf == 1 && pass == 3 && c == D / 32 - 1) {
+                if (o_empty != nullptr && hf == 1 && pass == 3 && c == D / 32 - 1) {
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(o_empty);
@@ -686,7 +822,7 @@ __device__ __noinline__ void merge_parts(const AttnParams& p, uint32_t tO, int h
         uint32_t o[16];
         tmem_ld16x256b_x4(tO + c * 32 + ((uint32_t)(hf * 16) << 16), o);
         tmem_wait_ld();
-        if (hf == 1 && c == D / 32 - 1) {
+        if (o_empty != nullptr && hf == 1 && c == D / 32 - 1) {
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(o_empty);
@@ -720,12 +856,32 @@ __device__ __noinline__ void merge_parts(const AttnParams& p, uint32_t tO, int h
     }
 }
 
+// 2^x for a pair x <= 0 on the FMA pipe: x = n + f with n = rint(x) (the 1.5 * 2^23 rounding
+// trick, exact for |x| < 2^22) and f in [-0.5, 0.5]; 2^f from a degree-3 polynomial whose
+// coefficients were fitted here by a Remez exchange for minimax relative error on [-0.5, 0.5]
+// (max 7.5e-5, below the fp16 rounding P gets next); n is added to the exponent field.  x is
+// clamped at -126 so that the exponent stays in range (2^-126 is below every P that matters).
+__device__ __forceinline__ float2 ex2_poly2(float2 x) {
+    constexpr float kRound = 12582912.0f;   // 1.5 * 2^23
+    x = make_float2(fmaxf(x.x, -126.0f), fmaxf(x.y, -126.0f));
+    const float2 t = __fadd2_rn(x, make_float2(kRound, kRound));
+    const float2 r = __fadd2_rn(t, make_float2(-kRound, -kRound));
+    const float2 f = __ffma2_rn(r, make_float2(-1.0f, -1.0f), x);
+    float2 q = __ffma2_rn(f, make_float2(0.0551716685f, 0.0551716685f), make_float2(0.2426111251f, 0.2426111251f));
+    q = __ffma2_rn(q, f, make_float2(0.6932609677f, 0.6932609677f));
+    q = __ffma2_rn(q, f, make_float2(0.9999280572f, 0.9999280572f));
+    return make_float2(__int_as_float(__float_as_int(q.x) + (__float_as_int(t.x) << 23)),
+                       __int_as_float(__float_as_int(q.y) + (__float_as_int(t.y) << 23)));
+}
+
 // Persistent, cooperatively launched (one CTA per SM, all resident): warps 0-7 softmax,
 // warp 8 loader, warp 9 MMA issuer, as described at the top of this file, looping over the
 // CTA's segments.  Barrier phases run on across segments (per step for the KV ring, S and P;
 // per segment for Q and O), so the next unit's Q load and first S MMAs overlap the previous
 // unit's epilogue.
-template <int D, bool PEERS>
+// EMU: one column pair in four of every score row takes its exponentials from ex2_poly2 on the
+// FMA pipe instead of the MUFU.
+template <int D, bool PEERS, bool EMU>
 __global__ void __launch_bounds__(kAttnThreads, 1)
     packed_attention_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ AttnParams p) {
     using L = AttnLayout<D, PEERS>;
@@ -748,7 +904,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     uint64_t* o_empty = bars + 16;      // [2] per query tile, 4 softmax warps (O read out)
     uint64_t* drain = bars + 18;        // commit, drain before TMEM release
     uint64_t* qc_full = bars + 19;      // loader warp: the segment's Q_c tiles are in shared memory
-    int* hp = reinterpret_cast<int*>(smem + L::kHP);
+    SchedSmem* ss = reinterpret_cast<SchedSmem*>(smem + L::kSch);
+    const int* hp = ss->hp;
     int* misc = reinterpret_cast<int*>(smem + L::kMisc);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kTmemSlot);
 
@@ -768,17 +925,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         mbar_init(drain, 1);
         mbar_init(qc_full, 1);
         fence_mbarrier_init();
-        int acc = 0;            // below 2^31: H * ntmax is checked on the host
-        int ntm = 0;
-        for (int hh = 0; hh < p.H; ++hh) {
-            const int* c = p.counts + (int64_t)(hh / p.rep) * 5;
-            const int n = (c[0] + c[1] + c[2] + c[3] + p.S_new + kBN - 1) / kBN;
-            hp[hh] = acc;
-            acc += n;
-            ntm = max(ntm, n);
-        }
-        hp[p.H] = acc;
-        misc[0] = ntm;
+        Schedule::setup(ss, p);
     }
     if (warp == kMmaWarp) {
         tmem_alloc(tmem_slot, kTmemCols);
@@ -790,26 +937,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     const uint32_t tmem = *tmem_slot;
 
     Schedule sched;
-    sched.hp = hp;
-    sched.H = p.H;
-    sched.QP = p.QP;
-    sched.per_batch = (long long)p.QP * hp[p.H];
-    sched.pos = sched.end = 0;
-    // CTA c takes steps [c*T/G, (c+1)*T/G).  G keeps at least ceil(max_nt / kMaxPartners) steps
-    // per CTA, so a unit spans at most kMaxPartners + 1 CTAs
-    const long long T = sched.per_batch * p.B;
-    int G = 0;
-    {
-        const int ntm = misc[0];
-        if (T > 0) {
-            const long long cap = T / ((ntm + kMaxPartners - 1) / kMaxPartners);
-            G = (int)min((long long)gridDim.x, cap);
-            if ((int)blockIdx.x < G) {
-                sched.pos = (long long)blockIdx.x * T / G;
-                sched.end = ((long long)blockIdx.x + 1) * T / G;
-            }
-        }
-    }
+    sched.init(ss);
 
     if (warp < kSoftmaxWarps) {
         // ------------------------------------------------------------------ softmax
@@ -874,7 +1002,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                         const int col = c * 32 + i;
                         const float2 x = __ffma2_rn(
                             make_float2(__uint_as_float(sc[col]), __uint_as_float(sc[col + 1])), sl2x2, negm2);
-                        const float2 e = make_float2(ex2(x.x), ex2(x.y));
+                        const float2 e = (EMU && ((i >> 1) & 3) == 3) ? ex2_poly2(x) : make_float2(ex2(x.x), ex2(x.y));
                         if ((col >> 1) & 1)
                             acc1 = __fadd2_rn(acc1, e);
                         else
@@ -909,11 +1037,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             const bool split_tail = sg.j0 > 0;                   // a later part: publish, unnormalised
             const bool split_head = first_part && sg.j1 < sg.nt; // first part: merge the later parts
             // later parts live in CTAs blockIdx.x + 1 .. + np (each publishes into its own slot)
-            int np = 0;
-            if (split_head) {
-                const long long ue = ((long long)blockIdx.x + 1) * T / G + (sg.nt - sg.j1);   // unit end
-                while (np < kMaxPartners && ((long long)blockIdx.x + 1 + np) * T / G < ue) ++np;
-            }
+            const int np = split_head ? sched.partners(sg) : 0;
             const int slot = blockIdx.x + 1;
             float mB = -INFINITY, lB = 0.0f;
             for (int i = 0; i < np; ++i) {
@@ -1351,6 +1475,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     }
 }
 
+
+
+#include "attention_1t.cuh"
+
 // ---------------------------------------------------------------------------------------
 // per-head row index
 // ---------------------------------------------------------------------------------------
@@ -1478,7 +1606,8 @@ int attn_params(const void* q, int B, int H, int S_q, int D, const skv_bucket* b
                 AttnParams& prm, const char* what, int max_ctas = 0, float* const* peers = nullptr,
                 int n_peers = 0, int head_off = 0, int H_out = 0, int flags = 0) {
     if (!rows || !counts || !scratch) return fail(SKV_ERR_INVALID_ARGUMENT, "%s: null pointer", what);
-    if (flags & ~SKV_ATTN_FAST_K) return fail(SKV_ERR_INVALID_ARGUMENT, "%s: unknown flags 0x%x", what, flags);
+    if (flags & ~(SKV_ATTN_FAST_K | SKV_ATTN_ONE_TILE | SKV_ATTN_FMA_EXP))
+        return fail(SKV_ERR_INVALID_ARGUMENT, "%s: unknown flags 0x%x", what, flags);
     if (B <= 0 || H <= 0 || S_q <= 0 || S_kv <= 0 || H_kv <= 0 || S_new < 0)
         return fail(SKV_ERR_INVALID_ARGUMENT, "%s: bad shape", what);
     if (H % H_kv) return fail(SKV_ERR_SHAPE, "%s: %d query heads do not group over %d KV heads", what, H, H_kv);
@@ -1537,7 +1666,9 @@ int attn_params(const void* q, int B, int H, int S_q, int D, const skv_bucket* b
     prm.S_q = S_q;
     prm.S_kv = S_kv;
     prm.G = G;
-    prm.QP = (S_q + kUnitRows - 1) / kUnitRows;
+    prm.one_tile = (flags & SKV_ATTN_ONE_TILE) ? 1 : 0;
+    prm.emu = (flags & SKV_ATTN_FMA_EXP) ? 1 : 0;
+    prm.QP = prm.one_tile ? (S_q + k1TUnitRows - 1) / k1TUnitRows : (S_q + kUnitRows - 1) / kUnitRows;
     prm.scale_log2 = scale * 1.4426950408889634f;
     prm.err = error_flag;
     prm.klo = (flags & SKV_ATTN_FAST_K) ? 0 : 1;
@@ -1624,13 +1755,27 @@ int launch_attention(const AttnParams& prm, cudaStream_t s) {
     if (r != CUDA_SUCCESS) return fail(SKV_ERR_CUDA, "attend_kv_tiles: tensor map encoding failed (%d)", (int)r);
     if (cudaMemsetAsync(prm.part_flag, 0, (size_t)prm.slots * sizeof(int), s) != cudaSuccess)
         return fail(SKV_ERR_CUDA, "attend_kv_tiles: memset failed");
-    const int smem = prm.n_peers > 0 ? AttnLayout<D, true>::kAlloc : AttnLayout<D, false>::kAlloc;
-    void* kern = prm.n_peers > 0 ? reinterpret_cast<void*>(packed_attention_kernel<D, true>)
-                                 : reinterpret_cast<void*>(packed_attention_kernel<D, false>);
+    int smem, threads;
+    void* kern;
+    if (!prm.one_tile) {
+        smem = prm.n_peers > 0 ? AttnLayout<D, true>::kAlloc : AttnLayout<D, false>::kAlloc;
+        if (prm.emu)
+            kern = prm.n_peers > 0 ? reinterpret_cast<void*>(packed_attention_kernel<D, true, true>)
+                                   : reinterpret_cast<void*>(packed_attention_kernel<D, false, true>);
+        else
+            kern = prm.n_peers > 0 ? reinterpret_cast<void*>(packed_attention_kernel<D, true, false>)
+                                   : reinterpret_cast<void*>(packed_attention_kernel<D, false, false>);
+        threads = kAttnThreads;
+    } else {
+        smem = prm.n_peers > 0 ? Attn1TLayout<D, true>::kAlloc : Attn1TLayout<D, false>::kAlloc;
+        kern = prm.n_peers > 0 ? reinterpret_cast<void*>(packed_attention_1t_kernel<D, true>)
+                               : reinterpret_cast<void*>(packed_attention_1t_kernel<D, false>);
+        threads = k1TThreads;
+    }
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     AttnParams a = prm;
     void* args[] = {&qmap, &a};
-    const cudaError_t e = cudaLaunchCooperativeKernel(kern, dim3((unsigned)prm.slots), dim3(kAttnThreads), args,
+    const cudaError_t e = cudaLaunchCooperativeKernel(kern, dim3((unsigned)prm.slots), dim3(threads), args,
                                                       (size_t)smem, s);
     if (e != cudaSuccess)
         return fail(SKV_ERR_CUDA, "attend_kv_tiles: cooperative launch failed: %s", cudaGetErrorString(e));

@@ -116,12 +116,15 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 __device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity, int* err, int code,
                                                uint64_t limit_ns = 1000000000ull) {
     if (mbar_try_wait(bar, parity)) return true;
-    const uint64_t t0 = globaltimer_ns();
+    // each try suspends for at most 20 us; the error word and the wall clock (both slow to read)
+    // are checked after a try that timed out, the clock's start taken at the first of those
+    uint64_t t0 = 0;
     for (;;) {
-        // each try suspends for at most 20 us; the wall-clock limit is checked after each
         if (mbar_try_wait_hint(bar, parity, 20000u)) return true;
         if (*reinterpret_cast<volatile int*>(err) != 0) return false;
-        if (globaltimer_ns() - t0 > limit_ns) {
+        const uint64_t now = globaltimer_ns();
+        if (t0 == 0) t0 = now;
+        else if (now - t0 > limit_ns) {
             atomicCAS(err, 0, code);
             return false;
         }

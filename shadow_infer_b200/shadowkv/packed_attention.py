@@ -36,6 +36,8 @@ def packed_attention(
     head_offset: int = 0,
     attention_mask: Optional[torch.Tensor] = None,
     fast_k: bool = False,
+    one_tile: bool = False,
+    fma_exp: bool = False,
 ) -> torch.Tensor:
     """Non-causal attention of ``q`` [B, H_q, S_q, D] over a packed cache; returns fp32 [B, H_q, S_q, D].
 
@@ -67,6 +69,13 @@ def packed_attention(
     channels ten times larger than the rest) do not turn fp16's 2^-11 rounding into the dominant
     error: relative L2 <= 1e-3 against the reference's fp32 attention.  ``fast_k=True`` skips the
     channel selection and the lo part (K in fp16 only; ~2e-3 with outlier channels).
+
+    ``one_tile=True`` runs the single-query-tile pipeline (units of 128 queries whose next KV
+    step's scores are computed while this step's softmax runs) instead of the default two-tile
+    one (units of 256 queries, one score buffer per tile); both compute the same result.
+
+    ``fma_exp=True`` (two-tile pipeline) computes a quarter of the softmax exponentials with a
+    polynomial on the FMA pipe instead of the MUFU.
 
     ``attention_mask``: accepted for the reference's signature; like
     ``SimpleDiffusionLLM._compute_block`` (simple_diffusion_llm.py:140-142), which raises when an
@@ -113,7 +122,8 @@ def packed_attention(
     tiles = scratch(lib.skv_packed_attention_scratch_bytes(B, H_kv, c.seq_len + S_new, D), dev)
     stream = _lib.stream_of(dev)
     g = c._int4_group_of()
-    flags = _lib.SKV_ATTN_FAST_K if fast_k else 0
+    flags = ((_lib.SKV_ATTN_FAST_K if fast_k else 0) | (_lib.SKV_ATTN_ONE_TILE if one_tile else 0) |
+             (_lib.SKV_ATTN_FMA_EXP if fma_exp else 0))
     if peer_outputs is not None:
         Bp, Hp, Sp, Dp = peer_outputs.shape
         if (Bp, Sp, Dp) != (B, S_q, D) or not 0 <= head_offset <= Hp - H:

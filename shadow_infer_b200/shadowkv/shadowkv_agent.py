@@ -17,6 +17,7 @@ zeros for evicted entries, previous-step rows for reused entries).
 
 from __future__ import annotations
 
+from collections.abc import Mapping
 from typing import Any, Dict, List, Optional, Set, Tuple
 
 import torch
@@ -91,10 +92,41 @@ def decide_reuse_mask(
         st = lib.skv_reuse_decide(_lib.ptr(kc), _lib.ptr(vc), _lib.ptr(kp), _lib.ptr(vp), B, H, S, D, _lib.ptr(imp),
                                   eff, _lib.ptr(mask), _lib.ptr(drift), _lib.ptr(counts), _lib.stream_of(dev))
     _lib.check(st, "decide_reuse_per_token")
-    full, partial, none, reused = counts.tolist()
-    stats = {"full_reuse_count": float(full), "partial_reuse_count": float(partial),
-             "no_reuse_count": float(none), "reuse_ratio": float(reused / max(S * H, 1))}
+    stats = ReuseStats(counts, S * H)
     return (mask, stats, drift) if return_drift else (mask, stats)
+
+
+class ReuseStats(Mapping):
+    """The stats dict of ``decide_reuse_per_token`` (full / partial / no reuse counts, reuse ratio),
+    read from the device on first access: a caller that does not look at them does not wait for
+    the decision kernel."""
+
+    _KEYS = ("full_reuse_count", "partial_reuse_count", "no_reuse_count", "reuse_ratio")
+
+    def __init__(self, counts: torch.Tensor, entries: int):
+        self._counts, self._entries, self._d = counts, entries, None
+
+    def _get(self) -> Dict[str, float]:
+        if self._d is None:
+            full, partial, none, reused = self._counts.tolist()
+            self._d = {"full_reuse_count": float(full), "partial_reuse_count": float(partial),
+                       "no_reuse_count": float(none), "reuse_ratio": float(reused / max(self._entries, 1))}
+        return self._d
+
+    def __getitem__(self, key):
+        return self._get()[key]
+
+    def __iter__(self):
+        return iter(self._KEYS)
+
+    def __len__(self):
+        return len(self._KEYS)
+
+    def __eq__(self, other):
+        return dict(self._get()) == (dict(other) if isinstance(other, Mapping) else other)
+
+    def __repr__(self):
+        return repr(self._get())
 
 
 class ShadowKVAgent:
@@ -151,7 +183,7 @@ class ShadowKVAgent:
         S, H = mask.shape
         flags: List[bool] = mask.reshape(-1).tolist()
         keys = [(t, h) for t in range(S) for h in range(H)]
-        return dict(zip(keys, flags)), stats
+        return dict(zip(keys, flags)), dict(stats)
 
     @staticmethod
     def _row_normalize(tensor: torch.Tensor) -> torch.Tensor:

@@ -370,3 +370,34 @@ def test_attention_channel_outliers(skv, D, rep, S_new):
     fast = skv.packed_attention(torch.from_numpy(q).cuda(), cache, fast_k=True, **kw).cpu().numpy()
     assert rel_l2(out, ref) < REL_L2_TOL
     assert rel_l2(out, ref) <= rel_l2(fast, ref) + 1e-6
+
+
+@pytest.mark.parametrize("B,H,S,SQ,D,probs,qs", [CASES[0], CASES[2], CASES[6]])
+def test_attention_one_tile_pipeline(skv, B, H, S, SQ, D, probs, qs):
+    """The single-query-tile pipeline computes the same attention as the default two-tile one
+    (both within 1e-3 of the oracle; they differ only in summation order)."""
+    rng = np.random.default_rng(S * 31 + D)
+    k = rng.standard_normal((B, H, S, D)).astype(np.float32)
+    v = rng.standard_normal((B, H, S, D)).astype(np.float32)
+    codes = rng.choice(5, size=(S, H), p=probs).astype(np.int8)
+    q = (rng.standard_normal((B, H, SQ, D)) * qs).astype(np.float16)
+    cache = _pack(skv, k, v, codes)
+    ref = O.packed_attention(q.astype(np.float32), O.pack(k, v, O.plan_from_codes(codes), 16))
+    one = skv.packed_attention(torch.from_numpy(q).cuda(), cache).cpu().numpy()
+    two = skv.packed_attention(torch.from_numpy(q).cuda(), cache, one_tile=True).cpu().numpy()
+    assert rel_l2(one, ref) < REL_L2_TOL and rel_l2(two, ref) < REL_L2_TOL
+    assert rel_l2(one, two) < 1e-4
+
+
+@pytest.mark.parametrize("B,H,S,SQ,D,probs,qs", [CASES[0], CASES[2], CASES[6]])
+def test_attention_fma_exponentials(skv, B, H, S, SQ, D, probs, qs):
+    """A quarter of the softmax exponentials on the FMA pipe (degree-3 polynomial): same bar."""
+    rng = np.random.default_rng(S * 31 + D)
+    k = rng.standard_normal((B, H, S, D)).astype(np.float32)
+    v = rng.standard_normal((B, H, S, D)).astype(np.float32)
+    codes = rng.choice(5, size=(S, H), p=probs).astype(np.int8)
+    q = (rng.standard_normal((B, H, SQ, D)) * qs).astype(np.float16)
+    cache = _pack(skv, k, v, codes)
+    ref = O.packed_attention(q.astype(np.float32), O.pack(k, v, O.plan_from_codes(codes), 16))
+    out = skv.packed_attention(torch.from_numpy(q).cuda(), cache, fma_exp=True).cpu().numpy()
+    assert rel_l2(out, ref) < REL_L2_TOL
