@@ -145,6 +145,27 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
     return d;
 }
 
+// Max of N floats (bit patterns) as a tree of 3-input maxes: depth log3(N) instead of a chain,
+// the max's latency rather than its instruction count bounds the softmax's first pass.
+template <int N>
+__device__ __forceinline__ float row_max(const uint32_t* v) {
+    float a[(N + 2) / 3];
+#pragma unroll
+    for (int i = 0; i < N / 3; ++i)
+        a[i] = fmax3(__uint_as_float(v[3 * i]), __uint_as_float(v[3 * i + 1]), __uint_as_float(v[3 * i + 2]));
+    if constexpr (N % 3 == 1) a[N / 3] = __uint_as_float(v[N - 1]);
+    if constexpr (N % 3 == 2) a[N / 3] = fmaxf(__uint_as_float(v[N - 2]), __uint_as_float(v[N - 1]));
+    constexpr int M = (N + 2) / 3;
+    if constexpr (M == 1) {
+        return a[0];
+    } else {
+        uint32_t b[M];
+#pragma unroll
+        for (int i = 0; i < M; ++i) b[i] = __float_as_uint(a[i]);
+        return row_max<M>(b);
+    }
+}
+
 __device__ __forceinline__ uint32_t half2_bits(__half2 h) {
     uint32_t u;
     memcpy(&u, &h, 4);
@@ -975,15 +996,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                     for (int c = 0; c < kBN; ++c)
                         if (c >= n_valid) sc[c] = __float_as_uint(-INFINITY);
                 }
-                float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
-#pragma unroll
-                for (int i = 0; i < kBN; i += 8) {
-                    mx0 = fmax3(mx0, __uint_as_float(sc[i]), __uint_as_float(sc[i + 1]));
-                    mx1 = fmax3(mx1, __uint_as_float(sc[i + 2]), __uint_as_float(sc[i + 3]));
-                    mx2 = fmax3(mx2, __uint_as_float(sc[i + 4]), __uint_as_float(sc[i + 5]));
-                    mx3 = fmax3(mx3, __uint_as_float(sc[i + 6]), __uint_as_float(sc[i + 7]));
-                }
-                const float mt = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * sl2;
+                const float mt = row_max<kBN>(sc) * sl2;
                 const bool need = mt > m_ref + kRescaleThreshold;
                 const bool rescale = __any_sync(0xffffffffu, need);
                 // rows that keep their reference max use factor 1 (TMEM access is warp-wide)
@@ -1365,32 +1378,45 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         if (lane == 0) {
             const uint32_t idesc_s = idesc_f16_f32(kBM, kBN, false, false);
             const uint32_t idesc_o = idesc_f16_f32(kBM, D, false, true);
-            const uint32_t q_base = smem_u32(smem + L::kQ);
-            const uint32_t qc_base = smem_u32(smem + L::kQc);
+            // Shared-memory descriptors of the operands, built once: the descriptor of address
+            // a + off is the descriptor of a plus off / 16 (shared addresses stay below 2^18, so
+            // the 14-bit address field never carries), so an MMA costs one add per operand.
+            const uint64_t qd0 = smem_desc_sw128(smem_u32(smem + L::kQ), 16, 1024);
+            const uint64_t kd0 = smem_desc_sw128(smem_u32(smem + L::kK), 16, 1024);
+            const uint64_t vd0 = smem_desc_sw128(smem_u32(smem + L::kV), kBN * 128, 1024);
+            const uint64_t qcd0 = smem_desc_sw32(smem_u32(smem + L::kQc), 16, 256);
+            const uint64_t kcd0 = smem_desc_sw32(smem_u32(smem + L::kKc), 16, 256);
             // K stage of step g and the parity of its full barrier
             auto kstage = [&](long long g) { return (int)(g & 1); };
             auto kparity = [&](long long g) { return (uint32_t)((g >> 1) & 1); };
             // S_t = Q_t K^T (fp16), then += Q_c,t K_lo^T over the selected channels (one K = 16 step)
             // unless the tile is exact in fp16
             auto issue_s = [&](int t, long long g, bool lo) {
-                const uint32_t k_base = smem_u32(smem + L::kK + kstage(g) * TB);
+                const uint64_t qd = qd0 + (uint64_t)((t * TB) >> 4);
+                const uint64_t kd = kd0 + (uint64_t)((kstage(g) * TB) >> 4);
+                const uint32_t d = tmem + t * kBN;
 #pragma unroll
                 for (int k = 0; k < D / 16; ++k) {
-                    const uint32_t off = (k >> 2) * (kBN * 128) + (k & 3) * 32;
-                    umma_f16(tmem + t * kBN, smem_desc_sw128(q_base + t * TB + off, 16, 1024),
-                             smem_desc_sw128(k_base + off, 16, 1024), idesc_s, k > 0 ? 1u : 0u);
+                    const uint64_t off = (uint64_t)((((k >> 2) * (kBN * 128)) + (k & 3) * 32) >> 4);
+                    if (k == 0)
+                        umma_f16(d, qd + off, kd + off, idesc_s, 0u);
+                    else
+                        umma_f16_acc(d, qd + off, kd + off, idesc_s);
                 }
                 if (lo)
-                    umma_f16(tmem + t * kBN, smem_desc_sw32(qc_base + t * kLoTile, 16, 256),
-                             smem_desc_sw32(smem_u32(smem + L::kKc + kstage(g) * kLoTile), 16, 256), idesc_s, 1u);
+                    umma_f16_acc(d, qcd0 + (uint64_t)((t * kLoTile) >> 4), kcd0 + (uint64_t)((kstage(g) * kLoTile) >> 4),
+                                 idesc_s);
             };
             auto issue_pv = [&](int t, long long g, bool acc) {
-                const uint32_t v_base = smem_u32(smem + L::kV + (int)(g & 1) * TB);
+                const uint64_t vd = vd0 + (uint64_t)(((int)(g & 1) * TB) >> 4);
+                const uint32_t d = tmem + 2 * kBN + t * D, a = tmem + t * kBN;
 #pragma unroll
-                for (int k = 0; k < kBN / 16; ++k)
-                    umma_f16_ts(tmem + 2 * kBN + t * D, tmem + t * kBN + k * 8,
-                                smem_desc_sw128(v_base + k * 16 * 128, kBN * 128, 1024), idesc_o,
-                                (acc || k > 0) ? 1u : 0u);
+                for (int k = 0; k < kBN / 16; ++k) {
+                    if (k == 0)
+                        umma_f16_ts(d, a, vd, idesc_o, acc ? 1u : 0u);
+                    else
+                        umma_f16_ts_acc(d, a + k * 8, vd + (uint64_t)((k * 16 * 128) >> 4), idesc_o);
+                }
             };
             Segment sg;
             long long g = 0;

@@ -4,8 +4,8 @@
 //                         packed_kv_cache.py:753-854): per current entry with the reuse
 //                         flag, copy the previous step's row (payload + scales) when the
 //                         previous cache holds the entry in the same precision; count the
-//                         cross-precision ones.  One warp per 32 entries, ballot over the
-//                         flags, then the warp copies each selected row with 16-byte vectors.
+//                         cross-precision ones.  One warp per 32 entries; the selected rows'
+//                         16-byte chunks are spread over the lanes through a warp prefix sum.
 //  * skv_evict_count / skv_evict_compact -- PackedKVCache.evict (packed_kv_cache.py:666-740):
 //                         stable compaction of every bucket without the evicted (t,h): a
 //                         tile-count pass, then a scan + row-move pass into new buckets.
@@ -13,56 +13,21 @@
 
 namespace skv {
 
-// Bit position of the n-th (0-based) set bit of m; requires popc(m) > n.
-__device__ __forceinline__ int nth_set_bit(unsigned m, int n) {
-    int pos = 0;
-#pragma unroll
-    for (int w = 16; w > 0; w >>= 1) {
-        const unsigned low = m & ((1u << w) - 1u);
-        const int c = __popc(low);
-        if (n >= c) {
-            n -= c;
-            m >>= w;
-            pos += w;
-        } else {
-            m = low;
-        }
-    }
-    return pos;
-}
-
 __device__ __forceinline__ bool aligned16(const void* a, const void* b, const void* c, const void* d) {
     return ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b) | reinterpret_cast<uintptr_t>(c) |
              reinterpret_cast<uintptr_t>(d)) & 15) == 0;
 }
 
-// Copy of one small row (payload of K and V, bytes a multiple of 16 and at most kLaneRowBytes)
-// by a single lane: every 16-byte load is issued before the first store.
-constexpr int kLaneRowBytes = 64;
-
-__device__ __forceinline__ void lane_copy_row(uint8_t* __restrict__ dk, uint8_t* __restrict__ dv,
-                                              const uint8_t* __restrict__ sk, const uint8_t* __restrict__ sv,
-                                              int chunks) {
-    uint4 a[kLaneRowBytes / 16], b[kLaneRowBytes / 16];
-#pragma unroll
-    for (int i = 0; i < kLaneRowBytes / 16; ++i)
-        if (i < chunks) {
-            a[i] = __ldg(reinterpret_cast<const uint4*>(sk) + i);
-            b[i] = __ldg(reinterpret_cast<const uint4*>(sv) + i);
-        }
-#pragma unroll
-    for (int i = 0; i < kLaneRowBytes / 16; ++i)
-        if (i < chunks) {
-            reinterpret_cast<uint4*>(dk)[i] = a[i];
-            reinterpret_cast<uint4*>(dv)[i] = b[i];
-        }
-}
-
 // One warp per 32 consecutive entries; the reuse flag and both slots of an entry are loaded
-// together.  A row of at most 128 bytes (int8/int4 at small batch) is copied by its own lane,
-// scales with it; larger rows are grouped by precision and their 16-byte chunks spread over
-// the lanes, so a warp has up to 32 independent copies in flight.
-__global__ void __launch_bounds__(256, 3) reuse_kernel(const __grid_constant__ Buckets cur,
+// together.  The payload rows to copy, of every precision, are cut into 16-byte chunks numbered
+// through a warp prefix sum of the rows' chunk counts; each pass hands every lane kChunks chunks
+// of K and of V, all loaded before the first store, so one warp keeps up to 2 * 32 * kChunks
+// loads in flight whatever the precision mix.  A lane copies its own entry's scales (at most 8
+// floats per row, as float4 loads issued with the first pass).  Rows that are not whole 16-byte
+// chunks at 16-byte aligned addresses take a per-row warp copy instead.
+constexpr int kChunks = 4;
+
+__global__ void __launch_bounds__(256, 2) reuse_kernel(const __grid_constant__ Buckets cur,
                                                        const int32_t* __restrict__ cur_slot, int S,
                                                        const __grid_constant__ Buckets prev,
                                                        const int32_t* __restrict__ prev_slot,
@@ -89,109 +54,103 @@ __global__ void __launch_bounds__(256, 3) reuse_kernel(const __grid_constant__ B
             else skipped += 1;
         }
         applied += copy ? 1 : 0;
-        const int code_l = copy ? slot_code(cs) : 0;
-        // small rows: this lane copies its own entry
-        bool wide = copy;
-        if (copy) {
-            const int64_t rb = payload_row_bytes(code_l, B, D);
-            const int64_t sf = scale_row_floats(code_l, B, D, NG);
-            const skv_bucket& cb = cur.b[code_l];
-            const skv_bucket& pb = prev.b[code_l];
-            if (rb <= kLaneRowBytes && (rb & 15) == 0 && aligned16(cb.k, cb.v, pb.k, pb.v)) {
-                wide = false;
-                const int64_t cp = slot_pos(cs), pp = slot_pos(ps);
-                // scales of up to 8 floats as 16-byte vectors, loaded with the payload
-                const bool vec = sf > 0 && (sf & 3) == 0 && sf <= 8 &&
-                                 aligned16(pb.scale_k + pp * sf, pb.scale_v + pp * sf, cb.scale_k + cp * sf,
-                                           cb.scale_v + cp * sf);
-                float4 k0 = make_float4(0.f, 0.f, 0.f, 0.f), v0 = k0, k1 = k0, v1 = k0;
-                if (vec) {
-                    const float4* ssk = reinterpret_cast<const float4*>(pb.scale_k + pp * sf);
-                    const float4* ssv = reinterpret_cast<const float4*>(pb.scale_v + pp * sf);
-                    k0 = __ldg(ssk);
-                    v0 = __ldg(ssv);
-                    if (sf > 4) {
-                        k1 = __ldg(ssk + 1);
-                        v1 = __ldg(ssv + 1);
-                    }
-                }
-                lane_copy_row(reinterpret_cast<uint8_t*>(cb.k) + cp * rb, reinterpret_cast<uint8_t*>(cb.v) + cp * rb,
-                              reinterpret_cast<const uint8_t*>(pb.k) + pp * rb,
-                              reinterpret_cast<const uint8_t*>(pb.v) + pp * rb, (int)(rb / 16));
-                if (vec) {
-                    float4* dsk = reinterpret_cast<float4*>(cb.scale_k + cp * sf);
-                    float4* dsv = reinterpret_cast<float4*>(cb.scale_v + cp * sf);
-                    dsk[0] = k0;
-                    dsv[0] = v0;
-                    if (sf > 4) {
-                        dsk[1] = k1;
-                        dsv[1] = v1;
-                    }
-                } else {
-                    for (int64_t i = 0; i < sf; ++i) {
-                        cb.scale_k[cp * sf + i] = pb.scale_k[pp * sf + i];
-                        cb.scale_v[cp * sf + i] = pb.scale_v[pp * sf + i];
-                    }
-                }
+        if (!__any_sync(0xffffffffu, copy)) continue;
+        const int code = copy ? slot_code(cs) : 0;
+        const int64_t rb = copy ? payload_row_bytes(code, B, D) : 0;
+        const int64_t sf = copy ? scale_row_floats(code, B, D, NG) : 0;
+        const int64_t cp = slot_pos(cs), pp = slot_pos(ps);
+        const skv_bucket& cb = cur.b[code];
+        const skv_bucket& pb = prev.b[code];
+        // scales: this lane's own row, loaded now (in flight with the first payload pass)
+        const bool svec = copy && sf > 0 && (sf & 3) == 0 && sf <= 8 &&
+                          aligned16(pb.scale_k + pp * sf, pb.scale_v + pp * sf, cb.scale_k + cp * sf,
+                                    cb.scale_v + cp * sf);
+        float4 k0 = make_float4(0.f, 0.f, 0.f, 0.f), v0 = k0, k1 = k0, v1 = k0;
+        if (svec) {
+            const float4* ssk = reinterpret_cast<const float4*>(pb.scale_k + pp * sf);
+            const float4* ssv = reinterpret_cast<const float4*>(pb.scale_v + pp * sf);
+            k0 = __ldg(ssk);
+            v0 = __ldg(ssv);
+            if (sf > 4) {
+                k1 = __ldg(ssk + 1);
+                v1 = __ldg(ssv + 1);
             }
         }
-        if (!__any_sync(0xffffffffu, wide)) continue;
-        // larger rows: grouped by precision, chunks spread over the lanes
-        for (int code = 0; code < kNumBuckets; ++code) {
-            const unsigned m = __ballot_sync(0xffffffffu, wide && code_l == code);
-            if (!m) continue;
-            const int nrows = __popc(m);
-            const int64_t rb = payload_row_bytes(code, B, D);
-            const int64_t sf = scale_row_floats(code, B, D, NG);
-            const skv_bucket& cb = cur.b[code];
-            const skv_bucket& pb = prev.b[code];
-            if ((rb & 15) == 0 && aligned16(cb.k, cb.v, pb.k, pb.v)) {
-                const int cpr = (int)(rb / 16);
-                const int total = nrows * cpr;
-                for (int j0 = 0; j0 < total; j0 += 32) {
-                    const int j = j0 + lane;
-                    const int rr = j < total ? j / cpr : 0;
-                    const int src = nth_set_bit(m, rr);
-                    const int32_t c2 = __shfl_sync(0xffffffffu, cs, src);
-                    const int32_t p2 = __shfl_sync(0xffffffffu, ps, src);
-                    if (j < total) {
-                        const int64_t off = (int64_t)(j - rr * cpr) * 16;
-                        const int64_t d_off = (int64_t)slot_pos(c2) * rb + off;
-                        const int64_t s_off = (int64_t)slot_pos(p2) * rb + off;
-                        const uint4 a = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint8_t*>(pb.k) + s_off);
-                        const uint4 b = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint8_t*>(pb.v) + s_off);
-                        *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(cb.k) + d_off) = a;
-                        *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(cb.v) + d_off) = b;
-                    }
-                }
-            } else {
-                unsigned todo = m;
-                while (todo) {
-                    const int src = __ffs(todo) - 1;
-                    todo &= todo - 1;
-                    const int64_t cpos = slot_pos(__shfl_sync(0xffffffffu, cs, src));
-                    const int64_t ppos = slot_pos(__shfl_sync(0xffffffffu, ps, src));
-                    warp_copy(reinterpret_cast<uint8_t*>(cb.k) + cpos * rb,
-                              reinterpret_cast<const uint8_t*>(pb.k) + ppos * rb, rb, lane);
-                    warp_copy(reinterpret_cast<uint8_t*>(cb.v) + cpos * rb,
-                              reinterpret_cast<const uint8_t*>(pb.v) + ppos * rb, rb, lane);
+        // payload: whole 16-byte chunks at aligned addresses go through the chunk passes
+        const bool chunked = copy && (rb & 15) == 0 && aligned16(cb.k, cb.v, pb.k, pb.v);
+        const int nch = chunked ? (int)(rb >> 4) : 0;
+        int incl = nch;                                      // inclusive prefix over the lanes
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int x = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += x;
+        }
+        const int total = __shfl_sync(0xffffffffu, incl, 31);
+        for (int j0 = 0; j0 < total; j0 += 32 * kChunks) {
+            uint4 a[kChunks], b[kChunks];
+            uint8_t* dk[kChunks];
+            uint8_t* dv[kChunks];
+#pragma unroll
+            for (int u = 0; u < kChunks; ++u) {
+                const int j = j0 + u * 32 + lane;
+                // the row holding chunk j: the first lane whose inclusive prefix exceeds j
+                int r = 0;
+#pragma unroll
+                for (int step = 16; step > 0; step >>= 1)
+                    if (__shfl_sync(0xffffffffu, incl, r + step - 1) <= j) r += step;
+                const int r_incl = __shfl_sync(0xffffffffu, incl, r);
+                const int r_n = __shfl_sync(0xffffffffu, nch, r);
+                const int r_code = __shfl_sync(0xffffffffu, code, r);
+                const int32_t r_cp = __shfl_sync(0xffffffffu, (int32_t)cp, r);
+                const int32_t r_pp = __shfl_sync(0xffffffffu, (int32_t)pp, r);
+                dk[u] = nullptr;
+                dv[u] = nullptr;
+                if (j < total) {
+                    const int64_t rbr = (int64_t)r_n * 16;
+                    const int64_t off = (int64_t)(j - (r_incl - r_n)) * 16;
+                    const skv_bucket& cbr = cur.b[r_code];
+                    const skv_bucket& pbr = prev.b[r_code];
+                    a[u] = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const uint8_t*>(pbr.k) + r_pp * rbr + off));
+                    b[u] = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const uint8_t*>(pbr.v) + r_pp * rbr + off));
+                    dk[u] = reinterpret_cast<uint8_t*>(cbr.k) + r_cp * rbr + off;
+                    dv[u] = reinterpret_cast<uint8_t*>(cbr.v) + r_cp * rbr + off;
                 }
             }
-            if (sf) {
-                const int total = nrows * (int)sf;
-                for (int j0 = 0; j0 < total; j0 += 32) {
-                    const int j = j0 + lane;
-                    const int rr = j < total ? j / (int)sf : 0;
-                    const int src = nth_set_bit(m, rr);
-                    const int32_t c2 = __shfl_sync(0xffffffffu, cs, src);
-                    const int32_t p2 = __shfl_sync(0xffffffffu, ps, src);
-                    if (j < total) {
-                        const int64_t i = j - (int64_t)rr * sf;
-                        cb.scale_k[slot_pos(c2) * sf + i] = pb.scale_k[slot_pos(p2) * sf + i];
-                        cb.scale_v[slot_pos(c2) * sf + i] = pb.scale_v[slot_pos(p2) * sf + i];
-                    }
+#pragma unroll
+            for (int u = 0; u < kChunks; ++u)
+                if (dk[u] != nullptr) {
+                    *reinterpret_cast<uint4*>(dk[u]) = a[u];
+                    *reinterpret_cast<uint4*>(dv[u]) = b[u];
                 }
+        }
+        if (svec) {
+            float4* dsk = reinterpret_cast<float4*>(cb.scale_k + cp * sf);
+            float4* dsv = reinterpret_cast<float4*>(cb.scale_v + cp * sf);
+            dsk[0] = k0;
+            dsv[0] = v0;
+            if (sf > 4) {
+                dsk[1] = k1;
+                dsv[1] = v1;
             }
+        } else if (copy) {
+            for (int64_t i = 0; i < sf; ++i) {
+                cb.scale_k[cp * sf + i] = pb.scale_k[pp * sf + i];
+                cb.scale_v[cp * sf + i] = pb.scale_v[pp * sf + i];
+            }
+        }
+        // rows the chunk passes do not cover: one warp copy per row
+        unsigned todo = __ballot_sync(0xffffffffu, copy && !chunked);
+        while (todo) {
+            const int src = __ffs(todo) - 1;
+            todo &= todo - 1;
+            const int c2 = __shfl_sync(0xffffffffu, code, src);
+            const int64_t cpos = __shfl_sync(0xffffffffu, (int32_t)cp, src);
+            const int64_t ppos = __shfl_sync(0xffffffffu, (int32_t)pp, src);
+            const int64_t rb2 = payload_row_bytes(c2, B, D);
+            warp_copy(reinterpret_cast<uint8_t*>(cur.b[c2].k) + cpos * rb2,
+                      reinterpret_cast<const uint8_t*>(prev.b[c2].k) + ppos * rb2, rb2, lane);
+            warp_copy(reinterpret_cast<uint8_t*>(cur.b[c2].v) + cpos * rb2,
+                      reinterpret_cast<const uint8_t*>(prev.b[c2].v) + ppos * rb2, rb2, lane);
         }
     }
     if (!stats) return;                                 // statistics not requested

@@ -116,14 +116,6 @@ def _bucket_parts(code: int, n: int, B: int, D: int, G: int):
             ("scale_k", _F32, (n * B, ng, 1), n * B * ng * 4), ("scale_v", _F32, (n * B, ng, 1), n * B * ng * 4))
 
 
-def _alloc_bucket(code: int, n: int, B: int, D: int, G: int, dev: torch.device) -> Dict[str, torch.Tensor]:
-    """Bucket tensors in the reference layout (packed_kv_cache.py:265-363)."""
-    out = {"scale_k": None, "scale_v": None}
-    for key, dt, shape, _ in _bucket_parts(code, n, B, D, G):
-        out[key] = torch.empty(shape, dtype=dt, device=dev)
-    return out
-
-
 def _nbytes(t: Optional[torch.Tensor]) -> int:
     return 0 if t is None else t.numel() * t.element_size()
 
@@ -172,6 +164,41 @@ def _slab_views(slab: torch.Tensor, layout, counts: Sequence[int], plan: Precisi
             es = t.element_size()
             stride = (shape[1] * shape[2], shape[2], 1) if len(shape) == 3 else (1,)
             b[key] = t.as_strided(shape, stride, off // es)
+        b["flat"] = flat_all[start:start + n]
+        b["count"] = n
+        start += n
+        buckets.append(b)
+    return buckets
+
+
+def _slab_buckets(counts: Sequence[int], B: int, D: int, G: int, dev: torch.device,
+                  skip: Sequence[bool] = (False,) * 4) -> List[Optional[Dict[str, Any]]]:
+    """Empty buckets of ``counts`` entries (None where a count is 0 or ``skip`` is set), every
+    tensor -- payload, scales and the int64 flat indices -- a view into ONE allocation, so that
+    sizing new buckets costs one allocator call instead of five per bucket."""
+    want = [0 if skip[c] else int(counts[c]) for c in range(4)]
+    layout, total = _slab_layout(want, B, D, G)
+    flat_off = total
+    total += sum(want) * 8
+    slab = torch.empty(max(total, 1), dtype=torch.uint8, device=dev)
+    typed: Dict[torch.dtype, torch.Tensor] = {}
+    flat_all = slab[flat_off:flat_off + sum(want) * 8].view(torch.int64)
+    buckets: List[Optional[Dict[str, Any]]] = []
+    start = 0
+    for code in range(4):
+        parts = layout[code]
+        if parts is None:
+            buckets.append(None)
+            continue
+        b: Dict[str, Any] = {"scale_k": None, "scale_v": None}
+        for key, dt, shape, off, nb in parts:
+            t = typed.get(dt)
+            if t is None:
+                t = typed[dt] = slab.view(dt)
+            es = t.element_size()
+            stride = (shape[1] * shape[2], shape[2], 1) if len(shape) == 3 else (1,)
+            b[key] = t.as_strided(shape, stride, off // es)
+        n = want[code]
         b["flat"] = flat_all[start:start + n]
         b["count"] = n
         start += n
@@ -670,22 +697,12 @@ class PackedKVCache:
         self._hidx = None
         self._arr_cache = None
         G = self._int4_group_of()
-        dst: List[Optional[Dict[str, Any]]] = []
-        work: List[Optional[Dict[str, Any]]] = []
-        for code, p in enumerate(PRECISION_ORDER):
-            b = src[code]
-            if b is None or kept[code] == b["count"]:
-                dst.append(b)           # untouched bucket: dst.count == src.count
-                work.append(None)
-                continue
-            work.append(b)
-            if kept[code] == 0:
-                dst.append(None)
-                continue
-            nb = _alloc_bucket(code, kept[code], self.batch_size, self.head_dim, G, dev)
-            nb["flat"] = torch.empty(kept[code], dtype=torch.int64, device=dev)
-            nb["count"] = kept[code]
-            dst.append(nb)
+        # untouched buckets (dst.count == src.count) stay as they are; the others get new
+        # buckets, all in one allocation
+        same = [src[c] is None or kept[c] == src[c]["count"] for c in range(4)]
+        fresh = _slab_buckets(kept[:4], self.batch_size, self.head_dim, G, dev, skip=same)
+        dst: List[Optional[Dict[str, Any]]] = [src[c] if same[c] else fresh[c] for c in range(4)]
+        work: List[Optional[Dict[str, Any]]] = [None if same[c] else src[c] for c in range(4)]
         with device_ctx(dev):
             st = lib.skv_evict_compact(src_arr, _lib.buckets(dst), _lib.ptr(mask), _lib.ptr(self._slot),
                                        self.batch_size, self.seq_len, self.num_heads, self.head_dim, G,
@@ -737,15 +754,7 @@ class PackedKVCache:
             self._slot = self._slot.clone()
             self._slot_owned = True
         G = _int4_group(self.head_dim, group_size)
-        dst: List[Optional[Dict[str, Any]]] = []
-        for code in range(4):
-            if counts[code] == 0 or kept[code] == 0:
-                dst.append(None)
-                continue
-            nb = _alloc_bucket(code, kept[code], self.batch_size, self.head_dim, G, dev)
-            nb["flat"] = torch.empty(kept[code], dtype=torch.int64, device=dev)
-            nb["count"] = kept[code]
-            dst.append(nb)
+        dst = _slab_buckets([kept[c] if counts[c] else 0 for c in range(4)], self.batch_size, self.head_dim, G, dev)
         with device_ctx(dev):
             st = lib.skv_evict_compact(src_arr, _lib.buckets(dst), _lib.ptr(mask), _lib.ptr(self._slot),
                                        self.batch_size, self.seq_len, self.num_heads, self.head_dim, G,
