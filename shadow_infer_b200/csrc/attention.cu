@@ -1447,9 +1447,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                     const int s = (int)(g & 1);
                     const bool more = j + 1 < len;
                     const bool lo1 = more && !hr.exact(sg.j0 + j + 1);
+                    // every operand of P_0 V and of the next S_0 before either is issued: a wait
+                    // between the two batches would let the tensor pipe run dry (a barrier wait
+                    // costs the issuing thread as long as the MMAs it could have queued)
                     if (!mbar_wait_spin(&v_full[s], (uint32_t)((g >> 1) & 1), p.err, kErrVFull) ||
-                        !mbar_wait_spin(&p_full[0], (uint32_t)(g & 1), p.err, kErrPFull) ||
-                        (j == 0 && si > 0 && !mbar_wait_spin(&o_empty[0], (uint32_t)((si - 1) & 1), p.err, kErrOEmpty))) {
+                        (more && !mbar_wait_spin(&k_full[kstage(g + 1)], kparity(g + 1), p.err, kErrKFull)) ||
+                        (j == 0 && si > 0 && !mbar_wait_spin(&o_empty[0], (uint32_t)((si - 1) & 1), p.err, kErrOEmpty)) ||
+                        !mbar_wait_spin(&p_full[0], (uint32_t)(g & 1), p.err, kErrPFull)) {
                         ok = false;
                         break;
                     }
@@ -1457,11 +1461,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                     issue_pv(0, g, j > 0);
                     if (!more) umma_commit(&o_full[0]);
                     if (more) {
-                        if (!mbar_wait_spin(&k_full[kstage(g + 1)], kparity(g + 1), p.err, kErrKFull)) {
-                            ok = false;
-                            break;
-                        }
-                        tc_fence_after();
                         // issued after P_0 V: the tensor pipe has read P_0 before S_0 is rewritten
                         issue_s(0, g + 1, lo1);
                         umma_commit(&s_full[0]);
