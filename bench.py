@@ -289,6 +289,38 @@ def run_reference(args):
 
 
 # ------------------------------------------------------------------------------- helpers
+def host_timer(tm):
+    """Call wrapper for the per-call host-time breakdown: with a dict, adds each call's host
+    microseconds under its name; without one, just calls."""
+    def t(name, fn):
+        if tm is None:
+            return fn()
+        h = time.perf_counter()
+        r = fn()
+        tm[name] = tm.get(name, 0.0) + (time.perf_counter() - h) * 1e6
+        return r
+    return t
+
+
+def host_breakdown(step, n, world, dist):
+    """Host microseconds per API call of ``step(tm)`` over n untimed steps (this rank), with the
+    note that a call that reads device results waits there for the GPU work queued before it."""
+    import torch
+    torch.cuda.synchronize()
+    tm = {}
+    for _ in range(n):
+        step(tm)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    out = {k: round(v / n, 1) for k, v in tm.items()}
+    out["total"] = round(sum(tm.values()) / n, 1)
+    out["note"] = ("perf_counter around each call, mean of %d untimed steps, this rank; a call that reads a "
+                   "device result on the host (pack: the plan's counts; admit_codes: Python ints; evict: the "
+                   "kept counts) includes its wait for the GPU work queued before it" % n)
+    return out
+
+
 def rel_l2(a, b) -> float:
     import numpy as np
     a = np.asarray(a, dtype=np.float64)
@@ -711,14 +743,15 @@ def cfg2_phase(args, world, rank, dev, dist, lib):
     prev = PackedKVCache.pack(I["k_prev"][:, sl].contiguous().to(dev), I["v_prev"][:, sl].contiguous().to(dev),
                               None, 16, plan=PrecisionPlan.from_codes(adm))["packed_kv"]
 
-    def step():
-        codes = allocate_precision_codes(imp, "balanced")
-        sens = kv_sensitivity(k, v)
-        a, _, _ = admit(codes, imp, sens)
-        plan = PrecisionPlan.from_codes(a, reuse_mask=reuse)
-        cache = PackedKVCache.pack(k, v, None, 16, plan=plan)["packed_kv"]
-        cache.apply_reuse_mask(prev, reuse)
-        cache.unpack()
+    def step(tm=None):
+        t = host_timer(tm)
+        codes = t("allocate_precision_codes", lambda: allocate_precision_codes(imp, "balanced"))
+        sens = t("kv_sensitivity", lambda: kv_sensitivity(k, v))
+        a, _, _ = t("admit_codes", lambda: admit(codes, imp, sens))
+        plan = t("PrecisionPlan.from_codes", lambda: PrecisionPlan.from_codes(a, reuse_mask=reuse))
+        cache = t("PackedKVCache.pack", lambda: PackedKVCache.pack(k, v, None, 16, plan=plan)["packed_kv"])
+        t("apply_reuse_mask", lambda: cache.apply_reuse_mask(prev, reuse))
+        t("unpack", lambda: cache.unpack())
         return cache, a
 
     cache, a = step()
@@ -761,13 +794,14 @@ def cfg2_phase(args, world, rank, dev, dist, lib):
     host_ms = (time.perf_counter() - h0_wall) * 1e3 / steps
     launches = (lib.skv_launch_count() - n0) // steps
     ms = max_over_ranks(t0.elapsed_time(t1) / steps, world, dist, dev)
+    host_calls = host_breakdown(step, 5, world, dist)
     peak, peak_kind = hbm_peak()
     kernels = cfg2_calls(k, v, imp, reuse, prev, budget, sink, parts, dev, peak) if world == 1 else None
     return {
         "metric": "budget data-plane step GB/s (cfg2 layer, heads sharded)",
         "value": nbytes / (ms / 1e3) / 1e9, "unit": "GB/s", "ms_per_step": ms, "steps": steps,
         "frac_of_hbm_per_gpu": nbytes / world / (ms / 1e3) / 1e9 / peak, "peak_source": f"{peak_kind} hbm_gbs",
-        "host_wall_ms_per_step": host_ms, "gpu_launches_per_step": launches,
+        "host_wall_ms_per_step": host_ms, "gpu_launches_per_step": launches, "host_us_per_call": host_calls,
         "config": {"workload": "cfg2 layer: codes, sensitivity, budget admission (30 % fp16, hard eviction, 4 "
                                "sinks), plan (50 % reuse), compress+pack, reuse, unpack", "B": B, "H": H, "S": S,
                    "D": D, "heads_per_gpu": hs, "budget_bytes": budget,
@@ -1115,18 +1149,20 @@ def denoise_phase(args, world, rank, dev, dist, lib):
         r = torch.randn(1, hs, S, 1, device=dev, generator=g).abs_() * r_scale
         return x + torch.randn(x.shape, device=dev, generator=g) * r * torch.linalg.vector_norm(x, dim=-1, keepdim=True)
 
-    def layer_step(layer, k1, v1):
-        mask, st = decide_reuse_mask(k1, v1, kprev[layer], vprev[layer], 16, 16, 0.0, "conservative", zeros)
-        plan = PrecisionPlan.from_codes(codes[layer], reuse_mask=mask)
-        cur = PackedKVCache.pack(k1, v1, None, c["group"], plan=plan)["packed_kv"]
-        cur.apply_reuse_mask(prev[layer], mask)
-        removed = cur.evict(emask[layer])
-        out = packed_attention(qs[layer], cur, check=False, peer_outputs=peers[0] if peers else None,
-                               head_offset=h0)
+    def layer_step(layer, k1, v1, tm=None):
+        t = host_timer(tm)
+        mask, st = t("decide_reuse_mask", lambda: decide_reuse_mask(k1, v1, kprev[layer], vprev[layer], 16, 16, 0.0,
+                                                                    "conservative", zeros))
+        plan = t("PrecisionPlan.from_codes", lambda: PrecisionPlan.from_codes(codes[layer], reuse_mask=mask))
+        cur = t("PackedKVCache.pack", lambda: PackedKVCache.pack(k1, v1, None, c["group"], plan=plan)["packed_kv"])
+        t("apply_reuse_mask", lambda: cur.apply_reuse_mask(prev[layer], mask))
+        removed = t("evict", lambda: cur.evict(emask[layer]))
+        out = t("packed_attention", lambda: packed_attention(qs[layer], cur, check=False,
+                                                             peer_outputs=peers[0] if peers else None, head_offset=h0))
         if gathered is not None:
-            all_gather_heads(out, out=gathered)
+            t("all_gather_heads", lambda: all_gather_heads(out, out=gathered))
         if world > 1:
-            dist.all_reduce(bar)
+            t("barrier_all_reduce", lambda: dist.all_reduce(bar))
         return cur, st, removed
 
     for _ in range(3):                                 # warm-up on layer 0, state untouched
@@ -1153,6 +1189,9 @@ def denoise_phase(args, world, rank, dev, dist, lib):
     torch.cuda.synchronize()
     wall = time.perf_counter() - w0
     launches = lib.skv_launch_count() - n0
+    # host time per call, on layer 0 (its cache state is not used afterwards except as the
+    # previous cache of the same layer, which each call leaves consistent)
+    host_calls = host_breakdown(lambda tm: layer_step(0, kprev[0], vprev[0], tm), 4, world, dist)
     packed_attention(qs[0], prev[0], peer_outputs=peers[0] if peers else None, head_offset=h0)   # error word
     if world > 1:
         dist.all_reduce(bar)
@@ -1167,6 +1206,7 @@ def denoise_phase(args, world, rank, dev, dist, lib):
         "attention_tflops_whole_loop": flops / (total_ms / 1e3) / 1e12,
         "reuse_ratio_mean": statistics.mean(st["reuse_ratio"] for st in stats),
         "evicted_entries_rank0": removed_n, "gpu_launches": launches, "exchange": exchange,
+        "host_us_per_layer_step": host_calls,
         "scaling": "strong (heads sharded over GPUs; outputs gathered to every rank)",
         "config": {"workload": "cfg4: per step and layer drift -> reuse decision (drift < 0.05) -> re-pack -> reuse "
                                "-> evict 25 % lowest importance -> packed attention", "B": B, "H": H, "S": S, "D": D,
