@@ -289,6 +289,55 @@ def run_reference(args):
 
 
 # ------------------------------------------------------------------------------- helpers
+def exchange_ceiling(peers, attn_fused, attn_local, h0, hs, world, dist, dev, reps=5):
+    """At N > 1: the plain exchange -- ``skv_peer_store`` copying this rank's heads of the output
+    (already in its buffer) into every rank's buffer -- timed alone, next to the fused epilogue's
+    cost (the attention storing into every rank's buffer against the same attention storing into
+    its local output only).  Events on the launching stream, a one-element all-reduce before each
+    call, max over ranks."""
+    import torch
+    from shadow_infer_b200 import _lib
+    lib = _lib.load()
+    buf = peers[0]
+    B, H, S_q, D = buf.local.shape
+    src = buf.local[:, h0:h0 + hs].clone()     # a copy, so that no store overwrites its own source
+    nbytes = src.numel() * 4
+    bar = torch.ones(1, device=dev)
+    stream = _lib.stream_of(dev)
+
+    def timed(fn):
+        ms = []
+        for _ in range(reps):
+            dist.all_reduce(bar)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn()
+            b.record()
+            torch.cuda.synchronize()
+            ms.append(a.elapsed_time(b))
+        dist.all_reduce(bar)
+        return max_over_ranks(statistics.median(ms), world, dist, dev)
+
+    def plain():
+        for b in range(B):
+            st = lib.skv_peer_store(_lib.ptr(src[b]), hs * S_q * D * 4, _lib.ptr(buf.ptrs), world,
+                                    ((b * H + h0) * S_q * D) * 4, stream)
+            if st != 0:
+                raise RuntimeError(_lib.last_error())
+
+    ms_plain = timed(plain)
+    ms_fused = timed(attn_fused)
+    ms_local = timed(attn_local)
+    egress = nbytes * (world - 1)
+    return {"plain_store": {"kernel": "skv_peer_store: 16-byte loads once, stores into every rank's buffer",
+                            "bytes_per_rank": nbytes, "ms": ms_plain,
+                            "egress_gbs_per_gpu": egress / (ms_plain / 1e3) / 1e9},
+            "fused_epilogue": {"attention_ms_storing_to_all_ranks": ms_fused, "attention_ms_local_only": ms_local,
+                               "exchange_cost_ms": ms_fused - ms_local,
+                               "egress_gbs_per_gpu_if_serial": egress / (max(ms_fused - ms_local, 1e-6) / 1e3) / 1e9},
+            "nvlink_reference": "peer copy 770 GB/s per direction per GPU (measured on this pool)"}
+
+
 def host_timer(tm):
     """Call wrapper for the per-call host-time breakdown: with a dict, adds each call's host
     microseconds under its name; without one, just calls."""
@@ -599,6 +648,10 @@ def long_context_phase(args, world, rank, dev, dist, lib, heads_total=None, extr
     }
     if extras and world == 1:
         res["vs_sdpa"] = sdpa_compare(args, dev, cache, q, parts["staging"] + attn_ms, reps=3)
+    if world > 1 and peers:
+        res["exchange_ceiling"] = exchange_ceiling(
+            peers, lambda: packed_attention(q, cache, check=False, peer_outputs=peers[0], head_offset=h0),
+            lambda: packed_attention(q, cache, check=False), h0, hs, world, dist, dev, reps=3)
     if extras:
         res["e2e"] = long_context_e2e(args, world, rank, dev, dist, L, imp_h, step, peers, gathered, h0, hs)
         if world == 1 and rank == 0:
@@ -941,6 +994,9 @@ def attention_phase(args, world, rank, dev, dist, lib):
 
     check = check_long_context(full, lambda: packed_attention(qd, cache), h0, hs, S, world, rank, dev, dist,
                                layer_fn, lambda Lh, h: codes_all[:, h:h + 1].numpy(), 200)
+    ceiling = exchange_ceiling(
+        peers, lambda: packed_attention(qd, cache, check=False, peer_outputs=peers[0], head_offset=h0),
+        lambda: packed_attention(qd, cache, check=False), h0, hs, world, dist, dev) if world > 1 and peers else None
     close_peers(peers, dist)
     ms = max_over_ranks(t0.elapsed_time(t1) / steps, world, dist, dev)
     stage_ms = statistics.mean(a.elapsed_time(b) for a, b, _ in kev)
@@ -953,7 +1009,7 @@ def attention_phase(args, world, rank, dev, dist, lib):
         "metric": "packed-attn tokens/s (32-layer stack, cfg3)",
         "value": B * S / (L * ms / 1e3), "unit": "tokens/s", "ms_per_layer": ms, "steps": steps,
         "scaling": "strong (heads sharded over GPUs; outputs gathered to every rank)",
-        "exchange": exchange,
+        "exchange": exchange, "exchange_ceiling": ceiling,
         "config": {"workload": "cfg3: packed K/V codes 20/50/30 fp16/int8/int4, fp16 queries, non-causal",
                    "B": B, "H": H, "S_q": S, "S_kv": S, "D": D, "layers": L, "heads_per_gpu": hs},
         "roofline": {"kernel": "packed_attention_kernel", "bound": "tensor",

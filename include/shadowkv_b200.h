@@ -222,6 +222,13 @@ int skv_ipc_handle_bytes(void);
 int skv_ipc_export(const void* ptr, void* handle, int64_t* offset);
 int skv_ipc_open(const void* handle, int64_t offset, void** base, void** ptr);
 int skv_ipc_close(void* base);
+/* The plain exchange, for measuring the fused epilogue against it: bytes of src (device, this
+ * rank's share) stored at byte offset dst_offset of each of the n_dst buffers whose addresses
+ * dst_ptrs (device int64[n_dst], e.g. a PeerOutputs' ptrs) holds -- this rank's own buffer and
+ * its peers' over NVLink.  Every 16-byte chunk is loaded once; no load reads peer memory.
+ * src, bytes and dst_offset 16-byte multiples; the destinations 16-byte aligned. */
+int skv_peer_store(const void* src, int64_t bytes, const int64_t* dst_ptrs, int n_dst, int64_t dst_offset,
+                   void* stream);
 /* max_ctas: CTAs of the persistent attention kernel (0 = one per SM); fewer leave SMs free for
  * work that should run beside it (e.g. the NCCL all-gather of the previous layer's outputs).
  * flags (the _gqa / _peers entry points; staging and attention take the same flags):

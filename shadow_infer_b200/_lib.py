@@ -101,6 +101,7 @@ _SIGNATURES = {
     "skv_ipc_export": (c_int, [c_void_p, c_void_p, ctypes.POINTER(c_int64)]),
     "skv_ipc_open": (c_int, [c_void_p, c_int64, ctypes.POINTER(c_void_p), ctypes.POINTER(c_void_p)]),
     "skv_ipc_close": (c_int, [c_void_p]),
+    "skv_peer_store": (c_int, [c_void_p, c_int64, c_void_p, c_int, c_int64, c_void_p]),
     "skv_packed_attention_gqa": (c_int, [c_void_p, c_int, c_int, c_int, c_int, ctypes.POINTER(SkvBucket), c_int, c_int,
                                          c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int, ctypes.c_float,
                                          c_void_p, c_size_t, c_void_p, c_void_p, c_int, c_int, c_void_p]),

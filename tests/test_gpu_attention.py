@@ -291,19 +291,49 @@ def _peer_worker(rank, world, port, ret):
         torch.cuda.synchronize()
         dist.barrier()                          # every rank's stores have landed
         full = out.cpu()
+        dist.barrier()                          # nobody rewrites a buffer another rank still reads
+        # the plain exchange: this rank's heads of the output copied into every rank's buffer
+        from shadow_infer_b200 import _lib
+        mine = out[:, h0:h1].clone()            # a copy: the buffer is cleared below
+        peers.local.zero_()
+        torch.cuda.synchronize()
+        dist.barrier()
+        st = _lib.load().skv_peer_store(_lib.ptr(mine), mine.numel() * 4, _lib.ptr(peers.ptrs), world,
+                                        h0 * SQ * D * 4, _lib.stream_of(torch.device("cuda", rank)))
+        torch.cuda.synchronize()
+        dist.barrier()
+        plain_ok = st == 0 and torch.equal(peers.local.cpu(), full)
         dist.barrier()                          # nobody unmaps a buffer another rank still reads
         peers.close()
         allf = [torch.empty_like(full) for _ in range(world)]
         dist.all_gather(allf, full)
         ref = O.packed_attention(q.astype(np.float32), O.pack(k, v, O.plan_from_codes(codes), 16))
-        ret[rank] = bool(all(torch.equal(f, full) for f in allf)) and rel_l2(full.numpy(), ref) < REL_L2_TOL
+        ret[rank] = (bool(all(torch.equal(f, full) for f in allf)) and rel_l2(full.numpy(), ref) < REL_L2_TOL
+                     and plain_ok)
     finally:
         dist.destroy_process_group()
 
 
+def test_peer_store_local_destinations(skv):
+    """skv_peer_store into two buffers of this GPU at a byte offset: both hold the source there
+    and nothing else changes."""
+    from shadow_infer_b200 import _lib
+    src = torch.randn(3, 1000, 4, device="cuda")
+    dst = [torch.full((5000 * 4,), -1.0, device="cuda") for _ in range(2)]
+    ptrs = torch.tensor([d.data_ptr() for d in dst], dtype=torch.int64, device="cuda")
+    st = _lib.load().skv_peer_store(_lib.ptr(src), src.numel() * 4, _lib.ptr(ptrs), 2, 1000 * 16,
+                                    _lib.stream_of(torch.device("cuda", 0)))
+    assert st == 0
+    torch.cuda.synchronize()
+    for d in dst:
+        assert torch.equal(d[4000:4000 + src.numel()], src.reshape(-1))
+        assert bool((d[:4000] == -1).all()) and bool((d[4000 + src.numel():] == -1).all())
+    assert _lib.load().skv_peer_store(_lib.ptr(src), 8, _lib.ptr(ptrs), 2, 0, None) != 0   # not 16-byte sized
+
+
 def test_attention_peer_outputs_two_gpus(skv):
     """Two ranks (one process per GPU), heads sharded, outputs exchanged by the kernel's own
-    stores into the CUDA IPC mappings of each other's buffers."""
+    stores into the CUDA IPC mappings of each other's buffers (and by the plain copy kernel)."""
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     import socket
