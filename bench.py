@@ -1658,7 +1658,7 @@ def run_b200(args):
         "dtype_note": "attention in fp16 tensor-core operands with fp32 accumulation and softmax; the data plane "
                       "quantises fp32 K/V to fp16/int8/int4 bit-exactly",
     }
-    for key in ("cpu_baseline", "attention_variants", "vs_sdpa"):
+    for key in ("cpu_baseline", "attention_variants", "vs_sdpa", "exchange_ceiling"):
         if key in head:
             line[key] = head[key]
     line.update(extras)
