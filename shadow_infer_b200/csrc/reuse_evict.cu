@@ -22,12 +22,12 @@ __device__ __forceinline__ bool aligned16(const void* a, const void* b, const vo
 // together.  The payload rows to copy, of every precision, are cut into 16-byte chunks numbered
 // through a warp prefix sum of the rows' chunk counts; each pass hands every lane kChunks chunks
 // of K and of V, all loaded before the first store, so one warp keeps up to 2 * 32 * kChunks
-// loads in flight whatever the precision mix.  A lane copies its own entry's scales (at most 8
-// floats per row, as float4 loads issued with the first pass).  Rows that are not whole 16-byte
+// loads in flight whatever the precision mix, and 64 registers allow 32 warps per SM.  A lane
+// copies its own entry's scales (at most 8 floats per row, as float4) after the payload.  Rows that are not whole 16-byte
 // chunks at 16-byte aligned addresses take a per-row warp copy instead.
-constexpr int kChunks = 4;
+constexpr int kChunks = 2;   // 16-byte chunks of K and of V per lane and pass
 
-__global__ void __launch_bounds__(256, 2) reuse_kernel(const __grid_constant__ Buckets cur,
+__global__ void __launch_bounds__(256, 4) reuse_kernel(const __grid_constant__ Buckets cur,
                                                        const int32_t* __restrict__ cur_slot, int S,
                                                        const __grid_constant__ Buckets prev,
                                                        const int32_t* __restrict__ prev_slot,
@@ -61,21 +61,6 @@ __global__ void __launch_bounds__(256, 2) reuse_kernel(const __grid_constant__ B
         const int64_t cp = slot_pos(cs), pp = slot_pos(ps);
         const skv_bucket& cb = cur.b[code];
         const skv_bucket& pb = prev.b[code];
-        // scales: this lane's own row, loaded now (in flight with the first payload pass)
-        const bool svec = copy && sf > 0 && (sf & 3) == 0 && sf <= 8 &&
-                          aligned16(pb.scale_k + pp * sf, pb.scale_v + pp * sf, cb.scale_k + cp * sf,
-                                    cb.scale_v + cp * sf);
-        float4 k0 = make_float4(0.f, 0.f, 0.f, 0.f), v0 = k0, k1 = k0, v1 = k0;
-        if (svec) {
-            const float4* ssk = reinterpret_cast<const float4*>(pb.scale_k + pp * sf);
-            const float4* ssv = reinterpret_cast<const float4*>(pb.scale_v + pp * sf);
-            k0 = __ldg(ssk);
-            v0 = __ldg(ssv);
-            if (sf > 4) {
-                k1 = __ldg(ssk + 1);
-                v1 = __ldg(ssv + 1);
-            }
-        }
         // payload: whole 16-byte chunks at aligned addresses go through the chunk passes
         const bool chunked = copy && (rb & 15) == 0 && aligned16(cb.k, cb.v, pb.k, pb.v);
         const int nch = chunked ? (int)(rb >> 4) : 0;
@@ -122,6 +107,21 @@ __global__ void __launch_bounds__(256, 2) reuse_kernel(const __grid_constant__ B
                     *reinterpret_cast<uint4*>(dk[u]) = a[u];
                     *reinterpret_cast<uint4*>(dv[u]) = b[u];
                 }
+        }
+        // scales: this lane's own row (after the payload passes, so that their registers are free)
+        const bool svec = copy && sf > 0 && (sf & 3) == 0 && sf <= 8 &&
+                          aligned16(pb.scale_k + pp * sf, pb.scale_v + pp * sf, cb.scale_k + cp * sf,
+                                    cb.scale_v + cp * sf);
+        float4 k0 = make_float4(0.f, 0.f, 0.f, 0.f), v0 = k0, k1 = k0, v1 = k0;
+        if (svec) {
+            const float4* ssk = reinterpret_cast<const float4*>(pb.scale_k + pp * sf);
+            const float4* ssv = reinterpret_cast<const float4*>(pb.scale_v + pp * sf);
+            k0 = __ldg(ssk);
+            v0 = __ldg(ssv);
+            if (sf > 4) {
+                k1 = __ldg(ssk + 1);
+                v1 = __ldg(ssv + 1);
+            }
         }
         if (svec) {
             float4* dsk = reinterpret_cast<float4*>(cb.scale_k + cp * sf);
