@@ -1043,6 +1043,8 @@ ATTN_VARIANTS = {
     "one_tile": ({"one_tile": True}, "one query tile of 128 rows per work unit, two score buffers (SKV_ATTN_ONE_TILE)"),
     "fma_exp": ({"fma_exp": True},
                 "a quarter of the softmax exponentials by a polynomial on the FMA pipe (SKV_ATTN_FMA_EXP)"),
+    "pair": ({"pair": True}, "two CTAs per unit, M=256 tensor-core MMAs over the pair, scores two KV steps "
+                             "ahead, softmax over eight warps per query tile (SKV_ATTN_PAIR)"),
 }
 
 

@@ -249,6 +249,13 @@ int skv_peer_store(const void* src, int64_t bytes, const int64_t* dst_ptrs, int 
  *                       exponentials with a polynomial on the FMA pipe (relative error <= 7.5e-5)
  *                       instead of the MUFU. */
 #define SKV_ATTN_FMA_EXP 4
+/*   SKV_ATTN_PAIR     -- head_dim 128: the CTA-pair pipeline.  Two CTAs (one cluster) take a unit of
+ *                       256 queries, one 128-row query tile each; the tensor-core MMAs are issued for
+ *                       both at once (M = 256), each CTA loading half of every staged K and V tile,
+ *                       so a CTA's TMEM holds two score buffers and the scores run two KV steps ahead
+ *                       of the P V products; the tile's softmax is split over eight warps.  Takes no
+ *                       other pipeline flag (FAST_K may be combined). */
+#define SKV_ATTN_PAIR 8
 int skv_packed_attention_gqa(const void* q, int B, int H_q, int S_q, int D, const skv_bucket* buckets, int H_kv,
                              int S_kv, int int4_group, const int32_t* rows, const int32_t* counts,
                              const float* k_new, const float* v_new, int S_new, float scale, void* scratch,

@@ -128,6 +128,7 @@ struct AttnParams {
     int* err;
     int klo;                   // 1: the head's kLoCh largest channels of K also contribute their lo part
     int one_tile;              // 1: the single-query-tile kernel (units of 128 queries); 0: two tiles (256)
+    int pair;                  // 1: the CTA-pair kernel (units of 256 queries over two CTAs, head_dim 128)
     int emu;                   // two-tile kernel: a quarter of the exponentials on the FMA pipe
     unsigned* chmax;           // [H_kv, D] max |K| per channel (float bits), channel selection input
     int* sel;                  // [H_kv, kLoCh] the selected channels, ascending
@@ -1503,6 +1504,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 
 
 #include "attention_1t.cuh"
+#include "attention_pair.cuh"
 
 // ---------------------------------------------------------------------------------------
 // per-head row index
@@ -1631,8 +1633,10 @@ int attn_params(const void* q, int B, int H, int S_q, int D, const skv_bucket* b
                 AttnParams& prm, const char* what, int max_ctas = 0, float* const* peers = nullptr,
                 int n_peers = 0, int head_off = 0, int H_out = 0, int flags = 0) {
     if (!rows || !counts || !scratch) return fail(SKV_ERR_INVALID_ARGUMENT, "%s: null pointer", what);
-    if (flags & ~(SKV_ATTN_FAST_K | SKV_ATTN_ONE_TILE | SKV_ATTN_FMA_EXP))
+    if (flags & ~(SKV_ATTN_FAST_K | SKV_ATTN_ONE_TILE | SKV_ATTN_FMA_EXP | SKV_ATTN_PAIR))
         return fail(SKV_ERR_INVALID_ARGUMENT, "%s: unknown flags 0x%x", what, flags);
+    if ((flags & SKV_ATTN_PAIR) && (flags & (SKV_ATTN_ONE_TILE | SKV_ATTN_FMA_EXP)))
+        return fail(SKV_ERR_INVALID_ARGUMENT, "%s: the CTA-pair pipeline takes no other pipeline flag", what);
     if (B <= 0 || H <= 0 || S_q <= 0 || S_kv <= 0 || H_kv <= 0 || S_new < 0)
         return fail(SKV_ERR_INVALID_ARGUMENT, "%s: bad shape", what);
     if (H % H_kv) return fail(SKV_ERR_SHAPE, "%s: %d query heads do not group over %d KV heads", what, H, H_kv);
@@ -1692,6 +1696,7 @@ int attn_params(const void* q, int B, int H, int S_q, int D, const skv_bucket* b
     prm.S_kv = S_kv;
     prm.G = G;
     prm.one_tile = (flags & SKV_ATTN_ONE_TILE) ? 1 : 0;
+    prm.pair = (flags & SKV_ATTN_PAIR) ? 1 : 0;
     prm.emu = (flags & SKV_ATTN_FMA_EXP) ? 1 : 0;
     prm.QP = prm.one_tile ? (S_q + k1TUnitRows - 1) / k1TUnitRows : (S_q + kUnitRows - 1) / kUnitRows;
     prm.scale_log2 = scale * 1.4426950408889634f;
@@ -1778,6 +1783,39 @@ int launch_attention(const AttnParams& prm, cudaStream_t s) {
                            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                            CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fail(SKV_ERR_CUDA, "attend_kv_tiles: tensor map encoding failed (%d)", (int)r);
+    if (prm.pair) {
+        if constexpr (D != 128) {
+            return fail(SKV_ERR_UNSUPPORTED, "attend_kv_tiles: the CTA-pair pipeline needs head_dim 128");
+        } else {
+            // the staged tiles as rows of 128 bytes (no swizzle: they are staged in the layout the
+            // MMA reads); boxes of 64 rows for K and V halves, of 16 rows for lo halves
+            const size_t staged = (size_t)prm.B * prm.H_kv * prm.ntmax * staged_set_bytes(D);
+            const cuuint64_t sdims[2] = {128, (cuuint64_t)(staged / 128)};
+            const cuuint64_t sstr[1] = {128};
+            const cuuint32_t sbox[2] = {128, 64}, lbox[2] = {128, 16};
+            CUtensorMap stmap, lomap;
+            CUresult r2 = enc(&stmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, prm.stage, sdims, sstr, sbox, estr,
+                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+            if (r2 == CUDA_SUCCESS)
+                r2 = enc(&lomap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, prm.stage, sdims, sstr, lbox, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+            if (r2 != CUDA_SUCCESS)
+                return fail(SKV_ERR_CUDA, "attend_kv_tiles: staged-tile tensor map encoding failed (%d)", (int)r2);
+            const int smem = prm.n_peers > 0 ? PairLayout<true>::kAlloc : PairLayout<false>::kAlloc;
+            void* kern = prm.n_peers > 0 ? reinterpret_cast<void*>(packed_attention_pair_kernel<true>)
+                                         : reinterpret_cast<void*>(packed_attention_pair_kernel<false>);
+            cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+            AttnParams a = prm;
+            void* args[] = {&qmap, &stmap, &lomap, &a};
+            const unsigned grid = (unsigned)(prm.slots & ~1);     // whole pairs (the kernel is clustered by 2)
+            const cudaError_t e = cudaLaunchKernel(kern, dim3(grid > 0 ? grid : 2), dim3(kPairThreads), args,
+                                                   (size_t)smem, s);
+            if (e != cudaSuccess) return fail(SKV_ERR_CUDA, "attend_kv_tiles: pair launch failed: %s", cudaGetErrorString(e));
+            return check_launch("attend_kv_tiles");
+        }
+    }
     if (cudaMemsetAsync(prm.part_flag, 0, (size_t)prm.slots * sizeof(int), s) != cudaSuccess)
         return fail(SKV_ERR_CUDA, "attend_kv_tiles: memset failed");
     int smem, threads;

@@ -38,6 +38,7 @@ def packed_attention(
     fast_k: bool = False,
     one_tile: bool = False,
     fma_exp: bool = False,
+    pair: bool = False,
 ) -> torch.Tensor:
     """Non-causal attention of ``q`` [B, H_q, S_q, D] over a packed cache; returns fp32 [B, H_q, S_q, D].
 
@@ -123,7 +124,7 @@ def packed_attention(
     stream = _lib.stream_of(dev)
     g = c._int4_group_of()
     flags = ((_lib.SKV_ATTN_FAST_K if fast_k else 0) | (_lib.SKV_ATTN_ONE_TILE if one_tile else 0) |
-             (_lib.SKV_ATTN_FMA_EXP if fma_exp else 0))
+             (_lib.SKV_ATTN_FMA_EXP if fma_exp else 0) | (_lib.SKV_ATTN_PAIR if pair else 0))
     if peer_outputs is not None:
         Bp, Hp, Sp, Dp = peer_outputs.shape
         if (Bp, Sp, Dp) != (B, S_q, D) or not 0 <= head_offset <= Hp - H:

@@ -431,3 +431,94 @@ def test_attention_fma_exponentials(skv, B, H, S, SQ, D, probs, qs):
     ref = O.packed_attention(q.astype(np.float32), O.pack(k, v, O.plan_from_codes(codes), 16))
     out = skv.packed_attention(torch.from_numpy(q).cuda(), cache, fma_exp=True).cpu().numpy()
     assert rel_l2(out, ref) < REL_L2_TOL
+
+
+# ---------------------------------------------------------------- the CTA-pair pipeline
+PAIR_CASES = [c for c in CASES if c[4] == 128]
+
+
+# P is rounded to fp16 relative to a running row max; the default pipeline's stream-K parts each
+# start their own, so the two pipelines round P differently: about 1.4e-4 relative each (the
+# output is an average of random V rows, which does not shrink the relative error), ~2e-4 apart.
+PAIR_VS_DEFAULT_TOL = 5e-4
+
+
+@pytest.mark.parametrize("B,H,S,SQ,D,probs,qs", PAIR_CASES)
+@pytest.mark.parametrize("outliers", [False, True])
+def test_attention_pair_pipeline(skv, B, H, S, SQ, D, probs, qs, outliers):
+    """Two CTAs per unit of 256 queries (tensor-core MMAs over the pair): the same attention as
+    the default two-tile pipeline, within 1e-3 of the oracle.  With outlier channels (four K
+    channels ten times larger) the lo correction is what keeps the error below 1e-3: K in
+    fp16 alone is ~2e-3 off, so a pair that dropped the lo MMA of either CTA's keys fails."""
+    rng = np.random.default_rng(S * 31 + D)
+    k = rng.standard_normal((B, H, S, D)).astype(np.float32)
+    if outliers:
+        k[..., [3, 17, 50, 99]] *= 10.0
+    v = rng.standard_normal((B, H, S, D)).astype(np.float32)
+    codes = rng.choice(5, size=(S, H), p=probs).astype(np.int8)
+    q = (rng.standard_normal((B, H, SQ, D)) * qs).astype(np.float16)
+    cache = _pack(skv, k, v, codes)
+    ref = O.packed_attention(q.astype(np.float32), O.pack(k, v, O.plan_from_codes(codes), 16))
+    qd = torch.from_numpy(q).cuda()
+    two = skv.packed_attention(qd, cache).cpu().numpy()
+    pair = skv.packed_attention(qd, cache, pair=True).cpu().numpy()
+    assert rel_l2(pair, ref) < REL_L2_TOL
+    assert rel_l2(pair, ref) < 1.5 * rel_l2(two, ref) + 1e-4
+    assert rel_l2(pair, two) < PAIR_VS_DEFAULT_TOL
+    fast = skv.packed_attention(qd, cache, pair=True, fast_k=True).cpu().numpy()
+    assert rel_l2(fast, skv.packed_attention(qd, cache, fast_k=True).cpu().numpy()) < PAIR_VS_DEFAULT_TOL
+
+
+@pytest.mark.parametrize("B,H_kv,rep,S,SN,SQ,D,probs", [c for c in GQA_CASES if c[6] == 128])
+def test_attention_pair_gqa_new_rows(skv, B, H_kv, rep, S, SN, SQ, D, probs):
+    rng = np.random.default_rng(S * 7 + SN * 3 + rep)
+    k = rng.standard_normal((B, H_kv, S, D)).astype(np.float32)
+    v = rng.standard_normal((B, H_kv, S, D)).astype(np.float32)
+    codes = rng.choice(5, size=(S, H_kv), p=probs).astype(np.int8)
+    kn = rng.standard_normal((B, H_kv, SN, D)).astype(np.float32)
+    vn = rng.standard_normal((B, H_kv, SN, D)).astype(np.float32)
+    q = rng.standard_normal((B, H_kv * rep, SQ, D)).astype(np.float16)
+    cache = _pack(skv, k, v, codes)
+    out = skv.packed_attention(torch.from_numpy(q).cuda(), cache, pair=True,
+                               k_new=torch.from_numpy(kn).cuda() if SN else None,
+                               v_new=torch.from_numpy(vn).cuda() if SN else None).cpu().numpy()
+    ref = O.packed_attention(q.astype(np.float32), O.pack(k, v, O.plan_from_codes(codes), 16),
+                             k_new=kn if SN else None, v_new=vn if SN else None)
+    assert rel_l2(out, ref) < REL_L2_TOL
+
+
+def test_attention_pair_evicted_head_few_pairs_and_peers(skv):
+    """A fully evicted head (zero output), units spread over two pairs only (max_ctas=4), and the
+    fused store into two output buffers."""
+    rng = np.random.default_rng(9)
+    B, H, S, SQ, D = 2, 3, 700, 600, 128
+    k = rng.standard_normal((B, H, S, D)).astype(np.float32)
+    v = rng.standard_normal((B, H, S, D)).astype(np.float32)
+    codes = rng.integers(0, 5, size=(S, H)).astype(np.int8)
+    codes[:, 1] = 4
+    q = rng.standard_normal((B, H, SQ, D)).astype(np.float16)
+    cache = _pack(skv, k, v, codes)
+    ref = O.packed_attention(q.astype(np.float32), O.pack(k, v, O.plan_from_codes(codes), 16))
+    qd = torch.from_numpy(q).cuda()
+    for mc in (0, 4):
+        out = skv.packed_attention(qd, cache, pair=True, max_ctas=mc).cpu().numpy()
+        assert rel_l2(out, ref) < REL_L2_TOL
+        assert np.abs(out[:, 1]).max() == 0.0
+    peers = _TwoBuffers((B, H, SQ, D), 0)
+    skv.packed_attention(qd, cache, pair=True, peer_outputs=peers, head_offset=0)
+    torch.cuda.synchronize()
+    assert torch.equal(peers.bufs[0], peers.bufs[1])
+    assert rel_l2(peers.bufs[0].cpu().numpy(), ref) < REL_L2_TOL
+
+
+def test_attention_pair_rejects_other_shapes_and_flags(skv):
+    rng = np.random.default_rng(2)
+    k = rng.standard_normal((1, 2, 64, 64)).astype(np.float32)
+    cache = _pack(skv, k, k, np.full((64, 2), 2, dtype=np.int8))
+    with pytest.raises(RuntimeError, match="head_dim 128"):
+        skv.packed_attention(torch.zeros(1, 2, 8, 64, dtype=torch.float16, device="cuda"), cache, pair=True)
+    k = rng.standard_normal((1, 2, 64, 128)).astype(np.float32)
+    cache = _pack(skv, k, k, np.full((64, 2), 2, dtype=np.int8))
+    with pytest.raises(ValueError, match="CTA-pair"):
+        skv.packed_attention(torch.zeros(1, 2, 8, 128, dtype=torch.float16, device="cuda"), cache, pair=True,
+                             one_tile=True)
