@@ -327,6 +327,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
         vc.start(ss, pair, npairs, U);
         long long gk = 0, gv = 0;
         bool ok = true;
+        HeadRows hr;      // the head of cursor kc's unit
         auto load_q = [&](const PairCursor& c) -> bool {
             const int qb = c.k & 1;
             if (c.k >= 2 && !warp_wait(&q_empty[qb], (uint32_t)(((c.k - 2) >> 1) & 1), p.err, kErrQEmpty))
@@ -373,8 +374,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
             const int s = (int)(g % kPairNK);
             const long long n = g / kPairNK;
             if (n >= 1 && !warp_wait(&k_empty[s], (uint32_t)((n - 1) & 1), p.err, kErrKEmpty)) return false;
-            HeadRows hr;
-            hr.load(p, c.h);
+            if (c.first()) hr.load(p, c.h);
             const bool lo = !hr.exact(c.j);
             if (lane == 0) {
                 const int64_t set = staged_offset(p, c.b, c.h / p.rep, c.j, D);
@@ -436,16 +436,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
             sc.start(ss, pair, npairs, U);
             long long g = 0, gs = 0;
             bool ok = true, issued = false;
+            HeadRows hr;      // the head of cursor sc's unit (global loads once per unit, off the step loop)
             // S of step gs (cursor sc) into S buffer gs & 1
             auto issue_s = [&]() -> bool {
                 const int ks = (int)(gs % kPairNK);
                 const int qb = sc.k & 1;
+                if (sc.first()) hr.load(p, sc.h);
                 if ((sc.first() && !mbar_wait_pair(&q_ready[qb], (uint32_t)((sc.k >> 1) & 1), p.err, kErrQFull)) ||
                     !mbar_wait_spin(&k_full[ks], (uint32_t)((gs / kPairNK) & 1), p.err, kErrKFull))
                     return false;
                 tc_fence_after();
-                HeadRows hr;
-                hr.load(p, sc.h);
                 const uint32_t d = tmem + (uint32_t)(gs & 1) * 128;
                 const uint64_t qd = qd0 + (uint64_t)((qb * TB) >> 4);
                 const uint64_t kd = kd0 + (uint64_t)((ks * kPairHalf) >> 4);
