@@ -64,6 +64,7 @@ def parse_args():
     ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
     ap.add_argument("--ref-rows", type=int, default=128, help="query rows per head timed by the CPU reference")
     ap.add_argument("--no-extras", action="store_true", help="the headline step only (no sub-objects)")
+    ap.add_argument("--clock-ms", type=int, default=100, help="nvidia-smi clock sampling period during the headline")
     ap.add_argument("--phase", choices=("all", "long-slice", "cfg2", "attention-cfg3", "paged", "paged-kernels",
                                         "decisions"),
                     default="all",
@@ -126,8 +127,9 @@ class ClockSampler:
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, index: int):
+    def __init__(self, index: int, period_ms: int = 100):
         self.index = index
+        self.period_ms = period_ms
         self.rows = []
         self._proc = None
         self._thread = None
@@ -136,7 +138,7 @@ class ClockSampler:
         try:
             self._proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                 "-lms", str(self.period_ms)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self._proc = None
             return
@@ -1624,7 +1626,7 @@ def run_b200(args):
             print(json.dumps({"phase": args.phase, "result": res}), flush=True)
         return 0
 
-    sampler = ClockSampler(local) if rank == 0 else None
+    sampler = ClockSampler(local, args.clock_ms) if rank == 0 else None
     if sampler:
         sampler.start()
     head = long_context_phase(args, world, rank, dev, dist, lib)
