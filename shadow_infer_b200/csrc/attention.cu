@@ -1511,84 +1511,97 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 // ---------------------------------------------------------------------------------------
 constexpr int kHiThreads = 1024;
 
-__global__ void __launch_bounds__(kHiThreads) head_index_kernel(const int32_t* __restrict__ slot, int S, int H,
+// Grid (chunks, H): block (c, h) first counts every token of head h per code -- the totals give
+// where each code's run of rows starts, the counts of the tokens before its chunk its offset
+// inside each run -- and then writes the rows of the stored entries of its chunk of tokens
+// (C tokens, a multiple of the block size) in token order: ballots per warp, an exclusive scan
+// of the warps' counts by warp 0, one pass of the block per 1024 tokens.  Splitting a head over
+// several blocks keeps the kernel short when there are few heads (a head-sharded rank).
+__global__ void __launch_bounds__(kHiThreads) head_index_kernel(const int32_t* __restrict__ slot, int S, int H, int C,
                                                                 int32_t* __restrict__ rows, int32_t* __restrict__ counts) {
-    const int h = blockIdx.x;
+    constexpr int NW = kHiThreads / 32;
+    const int h = blockIdx.y;
+    const int t_begin = blockIdx.x * C, t_end = min(S, t_begin + C);
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-    __shared__ int s_red[5][32];
-    __shared__ int s_base[4];
-    __shared__ int s_warp[4][32];
-    int c0 = 0, c1 = 0, c2 = 0, c3 = 0, c4 = 0;
+    __shared__ int s_red[9][NW];     // per warp: totals of codes 0-4, then codes 0-3 before the chunk
+    __shared__ int s_run[4];
+    __shared__ int s_cnt[4][NW];
+    __shared__ int s_pre[4][NW];
+    __shared__ int s_tot[4];
+    int c[9] = {0, 0, 0, 0, 0, 0, 0, 0, 0};
     for (int t = threadIdx.x; t < S; t += kHiThreads) {
         const int32_t sl = slot[(int64_t)t * H + h];
         const int code = sl < 0 ? 4 : slot_code(sl);
-        c0 += code == 0;
-        c1 += code == 1;
-        c2 += code == 2;
-        c3 += code == 3;
-        c4 += code == 4;
+        const bool before = t < t_begin;
+#pragma unroll
+        for (int k = 0; k < 5; ++k) c[k] += code == k;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) c[5 + k] += (code == k) & before;
     }
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        c0 += __shfl_xor_sync(0xffffffffu, c0, o);
-        c1 += __shfl_xor_sync(0xffffffffu, c1, o);
-        c2 += __shfl_xor_sync(0xffffffffu, c2, o);
-        c3 += __shfl_xor_sync(0xffffffffu, c3, o);
-        c4 += __shfl_xor_sync(0xffffffffu, c4, o);
+    for (int k = 0; k < 9; ++k) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) c[k] += __shfl_xor_sync(0xffffffffu, c[k], o);
     }
     if (lane == 0) {
-        s_red[0][w] = c0;
-        s_red[1][w] = c1;
-        s_red[2][w] = c2;
-        s_red[3][w] = c3;
-        s_red[4][w] = c4;
+#pragma unroll
+        for (int k = 0; k < 9; ++k) s_red[k][w] = c[k];
     }
     __syncthreads();
-    if (threadIdx.x == 0) {
-        int base = 0;
-        for (int k = 0; k < 5; ++k) {
-            int v = 0;
-            for (int q = 0; q < kHiThreads / 32; ++q) v += s_red[k][q];
-            if (k < 4) s_base[k] = base;
-            base += v;
-            counts[(int64_t)h * 5 + k] = v;
+    if (w == 0) {
+        // lane k < 9: the block's sum of row k
+        int v = 0;
+        if (lane < 9)
+            for (int q = 0; q < NW; ++q) v += s_red[lane][q];
+        const int t0 = __shfl_sync(0xffffffffu, v, 0), t1 = __shfl_sync(0xffffffffu, v, 1);
+        const int t2 = __shfl_sync(0xffffffffu, v, 2);
+        const int b = __shfl_sync(0xffffffffu, v, (lane & 3) + 5);     // code (lane & 3) before the chunk
+        if (lane < 4) {
+            // code k's run starts after the rows of codes 0 .. k-1
+            const int start = lane == 0 ? 0 : (lane == 1 ? t0 : (lane == 2 ? t0 + t1 : t0 + t1 + t2));
+            s_run[lane] = start + b;
         }
+        if (blockIdx.x == 0 && lane < 5) counts[(int64_t)h * 5 + lane] = v;
     }
     __syncthreads();
-    int r0 = s_base[0], r1 = s_base[1], r2 = s_base[2], r3 = s_base[3];
-    for (int t0 = 0; t0 < S; t0 += kHiThreads) {
+    int r0 = s_run[0], r1 = s_run[1], r2 = s_run[2], r3 = s_run[3];
+    for (int t0 = t_begin; t0 < t_end; t0 += kHiThreads) {
         const int t = t0 + threadIdx.x;
-        const int32_t sl = t < S ? slot[(int64_t)t * H + h] : -1;
+        const int32_t sl = t < t_end ? slot[(int64_t)t * H + h] : -1;
         const int code = sl < 0 ? 4 : slot_code(sl);
         const unsigned m0 = __ballot_sync(0xffffffffu, code == 0);
         const unsigned m1 = __ballot_sync(0xffffffffu, code == 1);
         const unsigned m2 = __ballot_sync(0xffffffffu, code == 2);
         const unsigned m3 = __ballot_sync(0xffffffffu, code == 3);
         if (lane == 0) {
-            s_warp[0][w] = __popc(m0);
-            s_warp[1][w] = __popc(m1);
-            s_warp[2][w] = __popc(m2);
-            s_warp[3][w] = __popc(m3);
+            s_cnt[0][w] = __popc(m0);
+            s_cnt[1][w] = __popc(m1);
+            s_cnt[2][w] = __popc(m2);
+            s_cnt[3][w] = __popc(m3);
+        }
+        __syncthreads();
+        if (w < 4) {
+            // warp k: exclusive scan of code k's counts over the warps
+            const int v = lane < NW ? s_cnt[w][lane] : 0;
+            int incl = v;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int u = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += u;
+            }
+            if (lane < NW) s_pre[w][lane] = incl - v;
+            if (lane == 31) s_tot[w] = incl;
         }
         __syncthreads();
         if (code < 4) {
             const unsigned m = code == 0 ? m0 : (code == 1 ? m1 : (code == 2 ? m2 : m3));
             const int run = code == 0 ? r0 : (code == 1 ? r1 : (code == 2 ? r2 : r3));
-            int before = 0;
-            for (int q = 0; q < w; ++q) before += s_warp[code][q];
-            rows[(int64_t)h * S + run + before + __popc(m & ((1u << lane) - 1u))] = sl;
+            rows[(int64_t)h * S + run + s_pre[code][w] + __popc(m & ((1u << lane) - 1u))] = sl;
         }
-        int t0s = 0, t1s = 0, t2s = 0, t3s = 0;
-        for (int q = 0; q < kHiThreads / 32; ++q) {
-            t0s += s_warp[0][q];
-            t1s += s_warp[1][q];
-            t2s += s_warp[2][q];
-            t3s += s_warp[3][q];
-        }
-        r0 += t0s;
-        r1 += t1s;
-        r2 += t2s;
-        r3 += t3s;
+        r0 += s_tot[0];
+        r1 += s_tot[1];
+        r2 += s_tot[2];
+        r3 += s_tot[3];
         __syncthreads();
     }
 }
@@ -1602,7 +1615,13 @@ extern "C" {
 int skv_head_index(const int32_t* slot, int S, int H, int32_t* rows, int32_t* counts, void* stream) {
     if (!slot || !rows || !counts) return fail(SKV_ERR_INVALID_ARGUMENT, "head_index: null pointer");
     if (S <= 0 || H <= 0) return fail(SKV_ERR_INVALID_ARGUMENT, "head_index: bad shape");
-    head_index_kernel<<<H, kHiThreads, 0, as_stream(stream)>>>(slot, S, H, rows, counts);
+    // chunks of whole 1024-token passes, enough of them for ~two blocks per SM in all
+    const int passes = (S + kHiThreads - 1) / kHiThreads;
+    const int want = std::max(1, std::min(passes, (2 * sm_count() + H - 1) / H));
+    const int C = (passes + want - 1) / want * kHiThreads;
+    const int nchunks = (S + C - 1) / C;
+    if (H > 65535) return fail(SKV_ERR_TOO_LARGE, "head_index: more than 65535 heads");
+    head_index_kernel<<<dim3(nchunks, H), kHiThreads, 0, as_stream(stream)>>>(slot, S, H, C, rows, counts);
     return check_launch("head_index");
 }
 

@@ -522,3 +522,26 @@ def test_attention_pair_rejects_other_shapes_and_flags(skv):
     with pytest.raises(ValueError, match="CTA-pair"):
         skv.packed_attention(torch.zeros(1, 2, 8, 128, dtype=torch.float16, device="cuda"), cache, pair=True,
                              one_tile=True)
+
+
+@pytest.mark.parametrize("S,H", [(1, 1), (77, 3), (1024, 2), (5000, 4), (32768, 4), (2048, 32), (40000, 1)])
+def test_head_index_rows_and_counts(skv, S, H):
+    """skv_head_index: per head, the slots of the stored entries in token order, fp32 entries first,
+    then fp16, int8, int4 (the order staging reads them), and the five counts per head (the four
+    precisions and the evicted entries); heads are split over several blocks when there are few."""
+    from shadow_infer_b200 import _lib
+    rng = np.random.default_rng(S + 7 * H)
+    codes = rng.integers(0, 5, size=(S, H))
+    slot = np.where(codes == 4, -1, (np.arange(S * H).reshape(S, H) << 2) | np.minimum(codes, 3)).astype(np.int32)
+    sd = torch.from_numpy(slot).cuda()
+    rows = torch.full((H * S,), -7, dtype=torch.int32, device="cuda")
+    counts = torch.empty(H * 5, dtype=torch.int32, device="cuda")
+    lib = _lib.load()
+    _lib.check(lib.skv_head_index(_lib.ptr(sd), S, H, _lib.ptr(rows), _lib.ptr(counts),
+                                  _lib.stream_of(torch.device("cuda"))), "head_index")
+    rows, counts = rows.cpu().numpy().reshape(H, S), counts.cpu().numpy().reshape(H, 5)
+    for h in range(H):
+        want = np.concatenate([slot[codes[:, h] == k, h] for k in range(4)])
+        assert np.array_equal(rows[h, :want.size], want)
+        assert np.all(rows[h, want.size:] == -7)
+        assert counts[h].tolist() == [int(np.sum(codes[:, h] == k)) for k in range(5)]
