@@ -206,6 +206,26 @@ def _slab_buckets(counts: Sequence[int], B: int, D: int, G: int, dev: torch.devi
     return buckets
 
 
+class _SlabFlat:
+    """The int64 flat indices of a slab's buckets, in bucket order (what ``_slab_views`` and
+    ``_bucket_array`` read from a plan's ``_flat_all``)."""
+    __slots__ = ("_flat_all",)
+
+    def __init__(self, flat_all: torch.Tensor):
+        self._flat_all = flat_all
+
+
+def _empty_slab(counts: Sequence[int], B: int, D: int, G: int, dev: torch.device):
+    """One allocation for buckets of ``counts`` entries (payload, scales, then the flat indices)
+    and its ``skv_bucket[4]`` array, without making any tensor views: (slab, layout, flat
+    holder, array).  The views come later from ``_slab_views`` (``_materialise``)."""
+    layout, total = _slab_layout(counts, B, D, G)
+    n = sum(counts)
+    slab = torch.empty(max(total + n * 8, 1), dtype=torch.uint8, device=dev)
+    flat = _SlabFlat(slab[total:total + n * 8].view(torch.int64))
+    return slab, layout, flat, _bucket_array(slab.data_ptr(), layout, counts, flat)
+
+
 def _bucket_array(slab_base: int, layout, counts: Sequence[int], plan: PrecisionPlan):
     arr = _lib.Buckets4()
     flat_base = plan._flat_all.data_ptr()
@@ -414,8 +434,8 @@ class PackedKVCache:
         self._pending = None
         arr = self._arr_cache[2]
         hidx = self._hidx
-        self._adopt(_slab_views(slab, layout, counts, plan), plan.slot, shared_slot=True, group_size=group_size,
-                    arr=arr)
+        self._adopt(_slab_views(slab, layout, counts, plan), self._slot, shared_slot=not self._slot_owned,
+                    group_size=group_size, arr=arr)
         self._hidx = hidx
 
     def _adopt(self, buckets, slot: torch.Tensor, shared_slot: bool, group_size: int, arr=None) -> None:
@@ -754,13 +774,21 @@ class PackedKVCache:
             self._slot = self._slot.clone()
             self._slot_owned = True
         G = _int4_group(self.head_dim, group_size)
-        dst = _slab_buckets([kept[c] if counts[c] else 0 for c in range(4)], self.batch_size, self.head_dim, G, dev)
+        want = [kept[c] if counts[c] else 0 for c in range(4)]
+        new_slab, new_layout, flat, dst_arr = _empty_slab(want, self.batch_size, self.head_dim, G, dev)
         with device_ctx(dev):
-            st = lib.skv_evict_compact(src_arr, _lib.buckets(dst), _lib.ptr(mask), _lib.ptr(self._slot),
+            st = lib.skv_evict_compact(src_arr, dst_arr, _lib.ptr(mask), _lib.ptr(self._slot),
                                        self.batch_size, self.seq_len, self.num_heads, self.head_dim, G,
                                        _lib.ptr(scr), scr.numel(), stream)
         _lib.check(st, "PackedKVCache.evict")
-        self._adopt(dst, self._slot, shared_slot=False, group_size=group_size)
+        # the survivors' slab replaces the pack's, its views again made on first access
+        self._hidx = None
+        self._packed_data = {}
+        self._flat = {}
+        self._count = {PRECISION_ORDER[c]: want[c] for c in range(4) if want[c]}
+        self._memory_bytes = sum(nb for parts in new_layout if parts for _, _, _, _, nb in parts)
+        self._pending = (new_slab, new_layout, want, flat, group_size)
+        self._arr_cache = (None, self._dev, dst_arr, None, True, None)
         return kept[4]
 
     def _entry_mask(self, entries: Any, dev: torch.device) -> torch.Tensor:

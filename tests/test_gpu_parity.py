@@ -341,3 +341,29 @@ def test_evict_fresh_pack_paths(case, skv, monkeypatch):
     assert eq(ku, ko) and eq(vu, vo)
     # idempotent: the same set again removes nothing
     assert cache.evict(cu(sel)) == 0
+
+
+def test_evict_chain_then_views_and_attention(skv):
+    """Three evictions in a row on a freshly packed cache (each leaves the survivors' slab with its
+    views still unmade), then reuse from the evicted cache, unpack, the bucket views and packed
+    attention, each against the oracle after the same evictions."""
+    rng = np.random.default_rng(31)
+    B, H, S, D = 2, 4, 300, 128
+    k = rng.standard_normal((B, H, S, D)).astype(np.float32)
+    v = rng.standard_normal((B, H, S, D)).astype(np.float32)
+    codes = rng.integers(0, 5, size=(S, H)).astype(np.int8)
+    cache = skv.PackedKVCache.pack(cu(k), cu(v), None, 16, plan=skv.PrecisionPlan.from_codes(cu(codes)))["packed_kv"]
+    ref = O.pack(k, v, O.plan_from_codes(codes), 16)
+    for frac in (0.2, 0.3, 0.5):
+        sel = rng.random((S, H)) < frac
+        assert cache.evict(cu(sel)) == O.evict(ref, sel)
+        assert cache.memory_bytes() == ref.memory_bytes()
+    ku, vu = cache.unpack()
+    ko, vo = O.unpack(ref)
+    assert eq(ku, ko) and eq(vu, vo)
+    q = rng.standard_normal((B, H, 70, D)).astype(np.float16)
+    out = skv.packed_attention(torch.from_numpy(q).cuda(), cache).cpu().numpy()
+    want = O.packed_attention(q.astype(np.float32), ref)
+    assert float(np.linalg.norm(out - want) / np.linalg.norm(want)) < 1e-3
+    assert packed_summary(cache.packed_data, cache.memory_bytes()) == packed_summary(ref.packed_data, ref.memory_bytes())
+    assert cache.resident_bytes() == ref.resident_bytes()
