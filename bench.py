@@ -1631,6 +1631,11 @@ def run_b200(args):
         sampler.start()
     head = long_context_phase(args, world, rank, dev, dist, lib)
     clocks = sampler.summary() if sampler else None
+    if sampler:
+        # the clocks are the headline's; nvidia-smi polling stops before the sub-objects, whose
+        # short launches it would otherwise disturb
+        sampler.stop()
+        sampler = None
     torch.cuda.empty_cache()
     extras = {}
     if not args.no_extras:
