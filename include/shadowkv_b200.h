@@ -256,6 +256,11 @@ int skv_peer_store(const void* src, int64_t bytes, const int64_t* dst_ptrs, int 
  *                       of the P V products; the tile's softmax is split over eight warps.  Takes no
  *                       other pipeline flag (FAST_K may be combined). */
 #define SKV_ATTN_PAIR 8
+/*   SKV_ATTN_OUT_F16  -- the output (`out`, and with peers every rank's buffer) is written as fp16,
+ *                       each value rounded to nearest even from the fp32 result: half the bytes
+ *                       to store and, head-sharded, to send over NVLink.  The pointers keep their
+ *                       float* type in the signatures; the buffers must hold B*H*S_q*D halves. */
+#define SKV_ATTN_OUT_F16 16
 int skv_packed_attention_gqa(const void* q, int B, int H_q, int S_q, int D, const skv_bucket* buckets, int H_kv,
                              int S_kv, int int4_group, const int32_t* rows, const int32_t* counts,
                              const float* k_new, const float* v_new, int S_new, float scale, void* scratch,

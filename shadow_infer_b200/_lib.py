@@ -31,6 +31,7 @@ SKV_ATTN_FAST_K = 1   # attention flag: K in fp16 only (include/shadowkv_b200.h)
 SKV_ATTN_ONE_TILE = 2  # attention flag: the single-query-tile pipeline
 SKV_ATTN_FMA_EXP = 4   # attention flag: a quarter of the softmax exponentials on the FMA pipe
 SKV_ATTN_PAIR = 8      # attention flag: the CTA-pair pipeline (head_dim 128)
+SKV_ATTN_OUT_F16 = 16  # attention flag: fp16 output (and fp16 peer buffers)
 
 c_void_p = ctypes.c_void_p
 c_int = ctypes.c_int

@@ -129,6 +129,7 @@ struct AttnParams {
     int klo;                   // 1: the head's kLoCh largest channels of K also contribute their lo part
     int one_tile;              // 1: the single-query-tile kernel (units of 128 queries); 0: two tiles (256)
     int pair;                  // 1: the CTA-pair kernel (units of 256 queries over two CTAs, head_dim 128)
+    int out_half;              // 1: `out` and every peer buffer hold fp16 (two-tile kernel only)
     int emu;                   // two-tile kernel: a quarter of the exponentials on the FMA pipe
     unsigned* chmax;           // [H_kv, D] max |K| per channel (float bits), channel selection input
     int* sel;                  // [H_kv, kLoCh] the selected channels, ascending
@@ -747,13 +748,26 @@ __device__ __forceinline__ bool wait_flag(const int* flag, int target, int* err,
 
 // One float2 of the final output at element offset idx of the [B, H_out, S_q, D] layout: into
 // every peer's buffer, or into `out`.
+// With out_half the two values go out as one fp16 pair (round to nearest even).
+__device__ __forceinline__ void st_global_h2(float* base, int64_t idx, float2 v) {
+    const uint32_t h = half2_bits(__floats2half2_rn(v.x, v.y));
+    asm volatile("st.global.b32 [%0], %1;" ::"l"(reinterpret_cast<__half*>(base) + idx), "r"(h));
+}
 template <bool PEERS>
 __device__ __forceinline__ void out_store(const AttnParams& p, int64_t idx, float2 v) {
     if (!PEERS) {
-        st_global_f2(p.out + idx, v);
+        if (p.out_half)
+            st_global_h2(p.out, idx, v);
+        else
+            st_global_f2(p.out + idx, v);
         return;
     }
-    for (int r = 0; r < p.n_peers; ++r) st_global_f2(p.peers[r] + idx, v);
+    for (int r = 0; r < p.n_peers; ++r) {
+        if (p.out_half)
+            st_global_h2(p.peers[r], idx, v);
+        else
+            st_global_f2(p.peers[r] + idx, v);
+    }
 }
 
 // Peer epilogue: a softmax warp stages 4 finished output rows -- contiguous in every rank's
@@ -767,10 +781,15 @@ __device__ __forceinline__ void stage_acquire(int lane) {
     __syncwarp();
 }
 // this lane's two values of chunk c, part k of slot row (lane >> 2) & 3, when its row is in half `sub`
+// (fp16 rows, half as long, when `half`)
 template <int D>
-__device__ __forceinline__ void stage_put(float* slot, int lane, int sub, int c, int k, float2 v) {
-    if ((lane >> 4) == sub)
-        *reinterpret_cast<float2*>(slot + ((lane >> 2) & 3) * D + c * 32 + 8 * k + 2 * (lane & 3)) = v;
+__device__ __forceinline__ void stage_put(float* slot, bool half, int lane, int sub, int c, int k, float2 v) {
+    if ((lane >> 4) != sub) return;
+    const int e = ((lane >> 2) & 3) * D + c * 32 + 8 * k + 2 * (lane & 3);
+    if (half)
+        *reinterpret_cast<__half2*>(reinterpret_cast<__half*>(slot) + e) = __floats2half2_rn(v.x, v.y);
+    else
+        *reinterpret_cast<float2*>(slot + e) = v;
 }
 // slot rows [0, n) -> element idx of every rank's buffer
 template <int D>
@@ -778,12 +797,14 @@ __device__ __noinline__ void stage_flush(const AttnParams& p, const float* slot,
     fence_proxy_async_smem();
     __syncwarp();
     if (n <= 0) return;
+    const int esz = p.out_half ? 2 : 4;
     for (int r = 0; r < p.n_peers; ++r) {
-        float* g = p.peers[r] + idx;
+        uint8_t* g = reinterpret_cast<uint8_t*>(p.peers[r]) + idx * esz;
         if ((reinterpret_cast<uintptr_t>(g) & 15) == 0) {
-            if (lane == 0) bulk_s2g(g, slot, (uint32_t)(n * D * 4));
+            if (lane == 0) bulk_s2g(g, slot, (uint32_t)(n * D * esz));
         } else {
-            for (int e = lane; e < n * D; e += 32) g[e] = slot[e];
+            const uint16_t* s16 = reinterpret_cast<const uint16_t*>(slot);
+            for (int e = lane; e < n * D * esz / 2; e += 32) reinterpret_cast<uint16_t*>(g)[e] = s16[e];
         }
     }
     if (lane == 0) bulk_commit();
@@ -832,7 +853,7 @@ __device__ __noinline__ void merge_parts(const AttnParams& p, uint32_t tO, int h
                     }
                 }
 #pragma unroll
-                for (int k = 0; k < 4; ++k) stage_put<D>(oslot, lane, sub, c, k, v[k]);
+                for (int k = 0; k < 4; ++k) stage_put<D>(oslot, p.out_half, lane, sub, c, k, v[k]);
             }
             const int r0 = hf * 16 + half * 8 + sub * 4;
             stage_flush<D>(p, oslot, lane, obase + (int64_t)r0 * D, min(4, nrows - r0));
@@ -1143,7 +1164,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                                     }
 #pragma unroll
                                     for (int k = 0; k < 4; ++k)
-                                        stage_put<D>(oslot, lane, sub, c, k,
+                                        stage_put<D>(oslot, p.out_half, lane, sub, c, k,
                                                      make_float2(fmaf(px[c][k].x, fbr, __uint_as_float(o[4 * k + 2 * half]) * far),
                                                                  fmaf(px[c][k].y, fbr, __uint_as_float(o[4 * k + 2 * half + 1]) * far)));
                                 }
@@ -1208,7 +1229,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                                 }
 #pragma unroll
                                 for (int k = 0; k < 4; ++k)
-                                    stage_put<D>(oslot, lane, sub, c, k,
+                                    stage_put<D>(oslot, p.out_half, lane, sub, c, k,
                                                  make_float2(__uint_as_float(o[4 * k + 2 * half]) * fr,
                                                              __uint_as_float(o[4 * k + 2 * half + 1]) * fr));
                             }
@@ -1652,7 +1673,7 @@ int attn_params(const void* q, int B, int H, int S_q, int D, const skv_bucket* b
                 AttnParams& prm, const char* what, int max_ctas = 0, float* const* peers = nullptr,
                 int n_peers = 0, int head_off = 0, int H_out = 0, int flags = 0) {
     if (!rows || !counts || !scratch) return fail(SKV_ERR_INVALID_ARGUMENT, "%s: null pointer", what);
-    if (flags & ~(SKV_ATTN_FAST_K | SKV_ATTN_ONE_TILE | SKV_ATTN_FMA_EXP | SKV_ATTN_PAIR))
+    if (flags & ~(SKV_ATTN_FAST_K | SKV_ATTN_ONE_TILE | SKV_ATTN_FMA_EXP | SKV_ATTN_PAIR | SKV_ATTN_OUT_F16))
         return fail(SKV_ERR_INVALID_ARGUMENT, "%s: unknown flags 0x%x", what, flags);
     if ((flags & SKV_ATTN_PAIR) && (flags & (SKV_ATTN_ONE_TILE | SKV_ATTN_FMA_EXP)))
         return fail(SKV_ERR_INVALID_ARGUMENT, "%s: the CTA-pair pipeline takes no other pipeline flag", what);
@@ -1716,6 +1737,7 @@ int attn_params(const void* q, int B, int H, int S_q, int D, const skv_bucket* b
     prm.G = G;
     prm.one_tile = (flags & SKV_ATTN_ONE_TILE) ? 1 : 0;
     prm.pair = (flags & SKV_ATTN_PAIR) ? 1 : 0;
+    prm.out_half = (flags & SKV_ATTN_OUT_F16) ? 1 : 0;
     prm.emu = (flags & SKV_ATTN_FMA_EXP) ? 1 : 0;
     prm.QP = prm.one_tile ? (S_q + k1TUnitRows - 1) / k1TUnitRows : (S_q + kUnitRows - 1) / kUnitRows;
     prm.scale_log2 = scale * 1.4426950408889634f;

@@ -329,7 +329,7 @@ __global__ void __launch_bounds__(k1TThreads, 1)
                                     }
 #pragma unroll
                                     for (int k = 0; k < 4; ++k)
-                                        stage_put<D>(oslot, lane, sub, c, k,
+                                        stage_put<D>(oslot, p.out_half, lane, sub, c, k,
                                                      make_float2(fmaf(px[c][k].x, fbr, __uint_as_float(o[4 * k + 2 * half]) * far),
                                                                  fmaf(px[c][k].y, fbr, __uint_as_float(o[4 * k + 2 * half + 1]) * far)));
                                 }
@@ -394,7 +394,7 @@ __global__ void __launch_bounds__(k1TThreads, 1)
                                 }
 #pragma unroll
                                 for (int k = 0; k < 4; ++k)
-                                    stage_put<D>(oslot, lane, sub, c, k,
+                                    stage_put<D>(oslot, p.out_half, lane, sub, c, k,
                                                  make_float2(__uint_as_float(o[4 * k + 2 * half]) * fr,
                                                              __uint_as_float(o[4 * k + 2 * half + 1]) * fr));
                             }

@@ -100,12 +100,21 @@ struct PairCursor {
     __device__ bool last() const { return j == nt - 1; }
 };
 
+// Four consecutive output values at element idx (a multiple of 4): fp32, or fp16 with out_half.
+__device__ __forceinline__ void pair_put4(const AttnParams& p, float* base, int64_t idx, float4 v) {
+    if (p.out_half) {
+        const uint2 h = make_uint2(half2_bits(__floats2half2_rn(v.x, v.y)), half2_bits(__floats2half2_rn(v.z, v.w)));
+        *reinterpret_cast<uint2*>(reinterpret_cast<__half*>(base) + idx) = h;
+    } else {
+        *reinterpret_cast<float4*>(base + idx) = v;
+    }
+}
 template <bool PEERS>
 __device__ __forceinline__ void pair_store4(const AttnParams& p, int64_t idx, float4 v) {
     if constexpr (PEERS) {
-        for (int i = 0; i < p.n_peers; ++i) *reinterpret_cast<float4*>(p.peers[i] + idx) = v;
+        for (int i = 0; i < p.n_peers; ++i) pair_put4(p, p.peers[i], idx, v);
     } else {
-        *reinterpret_cast<float4*>(p.out + idx) = v;
+        pair_put4(p, p.out, idx, v);
     }
 }
 

@@ -39,6 +39,7 @@ def packed_attention(
     one_tile: bool = False,
     fma_exp: bool = False,
     pair: bool = False,
+    out_dtype: torch.dtype = torch.float32,
 ) -> torch.Tensor:
     """Non-causal attention of ``q`` [B, H_q, S_q, D] over a packed cache; returns fp32 [B, H_q, S_q, D].
 
@@ -63,6 +64,11 @@ def packed_attention(
     all-reduce after the call, or a stream synchronize plus ``torch.distributed.barrier``)
     before reading it, and again before the next call that writes the same buffers, so that
     no rank overwrites a buffer another rank is still reading.
+
+    ``out_dtype=torch.float16``: the output is written in fp16, each value the fp32 result rounded
+    to nearest even (the same bits as ``.half()`` of the fp32 output) -- half the bytes to store
+    and, with ``peer_outputs`` (which must then be float16 buffers), half the bytes sent over
+    NVLink; it adds about 2.8e-4 of relative L2 error.
 
     Precision: Q, K, V and the softmax weights P are fp16 tensor-core operands with fp32
     accumulation and softmax; the 16 channels of largest max |K| in each KV head also contribute
@@ -110,13 +116,16 @@ def packed_attention(
         scale = 1.0 / math.sqrt(D)
     if not c.packed_data and S_new == 0:
         # every token-head evicted: unpack() would give zero K/V, so the output is zero
-        return torch.zeros(B, H, S_q, D, dtype=torch.float32, device=q.device)
+        return torch.zeros(B, H, S_q, D, dtype=out_dtype if out_dtype == torch.float16 else torch.float32,
+                           device=q.device)
     dev = c._ensure_state()
     qd = on(q, dev, torch.float16)
     kn = on(k_new, dev, torch.float32) if S_new else None
     vn = on(v_new, dev, torch.float32) if S_new else None
     rows, counts = c._head_index(dev)
-    out = torch.empty(B, H, S_q, D, dtype=torch.float32, device=dev)
+    if out_dtype not in (torch.float32, torch.float16):
+        raise ValueError(f"out_dtype must be torch.float32 or torch.float16, got {out_dtype}")
+    out = torch.empty(B, H, S_q, D, dtype=out_dtype, device=dev)
     err = torch.empty(1, dtype=torch.int32, device=dev)
     arr, _, _ = c._device_arr(dev)
     lib = _lib.load()
@@ -124,9 +133,13 @@ def packed_attention(
     stream = _lib.stream_of(dev)
     g = c._int4_group_of()
     flags = ((_lib.SKV_ATTN_FAST_K if fast_k else 0) | (_lib.SKV_ATTN_ONE_TILE if one_tile else 0) |
-             (_lib.SKV_ATTN_FMA_EXP if fma_exp else 0) | (_lib.SKV_ATTN_PAIR if pair else 0))
+             (_lib.SKV_ATTN_FMA_EXP if fma_exp else 0) | (_lib.SKV_ATTN_PAIR if pair else 0) |
+             (_lib.SKV_ATTN_OUT_F16 if out_dtype == torch.float16 else 0))
     if peer_outputs is not None:
         Bp, Hp, Sp, Dp = peer_outputs.shape
+        if getattr(peer_outputs, "dtype", torch.float32) != out_dtype:
+            raise ValueError(f"peer output buffers hold {getattr(peer_outputs, 'dtype', torch.float32)}, "
+                             f"out_dtype is {out_dtype}")
         if (Bp, Sp, Dp) != (B, S_q, D) or not 0 <= head_offset <= Hp - H:
             raise ValueError(f"peer output buffers {peer_outputs.shape} cannot take heads "
                              f"[{head_offset}, {head_offset + H}) of q {tuple(q.shape)}")

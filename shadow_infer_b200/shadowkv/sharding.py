@@ -104,7 +104,8 @@ def admit_codes_sharded(
 
 
 class PeerOutputs:
-    """One float32 output buffer ``shape`` = [B, H, S_q, D] per rank, each mapped into every rank
+    """One output buffer ``shape`` = [B, H, S_q, D] per rank (``dtype`` float32, or float16 for
+    ``packed_attention(..., out_dtype=torch.float16)``), each mapped into every rank
     of ``group`` through CUDA IPC.  ``ptrs`` is a device int64 array of the ranks' buffer
     addresses as seen from this process, in rank order; ``local`` is this rank's buffer.  A
     kernel that stores into all of them leaves every rank with the full result once all ranks'
@@ -117,14 +118,17 @@ class PeerOutputs:
     process group.
     """
 
-    def __init__(self, shape, group=None, device=None) -> None:
+    def __init__(self, shape, group=None, device=None, dtype: torch.dtype = torch.float32) -> None:
         from .. import _lib
         from .._device import device_ctx
 
         n, r = _world(group)
         dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
         self.world, self.rank = n, r
-        self.local = torch.zeros(tuple(shape), dtype=torch.float32, device=dev)
+        if dtype not in (torch.float32, torch.float16):
+            raise ValueError(f"PeerOutputs: dtype must be float32 or float16, got {dtype}")
+        self.dtype = dtype
+        self.local = torch.zeros(tuple(shape), dtype=dtype, device=dev)
         lib = _lib.load()
         hb = lib.skv_ipc_handle_bytes()
         handle = ctypes.create_string_buffer(hb)

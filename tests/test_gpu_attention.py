@@ -229,8 +229,9 @@ def test_attention_with_fewer_ctas(skv):
 class _TwoBuffers:
     """Two output buffers on one GPU standing in for two ranks' IPC-mapped buffers."""
 
-    def __init__(self, shape, local):
-        self.bufs = [torch.zeros(shape, dtype=torch.float32, device="cuda") for _ in range(2)]
+    def __init__(self, shape, local, dtype=torch.float32):
+        self.bufs = [torch.zeros(shape, dtype=dtype, device="cuda") for _ in range(2)]
+        self.dtype = dtype
         self.local = self.bufs[local]
         self.shape = tuple(shape)
         self.world = 2
@@ -545,3 +546,37 @@ def test_head_index_rows_and_counts(skv, S, H):
         assert np.array_equal(rows[h, :want.size], want)
         assert np.all(rows[h, want.size:] == -7)
         assert counts[h].tolist() == [int(np.sum(codes[:, h] == k)) for k in range(5)]
+
+
+# ---------------------------------------------------------------- fp16 output
+@pytest.mark.parametrize("pipeline", ["default", "one_tile", "pair"])
+@pytest.mark.parametrize("B,H,S,SQ,D,probs,qs", [CASES[0], CASES[2], CASES[6]])
+def test_attention_fp16_output_is_the_rounded_fp32_output(skv, pipeline, B, H, S, SQ, D, probs, qs):
+    """out_dtype=float16 stores the same results rounded to nearest even: bit-identical to
+    .half() of the fp32 output, through every epilogue path (whole units, units merged from
+    stream-K parts over two and over several CTAs, the two-buffer peer epilogue)."""
+    if pipeline == "pair" and D != 128:
+        pytest.skip("the CTA-pair pipeline is head_dim 128 only")
+    rng = np.random.default_rng(S * 31 + D)
+    k = rng.standard_normal((B, H, S, D)).astype(np.float32)
+    v = rng.standard_normal((B, H, S, D)).astype(np.float32)
+    codes = rng.choice(5, size=(S, H), p=probs).astype(np.int8)
+    q = (rng.standard_normal((B, H, SQ, D)) * qs).astype(np.float16)
+    cache = _pack(skv, k, v, codes)
+    qd = torch.from_numpy(q).cuda()
+    kw = {"one_tile": pipeline == "one_tile", "pair": pipeline == "pair"}
+    ref = O.packed_attention(q.astype(np.float32), O.pack(k, v, O.plan_from_codes(codes), 16))
+    for mc in (0, 2, 4, 7):
+        o32 = skv.packed_attention(qd, cache, max_ctas=mc, **kw)
+        o16 = skv.packed_attention(qd, cache, max_ctas=mc, out_dtype=torch.float16, **kw)
+        assert o16.dtype == torch.float16 and torch.equal(o16, o32.half()), mc
+        assert rel_l2(o16.float().cpu().numpy(), ref) < REL_L2_TOL
+    peers = _TwoBuffers((B, H, SQ, D), 1, dtype=torch.float16)
+    skv.packed_attention(qd, cache, peer_outputs=peers, head_offset=0, out_dtype=torch.float16, **kw)
+    torch.cuda.synchronize()
+    o32 = skv.packed_attention(qd, cache, **kw)
+    assert torch.equal(peers.bufs[0], o32.half()) and torch.equal(peers.bufs[1], o32.half())
+    with pytest.raises(ValueError, match="out_dtype"):
+        skv.packed_attention(qd, cache, peer_outputs=peers, head_offset=0, **kw)
+    with pytest.raises(ValueError, match="out_dtype"):
+        skv.packed_attention(qd, cache, out_dtype=torch.bfloat16)
