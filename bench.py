@@ -291,7 +291,8 @@ def run_reference(args):
 
 
 # ------------------------------------------------------------------------------- helpers
-def exchange_ceiling(peers, attn_fused, attn_local, h0, hs, world, dist, dev, reps=5):
+def exchange_ceiling(peers, attn_fused, attn_local, h0, hs, world, dist, dev, reps=5, peers16=None,
+                     attn_fused16=None):
     """At N > 1: the plain exchange -- ``skv_peer_store`` copying this rank's heads of the output
     (already in its buffer) into every rank's buffer -- timed alone, next to the fused epilogue's
     cost (the attention storing into every rank's buffer against the same attention storing into
@@ -335,7 +336,39 @@ def exchange_ceiling(peers, attn_fused, attn_local, h0, hs, world, dist, dev, re
     ms_local = timed(attn_local)
     egress = nbytes * (world - 1)
     ok = sum_over_ranks(1.0 if failed else 0.0, world, dist, dev) == 0
-    return {"plain_store": {"kernel": "skv_peer_store: 16-byte loads once, stores into every rank's buffer",
+    f16 = None
+    if peers16 is not None:
+        # the same exchange with fp16 outputs: half the bytes per rank; the gathered fp16 buffer
+        # against the fp32 one (every head, after both fused calls)
+        b16 = peers16[0]
+        src16 = src.half()
+
+        def plain16():
+            for b in range(B):
+                st = lib.skv_peer_store(_lib.ptr(src16[b]), hs * S_q * D * 2, _lib.ptr(b16.ptrs), world,
+                                        ((b * H + h0) * S_q * D) * 2, stream)
+                if st != 0 and not failed:
+                    failed.append(_lib.last_error())
+
+        ms_plain16 = timed(plain16)
+        ms_fused16 = timed(attn_fused16)
+        attn_fused()
+        attn_fused16()
+        torch.cuda.synchronize()
+        dist.all_reduce(bar)
+        torch.cuda.synchronize()
+        num = float(((b16.local.float() - buf.local) ** 2).sum().item())
+        den = float((buf.local ** 2).sum().item())
+        err = (sum_over_ranks(num, world, dist, dev) / max(sum_over_ranks(den, world, dist, dev), 1e-30)) ** 0.5
+        ok16 = sum_over_ranks(1.0 if failed else 0.0, world, dist, dev) == 0
+        f16 = {"bytes_per_rank": nbytes // 2, "plain_store_ms": ms_plain16,
+               "plain_store_egress_gbs_per_gpu": (egress // 2) / (ms_plain16 / 1e3) / 1e9 if ok16 else None,
+               "attention_ms_storing_to_all_ranks": ms_fused16, "exchange_cost_ms": ms_fused16 - ms_local,
+               "rel_l2_vs_f32_output": err,
+               "what": "out_dtype=float16: the epilogue rounds each value to fp16 (nearest even) and stores "
+                       "half the bytes into every rank's fp16 buffer"}
+    return {"fp16_exchange": f16,
+            "plain_store": {"kernel": "skv_peer_store: 16-byte loads once, stores into every rank's buffer",
                             "bytes_per_rank": nbytes, "ms": ms_plain,
                             "egress_gbs_per_gpu": egress / (ms_plain / 1e3) / 1e9 if ok else None,
                             "error": None if ok else (failed[0] if failed else "failed on another rank")},
@@ -384,7 +417,7 @@ def rel_l2(a, b) -> float:
     return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
 
 
-def make_peers(world, dev, dist, shape, count=1):
+def make_peers(world, dev, dist, shape, count=1, dtype=None):
     """``count`` PeerOutputs of ``shape`` (every rank's fp32 buffer mapped into all ranks), or
     (None, reason) on every rank if any rank cannot map its peers' buffers -- the ranks agree
     through a MIN all-reduce so that all of them keep taking the same collective steps."""
@@ -395,7 +428,7 @@ def make_peers(world, dev, dist, shape, count=1):
     bufs, err = [], None
     try:
         for _ in range(count):
-            bufs.append(PeerOutputs(shape, device=dev))
+            bufs.append(PeerOutputs(shape, device=dev, dtype=dtype or torch.float32))
     except Exception as e:          # noqa: BLE001 - reported in the line, then the fallback runs
         err = f"{type(e).__name__}: {e}"
     flag = torch.tensor([0 if err else 1], device=dev, dtype=torch.int32)
@@ -1001,9 +1034,16 @@ def attention_phase(args, world, rank, dev, dist, lib):
 
     check = check_long_context(full, lambda: packed_attention(qd, cache), h0, hs, S, world, rank, dev, dist,
                                layer_fn, lambda Lh, h: codes_all[:, h:h + 1].numpy(), 200)
+    peers16 = None
+    if world > 1 and peers:
+        peers16, _ = make_peers(world, dev, dist, (B, H, S, D), dtype=torch.float16)
     ceiling = exchange_ceiling(
         peers, lambda: packed_attention(qd, cache, check=False, peer_outputs=peers[0], head_offset=h0),
-        lambda: packed_attention(qd, cache, check=False), h0, hs, world, dist, dev) if world > 1 and peers else None
+        lambda: packed_attention(qd, cache, check=False), h0, hs, world, dist, dev, peers16=peers16,
+        attn_fused16=(lambda: packed_attention(qd, cache, check=False, peer_outputs=peers16[0], head_offset=h0,
+                                               out_dtype=torch.float16)) if peers16 else None) \
+        if world > 1 and peers else None
+    close_peers(peers16, dist)
     close_peers(peers, dist)
     ms = max_over_ranks(t0.elapsed_time(t1) / steps, world, dist, dev)
     stage_ms = statistics.mean(a.elapsed_time(b) for a, b, _ in kev)
@@ -1047,6 +1087,8 @@ ATTN_VARIANTS = {
                 "a quarter of the softmax exponentials by a polynomial on the FMA pipe (SKV_ATTN_FMA_EXP)"),
     "pair": ({"pair": True}, "two CTAs per unit, M=256 tensor-core MMAs over the pair, scores two KV steps "
                              "ahead, softmax over eight warps per query tile (SKV_ATTN_PAIR)"),
+    "out_f16": ({"out_dtype": "float16"}, "the default pipeline writing its output in fp16 (SKV_ATTN_OUT_F16): "
+                                          "half the output bytes"),
 }
 
 
@@ -1057,6 +1099,7 @@ def variant_compare(name, q, cache, flops, reps=3):
     import torch
     from shadow_infer_b200.shadowkv import packed_attention
     kw, what = ATTN_VARIANTS[name]
+    kw = {k: (getattr(torch, v) if k == "out_dtype" else v) for k, v in kw.items()}
     ref = packed_attention(q, cache)
     out = packed_attention(q, cache, **kw)
     diff = float(((out - ref).double().norm() / ref.double().norm()).item())
