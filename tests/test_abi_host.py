@@ -136,3 +136,33 @@ def test_slab_layout_agrees_with_library(B, D, group):
         for parts in layout:
             for _, _, _, off, nb in parts or ():
                 assert off % 256 == 0 and off + nb <= total
+
+
+@pytest.mark.parametrize("B,D,group", [(1, 128, 16), (8, 128, 16), (2, 64, 32), (3, 96, 48)])
+def test_empty_slab_array_matches_its_views(B, D, group):
+    """An evicted cache's survivors go into a slab whose ``skv_bucket[4]`` array is built from
+    the layout arithmetic alone (the compaction writes through it) while the tensor views are
+    made later: every pointer and count of the array must be where the views read."""
+    from shadow_infer_b200.shadowkv.packed_kv_cache import _empty_slab, _int4_group, _slab_views
+    rng = np.random.default_rng(B * 100 + D)
+    G = _int4_group(D, group)
+    for _ in range(20):
+        counts = [int(x) for x in rng.integers(0, 300, size=4)]
+        counts[int(rng.integers(0, 4))] = 0
+        slab, layout, flat, arr = _empty_slab(counts, B, D, G, torch.device("cpu"))
+        views = _slab_views(slab, layout, counts, flat)
+        end = slab.data_ptr() + slab.numel()
+        for code in range(4):
+            if counts[code] == 0:
+                assert views[code] is None
+                continue
+            b, a = views[code], arr[code]
+            assert a.count == counts[code] == b["count"] == b["flat"].numel()
+            assert a.flat == b["flat"].data_ptr() and b["flat"].dtype == torch.int64
+            for key in ("k", "v", "scale_k", "scale_v"):
+                t = b[key]
+                if t is None:
+                    assert getattr(a, key) is None
+                else:
+                    assert getattr(a, key) == t.data_ptr()
+                    assert t.data_ptr() + t.numel() * t.element_size() <= end
