@@ -254,7 +254,8 @@ int skv_peer_store(const void* src, int64_t bytes, const int64_t* dst_ptrs, int 
  *                       both at once (M = 256), each CTA loading half of every staged K and V tile,
  *                       so a CTA's TMEM holds two score buffers and the scores run two KV steps ahead
  *                       of the P V products; the tile's softmax is split over eight warps.  Takes no
- *                       other pipeline flag (FAST_K may be combined). */
+ *                       other pipeline flag (FAST_K and OUT_F16 may be combined); slower than the
+ *                       default on B200 (its M = 256 MMAs of N = 128 are issue-bound). */
 #define SKV_ATTN_PAIR 8
 /*   SKV_ATTN_OUT_F16  -- the output (`out`, and with peers every rank's buffer) is written as fp16,
  *                       each value rounded to nearest even from the fp32 result: half the bytes
