@@ -21,7 +21,8 @@
 // no swizzle: they are staged in the swizzled layout already), each CTA's loads counted on CTA
 // 0's barriers (cta_group::2 form, no multicast).  Work: whole units round-robin over the pairs.
 // Every wait is bounded; after a failure a role skips its remaining work and all roles reach the
-// final cluster barrier before TMEM is released.
+// final cluster barrier before TMEM is released.  CTA 0's loader first waits (bounded) for the
+// last copies issued into every K and V stage: its barriers count both CTAs' bytes.
 
 constexpr int kPairThreads = 10 * 32;
 constexpr int kPairNK = 3;                 // K (+ lo) stages
@@ -335,6 +336,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
         kc.start(ss, pair, npairs, U);
         vc.start(ss, pair, npairs, U);
         long long gk = 0, gv = 0;
+        long long k_issued = 0, v_issued = 0;     // K and V steps whose copies this CTA issued
         bool ok = true;
         HeadRows hr;      // the head of cursor kc's unit
         auto load_q = [&](const PairCursor& c) -> bool {
@@ -398,6 +400,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
                                      (int)((set + 2 * TB + rank * kPairLoHalf) / 128), bar);
             }
             __syncwarp();
+            k_issued = g + 1;
             return true;
         };
         auto load_v = [&](const PairCursor& c, long long g) -> bool {
@@ -414,6 +417,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
                                      (int)((set + TB + rank * kPairHalf + i * (kPairHalf / 2)) / 128), bar);
             }
             __syncwarp();
+            v_issued = g + 1;
             return true;
         };
         // K of the first two steps ahead of any V
@@ -430,6 +434,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
             }
             if (ok) ok = load_v(vc, gv);
         }
+        // every copy issued lands before the pair can exit (a no-op when the MMAs consumed them;
+        // after a pipeline timeout, bounded): CTA 0's barriers count both CTAs' bytes
+        if (rank == 0 && lane == 0) {
+            for (long long g = k_issued - 1; g >= 0 && g >= k_issued - kPairNK; --g)
+                mbar_wait_spin(&k_full[g % kPairNK], (uint32_t)((g / kPairNK) & 1), p.err, kErrCopy);
+            for (long long g = v_issued - 1; g >= 0 && g >= v_issued - kPairNV; --g)
+                mbar_wait_spin(&v_full[g % kPairNV], (uint32_t)((g / kPairNV) & 1), p.err, kErrCopy);
+        }
+        __syncwarp();
     } else if (rank == 0) {
         // ----------------------------------------------------------------- MMA issue (CTA 0)
         if (lane == 0) {
