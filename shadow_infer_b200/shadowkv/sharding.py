@@ -122,11 +122,11 @@ class PeerOutputs:
         from .. import _lib
         from .._device import device_ctx
 
+        if dtype not in (torch.float32, torch.float16):
+            raise ValueError(f"PeerOutputs: dtype must be float32 or float16, got {dtype}")
         n, r = _world(group)
         dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
         self.world, self.rank = n, r
-        if dtype not in (torch.float32, torch.float16):
-            raise ValueError(f"PeerOutputs: dtype must be float32 or float16, got {dtype}")
         self.dtype = dtype
         self.local = torch.zeros(tuple(shape), dtype=dtype, device=dev)
         lib = _lib.load()

@@ -86,3 +86,11 @@ def test_head_range_validation():
         head_range(30, 4, 0)
     with pytest.raises(ValueError):
         head_range(32, 4, 4)
+
+
+def test_peer_outputs_rejects_other_dtypes_before_any_collective():
+    """PeerOutputs takes float32 or float16 buffers; another dtype raises at once, on every rank
+    alike, before any handle exchange (so no rank is left waiting in a collective)."""
+    from shadow_infer_b200.shadowkv.sharding import PeerOutputs
+    with pytest.raises(ValueError, match="float32 or float16"):
+        PeerOutputs((1, 2, 8, 64), dtype=torch.bfloat16)
